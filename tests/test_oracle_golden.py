@@ -1,0 +1,137 @@
+"""Pin the CPU oracle against the reference's own known-answer vectors.
+
+Every case mirrors one reference test (cited) and compares bit-exactly, so a
+GPU result that matches the oracle matches the reference.
+"""
+import numpy as np
+import pytest
+
+from oracle import cross_oracle as O
+from tests.conftest import load_golden
+
+U32 = np.uint32
+parse = O.parse_ciphertext_string
+
+
+def test_ntt_intt_golden():
+    """ntt_mm_test.py:33-54 (test_NTT_Barrett)."""
+    g = load_golden("ntt_mm")
+    r, c, b = g["r"], g["c"], g["test_batch"]
+    coef = np.concatenate([np.array(g["coef_in"], np.uint64).T.reshape(1, r * c, -1)] * b, 0).astype(U32)
+    ev = np.concatenate([np.array(g["eval_in"], U32).T.reshape(1, r * c, -1)] * b, 0)
+    ctx = O.NTTBarrett(g["moduli"], r, c)
+    out = ctx.ntt(coef.reshape(b, r, c, -1))
+    np.testing.assert_array_equal(out.reshape(b, r * c, -1), ev)
+    np.testing.assert_array_equal(ctx.intt(out).reshape(b, r * c, -1), coef)
+
+
+def test_bconv_golden():
+    """bconv_test.py:28-48 (basis_change) and 138-158 (BAT congruent to plain)."""
+    g = load_golden("bconv")
+    x = np.array(g["in_tower"], np.uint64).T
+    ref = np.array(g["reference_result"], np.uint64).T
+    bc = O.BConvBarrett(g["original_moduli"] + g["target_moduli"])
+    bc.control_gen([(list(range(2)), list(range(2, 7)))])
+    assert bc.controls[0]["qhat_inv"].tolist() == g["QHatInvModq"]
+    assert bc.controls[0]["qhat_modp"].tolist() == g["QHatModp"]
+    np.testing.assert_array_equal(bc.basis_change(x), ref)
+    diff = (bc.basis_change_bat(x).astype(np.int64) - ref.astype(np.int64)) % np.array(g["target_moduli"])
+    assert not diff.any()
+
+
+def test_bconv_multiple_control_gen():
+    """bconv_test.py:78-120 (scalar known answers with primes 17/19/23/29)."""
+    bc = O.BConvBarrett([17, 19, 23, 29])
+    bc.control_gen([([0], [2]), ([1], [3])])
+    assert bc.basis_change(np.array([[[15]]], np.uint64), 0)[0, 0, 0] == 15
+    assert bc.basis_change(np.array([[[20]]], np.uint64), 1)[0, 0, 0] == 1
+    assert bc.basis_change(np.array([[[20]]], np.uint64), 0)[0, 0, 0] == 3
+
+
+def test_rescale_golden():
+    """rescale_test.py:49-87 (batch 1 and batch 2)."""
+    g = load_golden("rescale")
+    inc = np.array(parse(g["in_ciphertexts_str"])[0], U32)
+    fin = np.array(parse(g["final_result_str"])[0], U32)
+    rp = O.RescalePlan(g["q_towers"], 4, 4)
+    for b in (1, 2):
+        x = np.tile(np.transpose(inc, (0, 2, 1))[None], (b, 1, 1, 1)).reshape(b, 2, 4, 4, 5)
+        res = rp.rescale(x).reshape(b, 2, 16, 4)
+        for i in range(b):
+            np.testing.assert_array_equal(np.transpose(res[i], (0, 2, 1)), fin)
+
+
+def _herot_inputs():
+    g = load_golden("herot")
+    r, c, dnum = g["r"], g["c"], g["dnum"]
+    rin, rmod = parse(g["rotate_in_ciphertext_str"])
+    eb, ebm = parse(g["evalkey_b_vector_str"])
+    ea, _ = parse(g["evalkey_a_vector_str"])
+    x = np.array(rin, U32).transpose(0, 2, 1).reshape(1, -1, r, c, len(rmod))
+    evb = np.array(eb, np.uint64).transpose(0, 2, 1).reshape(dnum, r, c, len(ebm))
+    eva = np.array(ea, np.uint64).transpose(0, 2, 1).reshape(dnum, r, c, len(ebm))
+    fin = np.array(parse(g["final_result_str"])[0], U32).transpose(0, 2, 1).reshape(1, -1, r * c, len(rmod))
+    return g, x, eva, evb, rmod, ebm[len(rmod):], fin
+
+
+def test_herot_golden():
+    """herot_test.py:229-251 (coefMap known answer + final result)."""
+    g, x, eva, evb, q, p, fin = _herot_inputs()
+    cm = O.precompute_auto_map(16, O.find_automorphism_index_2n_complex(1, 16))
+    assert cm == g["coef_map"]
+    h = O.HERot(4, 4, 3, q, p)
+    h.control_gen(1)
+    h.setup_rotate(eva, evb, cm)
+    np.testing.assert_array_equal(h.rotate(x), fin)
+
+
+def test_hemul_golden_and_e2e():
+    """hemul_test.py:64-140: HE-Mult bit-exact, then decrypt bit-exact, then
+    decode within decimal=3 (|err| < 1.5e-3)."""
+    g = load_golden("hemul")
+    he = O.HEMul(1, 4, 4, 3, 1, g["q_towers"], g["p_towers"])
+    he.setup_relinearization(np.array(g["evalkey_a_vector"], U32), np.array(g["evalkey_b_vector"], U32))
+    out = he.mul(np.array(g["input_ciphertext"], U32))
+    np.testing.assert_array_equal(out, np.array(g["encrypted_mult_result_ref"], U32))
+    enc = out.reshape(1, 2, 16, 4)
+    dec = O.ckks_decrypt([enc[0, 0].tolist(), enc[0, 1].tolist()], g["secret_key"], g["q_towers"][:4])
+    assert dec == g["decrypted_result_ref"]
+    qt = g["q_towers"]
+    vals = O.ckks_decode(dec, qt, (g["scalingFactor"] / qt[-1]) ** 2, g["num_slots"], g["p"])
+    np.testing.assert_array_almost_equal(vals.real, g["real_values_multiply_result"], decimal=3)
+
+
+def test_barrett_known_answer():
+    """finite_field_test.py:51-55: Barrett(a*b) == a*b mod q for a 31-bit NTT prime."""
+    q = O.find_moduli_ntt(1, 31, 16)[0]
+    rng = np.random.default_rng(0)
+    a = rng.integers(0, q - 1, 4096, dtype=np.uint64)
+    b = rng.integers(0, q - 1, 4096, dtype=np.uint64)
+    ff = O.Barrett(q)
+    np.testing.assert_array_equal(ff.reduce((a * b)[:, None])[:, 0] % q, (a * b) % q)
+
+
+def test_moduli_search_and_roots():
+    """util.py:219-249 / 431-458 properties on the benchmark's 28-bit primes."""
+    qs = O.find_moduli_ntt(8, 28, 2 * 4096)
+    assert len(set(qs)) == 8 and all(q < 2 ** 28 and (q - 1) % 8192 == 0 for q in qs)
+    for q in qs[:2]:
+        psi = O.root_of_unity(8192, q)
+        assert pow(psi, 4096, q) == q - 1
+
+
+@pytest.mark.parametrize("n", [16, 64])
+def test_ntt_matches_schoolbook_negacyclic(n):
+    """Independent check: pre-twisted BAT NTT == bit-reversed negacyclic NTT
+    evaluated by definition (util.py:763-798)."""
+    q = O.find_moduli_ntt(1, 28, 2 * n)[0]
+    r, c = O.default_rc(n)
+    ctx = O.NTTBarrett([q], r, c)
+    rng = np.random.default_rng(1)
+    a = rng.integers(0, q, n, dtype=np.uint64)
+    psi = ctx.psi_list[0]
+    tw = (a * O.powers_mod(psi, n, q)) % q
+    out = ctx.ntt(tw.astype(U32).reshape(1, r, c, 1)).reshape(-1).astype(np.int64) % q
+    omega = psi * psi % q
+    nat = [sum(int(tw[i]) * pow(omega, i * k, q) for i in range(n)) % q for k in range(n)]
+    np.testing.assert_array_equal(out, np.array(O.bit_reverse_array(nat)))
