@@ -1,0 +1,305 @@
+"""Benchmark: CKKS HE-Mult with relinearisation at N = 2^16.
+
+Workload (one step): HEMul.mul over a batch of 64 ciphertexts with N = 2^16
+(256 x 256), L = 24 limbs of 28-bit NTT primes, K = 8 special limbs, dnum = 3;
+seeded uniform residues; evaluation keys seeded uniform.  Weak scaling: every
+rank processes its own batch of 64 (the reference shards the batch axis only).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_DEG, R, C, L, K, DNUM, BATCH = 65536, 256, 256, 24, 8, 3, 64
+METRIC = "HE-Mult/s (N=2^16, L=24, dnum=3)"
+WORKLOAD = "CKKS HE-Mult + relinearisation, N=2^16 (256x256), L=24 x 28-bit, K=8, dnum=3, batch 64 per GPU"
+
+
+def moduli():
+    from cross_b200 import util
+    ov = util.find_moduli_ntt(L + K, 28, 2 * N_DEG)
+    return ov[:L], ov[L:]
+
+
+def inputs(seed_ct: int, batch: int):
+    import numpy as np
+    Q, P = moduli()
+    rng = np.random.default_rng(seed_ct)
+    q = np.array(Q, np.uint64)
+    ct = (rng.integers(0, 2 ** 62, size=(batch, 4, R, C, L), dtype=np.uint64) % q).astype(np.uint32)
+    krng = np.random.default_rng(1)
+    ov = np.array(Q + P, np.uint64)
+    ea = (krng.integers(0, 2 ** 62, size=(DNUM, N_DEG, L + K), dtype=np.uint64) % ov).astype(np.uint32)
+    eb = (krng.integers(0, 2 ** 62, size=(DNUM, N_DEG, L + K), dtype=np.uint64) % ov).astype(np.uint32)
+    return ct, ea, eb
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[0]))
+                mx = float(r[1])
+                for n, v in zip(names, r[3:7]):
+                    if "Active" in v and "Not" not in v:
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def cpu_baseline(steps: int = 1):
+    """The oracle (numpy restatement of jaxite_word) on the host cores: one
+    ciphertext per step."""
+    import numpy as np
+    from oracle import cross_oracle as O
+    Q, P = moduli()
+    ct, ea, eb = inputs(0, 1)
+    he = O.HEMul(1, R, C, DNUM, 1, Q, P)
+    he.setup_relinearization(ea, eb)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        he.mul(ct)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": 1.0 / t, "unit": "HE-Mult/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} x 1 ciphertext of the workload (oracle/cross_oracle.py HEMul.mul, numpy BLAS threads)",
+            "seconds_per_ct": t}
+
+
+def run_reference(args):
+    """--impl reference: the oracle port of jaxite_word's HEMul.mul on the host
+    cores (all BLAS threads), W warm-up and K timed steps of one ciphertext."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cross_oracle as O
+    Q, P = moduli()
+    ct, ea, eb = inputs(0, 1)
+    he = O.HEMul(1, R, C, DNUM, 1, Q, P)
+    he.setup_relinearization(ea, eb)
+    for _ in range(args.warmup):
+        he.mul(ct)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        he.mul(ct)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    v = 1.0 / dt
+    sample = "1 ciphertext of the workload per step (oracle/cross_oracle.py HEMul.mul, numpy BLAS threads)"
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "HE-Mult/s", "n_gpus": args.gpus,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt,
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "u32 residues, u64 intermediates, u8 BAT contractions", "data": "synthetic seeded",
+                      "config": {"workload": WORKLOAD, "sample": "1 ciphertext per step"},
+                      "cpu_baseline": {"value": v, "unit": "HE-Mult/s", "cores": os.cpu_count(), "kind": "port",
+                                       "sample": sample},
+                      "e2e": {"value": v, "unit": "HE-Mult/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="cross_b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import numpy as np
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    from cross_b200 import _lib, hemul, ntt_mm
+    Q, P = moduli()
+    ct, ea, eb = inputs(100 + rank, BATCH)
+    he = hemul.HEMul(BATCH, R, C, DNUM, 1, Q, P)
+    he.control_gen(degree_layout=(R, C))
+    he.setup_relinearization(ea, eb)
+    dev = torch.device("cuda", local)
+    x = torch.from_numpy(ct).to(dev)
+    out = torch.empty((BATCH, 2, R, C, L - 1), dtype=torch.uint32, device=dev)
+    ws = torch.empty(he.workspace_size(BATCH), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        he.mul(x, out=out, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    lib = _lib.lib()
+    l0 = lib.cross_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = lib.cross_launch_count() - l0
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * BATCH * args.steps / (ms / 1000.0)
+
+    # e2e through the public API with pinned host buffers (H2D + compute + D2H).
+    hin = torch.from_numpy(ct).pin_memory()
+    hout = torch.empty(out.shape, dtype=torch.uint32).pin_memory()
+
+    def e2e_step():
+        x.copy_(hin, non_blocking=True)
+        he.mul(x, out=out, workspace=ws)
+        hout.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ems], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e = world * BATCH * args.steps / (ems / 1000.0)
+
+    # Dominant kernel: the BAT NTT (column + row contraction kernels) over the
+    # 4 x 64 x 23 limb-polynomials of the rescale NTT, timed alone.
+    ctx = ntt_mm.NTTCiphertextBarrettContext(Q[:L - 1], {"r": R, "c": C})
+    lps = BATCH * 4
+    xin = x.reshape(-1)[: lps * (L - 1) * N_DEG].reshape(lps, L - 1, R, C)   # residues < q
+    xo = torch.empty_like(xin)
+    nws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), lps, _lib.LAYOUT_LIMB_MAJOR), dtype=torch.uint8,
+                      device=dev)
+
+    def ntt_once():
+        _lib.check(lib.cross_ntt(ctx.plan(), 0, xin.data_ptr(), xo.data_ptr(), lps, _lib.LAYOUT_LIMB_MAJOR,
+                                 nws.data_ptr(), nws.numel(), stream.cuda_stream), "cross_ntt")
+
+    for _ in range(2):
+        ntt_once()
+    torch.cuda.synchronize()
+    reps = 3
+    e0.record(stream)
+    for _ in range(reps):
+        ntt_once()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ntt_ms = e0.elapsed_time(e1) / reps
+    transforms = lps * (L - 1)
+    ops = transforms * 32.0 * N_DEG * (R + C)              # int8 MAC x2 per limb-transform
+    pk, src = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]                     # TOPS: dense int8 = 2 x dense bf16 on B200
+    achieved = ops / (ntt_ms / 1000.0) / 1e12
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "HE-Mult/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u32 residues, u64 intermediates, u8 BAT contractions",
+        "data": "synthetic seeded uniform residues (no dataset in the reference)",
+        "config": {"workload": WORKLOAD, "global_batch": world * BATCH, "N": N_DEG, "r": R, "c": C, "L": L, "K": K,
+                   "dnum": DNUM, "parallelism": f"batch-sharded x{world}",
+                   "l2": "inputs 1.6 GB per GPU, larger than L2 (no flush needed)"},
+        "e2e": {"value": e2e, "unit": "HE-Mult/s", "h2d_bytes_per_step": int(hin.numel() * 4),
+                "d2h_bytes_per_step": int(hout.numel() * 4)},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "roofline": {"kernel": "BAT NTT forward (column + row contraction kernels), 23 limbs x 256 polys",
+                     "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
+                     "frac": achieved / int8_peak, "traffic": None,
+                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); no int8 measurement on this pool",
+                     "ms_per_launch": ntt_ms, "algorithmic_ops_per_launch": ops},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = {k: v for k, v in cpu_baseline(1).items() if k != "seconds_per_ct"}
+        except Exception as exc:  # noqa: BLE001
+            line["cpu_baseline"] = {"error": str(exc)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    del np
+
+
+if __name__ == "__main__":
+    main()

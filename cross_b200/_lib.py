@@ -1,0 +1,121 @@
+"""ctypes binding of libcross_b200.so (the C ABI declared in include/cross_b200.h).
+
+The library is built in-tree by ``cross_b200.build`` (or
+``__graft_entry__.build()``).  There is no fallback: importing an operator
+without the library, or without a CUDA device, raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libcross_b200.so")
+
+LAYOUT_REFERENCE = 0
+LAYOUT_LIMB_MAJOR = 1
+
+_STATUS = {-1: ValueError, -2: RuntimeError, -3: NotImplementedError, -4: MemoryError, -5: TimeoutError}
+
+vp = C.c_void_p
+i32 = C.c_int
+i64 = C.c_int64
+sz = C.c_size_t
+
+
+class HemulDesc(C.Structure):
+    _fields_ = [("r", i32), ("c", i32), ("L", i32), ("K", i32), ("dnum", i32),
+                ("ntt_qp", vp), ("ntt_p", vp), ("ntt_p_limb_offset", i32),
+                ("ks_bconv", C.POINTER(vp)), ("down_bconv", vp),
+                ("inv_psi_last", vp), ("gamma_psi", vp), ("betas", vp), ("inv_psi_q", vp),
+                ("psi_qp", vp), ("inv_psi_p", vp), ("p_inv_mod_q", vp)]
+
+
+class RescaleDesc(C.Structure):
+    _fields_ = [("r", i32), ("c", i32), ("L", i32), ("ntt_q", vp),
+                ("inv_psi_last", vp), ("gamma_psi", vp), ("betas", vp)]
+
+
+class HerotDesc(C.Structure):
+    _fields_ = [("r", i32), ("c", i32), ("L", i32), ("K", i32), ("dnum", i32),
+                ("ntt_qp", vp), ("ks_bconv", C.POINTER(vp)), ("down_bconv", vp),
+                ("inv_psi_q", vp), ("psi_qp", vp), ("inv_psi_p", vp), ("p_inv_mod_q", vp)]
+
+
+_SIGS = {
+    "cross_abi_version": (i32, []),
+    "cross_last_error": (C.c_char_p, []),
+    "cross_launch_count": (C.c_uint64, []),
+    "cross_moduli_create": (i32, [i32, vp, vp, vp, vp, C.POINTER(vp)]),
+    "cross_moduli_destroy": (i32, [vp]),
+    "cross_mod_reduce": (i32, [vp, vp, i32, vp, i64, vp]),
+    "cross_modmul": (i32, [vp, vp, i32, vp, i32, i64, vp, i64, vp]),
+    "cross_tensor_product": (i32, [vp, vp, vp, vp, i64, i64, vp]),
+    "cross_add_mod": (i32, [vp, vp, vp, vp, i64, i64, vp]),
+    "cross_automorphism": (i32, [vp, vp, vp, i64, i64, i32, vp]),
+    "cross_to_limb_major": (i32, [vp, vp, i64, i64, i32, vp]),
+    "cross_to_reference": (i32, [vp, vp, i64, i64, i32, vp]),
+    "cross_ntt_plan_create": (i32, [vp, i32, i32, vp, vp, vp, vp, vp, vp, C.POINTER(vp)]),
+    "cross_ntt_plan_destroy": (i32, [vp]),
+    "cross_ntt_workspace_size": (sz, [vp, i64, i32]),
+    "cross_ntt": (i32, [vp, i32, vp, vp, i64, i32, vp, sz, vp]),
+    "cross_bconv_plan_create": (i32, [vp, vp, vp, vp, vp, C.POINTER(vp)]),
+    "cross_bconv_plan_destroy": (i32, [vp]),
+    "cross_bconv": (i32, [vp, i32, vp, vp, i64, i64, i32, vp]),
+    "cross_rescale_plan_create": (i32, [C.POINTER(RescaleDesc), C.POINTER(vp)]),
+    "cross_rescale_plan_destroy": (i32, [vp]),
+    "cross_rescale_workspace_size": (sz, [vp, i64, i32]),
+    "cross_rescale": (i32, [vp, vp, vp, i64, i32, vp, sz, vp]),
+    "cross_hemul_plan_create": (i32, [C.POINTER(HemulDesc), C.POINTER(vp)]),
+    "cross_hemul_set_keys": (i32, [vp, vp, vp, i32]),
+    "cross_hemul_plan_destroy": (i32, [vp]),
+    "cross_hemul_workspace_size": (sz, [vp, i64, i32]),
+    "cross_hemul": (i32, [vp, vp, vp, i64, i32, vp, sz, vp]),
+    "cross_herot_plan_create": (i32, [C.POINTER(HerotDesc), C.POINTER(vp)]),
+    "cross_herot_set_keys": (i32, [vp, vp, vp, vp]),
+    "cross_herot_plan_destroy": (i32, [vp]),
+    "cross_herot_workspace_size": (sz, [vp, i64, i32]),
+    "cross_herot": (i32, [vp, vp, vp, i64, i32, vp, sz, vp]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load libcross_b200.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m cross_b200.build` "
+                "(there is no CPU fallback for the CROSS operators)")
+        h = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(h, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = h
+    return _lib
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def check(rc: int, what: str = ""):
+    """Raise the reference-style Python exception for a nonzero status."""
+    if rc != 0:
+        msg = lib().cross_last_error().decode(errors="replace")
+        raise _STATUS.get(rc, RuntimeError)(f"{what}: {msg}" if what else msg)
+
+
+def ptr(a) -> int:
+    """Raw device/host address of a torch tensor or numpy array."""
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+def cuda_stream():
+    import torch
+    return torch.cuda.current_stream().cuda_stream

@@ -1,0 +1,246 @@
+// Elementwise modular kernels: Barrett reduction, modmul with broadcast
+// tables, the HE tensor product, modular add, the Galois permutation and the
+// layout conversions.  All are HBM-bound; indices are 64-bit.
+#include "internal.hpp"
+
+namespace cross {
+
+namespace {
+
+constexpr int EW_THREADS = 256;
+
+unsigned ew_blocks(int64_t n, int per_thread = 1) {
+  int64_t b = (n + (int64_t)EW_THREADS * per_thread - 1) / ((int64_t)EW_THREADS * per_thread);
+  if (b < 1) b = 1;
+  return (unsigned)(b > (1 << 30) ? (1 << 30) : b);
+}
+
+template <bool U64IN>
+__global__ void k_mod_reduce(const void* __restrict__ in, uint32_t* __restrict__ out, int64_t total,
+                             int M, const ModC* __restrict__ mods) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t z = U64IN ? ((const uint64_t*)in)[i] : (uint64_t)((const uint32_t*)in)[i];
+    out[i] = barrett_any(z, mods[i % M]);
+  }
+}
+
+__global__ void k_modmul_ref(const void* __restrict__ a, int a64, const void* __restrict__ b, int b64,
+                             int64_t b_rows, uint32_t* __restrict__ out, int64_t total, int M,
+                             const ModC* __restrict__ mods) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i % M);
+    const int64_t row = i / M;
+    const int64_t bi = (row % b_rows) * M + m;
+    const uint64_t x = a64 ? ((const uint64_t*)a)[i] : (uint64_t)((const uint32_t*)a)[i];
+    const uint64_t y = b64 ? ((const uint64_t*)b)[bi] : (uint64_t)((const uint32_t*)b)[bi];
+    out[i] = barrett_any(x * y, mods[m]);
+  }
+}
+
+// ciphertext.py:309-324 on (batch, 4, n, M): elements a0, a1, b0, b1.
+__global__ void k_tensor_ref(const uint32_t* __restrict__ ct, uint32_t* __restrict__ o01,
+                             uint32_t* __restrict__ o2, int64_t batch, int64_t per, int M,
+                             const ModC* __restrict__ mods) {
+  const int64_t total = batch * per;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / per, t = i % per;
+    const ModC mc = mods[t % M];
+    const uint32_t* base = ct + b * 4 * per + t;
+    const uint64_t a0 = base[0], a1 = base[per], b0 = base[2 * per], b1 = base[3 * per];
+    o01[b * 2 * per + t] = barrett_any(a0 * b0, mc);
+    o01[b * 2 * per + per + t] = barrett_any(a0 * b1 + a1 * b0, mc);
+    o2[b * per + t] = barrett_any(a1 * b1, mc);
+  }
+}
+
+// add.py:7-27 on (E, M, n): result = a + b; result > q ? result - q : result.
+__global__ void k_add_mod(const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                          uint32_t* __restrict__ out, int64_t total, int64_t n, int M,
+                          const ModC* __restrict__ mods) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t q = (uint32_t)mods[(i / n) % M].q;
+    const uint32_t s = a[i] + b[i];
+    out[i] = s > q ? s - q : s;
+  }
+}
+
+// herot.py:300 jnp.take(x, coef_map, axis=2) on (polys, n, M): row gather.
+__global__ void k_gather_rows(const uint32_t* __restrict__ in, const int32_t* __restrict__ map,
+                              uint32_t* __restrict__ out, int64_t polys, int64_t n, int M) {
+  const int64_t total = polys * n * M;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i % M);
+    const int64_t row = i / M;
+    const int64_t p = row / n, j = row % n;
+    int64_t src = map[j];
+    // jnp.take's default mode: negative indices count from the end and any
+    // index still outside [0, n) yields the fill value (UINT32_MAX).
+    if (src < 0) src += n;
+    out[i] = (src < 0 || src >= n) ? 0xFFFFFFFFu : in[(p * n + src) * M + m];
+  }
+}
+
+// Batched transpose (batch, rows, cols) -> (batch, cols, rows) through a
+// 32x33 shared tile (coalesced on both sides).
+__global__ void k_transpose(const uint32_t* __restrict__ in, uint32_t* __restrict__ out, int64_t rows,
+                            int64_t cols) {
+  __shared__ uint32_t tile[32][33];
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  const uint32_t* src = in + b * rows * cols;
+  uint32_t* dst = out + b * rows * cols;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = src[r * cols + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[c * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+// y = Barrett(x * tab[row]) over strided limb-polynomials, 4 words per thread.
+__global__ void k_modmul_table_lm(LP x, LPo y, int64_t lps, int slots, int64_t n,
+                                  const uint32_t* __restrict__ tab, const uint16_t* __restrict__ trow,
+                                  const ModC* __restrict__ mods, const uint16_t* __restrict__ midx) {
+  const int64_t nv = n >> 2;
+  for (int64_t lp = blockIdx.y; lp < lps; lp += gridDim.y) {
+    const int64_t poly = lp / slots;
+    const int slot = (int)(lp % slots);
+    const ModC mc = mods[midx[slot]];
+    const uint4* xs = (const uint4*)(x.p + poly * x.ps + slot * x.ss);
+    uint4* ys = (uint4*)(y.p + poly * y.ps + slot * y.ss);
+    const uint4* ts = (const uint4*)(tab + (size_t)trow[slot] * n);
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 a = xs[v], t = ts[v];
+      uint4 o;
+      o.x = barrett_any((uint64_t)a.x * t.x, mc);
+      o.y = barrett_any((uint64_t)a.y * t.y, mc);
+      o.z = barrett_any((uint64_t)a.z * t.z, mc);
+      o.w = barrett_any((uint64_t)a.w * t.w, mc);
+      ys[v] = o;
+    }
+  }
+}
+
+}  // namespace
+
+int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows, int64_t cols,
+                  cudaStream_t st) {
+  if (batch == 0 || rows == 0 || cols == 0) return CROSS_OK;
+  if ((rows + 31) / 32 > 65535 || (cols + 31) / 32 > (int64_t)1 << 30) {
+    set_error("transpose: %lld x %lld matrix exceeds the launch grid", (long long)rows, (long long)cols);
+    return CROSS_ERR_UNSUPPORTED;
+  }
+  dim3 blk(32, 8);
+  for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
+    const int64_t nb = batch - b0 < 65535 ? batch - b0 : 65535;
+    dim3 grd((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)nb);
+    k_transpose<<<grd, blk, 0, st>>>(in + b0 * rows * cols, out + b0 * rows * cols, rows, cols); count_launch();
+  }
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int modmul_table_lm(LP x, LPo y, int64_t polys, int slots, int64_t n, const uint32_t* tab,
+                    const uint16_t* trow, const ModC* mods, const uint16_t* midx, cudaStream_t st) {
+  const int64_t lps = polys * slots;
+  if (lps == 0) return CROSS_OK;
+  if (n % 4) {
+    set_error("modmul_table_lm: n=%lld must be a multiple of 4", (long long)n);
+    return CROSS_ERR_UNSUPPORTED;
+  }
+  const int64_t nv = n / 4;
+  unsigned gx = (unsigned)((nv + EW_THREADS - 1) / EW_THREADS);
+  if (gx > 64) gx = 64;
+  dim3 grd(gx, (unsigned)(lps < 65535 ? lps : 65535));
+  k_modmul_table_lm<<<grd, EW_THREADS, 0, st>>>(x, y, lps, slots, n, tab, trow, mods, midx); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+}  // namespace cross
+
+using namespace cross;
+
+extern "C" {
+
+int cross_mod_reduce(cross_moduli mods, const void* in, int in_is_u64, uint32_t* out, int64_t rows,
+                     void* stream) {
+  CROSS_REQUIRE(mods && in && out && rows >= 0, "cross_mod_reduce: bad argument");
+  const int64_t total = rows * mods->n;
+  if (total == 0) return CROSS_OK;
+  if (in_is_u64) {
+    k_mod_reduce<true><<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, out, total, mods->n, mods->dev);
+  } else {
+    k_mod_reduce<false><<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, out, total, mods->n, mods->dev);
+  }
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_modmul(cross_moduli mods, const void* a, int a_is_u64, const void* b, int b_is_u64,
+                 int64_t b_rows, uint32_t* out, int64_t rows, void* stream) {
+  CROSS_REQUIRE(mods && a && b && out && rows >= 0 && b_rows >= 1, "cross_modmul: bad argument");
+  const int64_t total = rows * mods->n;
+  if (total == 0) return CROSS_OK;
+  k_modmul_ref<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, a_is_u64, b, b_is_u64, b_rows, out,
+                                                                            total, mods->n, mods->dev); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_tensor_product(cross_moduli mods, const uint32_t* ct, uint32_t* out01, uint32_t* out2,
+                         int64_t batch, int64_t n, void* stream) {
+  CROSS_REQUIRE(mods && ct && out01 && out2 && batch >= 0 && n >= 0, "cross_tensor_product: bad argument");
+  const int64_t per = n * mods->n;
+  if (batch * per == 0) return CROSS_OK;
+  k_tensor_ref<<<ew_blocks(batch * per, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(ct, out01, out2, batch, per,
+                                                                                  mods->n, mods->dev); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_add_mod(cross_moduli mods, const uint32_t* a, const uint32_t* b, uint32_t* out, int64_t elements,
+                  int64_t n, void* stream) {
+  CROSS_REQUIRE(mods && a && b && out && elements >= 0 && n >= 0, "cross_add_mod: bad argument");
+  const int64_t total = elements * mods->n * n;
+  if (total == 0) return CROSS_OK;
+  k_add_mod<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, b, out, total, n, mods->n, mods->dev); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_automorphism(const uint32_t* in, const int32_t* coef_map, uint32_t* out, int64_t polys, int64_t n,
+                       int num_limbs, void* stream) {
+  CROSS_REQUIRE(in && coef_map && out && polys >= 0 && n > 0 && num_limbs > 0 && in != out,
+                "cross_automorphism: bad argument (in and out must differ)");
+  const int64_t total = polys * n * num_limbs;
+  if (total == 0) return CROSS_OK;
+  k_gather_rows<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, coef_map, out, polys, n, num_limbs); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_to_limb_major(const uint32_t* in, uint32_t* out, int64_t polys, int64_t n, int num_limbs,
+                        void* stream) {
+  CROSS_REQUIRE(in && out && in != out && polys >= 0 && n > 0 && num_limbs > 0,
+                "cross_to_limb_major: bad argument (in and out must differ)");
+  return transpose_u32(in, out, polys, n, num_limbs, (cudaStream_t)stream);
+}
+
+int cross_to_reference(const uint32_t* in, uint32_t* out, int64_t polys, int64_t n, int num_limbs,
+                       void* stream) {
+  CROSS_REQUIRE(in && out && in != out && polys >= 0 && n > 0 && num_limbs > 0,
+                "cross_to_reference: bad argument (in and out must differ)");
+  return transpose_u32(in, out, polys, num_limbs, n, (cudaStream_t)stream);
+}
+
+}  // extern "C"

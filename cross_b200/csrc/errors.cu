@@ -1,0 +1,89 @@
+// Error state, device-memory helpers and the modulus-set entry points.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "internal.hpp"
+
+namespace cross {
+
+static thread_local char g_err[512] = "";
+static std::atomic<uint64_t> g_launches{0};
+
+void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int fail_cuda(cudaError_t e, const char* where) {
+  set_error("CUDA error %d (%s) at %s", (int)e, cudaGetErrorString(e), where);
+  return CROSS_ERR_CUDA;
+}
+
+template <class T>
+int upload(T** dst, const T* src, size_t count) {
+  *dst = nullptr;
+  if (count == 0) return CROSS_OK;
+  CROSS_CHECK_CUDA(cudaMalloc((void**)dst, count * sizeof(T)));
+  CROSS_CHECK_CUDA(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
+  return CROSS_OK;
+}
+template int upload<uint32_t>(uint32_t**, const uint32_t*, size_t);
+template int upload<uint16_t>(uint16_t**, const uint16_t*, size_t);
+template int upload<int16_t>(int16_t**, const int16_t*, size_t);
+template int upload<int32_t>(int32_t**, const int32_t*, size_t);
+template int upload<ModC>(ModC**, const ModC*, size_t);
+
+void dfree(void* p) {
+  if (p) cudaFree(p);
+}
+
+}  // namespace cross
+
+extern "C" {
+
+int cross_abi_version(void) { return CROSS_B200_ABI_VERSION; }
+
+const char* cross_last_error(void) { return cross::g_err; }
+
+uint64_t cross_launch_count(void) { return cross::g_launches.load(std::memory_order_relaxed); }
+
+int cross_moduli_create(int num_moduli, const uint32_t* moduli, const uint64_t* barrett_m,
+                        const uint32_t* barrett_w, const uint32_t* barrett_s_w, cross_moduli* out) {
+  CROSS_REQUIRE(out && moduli && barrett_m && barrett_w && barrett_s_w && num_moduli > 0,
+                "cross_moduli_create: null argument or num_moduli <= 0");
+  *out = nullptr;
+  auto* s = new cross_moduli_s();
+  s->n = num_moduli;
+  for (int i = 0; i < num_moduli; ++i) {
+    if (moduli[i] < 3 || (moduli[i] & 1u) == 0 || moduli[i] >= (1u << 31) || barrett_w[i] > 32 ||
+        barrett_s_w[i] > 63) {
+      cross::set_error("cross_moduli_create: modulus %u (index %d) must be odd, in [3, 2^31)",
+                       moduli[i], i);
+      delete s;
+      return CROSS_ERR_INVALID_ARG;
+    }
+    s->host.push_back(cross::ModC{moduli[i], barrett_m[i], barrett_w[i], barrett_s_w[i]});
+  }
+  int rc = cross::upload_vec(&s->dev, s->host);
+  if (rc) {
+    delete s;
+    return rc;
+  }
+  *out = s;
+  return CROSS_OK;
+}
+
+int cross_moduli_destroy(cross_moduli m) {
+  if (!m) return CROSS_OK;
+  cross::dfree(m->dev);
+  delete m;
+  return CROSS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,875 @@
+// HE-Mult with relinearisation (hemul.py:153-217) and HE-Rotate
+// (herot.py:183-302) as one stream of kernels over a limb-major workspace.
+//
+// Internal layout: every limb-polynomial is a contiguous run of N = r*c
+// uint32 words; a ciphertext element is [limb][N].  The reference layout
+// (..., r, c, limbs) is converted at entry and exit only.
+#include <algorithm>
+#include <vector>
+
+#include "internal.hpp"
+
+namespace cross {
+
+namespace {
+
+constexpr int MAXPARTS = 16;
+constexpr int T = 256;
+
+struct PartPtrs {
+  const uint32_t* e[MAXPARTS];   // E_j base
+  int64_t ps[MAXPARTS];          // E_j poly stride (words)
+};
+
+unsigned gx_for(int64_t nv) {
+  int64_t g = (nv + T - 1) / T;
+  return (unsigned)(g < 1 ? 1 : (g > 64 ? 64 : g));
+}
+unsigned gy_for(int64_t rows) { return (unsigned)(rows < 65535 ? rows : 65535); }
+
+// ciphertext.py:279-295: centred lift of the last limb into every q_i,
+// times gamma_i psi_i^t, Barrett.  LL: [polys][N]; out: [polys][L1][N].
+__global__ void k_rescale_lift(const uint32_t* __restrict__ LL, uint32_t* __restrict__ out, int64_t polys,
+                               int L1, int64_t n, uint32_t thr, uint32_t q_last,
+                               const uint32_t* __restrict__ gpsi, const ModC* __restrict__ mods) {
+  const int64_t nv = n >> 2, rows = polys * L1;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t p = row / L1;
+    const int i = (int)(row % L1);
+    const ModC mc = mods[i];
+    const uint4* src = (const uint4*)(LL + p * n);
+    const uint4* g = (const uint4*)(gpsi + (size_t)i * n);
+    uint4* dst = (uint4*)(out + row * n);
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 x = src[v], t = g[v];
+      auto lift = [&](uint32_t a) -> uint64_t {
+        return a < thr ? (uint64_t)a : (mc.q - (uint64_t)q_last + (uint64_t)a);
+      };
+      uint4 o;
+      o.x = barrett_any(lift(x.x) * t.x, mc);
+      o.y = barrett_any(lift(x.y) * t.y, mc);
+      o.z = barrett_any(lift(x.z) * t.z, mc);
+      o.w = barrett_any(lift(x.w) * t.w, mc);
+      dst[v] = o;
+    }
+  }
+}
+
+// ciphertext.py:299-302: out = Barrett(x * beta_i + y).
+__global__ void k_rescale_combine(LP x, LP y, LPo out, int64_t polys, int L1, int64_t n,
+                                  const uint32_t* __restrict__ betas, const ModC* __restrict__ mods) {
+  const int64_t nv = n >> 2, rows = polys * L1;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t p = row / L1;
+    const int i = (int)(row % L1);
+    const ModC mc = mods[i];
+    const uint64_t beta = betas[i];
+    const uint4* xs = (const uint4*)(x.p + p * x.ps + i * x.ss);
+    const uint4* ys = (const uint4*)(y.p + p * y.ps + i * y.ss);
+    uint4* os = (uint4*)(out.p + p * out.ps + i * out.ss);
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 a = xs[v], b = ys[v];
+      uint4 o;
+      o.x = barrett_any(a.x * beta + b.x, mc);
+      o.y = barrett_any(a.y * beta + b.y, mc);
+      o.z = barrett_any(a.z * beta + b.z, mc);
+      o.w = barrett_any(a.w * beta + b.w, mc);
+      os[v] = o;
+    }
+  }
+}
+
+// ciphertext.py:309-324 on [b][4][L1][N] -> D [b][3][L1][N].
+__global__ void k_tensor_lm(const uint32_t* __restrict__ R, uint32_t* __restrict__ D, int64_t batch, int L1,
+                            int64_t n, const ModC* __restrict__ mods) {
+  const int64_t nv = n >> 2, rows = batch * L1, es = (int64_t)L1 * n;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t b = row / L1;
+    const int i = (int)(row % L1);
+    const ModC mc = mods[i];
+    const uint32_t* base = R + b * 4 * es + (int64_t)i * n;
+    uint32_t* ob = D + b * 3 * es + (int64_t)i * n;
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 a0 = ((const uint4*)base)[v], a1 = ((const uint4*)(base + es))[v];
+      const uint4 b0 = ((const uint4*)(base + 2 * es))[v], b1 = ((const uint4*)(base + 3 * es))[v];
+      uint4 d0, d1, d2;
+#define TP(c)                                                                   \
+  d0.c = barrett_any((uint64_t)a0.c * b0.c, mc);                                \
+  d1.c = barrett_any((uint64_t)a0.c * b1.c + (uint64_t)a1.c * b0.c, mc);        \
+  d2.c = barrett_any((uint64_t)a1.c * b1.c, mc);
+      TP(x) TP(y) TP(z) TP(w)
+#undef TP
+      ((uint4*)ob)[v] = d0;
+      ((uint4*)(ob + es))[v] = d1;
+      ((uint4*)(ob + 2 * es))[v] = d2;
+    }
+  }
+}
+
+// Hybrid key-switch inner product (ciphertext.py:486-518, herot.py:212-247):
+// for every limb l of Q'+P, ext_j(l) is the NTT-form input limb when l is in
+// digit j and the ModUp result otherwise; acc0 = sum_j ext_j * evk_b[j],
+// acc1 = sum_j ext_j * evk_a[j] in uint64, then Barrett.
+__global__ void k_ks_inner(LP dig, PartPtrs parts, int nparts, const int16_t* __restrict__ src, int LT,
+                           int64_t n, int64_t batch, const uint32_t* __restrict__ evka,
+                           const uint32_t* __restrict__ evkb, uint32_t* __restrict__ KS,
+                           const ModC* __restrict__ mods) {
+  const int64_t nv = n >> 2, rows = batch * LT;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t b = row / LT;
+    const int l = (int)(row % LT);
+    const ModC mc = mods[l];
+    uint4* o0 = (uint4*)(KS + (b * 2 * LT + l) * n);
+    uint4* o1 = (uint4*)(KS + (b * 2 * LT + LT + l) * n);
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      uint64_t s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+      for (int j = 0; j < nparts; ++j) {
+        const int s = src[j * LT + l];
+        const uint4 e = s < 0 ? ((const uint4*)(dig.p + b * dig.ps + (int64_t)l * dig.ss))[v]
+                              : ((const uint4*)(parts.e[j] + b * parts.ps[j] + (int64_t)s * n))[v];
+        const uint4 kb = ((const uint4*)(evkb + ((size_t)j * LT + l) * n))[v];
+        const uint4 ka = ((const uint4*)(evka + ((size_t)j * LT + l) * n))[v];
+        s0[0] += (uint64_t)e.x * kb.x; s0[1] += (uint64_t)e.y * kb.y;
+        s0[2] += (uint64_t)e.z * kb.z; s0[3] += (uint64_t)e.w * kb.w;
+        s1[0] += (uint64_t)e.x * ka.x; s1[1] += (uint64_t)e.y * ka.y;
+        s1[2] += (uint64_t)e.z * ka.z; s1[3] += (uint64_t)e.w * ka.w;
+      }
+      o0[v] = make_uint4(barrett_any(s0[0], mc), barrett_any(s0[1], mc), barrett_any(s0[2], mc), barrett_any(s0[3], mc));
+      o1[v] = make_uint4(barrett_any(s1[0], mc), barrett_any(s1[1], mc), barrett_any(s1[2], mc), barrett_any(s1[3], mc));
+    }
+  }
+}
+
+// ModDown tail + final add (hemul.py:198-215, herot.py:276-296):
+//   sub = a < g ? a + q - g : a - g   (uint32 wrap)
+//   v   = Barrett(sub * P^{-1} mod q)
+//   res = base + v ; res >= q ? res - q : res     (when base is given)
+// a = KS[b][e][i], g = G[b][e][i], base = B[b][e][i] (or none).
+__global__ void k_moddown_final(LP A, int64_t a_es, LP G, int64_t g_es, LP Bs, int64_t b_es, int has_base_e0,
+                                int has_base_e1, LPo O, int64_t o_es, int64_t batch, int L1, int64_t n,
+                                const uint32_t* __restrict__ pinv, const ModC* __restrict__ mods) {
+  const int64_t nv = n >> 2, rows = batch * 2 * L1;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t be = row / L1;
+    const int i = (int)(row % L1);
+    const int64_t b = be / 2;
+    const int e = (int)(be % 2);
+    const ModC mc = mods[i];
+    const uint32_t q = (uint32_t)mc.q;
+    const uint64_t pi = pinv[i];
+    const bool add = e == 0 ? has_base_e0 : has_base_e1;
+    const uint4* as = (const uint4*)(A.p + b * A.ps + e * a_es + i * A.ss);
+    const uint4* gs = (const uint4*)(G.p + b * G.ps + e * g_es + i * G.ss);
+    const uint4* bs = (const uint4*)(Bs.p + b * Bs.ps + e * b_es + i * Bs.ss);
+    uint4* os = (uint4*)(O.p + b * O.ps + e * o_es + i * O.ss);
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 a = as[v], g = gs[v];
+      uint4 base = add ? bs[v] : make_uint4(0, 0, 0, 0);
+      auto f = [&](uint32_t x, uint32_t y, uint32_t bb) -> uint32_t {
+        const uint32_t sub = x < y ? x + q - y : x - y;
+        const uint32_t t = barrett_any((uint64_t)sub * pi, mc);
+        if (!add) return t;
+        const uint32_t s = bb + t;
+        return s >= q ? s - q : s;
+      };
+      os[v] = make_uint4(f(a.x, g.x, base.x), f(a.y, g.y, base.y), f(a.z, g.z, base.z), f(a.w, g.w, base.w));
+    }
+  }
+}
+
+// out[p][l][j] = in[p][l][map[j]] (limb-major automorphism, jnp.take semantics).
+__global__ void k_gather_lm(const uint32_t* __restrict__ in, const int32_t* __restrict__ map,
+                            uint32_t* __restrict__ out, int64_t rows, int64_t n) {
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
+      int64_t s = map[j];
+      if (s < 0) s += n;
+      out[row * n + j] = (s < 0 || s >= n) ? 0xFFFFFFFFu : in[row * n + s];
+    }
+  }
+}
+
+bool same_q(const ModC& a, const ModC& b) { return a.q == b.q && a.m == b.m && a.w == b.w && a.s_w == b.s_w; }
+
+// Rescale by the last prime (ciphertext.py:267-303) on `polys` limb-major
+// polynomials: X has L limbs per poly (stride xps), R receives L-1 limbs
+// (stride L1*N).  plan covers at least the L moduli of Q at indices 0..L-1
+// (m_last = {L-1}, m_q1 = 0..L-2); mods_q1 are the Barrett constants of Q'.
+struct RescaleArgs {
+  const cross_ntt_plan_s* ntt;
+  const uint16_t* m_last;
+  const uint16_t* m_zero;
+  const uint16_t* m_q1;
+  const ModC* mods_q1;
+  const uint32_t* inv_psi_last;
+  const uint32_t* gamma_psi;
+  const uint32_t* betas;
+  uint32_t thr, q_last;
+  int L;
+  int64_t N;
+};
+
+int rescale_run(const RescaleArgs& a, const uint32_t* X, int64_t xps, uint32_t* R, uint32_t* LL, uint32_t* tmp,
+                int64_t polys, cudaStream_t st) {
+  const int L1 = a.L - 1;
+  const int64_t N = a.N, nv = N / 4;
+  int rc;
+  if ((rc = ntt_run(a.ntt, true, LP{X + (int64_t)L1 * N, xps, 0}, LPo{LL, N, 0}, polys, 1, a.m_last, tmp, st)))
+    return rc;
+  if ((rc = modmul_table_lm(LP{LL, N, 0}, LPo{LL, N, 0}, polys, 1, N, a.inv_psi_last, a.m_zero, a.ntt->mods,
+                            a.m_last, st)))
+    return rc;
+  k_rescale_lift<<<dim3(gx_for(nv), gy_for(polys * L1)), T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last,
+                                                                      a.gamma_psi, a.mods_q1); count_launch();
+  if ((rc = ntt_run(a.ntt, false, LP{R, (int64_t)L1 * N, N}, LPo{R, (int64_t)L1 * N, N}, polys, L1, a.m_q1, tmp, st)))
+    return rc;
+  k_rescale_combine<<<dim3(gx_for(nv), gy_for(polys * L1)), T, 0, st>>>(
+      LP{X, xps, N}, LP{R, (int64_t)L1 * N, N}, LPo{R, (int64_t)L1 * N, N}, polys, L1, N, a.betas, a.mods_q1); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+}  // namespace
+}  // namespace cross
+
+using namespace cross;
+
+// ---------------------------------------------------------------------------
+// HE-Mult
+// ---------------------------------------------------------------------------
+
+struct cross_hemul_plan_s {
+  int r = 0, c = 0, L = 0, L1 = 0, K = 0, dnum = 0, alpha = 0, parts = 0;
+  int64_t N = 0;
+  cross_ntt_plan_s* ntt_qp = nullptr;
+  cross_ntt_plan_s* ntt_p = nullptr;
+  int p_off = 0;
+  std::vector<cross_bconv_plan_s*> ks_bconv;
+  cross_bconv_plan_s* down = nullptr;
+  std::vector<int> dstart, dlen;
+  std::vector<std::vector<int>> comp;   // complement, indices in Q'+P
+  uint32_t thr = 0, q_last = 0;
+  // device
+  uint32_t *inv_psi_last = nullptr, *gamma_psi = nullptr, *inv_psi_q = nullptr, *psi_qp = nullptr,
+           *inv_psi_p = nullptr, *betas = nullptr, *pinv = nullptr;
+  ModC* mods_dle = nullptr;
+  uint16_t *m_last = nullptr, *m_zero = nullptr, *seq = nullptr, *m_p_plan = nullptr, *m_p_dle = nullptr,
+           *m_q1_plan = nullptr;
+  std::vector<uint16_t*> comp_plan, comp_dle;
+  std::vector<uint16_t*> dig_plan;      // digit limbs as plan indices (unused by kernels, kept for checks)
+  int16_t* ks_src = nullptr;
+  uint32_t *evk_a = nullptr, *evk_b = nullptr;
+};
+
+namespace {
+
+struct HemulBufs {
+  uint32_t *X, *LL, *R, *D, *Cc, *KS, *KP, *F, *tmp, *O;
+  std::vector<uint32_t*> E;
+};
+
+void hemul_layout(const cross_hemul_plan_s* P, int64_t B, int layout, Arena& a, HemulBufs& b) {
+  const int64_t N = P->N;
+  const int L = P->L, L1 = P->L1, K = P->K;
+  b.X = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)B * 4 * L * N) : nullptr;
+  b.LL = a.take<uint32_t>((size_t)B * 4 * N);
+  b.R = a.take<uint32_t>((size_t)B * 4 * L1 * N);
+  b.D = a.take<uint32_t>((size_t)B * 3 * L1 * N);
+  b.Cc = a.take<uint32_t>((size_t)B * L1 * N);
+  b.E.clear();
+  for (int j = 0; j < P->parts; ++j) b.E.push_back(a.take<uint32_t>((size_t)B * (L1 + K - P->dlen[j]) * N));
+  b.KS = a.take<uint32_t>((size_t)B * 2 * (L1 + K) * N);
+  b.KP = a.take<uint32_t>((size_t)B * 2 * K * N);
+  b.F = a.take<uint32_t>((size_t)B * 2 * L1 * N);
+  b.O = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)B * 2 * L1 * N) : nullptr;
+  int64_t tmpw = B * 4 * L1;
+  for (int j = 0; j < P->parts; ++j) tmpw = std::max<int64_t>(tmpw, B * (L1 + K - P->dlen[j]));
+  tmpw = std::max<int64_t>(tmpw, B * 2 * K);
+  b.tmp = a.take<uint32_t>((size_t)tmpw * N);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cross_hemul_plan_destroy(cross_hemul_plan P) {
+  if (!P) return CROSS_OK;
+  for (void* p : {(void*)P->inv_psi_last, (void*)P->gamma_psi, (void*)P->inv_psi_q, (void*)P->psi_qp,
+                  (void*)P->inv_psi_p, (void*)P->betas, (void*)P->pinv, (void*)P->mods_dle, (void*)P->m_last,
+                  (void*)P->m_zero, (void*)P->seq, (void*)P->m_p_plan, (void*)P->m_p_dle, (void*)P->m_q1_plan,
+                  (void*)P->ks_src, (void*)P->evk_a, (void*)P->evk_b})
+    dfree(p);
+  for (auto* p : P->comp_plan) dfree(p);
+  for (auto* p : P->comp_dle) dfree(p);
+  for (auto* p : P->dig_plan) dfree(p);
+  delete P;
+  return CROSS_OK;
+}
+
+int cross_hemul_plan_create(const cross_hemul_desc* d, cross_hemul_plan* out) {
+  CROSS_REQUIRE(d && out, "cross_hemul_plan_create: null argument");
+  *out = nullptr;
+  CROSS_REQUIRE(d->L >= 2 && d->K >= 1 && d->dnum >= 1 && d->r >= 1 && d->c >= 1,
+                "cross_hemul_plan_create: need L >= 2, K >= 1, dnum >= 1");
+  CROSS_REQUIRE(d->ntt_qp && d->ntt_p && d->ks_bconv && d->down_bconv && d->inv_psi_last && d->gamma_psi &&
+                    d->betas && d->inv_psi_q && d->psi_qp && d->inv_psi_p && d->p_inv_mod_q,
+                "cross_hemul_plan_create: null table or plan");
+  const int L = d->L, L1 = L - 1, K = d->K;
+  const int64_t N = (int64_t)d->r * d->c;
+  CROSS_REQUIRE(N % 4 == 0, "cross_hemul_plan_create: N=%lld must be a multiple of 4", (long long)N);
+  CROSS_REQUIRE(d->ntt_qp->M == L + K && (int64_t)d->ntt_qp->r * d->ntt_qp->c == N,
+                "cross_hemul_plan_create: ntt_qp must cover L+K=%d limbs of N=%lld", L + K, (long long)N);
+  CROSS_REQUIRE(d->ntt_p->M >= d->ntt_p_limb_offset + K && (int64_t)d->ntt_p->r * d->ntt_p->c == N &&
+                    d->ntt_p_limb_offset >= 0,
+                "cross_hemul_plan_create: ntt_p does not cover the P limbs");
+  auto* P = new cross_hemul_plan_s();
+  P->r = d->r; P->c = d->c; P->L = L; P->L1 = L1; P->K = K; P->dnum = d->dnum; P->N = N;
+  P->ntt_qp = d->ntt_qp; P->ntt_p = d->ntt_p; P->p_off = d->ntt_p_limb_offset;
+  P->alpha = (L1 + d->dnum - 1) / d->dnum;                     // ciphertext.py:354
+  P->parts = (L1 + P->alpha - 1) / P->alpha;                   // ciphertext.py:356
+  auto fail = [&](const char* msg, int q = -1) {
+    set_error("cross_hemul_plan_create: %s (%d)", msg, q);
+    cross_hemul_plan_destroy(P);
+    return CROSS_ERR_INVALID_ARG;
+  };
+  if (P->parts > MAXPARTS) return fail("too many key-switch digits", P->parts);
+  const auto& mq = d->ntt_qp->mods_host;
+  std::vector<ModC> dle;
+  for (int i = 0; i < L1; ++i) dle.push_back(mq[i]);
+  for (int k = 0; k < K; ++k) dle.push_back(mq[L + k]);
+  for (int k = 0; k < K; ++k)
+    if (!same_q(d->ntt_p->mods_host[P->p_off + k], mq[L + k])) return fail("ntt_p moduli differ from P", k);
+  const int LT = L1 + K;
+  std::vector<int16_t> src((size_t)P->parts * LT, 0);
+  for (int j = 0; j < P->parts; ++j) {
+    const int s0 = j * P->alpha, len = std::min(P->alpha, L1 - s0);
+    P->dstart.push_back(s0);
+    P->dlen.push_back(len);
+    std::vector<int> comp;
+    for (int l = 0; l < LT; ++l)
+      if (l < s0 || l >= s0 + len) comp.push_back(l);
+    const cross_bconv_plan_s* bc = d->ks_bconv[j];
+    if (!bc || bc->sq != len || bc->sp != (int)comp.size()) return fail("ks_bconv shape mismatch", j);
+    for (int i = 0; i < len; ++i)
+      if (!same_q(bc->src_host[i], dle[s0 + i])) return fail("ks_bconv source moduli", j);
+    for (size_t i = 0; i < comp.size(); ++i)
+      if (!same_q(bc->dst_host[i], dle[comp[i]])) return fail("ks_bconv target moduli", j);
+    for (int l = 0; l < LT; ++l) src[(size_t)j * LT + l] = -1;
+    for (size_t i = 0; i < comp.size(); ++i) src[(size_t)j * LT + comp[i]] = (int16_t)i;
+    P->ks_bconv.push_back(d->ks_bconv[j]);
+    P->comp.push_back(comp);
+  }
+  P->down = d->down_bconv;
+  if (P->down->sq != K || P->down->sp != L1) return fail("down_bconv shape mismatch");
+  for (int k = 0; k < K; ++k)
+    if (!same_q(P->down->src_host[k], dle[L1 + k])) return fail("down_bconv source moduli", k);
+  for (int i = 0; i < L1; ++i)
+    if (!same_q(P->down->dst_host[i], dle[i])) return fail("down_bconv target moduli", i);
+  P->q_last = (uint32_t)mq[L - 1].q;
+  P->thr = (P->q_last + 1) / 2;                                 // ciphertext.py:260
+  std::vector<uint16_t> seq(std::max<int>(LT, 4) + 1), last{(uint16_t)(L - 1)}, zero{0}, pp, pd, q1;
+  for (size_t i = 0; i < seq.size(); ++i) seq[i] = (uint16_t)i;
+  for (int k = 0; k < K; ++k) { pp.push_back((uint16_t)(P->p_off + k)); pd.push_back((uint16_t)(L1 + k)); }
+  for (int i = 0; i < L1; ++i) q1.push_back((uint16_t)i);
+  int rc = CROSS_OK;
+  auto up32 = [&](uint32_t** dst, const uint32_t* s, size_t n) { if (!rc) rc = upload(dst, s, n); };
+  up32(&P->inv_psi_last, d->inv_psi_last, N);
+  up32(&P->gamma_psi, d->gamma_psi, (size_t)L1 * N);
+  up32(&P->inv_psi_q, d->inv_psi_q, (size_t)L1 * N);
+  up32(&P->psi_qp, d->psi_qp, (size_t)LT * N);
+  up32(&P->inv_psi_p, d->inv_psi_p, (size_t)K * N);
+  up32(&P->betas, d->betas, L1);
+  up32(&P->pinv, d->p_inv_mod_q, L1);
+  if (!rc) rc = upload_vec(&P->mods_dle, dle);
+  if (!rc) rc = upload_vec(&P->m_last, last);
+  if (!rc) rc = upload_vec(&P->m_zero, zero);
+  if (!rc) rc = upload_vec(&P->seq, seq);
+  if (!rc) rc = upload_vec(&P->m_p_plan, pp);
+  if (!rc) rc = upload_vec(&P->m_p_dle, pd);
+  if (!rc) rc = upload_vec(&P->m_q1_plan, q1);
+  if (!rc) rc = upload_vec(&P->ks_src, src);
+  for (int j = 0; j < P->parts && !rc; ++j) {
+    std::vector<uint16_t> cp, cd;
+    for (int l : P->comp[j]) { cd.push_back((uint16_t)l); cp.push_back((uint16_t)(l < L1 ? l : l + 1)); }
+    uint16_t *a = nullptr, *b = nullptr;
+    rc = upload_vec(&a, cp);
+    if (!rc) rc = upload_vec(&b, cd);
+    P->comp_plan.push_back(a);
+    P->comp_dle.push_back(b);
+  }
+  if (rc) {
+    cross_hemul_plan_destroy(P);
+    return rc;
+  }
+  *out = P;
+  return CROSS_OK;
+}
+
+int cross_hemul_set_keys(cross_hemul_plan P, const uint32_t* evk_a, const uint32_t* evk_b, int key_limbs) {
+  CROSS_REQUIRE(P && evk_a && evk_b, "cross_hemul_set_keys: null argument");
+  const int L1 = P->L1, K = P->K, LT = L1 + K;
+  CROSS_REQUIRE(key_limbs >= LT, "cross_hemul_set_keys: key has %d limbs, need >= %d", key_limbs, LT);
+  const int64_t N = P->N;
+  std::vector<uint32_t> a((size_t)P->parts * LT * N), b(a.size());
+  // ciphertext.py:450-451: keep key limbs [0, L1) and the last K.
+  for (int j = 0; j < P->parts; ++j)
+    for (int l = 0; l < LT; ++l) {
+      const int kl = l < L1 ? l : key_limbs - K + (l - L1);
+      for (int64_t t = 0; t < N; ++t) {
+        const size_t s = ((size_t)j * N + t) * key_limbs + kl;
+        a[((size_t)j * LT + l) * N + t] = evk_a[s];
+        b[((size_t)j * LT + l) * N + t] = evk_b[s];
+      }
+    }
+  dfree(P->evk_a);
+  dfree(P->evk_b);
+  P->evk_a = P->evk_b = nullptr;
+  int rc = upload_vec(&P->evk_a, a);
+  if (!rc) rc = upload_vec(&P->evk_b, b);
+  return rc;
+}
+
+size_t cross_hemul_workspace_size(cross_hemul_plan P, int64_t batch, int layout) {
+  if (!P || batch < 0) return 0;
+  Arena a(nullptr, 0);
+  HemulBufs b;
+  hemul_layout(P, batch, layout, a, b);
+  return a.off;
+}
+
+int cross_hemul(cross_hemul_plan P, const uint32_t* in, uint32_t* out, int64_t B, int layout, void* ws,
+                size_t ws_bytes, void* stream) {
+  CROSS_REQUIRE(P && in && out && B >= 0, "cross_hemul: bad argument");
+  CROSS_REQUIRE(P->evk_a && P->evk_b, "cross_hemul: keys not set (call cross_hemul_set_keys)");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR, "cross_hemul: bad layout");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || (((uintptr_t)in | (uintptr_t)out) & 15) == 0,
+                "cross_hemul: limb-major buffers must be 16-byte aligned");
+  if (B == 0) return CROSS_OK;
+  const size_t need = cross_hemul_workspace_size(P, B, layout);
+  if (!ws || ws_bytes < need) {
+    set_error("cross_hemul: workspace of %zu bytes required, %zu given", need, ws_bytes);
+    return CROSS_ERR_WORKSPACE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t N = P->N;
+  const int L = P->L, L1 = P->L1, K = P->K, LT = L1 + K;
+  Arena a(ws, ws_bytes);
+  HemulBufs b;
+  hemul_layout(P, B, layout, a, b);
+  int rc;
+  const uint32_t* X = in;
+  if (layout == CROSS_LAYOUT_REFERENCE) {
+    if ((rc = transpose_u32(in, b.X, B * 4, N, L, st))) return rc;
+    X = b.X;
+  }
+  const int64_t nv = N / 4;
+  const dim3 blk(T);
+  // 1. rescale (ciphertext.py:267-303)
+  {
+    RescaleArgs ra{P->ntt_qp, P->m_last, P->m_zero, P->m_q1_plan, P->mods_dle, P->inv_psi_last, P->gamma_psi,
+                   P->betas, P->thr, P->q_last, L, N};
+    if ((rc = rescale_run(ra, X, (int64_t)L * N, b.R, b.LL, b.tmp, B * 4, st))) return rc;
+  }
+  // 2. tensor product (ciphertext.py:309-324)
+  k_tensor_lm<<<dim3(gx_for(nv), gy_for(B * L1)), blk, 0, st>>>(b.R, b.D, B, L1, N, P->mods_dle); count_launch();
+  // 3. key switch on d2 (ciphertext.py:455-519)
+  const uint32_t* D2 = b.D + 2 * (int64_t)L1 * N;
+  const int64_t Dps = 3 * (int64_t)L1 * N;
+  if ((rc = ntt_run(P->ntt_qp, true, LP{D2, Dps, N}, LPo{b.Cc, (int64_t)L1 * N, N}, B, L1, P->m_q1_plan, b.tmp, st)))
+    return rc;
+  if ((rc = modmul_table_lm(LP{b.Cc, (int64_t)L1 * N, N}, LPo{b.Cc, (int64_t)L1 * N, N}, B, L1, N, P->inv_psi_q,
+                            P->seq, P->mods_dle, P->seq, st)))
+    return rc;
+  PartPtrs pp{};
+  for (int j = 0; j < P->parts; ++j) {
+    const int ns = LT - P->dlen[j];
+    const int64_t eps = (int64_t)ns * N;
+    if ((rc = bconv_run(P->ks_bconv[j], true, b.Cc + (int64_t)P->dstart[j] * N, (int64_t)L1 * N, N, 1, b.E[j], eps,
+                        N, 1, B, N, st)))
+      return rc;
+    if ((rc = modmul_table_lm(LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, N, P->psi_qp, P->comp_dle[j],
+                              P->mods_dle, P->comp_dle[j], st)))
+      return rc;
+    if ((rc = ntt_run(P->ntt_qp, false, LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, P->comp_plan[j], b.tmp, st)))
+      return rc;
+    pp.e[j] = b.E[j];
+    pp.ps[j] = eps;
+  }
+  k_ks_inner<<<dim3(gx_for(nv), gy_for(B * LT)), blk, 0, st>>>(LP{D2, Dps, N}, pp, P->parts, P->ks_src, LT, N, B,
+                                                               P->evk_a, P->evk_b, b.KS, P->mods_dle); count_launch();
+  // 4. ModDown (hemul.py:175-211)
+  const int64_t KSps = 2 * (int64_t)LT * N;
+  for (int e = 0; e < 2; ++e) {
+    if ((rc = ntt_run(P->ntt_p, true, LP{b.KS + ((int64_t)e * LT + L1) * N, KSps, N},
+                      LPo{b.KP + (int64_t)e * K * N, 2 * (int64_t)K * N, N}, B, K, P->m_p_plan, b.tmp, st)))
+      return rc;
+  }
+  if ((rc = modmul_table_lm(LP{b.KP, (int64_t)K * N, N}, LPo{b.KP, (int64_t)K * N, N}, B * 2, K, N, P->inv_psi_p,
+                            P->seq, P->mods_dle, P->m_p_dle, st)))
+    return rc;
+  if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L1 * N, N, 1, B * 2, N, st))) return rc;
+  if ((rc = modmul_table_lm(LP{b.F, (int64_t)L1 * N, N}, LPo{b.F, (int64_t)L1 * N, N}, B * 2, L1, N, P->psi_qp,
+                            P->seq, P->mods_dle, P->seq, st)))
+    return rc;
+  if ((rc = ntt_run(P->ntt_qp, false, LP{b.F, (int64_t)L1 * N, N}, LPo{b.F, (int64_t)L1 * N, N}, B * 2, L1,
+                    P->m_q1_plan, b.tmp, st)))
+    return rc;
+  // 5. final add (hemul.py:214-215): res = d_e + ModDown_e
+  uint32_t* O = layout == CROSS_LAYOUT_REFERENCE ? b.O : out;
+  k_moddown_final<<<dim3(gx_for(nv), gy_for(B * 2 * L1)), blk, 0, st>>>(
+      LP{b.KS, KSps, N}, (int64_t)LT * N, LP{b.F, 2 * (int64_t)L1 * N, N}, (int64_t)L1 * N, LP{b.D, Dps, N},
+      (int64_t)L1 * N, 1, 1, LPo{O, 2 * (int64_t)L1 * N, N}, (int64_t)L1 * N, B, L1, N, P->pinv, P->mods_dle); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  if (layout == CROSS_LAYOUT_REFERENCE) return transpose_u32(b.O, out, B * 2, L1, N, st);
+  return CROSS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// HE-Rotate
+// ---------------------------------------------------------------------------
+
+struct cross_herot_plan_s {
+  int L = 0, K = 0, dnum = 0, alpha = 0, parts = 0;
+  int64_t N = 0;
+  cross_ntt_plan_s* ntt = nullptr;
+  std::vector<cross_bconv_plan_s*> ks_bconv;
+  cross_bconv_plan_s* down = nullptr;
+  std::vector<int> dstart, dlen;
+  uint32_t *inv_psi_q = nullptr, *psi_qp = nullptr, *inv_psi_p = nullptr, *pinv = nullptr;
+  uint16_t *seq = nullptr, *m_p = nullptr;
+  std::vector<uint16_t*> comp;
+  int16_t* ks_src = nullptr;
+  uint32_t *evk_a = nullptr, *evk_b = nullptr;
+  int32_t* coef_map = nullptr;
+};
+
+namespace {
+
+struct HerotBufs {
+  uint32_t *X, *Cq, *KS, *KP, *F, *Rz, *tmp, *Tr;
+  std::vector<uint32_t*> E;
+};
+
+void herot_layout(const cross_herot_plan_s* P, int64_t B, int layout, Arena& a, HerotBufs& b) {
+  const int64_t N = P->N;
+  const int L = P->L, K = P->K;
+  b.X = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)B * 2 * L * N) : nullptr;
+  b.Cq = a.take<uint32_t>((size_t)B * L * N);
+  b.E.clear();
+  for (int j = 0; j < P->parts; ++j) b.E.push_back(a.take<uint32_t>((size_t)B * (L + K - P->dlen[j]) * N));
+  b.KS = a.take<uint32_t>((size_t)B * 2 * (L + K) * N);
+  b.KP = a.take<uint32_t>((size_t)B * 2 * K * N);
+  b.F = a.take<uint32_t>((size_t)B * 2 * L * N);
+  b.Rz = a.take<uint32_t>((size_t)B * 2 * L * N);
+  b.Tr = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)B * 2 * L * N) : nullptr;
+  int64_t tmpw = B * std::max(L, 2 * K);
+  for (int j = 0; j < P->parts; ++j) tmpw = std::max<int64_t>(tmpw, B * (L + K - P->dlen[j]));
+  tmpw = std::max<int64_t>(tmpw, B * 2 * L);
+  b.tmp = a.take<uint32_t>((size_t)tmpw * N);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cross_herot_plan_destroy(cross_herot_plan P) {
+  if (!P) return CROSS_OK;
+  for (void* p : {(void*)P->inv_psi_q, (void*)P->psi_qp, (void*)P->inv_psi_p, (void*)P->pinv, (void*)P->seq,
+                  (void*)P->m_p, (void*)P->ks_src, (void*)P->evk_a, (void*)P->evk_b, (void*)P->coef_map})
+    dfree(p);
+  for (auto* p : P->comp) dfree(p);
+  delete P;
+  return CROSS_OK;
+}
+
+int cross_herot_plan_create(const cross_herot_desc* d, cross_herot_plan* out) {
+  CROSS_REQUIRE(d && out, "cross_herot_plan_create: null argument");
+  *out = nullptr;
+  CROSS_REQUIRE(d->L >= 1 && d->K >= 1 && d->dnum >= 1 && d->ntt_qp && d->ks_bconv && d->down_bconv &&
+                    d->inv_psi_q && d->psi_qp && d->inv_psi_p && d->p_inv_mod_q,
+                "cross_herot_plan_create: bad descriptor");
+  const int L = d->L, K = d->K, LT = L + K;
+  const int64_t N = (int64_t)d->r * d->c;
+  CROSS_REQUIRE(N % 4 == 0 && d->ntt_qp->M == LT && (int64_t)d->ntt_qp->r * d->ntt_qp->c == N,
+                "cross_herot_plan_create: ntt_qp must cover L+K limbs of N");
+  auto* P = new cross_herot_plan_s();
+  P->L = L; P->K = K; P->dnum = d->dnum; P->N = N; P->ntt = d->ntt_qp;
+  P->alpha = (L + d->dnum - 1) / d->dnum;                       // herot.py:73
+  P->parts = (L + P->alpha - 1) / P->alpha;                     // herot.py:119
+  auto fail = [&](const char* msg, int q = -1) {
+    set_error("cross_herot_plan_create: %s (%d)", msg, q);
+    cross_herot_plan_destroy(P);
+    return CROSS_ERR_INVALID_ARG;
+  };
+  // herot.py:212 loops over dnum digits; the reference fails with an
+  // IndexError when fewer than dnum digits exist.
+  if (P->parts < d->dnum) return fail("dnum exceeds the number of digits ceil(L/alpha)", P->parts);
+  if (P->parts > MAXPARTS) return fail("too many key-switch digits", P->parts);
+  const auto& mq = d->ntt_qp->mods_host;
+  std::vector<int16_t> src((size_t)d->dnum * LT, -1);
+  for (int j = 0; j < d->dnum; ++j) {
+    const int s0 = j * P->alpha, len = std::min(P->alpha, L - s0);
+    P->dstart.push_back(s0);
+    P->dlen.push_back(len);
+    std::vector<int> comp;
+    for (int l = 0; l < LT; ++l)
+      if (l < s0 || l >= s0 + len) comp.push_back(l);
+    const cross_bconv_plan_s* bc = d->ks_bconv[j];
+    if (!bc || bc->sq != len || bc->sp != (int)comp.size()) return fail("ks_bconv shape mismatch", j);
+    for (int i = 0; i < len; ++i)
+      if (!same_q(bc->src_host[i], mq[s0 + i])) return fail("ks_bconv source moduli", j);
+    for (size_t i = 0; i < comp.size(); ++i)
+      if (!same_q(bc->dst_host[i], mq[comp[i]])) return fail("ks_bconv target moduli", j);
+    for (size_t i = 0; i < comp.size(); ++i) src[(size_t)j * LT + comp[i]] = (int16_t)i;
+    P->ks_bconv.push_back(d->ks_bconv[j]);
+    std::vector<uint16_t> cu(comp.begin(), comp.end());
+    uint16_t* dp = nullptr;
+    if (upload_vec(&dp, cu)) return fail("upload");
+    P->comp.push_back(dp);
+  }
+  P->parts = d->dnum;
+  P->down = d->down_bconv;
+  if (P->down->sq != K || P->down->sp != L) return fail("down_bconv shape mismatch");
+  std::vector<uint16_t> seq(LT + 1), mp;
+  for (size_t i = 0; i < seq.size(); ++i) seq[i] = (uint16_t)i;
+  for (int k = 0; k < K; ++k) mp.push_back((uint16_t)(L + k));
+  int rc = CROSS_OK;
+  auto up32 = [&](uint32_t** dst, const uint32_t* s, size_t n) { if (!rc) rc = upload(dst, s, n); };
+  up32(&P->inv_psi_q, d->inv_psi_q, (size_t)L * N);
+  up32(&P->psi_qp, d->psi_qp, (size_t)LT * N);
+  up32(&P->inv_psi_p, d->inv_psi_p, (size_t)K * N);
+  up32(&P->pinv, d->p_inv_mod_q, L);
+  if (!rc) rc = upload_vec(&P->seq, seq);
+  if (!rc) rc = upload_vec(&P->m_p, mp);
+  if (!rc) rc = upload_vec(&P->ks_src, src);
+  if (rc) {
+    cross_herot_plan_destroy(P);
+    return rc;
+  }
+  *out = P;
+  return CROSS_OK;
+}
+
+int cross_herot_set_keys(cross_herot_plan P, const uint32_t* evk_a, const uint32_t* evk_b, const int32_t* coef_map) {
+  CROSS_REQUIRE(P && evk_a && evk_b && coef_map, "cross_herot_set_keys: null argument");
+  const int LT = P->L + P->K;
+  const int64_t N = P->N;
+  std::vector<uint32_t> a((size_t)P->parts * LT * N), b(a.size());
+  for (int j = 0; j < P->parts; ++j)
+    for (int l = 0; l < LT; ++l)
+      for (int64_t t = 0; t < N; ++t) {
+        const size_t s = ((size_t)j * N + t) * LT + l;
+        a[((size_t)j * LT + l) * N + t] = evk_a[s];
+        b[((size_t)j * LT + l) * N + t] = evk_b[s];
+      }
+  dfree(P->evk_a);
+  dfree(P->evk_b);
+  dfree(P->coef_map);
+  P->evk_a = P->evk_b = nullptr;
+  P->coef_map = nullptr;
+  int rc = upload_vec(&P->evk_a, a);
+  if (!rc) rc = upload_vec(&P->evk_b, b);
+  if (!rc) rc = upload(&P->coef_map, coef_map, (size_t)N);
+  return rc;
+}
+
+size_t cross_herot_workspace_size(cross_herot_plan P, int64_t batch, int layout) {
+  if (!P || batch < 0) return 0;
+  Arena a(nullptr, 0);
+  HerotBufs b;
+  herot_layout(P, batch, layout, a, b);
+  return a.off;
+}
+
+int cross_herot(cross_herot_plan P, const uint32_t* in, uint32_t* out, int64_t B, int layout, void* ws,
+                size_t ws_bytes, void* stream) {
+  CROSS_REQUIRE(P && in && out && B >= 0, "cross_herot: bad argument");
+  CROSS_REQUIRE(P->evk_a && P->evk_b && P->coef_map, "cross_herot: keys not set (call cross_herot_set_keys)");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR, "cross_herot: bad layout");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || (((uintptr_t)in | (uintptr_t)out) & 15) == 0,
+                "cross_herot: limb-major buffers must be 16-byte aligned");
+  if (B == 0) return CROSS_OK;
+  const size_t need = cross_herot_workspace_size(P, B, layout);
+  if (!ws || ws_bytes < need) {
+    set_error("cross_herot: workspace of %zu bytes required, %zu given", need, ws_bytes);
+    return CROSS_ERR_WORKSPACE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t N = P->N;
+  const int L = P->L, K = P->K, LT = L + K;
+  Arena a(ws, ws_bytes);
+  HerotBufs b;
+  herot_layout(P, B, layout, a, b);
+  int rc;
+  const uint32_t* X = in;
+  if (layout == CROSS_LAYOUT_REFERENCE) {
+    if ((rc = transpose_u32(in, b.X, B * 2, N, L, st))) return rc;
+    X = b.X;
+  }
+  const int64_t nv = N / 4;
+  const dim3 blk(T);
+  const int64_t Xps = 2 * (int64_t)L * N;
+  const uint32_t* X1 = X + (int64_t)L * N;   // in_tower = element 1 (herot.py:201)
+  // 1. key switch of element 1 (herot.py:203-247)
+  if ((rc = ntt_run(P->ntt, true, LP{X1, Xps, N}, LPo{b.Cq, (int64_t)L * N, N}, B, L, P->seq, b.tmp, st))) return rc;
+  if ((rc = modmul_table_lm(LP{b.Cq, (int64_t)L * N, N}, LPo{b.Cq, (int64_t)L * N, N}, B, L, N, P->inv_psi_q, P->seq,
+                            P->ntt->mods, P->seq, st)))
+    return rc;
+  PartPtrs pp{};
+  for (int j = 0; j < P->parts; ++j) {
+    const int ns = LT - P->dlen[j];
+    const int64_t eps = (int64_t)ns * N;
+    if ((rc = bconv_run(P->ks_bconv[j], true, b.Cq + (int64_t)P->dstart[j] * N, (int64_t)L * N, N, 1, b.E[j], eps, N,
+                        1, B, N, st)))
+      return rc;
+    if ((rc = modmul_table_lm(LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, N, P->psi_qp, P->comp[j], P->ntt->mods,
+                              P->comp[j], st)))
+      return rc;
+    if ((rc = ntt_run(P->ntt, false, LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, P->comp[j], b.tmp, st))) return rc;
+    pp.e[j] = b.E[j];
+    pp.ps[j] = eps;
+  }
+  k_ks_inner<<<dim3(gx_for(nv), gy_for(B * LT)), blk, 0, st>>>(LP{X1, Xps, N}, pp, P->parts, P->ks_src, LT, N, B,
+                                                               P->evk_a, P->evk_b, b.KS, P->ntt->mods); count_launch();
+  // 2. ModDown per element (herot.py:255-289)
+  const int64_t KSps = 2 * (int64_t)LT * N;
+  for (int e = 0; e < 2; ++e) {
+    if ((rc = ntt_run(P->ntt, true, LP{b.KS + ((int64_t)e * LT + L) * N, KSps, N},
+                      LPo{b.KP + (int64_t)e * K * N, 2 * (int64_t)K * N, N}, B, K, P->m_p, b.tmp, st)))
+      return rc;
+  }
+  if ((rc = modmul_table_lm(LP{b.KP, (int64_t)K * N, N}, LPo{b.KP, (int64_t)K * N, N}, B * 2, K, N, P->inv_psi_p,
+                            P->seq, P->ntt->mods, P->m_p, st)))
+    return rc;
+  if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L * N, N, 1, B * 2, N, st))) return rc;
+  if ((rc = modmul_table_lm(LP{b.F, (int64_t)L * N, N}, LPo{b.F, (int64_t)L * N, N}, B * 2, L, N, P->psi_qp, P->seq,
+                            P->ntt->mods, P->seq, st)))
+    return rc;
+  if ((rc = ntt_run(P->ntt, false, LP{b.F, (int64_t)L * N, N}, LPo{b.F, (int64_t)L * N, N}, B * 2, L, P->seq, b.tmp,
+                    st)))
+    return rc;
+  // 3. c0 += ModDown_0 (herot.py:292-296); element 1 is ModDown_1
+  k_moddown_final<<<dim3(gx_for(nv), gy_for(B * 2 * L)), blk, 0, st>>>(
+      LP{b.KS, KSps, N}, (int64_t)LT * N, LP{b.F, 2 * (int64_t)L * N, N}, (int64_t)L * N, LP{X, Xps, N},
+      (int64_t)L * N, 1, 0, LPo{b.Rz, 2 * (int64_t)L * N, N}, (int64_t)L * N, B, L, N, P->pinv, P->ntt->mods); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  // 4. automorphism (herot.py:300)
+  if (layout == CROSS_LAYOUT_REFERENCE) {
+    if ((rc = transpose_u32(b.Rz, b.Tr, B * 2, L, N, st))) return rc;
+    return cross_automorphism(b.Tr, P->coef_map, out, B * 2, N, L, st);
+  }
+  const int64_t rows = B * 2 * L;
+  k_gather_lm<<<dim3((unsigned)((N + T - 1) / T > 64 ? 64 : (N + T - 1) / T), gy_for(rows)), blk, 0, st>>>(
+      b.Rz, P->coef_map, out, rows, N); count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Standalone rescale
+// ---------------------------------------------------------------------------
+
+struct cross_rescale_plan_s {
+  int L = 0;
+  int64_t N = 0;
+  cross_ntt_plan_s* ntt = nullptr;
+  uint32_t *inv_psi_last = nullptr, *gamma_psi = nullptr, *betas = nullptr;
+  uint16_t *m_last = nullptr, *m_zero = nullptr, *m_q1 = nullptr;
+  uint32_t thr = 0, q_last = 0;
+};
+
+namespace {
+struct RescaleBufs {
+  uint32_t *X, *R, *LL, *tmp;
+};
+void rescale_layout(const cross_rescale_plan_s* P, int64_t polys, int layout, Arena& a, RescaleBufs& b) {
+  const int64_t N = P->N;
+  b.X = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)polys * P->L * N) : nullptr;
+  b.R = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)polys * (P->L - 1) * N) : nullptr;
+  b.LL = a.take<uint32_t>((size_t)polys * N);
+  b.tmp = a.take<uint32_t>((size_t)polys * (P->L - 1) * N + (size_t)polys * N);
+}
+}  // namespace
+
+extern "C" {
+
+int cross_rescale_plan_destroy(cross_rescale_plan P) {
+  if (!P) return CROSS_OK;
+  for (void* p : {(void*)P->inv_psi_last, (void*)P->gamma_psi, (void*)P->betas, (void*)P->m_last, (void*)P->m_zero,
+                  (void*)P->m_q1})
+    dfree(p);
+  delete P;
+  return CROSS_OK;
+}
+
+int cross_rescale_plan_create(const cross_rescale_desc* d, cross_rescale_plan* out) {
+  CROSS_REQUIRE(d && out && d->ntt_q && d->inv_psi_last && d->gamma_psi && d->betas && d->L >= 2,
+                "cross_rescale_plan_create: bad descriptor");
+  *out = nullptr;
+  const int64_t N = (int64_t)d->r * d->c;
+  CROSS_REQUIRE(N % 4 == 0 && (int64_t)d->ntt_q->r * d->ntt_q->c == N && d->ntt_q->M >= d->L,
+                "cross_rescale_plan_create: ntt_q must cover the L moduli with N = r*c (N %% 4 == 0)");
+  auto* P = new cross_rescale_plan_s();
+  P->L = d->L;
+  P->N = N;
+  P->ntt = d->ntt_q;
+  P->q_last = (uint32_t)d->ntt_q->mods_host[d->L - 1].q;
+  P->thr = (P->q_last + 1) / 2;
+  std::vector<uint16_t> last{(uint16_t)(d->L - 1)}, zero{0}, q1;
+  for (int i = 0; i < d->L - 1; ++i) q1.push_back((uint16_t)i);
+  int rc = upload(&P->inv_psi_last, d->inv_psi_last, (size_t)N);
+  if (!rc) rc = upload(&P->gamma_psi, d->gamma_psi, (size_t)(d->L - 1) * N);
+  if (!rc) rc = upload(&P->betas, d->betas, (size_t)(d->L - 1));
+  if (!rc) rc = upload_vec(&P->m_last, last);
+  if (!rc) rc = upload_vec(&P->m_zero, zero);
+  if (!rc) rc = upload_vec(&P->m_q1, q1);
+  if (rc) {
+    cross_rescale_plan_destroy(P);
+    return rc;
+  }
+  *out = P;
+  return CROSS_OK;
+}
+
+size_t cross_rescale_workspace_size(cross_rescale_plan P, int64_t polys, int layout) {
+  if (!P || polys < 0) return 0;
+  Arena a(nullptr, 0);
+  RescaleBufs b;
+  rescale_layout(P, polys, layout, a, b);
+  return a.off;
+}
+
+int cross_rescale(cross_rescale_plan P, const uint32_t* in, uint32_t* out, int64_t polys, int layout, void* ws,
+                  size_t ws_bytes, void* stream) {
+  CROSS_REQUIRE(P && in && out && polys >= 0, "cross_rescale: bad argument");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR, "cross_rescale: bad layout");
+  if (polys == 0) return CROSS_OK;
+  const size_t need = cross_rescale_workspace_size(P, polys, layout);
+  if (!ws || ws_bytes < need) {
+    set_error("cross_rescale: workspace of %zu bytes required, %zu given", need, ws_bytes);
+    return CROSS_ERR_WORKSPACE;
+  }
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || in != out, "cross_rescale: limb-major in and out must differ");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || (((uintptr_t)in | (uintptr_t)out) & 15) == 0,
+                "cross_rescale: limb-major buffers must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t N = P->N;
+  const int L = P->L;
+  Arena a(ws, ws_bytes);
+  RescaleBufs b;
+  rescale_layout(P, polys, layout, a, b);
+  // Barrett constants of Q' are the first L-1 entries of the plan's table.
+  RescaleArgs ra{P->ntt, P->m_last, P->m_zero, P->m_q1, P->ntt->mods, P->inv_psi_last, P->gamma_psi, P->betas,
+                 P->thr, P->q_last, L, N};
+  int rc;
+  if (layout == CROSS_LAYOUT_LIMB_MAJOR) return rescale_run(ra, in, (int64_t)L * N, out, b.LL, b.tmp, polys, st);
+  if ((rc = transpose_u32(in, b.X, polys, N, L, st))) return rc;
+  if ((rc = rescale_run(ra, b.X, (int64_t)L * N, b.R, b.LL, b.tmp, polys, st))) return rc;
+  return transpose_u32(b.R, out, polys, L - 1, N, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Internal plan structures and launchers shared by the translation units.
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+#include "common.cuh"
+
+struct cross_moduli_s {
+  int n = 0;
+  std::vector<cross::ModC> host;
+  cross::ModC* dev = nullptr;
+};
+
+// NTT plan: the reference's BAT tables re-laid out for the kernels.
+// "col" matrices contract over the row index r of the (r, c) matrix
+// (ntt step 1 "brcmq,zqrpm", intt step 3 "brcmq,lqrpm"); "row" matrices
+// contract over the column index (ntt step 3 "brcmq,cqnpm", intt step 1
+// "brcmq,cqlpm").
+struct cross_ntt_plan_s {
+  int r = 0, c = 0, M = 0;
+  std::vector<cross::ModC> mods_host;
+  cross::ModC* mods = nullptr;      // [M]
+  // dp4a operands: 4 bytes over q packed into one u32, planes p separate.
+  uint32_t* col_fwd = nullptr;      // [M][4 p][r z][r k]   from ntt_bat_tf_step1
+  uint32_t* col_inv = nullptr;      // [M][4 p][r l][r k]   from intt_bat_tf_step3
+  uint32_t* row_fwd = nullptr;      // [M][4 p][c k][c n]   from ntt_bat_tf_step3
+  uint32_t* row_inv = nullptr;      // [M][4 p][c k][c n]   from intt_bat_tf_step1
+  uint32_t* tw_fwd = nullptr;       // [M][r][c]            ntt_tf_step2
+  uint32_t* tw_inv = nullptr;       // [M][r][c]            intt_tf_step2
+  uint16_t* identity = nullptr;     // [M] 0..M-1
+};
+
+struct cross_bconv_plan_s {
+  int sq = 0, sp = 0;
+  std::vector<cross::ModC> src_host, dst_host;
+  cross::ModC* src = nullptr;       // [sq]
+  cross::ModC* dst = nullptr;       // [sp]
+  uint32_t* qhat_inv = nullptr;     // [sq]
+  uint32_t* bat = nullptr;          // [sp][4 b][sq]: sum_a bat[(i*4+a), j, b] << 8a
+  uint32_t* qhat_modp = nullptr;    // [sp][sq]
+};
+
+namespace cross {
+
+// Bump allocator over a caller-provided workspace (or a size query when
+// base == nullptr).
+struct Arena {
+  char* base;
+  size_t cap;
+  size_t off = 0;
+  Arena(void* b, size_t c) : base((char*)b), cap(c) {}
+  template <class T>
+  T* take(size_t count) {
+    size_t bytes = (count * sizeof(T) + 255) & ~(size_t)255;
+    T* r = base ? (T*)(base + off) : nullptr;
+    off += bytes;
+    return r;
+  }
+  bool ok() const { return base == nullptr || off <= cap; }
+};
+
+// A strided set of limb-polynomials: element (poly, slot, t) lives at
+// ptr + poly*ps + slot*ss + t.
+struct LP {
+  const uint32_t* p;
+  int64_t ps, ss;
+};
+struct LPo {
+  uint32_t* p;
+  int64_t ps, ss;
+};
+
+template <class T>
+int upload(T** dst, const T* src, size_t count);
+template <class T>
+int upload_vec(T** dst, const std::vector<T>& v) { return upload(dst, v.data(), v.size()); }
+void dfree(void* p);
+
+// NTT over polys x slots limb-polynomials (internal layout); limbs[slot] is the
+// plan limb of each slot (device array).  tmp holds polys*slots*N words.
+int ntt_run(const cross_ntt_plan_s* plan, bool inverse, LP in, LPo out, int64_t polys, int slots,
+            const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
+
+// bconv over polys with arbitrary limb / coefficient strides.
+int bconv_run(const cross_bconv_plan_s* plan, bool bat, const uint32_t* in, int64_t in_ps,
+              int64_t in_ls, int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls,
+              int64_t out_ts, int64_t polys, int64_t n, cudaStream_t st);
+
+// y[poly, slot, t] = Barrett_{mods[midx[slot]]}(x * tab[trow[slot] * n + t])
+int modmul_table_lm(LP x, LPo y, int64_t polys, int slots, int64_t n, const uint32_t* tab,
+                    const uint16_t* trow, const ModC* mods, const uint16_t* midx, cudaStream_t st);
+// batched 2-D transpose: in (batch, rows, cols) -> out (batch, cols, rows)
+int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows, int64_t cols,
+                  cudaStream_t st);
+
+}  // namespace cross

@@ -1,0 +1,299 @@
+// BAT matrix NTT / INTT (ntt_mm.py:351-407) -- plan creation and the
+// CUDA-core kernels used for every size (dp4a contractions; the tcgen05
+// tensor-core path in ntt_tc.cu takes over for the large factorisations).
+//
+// The 3-step NTT of one limb-polynomial, viewed as an R x C matrix X:
+//   step 1 ("col"):  S1[z,c] = sum_{r,q} byte_q(X[r,c]) * T1bat[z,q,r,p] << 8p
+//                    Y = Barrett(Barrett(S1) * T2)                  (ntt_mm.py:372-375)
+//   step 3 ("row"):  S3[z,n] = sum_{c,q} byte_q(Y[z,c]) * T3bat[c,q,n,p] << 8p
+//                    out = Barrett(S3)                               (ntt_mm.py:376-377)
+// and the INTT is the row transform (with the intt_tf_step2 twiddle) followed
+// by the column transform (ntt_mm.py:401-406).  Sums are exact integers, so any
+// exact evaluation order reproduces the reference bit for bit.
+#include <cstring>
+#include <vector>
+
+#include "internal.hpp"
+
+namespace cross {
+
+namespace {
+
+constexpr int TM = 16;   // output rows per block
+constexpr int TN = 64;   // output cols per block
+constexpr int TK = 32;   // contraction chunk
+
+// Column transform: out[z, c] = epi( sum_k W[z, k] (.) X[k, c] ), k over R.
+template <bool TWIDDLE>
+__global__ void __launch_bounds__(256) k_col_dp4a(LP in, LPo out, int64_t lps, int slots,
+                                                  const uint16_t* __restrict__ limbs, int R, int C,
+                                                  const uint32_t* __restrict__ W,
+                                                  const uint32_t* __restrict__ T2,
+                                                  const ModC* __restrict__ mods) {
+  __shared__ uint32_t Xs[TK][TN + 4];
+  __shared__ uint32_t Ws[4][TM][TK + 1];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int c0 = blockIdx.x * TN, z0 = blockIdx.y * TM;
+  for (int64_t lp = blockIdx.z; lp < lps; lp += gridDim.z) {
+    const int64_t poly = lp / slots;
+    const int slot = (int)(lp % slots);
+    const int limb = limbs[slot];
+    const uint32_t* x = in.p + poly * in.ps + slot * in.ss;
+    uint32_t* y = out.p + poly * out.ps + slot * out.ss;
+    const uint32_t* w = W + (size_t)limb * 4 * R * R;
+    uint32_t acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int p = 0; p < 4; ++p) acc[j][p] = 0;
+    for (int k0 = 0; k0 < R; k0 += TK) {
+      for (int i = tid; i < TK * TN; i += 256) {
+        const int k = i / TN, cc = i % TN;
+        const int gk = k0 + k, gc = c0 + cc;
+        Xs[k][cc] = (gk < R && gc < C) ? x[(size_t)gk * C + gc] : 0u;
+      }
+      for (int i = tid; i < 4 * TM * TK; i += 256) {
+        const int p = i / (TM * TK), zz = (i / TK) % TM, k = i % TK;
+        const int gz = z0 + zz, gk = k0 + k;
+        Ws[p][zz][k] = (gz < R && gk < R) ? w[((size_t)p * R + gz) * R + gk] : 0u;
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int k = 0; k < TK; ++k) {
+        const uint32_t a0 = Ws[0][ty][k], a1 = Ws[1][ty][k], a2 = Ws[2][ty][k], a3 = Ws[3][ty][k];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t b = Xs[k][tx * 4 + j];
+          acc[j][0] = __dp4a(b, a0, acc[j][0]);
+          acc[j][1] = __dp4a(b, a1, acc[j][1]);
+          acc[j][2] = __dp4a(b, a2, acc[j][2]);
+          acc[j][3] = __dp4a(b, a3, acc[j][3]);
+        }
+      }
+      __syncthreads();
+    }
+    const int z = z0 + ty;
+    if (z < R) {
+      const ModC mc = mods[limb];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int cc = c0 + tx * 4 + j;
+        if (cc < C) {
+          uint32_t v = barrett_any(combine4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]), mc);
+          if (TWIDDLE) v = barrett_any((uint64_t)v * T2[((size_t)limb * R + z) * C + cc], mc);
+          y[(size_t)z * C + cc] = v;
+        }
+      }
+    }
+  }
+}
+
+// Row transform: out[r, n] = epi( sum_k X[r, k] (.) U[k, n] ), k over C.
+template <bool TWIDDLE>
+__global__ void __launch_bounds__(256) k_row_dp4a(LP in, LPo out, int64_t lps, int slots,
+                                                  const uint16_t* __restrict__ limbs, int R, int C,
+                                                  const uint32_t* __restrict__ U,
+                                                  const uint32_t* __restrict__ T2,
+                                                  const ModC* __restrict__ mods) {
+  __shared__ uint32_t Xs[TM][TK + 1];
+  __shared__ uint32_t Us[4][TK][TN + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int n0 = blockIdx.x * TN, r0 = blockIdx.y * TM;
+  for (int64_t lp = blockIdx.z; lp < lps; lp += gridDim.z) {
+    const int64_t poly = lp / slots;
+    const int slot = (int)(lp % slots);
+    const int limb = limbs[slot];
+    const uint32_t* x = in.p + poly * in.ps + slot * in.ss;
+    uint32_t* y = out.p + poly * out.ps + slot * out.ss;
+    const uint32_t* u = U + (size_t)limb * 4 * C * C;
+    uint32_t acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int p = 0; p < 4; ++p) acc[j][p] = 0;
+    for (int k0 = 0; k0 < C; k0 += TK) {
+      for (int i = tid; i < TM * TK; i += 256) {
+        const int rr = i / TK, k = i % TK;
+        const int gr = r0 + rr, gk = k0 + k;
+        Xs[rr][k] = (gr < R && gk < C) ? x[(size_t)gr * C + gk] : 0u;
+      }
+      for (int i = tid; i < 4 * TK * TN; i += 256) {
+        const int p = i / (TK * TN), k = (i / TN) % TK, nn = i % TN;
+        const int gk = k0 + k, gn = n0 + nn;
+        Us[p][k][nn] = (gk < C && gn < C) ? u[((size_t)p * C + gk) * C + gn] : 0u;
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int k = 0; k < TK; ++k) {
+        const uint32_t a = Xs[ty][k];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[j][0] = __dp4a(a, Us[0][k][tx * 4 + j], acc[j][0]);
+          acc[j][1] = __dp4a(a, Us[1][k][tx * 4 + j], acc[j][1]);
+          acc[j][2] = __dp4a(a, Us[2][k][tx * 4 + j], acc[j][2]);
+          acc[j][3] = __dp4a(a, Us[3][k][tx * 4 + j], acc[j][3]);
+        }
+      }
+      __syncthreads();
+    }
+    const int r = r0 + ty;
+    if (r < R) {
+      const ModC mc = mods[limb];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int nn = n0 + tx * 4 + j;
+        if (nn < C) {
+          uint32_t v = barrett_any(combine4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]), mc);
+          if (TWIDDLE) v = barrett_any((uint64_t)v * T2[((size_t)limb * R + r) * C + nn], mc);
+          y[(size_t)r * C + nn] = v;
+        }
+      }
+    }
+  }
+}
+
+// Pack the reference's (X, 4 q, Y, 4 p, M) u8 BAT array into
+// dst[m][p][row][col] u32 (4 q-bytes per word).  `transpose_xy` selects
+// whether the first BAT axis (X) is the output row (col transforms: [z][k]) or
+// the contraction row (row transforms: [k][n]).
+void pack_bat(const uint8_t* bat, int X, int Y, int M, std::vector<uint32_t>& dst) {
+  dst.assign((size_t)M * 4 * X * Y, 0u);
+  for (int x = 0; x < X; ++x)
+    for (int q = 0; q < 4; ++q)
+      for (int y = 0; y < Y; ++y)
+        for (int p = 0; p < 4; ++p)
+          for (int m = 0; m < M; ++m) {
+            const uint8_t b = bat[((((size_t)x * 4 + q) * Y + y) * 4 + p) * M + m];
+            dst[(((size_t)m * 4 + p) * X + x) * Y + y] |= (uint32_t)b << (8 * q);
+          }
+}
+
+void unpack_tw(const uint32_t* tw, int R, int C, int M, std::vector<uint32_t>& dst) {
+  dst.resize((size_t)M * R * C);
+  for (int r = 0; r < R; ++r)
+    for (int c = 0; c < C; ++c)
+      for (int m = 0; m < M; ++m) dst[((size_t)m * R + r) * C + c] = tw[((size_t)r * C + c) * M + m];
+}
+
+unsigned grid_z(int64_t lps) { return (unsigned)(lps < 65535 ? lps : 65535); }
+
+}  // namespace
+
+int ntt_run(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+            const uint16_t* limbs, uint32_t* tmp, cudaStream_t st) {
+  const int R = P->r, C = P->c;
+  const int64_t N = (int64_t)R * C;
+  const int64_t lps = polys * slots;
+  if (lps == 0) return CROSS_OK;
+  LPo mid{tmp, (int64_t)slots * N, N};
+  LP mid_in{tmp, (int64_t)slots * N, N};
+  dim3 blk(256);
+  if (!inverse) {
+    dim3 g1((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
+    k_col_dp4a<true><<<g1, blk, 0, st>>>(in, mid, lps, slots, limbs, R, C, P->col_fwd, P->tw_fwd, P->mods); count_launch();
+    dim3 g2((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
+    k_row_dp4a<false><<<g2, blk, 0, st>>>(mid_in, out, lps, slots, limbs, R, C, P->row_fwd, nullptr, P->mods); count_launch();
+  } else {
+    dim3 g1((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
+    k_row_dp4a<true><<<g1, blk, 0, st>>>(in, mid, lps, slots, limbs, R, C, P->row_inv, P->tw_inv, P->mods); count_launch();
+    dim3 g2((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
+    k_col_dp4a<false><<<g2, blk, 0, st>>>(mid_in, out, lps, slots, limbs, R, C, P->col_inv, nullptr, P->mods); count_launch();
+  }
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+}  // namespace cross
+
+using namespace cross;
+
+extern "C" {
+
+int cross_ntt_plan_create(cross_moduli moduli, int r, int c, const uint8_t* ntt_bat_tf_step1,
+                          const uint32_t* ntt_tf_step2, const uint8_t* ntt_bat_tf_step3,
+                          const uint8_t* intt_bat_tf_step1, const uint32_t* intt_tf_step2,
+                          const uint8_t* intt_bat_tf_step3, cross_ntt_plan* out) {
+  CROSS_REQUIRE(out && moduli && ntt_bat_tf_step1 && ntt_tf_step2 && ntt_bat_tf_step3 &&
+                    intt_bat_tf_step1 && intt_tf_step2 && intt_bat_tf_step3,
+                "cross_ntt_plan_create: null argument");
+  CROSS_REQUIRE(r >= 1 && c >= 1 && r <= 4096 && c <= 4096,
+                "cross_ntt_plan_create: r=%d c=%d out of range", r, c);
+  *out = nullptr;
+  const int M = moduli->n;
+  auto* P = new cross_ntt_plan_s();
+  P->r = r;
+  P->c = c;
+  P->M = M;
+  P->mods_host = moduli->host;
+  std::vector<uint32_t> buf;
+  std::vector<uint16_t> ident(M);
+  for (int i = 0; i < M; ++i) ident[i] = (uint16_t)i;
+  int rc = CROSS_OK;
+  if (!rc) rc = upload_vec(&P->mods, P->mods_host);
+  if (!rc) rc = upload_vec(&P->identity, ident);
+  if (!rc) { pack_bat(ntt_bat_tf_step1, r, r, M, buf); rc = upload_vec(&P->col_fwd, buf); }
+  if (!rc) { pack_bat(intt_bat_tf_step3, r, r, M, buf); rc = upload_vec(&P->col_inv, buf); }
+  if (!rc) { pack_bat(ntt_bat_tf_step3, c, c, M, buf); rc = upload_vec(&P->row_fwd, buf); }
+  if (!rc) { pack_bat(intt_bat_tf_step1, c, c, M, buf); rc = upload_vec(&P->row_inv, buf); }
+  if (!rc) { unpack_tw(ntt_tf_step2, r, c, M, buf); rc = upload_vec(&P->tw_fwd, buf); }
+  if (!rc) { unpack_tw(intt_tf_step2, r, c, M, buf); rc = upload_vec(&P->tw_inv, buf); }
+  if (rc) {
+    cross_ntt_plan_destroy(P);
+    return rc;
+  }
+  *out = P;
+  return CROSS_OK;
+}
+
+int cross_ntt_plan_destroy(cross_ntt_plan P) {
+  if (!P) return CROSS_OK;
+  dfree(P->mods);
+  dfree(P->identity);
+  dfree(P->col_fwd);
+  dfree(P->col_inv);
+  dfree(P->row_fwd);
+  dfree(P->row_inv);
+  dfree(P->tw_fwd);
+  dfree(P->tw_inv);
+  delete P;
+  return CROSS_OK;
+}
+
+size_t cross_ntt_workspace_size(cross_ntt_plan P, int64_t batch, int layout) {
+  if (!P || batch < 0) return 0;
+  const size_t words = (size_t)batch * P->M * P->r * P->c;
+  Arena a(nullptr, 0);
+  a.take<uint32_t>(words);
+  if (layout == CROSS_LAYOUT_REFERENCE) a.take<uint32_t>(words);
+  return a.off;
+}
+
+int cross_ntt(cross_ntt_plan P, int inverse, const uint32_t* in, uint32_t* out, int64_t batch, int layout,
+              void* workspace, size_t workspace_bytes, void* stream) {
+  CROSS_REQUIRE(P && in && out && batch >= 0, "cross_ntt: null argument or negative batch");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR,
+                "cross_ntt: unknown layout %d", layout);
+  if (batch == 0) return CROSS_OK;
+  const size_t need = cross_ntt_workspace_size(P, batch, layout);
+  if (!workspace || workspace_bytes < need) {
+    set_error("cross_ntt: workspace of %zu bytes required, %zu given", need, workspace_bytes);
+    return CROSS_ERR_WORKSPACE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t N = (int64_t)P->r * P->c;
+  const int M = P->M;
+  const size_t words = (size_t)batch * M * N;
+  Arena a(workspace, workspace_bytes);
+  uint32_t* tmp = a.take<uint32_t>(words);
+  if (layout == CROSS_LAYOUT_LIMB_MAJOR) {
+    return ntt_run(P, inverse != 0, LP{in, M * N, N}, LPo{out, M * N, N}, batch, M, P->identity, tmp, st);
+  }
+  uint32_t* lm = a.take<uint32_t>(words);
+  int rc = transpose_u32(in, lm, batch, N, M, st);
+  if (rc) return rc;
+  rc = ntt_run(P, inverse != 0, LP{lm, M * N, N}, LPo{lm, M * N, N}, batch, M, P->identity, tmp, st);
+  if (rc) return rc;
+  return transpose_u32(lm, out, batch, M, N, st);
+}
+
+}  // extern "C"

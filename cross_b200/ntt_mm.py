@@ -1,0 +1,207 @@
+"""Multi-modulus BAT 3-step NTT (jaxite_word ntt_mm.py) on the GPU.
+
+The constructors precompute exactly the reference's tables (same names,
+shapes and values, ntt_mm.py:136-255); ``ntt`` / ``intt`` run the CUDA
+kernels of libcross_b200.so through the C ABI.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import _lib, _tensor, util
+from . import finite_field as ff_context
+
+U32, U64 = np.uint32, np.uint64
+
+
+def get_bit_reverse_perm(n: int):
+    """ntt_mm.py:261-274."""
+    bits = n.bit_length() - 1
+    return [util.bit_reverse(i, bits) for i in range(n)] if n > 0 else []
+
+
+def basis_aligned_transformation(matrix: np.ndarray, moduli) -> np.ndarray:
+    """ntt_mm.py:248-255: (rows, cols, M) -> (rows, 4, cols, 4, M) uint8 with
+    [x, q, y, p, m] = byte_p((T[x, y, m] << 8q) mod q_m)."""
+    mu = np.asarray(matrix).astype(U64)
+    qs = np.array(moduli, U64)
+    red = np.stack([((mu << U64(8 * i)) % qs).astype(U32) for i in range(4)], 0)
+    u8 = np.ascontiguousarray(red).view(np.uint8).reshape(*red.shape, 4)
+    return np.ascontiguousarray(u8.transpose(1, 0, 2, 4, 3))
+
+
+class NTTCiphertextContextBase:
+    """ntt_mm.py:125-419."""
+
+    def __init__(self, moduli, parameters: dict, perf_test: bool = False):
+        self.ff_ctx = parameters.get("finite_field_context", None)
+        self.num_bytes = 4
+        self.moduli = [moduli] if isinstance(moduli, int) else list(moduli)
+        self.parameters = parameters
+        assert all(q < 2 ** 31 for q in self.moduli), "moduli must be less than 2**31"
+        self.r = parameters.get("r", 0)
+        self.c = parameters.get("c", 0)
+        assert self.r != 0, "r must be non-zero"
+        assert self.c != 0, "c must be non-zero"
+        self.transform_length = self.r * self.c
+        self.psi_list = [util.root_of_unity(2 * self.transform_length, q) for q in self.moduli]
+        self.omega_list = [(psi * psi) % q for psi, q in zip(self.psi_list, self.moduli)]
+        # perf_test replaced the tables by random bits in the reference
+        # (ntt_mm.py:150-171); the real tables cost the same here, so they are
+        # always used and results stay checkable.
+        self.perf_test = perf_test
+        self.memory_aligned_transformation()
+        self.ntt_tf_step1, self.ntt_tf_step2, self.ntt_tf_step3 = self.ntt_coefficients_precompute()
+        self.intt_tf_step1, self.intt_tf_step2, self.intt_tf_step3 = self.intt_coefficients_precompute()
+        self.ntt_bat_tf_step1 = basis_aligned_transformation(self.ntt_tf_step1, self.moduli)
+        self.ntt_bat_tf_step3 = basis_aligned_transformation(self.ntt_tf_step3, self.moduli)
+        self.intt_bat_tf_step1 = basis_aligned_transformation(self.intt_tf_step1, self.moduli)
+        self.intt_bat_tf_step3 = basis_aligned_transformation(self.intt_tf_step3, self.moduli)
+        self._plan = None
+        self._plan_barrett = None
+
+    # -- offline --------------------------------------------------------------
+    def memory_aligned_transformation(self):
+        """ntt_mm.py:257-277."""
+        self.perm_r = get_bit_reverse_perm(self.r)
+        self.perm_c = get_bit_reverse_perm(self.c)
+
+    def ntt_coefficients_precompute(self):
+        """ntt_mm.py:186-209."""
+        t1, t2, t3 = [], [], []
+        for i, q in enumerate(self.moduli):
+            om = self.omega_list[i]
+            t1.append(util.twiddle_matrix(self.r, self.r, q, pow(om, self.c, q))[self.perm_r, :])
+            t2.append(util.twiddle_matrix(self.r, self.c, q, om)[self.perm_r, :])
+            t3.append(util.twiddle_matrix(self.c, self.c, q, pow(om, self.r, q))[:, self.perm_c])
+        st = lambda v: np.stack(v, -1).astype(U32)  # noqa: E731
+        return st(t1), st(t2), st(t3)
+
+    def intt_coefficients_precompute(self):
+        """ntt_mm.py:211-240."""
+        t1, t2, t3 = [], [], []
+        for i, q in enumerate(self.moduli):
+            om = self.omega_list[i]
+            inv_col = pow(pow(om, self.c, q), -1, q)
+            inv_row = pow(pow(om, self.r, q), -1, q)
+            a = util.twiddle_matrix(self.c, self.c, q, inv_row)[self.perm_c, :]
+            b = util.twiddle_matrix(self.r, self.c, q, pow(om, -1, q))[self.perm_r, :]
+            d = util.twiddle_matrix(self.r, self.r, q, inv_col)[:, self.perm_r]
+            b = (b * U64(pow(self.c, -1, q))) % U64(q)
+            d = (d * U64(pow(self.r, -1, q))) % U64(q)
+            t1.append(a)
+            t2.append(b)
+            t3.append(d)
+        st = lambda v: np.stack(v, -1).astype(U32)  # noqa: E731
+        return st(t1), st(t2), st(t3)
+
+    def to_computation_format(self, a):
+        return self.ff_ctx.to_computation_format(np.asarray(a).astype(U64)).astype(U32)
+
+    def to_original_format(self, a):
+        return self.ff_ctx.to_original_format(np.asarray(a).astype(U64)).astype(U32)
+
+    def get_jax_parameters(self):
+        return {"rows": self.r, "cols": self.c, "finite_field_parameters": self.ff_ctx.get_jax_parameters()}
+
+    # -- device plan ----------------------------------------------------------
+    def _moduli_ctx(self) -> ff_context.BarrettContext:
+        M = self.ntt_tf_step2.shape[-1]
+        if self._plan_barrett is None or len(self._plan_barrett.moduli) != M:
+            self._plan_barrett = ff_context.BarrettContext(self.moduli[:M])
+        return self._plan_barrett
+
+    def plan(self):
+        """The cross_ntt_plan of the current (possibly dropped) moduli."""
+        if self._plan is None:
+            c = lambda a: np.ascontiguousarray(a)  # noqa: E731
+            arrs = [c(self.ntt_bat_tf_step1), c(self.ntt_tf_step2.astype(U32)), c(self.ntt_bat_tf_step3),
+                    c(self.intt_bat_tf_step1), c(self.intt_tf_step2.astype(U32)), c(self.intt_bat_tf_step3)]
+            out = _lib.vp()
+            _lib.check(_lib.lib().cross_ntt_plan_create(self._moduli_ctx().handle(), self.r, self.c,
+                                                        *[a.ctypes.data for a in arrs], _lib.C.byref(out)),
+                       "cross_ntt_plan_create")
+            self._plan = out
+        return self._plan
+
+    def __del__(self):
+        if getattr(self, "_plan", None) is not None and _lib._lib is not None:
+            _lib._lib.cross_ntt_plan_destroy(self._plan)
+            self._plan = None
+
+    # -- online ---------------------------------------------------------------
+    def _run(self, v, inverse: bool):
+        x = _tensor.to_u32(v)
+        M = self.ntt_tf_step2.shape[-1]
+        if x.dim() != 4 or tuple(x.shape[1:]) != (self.r, self.c, M):
+            raise ValueError(f"expected (B, {self.r}, {self.c}, {M}), got {tuple(x.shape)}")
+        out = _tensor.empty_u32(x.shape)
+        B = x.shape[0]
+        L = _lib.lib()
+        ws = _tensor.workspace(L.cross_ntt_workspace_size(self.plan(), B, _lib.LAYOUT_REFERENCE))
+        _tensor.call("cross_ntt", self.plan(), int(inverse), x.data_ptr(), out.data_ptr(), B,
+                     _lib.LAYOUT_REFERENCE, ws.data_ptr(), ws.numel(), _lib.cuda_stream())
+        return out
+
+    def ntt(self, v):
+        """ntt_mm.py:351-378: (B, R, C, M) uint32 -> bit-reversed evaluations."""
+        return self._run(v, False)
+
+    def intt(self, v):
+        """ntt_mm.py:380-407."""
+        return self._run(v, True)
+
+    def ntt_limb(self, v, limb_index: int):
+        """ntt_mm.py:295-321: (B, R, C) for one limb."""
+        return self._single(limb_index).ntt(_tensor.to_u32(v).unsqueeze(-1))[..., 0]
+
+    def intt_limb(self, v, limb_index: int):
+        """ntt_mm.py:323-349."""
+        return self._single(limb_index).intt(_tensor.to_u32(v).unsqueeze(-1))[..., 0]
+
+    def _single(self, i):
+        return NTTCiphertextBarrettContext([self.moduli[i]], {"r": self.r, "c": self.c})
+
+    def drop_last_modulus(self):
+        """ntt_mm.py:412-419."""
+        for name in ("ntt_bat_tf_step1", "ntt_tf_step2", "ntt_bat_tf_step3",
+                     "intt_bat_tf_step1", "intt_tf_step2", "intt_bat_tf_step3"):
+            setattr(self, name, np.ascontiguousarray(getattr(self, name)[..., :-1]))
+        self.ff_ctx.drop_last_modulus()
+        if self._plan is not None:
+            _lib.lib().cross_ntt_plan_destroy(self._plan)
+            self._plan = None
+
+
+class NTTCiphertextBarrettContext(NTTCiphertextContextBase):
+    """ntt_mm.py:421-429."""
+
+    def __init__(self, moduli, parameters: dict, perf_test: bool = False):
+        super().__init__(moduli, parameters, perf_test=perf_test)
+        if self.ff_ctx is None:
+            self.ff_ctx = ff_context.BarrettContext(self.moduli)
+        assert self.ff_ctx is not None, "finite_field_context must be provided"
+        assert self.moduli == list(self.ff_ctx.moduli), "moduli must be the same as the moduli of the finite_field_context"
+
+
+class _UnsupportedDeviceNTT(NTTCiphertextContextBase):
+    """Montgomery / Shoup / BAT-lazy NTT contexts: the constructors and tables
+    are the reference's; the device transforms are not implemented (they are
+    off the HE-Mult / HE-Rotate path, which always uses Barrett)."""
+
+    def ntt(self, v):
+        raise NotImplementedError(f"{type(self).__name__}.ntt has no device kernel; use NTTCiphertextBarrettContext")
+
+    intt = ntt
+
+
+class NTTCiphertextMontgomeryContext(_UnsupportedDeviceNTT):
+    """ntt_mm.py:432-440."""
+
+
+class NTTCiphertextShoupContext(_UnsupportedDeviceNTT):
+    """ntt_mm.py:443-587."""
+
+
+class NTTCiphertextBATLazyContext(_UnsupportedDeviceNTT):
+    """ntt_mm.py:590-658."""

@@ -1,0 +1,260 @@
+/*
+ * cross_b200.h -- C ABI of the B200-native (sm_100a) CKKS hot path of
+ * EfficientPPML/CROSS (jaxite_word).
+ *
+ * Conventions
+ *   - Every entry point returns 0 (CROSS_OK) or a negative cross_status;
+ *     nothing is thrown across the ABI.  cross_last_error() returns a
+ *     per-thread message describing the last failure.
+ *   - Device buffers are caller-owned.  Operators that need scratch take a
+ *     (workspace, workspace_bytes) pair sized by the matching
+ *     *_workspace_size() query; nothing is allocated on the operator path.
+ *     Plan creation allocates and uploads the plan's constants once.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *   - Plans are immutable after creation (the *_set_keys calls complete
+ *     creation) and may be used concurrently on different streams.
+ *   - Integer semantics are those of the reference: uint32 residues, uint64
+ *     intermediates with wrap-around, lazy Barrett outputs (values may lie in
+ *     [q, 2q)), so results are bit-identical to jaxite_word.
+ *   - Layouts: CROSS_LAYOUT_REFERENCE is jaxite_word's (..., r, c, limbs),
+ *     limb-innermost.  CROSS_LAYOUT_LIMB_MAJOR is (..., limbs, r, c): each
+ *     limb-polynomial contiguous, the internal layout of the kernels.
+ */
+#ifndef CROSS_B200_H_
+#define CROSS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CROSS_B200_ABI_VERSION 1
+
+typedef enum cross_status {
+  CROSS_OK = 0,
+  CROSS_ERR_INVALID_ARG = -1,
+  CROSS_ERR_CUDA = -2,
+  CROSS_ERR_UNSUPPORTED = -3,
+  CROSS_ERR_WORKSPACE = -4,
+  CROSS_ERR_TIMEOUT = -5
+} cross_status;
+
+typedef enum cross_layout {
+  CROSS_LAYOUT_REFERENCE = 0,
+  CROSS_LAYOUT_LIMB_MAJOR = 1
+} cross_layout;
+
+typedef struct cross_moduli_s* cross_moduli;
+typedef struct cross_ntt_plan_s* cross_ntt_plan;
+typedef struct cross_bconv_plan_s* cross_bconv_plan;
+typedef struct cross_hemul_plan_s* cross_hemul_plan;
+typedef struct cross_herot_plan_s* cross_herot_plan;
+
+int cross_abi_version(void);
+const char* cross_last_error(void);
+/* Number of CUDA kernels this library has launched in the process (all
+ * threads); a diagnostic for benchmarks. */
+uint64_t cross_launch_count(void);
+
+/* ------------------------------------------------------------------ */
+/* Modulus sets                                                        */
+/* ------------------------------------------------------------------ */
+
+/* A list of RNS moduli with their Barrett constants.
+ * Replaces finite_field.BarrettContext.__init__ (finite_field.py:171-185):
+ * barrett_m = floor(2^s / q), barrett_w = min(s, 32),
+ * barrett_s_w = s - w with s = 2*ceil(log2 q), computed by the caller.
+ * Moduli must be odd and below 2^31 (ntt_mm.py:142).  Host arrays. */
+int cross_moduli_create(int num_moduli, const uint32_t* moduli, const uint64_t* barrett_m,
+                        const uint32_t* barrett_w, const uint32_t* barrett_s_w,
+                        cross_moduli* out);
+int cross_moduli_destroy(cross_moduli moduli);
+
+/* ------------------------------------------------------------------ */
+/* Elementwise modular kernels (reference layout: last axis = limbs;   */
+/* `rows` is the product of all other axes)                            */
+/* ------------------------------------------------------------------ */
+
+/* BarrettContext.modular_reduction (finite_field.py:201-230) as used by
+ * Ciphertext.mod_reduce (ciphertext.py:195-197): out[i,m] = Barrett_m(in[i,m]).
+ * `in` is uint64 when in_is_u64, else uint32. */
+int cross_mod_reduce(cross_moduli moduli, const void* in, int in_is_u64, uint32_t* out,
+                     int64_t rows, void* stream);
+
+/* Ciphertext.modmul (ciphertext.py:189-193) with the broadcast the reference
+ * uses for its constant tables: out[i,m] = Barrett_m(a[i,m] * b[i % b_rows, m])
+ * computed in uint64 with wrap-around. */
+int cross_modmul(cross_moduli moduli, const void* a, int a_is_u64, const void* b, int b_is_u64,
+                 int64_t b_rows, uint32_t* out, int64_t rows, void* stream);
+
+/* Ciphertext.ciphertext_mult (ciphertext.py:309-324).  ct: (batch, 4, n, M);
+ * out01: (batch, 2, n, M) = (a0*b0, a0*b1 + a1*b0); out2: (batch, 1, n, M) = a1*b1. */
+int cross_tensor_product(cross_moduli moduli, const uint32_t* ct, uint32_t* out01, uint32_t* out2,
+                         int64_t batch, int64_t n, void* stream);
+
+/* add.jax_add (add.py:7-27): a, b, out (elements, M, n); result a+b (uint32
+ * wrap) minus q where it is strictly greater than q. */
+int cross_add_mod(cross_moduli moduli, const uint32_t* a, const uint32_t* b, uint32_t* out,
+                  int64_t elements, int64_t n, void* stream);
+
+/* Galois automorphism of herot.py:300: out[b, e, j, :] = in[b, e, coef_map[j], :]
+ * for in/out (batch*elements, n, M); coef_map is a device int32 array of n. */
+int cross_automorphism(const uint32_t* in, const int32_t* coef_map, uint32_t* out,
+                       int64_t polys, int64_t n, int num_limbs, void* stream);
+
+/* Layout conversion between (polys, n, M) and (polys, M, n). */
+int cross_to_limb_major(const uint32_t* in, uint32_t* out, int64_t polys, int64_t n, int num_limbs,
+                        void* stream);
+int cross_to_reference(const uint32_t* in, uint32_t* out, int64_t polys, int64_t n, int num_limbs,
+                       void* stream);
+
+/* ------------------------------------------------------------------ */
+/* BAT matrix NTT / INTT                                               */
+/* ------------------------------------------------------------------ */
+
+/* Replaces NTTCiphertextBarrettContext.__init__ (ntt_mm.py:136-181, 421-429):
+ * the plan takes the reference's precomputed tables (host arrays, reference
+ * shapes) and stores them in the kernels' layouts:
+ *   ntt_bat_tf_step1  (r, 4, r, 4, M) u8      ntt_tf_step2  (r, c, M) u32
+ *   ntt_bat_tf_step3  (c, 4, c, 4, M) u8
+ *   intt_bat_tf_step1 (c, 4, c, 4, M) u8      intt_tf_step2 (r, c, M) u32
+ *   intt_bat_tf_step3 (r, 4, r, 4, M) u8
+ * (the reference keeps tf_step2 as uint64; every value is below q < 2^31). */
+int cross_ntt_plan_create(cross_moduli moduli, int r, int c,
+                          const uint8_t* ntt_bat_tf_step1, const uint32_t* ntt_tf_step2,
+                          const uint8_t* ntt_bat_tf_step3, const uint8_t* intt_bat_tf_step1,
+                          const uint32_t* intt_tf_step2, const uint8_t* intt_bat_tf_step3,
+                          cross_ntt_plan* out);
+int cross_ntt_plan_destroy(cross_ntt_plan plan);
+
+/* Scratch needed by cross_ntt for `batch` polynomials of all plan limbs. */
+size_t cross_ntt_workspace_size(cross_ntt_plan plan, int64_t batch, int layout);
+
+/* NTTCiphertextBarrettContext.ntt / .intt (ntt_mm.py:351-407):
+ * in/out (batch, r, c, M) for CROSS_LAYOUT_REFERENCE or (batch, M, r, c) for
+ * CROSS_LAYOUT_LIMB_MAJOR, uint32.  Output of ntt is in bit-reversed
+ * evaluation order, exactly as the reference.  in may equal out. */
+int cross_ntt(cross_ntt_plan plan, int inverse, const uint32_t* in, uint32_t* out, int64_t batch,
+              int layout, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* BAT basis conversion                                                */
+/* ------------------------------------------------------------------ */
+
+/* Replaces BConv.control_gen for one (src, dst) control
+ * (bconv.py:67-155): qhat_inv_modq (size_q) u32, qhat_modp (size_q, size_p)
+ * u32 and its BAT form qhat_modp_bat (4*size_q, size_p, 4) u8. */
+int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* qhat_inv_modq,
+                            const uint32_t* qhat_modp, const uint8_t* qhat_modp_bat,
+                            cross_bconv_plan* out);
+int cross_bconv_plan_destroy(cross_bconv_plan plan);
+
+/* BConv.basis_change_bat (bconv.py:215-252) when bat != 0, else
+ * BConv.basis_change (bconv.py:173-212).  CROSS_LAYOUT_REFERENCE:
+ * in (batch, n, size_q) -> out (batch, n, size_p);  CROSS_LAYOUT_LIMB_MAJOR:
+ * in (batch, size_q, n) -> out (batch, size_p, n). */
+int cross_bconv(cross_bconv_plan plan, int bat, const uint32_t* in, uint32_t* out, int64_t batch,
+                int64_t n, int layout, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Rescale by the last prime (ciphertext.py:223-303)                   */
+/* ------------------------------------------------------------------ */
+
+typedef struct cross_rescale_plan_s* cross_rescale_plan;
+
+typedef struct cross_rescale_desc {
+  int r, c;                   /* degree layout of the ciphertext                        */
+  int L;                      /* limbs before rescale                                   */
+  cross_ntt_plan ntt_q;       /* plan over Q (L moduli, same order) with (r, c)         */
+  const uint32_t* inv_psi_last;  /* (N)      psi_{q_{L-1}}^{-i}     (ciphertext.py:244-248) */
+  const uint32_t* gamma_psi;     /* (L-1, N) gamma_i psi_i^i        (ciphertext.py:239-243) */
+  const uint32_t* betas;         /* (L-1)    q_{L-1}^{-1} mod q_i   (ciphertext.py:254)     */
+} cross_rescale_desc;
+
+/* Ciphertext.modulus_switch_control_gen (ciphertext.py:223-265). */
+int cross_rescale_plan_create(const cross_rescale_desc* desc, cross_rescale_plan* out);
+int cross_rescale_plan_destroy(cross_rescale_plan plan);
+size_t cross_rescale_workspace_size(cross_rescale_plan plan, int64_t polys, int layout);
+/* Ciphertext.rescale (ciphertext.py:267-303): in (polys, r, c, L) -> out
+ * (polys, r, c, L-1) (limb-major: (polys, L, N) -> (polys, L-1, N)). */
+int cross_rescale(cross_rescale_plan plan, const uint32_t* in, uint32_t* out, int64_t polys, int layout,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* HE-Mult with relinearisation (hemul.py)                             */
+/* ------------------------------------------------------------------ */
+
+typedef struct cross_hemul_desc {
+  int r, c;            /* HEMul degree layout (hemul.py:12-28)                        */
+  int L;               /* limbs of the input ciphertext, |Q| (dropped to L-1 by rescale) */
+  int K;               /* special limbs |P|                                           */
+  int dnum;            /* key-switch digits (ciphertext.py:354)                       */
+  /* plan over Q then P (L + K moduli) with factorisation (r, c)                      */
+  cross_ntt_plan ntt_qp;
+  /* plan over P with the default factorisation of ciphertext.py:69-70, used by the
+   * ModDown INTT (hemul.py:76-77,179-180); may equal ntt_qp when (r, c) is it       */
+  cross_ntt_plan ntt_p;
+  int ntt_p_limb_offset;   /* index of P[0] inside ntt_p (L when ntt_p == ntt_qp, else 0) */
+  /* ceil((L-1)/alpha) controls: digit j -> its complement in Q' + P (bconv indices
+   * are positions in the Q' + P list), then one control P -> Q'                    */
+  cross_bconv_plan* ks_bconv;
+  cross_bconv_plan down_bconv;
+  const uint32_t* inv_psi_last;   /* (N)      psi_{q_{L-1}}^{-i}   (hemul.py:47-50)   */
+  const uint32_t* gamma_psi;      /* (L-1, N) gamma_i psi_i^i      (ciphertext.py:239-243) */
+  const uint32_t* betas;          /* (L-1)                         (ciphertext.py:254) */
+  const uint32_t* inv_psi_q;      /* (L-1, N) psi_i^{-i} over Q'   (ciphertext.py:381-394) */
+  const uint32_t* psi_qp;         /* (L-1+K, N) psi^i over Q' + P  (ciphertext.py:343-350) */
+  const uint32_t* inv_psi_p;      /* (K, N)   psi^{-i} over P      (hemul.py:91-97)    */
+  const uint32_t* p_inv_mod_q;    /* (L-1)    P^{-1} mod q_i       (hemul.py:105-111)  */
+} cross_hemul_desc;
+
+int cross_hemul_plan_create(const cross_hemul_desc* desc, cross_hemul_plan* out);
+/* HEMul.setup_relinearization (hemul.py:134-151, ciphertext.py:445-451):
+ * evk_a, evk_b host arrays (dnum, N, key_limbs) with key_limbs >= L-1+K;
+ * limbs [0, L-1) and the last K are used. */
+int cross_hemul_set_keys(cross_hemul_plan plan, const uint32_t* evk_a, const uint32_t* evk_b,
+                         int key_limbs);
+int cross_hemul_plan_destroy(cross_hemul_plan plan);
+size_t cross_hemul_workspace_size(cross_hemul_plan plan, int64_t batch, int layout);
+/* HEMul.mul (hemul.py:153-217): in (batch, 4, r, c, L) -> out (batch, 2, r, c, L-1)
+ * (limb-major: (batch, 4, L, r, c) -> (batch, 2, L-1, r, c)). */
+int cross_hemul(cross_hemul_plan plan, const uint32_t* in, uint32_t* out, int64_t batch, int layout,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* HE-Rotate (herot.py)                                                */
+/* ------------------------------------------------------------------ */
+
+typedef struct cross_herot_desc {
+  int r, c;            /* input degree layout (only N = r*c matters)                 */
+  int L, K, dnum;
+  /* plan over Q then P with the default factorisation (herot.py:160-175 build every
+   * Ciphertext without a finite_field_context)                                       */
+  cross_ntt_plan ntt_qp;
+  cross_bconv_plan* ks_bconv;     /* dnum controls: digit j -> complement in Q + P    */
+  cross_bconv_plan down_bconv;    /* P -> Q                                           */
+  const uint32_t* inv_psi_q;      /* (L, N)                                           */
+  const uint32_t* psi_qp;         /* (L+K, N)                                         */
+  const uint32_t* inv_psi_p;      /* (K, N)                                           */
+  const uint32_t* p_inv_mod_q;    /* (L)                                              */
+} cross_herot_desc;
+
+int cross_herot_plan_create(const cross_herot_desc* desc, cross_herot_plan* out);
+/* HERot.setup_rotate (herot.py:178-181): evk (dnum, N, L+K) host arrays and the
+ * coefficient map (N) host int32 array. */
+int cross_herot_set_keys(cross_herot_plan plan, const uint32_t* evk_a, const uint32_t* evk_b,
+                         const int32_t* coef_map);
+int cross_herot_plan_destroy(cross_herot_plan plan);
+size_t cross_herot_workspace_size(cross_herot_plan plan, int64_t batch, int layout);
+/* HERot.rotate (herot.py:183-302): in (batch, 2, r, c, L) -> out (batch, 2, N, L)
+ * (limb-major: (batch, 2, L, N) -> (batch, 2, L, N)). */
+int cross_herot(cross_herot_plan plan, const uint32_t* in, uint32_t* out, int64_t batch, int layout,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* CROSS_B200_H_ */

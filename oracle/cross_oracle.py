@@ -17,6 +17,7 @@ limb-innermost, uint32.
 
 from __future__ import annotations
 
+import functools
 import math
 from typing import List, Sequence
 
@@ -47,6 +48,7 @@ def prime_factors(n: int) -> set:
     return factors
 
 
+@functools.lru_cache(maxsize=None)
 def find_generator(q: int) -> int:
     """util.py:193-213: smallest generator of GF(q)^*."""
     phi = q - 1
@@ -57,6 +59,7 @@ def find_generator(q: int) -> int:
     raise ValueError("No generator found, check that q is prime.")
 
 
+@functools.lru_cache(maxsize=None)
 def root_of_unity(m: int, q: int) -> int:
     """util.py:219-249: minimal primitive m-th root of unity mod q."""
     assert (q - 1) % m == 0, "q-1 must be divisible by m"

@@ -1,0 +1,318 @@
+"""GPU parity: every operator through the C ABI against the CPU oracle
+(bit-exact) and against the reference's golden vectors."""
+import numpy as np
+import pytest
+
+from oracle import cross_oracle as O
+from tests.conftest import load_golden, rng_residues
+
+pytestmark = pytest.mark.gpu
+U32 = np.uint32
+parse = O.parse_ciphertext_string
+
+
+def _np(t):
+    return t.cpu().numpy()
+
+
+# ---------------------------------------------------------------------------
+# NTT
+# ---------------------------------------------------------------------------
+
+def test_ntt_golden():
+    """ntt_mm_test.py:33-54."""
+    from cross_b200 import ntt_mm, finite_field
+    g = load_golden("ntt_mm")
+    r, c, b = g["r"], g["c"], 2
+    coef = np.concatenate([np.array(g["coef_in"], np.uint64).T.reshape(1, r * c, -1)] * b, 0).astype(U32)
+    ev = np.concatenate([np.array(g["eval_in"], U32).T.reshape(1, r * c, -1)] * b, 0)
+    ctx = ntt_mm.NTTCiphertextBarrettContext(g["moduli"], {"r": r, "c": c,
+                                                           "finite_field_context": finite_field.BarrettContext(g["moduli"])})
+    out = ctx.ntt(coef.reshape(b, r, c, -1))
+    np.testing.assert_array_equal(_np(out).reshape(b, r * c, -1), ev)
+    np.testing.assert_array_equal(_np(ctx.intt(out)).reshape(b, r * c, -1), coef)
+
+
+@pytest.mark.parametrize("n,r,c,limbs,batch", [(4096, 64, 64, 8, 16), (4096, 32, 128, 3, 2), (1024, 32, 32, 5, 3),
+                                               (65536, 256, 256, 4, 2), (65536, 128, 512, 2, 1)])
+def test_ntt_intt_vs_oracle(n, r, c, limbs, batch):
+    from cross_b200 import ntt_mm
+    q = O.find_moduli_ntt(limbs, 28, 2 * n)
+    x = rng_residues(np.random.default_rng(n + limbs), (batch, r, c, limbs), q)
+    ctx = ntt_mm.NTTCiphertextBarrettContext(q, {"r": r, "c": c})
+    ref = O.NTTBarrett(q, r, c)
+    y = ctx.ntt(x)
+    yr = ref.ntt(x)
+    np.testing.assert_array_equal(_np(y), yr)
+    np.testing.assert_array_equal(_np(ctx.intt(y)), ref.intt(yr))
+
+
+def test_ntt_round_trip_and_linearity_full_size():
+    """Size-independent properties at N = 2^16, 24 limbs: INTT(NTT(x)) == x mod q
+    and NTT(x + y) == NTT(x) + NTT(y) mod q."""
+    from cross_b200 import ntt_mm
+    n, L, B = 65536, 24, 2
+    q = O.find_moduli_ntt(L, 28, 2 * n)
+    qa = np.array(q, np.int64)
+    rng = np.random.default_rng(7)
+    x = rng_residues(rng, (B, 256, 256, L), q)
+    y = rng_residues(rng, (B, 256, 256, L), q)
+    ctx = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 256, "c": 256})
+    fx, fy = _np(ctx.ntt(x)).astype(np.int64), _np(ctx.ntt(y)).astype(np.int64)
+    back = _np(ctx.intt(ctx.ntt(x))).astype(np.int64)
+    assert not ((back - x) % qa).any()
+    s = ((x.astype(np.int64) + y) % qa).astype(U32)
+    fs = _np(ctx.ntt(s)).astype(np.int64)
+    assert not ((fs - fx - fy) % qa).any()
+
+
+# ---------------------------------------------------------------------------
+# BConv
+# ---------------------------------------------------------------------------
+
+def test_bconv_golden():
+    """bconv_test.py:28-48 (+ BAT congruence)."""
+    from cross_b200 import bconv
+    g = load_golden("bconv")
+    x = np.array(g["in_tower"], np.uint64).T.astype(U32)
+    ref = np.array(g["reference_result"], np.uint64).T
+    b = bconv.BConvBarrett(g["original_moduli"] + g["target_moduli"])
+    b.control_gen([(list(range(2)), list(range(2, 7)))])
+    np.testing.assert_array_equal(_np(b.basis_change(x)), ref)
+    o = O.BConvBarrett(g["original_moduli"] + g["target_moduli"])
+    o.control_gen([(list(range(2)), list(range(2, 7)))])
+    np.testing.assert_array_equal(_np(b.basis_change_bat(x)), o.basis_change_bat(x))
+
+
+def test_bconv_small_primes():
+    """bconv_test.py:78-120."""
+    from cross_b200 import bconv
+    b = bconv.BConvBarrett([17, 19, 23, 29])
+    b.control_gen([([0], [2]), ([1], [3])])
+    assert int(_np(b.basis_change(np.array([[[15]]], U32), 0))[0, 0, 0]) == 15
+    assert int(_np(b.basis_change(np.array([[[20]]], U32), 1))[0, 0, 0]) == 1
+    assert int(_np(b.basis_change(np.array([[[20]]], U32), 0))[0, 0, 0]) == 3
+
+
+@pytest.mark.parametrize("n,sq,sp,batch", [(4096, 24, 25, 2), (256, 8, 23, 3), (65536, 24, 25, 1)])
+def test_bconv_vs_oracle(n, sq, sp, batch):
+    from cross_b200 import bconv
+    ov = O.find_moduli_ntt(sq + sp, 28, 2 * n)
+    x = rng_residues(np.random.default_rng(sq), (batch, n, sq), ov[:sq])
+    b = bconv.BConvBarrett(ov)
+    b.control_gen([(list(range(sq)), list(range(sq, sq + sp)))])
+    o = O.BConvBarrett(ov)
+    o.control_gen([(list(range(sq)), list(range(sq, sq + sp)))])
+    np.testing.assert_array_equal(_np(b.basis_change_bat(x)), o.basis_change_bat(x))
+    np.testing.assert_array_equal(_np(b.basis_change(x)), o.basis_change(x))
+
+
+# ---------------------------------------------------------------------------
+# Elementwise
+# ---------------------------------------------------------------------------
+
+def test_elementwise_vs_oracle():
+    from cross_b200 import add, finite_field
+    from cross_b200.ciphertext import Ciphertext
+    q = O.find_moduli_ntt(5, 30, 2 * 64)
+    rng = np.random.default_rng(3)
+    z = rng.integers(0, 2 ** 64 - 1, size=(7, 5), dtype=np.uint64)
+    ff = finite_field.BarrettContext(q)
+    np.testing.assert_array_equal(_np(ff.modular_reduction(z)), O.Barrett(q).reduce(z))
+    a = rng_residues(rng, (3, 5, 64), q)
+    b = rng_residues(rng, (3, 5, 64), q)
+    a[0, 0, :4] = np.array(q[0]) - b[0, 0, :4]  # sums equal to q stay (add.py uses >)
+    np.testing.assert_array_equal(_np(add.jax_add(a, b, np.array(q))), O.jax_add(a, b, q))
+    ct = Ciphertext({"batch": 2, "num_elements": 4, "degree": 64, "num_moduli": 5, "precision": 32,
+                     "degree_layout": (8, 8)}, {"moduli": q})
+    x = rng_residues(rng, (2, 4, 8, 8, 5), q)
+    ct.set_batch_ciphertext(x)
+    m01, m2 = ct.ciphertext_mult()
+    r01, r2 = O.ciphertext_mult(x, O.Barrett(q))
+    np.testing.assert_array_equal(_np(m01), r01)
+    np.testing.assert_array_equal(_np(m2), r2)
+    tab = rng_residues(rng, (8, 8, 5), q).astype(np.uint64)
+    ct.set_batch_ciphertext(x)
+    ct.modmul(tab)
+    np.testing.assert_array_equal(_np(ct.ciphertext), O._modmul(O.Barrett(q), x, tab))
+
+
+# ---------------------------------------------------------------------------
+# Ciphertext: rescale and key switch
+# ---------------------------------------------------------------------------
+
+def test_rescale_golden():
+    """rescale_test.py:49-87."""
+    from cross_b200.ciphertext import Ciphertext
+    g = load_golden("rescale")
+    inc = np.array(parse(g["in_ciphertexts_str"])[0], U32)
+    fin = np.array(parse(g["final_result_str"])[0], U32)
+    for b in (1, 2):
+        x = np.tile(np.transpose(inc, (0, 2, 1))[None], (b, 1, 1, 1)).reshape(b, 2, 4, 4, 5)
+        ct = Ciphertext({"batch": b, "num_elements": 2, "degree": 16, "num_moduli": 5, "precision": 32},
+                        {"moduli": g["q_towers"], "r": 4, "c": 4})
+        ct.modulus_switch_control_gen(degree_layout=(4, 4))
+        ct.set_batch_ciphertext(x)
+        ct.rescale()
+        res = _np(ct.get_batch_ciphertext()).reshape(b, 2, 16, 4)
+        for i in range(b):
+            np.testing.assert_array_equal(np.transpose(res[i], (0, 2, 1)), fin)
+
+
+def test_rescale_vs_oracle_n4096():
+    from cross_b200.ciphertext import Ciphertext
+    q = O.find_moduli_ntt(6, 28, 2 * 4096)
+    x = rng_residues(np.random.default_rng(11), (2, 2, 64, 64, 6), q)
+    ct = Ciphertext({"batch": 2, "num_elements": 2, "degree": 4096, "num_moduli": 6, "precision": 32,
+                     "degree_layout": (64, 64)}, {"moduli": q})
+    ct.modulus_switch_control_gen(degree_layout=(64, 64))
+    ct.set_batch_ciphertext(x)
+    np.testing.assert_array_equal(_np(ct.rescale()), O.RescalePlan(q, 64, 64).rescale(x))
+
+
+def test_key_switch_vs_oracle():
+    from cross_b200.ciphertext import Ciphertext
+    from cross_b200 import finite_field
+    n, L, K, dnum = 256, 5, 2, 3
+    q = O.find_moduli_ntt(L + K, 28, 2 * n)
+    rng = np.random.default_rng(5)
+    evk_a = rng_residues(rng, (dnum, n, L + K), q)
+    evk_b = rng_residues(rng, (dnum, n, L + K), q)
+    x = rng_residues(rng, (2, 1, 16, 16, L), q[:L])
+    ct = Ciphertext({"batch": 2, "num_elements": 1, "degree": n, "num_moduli": L, "precision": 32,
+                     "degree_layout": (16, 16)},
+                    {"moduli": q[:L], "r": 16, "c": 16, "finite_field_context": finite_field.BarrettContext})
+    ct.key_switch_control_gen(q[L:], dnum, evk_a, evk_b)
+    ct.set_batch_ciphertext(x)
+    ct.key_switch()
+    ref = O.KeySwitchPlan(q[:L], q[L:], dnum, evk_a, evk_b, 16, 16).key_switch(x)
+    np.testing.assert_array_equal(_np(ct.get_batch_ciphertext()), ref)
+
+
+# ---------------------------------------------------------------------------
+# HE-Mult / HE-Rotate
+# ---------------------------------------------------------------------------
+
+def test_hemul_golden_e2e():
+    """hemul_test.py:64-140: bit-exact HE-Mult, decrypt bit-exact, decode within
+    an absolute tolerance of 1.5e-3 (decimal=3)."""
+    from cross_b200 import hemul
+    g = load_golden("hemul")
+    he = hemul.HEMul(1, 4, 4, 3, 1, g["q_towers"], g["p_towers"])
+    he.control_gen(degree_layout=(4, 4))
+    he.setup_relinearization(np.array(g["evalkey_a_vector"], U32), np.array(g["evalkey_b_vector"], U32))
+    out = _np(he.mul(np.array(g["input_ciphertext"], U32)))
+    np.testing.assert_array_equal(out, np.array(g["encrypted_mult_result_ref"], U32))
+    enc = out.reshape(1, 2, 16, 4)
+    dec = O.ckks_decrypt([enc[0, 0].tolist(), enc[0, 1].tolist()], g["secret_key"], g["q_towers"][:4])
+    assert dec == g["decrypted_result_ref"]
+    qt = g["q_towers"]
+    vals = O.ckks_decode(dec, qt, (g["scalingFactor"] / qt[-1]) ** 2, g["num_slots"], g["p"])
+    assert np.max(np.abs(vals.real - np.array(g["real_values_multiply_result"]))) < 1.5e-3
+
+
+def test_herot_golden():
+    """herot_test.py:229-251."""
+    from cross_b200 import herot, util
+    g = load_golden("herot")
+    r, c, dnum = 4, 4, 3
+    rin, rmod = parse(g["rotate_in_ciphertext_str"])
+    eb, ebm = parse(g["evalkey_b_vector_str"])
+    ea, _ = parse(g["evalkey_a_vector_str"])
+    x = np.array(rin, U32).transpose(0, 2, 1).reshape(1, -1, r, c, len(rmod))
+    evb = np.array(eb, np.uint64).transpose(0, 2, 1).reshape(dnum, r, c, len(ebm))
+    eva = np.array(ea, np.uint64).transpose(0, 2, 1).reshape(dnum, r, c, len(ebm))
+    fin = np.array(parse(g["final_result_str"])[0], U32).transpose(0, 2, 1).reshape(1, -1, 16, len(rmod))
+    cm = util.precompute_auto_map(16, util.find_automorphism_index_2n_complex(1, 16))
+    assert cm == g["coef_map"]
+    h = herot.HERot(r, c, dnum, rmod, ebm[len(rmod):])
+    h.control_gen(batch=1, degree_layout=(r, c))
+    h.setup_rotate(eva, evb, cm)
+    np.testing.assert_array_equal(_np(h.rotate(x)), fin)
+
+
+@pytest.mark.parametrize("n,r,c,L,K,dnum,batch", [(4096, 64, 64, 8, 3, 3, 2), (4096, 32, 128, 6, 2, 2, 1),
+                                                  (1024, 32, 32, 5, 2, 3, 3)])
+def test_hemul_vs_oracle(n, r, c, L, K, dnum, batch):
+    from cross_b200 import hemul
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    Q, P = ov[:L], ov[L:]
+    rng = np.random.default_rng(n + L)
+    ct = rng_residues(rng, (batch, 4, r, c, L), Q)
+    evk_a = rng_residues(rng, (dnum, n, L + K), ov)
+    evk_b = rng_residues(rng, (dnum, n, L + K), ov)
+    he = hemul.HEMul(batch, r, c, dnum, 1, Q, P)
+    he.control_gen(degree_layout=(r, c))
+    he.setup_relinearization(evk_a, evk_b)
+    ref = O.HEMul(batch, r, c, dnum, 1, Q, P)
+    ref.setup_relinearization(evk_a, evk_b)
+    np.testing.assert_array_equal(_np(he.mul(ct)), ref.mul(ct))
+
+
+@pytest.mark.parametrize("n,L,K,dnum,batch,k", [(4096, 6, 2, 3, 2, 3), (1024, 4, 2, 2, 1, 100)])
+def test_herot_vs_oracle(n, L, K, dnum, batch, k):
+    from cross_b200 import herot, util
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    Q, P = ov[:L], ov[L:]
+    r, c = util.default_rc(n)
+    rng = np.random.default_rng(k)
+    ct = rng_residues(rng, (batch, 2, r, c, L), Q)
+    evk_a = rng_residues(rng, (dnum, n, L + K), ov)
+    evk_b = rng_residues(rng, (dnum, n, L + K), ov)
+    cm = util.precompute_auto_map(n, util.find_automorphism_index_2n_complex(k, 2 * n))
+    h = herot.HERot(r, c, dnum, Q, P)
+    h.control_gen(batch=batch, degree_layout=(r, c))
+    h.setup_rotate(evk_a, evk_b, cm)
+    ref = O.HERot(r, c, dnum, Q, P)
+    ref.control_gen(batch)
+    ref.setup_rotate(evk_a.reshape(dnum, r, c, -1), evk_b.reshape(dnum, r, c, -1), cm)
+    np.testing.assert_array_equal(_np(h.rotate(ct)), ref.rotate(ct))
+
+
+def test_hemul_full_size_vs_oracle():
+    """The benchmark parameter set (N = 2^16, L = 24, K = 8, dnum = 3) for one
+    ciphertext, bit-exact against the oracle."""
+    from cross_b200 import hemul
+    n, L, K, dnum = 65536, 24, 8, 3
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    Q, P = ov[:L], ov[L:]
+    rng = np.random.default_rng(2024)
+    ct = rng_residues(rng, (1, 4, 256, 256, L), Q)
+    evk_a = rng_residues(rng, (dnum, n, L + K), ov)
+    evk_b = rng_residues(rng, (dnum, n, L + K), ov)
+    he = hemul.HEMul(1, 256, 256, dnum, 1, Q, P)
+    he.control_gen(degree_layout=(256, 256))
+    he.setup_relinearization(evk_a, evk_b)
+    got = _np(he.mul(ct))
+    ref = O.HEMul(1, 256, 256, dnum, 1, Q, P)
+    ref.setup_relinearization(evk_a, evk_b)
+    np.testing.assert_array_equal(got, ref.mul(ct))
+
+
+def test_limb_major_layout_matches_reference_layout():
+    import torch
+    from cross_b200 import hemul, LAYOUT_LIMB_MAJOR
+    n, L, K, dnum, B = 1024, 5, 2, 3, 2
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    rng = np.random.default_rng(1)
+    ct = rng_residues(rng, (B, 4, 32, 32, L), ov[:L])
+    ek = [rng_residues(rng, (dnum, n, L + K), ov) for _ in range(2)]
+    he = hemul.HEMul(B, 32, 32, dnum, 1, ov[:L], ov[L:])
+    he.control_gen()
+    he.setup_relinearization(*ek)
+    ref_layout = _np(he.mul(ct))
+    lm_in = torch.from_numpy(np.ascontiguousarray(ct.reshape(B, 4, n, L).transpose(0, 1, 3, 2))).cuda()
+    lm = _np(he.mul(lm_in, layout=LAYOUT_LIMB_MAJOR))
+    np.testing.assert_array_equal(lm.transpose(0, 1, 3, 2).reshape(ref_layout.shape), ref_layout)
+
+
+def test_errors_are_reference_exceptions():
+    from cross_b200 import hemul, ntt_mm
+    q = O.find_moduli_ntt(2, 28, 2 * 16)
+    ctx = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 4, "c": 4})
+    with pytest.raises(ValueError):
+        ctx.ntt(np.zeros((1, 4, 4, 3), U32))
+    he = hemul.HEMul(1, 4, 4, 2, 1, q, O.find_moduli_ntt(3, 28, 32)[2:])
+    he.control_gen()
+    with pytest.raises(RuntimeError):
+        he.mul(np.zeros((1, 4, 4, 4, 2), U32))
