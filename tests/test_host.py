@@ -13,7 +13,7 @@ from tests.conftest import ROOT
 def _header_symbols():
     with open(os.path.join(ROOT, "include", "cross_b200.h")) as f:
         text = f.read()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(cross_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|uint64_t|const char\*)\s+(cross_\w+)\s*\(", text, re.M)))
 
 
 def test_library_exports_every_declared_symbol():
