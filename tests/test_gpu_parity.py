@@ -119,9 +119,9 @@ def test_elementwise_vs_oracle():
     z = rng.integers(0, 2 ** 64 - 1, size=(7, 5), dtype=np.uint64)
     ff = finite_field.BarrettContext(q)
     np.testing.assert_array_equal(_np(ff.modular_reduction(z)), O.Barrett(q).reduce(z))
-    a = rng_residues(rng, (3, 5, 64), q)
-    b = rng_residues(rng, (3, 5, 64), q)
-    a[0, 0, :4] = np.array(q[0]) - b[0, 0, :4]  # sums equal to q stay (add.py uses >)
+    a = rng_residues(rng, (3, 64, 5), q).transpose(0, 2, 1).copy()    # (E, L, N) as add.py
+    b = rng_residues(rng, (3, 64, 5), q).transpose(0, 2, 1).copy()
+    a[0, 0, :4] = np.uint32(q[0]) - b[0, 0, :4]  # sums equal to q stay (add.py uses >)
     np.testing.assert_array_equal(_np(add.jax_add(a, b, np.array(q))), O.jax_add(a, b, q))
     ct = Ciphertext({"batch": 2, "num_elements": 4, "degree": 64, "num_moduli": 5, "precision": 32,
                      "degree_layout": (8, 8)}, {"moduli": q})
