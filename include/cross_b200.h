@@ -139,6 +139,23 @@ size_t cross_ntt_workspace_size(cross_ntt_plan plan, int64_t batch, int layout);
 int cross_ntt(cross_ntt_plan plan, int inverse, const uint32_t* in, uint32_t* out, int64_t batch,
               int layout, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of cross_ntt; it has no counterpart in the
+ * reference.  For callers that cannot allocate device memory on their call
+ * path (a plugin inside a framework that has already reserved the GPU's
+ * memory, a loop that cannot afford cudaFree's synchronisation): it takes
+ * only in/out (limb-major layout, (batch, M, r, c) uint32, in may equal out)
+ * and keeps the NTT intermediate in a file-scope static device array of
+ * CROSS_NTT_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits.
+ * batch * M * r * c must not exceed CROSS_NTT_NOALLOC_SCRATCH_BYTES / 4
+ * words, else CROSS_ERR_WORKSPACE.  It calls no allocator.  The first call on
+ * each device looks up the array's device address (cudaGetSymbolAddress) and
+ * caches it; make that first call before any stream capture.  All calls share
+ * the array: calls that overlap on the GPU (other streams or threads) race,
+ * so issue them on one stream. */
+#define CROSS_NTT_NOALLOC_SCRATCH_BYTES (16u << 20)
+int cross_ntt_noalloc(cross_ntt_plan plan, int inverse, const uint32_t* in, uint32_t* out, int64_t batch,
+                      void* stream);
+
 /* ------------------------------------------------------------------ */
 /* BAT basis conversion                                                */
 /* ------------------------------------------------------------------ */
