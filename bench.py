@@ -162,6 +162,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling runs use a small case)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -179,15 +180,16 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     from cross_b200 import _lib, hemul, ntt_mm
+    batch = args.batch
     Q, P = moduli()
-    ct, ea, eb = inputs(100 + rank, BATCH)
-    he = hemul.HEMul(BATCH, R, C, DNUM, 1, Q, P)
+    ct, ea, eb = inputs(100 + rank, batch)
+    he = hemul.HEMul(batch, R, C, DNUM, 1, Q, P)
     he.control_gen(degree_layout=(R, C))
     he.setup_relinearization(ea, eb)
     dev = torch.device("cuda", local)
     x = torch.from_numpy(ct).to(dev)
-    out = torch.empty((BATCH, 2, R, C, L - 1), dtype=torch.uint32, device=dev)
-    ws = torch.empty(he.workspace_size(BATCH), dtype=torch.uint8, device=dev)
+    out = torch.empty((batch, 2, R, C, L - 1), dtype=torch.uint32, device=dev)
+    ws = torch.empty(he.workspace_size(batch), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
 
     def step():
@@ -214,7 +216,7 @@ def main():
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * BATCH * args.steps / (ms / 1000.0)
+    value = world * batch * args.steps / (ms / 1000.0)
 
     # e2e through the public API with pinned host buffers (H2D + compute + D2H).
     hin = torch.from_numpy(ct).pin_memory()
@@ -239,12 +241,12 @@ def main():
         t = torch.tensor([ems], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ems = float(t.item())
-    e2e = world * BATCH * args.steps / (ems / 1000.0)
+    e2e = world * batch * args.steps / (ems / 1000.0)
 
     # Dominant kernel: the BAT NTT (column + row contraction kernels) over the
     # 4 x 64 x 23 limb-polynomials of the rescale NTT, timed alone.
     ctx = ntt_mm.NTTCiphertextBarrettContext(Q[:L - 1], {"r": R, "c": C})
-    lps = BATCH * 4
+    lps = batch * 4
     xin = x.reshape(-1)[: lps * (L - 1) * N_DEG].reshape(lps, L - 1, R, C)   # residues < q
     xo = torch.empty_like(xin)
     nws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), lps, _lib.LAYOUT_LIMB_MAJOR), dtype=torch.uint8,
@@ -275,7 +277,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u32 residues, u64 intermediates, u8 BAT contractions",
         "data": "synthetic seeded uniform residues (no dataset in the reference)",
-        "config": {"workload": WORKLOAD, "global_batch": world * BATCH, "N": N_DEG, "r": R, "c": C, "L": L, "K": K,
+        "config": {"workload": WORKLOAD, "global_batch": world * batch, "batch_per_gpu": batch, "N": N_DEG, "r": R, "c": C, "L": L, "K": K,
                    "dnum": DNUM, "parallelism": f"batch-sharded x{world}",
                    "l2": "inputs 1.6 GB per GPU, larger than L2 (no flush needed)"},
         "e2e": {"value": e2e, "unit": "HE-Mult/s", "h2d_bytes_per_step": int(hin.numel() * 4),
