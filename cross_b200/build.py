@@ -11,7 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 SRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libcross_b200.so")
-SOURCES = ["errors.cu", "ntt.cu", "ntt_noalloc.cu", "elementwise.cu", "bconv.cu", "hemul.cu"]
+SOURCES = ["errors.cu", "ntt.cu", "ntt_tc.cu", "ntt_noalloc.cu", "elementwise.cu", "bconv.cu", "hemul.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared", "--expt-relaxed-constexpr"]
 

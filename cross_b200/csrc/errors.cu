@@ -35,6 +35,7 @@ int upload(T** dst, const T* src, size_t count) {
 }
 template int upload<uint32_t>(uint32_t**, const uint32_t*, size_t);
 template int upload<uint16_t>(uint16_t**, const uint16_t*, size_t);
+template int upload<uint8_t>(uint8_t**, const uint8_t*, size_t);
 template int upload<int16_t>(int16_t**, const int16_t*, size_t);
 template int upload<int32_t>(int32_t**, const int32_t*, size_t);
 template int upload<ModC>(ModC**, const ModC*, size_t);

@@ -285,7 +285,7 @@ void hemul_layout(const cross_hemul_plan_s* P, int64_t B, int layout, Arena& a, 
   int64_t tmpw = B * 4 * L1;
   for (int j = 0; j < P->parts; ++j) tmpw = std::max<int64_t>(tmpw, B * (L1 + K - P->dlen[j]));
   tmpw = std::max<int64_t>(tmpw, B * 2 * K);
-  b.tmp = a.take<uint32_t>((size_t)tmpw * N);
+  b.tmp = a.take<uint32_t>((size_t)std::max(ntt_tmp_words(P->ntt_qp, tmpw), ntt_tmp_words(P->ntt_p, tmpw)));
 }
 
 }  // namespace
@@ -567,7 +567,7 @@ void herot_layout(const cross_herot_plan_s* P, int64_t B, int layout, Arena& a, 
   int64_t tmpw = B * std::max(L, 2 * K);
   for (int j = 0; j < P->parts; ++j) tmpw = std::max<int64_t>(tmpw, B * (L + K - P->dlen[j]));
   tmpw = std::max<int64_t>(tmpw, B * 2 * L);
-  b.tmp = a.take<uint32_t>((size_t)tmpw * N);
+  b.tmp = a.take<uint32_t>((size_t)ntt_tmp_words(P->ntt, tmpw));
 }
 
 }  // namespace
@@ -791,7 +791,7 @@ void rescale_layout(const cross_rescale_plan_s* P, int64_t polys, int layout, Ar
   b.X = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)polys * P->L * N) : nullptr;
   b.R = layout == CROSS_LAYOUT_REFERENCE ? a.take<uint32_t>((size_t)polys * (P->L - 1) * N) : nullptr;
   b.LL = a.take<uint32_t>((size_t)polys * N);
-  b.tmp = a.take<uint32_t>((size_t)polys * (P->L - 1) * N + (size_t)polys * N);
+  b.tmp = a.take<uint32_t>((size_t)ntt_tmp_words(P->ntt, polys * (P->L - 1)));
 }
 }  // namespace
 

@@ -1,6 +1,8 @@
 // Internal plan structures and launchers shared by the translation units.
 #pragma once
 
+#include <cuda.h>
+
 #include <cstdint>
 #include <vector>
 
@@ -29,6 +31,16 @@ struct cross_ntt_plan_s {
   uint32_t* tw_fwd = nullptr;       // [M][r][c]            ntt_tf_step2
   uint32_t* tw_inv = nullptr;       // [M][r][c]            intt_tf_step2
   uint16_t* identity = nullptr;     // [M] 0..M-1
+  // tcgen05 operands (r and c multiples of 128): B matrices (4*nout x 4*kw bytes
+  // per limb, row 4n + p, column 4w + q) with their TMA descriptors.
+  bool tc = false;
+  uint8_t* tc_col_fwd = nullptr;    // [M][4r][4r]  from ntt_bat_tf_step1
+  uint8_t* tc_col_inv = nullptr;    // [M][4r][4r]  from intt_bat_tf_step3
+  uint8_t* tc_row_fwd = nullptr;    // [M][4c][4c]  from ntt_bat_tf_step3
+  uint8_t* tc_row_inv = nullptr;    // [M][4c][4c]  from intt_bat_tf_step1
+  uint32_t* tc_tw_inv = nullptr;    // [M][c][r]    intt_tf_step2 transposed
+  int* tc_err = nullptr;            // device error word of the tensor-core kernels
+  CUtensorMap tm_col_fwd, tm_col_inv, tm_row_fwd, tm_row_inv;
 };
 
 struct cross_bconv_plan_s {
@@ -77,8 +89,19 @@ template <class T>
 int upload_vec(T** dst, const std::vector<T>& v) { return upload(dst, v.data(), v.size()); }
 void dfree(void* p);
 
+// Scratch words ntt_run needs for lps limb-polynomials.
+int64_t ntt_tmp_words(const cross_ntt_plan_s* plan, int64_t lps);
+
+// tensor-core path (ntt_tc.cu)
+bool tc_supported(int r, int c);
+int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, const uint8_t* intt1,
+                 const uint8_t* intt3, const uint32_t* intt_tw);
+void tc_plan_free(cross_ntt_plan_s* P);
+int ntt_run_tc(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+               const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
+
 // NTT over polys x slots limb-polynomials (internal layout); limbs[slot] is the
-// plan limb of each slot (device array).  tmp holds polys*slots*N words.
+// plan limb of each slot (device array).  tmp holds ntt_tmp_words() words.
 int ntt_run(const cross_ntt_plan_s* plan, bool inverse, LP in, LPo out, int64_t polys, int slots,
             const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
 

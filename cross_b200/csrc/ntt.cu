@@ -10,6 +10,7 @@
 // and the INTT is the row transform (with the intt_tf_step2 twiddle) followed
 // by the column transform (ntt_mm.py:401-406).  Sums are exact integers, so any
 // exact evaluation order reproduces the reference bit for bit.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -179,8 +180,13 @@ unsigned grid_z(int64_t lps) { return (unsigned)(lps < 65535 ? lps : 65535); }
 
 }  // namespace
 
+int64_t ntt_tmp_words(const cross_ntt_plan_s* P, int64_t lps) {
+  return lps * P->r * P->c * (P->tc ? 2 : 1);
+}
+
 int ntt_run(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
             const uint16_t* limbs, uint32_t* tmp, cudaStream_t st) {
+  if (P->tc && polys * slots > 0) return ntt_run_tc(P, inverse, in, out, polys, slots, limbs, tmp, st);
   const int R = P->r, C = P->c;
   const int64_t N = (int64_t)R * C;
   const int64_t lps = polys * slots;
@@ -237,12 +243,30 @@ int cross_ntt_plan_create(cross_moduli moduli, int r, int c, const uint8_t* ntt_
   if (!rc) { pack_bat(intt_bat_tf_step1, c, c, M, buf); rc = upload_vec(&P->row_inv, buf); }
   if (!rc) { unpack_tw(ntt_tf_step2, r, c, M, buf); rc = upload_vec(&P->tw_fwd, buf); }
   if (!rc) { unpack_tw(intt_tf_step2, r, c, M, buf); rc = upload_vec(&P->tw_inv, buf); }
+  // CROSS_B200_DISABLE_TC=1 keeps the CUDA-core contraction for every size (a
+  // diagnostic for comparing the two exact implementations).
+  const char* no_tc = getenv("CROSS_B200_DISABLE_TC");
+  if (!rc && !(no_tc && no_tc[0] == '1'))
+    rc = tc_plan_init(P, ntt_bat_tf_step1, ntt_bat_tf_step3, intt_bat_tf_step1, intt_bat_tf_step3, intt_tf_step2);
   if (rc) {
     cross_ntt_plan_destroy(P);
     return rc;
   }
   *out = P;
   return CROSS_OK;
+}
+
+int cross_ntt_plan_check(cross_ntt_plan P) {
+  CROSS_REQUIRE(P, "cross_ntt_plan_check: null plan");
+  if (!P->tc_err) return CROSS_OK;
+  int code = 0;
+  CROSS_CHECK_CUDA(cudaDeviceSynchronize());
+  CROSS_CHECK_CUDA(cudaMemcpy(&code, P->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (!code) return CROSS_OK;
+  const int zero = 0;
+  CROSS_CHECK_CUDA(cudaMemcpy(P->tc_err, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  set_error("tensor-core NTT kernel: a bounded wait expired (role code %d)", code);
+  return CROSS_ERR_TIMEOUT;
 }
 
 int cross_ntt_plan_destroy(cross_ntt_plan P) {
@@ -255,6 +279,7 @@ int cross_ntt_plan_destroy(cross_ntt_plan P) {
   dfree(P->row_inv);
   dfree(P->tw_fwd);
   dfree(P->tw_inv);
+  tc_plan_free(P);
   delete P;
   return CROSS_OK;
 }
@@ -263,7 +288,7 @@ size_t cross_ntt_workspace_size(cross_ntt_plan P, int64_t batch, int layout) {
   if (!P || batch < 0) return 0;
   const size_t words = (size_t)batch * P->M * P->r * P->c;
   Arena a(nullptr, 0);
-  a.take<uint32_t>(words);
+  a.take<uint32_t>((size_t)ntt_tmp_words(P, batch * P->M));
   if (layout == CROSS_LAYOUT_REFERENCE) a.take<uint32_t>(words);
   return a.off;
 }
@@ -284,7 +309,7 @@ int cross_ntt(cross_ntt_plan P, int inverse, const uint32_t* in, uint32_t* out, 
   const int M = P->M;
   const size_t words = (size_t)batch * M * N;
   Arena a(workspace, workspace_bytes);
-  uint32_t* tmp = a.take<uint32_t>(words);
+  uint32_t* tmp = a.take<uint32_t>((size_t)ntt_tmp_words(P, batch * M));
   if (layout == CROSS_LAYOUT_LIMB_MAJOR) {
     return ntt_run(P, inverse != 0, LP{in, M * N, N}, LPo{out, M * N, N}, batch, M, P->identity, tmp, st);
   }

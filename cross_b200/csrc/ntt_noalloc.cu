@@ -57,11 +57,11 @@ extern "C" int cross_ntt_noalloc(cross_ntt_plan P, int inverse, const uint32_t* 
   if (batch == 0) return CROSS_OK;
   const int64_t N = (int64_t)P->r * P->c;
   const int M = P->M;
-  const int64_t words = batch * M * N;
+  const int64_t words = cross::ntt_tmp_words(P, batch * M);
   if (words > (int64_t)kScratchWords) {
     cross::set_error(
-        "cross_ntt_noalloc: batch %lld x %d limbs x N %lld = %lld words exceeds the %zu-word (%u MiB) static scratch; "
-        "use cross_ntt with a workspace",
+        "cross_ntt_noalloc: batch %lld x %d limbs x N %lld needs %lld scratch words, which exceeds the %zu-word "
+        "(%u MiB) static scratch; use cross_ntt with a workspace",
         (long long)batch, M, (long long)N, (long long)words, kScratchWords, CROSS_NTT_NOALLOC_SCRATCH_BYTES >> 20);
     return CROSS_ERR_WORKSPACE;
   }

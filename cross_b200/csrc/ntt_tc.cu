@@ -1,0 +1,533 @@
+// tcgen05 tensor-core BAT contraction (sm_100a) for the NTT / INTT steps.
+//
+// One launch computes, for a batch of limb-polynomials that share a plan,
+//     S[m, n] = sum_{w, q} byte_q(A[m, w]) * T_n[w, q]          (exact int)
+//     out     = epilogue(Barrett(sum_p S_p << 8p))
+// where A is an (rows_m x kw) uint32 matrix per limb-polynomial read as
+// (rows_m x 4kw) uint8, and B is the reference's BAT twiddle array
+// re-laid out as (4*nout x 4*kw) uint8 with row j = 4n + p, column 4w + q.
+// This is matmul_bat_einsum + BarrettContext.modular_reduction of
+// ntt_mm.py:20-37,201-230 for one 3-step NTT stage.
+//
+// Kernel structure (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile 128 x 128 B, B tile 256 x 128 B per stage,
+//               SWIZZLE_128B, 4-stage ring (plain loads, no multicast).
+//   warp 1      TMEM allocation (512 columns) and the single MMA-issuing thread:
+//               tcgen05.mma.cta_group::1.kind::i8, M=128 N=256 K=32, u8 x u8 -> s32,
+//               accumulating into one of two 256-column TMEM buffers.
+//   warps 2..5  epilogue: tcgen05.ld rows, byte recombination, Barrett, optional
+//               twiddle multiply + Barrett, stores; runs while the MMA fills the
+//               other accumulator.
+// Every mbarrier wait is bounded (about two seconds of wall time); on expiry the
+// kernel records an error code, stops issuing work, lets its copies and MMAs
+// drain (again bounded), frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <vector>
+
+#include "internal.hpp"
+
+namespace cross {
+namespace tc {
+
+constexpr int BM = 128;            // rows per tile (TMEM lanes)
+constexpr int BN = 256;            // MMA N per tile: 64 outputs x 4 byte-planes
+constexpr int BKB = 128;           // K bytes per pipeline stage (4 MMAs of K = 32)
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BKB;  // 16 KiB
+constexpr int B_STAGE = BN * BKB;  // 32 KiB
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint64_t WAIT_NS = 2000000000ull;   // bound on any single wait
+
+struct Smem {
+  uint8_t a[STAGES][A_STAGE];
+  uint8_t b[STAGES][B_STAGE];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+
+struct Args {
+  uint32_t* out;
+  int64_t out_ps, out_ss;          // words
+  const uint16_t* limbs;           // slot -> plan limb
+  int slots;
+  int64_t polys;
+  int rows_m, kw, nout;
+  const uint32_t* tw;              // [M][nout][rows_m] or null
+  const ModC* mods;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase of `parity` to complete.  Returns false (and
+// raises the CTA abort flag, recording `code`) when the bound expires or
+// another role of the CTA has already aborted.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Smem& S, int* err, int code) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if (S.abort) return false;
+    if (i >= 32) __nanosleep(i < 1024 ? 20 : 200);
+    if ((i & 255) == 255 && globaltimer() - t0 > WAIT_NS) {
+      atomicCAS(err, 0, code);
+      S.abort = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::
+          "r"(saddr(dst)),
+      "l"((uint64_t)tm), "r"(saddr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          saddr(dst)),
+      "l"((uint64_t)tm), "r"(saddr(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, SWIZZLE_128B shared-memory matrix descriptor: 8-row atoms of
+// 1024 B (stride-byte-offset 1024), leading-byte-offset 16 (unused when
+// swizzled), descriptor version 1, layout type 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::i8: D = S32 (bits 4-5 = 2), A = B = unsigned
+// 8-bit (0), both K-major, N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+constexpr uint32_t IDESC = (2u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate), "r"(z));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct Unit {
+  int nt, mt, slot;
+  int64_t poly;
+};
+__device__ __forceinline__ Unit decode(int64_t u, int n_tiles, int m_tiles, int64_t polys) {
+  Unit r;
+  r.nt = (int)(u % n_tiles);
+  u /= n_tiles;
+  r.mt = (int)(u % m_tiles);
+  u /= m_tiles;
+  r.poly = u % polys;
+  r.slot = (int)(u / polys);
+  return r;
+}
+
+template <bool TWIDDLE, bool NMAJOR>
+__global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ CUtensorMap tmA,
+                                                       const __grid_constant__ CUtensorMap tmB, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = a.rows_m / BM, n_tiles = a.nout / 64, kst = a.kw / 32;
+  const int64_t units = (int64_t)a.slots * a.polys * m_tiles * n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.tfull[i], 1);
+      mbar_init(&S.tempty[i], 128);
+    }
+    mbar_init(&S.drain, 1);
+    S.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&S.tmem_base)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      uint32_t stage = 0, phase = 0;
+      int issued = 0;
+      for (int64_t u = blockIdx.x; u < units && !S.abort; u += gridDim.x) {
+        const Unit w = decode(u, n_tiles, m_tiles, a.polys);
+        const int limb = a.limbs[w.slot];
+        for (int ks = 0; ks < kst; ++ks) {
+          if (!mbar_wait(&S.empty[stage], phase ^ 1, S, a.err, 1)) break;
+          mbar_expect_tx(&S.full[stage], A_STAGE + B_STAGE);
+          tma_load_4d(S.a[stage], &tmA, &S.full[stage], ks * 32, w.mt * BM, w.slot, (int)w.poly);
+          tma_load_2d(S.b[stage], &tmB, &S.full[stage], ks * BKB, limb * 4 * a.nout + w.nt * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (S.abort) {
+        // let the copies already issued land before the CTA exits
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          stage = stage == 0 ? STAGES - 1 : stage - 1;
+          if (stage == STAGES - 1) phase ^= 1;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_test(&S.full[stage], phase) && globaltimer() - t0 < WAIT_NS) __nanosleep(200);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      uint32_t stage = 0, phase = 0, acc = 0, aphase = 0;
+      for (int64_t u = blockIdx.x; u < units && !S.abort; u += gridDim.x) {
+        if (!mbar_wait(&S.tempty[acc], aphase ^ 1, S, a.err, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        bool ok = true;
+        for (int ks = 0; ks < kst; ++ks) {
+          if (!mbar_wait(&S.full[stage], phase, S, a.err, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t as = saddr(S.a[stage]), bs = saddr(S.b[stage]);
+#pragma unroll
+          for (int k = 0; k < BKB / 32; ++k)
+            mma_i8(d, sw128_desc(as + 32 * k), sw128_desc(bs + 32 * k), (ks | k) != 0);
+          mma_commit(&S.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&S.tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1;
+      }
+      // every MMA issued by this thread has completed once `drain` flips
+      mma_commit(&S.drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_test(&S.drain, 0) && globaltimer() - t0 < WAIT_NS) __nanosleep(100);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 -> TMEM lane quadrants 2, 3, 0, 1) ----------------
+    const int quad = warp & 3;
+    uint32_t acc = 0, aphase = 0;
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+      const Unit w = decode(u, n_tiles, m_tiles, a.polys);
+      const int limb = a.limbs[w.slot];
+      bool ok = mbar_wait(&S.tfull[acc], aphase, S, a.err, 4);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int m = w.mt * BM + quad * 32 + lane;
+      uint32_t* o = a.out + w.poly * a.out_ps + (int64_t)w.slot * a.out_ss;
+      const ModC mc = a.mods[limb];
+      const uint32_t* twp = TWIDDLE ? a.tw + (size_t)limb * a.nout * a.rows_m : nullptr;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + chunk * 32, v);
+        uint32_t res[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int n = w.nt * 64 + chunk * 8 + j;
+          uint32_t r = barrett_any(combine4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]), mc);
+          if (TWIDDLE) r = barrett_any((uint64_t)r * twp[(size_t)n * a.rows_m + m], mc);
+          if (NMAJOR)
+            o[(size_t)n * a.rows_m + m] = r;
+          else
+            res[j] = r;
+        }
+        if (!NMAJOR) {
+          uint4* dst = reinterpret_cast<uint4*>(o + (size_t)m * a.nout + w.nt * 64 + chunk * 8);
+          dst[0] = make_uint4(res[0], res[1], res[2], res[3]);
+          dst[1] = make_uint4(res[4], res[5], res[6], res[7]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&S.tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) aphase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+// Strided batched transpose of limb-polynomials: out[lp][c][r] = in[lp][r][c].
+__global__ void k_transpose_lp(LP in, uint32_t* __restrict__ out, int64_t lps, int slots, int R, int C) {
+  __shared__ uint32_t tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int64_t N = (int64_t)R * C;
+  for (int64_t lp = blockIdx.z; lp < lps; lp += gridDim.z) {
+    const uint32_t* src = in.p + (lp / slots) * in.ps + (lp % slots) * in.ss;
+    uint32_t* dst = out + lp * N;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) tile[i][threadIdx.x] = src[(int64_t)(r0 + i) * C + c0 + threadIdx.x];
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) dst[(int64_t)(c0 + i) * R + r0 + threadIdx.x] = tile[threadIdx.x][i];
+    __syncthreads();
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+int g_num_sms = 0;
+
+int init_driver() {
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CROSS_CHECK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn) {
+      set_error("cuTensorMapEncodeTiled is not available from the driver");
+      return CROSS_ERR_UNSUPPORTED;
+    }
+    g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  if (!g_num_sms) {
+    int dev = 0;
+    CROSS_CHECK_CUDA(cudaGetDevice(&dev));
+    CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return CROSS_OK;
+}
+
+int encode(CUtensorMap* tm, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+           const cuuint64_t* strides, const cuuint32_t* box) {
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(tm, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return CROSS_ERR_CUDA;
+  }
+  return CROSS_OK;
+}
+
+// Tensor map of A: (kw words, rows, slots, polys) with word strides.
+int make_tmap_a(CUtensorMap* tm, const uint32_t* base, int kw, int rows, int slots, int64_t polys, int64_t ss,
+                int64_t ps) {
+  const int64_t mat = (int64_t)kw * rows;
+  if (slots == 1 || ss == 0) ss = mat;
+  if (polys == 1 || ps == 0) ps = ss * slots;
+  if (((uintptr_t)base & 15) || (ss * 4) % 16 || (ps * 4) % 16) {
+    set_error("tcgen05 NTT: limb-polynomial base and strides must be 16-byte aligned");
+    return CROSS_ERR_UNSUPPORTED;
+  }
+  cuuint64_t dims[4] = {(cuuint64_t)kw, (cuuint64_t)rows, (cuuint64_t)slots, (cuuint64_t)polys};
+  cuuint64_t strides[3] = {(cuuint64_t)kw * 4, (cuuint64_t)ss * 4, (cuuint64_t)ps * 4};
+  cuuint32_t box[4] = {32, (cuuint32_t)BM, 1, 1};
+  return encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, base, dims, strides, box);
+}
+
+// Tensor map of a plan's B matrices: (4*kw bytes, M*4*nout rows).
+int make_tmap_b(CUtensorMap* tm, const uint8_t* base, int kw, int nout, int M) {
+  cuuint64_t dims[2] = {(cuuint64_t)4 * kw, (cuuint64_t)M * 4 * nout};
+  cuuint64_t strides[1] = {(cuuint64_t)4 * kw};
+  cuuint32_t box[2] = {(cuuint32_t)BKB, (cuuint32_t)BN};
+  return encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box);
+}
+
+template <bool TW, bool NM>
+int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<TW, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)SMEM_BYTES));
+    attr = true;
+  }
+  const int64_t units = (int64_t)a.slots * a.polys * (a.rows_m / BM) * (a.nout / 64);
+  const unsigned grid = (unsigned)(units < g_num_sms ? units : g_num_sms);
+  k_bat_tc<TW, NM><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+// One contraction stage over polys x slots limb-polynomials.
+int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, bool twiddle, bool nmajor, const uint32_t* tw,
+          const uint32_t* A, int64_t a_ps, int64_t a_ss, int rows_m, int kw, int nout, LPo out, int64_t polys, int slots,
+          const uint16_t* limbs, cudaStream_t st) {
+  CUtensorMap tmA;
+  int rc = make_tmap_a(&tmA, A, kw, rows_m, slots, polys, a_ss, a_ps);
+  if (rc) return rc;
+  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, tw, P->mods, P->tc_err};
+  if (twiddle) return nmajor ? launch<true, true>(tmA, tmB, a, st) : launch<true, false>(tmA, tmB, a, st);
+  return nmajor ? launch<false, true>(tmA, tmB, a, st) : launch<false, false>(tmA, tmB, a, st);
+}
+
+}  // namespace tc
+
+bool tc_supported(int r, int c) {
+  auto ok = [](int x) { return x % 128 == 0 && x >= 128 && x <= 1024; };
+  return ok(r) && ok(c);
+}
+
+// B matrices of the tensor-core path from the reference BAT arrays:
+//   bat (X, 4 q, Y, 4 p, M); `x_is_out` when the first axis indexes the output n
+//   (ntt step 1 / intt step 3: n = z or l, w = r), else the second spatial axis does
+//   (ntt step 3 / intt step 1: w = c, n = n or l).
+void pack_tc(const uint8_t* bat, int X, int Y, int M, bool x_is_out, std::vector<uint8_t>& dst) {
+  const int nout = x_is_out ? X : Y, kw = x_is_out ? Y : X;
+  dst.assign((size_t)M * 4 * nout * 4 * kw, 0);
+  for (int x = 0; x < X; ++x)
+    for (int q = 0; q < 4; ++q)
+      for (int y = 0; y < Y; ++y)
+        for (int p = 0; p < 4; ++p) {
+          const int n = x_is_out ? x : y, w = x_is_out ? y : x;
+          const size_t src = (((size_t)x * 4 + q) * Y + y) * 4 + p;
+          for (int m = 0; m < M; ++m)
+            dst[((size_t)m * 4 * nout + (size_t)n * 4 + p) * 4 * kw + (size_t)w * 4 + q] = bat[src * M + m];
+        }
+}
+
+int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, const uint8_t* intt1,
+                 const uint8_t* intt3, const uint32_t* intt_tw) {
+  if (!tc_supported(P->r, P->c)) return CROSS_OK;
+  int rc = tc::init_driver();
+  if (rc) return rc;
+  const int R = P->r, C = P->c, M = P->M;
+  std::vector<uint8_t> buf;
+  pack_tc(ntt1, R, R, M, true, buf);
+  if ((rc = upload_vec(&P->tc_col_fwd, buf))) return rc;
+  pack_tc(intt3, R, R, M, true, buf);
+  if ((rc = upload_vec(&P->tc_col_inv, buf))) return rc;
+  pack_tc(ntt3, C, C, M, false, buf);
+  if ((rc = upload_vec(&P->tc_row_fwd, buf))) return rc;
+  pack_tc(intt1, C, C, M, false, buf);
+  if ((rc = upload_vec(&P->tc_row_inv, buf))) return rc;
+  // intt twiddle as [limb][l][r] (output index major) for the row-stage epilogue
+  std::vector<uint32_t> tw((size_t)M * R * C);
+  for (int r = 0; r < R; ++r)
+    for (int l = 0; l < C; ++l)
+      for (int m = 0; m < M; ++m) tw[((size_t)m * C + l) * R + r] = intt_tw[((size_t)r * C + l) * M + m];
+  if ((rc = upload_vec(&P->tc_tw_inv, tw))) return rc;
+  std::vector<int> zero(1, 0);
+  if ((rc = upload(&P->tc_err, zero.data(), 1))) return rc;
+  if ((rc = tc::make_tmap_b(&P->tm_col_fwd, P->tc_col_fwd, R, R, M))) return rc;
+  if ((rc = tc::make_tmap_b(&P->tm_col_inv, P->tc_col_inv, R, R, M))) return rc;
+  if ((rc = tc::make_tmap_b(&P->tm_row_fwd, P->tc_row_fwd, C, C, M))) return rc;
+  if ((rc = tc::make_tmap_b(&P->tm_row_inv, P->tc_row_inv, C, C, M))) return rc;
+  P->tc = true;
+  return CROSS_OK;
+}
+
+void tc_plan_free(cross_ntt_plan_s* P) {
+  dfree(P->tc_col_fwd);
+  dfree(P->tc_col_inv);
+  dfree(P->tc_row_fwd);
+  dfree(P->tc_row_inv);
+  dfree(P->tc_tw_inv);
+  dfree(P->tc_err);
+}
+
+// NTT / INTT on the tensor cores.  tmp holds 2 * polys * slots * N words.
+//   ntt:  transpose -> column stage (x T2, output index major) -> row stage (row major)
+//   intt: row stage (x iT2, output index major) -> column stage (output index major)
+int ntt_run_tc(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+               const uint16_t* limbs, uint32_t* tmp, cudaStream_t st) {
+  const int R = P->r, C = P->c;
+  const int64_t N = (int64_t)R * C, lps = polys * slots;
+  uint32_t* t1 = tmp;
+  uint32_t* t2 = tmp + lps * N;
+  int rc;
+  if (!inverse) {
+    dim3 blk(32, 8), grd(C / 32, R / 32, (unsigned)(lps < 65535 ? lps : 65535));
+    tc::k_transpose_lp<<<grd, blk, 0, st>>>(in, t1, lps, slots, R, C);
+    count_launch();
+    CROSS_CHECK_CUDA(cudaGetLastError());
+    // column stage: A = X^T (C rows x R words), out Y[z][c] = out[n][m]
+    if ((rc = tc::stage(P, P->tm_col_fwd, true, true, P->tw_fwd, t1, slots * N, N, C, R, R,
+                        LPo{t2, slots * N, N}, polys, slots, limbs, st)))
+      return rc;
+    // row stage: A = Y (R rows x C words), out Z[z][n] = out[m][n]
+    return tc::stage(P, P->tm_row_fwd, false, false, nullptr, t2, slots * N, N, R, C, C, out, polys, slots, limbs, st);
+  }
+  // row stage: A = X (R rows x C words), out Y^T[l][r] = out[n][m]
+  if ((rc = tc::stage(P, P->tm_row_inv, true, true, P->tc_tw_inv, in.p, in.ps, in.ss, R, C, C, LPo{t1, slots * N, N},
+                      polys, slots, limbs, st)))
+    return rc;
+  // column stage: A = Y^T (C rows x R words), out Z[l'][c'] = out[n][m]
+  return tc::stage(P, P->tm_col_inv, false, true, nullptr, t1, slots * N, N, C, R, R, out, polys, slots, limbs, st);
+}
+
+}  // namespace cross

@@ -129,6 +129,11 @@ class NTTCiphertextContextBase:
             _lib._lib.cross_ntt_plan_destroy(self._plan)
             self._plan = None
 
+    def check_device(self):
+        """Raise TimeoutError if a tensor-core kernel of this plan hit a bounded wait."""
+        if self._plan is not None:
+            _lib.check(_lib.lib().cross_ntt_plan_check(self._plan), "cross_ntt_plan_check")
+
     # -- online ---------------------------------------------------------------
     def _run(self, v, inverse: bool):
         x = _tensor.to_u32(v)

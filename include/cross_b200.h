@@ -139,6 +139,12 @@ size_t cross_ntt_workspace_size(cross_ntt_plan plan, int64_t batch, int layout);
 int cross_ntt(cross_ntt_plan plan, int inverse, const uint32_t* in, uint32_t* out, int64_t batch,
               int layout, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Reports (and clears) the error word of the plan's tensor-core kernels:
+ * CROSS_OK, or CROSS_ERR_TIMEOUT when a bounded wait inside a kernel expired
+ * (the kernel then stopped early and its output is invalid).  Synchronises
+ * the device. */
+int cross_ntt_plan_check(cross_ntt_plan plan);
+
 /* Allocation-free variant of cross_ntt; it has no counterpart in the
  * reference.  For callers that cannot allocate device memory on their call
  * path (a plugin inside a framework that has already reserved the GPU's

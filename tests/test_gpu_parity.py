@@ -47,6 +47,23 @@ def test_ntt_intt_vs_oracle(n, r, c, limbs, batch):
     np.testing.assert_array_equal(_np(ctx.intt(y)), ref.intt(yr))
 
 
+def test_tensor_core_path_matches_cuda_core_path(monkeypatch):
+    """The tcgen05 contraction (r, c multiples of 128) and the dp4a contraction
+    are both exact: their NTT / INTT outputs must be identical."""
+    from cross_b200 import ntt_mm
+    n, L, B = 65536, 8, 6
+    q = O.find_moduli_ntt(L, 28, 2 * n)
+    x = rng_residues(np.random.default_rng(42), (B, 256, 256, L), q)
+    tc = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 256, "c": 256})
+    y_tc = _np(tc.ntt(x))
+    z_tc = _np(tc.intt(y_tc))
+    tc.check_device()
+    monkeypatch.setenv("CROSS_B200_DISABLE_TC", "1")
+    cc = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 256, "c": 256})
+    np.testing.assert_array_equal(y_tc, _np(cc.ntt(x)))
+    np.testing.assert_array_equal(z_tc, _np(cc.intt(y_tc)))
+
+
 def test_ntt_round_trip_and_linearity_full_size():
     """Size-independent properties at N = 2^16, 24 limbs: INTT(NTT(x)) == x mod q
     and NTT(x + y) == NTT(x) + NTT(y) mod q."""
