@@ -48,7 +48,8 @@ def inputs(seed_ct: int, batch: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons, sampled every 50 ms; summary() keeps
+    the samples received inside a host-time window (the timed region)."""
     Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -59,17 +60,20 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 3.0:    # wait for the first sample
+                time.sleep(0.02)
         except OSError:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            self.rows.append((time.time(), [x.strip() for x in line.split(",")]))
 
     def __exit__(self, *a):
         if self.proc:
@@ -79,20 +83,22 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
+    def summary(self, t0=None, t1=None):
+        sm, mx, pw, reasons = [], None, [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
+        rows = [r for t, r in self.rows if (t0 is None or t >= t0) and (t1 is None or t <= t1 + 0.06)]
+        for r in rows:
             try:
                 sm.append(float(r[0]))
                 mx = float(r[1])
+                pw.append(float(r[2]))
                 for n, v in zip(names, r[3:7]):
                     if "Active" in v and "Not" not in v:
                         reasons.add(n)
             except (ValueError, IndexError):
                 pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "power_w_max": max(pw) if pw else None, "reasons": sorted(reasons), "samples": len(sm)}
 
 
 def peaks():
@@ -158,7 +164,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -201,16 +207,18 @@ def main():
     if dist:
         dist.barrier()
     lib = _lib.lib()
-    l0 = lib.cross_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
+        l0 = lib.cross_launch_count()
+        h0 = time.time()
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
-    launches = lib.cross_launch_count() - l0
+        h1 = time.time()
+        launches = lib.cross_launch_count() - l0
     ms = e0.elapsed_time(e1)
     if dist:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -283,7 +291,7 @@ def main():
         "e2e": {"value": e2e, "unit": "HE-Mult/s", "h2d_bytes_per_step": int(hin.numel() * 4),
                 "d2h_bytes_per_step": int(hout.numel() * 4)},
         "gpu_launches": int(launches),
-        "clocks": clk.summary(),
+        "clocks": clk.summary(h0, h1),
         "roofline": {"kernel": "BAT NTT forward (column + row contraction kernels), 23 limbs x 256 polys",
                      "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
                      "frac": achieved / int8_peak, "traffic": None,

@@ -40,6 +40,7 @@ struct cross_ntt_plan_s {
   uint8_t* tc_row_inv = nullptr;    // [M][4c][4c]  from intt_bat_tf_step1
   uint32_t* tc_tw_inv = nullptr;    // [M][c][r]    intt_tf_step2 transposed
   int* tc_err = nullptr;            // device error word of the tensor-core kernels
+  int tc_fast = 0;                  // 32-bit remainder Barrett is exact for every limb
   CUtensorMap tm_col_fwd, tm_col_inv, tm_row_fwd, tm_row_inv;
 };
 

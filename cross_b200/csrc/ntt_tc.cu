@@ -15,9 +15,11 @@
 //   warp 1      TMEM allocation (512 columns) and the single MMA-issuing thread:
 //               tcgen05.mma.cta_group::1.kind::i8, M=128 N=256 K=32, u8 x u8 -> s32,
 //               accumulating into one of two 256-column TMEM buffers.
-//   warps 2..5  epilogue: tcgen05.ld rows, byte recombination, Barrett, optional
-//               twiddle multiply + Barrett, stores; runs while the MMA fills the
-//               other accumulator.
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant (each takes half of
+//               the 256 accumulator columns): tcgen05.ld rows, byte
+//               recombination, Barrett, optional twiddle multiply (twiddles
+//               prefetched before the accumulator is ready) + Barrett, stores;
+//               runs while the MMA fills the other accumulator.
 // Every mbarrier wait is bounded (about two seconds of wall time); on expiry the
 // kernel records an error code, stops issuing work, lets its copies and MMAs
 // drain (again bounded), frees TMEM and returns.
@@ -37,7 +39,8 @@ constexpr int BKB = 128;           // K bytes per pipeline stage (4 MMAs of K = 
 constexpr int STAGES = 4;
 constexpr int A_STAGE = BM * BKB;  // 16 KiB
 constexpr int B_STAGE = BN * BKB;  // 32 KiB
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint64_t WAIT_NS = 2000000000ull;   // bound on any single wait
 
@@ -64,6 +67,7 @@ struct Args {
   const uint32_t* tw;              // [M][nout][rows_m] or null
   const ModC* mods;
   int* err;
+  int fast;                        // every limb qualifies for reduce_fast (see below)
 };
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -144,6 +148,20 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 // 8-bit (0), both K-major, N >> 3 in bits 17-22, M >> 4 in bits 24-28.
 constexpr uint32_t IDESC = (2u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 
+// Barrett of finite_field.py:224-230 for w = 32 with the remainder taken in
+// 32-bit arithmetic.  The reference forms r = z - t*q in uint64 and then keeps
+// r >= q ? r - q : r truncated to uint32; t = floor(floor(z*m / 2^32) / 2^s_w)
+// is computed exactly here, and whenever the true r lies in (-(2^32 - q), 2^32)
+// the 32-bit remainder and comparison give the same uint32.  The plan enables
+// this path only when z_max / 2^s + 2 < (2^32 - q) / q for every limb and both
+// epilogue inputs (z < 2^53 sums and z < 2^31 * q twiddle products).
+__device__ __forceinline__ uint32_t reduce_fast(uint64_t z, uint32_t q, uint32_t m, uint32_t s_w) {
+  const uint32_t zlo = (uint32_t)z, zhi = (uint32_t)(z >> 32);
+  const uint64_t t = ((uint64_t)__umulhi(zlo, m) + (uint64_t)zhi * m) >> s_w;
+  const uint32_t r = zlo - (uint32_t)t * q;
+  return r >= q ? r - q : r;
+}
+
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   const uint32_t z = 0;
   asm volatile(
@@ -200,7 +218,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.tfull[i], 1);
-      mbar_init(&S.tempty[i], 128);
+      mbar_init(&S.tempty[i], 32 * EPI_WARPS);
     }
     mbar_init(&S.drain, 1);
     S.abort = 0;
@@ -285,37 +303,47 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
       while (!mbar_test(&S.drain, 0) && globaltimer() - t0 < WAIT_NS) __nanosleep(100);
     }
   } else {
-    // ---------------- epilogue (warps 2..5 -> TMEM lane quadrants 2, 3, 0, 1) ----------------
-    const int quad = warp & 3;
+    // ---------------- epilogue (warps 2..9: TMEM lane quadrant warp % 4, column half) ----------------
+    const int quad = warp & 3, half = (warp - 2) >> 2;
     uint32_t acc = 0, aphase = 0;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit w = decode(u, n_tiles, m_tiles, a.polys);
       const int limb = a.limbs[w.slot];
+      const int m = w.mt * BM + quad * 32 + lane;
+      const int n0 = w.nt * 64 + half * 32;
+      uint32_t twv[TWIDDLE ? 32 : 1];
+      if (TWIDDLE) {
+        const uint32_t* twp = a.tw + ((size_t)limb * a.nout + n0) * a.rows_m + m;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) twv[j] = __ldg(twp + (size_t)j * a.rows_m);
+      }
+      const ModC mc = a.mods[limb];
       bool ok = mbar_wait(&S.tfull[acc], aphase, S, a.err, 4);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int m = w.mt * BM + quad * 32 + lane;
       uint32_t* o = a.out + w.poly * a.out_ps + (int64_t)w.slot * a.out_ss;
-      const ModC mc = a.mods[limb];
-      const uint32_t* twp = TWIDDLE ? a.tw + (size_t)limb * a.nout * a.rows_m : nullptr;
-#pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+      const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
+#pragma unroll
+      for (int chunk = 0; chunk < 4; ++chunk) {
         uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + chunk * 32, v);
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + half * 128 + chunk * 32, v);
         uint32_t res[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const int n = w.nt * 64 + chunk * 8 + j;
-          uint32_t r = barrett_any(combine4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]), mc);
-          if (TWIDDLE) r = barrett_any((uint64_t)r * twp[(size_t)n * a.rows_m + m], mc);
-          if (NMAJOR)
-            o[(size_t)n * a.rows_m + m] = r;
-          else
-            res[j] = r;
+          const uint64_t z = combine4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          uint32_t r = a.fast ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
+          if (TWIDDLE) {
+            const uint64_t zt = (uint64_t)r * twv[chunk * 8 + j];
+            r = a.fast ? reduce_fast(zt, q32, m32, sw) : barrett(zt, mc);
+          }
+          res[j] = r;
         }
-        if (!NMAJOR) {
-          uint4* dst = reinterpret_cast<uint4*>(o + (size_t)m * a.nout + w.nt * 64 + chunk * 8);
+        if (NMAJOR) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[(size_t)(n0 + chunk * 8 + j) * a.rows_m + m] = res[j];
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(o + (size_t)m * a.nout + n0 + chunk * 8);
           dst[0] = make_uint4(res[0], res[1], res[2], res[3]);
           dst[1] = make_uint4(res[4], res[5], res[6], res[7]);
         }
@@ -430,7 +458,7 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, bool twiddle, bool 
   CUtensorMap tmA;
   int rc = make_tmap_a(&tmA, A, kw, rows_m, slots, polys, a_ss, a_ps);
   if (rc) return rc;
-  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, tw, P->mods, P->tc_err};
+  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, tw, P->mods, P->tc_err, P->tc_fast};
   if (twiddle) return nmajor ? launch<true, true>(tmA, tmB, a, st) : launch<true, false>(tmA, tmB, a, st);
   return nmajor ? launch<false, true>(tmA, tmB, a, st) : launch<false, false>(tmA, tmB, a, st);
 }
@@ -487,6 +515,20 @@ int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, 
   if ((rc = tc::make_tmap_b(&P->tm_col_inv, P->tc_col_inv, R, R, M))) return rc;
   if ((rc = tc::make_tmap_b(&P->tm_row_fwd, P->tc_row_fwd, C, C, M))) return rc;
   if ((rc = tc::make_tmap_b(&P->tm_row_inv, P->tc_row_inv, C, C, M))) return rc;
+  // reduce_fast is exact when the true remainder stays in (-(2^32 - q), 2^32):
+  // with t = floor(z m / 2^s) and m within one of 2^s / q, |r| < (z / 2^s + 2) q.
+  // Epilogue inputs: contraction sums z < 2^53 (kw <= 1024), twiddle products
+  // z < 2^31 q.
+  bool fast = true;
+  for (const ModC& mc : P->mods_host) {
+    const unsigned __int128 q = mc.q;
+    const unsigned s_bits = mc.w + mc.s_w;
+    const unsigned __int128 z1 = (unsigned __int128)1 << 53, z2 = ((unsigned __int128)1 << 31) * q;
+    const unsigned __int128 lim = ((unsigned __int128)1 << 32) - q;
+    for (unsigned __int128 z : {z1, z2})
+      if (mc.w != 32 || mc.m >= (1ull << 32) || ((z >> s_bits) + 3) * q >= lim) fast = false;
+  }
+  P->tc_fast = fast ? 1 : 0;
   P->tc = true;
   return CROSS_OK;
 }
