@@ -23,7 +23,9 @@ __global__ void __launch_bounds__(BC_THREADS) k_bconv(const uint32_t* __restrict
                                                       int64_t polys, int64_t n, int sq, int sp,
                                                       const ModC* __restrict__ src, const ModC* __restrict__ dst,
                                                       const uint32_t* __restrict__ qhat_inv,
-                                                      const uint32_t* __restrict__ tab) {
+                                                      const uint32_t* __restrict__ tab,
+                                                      const uint32_t* __restrict__ twist,
+                                                      const uint16_t* __restrict__ trow) {
   extern __shared__ uint32_t sm[];
   uint32_t* cs = sm;                          // [sq][BC_THREADS]
   uint32_t* ts = sm + (size_t)sq * BC_THREADS;  // BAT: [sp][4][sq], else [sp][sq]
@@ -57,7 +59,9 @@ __global__ void __launch_bounds__(BC_THREADS) k_bconv(const uint32_t* __restrict
           const uint32_t* tj = ts + (size_t)j * sq;
           for (int i = 0; i < sq; ++i) s += (uint64_t)cs[i * BC_THREADS + threadIdx.x] * tj[i];
         }
-        y[j * out_ls] = barrett_any(s, dst[j]);
+        uint32_t r = barrett_any(s, dst[j]);
+        if (twist) r = barrett_any((uint64_t)r * twist[(int64_t)trow[j] * n + t], dst[j]);
+        y[j * out_ls] = r;
       }
     }
   }
@@ -67,7 +71,7 @@ __global__ void __launch_bounds__(BC_THREADS) k_bconv(const uint32_t* __restrict
 
 int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t in_ps, int64_t in_ls,
               int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
-              int64_t n, cudaStream_t st) {
+              int64_t n, cudaStream_t st, const uint32_t* twist, const uint16_t* trow) {
   if (polys == 0 || n == 0) return CROSS_OK;
   const size_t smem = ((size_t)P->sq * BC_THREADS + (size_t)P->sp * 4 * P->sq) * sizeof(uint32_t);
   if (smem > 200 * 1024) {
@@ -79,11 +83,11 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
   if (bat) {
     cudaFuncSetAttribute(k_bconv<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_bconv<true><<<grid, BC_THREADS, smem, st>>>(in, in_ps, in_ls, in_ts, out, out_ps, out_ls, out_ts, polys, n,
-                                                   P->sq, P->sp, P->src, P->dst, P->qhat_inv, P->bat); count_launch();
+                                                   P->sq, P->sp, P->src, P->dst, P->qhat_inv, P->bat, twist, trow); count_launch();
   } else {
     cudaFuncSetAttribute(k_bconv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_bconv<false><<<grid, BC_THREADS, smem, st>>>(in, in_ps, in_ls, in_ts, out, out_ps, out_ls, out_ts, polys, n,
-                                                    P->sq, P->sp, P->src, P->dst, P->qhat_inv, P->qhat_modp); count_launch();
+                                                    P->sq, P->sp, P->src, P->dst, P->qhat_inv, P->qhat_modp, twist, trow); count_launch();
   }
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;

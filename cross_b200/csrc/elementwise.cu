@@ -129,6 +129,62 @@ __global__ void k_modmul_table_lm(LP x, LPo y, int64_t lps, int slots, int64_t n
   }
 }
 
+// out[lp][c][r] = in[lp][r][c] over strided limb-polynomials (32x33 tile).
+__global__ void k_transpose_lp_any(LP in, LPo out, int64_t lps, int slots, int rows, int cols) {
+  __shared__ uint32_t tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int64_t lp = blockIdx.z; lp < lps; lp += gridDim.z) {
+    const uint32_t* src = in.p + (lp / slots) * in.ps + (lp % slots) * in.ss;
+    uint32_t* dst = out.p + (lp / slots) * out.ps + (lp % slots) * out.ss;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const int r = r0 + i, c = c0 + threadIdx.x;
+      if (r < rows && c < cols) tile[i][threadIdx.x] = src[(int64_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const int c = c0 + i, r = r0 + threadIdx.x;
+      if (r < rows && c < cols) dst[(int64_t)c * rows + r] = tile[threadIdx.x][i];
+    }
+    __syncthreads();
+  }
+}
+
+// Position-wise EpiOp applied in place (the CUDA-core counterpart of the
+// tensor-core epilogue).
+__global__ void k_apply_epi(Epi e, LPo out, int64_t lps, int slots, int64_t n, const uint16_t* __restrict__ limbs,
+                            const ModC* __restrict__ mods) {
+  for (int64_t lp = blockIdx.y; lp < lps; lp += gridDim.y) {
+    const int64_t poly = lp / slots;
+    const int slot = (int)(lp % slots);
+    const ModC mc = mods[limbs[slot]];
+    const uint32_t q = (uint32_t)mc.q;
+    uint32_t* o = out.p + poly * out.ps + slot * out.ss;
+    const uint32_t* tab = e.op == EPI_MUL ? e.tab + (int64_t)e.trow[slot] * n : nullptr;
+    const uint32_t* x = (e.op == EPI_COMBINE || e.op == EPI_MODDOWN) ? e.x.at(poly, slot) : nullptr;
+    const bool add_base = e.op == EPI_MODDOWN && ((e.base_mask >> (poly % e.base.E)) & 1u);
+    const uint32_t* b = add_base ? e.base.at(poly, slot) : nullptr;
+    const uint64_t scal = (e.op == EPI_COMBINE || e.op == EPI_MODDOWN) ? e.scal[slot] : 0;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+      uint32_t r = o[t];
+      if (e.op == EPI_MUL) {
+        r = barrett_any((uint64_t)r * tab[t], mc);
+      } else if (e.op == EPI_COMBINE) {
+        r = barrett_any((uint64_t)x[t] * scal + r, mc);
+      } else if (e.op == EPI_MODDOWN) {
+        const uint32_t sub = x[t] < r ? x[t] + q - r : x[t] - r;
+        const uint32_t tt = barrett_any((uint64_t)sub * scal, mc);
+        if (add_base) {
+          const uint32_t s2 = b[t] + tt;
+          r = s2 >= q ? s2 - q : s2;
+        } else {
+          r = tt;
+        }
+      }
+      o[t] = r;
+    }
+  }
+}
+
 }  // namespace
 
 int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows, int64_t cols,
@@ -144,6 +200,32 @@ int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows
     dim3 grd((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)nb);
     k_transpose<<<grd, blk, 0, st>>>(in + b0 * rows * cols, out + b0 * rows * cols, rows, cols); count_launch();
   }
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int transpose_lp(LP in, LPo out, int64_t polys, int slots, int rows, int cols, cudaStream_t st) {
+  const int64_t lps = polys * slots;
+  if (lps == 0) return CROSS_OK;
+  if ((rows + 31) / 32 > 65535) {
+    set_error("transpose_lp: %d rows exceed the launch grid", rows);
+    return CROSS_ERR_UNSUPPORTED;
+  }
+  dim3 blk(32, 8), grd((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)(lps < 65535 ? lps : 65535));
+  k_transpose_lp_any<<<grd, blk, 0, st>>>(in, out, lps, slots, rows, cols);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int apply_epi(const Epi& e, LPo out, int64_t polys, int slots, int64_t N, const uint16_t* limbs, const ModC* mods,
+              cudaStream_t st) {
+  const int64_t lps = polys * slots;
+  if (e.op == EPI_NONE || lps == 0) return CROSS_OK;
+  unsigned gx = (unsigned)((N + EW_THREADS - 1) / EW_THREADS);
+  if (gx > 64) gx = 64;
+  k_apply_epi<<<dim3(gx, (unsigned)(lps < 65535 ? lps : 65535)), EW_THREADS, 0, st>>>(e, out, lps, slots, N, limbs, mods);
+  count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }

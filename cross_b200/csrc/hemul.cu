@@ -55,30 +55,6 @@ __global__ void k_rescale_lift(const uint32_t* __restrict__ LL, uint32_t* __rest
   }
 }
 
-// ciphertext.py:299-302: out = Barrett(x * beta_i + y).
-__global__ void k_rescale_combine(LP x, LP y, LPo out, int64_t polys, int L1, int64_t n,
-                                  const uint32_t* __restrict__ betas, const ModC* __restrict__ mods) {
-  const int64_t nv = n >> 2, rows = polys * L1;
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    const int64_t p = row / L1;
-    const int i = (int)(row % L1);
-    const ModC mc = mods[i];
-    const uint64_t beta = betas[i];
-    const uint4* xs = (const uint4*)(x.p + p * x.ps + i * x.ss);
-    const uint4* ys = (const uint4*)(y.p + p * y.ps + i * y.ss);
-    uint4* os = (uint4*)(out.p + p * out.ps + i * out.ss);
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
-      const uint4 a = xs[v], b = ys[v];
-      uint4 o;
-      o.x = barrett_any(a.x * beta + b.x, mc);
-      o.y = barrett_any(a.y * beta + b.y, mc);
-      o.z = barrett_any(a.z * beta + b.z, mc);
-      o.w = barrett_any(a.w * beta + b.w, mc);
-      os[v] = o;
-    }
-  }
-}
-
 // ciphertext.py:309-324 on [b][4][L1][N] -> D [b][3][L1][N].
 __global__ void k_tensor_lm(const uint32_t* __restrict__ R, uint32_t* __restrict__ D, int64_t batch, int L1,
                             int64_t n, const ModC* __restrict__ mods) {
@@ -140,43 +116,6 @@ __global__ void k_ks_inner(LP dig, PartPtrs parts, int nparts, const int16_t* __
   }
 }
 
-// ModDown tail + final add (hemul.py:198-215, herot.py:276-296):
-//   sub = a < g ? a + q - g : a - g   (uint32 wrap)
-//   v   = Barrett(sub * P^{-1} mod q)
-//   res = base + v ; res >= q ? res - q : res     (when base is given)
-// a = KS[b][e][i], g = G[b][e][i], base = B[b][e][i] (or none).
-__global__ void k_moddown_final(LP A, int64_t a_es, LP G, int64_t g_es, LP Bs, int64_t b_es, int has_base_e0,
-                                int has_base_e1, LPo O, int64_t o_es, int64_t batch, int L1, int64_t n,
-                                const uint32_t* __restrict__ pinv, const ModC* __restrict__ mods) {
-  const int64_t nv = n >> 2, rows = batch * 2 * L1;
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    const int64_t be = row / L1;
-    const int i = (int)(row % L1);
-    const int64_t b = be / 2;
-    const int e = (int)(be % 2);
-    const ModC mc = mods[i];
-    const uint32_t q = (uint32_t)mc.q;
-    const uint64_t pi = pinv[i];
-    const bool add = e == 0 ? has_base_e0 : has_base_e1;
-    const uint4* as = (const uint4*)(A.p + b * A.ps + e * a_es + i * A.ss);
-    const uint4* gs = (const uint4*)(G.p + b * G.ps + e * g_es + i * G.ss);
-    const uint4* bs = (const uint4*)(Bs.p + b * Bs.ps + e * b_es + i * Bs.ss);
-    uint4* os = (uint4*)(O.p + b * O.ps + e * o_es + i * O.ss);
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
-      const uint4 a = as[v], g = gs[v];
-      uint4 base = add ? bs[v] : make_uint4(0, 0, 0, 0);
-      auto f = [&](uint32_t x, uint32_t y, uint32_t bb) -> uint32_t {
-        const uint32_t sub = x < y ? x + q - y : x - y;
-        const uint32_t t = barrett_any((uint64_t)sub * pi, mc);
-        if (!add) return t;
-        const uint32_t s = bb + t;
-        return s >= q ? s - q : s;
-      };
-      os[v] = make_uint4(f(a.x, g.x, base.x), f(a.y, g.y, base.y), f(a.z, g.z, base.z), f(a.w, g.w, base.w));
-    }
-  }
-}
-
 // out[p][l][j] = in[p][l][map[j]] (limb-major automorphism, jnp.take semantics).
 __global__ void k_gather_lm(const uint32_t* __restrict__ in, const int32_t* __restrict__ map,
                             uint32_t* __restrict__ out, int64_t rows, int64_t n) {
@@ -191,18 +130,32 @@ __global__ void k_gather_lm(const uint32_t* __restrict__ in, const int32_t* __re
 
 bool same_q(const ModC& a, const ModC& b) { return a.q == b.q && a.m == b.m && a.w == b.w && a.s_w == b.s_w; }
 
+// rows x N table, natural coefficient order -> transposed order for an (R x C)
+// factorisation: out[row][c*R + r] = in[row][r*C + c].
+std::vector<uint32_t> to_transposed(const uint32_t* tab, int rows, int R, int C) {
+  const int64_t N = (int64_t)R * C;
+  std::vector<uint32_t> out((size_t)rows * N);
+  for (int row = 0; row < rows; ++row)
+    for (int r = 0; r < R; ++r)
+      for (int c = 0; c < C; ++c) out[(size_t)row * N + (size_t)c * R + r] = tab[(size_t)row * N + (size_t)r * C + c];
+  return out;
+}
+
 // Rescale by the last prime (ciphertext.py:267-303) on `polys` limb-major
-// polynomials: X has L limbs per poly (stride xps), R receives L-1 limbs
-// (stride L1*N).  plan covers at least the L moduli of Q at indices 0..L-1
-// (m_last = {L-1}, m_q1 = 0..L-2); mods_q1 are the Barrett constants of Q'.
+// polynomials: X has L limbs per poly (stride xps, evaluation order), R
+// receives L-1 limbs (stride L1*N).  The coefficient-domain intermediates stay
+// in transposed order: INTT(last limb) x psi^-i (fused) -> lift x gamma psi
+// -> NTT with x*beta + y fused into its last stage.  plan covers the L moduli
+// of Q at indices 0..L-1 (m_last = {L-1}, m_q1 = 0..L-2); mods_q1 are the
+// Barrett constants of Q'; the two tables are in transposed order.
 struct RescaleArgs {
   const cross_ntt_plan_s* ntt;
   const uint16_t* m_last;
   const uint16_t* m_zero;
   const uint16_t* m_q1;
   const ModC* mods_q1;
-  const uint32_t* inv_psi_last;
-  const uint32_t* gamma_psi;
+  const uint32_t* inv_psi_last_t;
+  const uint32_t* gamma_psi_t;
   const uint32_t* betas;
   uint32_t thr, q_last;
   int L;
@@ -214,21 +167,26 @@ int rescale_run(const RescaleArgs& a, const uint32_t* X, int64_t xps, uint32_t* 
   const int L1 = a.L - 1;
   const int64_t N = a.N, nv = N / 4;
   int rc;
-  if ((rc = ntt_run(a.ntt, true, LP{X + (int64_t)L1 * N, xps, 0}, LPo{LL, N, 0}, polys, 1, a.m_last, tmp, st)))
-    return rc;
-  if ((rc = modmul_table_lm(LP{LL, N, 0}, LPo{LL, N, 0}, polys, 1, N, a.inv_psi_last, a.m_zero, a.ntt->mods,
-                            a.m_last, st)))
+  Epi twist;
+  twist.op = EPI_MUL;
+  twist.tab = a.inv_psi_last_t;
+  twist.trow = a.m_zero;
+  if ((rc = ntt_exec(a.ntt, true, LP{X + (int64_t)L1 * N, xps, 0}, COEF_NATURAL, LPo{LL, N, 0}, COEF_TRANSPOSED, polys,
+                     1, a.m_last, twist, tmp, st)))
     return rc;
   k_rescale_lift<<<dim3(gx_for(nv), gy_for(polys * L1)), T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last,
-                                                                      a.gamma_psi, a.mods_q1); count_launch();
-  if ((rc = ntt_run(a.ntt, false, LP{R, (int64_t)L1 * N, N}, LPo{R, (int64_t)L1 * N, N}, polys, L1, a.m_q1, tmp, st)))
+                                                                      a.gamma_psi_t, a.mods_q1);
+  count_launch();
+  Epi comb;
+  comb.op = EPI_COMBINE;
+  comb.x = View{X, xps, 0, N, 1};
+  comb.scal = a.betas;
+  if ((rc = ntt_exec(a.ntt, false, LP{R, (int64_t)L1 * N, N}, COEF_TRANSPOSED, LPo{R, (int64_t)L1 * N, N},
+                     COEF_NATURAL, polys, L1, a.m_q1, comb, tmp, st)))
     return rc;
-  k_rescale_combine<<<dim3(gx_for(nv), gy_for(polys * L1)), T, 0, st>>>(
-      LP{X, xps, N}, LP{R, (int64_t)L1 * N, N}, LPo{R, (int64_t)L1 * N, N}, polys, L1, N, a.betas, a.mods_q1); count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }
-
 }  // namespace
 }  // namespace cross
 
@@ -244,19 +202,18 @@ struct cross_hemul_plan_s {
   cross_ntt_plan_s* ntt_qp = nullptr;
   cross_ntt_plan_s* ntt_p = nullptr;
   int p_off = 0;
+  int down_layout = COEF_TRANSPOSED;   // coefficient order of the ModDown INTT / BConv / NTT
   std::vector<cross_bconv_plan_s*> ks_bconv;
   cross_bconv_plan_s* down = nullptr;
   std::vector<int> dstart, dlen;
   std::vector<std::vector<int>> comp;   // complement, indices in Q'+P
   uint32_t thr = 0, q_last = 0;
-  // device
-  uint32_t *inv_psi_last = nullptr, *gamma_psi = nullptr, *inv_psi_q = nullptr, *psi_qp = nullptr,
-           *inv_psi_p = nullptr, *betas = nullptr, *pinv = nullptr;
+  // device tables; _t = transposed coefficient order, _d = ModDown order
+  uint32_t *inv_psi_last_t = nullptr, *gamma_psi_t = nullptr, *inv_psi_q_t = nullptr, *psi_qp_t = nullptr,
+           *inv_psi_p_d = nullptr, *psi_q_d = nullptr, *betas = nullptr, *pinv = nullptr;
   ModC* mods_dle = nullptr;
-  uint16_t *m_last = nullptr, *m_zero = nullptr, *seq = nullptr, *m_p_plan = nullptr, *m_p_dle = nullptr,
-           *m_q1_plan = nullptr;
+  uint16_t *m_last = nullptr, *m_zero = nullptr, *seq = nullptr, *m_p_plan = nullptr, *m_q1_plan = nullptr;
   std::vector<uint16_t*> comp_plan, comp_dle;
-  std::vector<uint16_t*> dig_plan;      // digit limbs as plan indices (unused by kernels, kept for checks)
   int16_t* ks_src = nullptr;
   uint32_t *evk_a = nullptr, *evk_b = nullptr;
 };
@@ -294,14 +251,13 @@ extern "C" {
 
 int cross_hemul_plan_destroy(cross_hemul_plan P) {
   if (!P) return CROSS_OK;
-  for (void* p : {(void*)P->inv_psi_last, (void*)P->gamma_psi, (void*)P->inv_psi_q, (void*)P->psi_qp,
-                  (void*)P->inv_psi_p, (void*)P->betas, (void*)P->pinv, (void*)P->mods_dle, (void*)P->m_last,
-                  (void*)P->m_zero, (void*)P->seq, (void*)P->m_p_plan, (void*)P->m_p_dle, (void*)P->m_q1_plan,
+  for (void* p : {(void*)P->inv_psi_last_t, (void*)P->gamma_psi_t, (void*)P->inv_psi_q_t, (void*)P->psi_qp_t,
+                  (void*)P->inv_psi_p_d, (void*)P->psi_q_d, (void*)P->betas, (void*)P->pinv, (void*)P->mods_dle,
+                  (void*)P->m_last, (void*)P->m_zero, (void*)P->seq, (void*)P->m_p_plan, (void*)P->m_q1_plan,
                   (void*)P->ks_src, (void*)P->evk_a, (void*)P->evk_b})
     dfree(p);
   for (auto* p : P->comp_plan) dfree(p);
   for (auto* p : P->comp_dle) dfree(p);
-  for (auto* p : P->dig_plan) dfree(p);
   delete P;
   return CROSS_OK;
 }
@@ -317,14 +273,17 @@ int cross_hemul_plan_create(const cross_hemul_desc* d, cross_hemul_plan* out) {
   const int L = d->L, L1 = L - 1, K = d->K;
   const int64_t N = (int64_t)d->r * d->c;
   CROSS_REQUIRE(N % 4 == 0, "cross_hemul_plan_create: N=%lld must be a multiple of 4", (long long)N);
-  CROSS_REQUIRE(d->ntt_qp->M == L + K && (int64_t)d->ntt_qp->r * d->ntt_qp->c == N,
-                "cross_hemul_plan_create: ntt_qp must cover L+K=%d limbs of N=%lld", L + K, (long long)N);
+  CROSS_REQUIRE(d->ntt_qp->M == L + K && d->ntt_qp->r == d->r && d->ntt_qp->c == d->c,
+                "cross_hemul_plan_create: ntt_qp must cover L+K=%d limbs with factorisation (%d, %d)", L + K, d->r, d->c);
   CROSS_REQUIRE(d->ntt_p->M >= d->ntt_p_limb_offset + K && (int64_t)d->ntt_p->r * d->ntt_p->c == N &&
                     d->ntt_p_limb_offset >= 0,
                 "cross_hemul_plan_create: ntt_p does not cover the P limbs");
   auto* P = new cross_hemul_plan_s();
   P->r = d->r; P->c = d->c; P->L = L; P->L1 = L1; P->K = K; P->dnum = d->dnum; P->N = N;
   P->ntt_qp = d->ntt_qp; P->ntt_p = d->ntt_p; P->p_off = d->ntt_p_limb_offset;
+  // The ModDown transforms keep transposed coefficients only when ntt_p has the
+  // same (r, c) split as ntt_qp; otherwise natural order (factorisation-free).
+  P->down_layout = (d->ntt_p->r == d->r && d->ntt_p->c == d->c) ? COEF_TRANSPOSED : COEF_NATURAL;
   P->alpha = (L1 + d->dnum - 1) / d->dnum;                     // ciphertext.py:354
   P->parts = (L1 + P->alpha - 1) / P->alpha;                   // ciphertext.py:356
   auto fail = [&](const char* msg, int q = -1) {
@@ -367,25 +326,31 @@ int cross_hemul_plan_create(const cross_hemul_desc* d, cross_hemul_plan* out) {
     if (!same_q(P->down->dst_host[i], dle[i])) return fail("down_bconv target moduli", i);
   P->q_last = (uint32_t)mq[L - 1].q;
   P->thr = (P->q_last + 1) / 2;                                 // ciphertext.py:260
-  std::vector<uint16_t> seq(std::max<int>(LT, 4) + 1), last{(uint16_t)(L - 1)}, zero{0}, pp, pd, q1;
+  std::vector<uint16_t> seq(std::max<int>(LT, 4) + 1), last{(uint16_t)(L - 1)}, zero{0}, pp, q1;
   for (size_t i = 0; i < seq.size(); ++i) seq[i] = (uint16_t)i;
-  for (int k = 0; k < K; ++k) { pp.push_back((uint16_t)(P->p_off + k)); pd.push_back((uint16_t)(L1 + k)); }
+  for (int k = 0; k < K; ++k) pp.push_back((uint16_t)(P->p_off + k));
   for (int i = 0; i < L1; ++i) q1.push_back((uint16_t)i);
+  const int R = d->r, C = d->c;
   int rc = CROSS_OK;
-  auto up32 = [&](uint32_t** dst, const uint32_t* s, size_t n) { if (!rc) rc = upload(dst, s, n); };
-  up32(&P->inv_psi_last, d->inv_psi_last, N);
-  up32(&P->gamma_psi, d->gamma_psi, (size_t)L1 * N);
-  up32(&P->inv_psi_q, d->inv_psi_q, (size_t)L1 * N);
-  up32(&P->psi_qp, d->psi_qp, (size_t)LT * N);
-  up32(&P->inv_psi_p, d->inv_psi_p, (size_t)K * N);
-  up32(&P->betas, d->betas, L1);
-  up32(&P->pinv, d->p_inv_mod_q, L1);
+  auto upv = [&](uint32_t** dst, const std::vector<uint32_t>& v) { if (!rc) rc = upload_vec(dst, v); };
+  upv(&P->inv_psi_last_t, to_transposed(d->inv_psi_last, 1, R, C));
+  upv(&P->gamma_psi_t, to_transposed(d->gamma_psi, L1, R, C));
+  upv(&P->inv_psi_q_t, to_transposed(d->inv_psi_q, L1, R, C));
+  upv(&P->psi_qp_t, to_transposed(d->psi_qp, LT, R, C));
+  if (P->down_layout == COEF_TRANSPOSED) {
+    upv(&P->inv_psi_p_d, to_transposed(d->inv_psi_p, K, R, C));
+    upv(&P->psi_q_d, to_transposed(d->psi_qp, L1, R, C));
+  } else {
+    upv(&P->inv_psi_p_d, std::vector<uint32_t>(d->inv_psi_p, d->inv_psi_p + (size_t)K * N));
+    upv(&P->psi_q_d, std::vector<uint32_t>(d->psi_qp, d->psi_qp + (size_t)L1 * N));
+  }
+  if (!rc) rc = upload(&P->betas, d->betas, L1);
+  if (!rc) rc = upload(&P->pinv, d->p_inv_mod_q, L1);
   if (!rc) rc = upload_vec(&P->mods_dle, dle);
   if (!rc) rc = upload_vec(&P->m_last, last);
   if (!rc) rc = upload_vec(&P->m_zero, zero);
   if (!rc) rc = upload_vec(&P->seq, seq);
   if (!rc) rc = upload_vec(&P->m_p_plan, pp);
-  if (!rc) rc = upload_vec(&P->m_p_dle, pd);
   if (!rc) rc = upload_vec(&P->m_q1_plan, q1);
   if (!rc) rc = upload_vec(&P->ks_src, src);
   for (int j = 0; j < P->parts && !rc; ++j) {
@@ -466,59 +431,61 @@ int cross_hemul(cross_hemul_plan P, const uint32_t* in, uint32_t* out, int64_t B
   const dim3 blk(T);
   // 1. rescale (ciphertext.py:267-303)
   {
-    RescaleArgs ra{P->ntt_qp, P->m_last, P->m_zero, P->m_q1_plan, P->mods_dle, P->inv_psi_last, P->gamma_psi,
+    RescaleArgs ra{P->ntt_qp, P->m_last, P->m_zero, P->m_q1_plan, P->mods_dle, P->inv_psi_last_t, P->gamma_psi_t,
                    P->betas, P->thr, P->q_last, L, N};
     if ((rc = rescale_run(ra, X, (int64_t)L * N, b.R, b.LL, b.tmp, B * 4, st))) return rc;
   }
   // 2. tensor product (ciphertext.py:309-324)
-  k_tensor_lm<<<dim3(gx_for(nv), gy_for(B * L1)), blk, 0, st>>>(b.R, b.D, B, L1, N, P->mods_dle); count_launch();
-  // 3. key switch on d2 (ciphertext.py:455-519)
+  k_tensor_lm<<<dim3(gx_for(nv), gy_for(B * L1)), blk, 0, st>>>(b.R, b.D, B, L1, N, P->mods_dle);
+  count_launch();
+  // 3. key switch on d2 (ciphertext.py:455-519): INTT x psi^-i (fused, transposed
+  // coefficients) -> per digit BConv x psi^i (fused) -> NTT -> inner product
   const uint32_t* D2 = b.D + 2 * (int64_t)L1 * N;
   const int64_t Dps = 3 * (int64_t)L1 * N;
-  if ((rc = ntt_run(P->ntt_qp, true, LP{D2, Dps, N}, LPo{b.Cc, (int64_t)L1 * N, N}, B, L1, P->m_q1_plan, b.tmp, st)))
-    return rc;
-  if ((rc = modmul_table_lm(LP{b.Cc, (int64_t)L1 * N, N}, LPo{b.Cc, (int64_t)L1 * N, N}, B, L1, N, P->inv_psi_q,
-                            P->seq, P->mods_dle, P->seq, st)))
+  Epi tw;
+  tw.op = EPI_MUL;
+  tw.tab = P->inv_psi_q_t;
+  tw.trow = P->seq;
+  if ((rc = ntt_exec(P->ntt_qp, true, LP{D2, Dps, N}, COEF_NATURAL, LPo{b.Cc, (int64_t)L1 * N, N}, COEF_TRANSPOSED, B,
+                     L1, P->m_q1_plan, tw, b.tmp, st)))
     return rc;
   PartPtrs pp{};
   for (int j = 0; j < P->parts; ++j) {
     const int ns = LT - P->dlen[j];
     const int64_t eps = (int64_t)ns * N;
     if ((rc = bconv_run(P->ks_bconv[j], true, b.Cc + (int64_t)P->dstart[j] * N, (int64_t)L1 * N, N, 1, b.E[j], eps,
-                        N, 1, B, N, st)))
+                        N, 1, B, N, st, P->psi_qp_t, P->comp_dle[j])))
       return rc;
-    if ((rc = modmul_table_lm(LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, N, P->psi_qp, P->comp_dle[j],
-                              P->mods_dle, P->comp_dle[j], st)))
-      return rc;
-    if ((rc = ntt_run(P->ntt_qp, false, LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, P->comp_plan[j], b.tmp, st)))
+    if ((rc = ntt_exec(P->ntt_qp, false, LP{b.E[j], eps, N}, COEF_TRANSPOSED, LPo{b.E[j], eps, N}, COEF_NATURAL, B, ns,
+                       P->comp_plan[j], Epi{}, b.tmp, st)))
       return rc;
     pp.e[j] = b.E[j];
     pp.ps[j] = eps;
   }
   k_ks_inner<<<dim3(gx_for(nv), gy_for(B * LT)), blk, 0, st>>>(LP{D2, Dps, N}, pp, P->parts, P->ks_src, LT, N, B,
-                                                               P->evk_a, P->evk_b, b.KS, P->mods_dle); count_launch();
-  // 4. ModDown (hemul.py:175-211)
-  const int64_t KSps = 2 * (int64_t)LT * N;
-  for (int e = 0; e < 2; ++e) {
-    if ((rc = ntt_run(P->ntt_p, true, LP{b.KS + ((int64_t)e * LT + L1) * N, KSps, N},
-                      LPo{b.KP + (int64_t)e * K * N, 2 * (int64_t)K * N, N}, B, K, P->m_p_plan, b.tmp, st)))
-      return rc;
-  }
-  if ((rc = modmul_table_lm(LP{b.KP, (int64_t)K * N, N}, LPo{b.KP, (int64_t)K * N, N}, B * 2, K, N, P->inv_psi_p,
-                            P->seq, P->mods_dle, P->m_p_dle, st)))
+                                                               P->evk_a, P->evk_b, b.KS, P->mods_dle);
+  count_launch();
+  // 4. ModDown (hemul.py:175-215): INTT of the P limbs of both elements x psi^-i
+  // -> BConv P -> Q' x psi^i -> NTT whose last stage applies the subtraction, the
+  // P^-1 scaling and the add of (d0, d1).  Element e of ciphertext b is e' = 2b + e.
+  const int64_t KSes = (int64_t)LT * N;
+  tw.tab = P->inv_psi_p_d;
+  if ((rc = ntt_exec(P->ntt_p, true, LP{b.KS + (int64_t)L1 * N, KSes, N}, COEF_NATURAL, LPo{b.KP, (int64_t)K * N, N},
+                     P->down_layout, B * 2, K, P->m_p_plan, tw, b.tmp, st)))
     return rc;
-  if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L1 * N, N, 1, B * 2, N, st))) return rc;
-  if ((rc = modmul_table_lm(LP{b.F, (int64_t)L1 * N, N}, LPo{b.F, (int64_t)L1 * N, N}, B * 2, L1, N, P->psi_qp,
-                            P->seq, P->mods_dle, P->seq, st)))
+  if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L1 * N, N, 1, B * 2, N, st, P->psi_q_d,
+                      P->seq)))
     return rc;
-  if ((rc = ntt_run(P->ntt_qp, false, LP{b.F, (int64_t)L1 * N, N}, LPo{b.F, (int64_t)L1 * N, N}, B * 2, L1,
-                    P->m_q1_plan, b.tmp, st)))
-    return rc;
-  // 5. final add (hemul.py:214-215): res = d_e + ModDown_e
+  Epi md;
+  md.op = EPI_MODDOWN;
+  md.x = View{b.KS, KSes, 0, N, 1};
+  md.scal = P->pinv;
+  md.base = View{b.D, Dps, (int64_t)L1 * N, N, 2};
+  md.base_mask = 3u;
   uint32_t* O = layout == CROSS_LAYOUT_REFERENCE ? b.O : out;
-  k_moddown_final<<<dim3(gx_for(nv), gy_for(B * 2 * L1)), blk, 0, st>>>(
-      LP{b.KS, KSps, N}, (int64_t)LT * N, LP{b.F, 2 * (int64_t)L1 * N, N}, (int64_t)L1 * N, LP{b.D, Dps, N},
-      (int64_t)L1 * N, 1, 1, LPo{O, 2 * (int64_t)L1 * N, N}, (int64_t)L1 * N, B, L1, N, P->pinv, P->mods_dle); count_launch();
+  if ((rc = ntt_exec(P->ntt_qp, false, LP{b.F, (int64_t)L1 * N, N}, P->down_layout, LPo{O, (int64_t)L1 * N, N},
+                     COEF_NATURAL, B * 2, L1, P->m_q1_plan, md, b.tmp, st)))
+    return rc;
   CROSS_CHECK_CUDA(cudaGetLastError());
   if (layout == CROSS_LAYOUT_REFERENCE) return transpose_u32(b.O, out, B * 2, L1, N, st);
   return CROSS_OK;
@@ -537,7 +504,8 @@ struct cross_herot_plan_s {
   std::vector<cross_bconv_plan_s*> ks_bconv;
   cross_bconv_plan_s* down = nullptr;
   std::vector<int> dstart, dlen;
-  uint32_t *inv_psi_q = nullptr, *psi_qp = nullptr, *inv_psi_p = nullptr, *pinv = nullptr;
+  // coefficient-order tables, transposed for the (r, c) split of the plan
+  uint32_t *inv_psi_q_t = nullptr, *psi_qp_t = nullptr, *inv_psi_p_t = nullptr, *pinv = nullptr;
   uint16_t *seq = nullptr, *m_p = nullptr;
   std::vector<uint16_t*> comp;
   int16_t* ks_src = nullptr;
@@ -576,7 +544,7 @@ extern "C" {
 
 int cross_herot_plan_destroy(cross_herot_plan P) {
   if (!P) return CROSS_OK;
-  for (void* p : {(void*)P->inv_psi_q, (void*)P->psi_qp, (void*)P->inv_psi_p, (void*)P->pinv, (void*)P->seq,
+  for (void* p : {(void*)P->inv_psi_q_t, (void*)P->psi_qp_t, (void*)P->inv_psi_p_t, (void*)P->pinv, (void*)P->seq,
                   (void*)P->m_p, (void*)P->ks_src, (void*)P->evk_a, (void*)P->evk_b, (void*)P->coef_map})
     dfree(p);
   for (auto* p : P->comp) dfree(p);
@@ -636,11 +604,12 @@ int cross_herot_plan_create(const cross_herot_desc* d, cross_herot_plan* out) {
   for (size_t i = 0; i < seq.size(); ++i) seq[i] = (uint16_t)i;
   for (int k = 0; k < K; ++k) mp.push_back((uint16_t)(L + k));
   int rc = CROSS_OK;
-  auto up32 = [&](uint32_t** dst, const uint32_t* s, size_t n) { if (!rc) rc = upload(dst, s, n); };
-  up32(&P->inv_psi_q, d->inv_psi_q, (size_t)L * N);
-  up32(&P->psi_qp, d->psi_qp, (size_t)LT * N);
-  up32(&P->inv_psi_p, d->inv_psi_p, (size_t)K * N);
-  up32(&P->pinv, d->p_inv_mod_q, L);
+  const int R = d->ntt_qp->r, C = d->ntt_qp->c;
+  auto upv = [&](uint32_t** dst, const std::vector<uint32_t>& v) { if (!rc) rc = upload_vec(dst, v); };
+  upv(&P->inv_psi_q_t, to_transposed(d->inv_psi_q, L, R, C));
+  upv(&P->psi_qp_t, to_transposed(d->psi_qp, LT, R, C));
+  upv(&P->inv_psi_p_t, to_transposed(d->inv_psi_p, K, R, C));
+  if (!rc) rc = upload(&P->pinv, d->p_inv_mod_q, L);
   if (!rc) rc = upload_vec(&P->seq, seq);
   if (!rc) rc = upload_vec(&P->m_p, mp);
   if (!rc) rc = upload_vec(&P->ks_src, src);
@@ -712,48 +681,50 @@ int cross_herot(cross_herot_plan P, const uint32_t* in, uint32_t* out, int64_t B
   const dim3 blk(T);
   const int64_t Xps = 2 * (int64_t)L * N;
   const uint32_t* X1 = X + (int64_t)L * N;   // in_tower = element 1 (herot.py:201)
-  // 1. key switch of element 1 (herot.py:203-247)
-  if ((rc = ntt_run(P->ntt, true, LP{X1, Xps, N}, LPo{b.Cq, (int64_t)L * N, N}, B, L, P->seq, b.tmp, st))) return rc;
-  if ((rc = modmul_table_lm(LP{b.Cq, (int64_t)L * N, N}, LPo{b.Cq, (int64_t)L * N, N}, B, L, N, P->inv_psi_q, P->seq,
-                            P->ntt->mods, P->seq, st)))
+  // 1. key switch of element 1 (herot.py:203-247): INTT x psi^-i (fused,
+  // transposed coefficients) -> per digit BConv x psi^i -> NTT -> inner product
+  Epi tw;
+  tw.op = EPI_MUL;
+  tw.tab = P->inv_psi_q_t;
+  tw.trow = P->seq;
+  if ((rc = ntt_exec(P->ntt, true, LP{X1, Xps, N}, COEF_NATURAL, LPo{b.Cq, (int64_t)L * N, N}, COEF_TRANSPOSED, B, L,
+                     P->seq, tw, b.tmp, st)))
     return rc;
   PartPtrs pp{};
   for (int j = 0; j < P->parts; ++j) {
     const int ns = LT - P->dlen[j];
     const int64_t eps = (int64_t)ns * N;
     if ((rc = bconv_run(P->ks_bconv[j], true, b.Cq + (int64_t)P->dstart[j] * N, (int64_t)L * N, N, 1, b.E[j], eps, N,
-                        1, B, N, st)))
+                        1, B, N, st, P->psi_qp_t, P->comp[j])))
       return rc;
-    if ((rc = modmul_table_lm(LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, N, P->psi_qp, P->comp[j], P->ntt->mods,
-                              P->comp[j], st)))
+    if ((rc = ntt_exec(P->ntt, false, LP{b.E[j], eps, N}, COEF_TRANSPOSED, LPo{b.E[j], eps, N}, COEF_NATURAL, B, ns,
+                       P->comp[j], Epi{}, b.tmp, st)))
       return rc;
-    if ((rc = ntt_run(P->ntt, false, LP{b.E[j], eps, N}, LPo{b.E[j], eps, N}, B, ns, P->comp[j], b.tmp, st))) return rc;
     pp.e[j] = b.E[j];
     pp.ps[j] = eps;
   }
   k_ks_inner<<<dim3(gx_for(nv), gy_for(B * LT)), blk, 0, st>>>(LP{X1, Xps, N}, pp, P->parts, P->ks_src, LT, N, B,
-                                                               P->evk_a, P->evk_b, b.KS, P->ntt->mods); count_launch();
-  // 2. ModDown per element (herot.py:255-289)
-  const int64_t KSps = 2 * (int64_t)LT * N;
-  for (int e = 0; e < 2; ++e) {
-    if ((rc = ntt_run(P->ntt, true, LP{b.KS + ((int64_t)e * LT + L) * N, KSps, N},
-                      LPo{b.KP + (int64_t)e * K * N, 2 * (int64_t)K * N, N}, B, K, P->m_p, b.tmp, st)))
-      return rc;
-  }
-  if ((rc = modmul_table_lm(LP{b.KP, (int64_t)K * N, N}, LPo{b.KP, (int64_t)K * N, N}, B * 2, K, N, P->inv_psi_p,
-                            P->seq, P->ntt->mods, P->m_p, st)))
+                                                               P->evk_a, P->evk_b, b.KS, P->ntt->mods);
+  count_launch();
+  // 2. ModDown of both elements (herot.py:255-289) and c0 += ModDown_0
+  // (herot.py:292-296), the tail fused into the last NTT stage.
+  const int64_t KSes = (int64_t)LT * N;
+  tw.tab = P->inv_psi_p_t;
+  if ((rc = ntt_exec(P->ntt, true, LP{b.KS + (int64_t)L * N, KSes, N}, COEF_NATURAL, LPo{b.KP, (int64_t)K * N, N},
+                     COEF_TRANSPOSED, B * 2, K, P->m_p, tw, b.tmp, st)))
     return rc;
-  if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L * N, N, 1, B * 2, N, st))) return rc;
-  if ((rc = modmul_table_lm(LP{b.F, (int64_t)L * N, N}, LPo{b.F, (int64_t)L * N, N}, B * 2, L, N, P->psi_qp, P->seq,
-                            P->ntt->mods, P->seq, st)))
+  if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L * N, N, 1, B * 2, N, st, P->psi_qp_t,
+                      P->seq)))
     return rc;
-  if ((rc = ntt_run(P->ntt, false, LP{b.F, (int64_t)L * N, N}, LPo{b.F, (int64_t)L * N, N}, B * 2, L, P->seq, b.tmp,
-                    st)))
+  Epi md;
+  md.op = EPI_MODDOWN;
+  md.x = View{b.KS, KSes, 0, N, 1};
+  md.scal = P->pinv;
+  md.base = View{X, Xps, (int64_t)L * N, N, 2};
+  md.base_mask = 1u;
+  if ((rc = ntt_exec(P->ntt, false, LP{b.F, (int64_t)L * N, N}, COEF_TRANSPOSED, LPo{b.Rz, (int64_t)L * N, N},
+                     COEF_NATURAL, B * 2, L, P->seq, md, b.tmp, st)))
     return rc;
-  // 3. c0 += ModDown_0 (herot.py:292-296); element 1 is ModDown_1
-  k_moddown_final<<<dim3(gx_for(nv), gy_for(B * 2 * L)), blk, 0, st>>>(
-      LP{b.KS, KSps, N}, (int64_t)LT * N, LP{b.F, 2 * (int64_t)L * N, N}, (int64_t)L * N, LP{X, Xps, N},
-      (int64_t)L * N, 1, 0, LPo{b.Rz, 2 * (int64_t)L * N, N}, (int64_t)L * N, B, L, N, P->pinv, P->ntt->mods); count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   // 4. automorphism (herot.py:300)
   if (layout == CROSS_LAYOUT_REFERENCE) {
@@ -777,7 +748,7 @@ struct cross_rescale_plan_s {
   int L = 0;
   int64_t N = 0;
   cross_ntt_plan_s* ntt = nullptr;
-  uint32_t *inv_psi_last = nullptr, *gamma_psi = nullptr, *betas = nullptr;
+  uint32_t *inv_psi_last_t = nullptr, *gamma_psi_t = nullptr, *betas = nullptr;
   uint16_t *m_last = nullptr, *m_zero = nullptr, *m_q1 = nullptr;
   uint32_t thr = 0, q_last = 0;
 };
@@ -799,8 +770,8 @@ extern "C" {
 
 int cross_rescale_plan_destroy(cross_rescale_plan P) {
   if (!P) return CROSS_OK;
-  for (void* p : {(void*)P->inv_psi_last, (void*)P->gamma_psi, (void*)P->betas, (void*)P->m_last, (void*)P->m_zero,
-                  (void*)P->m_q1})
+  for (void* p : {(void*)P->inv_psi_last_t, (void*)P->gamma_psi_t, (void*)P->betas, (void*)P->m_last,
+                  (void*)P->m_zero, (void*)P->m_q1})
     dfree(p);
   delete P;
   return CROSS_OK;
@@ -821,8 +792,8 @@ int cross_rescale_plan_create(const cross_rescale_desc* d, cross_rescale_plan* o
   P->thr = (P->q_last + 1) / 2;
   std::vector<uint16_t> last{(uint16_t)(d->L - 1)}, zero{0}, q1;
   for (int i = 0; i < d->L - 1; ++i) q1.push_back((uint16_t)i);
-  int rc = upload(&P->inv_psi_last, d->inv_psi_last, (size_t)N);
-  if (!rc) rc = upload(&P->gamma_psi, d->gamma_psi, (size_t)(d->L - 1) * N);
+  int rc = upload_vec(&P->inv_psi_last_t, to_transposed(d->inv_psi_last, 1, d->ntt_q->r, d->ntt_q->c));
+  if (!rc) rc = upload_vec(&P->gamma_psi_t, to_transposed(d->gamma_psi, d->L - 1, d->ntt_q->r, d->ntt_q->c));
   if (!rc) rc = upload(&P->betas, d->betas, (size_t)(d->L - 1));
   if (!rc) rc = upload_vec(&P->m_last, last);
   if (!rc) rc = upload_vec(&P->m_zero, zero);
@@ -863,7 +834,7 @@ int cross_rescale(cross_rescale_plan P, const uint32_t* in, uint32_t* out, int64
   RescaleBufs b;
   rescale_layout(P, polys, layout, a, b);
   // Barrett constants of Q' are the first L-1 entries of the plan's table.
-  RescaleArgs ra{P->ntt, P->m_last, P->m_zero, P->m_q1, P->ntt->mods, P->inv_psi_last, P->gamma_psi, P->betas,
+  RescaleArgs ra{P->ntt, P->m_last, P->m_zero, P->m_q1, P->ntt->mods, P->inv_psi_last_t, P->gamma_psi_t, P->betas,
                  P->thr, P->q_last, L, N};
   int rc;
   if (layout == CROSS_LAYOUT_LIMB_MAJOR) return rescale_run(ra, in, (int64_t)L * N, out, b.LL, b.tmp, polys, st);

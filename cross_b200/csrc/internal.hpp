@@ -90,30 +90,77 @@ template <class T>
 int upload_vec(T** dst, const std::vector<T>& v) { return upload(dst, v.data(), v.size()); }
 void dfree(void* p);
 
-// Scratch words ntt_run needs for lps limb-polynomials.
+// Scratch words ntt_run / ntt_exec need for lps limb-polynomials.
 int64_t ntt_tmp_words(const cross_ntt_plan_s* plan, int64_t lps);
+
+// Coefficient-domain order of a limb-polynomial: natural (index r*C + c at
+// position r*C + c) or transposed (index r*C + c at position c*R + r).  The
+// evaluation domain is always in the reference's (bit-reversed) order.
+enum CoefLayout { COEF_NATURAL = 0, COEF_TRANSPOSED = 1 };
+
+// An operand that shares the output's position layout.  Element index e of a
+// batch splits as (e / E, e % E) with strides (ps, es); slots stride ss.
+struct View {
+  const uint32_t* p = nullptr;
+  int64_t ps = 0, es = 0, ss = 0;
+  int E = 1;
+  __host__ __device__ const uint32_t* at(int64_t e, int slot) const { return p + (e / E) * ps + (e % E) * es + slot * ss; }
+};
+
+// Position-wise operation fused into the last stage of a transform; r is the
+// Barrett-reduced transform output at a position:
+//   EPI_MUL      r = Barrett(r * tab[trow[slot]][pos])              (psi twists)
+//   EPI_COMBINE  r = Barrett(x[pos] * scal[slot] + r)               (rescale, ciphertext.py:299-302)
+//   EPI_MODDOWN  s = x[pos] < r ? x[pos] + q - r : x[pos] - r       (ModDown, hemul.py:198-215)
+//                t = Barrett(s * scal[slot]);
+//                r = base on for e % E ? (base[pos] + t >= q ? base[pos] + t - q : base[pos] + t) : t
+enum EpiOp { EPI_NONE = 0, EPI_MUL = 1, EPI_COMBINE = 2, EPI_MODDOWN = 3 };
+struct Epi {
+  int op = EPI_NONE;
+  const uint32_t* tab = nullptr;
+  const uint16_t* trow = nullptr;
+  View x;
+  const uint32_t* scal = nullptr;
+  View base;
+  unsigned base_mask = 0;
+};
+
+// NTT (inverse = false): input coefficients in `in_layout`, output evaluations.
+// INTT (inverse = true): input evaluations, output coefficients in `out_layout`.
+// epi is applied to the final output.  tmp holds ntt_tmp_words() words.
+int ntt_exec(const cross_ntt_plan_s* plan, bool inverse, LP in, int in_layout, LPo out, int out_layout,
+             int64_t polys, int slots, const uint16_t* limbs, const Epi& epi, uint32_t* tmp, cudaStream_t st);
 
 // tensor-core path (ntt_tc.cu)
 bool tc_supported(int r, int c);
 int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, const uint8_t* intt1,
                  const uint8_t* intt3, const uint32_t* intt_tw);
 void tc_plan_free(cross_ntt_plan_s* P);
-int ntt_run_tc(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
-               const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
+int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo out, int out_layout,
+                int64_t polys, int slots, const uint16_t* limbs, const Epi& epi, uint32_t* tmp, cudaStream_t st);
 
 // NTT over polys x slots limb-polynomials (internal layout); limbs[slot] is the
 // plan limb of each slot (device array).  tmp holds ntt_tmp_words() words.
 int ntt_run(const cross_ntt_plan_s* plan, bool inverse, LP in, LPo out, int64_t polys, int slots,
             const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
 
-// bconv over polys with arbitrary limb / coefficient strides.
+// bconv over polys with arbitrary limb / coefficient strides.  With tab set,
+// output limb j is further multiplied by tab[trow[j]][t] (position t) and
+// Barrett-reduced with the target modulus (the psi twist of ciphertext.py:496).
 int bconv_run(const cross_bconv_plan_s* plan, bool bat, const uint32_t* in, int64_t in_ps,
               int64_t in_ls, int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls,
-              int64_t out_ts, int64_t polys, int64_t n, cudaStream_t st);
+              int64_t out_ts, int64_t polys, int64_t n, cudaStream_t st, const uint32_t* tab = nullptr,
+              const uint16_t* trow = nullptr);
 
 // y[poly, slot, t] = Barrett_{mods[midx[slot]]}(x * tab[trow[slot] * n + t])
 int modmul_table_lm(LP x, LPo y, int64_t polys, int slots, int64_t n, const uint32_t* tab,
                     const uint16_t* trow, const ModC* mods, const uint16_t* midx, cudaStream_t st);
+// Strided batched transpose of limb-polynomials: out[lp][c][r] = in[lp][r][c]
+// for (rows x cols) matrices; any sizes.
+int transpose_lp(LP in, LPo out, int64_t polys, int slots, int rows, int cols, cudaStream_t st);
+// Apply epi (EpiOp) in place to out, N words per limb-polynomial.
+int apply_epi(const Epi& e, LPo out, int64_t polys, int slots, int64_t N, const uint16_t* limbs, const ModC* mods,
+              cudaStream_t st);
 // batched 2-D transpose: in (batch, rows, cols) -> out (batch, cols, rows)
 int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows, int64_t cols,
                   cudaStream_t st);

@@ -180,13 +180,45 @@ unsigned grid_z(int64_t lps) { return (unsigned)(lps < 65535 ? lps : 65535); }
 
 }  // namespace
 
-int64_t ntt_tmp_words(const cross_ntt_plan_s* P, int64_t lps) {
-  return lps * P->r * P->c * (P->tc ? 2 : 1);
-}
+int64_t ntt_tmp_words(const cross_ntt_plan_s* P, int64_t lps) { return lps * P->r * P->c * 2; }
+
+static int ntt_run_dp4a(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+                        const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
 
 int ntt_run(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
             const uint16_t* limbs, uint32_t* tmp, cudaStream_t st) {
-  if (P->tc && polys * slots > 0) return ntt_run_tc(P, inverse, in, out, polys, slots, limbs, tmp, st);
+  return ntt_exec(P, inverse, in, COEF_NATURAL, out, COEF_NATURAL, polys, slots, limbs, Epi{}, tmp, st);
+}
+
+int ntt_exec(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo out, int out_layout, int64_t polys,
+             int slots, const uint16_t* limbs, const Epi& epi, uint32_t* tmp, cudaStream_t st) {
+  const int64_t lps = polys * slots;
+  if (lps == 0) return CROSS_OK;
+  if (P->tc) return ntt_exec_tc(P, inverse, in, in_layout, out, out_layout, polys, slots, limbs, epi, tmp, st);
+  // CUDA-core path: natural-order transforms composed with the layout
+  // conversions and the position-wise op.
+  const int R = P->r, C = P->c;
+  const int64_t N = (int64_t)R * C;
+  uint32_t* t2 = tmp + lps * N;
+  int rc;
+  if (!inverse) {
+    LP src = in;
+    if (in_layout == COEF_TRANSPOSED) {
+      if ((rc = transpose_lp(in, LPo{t2, slots * N, N}, polys, slots, C, R, st))) return rc;
+      src = LP{t2, slots * N, N};
+    }
+    if ((rc = ntt_run_dp4a(P, false, src, out, polys, slots, limbs, tmp, st))) return rc;
+  } else if (out_layout == COEF_NATURAL) {
+    if ((rc = ntt_run_dp4a(P, true, in, out, polys, slots, limbs, tmp, st))) return rc;
+  } else {
+    if ((rc = ntt_run_dp4a(P, true, in, LPo{t2, slots * N, N}, polys, slots, limbs, tmp, st))) return rc;
+    if ((rc = transpose_lp(LP{t2, slots * N, N}, out, polys, slots, R, C, st))) return rc;
+  }
+  return apply_epi(epi, out, polys, slots, N, limbs, P->mods, st);
+}
+
+static int ntt_run_dp4a(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+                        const uint16_t* limbs, uint32_t* tmp, cudaStream_t st) {
   const int R = P->r, C = P->c;
   const int64_t N = (int64_t)R * C;
   const int64_t lps = polys * slots;

@@ -64,10 +64,10 @@ struct Args {
   int slots;
   int64_t polys;
   int rows_m, kw, nout;
-  const uint32_t* tw;              // [M][nout][rows_m] or null
   const ModC* mods;
   int* err;
   int fast;                        // every limb qualifies for reduce_fast (see below)
+  Epi e;                           // fused position-wise op (EpiOp)
 };
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -202,7 +202,7 @@ __device__ __forceinline__ Unit decode(int64_t u, int n_tiles, int m_tiles, int6
   return r;
 }
 
-template <bool TWIDDLE, bool NMAJOR>
+template <int EPI, bool NMAJOR>
 __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ CUtensorMap tmA,
                                                        const __grid_constant__ CUtensorMap tmB, const Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -304,18 +304,41 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
     }
   } else {
     // ---------------- epilogue (warps 2..9: TMEM lane quadrant warp % 4, column half) ----------------
+    // Output position of (row m, output n): NMAJOR n*rows_m + m, else m*nout + n.
+    // The operands of the fused op are read at the same positions, before the
+    // accumulator is ready.
     const int quad = warp & 3, half = (warp - 2) >> 2;
+    const int64_t N = (int64_t)a.rows_m * a.nout;
+    constexpr int P0 = EPI == EPI_NONE ? 1 : 32;
+    constexpr int P1 = EPI == EPI_MODDOWN ? 32 : 1;
     uint32_t acc = 0, aphase = 0;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit w = decode(u, n_tiles, m_tiles, a.polys);
       const int limb = a.limbs[w.slot];
       const int m = w.mt * BM + quad * 32 + lane;
       const int n0 = w.nt * 64 + half * 32;
-      uint32_t twv[TWIDDLE ? 32 : 1];
-      if (TWIDDLE) {
-        const uint32_t* twp = a.tw + ((size_t)limb * a.nout + n0) * a.rows_m + m;
+      const int64_t p0 = NMAJOR ? (int64_t)n0 * a.rows_m + m : (int64_t)m * a.nout + n0;
+      const int64_t pstep = NMAJOR ? a.rows_m : 1;
+      uint32_t pre0[P0], pre1[P1];
+      uint64_t scal = 0;
+      bool add_base = false;
+      if (EPI == EPI_MUL) {
+        const uint32_t* t = a.e.tab + (int64_t)a.e.trow[w.slot] * N + p0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) twv[j] = __ldg(twp + (size_t)j * a.rows_m);
+        for (int j = 0; j < 32; ++j) pre0[j] = __ldg(t + j * pstep);
+      } else if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) {
+        const uint32_t* x = a.e.x.at(w.poly, w.slot) + p0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pre0[j] = x[j * pstep];
+        scal = a.e.scal[w.slot];
+        if (EPI == EPI_MODDOWN) {
+          add_base = (a.e.base_mask >> (w.poly % a.e.base.E)) & 1u;
+          if (add_base) {
+            const uint32_t* b = a.e.base.at(w.poly, w.slot) + p0;
+#pragma unroll
+            for (int j = 0; j < P1; ++j) pre1[j] = b[j * pstep];
+          }
+        }
       }
       const ModC mc = a.mods[limb];
       bool ok = mbar_wait(&S.tfull[acc], aphase, S, a.err, 4);
@@ -331,11 +354,24 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
         uint32_t res[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
+          const int jj = chunk * 8 + j;
           const uint64_t z = combine4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           uint32_t r = a.fast ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
-          if (TWIDDLE) {
-            const uint64_t zt = (uint64_t)r * twv[chunk * 8 + j];
+          if (EPI == EPI_MUL) {
+            const uint64_t zt = (uint64_t)r * pre0[jj];
             r = a.fast ? reduce_fast(zt, q32, m32, sw) : barrett(zt, mc);
+          } else if (EPI == EPI_COMBINE) {
+            r = barrett((uint64_t)pre0[jj] * scal + r, mc);
+          } else if (EPI == EPI_MODDOWN) {
+            const uint32_t x = pre0[jj];
+            const uint32_t sub = x < r ? x + q32 - r : x - r;
+            const uint32_t t = barrett((uint64_t)sub * scal, mc);
+            if (add_base) {
+              const uint32_t s2 = pre1[jj] + t;
+              r = s2 >= q32 ? s2 - q32 : s2;
+            } else {
+              r = t;
+            }
           }
           res[j] = r;
         }
@@ -435,32 +471,38 @@ int make_tmap_b(CUtensorMap* tm, const uint8_t* base, int kw, int nout, int M) {
   return encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box);
 }
 
-template <bool TW, bool NM>
+template <int EPI, bool NM>
 int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<TW, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)SMEM_BYTES));
-    attr = true;
-  }
+  CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<EPI, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)SMEM_BYTES));
   const int64_t units = (int64_t)a.slots * a.polys * (a.rows_m / BM) * (a.nout / 64);
   const unsigned grid = (unsigned)(units < g_num_sms ? units : g_num_sms);
-  k_bat_tc<TW, NM><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
+  k_bat_tc<EPI, NM><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }
 
 // One contraction stage over polys x slots limb-polynomials.
-int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, bool twiddle, bool nmajor, const uint32_t* tw,
-          const uint32_t* A, int64_t a_ps, int64_t a_ss, int rows_m, int kw, int nout, LPo out, int64_t polys, int slots,
+int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, bool nmajor, const Epi& e, const uint32_t* A,
+          int64_t a_ps, int64_t a_ss, int rows_m, int kw, int nout, LPo out, int64_t polys, int slots,
           const uint16_t* limbs, cudaStream_t st) {
   CUtensorMap tmA;
   int rc = make_tmap_a(&tmA, A, kw, rows_m, slots, polys, a_ss, a_ps);
   if (rc) return rc;
-  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, tw, P->mods, P->tc_err, P->tc_fast};
-  if (twiddle) return nmajor ? launch<true, true>(tmA, tmB, a, st) : launch<true, false>(tmA, tmB, a, st);
-  return nmajor ? launch<false, true>(tmA, tmB, a, st) : launch<false, false>(tmA, tmB, a, st);
+  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->tc_err, P->tc_fast, e};
+  switch (e.op) {
+    case EPI_NONE: return nmajor ? launch<EPI_NONE, true>(tmA, tmB, a, st) : launch<EPI_NONE, false>(tmA, tmB, a, st);
+    case EPI_MUL: return nmajor ? launch<EPI_MUL, true>(tmA, tmB, a, st) : launch<EPI_MUL, false>(tmA, tmB, a, st);
+    case EPI_COMBINE:
+      if (nmajor) break;
+      return launch<EPI_COMBINE, false>(tmA, tmB, a, st);
+    case EPI_MODDOWN:
+      if (nmajor) break;
+      return launch<EPI_MODDOWN, false>(tmA, tmB, a, st);
+  }
+  set_error("tcgen05 stage: unsupported epilogue %d (output major %d)", e.op, (int)nmajor);
+  return CROSS_ERR_UNSUPPORTED;
 }
 
 }  // namespace tc
@@ -543,33 +585,49 @@ void tc_plan_free(cross_ntt_plan_s* P) {
 }
 
 // NTT / INTT on the tensor cores.  tmp holds 2 * polys * slots * N words.
-//   ntt:  transpose -> column stage (x T2, output index major) -> row stage (row major)
-//   intt: row stage (x iT2, output index major) -> column stage (output index major)
-int ntt_run_tc(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
-               const uint16_t* limbs, uint32_t* tmp, cudaStream_t st) {
+//   ntt:  [transpose natural input] -> column stage (x T2, output index major)
+//         -> row stage (row major) with epi
+//   intt: row stage (x iT2, output index major) -> column stage with epi,
+//         output index major (natural coefficients) or row major (transposed)
+int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo out, int out_layout,
+                int64_t polys, int slots, const uint16_t* limbs, const Epi& epi, uint32_t* tmp, cudaStream_t st) {
   const int R = P->r, C = P->c;
   const int64_t N = (int64_t)R * C, lps = polys * slots;
   uint32_t* t1 = tmp;
   uint32_t* t2 = tmp + lps * N;
+  Epi tw;
+  tw.op = EPI_MUL;
+  tw.trow = limbs;
   int rc;
   if (!inverse) {
-    dim3 blk(32, 8), grd(C / 32, R / 32, (unsigned)(lps < 65535 ? lps : 65535));
-    tc::k_transpose_lp<<<grd, blk, 0, st>>>(in, t1, lps, slots, R, C);
-    count_launch();
-    CROSS_CHECK_CUDA(cudaGetLastError());
-    // column stage: A = X^T (C rows x R words), out Y[z][c] = out[n][m]
-    if ((rc = tc::stage(P, P->tm_col_fwd, true, true, P->tw_fwd, t1, slots * N, N, C, R, R,
-                        LPo{t2, slots * N, N}, polys, slots, limbs, st)))
+    const uint32_t* A = in.p;
+    int64_t aps = in.ps, ass = in.ss;
+    if (in_layout == COEF_NATURAL) {
+      dim3 blk(32, 8), grd(C / 32, R / 32, (unsigned)(lps < 65535 ? lps : 65535));
+      tc::k_transpose_lp<<<grd, blk, 0, st>>>(in, t1, lps, slots, R, C);
+      count_launch();
+      CROSS_CHECK_CUDA(cudaGetLastError());
+      A = t1;
+      aps = slots * N;
+      ass = N;
+    }
+    // column stage: A = X^T (C rows x R words), out Y[z][c] = out[n][m], x T2[z][c]
+    tw.tab = P->tw_fwd;
+    if ((rc = tc::stage(P, P->tm_col_fwd, true, tw, A, aps, ass, C, R, R, LPo{t2, slots * N, N}, polys, slots, limbs,
+                        st)))
       return rc;
     // row stage: A = Y (R rows x C words), out Z[z][n] = out[m][n]
-    return tc::stage(P, P->tm_row_fwd, false, false, nullptr, t2, slots * N, N, R, C, C, out, polys, slots, limbs, st);
+    return tc::stage(P, P->tm_row_fwd, false, epi, t2, slots * N, N, R, C, C, out, polys, slots, limbs, st);
   }
-  // row stage: A = X (R rows x C words), out Y^T[l][r] = out[n][m]
-  if ((rc = tc::stage(P, P->tm_row_inv, true, true, P->tc_tw_inv, in.p, in.ps, in.ss, R, C, C, LPo{t1, slots * N, N},
-                      polys, slots, limbs, st)))
+  // row stage: A = X (R rows x C words), out Y^T[l][r] = out[n][m], x iT2[r][l]
+  tw.tab = P->tc_tw_inv;
+  if ((rc = tc::stage(P, P->tm_row_inv, true, tw, in.p, in.ps, in.ss, R, C, C, LPo{t1, slots * N, N}, polys, slots,
+                      limbs, st)))
     return rc;
-  // column stage: A = Y^T (C rows x R words), out Z[l'][c'] = out[n][m]
-  return tc::stage(P, P->tm_col_inv, false, true, nullptr, t1, slots * N, N, C, R, R, out, polys, slots, limbs, st);
+  // column stage: A = Y^T (C rows x R words), out Z[l'][c'] = out[n][m] (natural)
+  // or Z^T[c'][l'] = out[m][n] (transposed)
+  return tc::stage(P, P->tm_col_inv, out_layout == COEF_NATURAL, epi, t1, slots * N, N, C, R, R, out, polys, slots,
+                   limbs, st);
 }
 
 }  // namespace cross
