@@ -41,6 +41,7 @@ struct cross_ntt_plan_s {
   uint32_t* tc_tw_inv = nullptr;    // [M][c][r]    intt_tf_step2 transposed
   int* tc_err = nullptr;            // device error word of the tensor-core kernels
   int tc_fast = 0;                  // 32-bit remainder Barrett is exact for every limb
+  int tc_w32 = 0;                   // every limb has w = 32 and m < 2^32
   CUtensorMap tm_col_fwd, tm_col_inv, tm_row_fwd, tm_row_inv;
 };
 

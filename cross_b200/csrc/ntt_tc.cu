@@ -15,8 +15,8 @@
 //   warp 1      TMEM allocation (512 columns) and the single MMA-issuing thread:
 //               tcgen05.mma.cta_group::1.kind::i8, M=128 N=256 K=32, u8 x u8 -> s32,
 //               accumulating into one of two 256-column TMEM buffers.
-//   warps 2..9  epilogue, two warps per TMEM lane quadrant (each takes half of
-//               the 256 accumulator columns): tcgen05.ld rows, byte
+//   warps 2..17 epilogue, four warps per TMEM lane quadrant (each takes a
+//               quarter of the 256 accumulator columns): tcgen05.ld rows, byte
 //               recombination, Barrett, optional twiddle multiply (twiddles
 //               prefetched before the accumulator is ready) + Barrett, stores;
 //               runs while the MMA fills the other accumulator.
@@ -39,7 +39,7 @@ constexpr int BKB = 128;           // K bytes per pipeline stage (4 MMAs of K = 
 constexpr int STAGES = 4;
 constexpr int A_STAGE = BM * BKB;  // 16 KiB
 constexpr int B_STAGE = BN * BKB;  // 32 KiB
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint64_t WAIT_NS = 2000000000ull;   // bound on any single wait
@@ -67,6 +67,7 @@ struct Args {
   const ModC* mods;
   int* err;
   int fast;                        // every limb qualifies for reduce_fast (see below)
+  int w32;                         // every limb has w = 32 and m < 2^32 (barrett_w32 is exact)
   Epi e;                           // fused position-wise op (EpiOp)
 };
 
@@ -303,20 +304,21 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
       while (!mbar_test(&S.drain, 0) && globaltimer() - t0 < WAIT_NS) __nanosleep(100);
     }
   } else {
-    // ---------------- epilogue (warps 2..9: TMEM lane quadrant warp % 4, column half) ----------------
+    // ---------------- epilogue (warps 2..17: TMEM lane quadrant warp % 4, column quarter) ----------------
     // Output position of (row m, output n): NMAJOR n*rows_m + m, else m*nout + n.
     // The operands of the fused op are read at the same positions, before the
     // accumulator is ready.
-    const int quad = warp & 3, half = (warp - 2) >> 2;
+    constexpr int OUTS = 16;                     // outputs (64 columns) per thread and unit
+    const int quad = warp & 3, part = (warp - 2) >> 2;
     const int64_t N = (int64_t)a.rows_m * a.nout;
-    constexpr int P0 = EPI == EPI_NONE ? 1 : 32;
-    constexpr int P1 = EPI == EPI_MODDOWN ? 32 : 1;
+    constexpr int P0 = EPI == EPI_NONE ? 1 : OUTS;
+    constexpr int P1 = EPI == EPI_MODDOWN ? OUTS : 1;
     uint32_t acc = 0, aphase = 0;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit w = decode(u, n_tiles, m_tiles, a.polys);
       const int limb = a.limbs[w.slot];
       const int m = w.mt * BM + quad * 32 + lane;
-      const int n0 = w.nt * 64 + half * 32;
+      const int n0 = w.nt * 64 + part * OUTS;
       const int64_t p0 = NMAJOR ? (int64_t)n0 * a.rows_m + m : (int64_t)m * a.nout + n0;
       const int64_t pstep = NMAJOR ? a.rows_m : 1;
       uint32_t pre0[P0], pre1[P1];
@@ -325,11 +327,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
       if (EPI == EPI_MUL) {
         const uint32_t* t = a.e.tab + (int64_t)a.e.trow[w.slot] * N + p0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) pre0[j] = __ldg(t + j * pstep);
+        for (int j = 0; j < OUTS; ++j) pre0[j] = __ldg(t + j * pstep);
       } else if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) {
         const uint32_t* x = a.e.x.at(w.poly, w.slot) + p0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) pre0[j] = x[j * pstep];
+        for (int j = 0; j < OUTS; ++j) pre0[j] = x[j * pstep];
         scal = a.e.scal[w.slot];
         if (EPI == EPI_MODDOWN) {
           add_base = (a.e.base_mask >> (w.poly % a.e.base.E)) & 1u;
@@ -348,9 +350,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
       uint32_t* o = a.out + w.poly * a.out_ps + (int64_t)w.slot * a.out_ss;
       const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
 #pragma unroll
-      for (int chunk = 0; chunk < 4; ++chunk) {
+      for (int chunk = 0; chunk < OUTS / 8; ++chunk) {
         uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + half * 128 + chunk * 32, v);
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + part * 64 + chunk * 32, v);
         uint32_t res[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -361,11 +363,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
             const uint64_t zt = (uint64_t)r * pre0[jj];
             r = a.fast ? reduce_fast(zt, q32, m32, sw) : barrett(zt, mc);
           } else if (EPI == EPI_COMBINE) {
-            r = barrett((uint64_t)pre0[jj] * scal + r, mc);
+            const uint64_t zc = (uint64_t)pre0[jj] * scal + r;
+            r = a.w32 ? barrett_w32(zc, q32, m32, sw) : barrett(zc, mc);
           } else if (EPI == EPI_MODDOWN) {
             const uint32_t x = pre0[jj];
             const uint32_t sub = x < r ? x + q32 - r : x - r;
-            const uint32_t t = barrett((uint64_t)sub * scal, mc);
+            const uint64_t zm = (uint64_t)sub * scal;
+            const uint32_t t = a.w32 ? barrett_w32(zm, q32, m32, sw) : barrett(zm, mc);
             if (add_base) {
               const uint32_t s2 = pre1[jj] + t;
               r = s2 >= q32 ? s2 - q32 : s2;
@@ -490,7 +494,7 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, bool nmajor, const 
   CUtensorMap tmA;
   int rc = make_tmap_a(&tmA, A, kw, rows_m, slots, polys, a_ss, a_ps);
   if (rc) return rc;
-  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->tc_err, P->tc_fast, e};
+  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->tc_err, P->tc_fast, P->tc_w32, e};
   switch (e.op) {
     case EPI_NONE: return nmajor ? launch<EPI_NONE, true>(tmA, tmB, a, st) : launch<EPI_NONE, false>(tmA, tmB, a, st);
     case EPI_MUL: return nmajor ? launch<EPI_MUL, true>(tmA, tmB, a, st) : launch<EPI_MUL, false>(tmA, tmB, a, st);
@@ -571,6 +575,9 @@ int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, 
       if (mc.w != 32 || mc.m >= (1ull << 32) || ((z >> s_bits) + 3) * q >= lim) fast = false;
   }
   P->tc_fast = fast ? 1 : 0;
+  bool w32 = true;
+  for (const ModC& mc : P->mods_host) w32 = w32 && mc.w == 32 && mc.m < (1ull << 32);
+  P->tc_w32 = w32 ? 1 : 0;
   P->tc = true;
   return CROSS_OK;
 }
