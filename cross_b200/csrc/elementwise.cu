@@ -105,6 +105,52 @@ __global__ void k_transpose(const uint32_t* __restrict__ in, uint32_t* __restric
   }
 }
 
+// Transpose between the reference layout (P, N, L) (limbs innermost) and the
+// limb-major layout (P, L, N) for a small limb count L.  A block moves TT
+// consecutive positions of one polynomial: TT * L contiguous words on the
+// reference side, L runs of TT contiguous words on the limb-major side; both
+// sides are read and written fully coalesced through a padded shared tile
+// [TT][L + 1].  (t, l) = divmod(k, L) uses a float reciprocal: k < TT * L <=
+// 2^13 and the fractional part of (k + 0.5) / L is at least 0.5 / L, so the
+// floor is exact.
+constexpr int TT = 128;
+constexpr int TT_MAX_L = 64;
+template <bool TO_LM>
+__global__ void __launch_bounds__(256) k_transpose_ref(const uint32_t* __restrict__ in, uint32_t* __restrict__ out,
+                                                      int64_t n, int L, int64_t tiles) {
+  extern __shared__ uint32_t sm[];
+  const int ld = L + 1;
+  const int per = TT * L;
+  const float inv = 1.0f / (float)L;
+  const int64_t tiles_per_poly = n / TT;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int64_t p = tile / tiles_per_poly;
+    const int64_t t0 = (tile % tiles_per_poly) * TT;
+    const uint32_t* ref_in = in + p * n * L + t0 * L;
+    const uint32_t* lm_in = in + p * L * n + t0;
+    if (TO_LM) {
+      for (int k = threadIdx.x; k < per; k += blockDim.x) {
+        const int t = (int)(((float)k + 0.5f) * inv), l = k - t * L;
+        sm[t * ld + l] = ref_in[k];
+      }
+    } else {
+      for (int l = threadIdx.x / TT; l < L; l += blockDim.x / TT) sm[(threadIdx.x % TT) * ld + l] = lm_in[(int64_t)l * n + threadIdx.x % TT];
+    }
+    __syncthreads();
+    if (TO_LM) {
+      uint32_t* o = out + p * L * n + t0;
+      for (int l = threadIdx.x / TT; l < L; l += blockDim.x / TT) o[(int64_t)l * n + threadIdx.x % TT] = sm[(threadIdx.x % TT) * ld + l];
+    } else {
+      uint32_t* o = out + p * n * L + t0 * L;
+      for (int k = threadIdx.x; k < per; k += blockDim.x) {
+        const int t = (int)(((float)k + 0.5f) * inv), l = k - t * L;
+        o[k] = sm[t * ld + l];
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // y = Barrett(x * tab[row]) over strided limb-polynomials, 4 words per thread.
 __global__ void k_modmul_table_lm(LP x, LPo y, int64_t lps, int slots, int64_t n,
                                   const uint32_t* __restrict__ tab, const uint16_t* __restrict__ trow,
@@ -193,6 +239,29 @@ int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows
   if ((rows + 31) / 32 > 65535 || (cols + 31) / 32 > (int64_t)1 << 30) {
     set_error("transpose: %lld x %lld matrix exceeds the launch grid", (long long)rows, (long long)cols);
     return CROSS_ERR_UNSUPPORTED;
+  }
+  // (P, N, L) <-> (P, L, N) with few limbs: the coalesced tile kernel
+  const bool to_lm = cols <= TT_MAX_L && rows % TT == 0, to_ref = rows <= TT_MAX_L && cols % TT == 0;
+  if (to_lm || to_ref) {
+    const int64_t n = to_lm ? rows : cols;
+    const int L = (int)(to_lm ? cols : rows);
+    const int64_t tiles = batch * (n / TT);
+    static int blocks = 0;
+    if (!blocks) {
+      int dev = 0, sms = 0;
+      CROSS_CHECK_CUDA(cudaGetDevice(&dev));
+      CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      blocks = sms * 8;
+    }
+    const unsigned grid = (unsigned)(tiles < blocks ? tiles : blocks);
+    const size_t smem = (size_t)TT * (L + 1) * sizeof(uint32_t);
+    if (to_lm)
+      k_transpose_ref<true><<<grid, 256, smem, st>>>(in, out, n, L, tiles);
+    else
+      k_transpose_ref<false><<<grid, 256, smem, st>>>(in, out, n, L, tiles);
+    count_launch();
+    CROSS_CHECK_CUDA(cudaGetLastError());
+    return CROSS_OK;
   }
   dim3 blk(32, 8);
   for (int64_t b0 = 0; b0 < batch; b0 += 65535) {

@@ -41,8 +41,9 @@ struct cross_ntt_plan_s {
   uint32_t* tc_tw_inv = nullptr;    // [M][c][r]    intt_tf_step2 transposed
   int* tc_err = nullptr;            // device error word of the tensor-core kernels
   int tc_fast = 0;                  // 32-bit remainder Barrett is exact for every limb
-  int tc_w32 = 0;                   // every limb has w = 32 and m < 2^32
-  CUtensorMap tm_col_fwd, tm_col_inv, tm_row_fwd, tm_row_inv;
+  int tc_pair = 0;                  // two-SM kernel (k_bat_tc2) for K extents kw <= 256
+  CUtensorMap tm_col_fwd, tm_col_inv, tm_row_fwd, tm_row_inv;       // boxes of 256 B rows
+  CUtensorMap tm2_col_fwd, tm2_col_inv, tm2_row_fwd, tm2_row_inv;   // boxes of 128 B rows
 };
 
 struct cross_bconv_plan_s {

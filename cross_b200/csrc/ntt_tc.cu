@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <vector>
 
 #include "internal.hpp"
@@ -66,8 +67,6 @@ struct Args {
   int rows_m, kw, nout;
   const ModC* mods;
   int* err;
-  int fast;                        // every limb qualifies for reduce_fast (see below)
-  int w32;                         // every limb has w = 32 and m < 2^32 (barrett_w32 is exact)
   Epi e;                           // fused position-wise op (EpiOp)
 };
 
@@ -103,16 +102,16 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase of `parity` to complete.  Returns false (and
 // raises the CTA abort flag, recording `code`) when the bound expires or
 // another role of the CTA has already aborted.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Smem& S, int* err, int code) {
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int& abort, int* err, int code) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 0;; ++i) {
     if (mbar_test(bar, parity)) return true;
-    if (S.abort) return false;
+    if (abort) return false;
     if (i >= 32) __nanosleep(i < 1024 ? 20 : 200);
     if ((i & 255) == 255 && globaltimer() - t0 > WAIT_NS) {
       atomicCAS(err, 0, code);
-      S.abort = 1;
+      abort = 1;
       return false;
     }
   }
@@ -152,15 +151,34 @@ constexpr uint32_t IDESC = (2u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)
 // Barrett of finite_field.py:224-230 for w = 32 with the remainder taken in
 // 32-bit arithmetic.  The reference forms r = z - t*q in uint64 and then keeps
 // r >= q ? r - q : r truncated to uint32; t = floor(floor(z*m / 2^32) / 2^s_w)
-// is computed exactly here, and whenever the true r lies in (-(2^32 - q), 2^32)
-// the 32-bit remainder and comparison give the same uint32.  The plan enables
-// this path only when z_max / 2^s + 2 < (2^32 - q) / q for every limb and both
-// epilogue inputs (z < 2^53 sums and z < 2^31 * q twiddle products).
+// is computed exactly here (u = zhi*m + floor(zlo*m / 2^32) < 2^64, and only
+// t mod 2^32 enters the 32-bit remainder), and whenever the true r lies in
+// (-(2^32 - q), 2^32) the 32-bit remainder and comparison give the same uint32;
+// min(r, r - q) is that comparison (r - q wraps above r exactly when r < q).
+// The plan enables this path only when z_max / 2^s + 2 < (2^32 - q) / q for
+// every limb and both epilogue inputs (z < 2^53 sums and z < 2^31 * q twiddle
+// products).
+__device__ __forceinline__ uint32_t reduce_fast2(uint32_t zlo, uint32_t zhi, uint32_t q, uint32_t m, uint32_t s_w) {
+  const uint64_t u = (uint64_t)zhi * m + __umulhi(zlo, m);
+  const uint32_t t = __funnelshift_r((uint32_t)u, (uint32_t)(u >> 32), s_w);
+  const uint32_t r = zlo - t * q;
+  return min(r, r - q);
+}
 __device__ __forceinline__ uint32_t reduce_fast(uint64_t z, uint32_t q, uint32_t m, uint32_t s_w) {
-  const uint32_t zlo = (uint32_t)z, zhi = (uint32_t)(z >> 32);
-  const uint64_t t = ((uint64_t)__umulhi(zlo, m) + (uint64_t)zhi * m) >> s_w;
-  const uint32_t r = zlo - (uint32_t)t * q;
-  return r >= q ? r - q : r;
+  return reduce_fast2((uint32_t)z, (uint32_t)(z >> 32), q, m, s_w);
+}
+
+// sum_p acc_p << 8p (ntt_mm.py:33-37) as three 32 x 32 -> 64 multiply-adds.
+__device__ __forceinline__ uint64_t combine4_mad(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {
+  uint64_t z;
+  asm("{\n\t.reg .u64 t0, t1;\n\t"
+      "cvt.u64.u32 t0, %1;\n\t"
+      "mad.wide.u32 t1, %2, 256, t0;\n\t"
+      "mad.wide.u32 t0, %3, 65536, t1;\n\t"
+      "mad.wide.u32 %0, %4, 16777216, t0;\n\t}"
+      : "=l"(z)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3));
+  return z;
 }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
@@ -203,7 +221,113 @@ __device__ __forceinline__ Unit decode(int64_t u, int n_tiles, int m_tiles, int6
   return r;
 }
 
-template <int EPI, bool NMAJOR>
+// Epilogue of one 128 x 256 accumulator tile, run by the 16 epilogue warps
+// (TMEM lane quadrant warp % 4, column quarter (warp - 2) / 4): tcgen05.ld,
+// byte recombination, Barrett, the fused position-wise op, stores.  Output
+// position of (row m, output n): NMAJOR n*rows_m + m, else m*nout + n.  The
+// operands of the fused op are read at the same positions before the
+// accumulator is ready (16 consecutive words per thread when row major: four
+// 16-byte loads).  Returns false when the wait for the accumulator gave up.
+template <int EPI, bool NMAJOR, bool FAST>
+__device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, uint64_t* tfull, uint32_t parity,
+                                              volatile int& abort, const Unit& w, bool store, int warp, int lane) {
+  constexpr int OUTS = 16;                     // outputs (64 columns) per thread and tile
+  const int quad = warp & 3, part = (warp - 2) >> 2;
+  const int64_t N = (int64_t)a.rows_m * a.nout;
+  constexpr int P0 = EPI == EPI_NONE ? 1 : OUTS;
+  constexpr int P1 = EPI == EPI_MODDOWN ? OUTS : 1;
+  const int limb = a.limbs[w.slot];
+  const int m = w.mt * BM + quad * 32 + lane;
+  const int n0 = w.nt * 64 + part * OUTS;
+  const int64_t p0 = NMAJOR ? (int64_t)n0 * a.rows_m + m : (int64_t)m * a.nout + n0;
+  uint32_t pre0[P0], pre1[P1];
+  uint32_t scal = 0;
+  bool add_base = false;
+  if (EPI != EPI_NONE) {
+    const uint32_t* src = EPI == EPI_MUL ? a.e.tab + (int64_t)a.e.trow[w.slot] * N + p0 : a.e.x.at(w.poly, w.slot) + p0;
+    if (NMAJOR) {
+#pragma unroll
+      for (int j = 0; j < OUTS; ++j) pre0[j] = __ldg(src + (int64_t)j * a.rows_m);
+    } else {
+#pragma unroll
+      for (int j = 0; j < OUTS / 4; ++j) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + j);
+        pre0[4 * j] = v.x;
+        pre0[4 * j + 1] = v.y;
+        pre0[4 * j + 2] = v.z;
+        pre0[4 * j + 3] = v.w;
+      }
+    }
+  }
+  if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) scal = a.e.scal[w.slot];
+  if (EPI == EPI_MODDOWN) {
+    add_base = (a.e.base_mask >> (w.poly % a.e.base.E)) & 1u;
+    if (add_base) {
+      const uint4* b = reinterpret_cast<const uint4*>(a.e.base.at(w.poly, w.slot) + p0);
+#pragma unroll
+      for (int j = 0; j < OUTS / 4; ++j) {
+        const uint4 v = __ldg(b + j);
+        pre1[4 * j] = v.x;
+        pre1[4 * j + 1] = v.y;
+        pre1[4 * j + 2] = v.z;
+        pre1[4 * j + 3] = v.w;
+      }
+    }
+  }
+  const ModC mc = a.mods[limb];
+  bool ok = mbar_wait(tfull, parity, abort, a.err, 4);
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) return false;
+  tc_fence_after();
+  uint32_t* o = a.out + w.poly * a.out_ps + (int64_t)w.slot * a.out_ss + p0;
+  const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
+#pragma unroll
+  for (int chunk = 0; chunk < OUTS / 8; ++chunk) {
+    uint32_t v[32];
+    tmem_ld32(tmem_acc + ((uint32_t)(quad * 32) << 16) + part * 64 + chunk * 32, v);
+    uint32_t res[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int jj = chunk * 8 + j;
+      const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      uint32_t r = FAST ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
+      if (EPI == EPI_MUL) {
+        if (FAST)
+          r = reduce_fast2(r * pre0[jj], __umulhi(r, pre0[jj]), q32, m32, sw);
+        else
+          r = barrett((uint64_t)r * pre0[jj], mc);
+      } else if (EPI == EPI_COMBINE) {
+        const uint64_t zc = (uint64_t)pre0[jj] * scal + r;
+        r = FAST ? barrett_w32(zc, q32, m32, sw) : barrett(zc, mc);
+      } else if (EPI == EPI_MODDOWN) {
+        const uint32_t x = pre0[jj];
+        const uint32_t sub = x < r ? x + q32 - r : x - r;
+        const uint64_t zm = (uint64_t)sub * scal;
+        const uint32_t t = FAST ? barrett_w32(zm, q32, m32, sw) : barrett(zm, mc);
+        if (add_base) {
+          const uint32_t s2 = pre1[jj] + t;
+          r = s2 >= q32 ? s2 - q32 : s2;
+        } else {
+          r = t;
+        }
+      }
+      res[j] = r;
+    }
+    if (store) {
+      if (NMAJOR) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[(int64_t)(chunk * 8 + j) * a.rows_m] = res[j];
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(o + chunk * 8);
+        dst[0] = make_uint4(res[0], res[1], res[2], res[3]);
+        dst[1] = make_uint4(res[4], res[5], res[6], res[7]);
+      }
+    }
+  }
+  return true;
+}
+
+template <int EPI, bool NMAJOR, bool FAST>
 __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ CUtensorMap tmA,
                                                        const __grid_constant__ CUtensorMap tmB, const Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -247,7 +371,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
         const Unit w = decode(u, n_tiles, m_tiles, a.polys);
         const int limb = a.limbs[w.slot];
         for (int ks = 0; ks < kst; ++ks) {
-          if (!mbar_wait(&S.empty[stage], phase ^ 1, S, a.err, 1)) break;
+          if (!mbar_wait(&S.empty[stage], phase ^ 1, S.abort, a.err, 1)) break;
           mbar_expect_tx(&S.full[stage], A_STAGE + B_STAGE);
           tma_load_4d(S.a[stage], &tmA, &S.full[stage], ks * 32, w.mt * BM, w.slot, (int)w.poly);
           tma_load_2d(S.b[stage], &tmB, &S.full[stage], ks * BKB, limb * 4 * a.nout + w.nt * BN);
@@ -273,12 +397,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
       // ---------------- MMA issuer ----------------
       uint32_t stage = 0, phase = 0, acc = 0, aphase = 0;
       for (int64_t u = blockIdx.x; u < units && !S.abort; u += gridDim.x) {
-        if (!mbar_wait(&S.tempty[acc], aphase ^ 1, S, a.err, 2)) break;
+        if (!mbar_wait(&S.tempty[acc], aphase ^ 1, S.abort, a.err, 2)) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         bool ok = true;
         for (int ks = 0; ks < kst; ++ks) {
-          if (!mbar_wait(&S.full[stage], phase, S, a.err, 3)) {
+          if (!mbar_wait(&S.full[stage], phase, S.abort, a.err, 3)) {
             ok = false;
             break;
           }
@@ -304,90 +428,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
       while (!mbar_test(&S.drain, 0) && globaltimer() - t0 < WAIT_NS) __nanosleep(100);
     }
   } else {
-    // ---------------- epilogue (warps 2..17: TMEM lane quadrant warp % 4, column quarter) ----------------
-    // Output position of (row m, output n): NMAJOR n*rows_m + m, else m*nout + n.
-    // The operands of the fused op are read at the same positions, before the
-    // accumulator is ready.
-    constexpr int OUTS = 16;                     // outputs (64 columns) per thread and unit
-    const int quad = warp & 3, part = (warp - 2) >> 2;
-    const int64_t N = (int64_t)a.rows_m * a.nout;
-    constexpr int P0 = EPI == EPI_NONE ? 1 : OUTS;
-    constexpr int P1 = EPI == EPI_MODDOWN ? OUTS : 1;
+    // ---------------- epilogue (warps 2..17) ----------------
     uint32_t acc = 0, aphase = 0;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit w = decode(u, n_tiles, m_tiles, a.polys);
-      const int limb = a.limbs[w.slot];
-      const int m = w.mt * BM + quad * 32 + lane;
-      const int n0 = w.nt * 64 + part * OUTS;
-      const int64_t p0 = NMAJOR ? (int64_t)n0 * a.rows_m + m : (int64_t)m * a.nout + n0;
-      const int64_t pstep = NMAJOR ? a.rows_m : 1;
-      uint32_t pre0[P0], pre1[P1];
-      uint64_t scal = 0;
-      bool add_base = false;
-      if (EPI == EPI_MUL) {
-        const uint32_t* t = a.e.tab + (int64_t)a.e.trow[w.slot] * N + p0;
-#pragma unroll
-        for (int j = 0; j < OUTS; ++j) pre0[j] = __ldg(t + j * pstep);
-      } else if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) {
-        const uint32_t* x = a.e.x.at(w.poly, w.slot) + p0;
-#pragma unroll
-        for (int j = 0; j < OUTS; ++j) pre0[j] = x[j * pstep];
-        scal = a.e.scal[w.slot];
-        if (EPI == EPI_MODDOWN) {
-          add_base = (a.e.base_mask >> (w.poly % a.e.base.E)) & 1u;
-          if (add_base) {
-            const uint32_t* b = a.e.base.at(w.poly, w.slot) + p0;
-#pragma unroll
-            for (int j = 0; j < P1; ++j) pre1[j] = b[j * pstep];
-          }
-        }
-      }
-      const ModC mc = a.mods[limb];
-      bool ok = mbar_wait(&S.tfull[acc], aphase, S, a.err, 4);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t* o = a.out + w.poly * a.out_ps + (int64_t)w.slot * a.out_ss;
-      const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
-#pragma unroll
-      for (int chunk = 0; chunk < OUTS / 8; ++chunk) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + part * 64 + chunk * 32, v);
-        uint32_t res[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int jj = chunk * 8 + j;
-          const uint64_t z = combine4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          uint32_t r = a.fast ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
-          if (EPI == EPI_MUL) {
-            const uint64_t zt = (uint64_t)r * pre0[jj];
-            r = a.fast ? reduce_fast(zt, q32, m32, sw) : barrett(zt, mc);
-          } else if (EPI == EPI_COMBINE) {
-            const uint64_t zc = (uint64_t)pre0[jj] * scal + r;
-            r = a.w32 ? barrett_w32(zc, q32, m32, sw) : barrett(zc, mc);
-          } else if (EPI == EPI_MODDOWN) {
-            const uint32_t x = pre0[jj];
-            const uint32_t sub = x < r ? x + q32 - r : x - r;
-            const uint64_t zm = (uint64_t)sub * scal;
-            const uint32_t t = a.w32 ? barrett_w32(zm, q32, m32, sw) : barrett(zm, mc);
-            if (add_base) {
-              const uint32_t s2 = pre1[jj] + t;
-              r = s2 >= q32 ? s2 - q32 : s2;
-            } else {
-              r = t;
-            }
-          }
-          res[j] = r;
-        }
-        if (NMAJOR) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) o[(size_t)(n0 + chunk * 8 + j) * a.rows_m + m] = res[j];
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(o + (size_t)m * a.nout + n0 + chunk * 8);
-          dst[0] = make_uint4(res[0], res[1], res[2], res[3]);
-          dst[1] = make_uint4(res[4], res[5], res[6], res[7]);
-        }
-      }
+      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, true, warp, lane))
+        break;
       tc_fence_before();
       mbar_arrive(&S.tempty[acc]);
       acc ^= 1;
@@ -399,6 +445,274 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
   tc_fence_after();
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Two-SM variant: a cluster of two CTAs issues tcgen05.mma.cta_group::2 with
+// M = 256 (128 rows from each CTA's shared memory), N = 256.  Each CTA keeps
+// its half of the B tile (128 rows x 4*kw bytes, kw <= 256) resident in shared
+// memory for as long as the pair stays on one (limb, n tile) and streams only
+// A, so a CTA reads 16 KiB from L2 per 512 tensor cycles instead of 48 KiB.
+// Pairs form groups of n_tiles; the pairs of a group walk the same sequence of
+// (slot, row-block pair) items, one n tile each, so the A tiles they share are
+// read from L2 at about the same time.
+//
+// Roles per CTA as in k_bat_tc; only the leader (cluster rank 0) issues MMAs.
+// Barriers: full[s] and bfull live in the leader and count the copies of both
+// CTAs (TMA with .cta_group::2 signals the leader's barrier); empty[s],
+// tfull[acc] and bempty live in both CTAs and are signalled by a multicast
+// tcgen05.commit; tempty[acc] lives in the leader and counts one arrival per
+// epilogue warp of both CTAs.  Every wait is bounded as in k_bat_tc; a
+// cluster barrier keeps both CTAs alive until neither can signal the other.
+constexpr int B2_ROWS = BN / 2;                  // B rows held per CTA
+constexpr int B2_CHUNK = B2_ROWS * BKB;          // 16 KiB per 128-byte K chunk
+constexpr int B2_CHUNKS = 8;                     // kw <= 256
+constexpr uint32_t IDESC2 = (2u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+
+struct Smem2 {
+  uint8_t a[STAGES][A_STAGE];
+  uint8_t b[B2_CHUNKS][B2_CHUNK];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t bfull, bempty, drain;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+constexpr size_t SMEM2_BYTES = sizeof(Smem2) + 1024;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* tm, uint32_t bar_cl, int c0, int c1,
+                                                 int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6}], [%2];" ::"r"(saddr(dst)),
+      "l"((uint64_t)tm), "r"(bar_cl), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, uint32_t bar_cl, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(saddr(dst)),
+      "l"((uint64_t)tm), "r"(bar_cl), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC2), "r"(accumulate), "r"(z));
+}
+// arrive on the barrier at this offset in both CTAs of the pair once the MMAs
+// issued so far have completed
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+  const uint16_t mask = 3;
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   saddr(bar)),
+               "h"(mask)
+               : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+               : "memory");
+}
+
+// Work of a pair: group g = pair / n_tiles over items [t0, t1) of the
+// (slot, j) sequence (j = row-block pair, ipc per slot), n tile pair % n_tiles.
+struct PairWork {
+  int64_t t0, t1, ipc, rbs;
+  int nt;
+};
+__device__ __forceinline__ PairWork pair_work(const Args& a, int m_tiles, int n_tiles) {
+  PairWork pw;
+  const int64_t pair = blockIdx.x >> 1, groups = (gridDim.x >> 1) / n_tiles;
+  const int64_t g = pair / n_tiles;
+  pw.nt = (int)(pair % n_tiles);
+  pw.rbs = a.polys * m_tiles;
+  pw.ipc = (pw.rbs + 1) / 2;
+  const int64_t total = (int64_t)a.slots * pw.ipc;
+  pw.t0 = total * g / groups;
+  pw.t1 = total * (g + 1) / groups;
+  return pw;
+}
+// Row block of this CTA in item t (the peer of an odd last pair repeats the
+// leader's row block and stores nothing).
+__device__ __forceinline__ Unit pair_unit(int64_t t, const PairWork& pw, uint32_t rank, int m_tiles, bool& valid) {
+  Unit w;
+  w.slot = (int)(t / pw.ipc);
+  const int64_t j = t % pw.ipc;
+  int64_t rb = 2 * j + rank;
+  valid = rb < pw.rbs;
+  if (!valid) rb = 2 * j;
+  w.poly = rb / m_tiles;
+  w.mt = (int)(rb % m_tiles);
+  w.nt = pw.nt;
+  return w;
+}
+
+template <int EPI, bool NMAJOR, bool FAST>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    k_bat_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem2& S = *reinterpret_cast<Smem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int m_tiles = a.rows_m / BM, n_tiles = a.nout / 64, kst = a.kw / 32;
+  const PairWork pw = pair_work(a, m_tiles, n_tiles);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.tfull[i], 1);
+      mbar_init(&S.tempty[i], 2 * EPI_WARPS);
+    }
+    mbar_init(&S.bfull, 1);
+    mbar_init(&S.bempty, 1);
+    mbar_init(&S.drain, 1);
+    S.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&S.tmem_base)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      uint32_t stage = 0, phase = 0, bphase = 0;
+      int prev_slot = -1;
+      int issued = 0;
+      for (int64_t t = pw.t0; t < pw.t1 && !S.abort; ++t) {
+        bool valid;
+        const Unit w = pair_unit(t, pw, rank, m_tiles, valid);
+        if (w.slot != prev_slot) {
+          // the MMAs that read the resident B half have completed
+          if (!mbar_wait(&S.bempty, bphase ^ 1, S.abort, a.err, 11)) break;
+          bphase ^= 1;
+          const int limb = a.limbs[w.slot];
+          if (rank == 0) mbar_expect_tx(&S.bfull, 2 * kst * B2_CHUNK);
+          const uint32_t bar = mapa(&S.bfull, 0);
+          for (int kc = 0; kc < kst; ++kc)
+            tma_load_2d_pair(S.b[kc], &tmB, bar, kc * BKB, limb * 4 * a.nout + w.nt * BN + (int)rank * B2_ROWS);
+          prev_slot = w.slot;
+        }
+        for (int kc = 0; kc < kst; ++kc) {
+          if (!mbar_wait(&S.empty[stage], phase ^ 1, S.abort, a.err, 12)) break;
+          if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * A_STAGE);
+          tma_load_4d_pair(S.a[stage], &tmA, mapa(&S.full[stage], 0), kc * 32, w.mt * BM, w.slot, (int)w.poly);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (S.abort && rank == 0) {
+        // let the copies already issued land before the CTA exits
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          stage = stage == 0 ? STAGES - 1 : stage - 1;
+          if (stage == STAGES - 1) phase ^= 1;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_test(&S.full[stage], phase) && globaltimer() - t0 < WAIT_NS) __nanosleep(200);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader) ----------------
+      uint32_t stage = 0, phase = 0, acc = 0, aphase = 0, bphase = 0;
+      int prev_slot = -1;
+      for (int64_t t = pw.t0; t < pw.t1 && !S.abort; ++t) {
+        const int slot = (int)(t / pw.ipc);
+        if (!mbar_wait(&S.tempty[acc], aphase ^ 1, S.abort, a.err, 13)) break;
+        if (slot != prev_slot) {
+          if (!mbar_wait(&S.bfull, bphase, S.abort, a.err, 14)) break;
+          bphase ^= 1;
+          prev_slot = slot;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        bool ok = true;
+        for (int kc = 0; kc < kst; ++kc) {
+          if (!mbar_wait(&S.full[stage], phase, S.abort, a.err, 15)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t as = saddr(S.a[stage]), bs = saddr(S.b[kc]);
+#pragma unroll
+          for (int k = 0; k < BKB / 32; ++k)
+            mma_i8_pair(d, sw128_desc(as + 32 * k), sw128_desc(bs + 32 * k), (kc | k) != 0);
+          mma_commit_pair_both(&S.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair_both(&S.tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1;
+        if (t + 1 == pw.t1 || (int)((t + 1) / pw.ipc) != slot) mma_commit_pair_both(&S.bempty);
+      }
+      // every MMA issued by this thread has completed once `drain` flips
+      mma_commit_pair_local(&S.drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_test(&S.drain, 0) && globaltimer() - t0 < WAIT_NS) __nanosleep(100);
+    }
+  } else {
+    // ---------------- epilogue (both CTAs, warps 2..17) ----------------
+    uint32_t acc = 0, aphase = 0;
+    for (int64_t t = pw.t0; t < pw.t1; ++t) {
+      bool valid;
+      const Unit w = pair_unit(t, pw, rank, m_tiles, valid);
+      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, valid, warp, lane))
+        break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa(&S.tempty[acc], 0));
+      acc ^= 1;
+      if (acc == 0) aphase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
 }
 
 // Strided batched transpose of limb-polynomials: out[lp][c][r] = in[lp][r][c].
@@ -467,44 +781,100 @@ int make_tmap_a(CUtensorMap* tm, const uint32_t* base, int kw, int rows, int slo
   return encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, base, dims, strides, box);
 }
 
-// Tensor map of a plan's B matrices: (4*kw bytes, M*4*nout rows).
-int make_tmap_b(CUtensorMap* tm, const uint8_t* base, int kw, int nout, int M) {
+// Tensor map of a plan's B matrices: (4*kw bytes, M*4*nout rows), boxes of
+// `rows` rows (BN for k_bat_tc, BN / 2 for one CTA of k_bat_tc2).
+int make_tmap_b(CUtensorMap* tm, const uint8_t* base, int kw, int nout, int M, int rows) {
   cuuint64_t dims[2] = {(cuuint64_t)4 * kw, (cuuint64_t)M * 4 * nout};
   cuuint64_t strides[1] = {(cuuint64_t)4 * kw};
-  cuuint32_t box[2] = {(cuuint32_t)BKB, (cuuint32_t)BN};
+  cuuint32_t box[2] = {(cuuint32_t)BKB, (cuuint32_t)rows};
   return encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box);
 }
 
-template <int EPI, bool NM>
+template <int EPI, bool NM, bool FAST>
 int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
-  CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<EPI, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<EPI, NM, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)SMEM_BYTES));
   const int64_t units = (int64_t)a.slots * a.polys * (a.rows_m / BM) * (a.nout / 64);
   const unsigned grid = (unsigned)(units < g_num_sms ? units : g_num_sms);
-  k_bat_tc<EPI, NM><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
+  k_bat_tc<EPI, NM, FAST><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }
 
-// One contraction stage over polys x slots limb-polynomials.
-int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, bool nmajor, const Epi& e, const uint32_t* A,
+int g_max_pairs = 0;
+
+template <int EPI, bool NM, bool FAST>
+int launch2(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
+  auto kern = k_bat_tc2<EPI, NM, FAST>;
+  CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES));
+  if (!g_max_pairs) {
+    // clusters of two 197 KiB CTAs that fit at once (compile-time cluster dims)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(g_num_sms & ~1));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &cfg) != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = g_num_sms / 2;
+    }
+    g_max_pairs = n;
+  }
+  const int m_tiles = a.rows_m / BM, n_tiles = a.nout / 64;
+  const int64_t rbs = a.polys * m_tiles, total = (int64_t)a.slots * ((rbs + 1) / 2);
+  if (total == 0) return CROSS_OK;
+  int64_t groups = g_max_pairs / n_tiles;
+  if (groups < 1) groups = 1;
+  if (groups > total) groups = total;
+  kern<<<(unsigned)(2 * groups * n_tiles), THREADS, SMEM2_BYTES, st>>>(tmA, tmB, a);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+// One contraction stage over polys x slots limb-polynomials.  tmB2 is the
+// half-height map of the same B matrices (used by k_bat_tc2 when kw <= 256).
+int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& tmB2, bool nmajor, const Epi& e,
+          const uint32_t* A,
           int64_t a_ps, int64_t a_ss, int rows_m, int kw, int nout, LPo out, int64_t polys, int slots,
           const uint16_t* limbs, cudaStream_t st) {
   CUtensorMap tmA;
   int rc = make_tmap_a(&tmA, A, kw, rows_m, slots, polys, a_ss, a_ps);
   if (rc) return rc;
-  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->tc_err, P->tc_fast, P->tc_w32, e};
+  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->tc_err, e};
+  if (!nmajor && e.op != EPI_NONE) {
+    // row-major operands are read with 16-byte loads
+    const View& x = e.op == EPI_MUL ? View{e.tab, 0, 0, 0, 1} : e.x;
+    bool al = ((uintptr_t)x.p & 15) == 0 && x.ps % 4 == 0 && x.es % 4 == 0 && x.ss % 4 == 0;
+    if (e.op == EPI_MUL) al = al && ((int64_t)rows_m * nout) % 4 == 0;
+    if (e.op == EPI_MODDOWN && e.base_mask)
+      al = al && ((uintptr_t)e.base.p & 15) == 0 && e.base.ps % 4 == 0 && e.base.es % 4 == 0 && e.base.ss % 4 == 0;
+    if (!al) {
+      set_error("tcgen05 stage: epilogue operands must be 16-byte aligned");
+      return CROSS_ERR_UNSUPPORTED;
+    }
+  }
+  const bool f = P->tc_fast != 0;
+  const bool pair = P->tc_pair && kw <= 32 * B2_CHUNKS;
+#define CROSS_TC_LAUNCH(OP, NM)                                                                      \
+  return pair ? (f ? launch2<OP, NM, true>(tmA, tmB2, a, st) : launch2<OP, NM, false>(tmA, tmB2, a, st)) \
+              : (f ? launch<OP, NM, true>(tmA, tmB, a, st) : launch<OP, NM, false>(tmA, tmB, a, st))
   switch (e.op) {
-    case EPI_NONE: return nmajor ? launch<EPI_NONE, true>(tmA, tmB, a, st) : launch<EPI_NONE, false>(tmA, tmB, a, st);
-    case EPI_MUL: return nmajor ? launch<EPI_MUL, true>(tmA, tmB, a, st) : launch<EPI_MUL, false>(tmA, tmB, a, st);
+    case EPI_NONE:
+      if (nmajor) CROSS_TC_LAUNCH(EPI_NONE, true);
+      CROSS_TC_LAUNCH(EPI_NONE, false);
+    case EPI_MUL:
+      if (nmajor) CROSS_TC_LAUNCH(EPI_MUL, true);
+      CROSS_TC_LAUNCH(EPI_MUL, false);
     case EPI_COMBINE:
       if (nmajor) break;
-      return launch<EPI_COMBINE, false>(tmA, tmB, a, st);
+      CROSS_TC_LAUNCH(EPI_COMBINE, false);
     case EPI_MODDOWN:
       if (nmajor) break;
-      return launch<EPI_MODDOWN, false>(tmA, tmB, a, st);
+      CROSS_TC_LAUNCH(EPI_MODDOWN, false);
   }
+#undef CROSS_TC_LAUNCH
   set_error("tcgen05 stage: unsupported epilogue %d (output major %d)", e.op, (int)nmajor);
   return CROSS_ERR_UNSUPPORTED;
 }
@@ -557,10 +927,16 @@ int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, 
   if ((rc = upload_vec(&P->tc_tw_inv, tw))) return rc;
   std::vector<int> zero(1, 0);
   if ((rc = upload(&P->tc_err, zero.data(), 1))) return rc;
-  if ((rc = tc::make_tmap_b(&P->tm_col_fwd, P->tc_col_fwd, R, R, M))) return rc;
-  if ((rc = tc::make_tmap_b(&P->tm_col_inv, P->tc_col_inv, R, R, M))) return rc;
-  if ((rc = tc::make_tmap_b(&P->tm_row_fwd, P->tc_row_fwd, C, C, M))) return rc;
-  if ((rc = tc::make_tmap_b(&P->tm_row_inv, P->tc_row_inv, C, C, M))) return rc;
+  for (int h = 0; h < 2; ++h) {
+    const int rows = h ? tc::BN / 2 : tc::BN;
+    if ((rc = tc::make_tmap_b(h ? &P->tm2_col_fwd : &P->tm_col_fwd, P->tc_col_fwd, R, R, M, rows))) return rc;
+    if ((rc = tc::make_tmap_b(h ? &P->tm2_col_inv : &P->tm_col_inv, P->tc_col_inv, R, R, M, rows))) return rc;
+    if ((rc = tc::make_tmap_b(h ? &P->tm2_row_fwd : &P->tm_row_fwd, P->tc_row_fwd, C, C, M, rows))) return rc;
+    if ((rc = tc::make_tmap_b(h ? &P->tm2_row_inv : &P->tm_row_inv, P->tc_row_inv, C, C, M, rows))) return rc;
+  }
+  // two-SM kernel unless CROSS_B200_TC_1SM=1 (kept for comparison runs)
+  const char* one = getenv("CROSS_B200_TC_1SM");
+  P->tc_pair = !(one && one[0] == '1');
   // reduce_fast is exact when the true remainder stays in (-(2^32 - q), 2^32):
   // with t = floor(z m / 2^s) and m within one of 2^s / q, |r| < (z / 2^s + 2) q.
   // Epilogue inputs: contraction sums z < 2^53 (kw <= 1024), twiddle products
@@ -572,12 +948,11 @@ int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, 
     const unsigned __int128 z1 = (unsigned __int128)1 << 53, z2 = ((unsigned __int128)1 << 31) * q;
     const unsigned __int128 lim = ((unsigned __int128)1 << 32) - q;
     for (unsigned __int128 z : {z1, z2})
-      if (mc.w != 32 || mc.m >= (1ull << 32) || ((z >> s_bits) + 3) * q >= lim) fast = false;
+      if (mc.w != 32 || mc.s_w >= 32 || mc.m >= (1ull << 32) || ((z >> s_bits) + 3) * q >= lim) fast = false;
   }
+  // FAST also selects barrett_w32 (exact for w = 32, m < 2^32) in the
+  // combine / ModDown epilogues.
   P->tc_fast = fast ? 1 : 0;
-  bool w32 = true;
-  for (const ModC& mc : P->mods_host) w32 = w32 && mc.w == 32 && mc.m < (1ull << 32);
-  P->tc_w32 = w32 ? 1 : 0;
   P->tc = true;
   return CROSS_OK;
 }
@@ -620,20 +995,20 @@ int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, L
     }
     // column stage: A = X^T (C rows x R words), out Y[z][c] = out[n][m], x T2[z][c]
     tw.tab = P->tw_fwd;
-    if ((rc = tc::stage(P, P->tm_col_fwd, true, tw, A, aps, ass, C, R, R, LPo{t2, slots * N, N}, polys, slots, limbs,
+    if ((rc = tc::stage(P, P->tm_col_fwd, P->tm2_col_fwd, true, tw, A, aps, ass, C, R, R, LPo{t2, slots * N, N}, polys, slots, limbs,
                         st)))
       return rc;
     // row stage: A = Y (R rows x C words), out Z[z][n] = out[m][n]
-    return tc::stage(P, P->tm_row_fwd, false, epi, t2, slots * N, N, R, C, C, out, polys, slots, limbs, st);
+    return tc::stage(P, P->tm_row_fwd, P->tm2_row_fwd, false, epi, t2, slots * N, N, R, C, C, out, polys, slots, limbs, st);
   }
   // row stage: A = X (R rows x C words), out Y^T[l][r] = out[n][m], x iT2[r][l]
   tw.tab = P->tc_tw_inv;
-  if ((rc = tc::stage(P, P->tm_row_inv, true, tw, in.p, in.ps, in.ss, R, C, C, LPo{t1, slots * N, N}, polys, slots,
+  if ((rc = tc::stage(P, P->tm_row_inv, P->tm2_row_inv, true, tw, in.p, in.ps, in.ss, R, C, C, LPo{t1, slots * N, N}, polys, slots,
                       limbs, st)))
     return rc;
   // column stage: A = Y^T (C rows x R words), out Z[l'][c'] = out[n][m] (natural)
   // or Z^T[c'][l'] = out[m][n] (transposed)
-  return tc::stage(P, P->tm_col_inv, out_layout == COEF_NATURAL, epi, t1, slots * N, N, C, R, R, out, polys, slots,
+  return tc::stage(P, P->tm_col_inv, P->tm2_col_inv, out_layout == COEF_NATURAL, epi, t1, slots * N, N, C, R, R, out, polys, slots,
                    limbs, st);
 }
 

@@ -34,7 +34,8 @@ def test_ntt_golden():
 
 
 @pytest.mark.parametrize("n,r,c,limbs,batch", [(4096, 64, 64, 8, 16), (4096, 32, 128, 3, 2), (1024, 32, 32, 5, 3),
-                                               (65536, 256, 256, 4, 2), (65536, 128, 512, 2, 1)])
+                                               (65536, 256, 256, 4, 2), (65536, 128, 512, 2, 1),
+                                               (16384, 128, 128, 3, 3), (32768, 128, 256, 2, 1)])
 def test_ntt_intt_vs_oracle(n, r, c, limbs, batch):
     from cross_b200 import ntt_mm
     q = O.find_moduli_ntt(limbs, 28, 2 * n)
@@ -62,6 +63,28 @@ def test_tensor_core_path_matches_cuda_core_path(monkeypatch):
     cc = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 256, "c": 256})
     np.testing.assert_array_equal(y_tc, _np(cc.ntt(x)))
     np.testing.assert_array_equal(z_tc, _np(cc.intt(y_tc)))
+
+
+@pytest.mark.parametrize("r,c,L,B", [(256, 256, 5, 5), (128, 128, 3, 5), (128, 256, 4, 3), (512, 128, 2, 3)])
+def test_two_sm_kernel_matches_one_sm_kernel(monkeypatch, r, c, L, B):
+    """The cta_group::2 contraction (B half resident per CTA, K extent <= 256
+    words) and the one-SM contraction give identical NTT / INTT outputs, for
+    even and odd numbers of 128-row blocks (odd: the last pair's second CTA
+    repeats the first CTA's rows and stores nothing)."""
+    from cross_b200 import ntt_mm
+    n = r * c
+    q = O.find_moduli_ntt(L, 28, 2 * n)
+    x = rng_residues(np.random.default_rng(r + c + L), (B, r, c, L), q)
+    two = ntt_mm.NTTCiphertextBarrettContext(q, {"r": r, "c": c})
+    y2 = _np(two.ntt(x))
+    z2 = _np(two.intt(y2))
+    two.check_device()
+    monkeypatch.setenv("CROSS_B200_TC_1SM", "1")
+    one = ntt_mm.NTTCiphertextBarrettContext(q, {"r": r, "c": c})
+    np.testing.assert_array_equal(y2, _np(one.ntt(x)))
+    np.testing.assert_array_equal(z2, _np(one.intt(y2)))
+    one.check_device()
+    assert not ((z2.astype(np.int64) - x) % np.array(q, np.int64)).any()
 
 
 def test_ntt_round_trip_and_linearity_full_size():
@@ -321,6 +344,26 @@ def test_limb_major_layout_matches_reference_layout():
     lm_in = torch.from_numpy(np.ascontiguousarray(ct.reshape(B, 4, n, L).transpose(0, 1, 3, 2))).cuda()
     lm = _np(he.mul(lm_in, layout=LAYOUT_LIMB_MAJOR))
     np.testing.assert_array_equal(lm.transpose(0, 1, 3, 2).reshape(ref_layout.shape), ref_layout)
+
+
+@pytest.mark.parametrize("polys,n,L", [(3, 128, 1), (2, 4096, 24), (5, 1024, 7), (1, 256, 64),
+                                        (2, 256, 65), (3, 96, 5), (2, 65536, 24)])
+def test_layout_conversions(polys, n, L):
+    """cross_to_limb_major / cross_to_reference are exact permutations (coalesced
+    tile kernel for L <= 64 and n % 128 == 0, generic tile transpose otherwise)."""
+    import torch
+    from cross_b200 import _lib
+    rng = np.random.default_rng(n + L)
+    x = rng.integers(0, 2 ** 32, size=(polys, n, L), dtype=np.uint64).astype(U32)
+    xd = torch.from_numpy(x).cuda()
+    lm = torch.empty((polys, L, n), dtype=xd.dtype, device="cuda")
+    back = torch.empty_like(xd)
+    lib = _lib.lib()
+    _lib.check(lib.cross_to_limb_major(xd.data_ptr(), lm.data_ptr(), polys, n, L, None), "cross_to_limb_major")
+    _lib.check(lib.cross_to_reference(lm.data_ptr(), back.data_ptr(), polys, n, L, None), "cross_to_reference")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(lm.cpu().numpy(), x.transpose(0, 2, 1))
+    np.testing.assert_array_equal(back.cpu().numpy(), x)
 
 
 def test_errors_are_reference_exceptions():
