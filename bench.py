@@ -251,17 +251,19 @@ def main():
         ems = float(t.item())
     e2e = world * batch * args.steps / (ems / 1000.0)
 
-    # Dominant kernel: the BAT NTT (column + row contraction kernels) over the
-    # 4 x 64 x 23 limb-polynomials of the rescale NTT, timed alone.
+    # Dominant kernel: the tensor-core BAT contraction.  One forward NTT in the
+    # kernels' native coefficient order is exactly two contraction launches (the
+    # column stage with its twiddle epilogue, the row stage); timed alone over
+    # the 4 x 64 x 23 limb-polynomials of the rescale NTT.
     ctx = ntt_mm.NTTCiphertextBarrettContext(Q[:L - 1], {"r": R, "c": C})
     lps = batch * 4
     xin = x.reshape(-1)[: lps * (L - 1) * N_DEG].reshape(lps, L - 1, R, C)   # residues < q
     xo = torch.empty_like(xin)
-    nws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), lps, _lib.LAYOUT_LIMB_MAJOR), dtype=torch.uint8,
-                      device=dev)
+    nws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), lps, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED),
+                      dtype=torch.uint8, device=dev)
 
     def ntt_once():
-        _lib.check(lib.cross_ntt(ctx.plan(), 0, xin.data_ptr(), xo.data_ptr(), lps, _lib.LAYOUT_LIMB_MAJOR,
+        _lib.check(lib.cross_ntt(ctx.plan(), 0, xin.data_ptr(), xo.data_ptr(), lps, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED,
                                  nws.data_ptr(), nws.numel(), stream.cuda_stream), "cross_ntt")
 
     for _ in range(2):
@@ -274,6 +276,10 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize()
     ntt_ms = e0.elapsed_time(e1) / reps
+    l0 = lib.cross_launch_count()
+    ntt_once()
+    torch.cuda.synchronize()
+    ntt_launches = lib.cross_launch_count() - l0              # 2: column + row contraction
     transforms = lps * (L - 1)
     ops = transforms * 32.0 * N_DEG * (R + C)              # int8 MAC x2 per limb-transform
     pk, src = peaks()
@@ -292,11 +298,13 @@ def main():
                 "d2h_bytes_per_step": int(hout.numel() * 4)},
         "gpu_launches": int(launches),
         "clocks": clk.summary(h0, h1),
-        "roofline": {"kernel": "BAT NTT forward (column + row contraction kernels), 23 limbs x 256 polys",
+        "roofline": {"kernel": "k_bat_tc2 tensor-core BAT contraction (NTT column + row stage launches), "
+                               "23 limbs x 256 polys, N=2^16",
                      "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
                      "frac": achieved / int8_peak, "traffic": None,
                      "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); no int8 measurement on this pool",
-                     "ms_per_launch": ntt_ms, "algorithmic_ops_per_launch": ops},
+                     "launches": ntt_launches, "ms_per_launch": ntt_ms / max(ntt_launches, 1),
+                     "algorithmic_ops_per_launch": ops / max(ntt_launches, 1)},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libcross_b200.so")
 
 LAYOUT_REFERENCE = 0
 LAYOUT_LIMB_MAJOR = 1
+LAYOUT_LIMB_MAJOR_TRANSPOSED = 2   # cross_ntt only: coefficients (M, c, r), evaluations (M, r, c)
 
 _STATUS = {-1: ValueError, -2: RuntimeError, -3: NotImplementedError, -4: MemoryError, -5: TimeoutError}
 

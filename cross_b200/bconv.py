@@ -63,7 +63,7 @@ class BConv:
         return self._plans[control_index]
 
     def __del__(self):
-        if _lib._lib is not None:
+        if getattr(_lib, "_lib", None) is not None:
             for p in getattr(self, "_plans", []):
                 if p is not None:
                     _lib._lib.cross_bconv_plan_destroy(p)

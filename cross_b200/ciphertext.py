@@ -266,7 +266,7 @@ class Ciphertext:
         return out
 
     def __del__(self):
-        if getattr(self, "_rs_plan", None) is not None and _lib._lib is not None:
+        if getattr(self, "_rs_plan", None) is not None and getattr(_lib, "_lib", None) is not None:
             _lib._lib.cross_rescale_plan_destroy(self._rs_plan)
 
     # -- HE kernels (ciphertext.py:309-519) ----------------------------------

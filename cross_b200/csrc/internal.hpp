@@ -106,7 +106,11 @@ struct View {
   const uint32_t* p = nullptr;
   int64_t ps = 0, es = 0, ss = 0;
   int E = 1;
-  __host__ __device__ const uint32_t* at(int64_t e, int slot) const { return p + (e / E) * ps + (e % E) * es + slot * ss; }
+  __host__ __device__ const uint32_t* at(int64_t e, int slot) const {
+    if (E == 1) return p + e * ps + slot * ss;
+    const unsigned c = (unsigned)e / (unsigned)E;   // element indices stay below 2^31
+    return p + (int64_t)c * ps + (int64_t)((unsigned)e - c * E) * es + slot * ss;
+  }
 };
 
 // Position-wise operation fused into the last stage of a transform; r is the

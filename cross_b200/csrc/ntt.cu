@@ -328,7 +328,8 @@ size_t cross_ntt_workspace_size(cross_ntt_plan P, int64_t batch, int layout) {
 int cross_ntt(cross_ntt_plan P, int inverse, const uint32_t* in, uint32_t* out, int64_t batch, int layout,
               void* workspace, size_t workspace_bytes, void* stream) {
   CROSS_REQUIRE(P && in && out && batch >= 0, "cross_ntt: null argument or negative batch");
-  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR,
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR ||
+                    layout == CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED,
                 "cross_ntt: unknown layout %d", layout);
   if (batch == 0) return CROSS_OK;
   const size_t need = cross_ntt_workspace_size(P, batch, layout);
@@ -344,6 +345,10 @@ int cross_ntt(cross_ntt_plan P, int inverse, const uint32_t* in, uint32_t* out, 
   uint32_t* tmp = a.take<uint32_t>((size_t)ntt_tmp_words(P, batch * M));
   if (layout == CROSS_LAYOUT_LIMB_MAJOR) {
     return ntt_run(P, inverse != 0, LP{in, M * N, N}, LPo{out, M * N, N}, batch, M, P->identity, tmp, st);
+  }
+  if (layout == CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED) {
+    return ntt_exec(P, inverse != 0, LP{in, M * N, N}, COEF_TRANSPOSED, LPo{out, M * N, N}, COEF_TRANSPOSED, batch, M,
+                    P->identity, Epi{}, tmp, st);
   }
   uint32_t* lm = a.take<uint32_t>(words);
   int rc = transpose_u32(in, lm, batch, N, M, st);

@@ -99,17 +99,35 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase of `parity` to complete.  Returns false (and
-// raises the CTA abort flag, recording `code`) when the bound expires or
-// another role of the CTA has already aborted.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int& abort, int* err, int code) {
-  if (mbar_test(bar, parity)) return true;
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase of `parity` to complete.  try_wait suspends the
+// thread in hardware until the phase completes or a short system-defined
+// interval passes, so a waiting role wakes as soon as its barrier flips.
+// Returns false (and raises the CTA abort flag, recording `code`) when the
+// bound expires or another role of the CTA has already aborted.  The first
+// try is inline; the bounded loop is out of line.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int& abort, int* err, int code);
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int& abort, int* err, int code) {
+  if (mbar_try(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort, err, code);
+}
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int& abort, int* err, int code) {
   const uint64_t t0 = globaltimer();
-  for (uint32_t i = 0;; ++i) {
-    if (mbar_test(bar, parity)) return true;
+  for (;;) {
+    if (mbar_try(bar, parity)) return true;
     if (abort) return false;
-    if (i >= 32) __nanosleep(i < 1024 ? 20 : 200);
-    if ((i & 255) == 255 && globaltimer() - t0 > WAIT_NS) {
+    if (globaltimer() - t0 > WAIT_NS) {
       atomicCAS(err, 0, code);
       abort = 1;
       return false;
@@ -207,19 +225,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 
 struct Unit {
-  int nt, mt, slot;
-  int64_t poly;
+  int nt, mt, slot, poly;
 };
-__device__ __forceinline__ Unit decode(int64_t u, int n_tiles, int m_tiles, int64_t polys) {
+// Unit u of k_bat_tc (n tile fastest, then m tile, poly, slot); tile counts are
+// powers of two and the host keeps every unit index below 2^31.
+__device__ __forceinline__ Unit decode(int u, int nt_shift, int mt_shift, int polys) {
   Unit r;
-  r.nt = (int)(u % n_tiles);
-  u /= n_tiles;
-  r.mt = (int)(u % m_tiles);
-  u /= m_tiles;
-  r.poly = u % polys;
-  r.slot = (int)(u / polys);
+  r.nt = u & ((1 << nt_shift) - 1);
+  u >>= nt_shift;
+  r.mt = u & ((1 << mt_shift) - 1);
+  u >>= mt_shift;
+  r.slot = (unsigned)u / (unsigned)polys;
+  r.poly = u - r.slot * polys;
   return r;
 }
+
+// Per-slot constants of the epilogue, reloaded only when the slot changes.
+struct SlotCache {
+  int slot = -1;
+  ModC mc;
+  const uint32_t* tab = nullptr;   // EPI_MUL table row of the slot
+  uint32_t scal = 0;               // EPI_COMBINE / EPI_MODDOWN scalar of the slot
+};
 
 // Epilogue of one 128 x 256 accumulator tile, run by the 16 epilogue warps
 // (TMEM lane quadrant warp % 4, column quarter (warp - 2) / 4): tcgen05.ld,
@@ -230,21 +257,26 @@ __device__ __forceinline__ Unit decode(int64_t u, int n_tiles, int m_tiles, int6
 // 16-byte loads).  Returns false when the wait for the accumulator gave up.
 template <int EPI, bool NMAJOR, bool FAST>
 __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, uint64_t* tfull, uint32_t parity,
-                                              volatile int& abort, const Unit& w, bool store, int warp, int lane) {
+                                              volatile int& abort, const Unit& w, bool store, int warp, int lane,
+                                              SlotCache& sc) {
   constexpr int OUTS = 16;                     // outputs (64 columns) per thread and tile
   const int quad = warp & 3, part = (warp - 2) >> 2;
-  const int64_t N = (int64_t)a.rows_m * a.nout;
   constexpr int P0 = EPI == EPI_NONE ? 1 : OUTS;
   constexpr int P1 = EPI == EPI_MODDOWN ? OUTS : 1;
-  const int limb = a.limbs[w.slot];
+  if (w.slot != sc.slot) {
+    sc.slot = w.slot;
+    sc.mc = a.mods[a.limbs[w.slot]];
+    if (EPI == EPI_MUL) sc.tab = a.e.tab + (int64_t)a.e.trow[w.slot] * ((int64_t)a.rows_m * a.nout);
+    if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) sc.scal = a.e.scal[w.slot];
+  }
   const int m = w.mt * BM + quad * 32 + lane;
   const int n0 = w.nt * 64 + part * OUTS;
   const int64_t p0 = NMAJOR ? (int64_t)n0 * a.rows_m + m : (int64_t)m * a.nout + n0;
   uint32_t pre0[P0], pre1[P1];
-  uint32_t scal = 0;
+  const uint32_t scal = sc.scal;
   bool add_base = false;
   if (EPI != EPI_NONE) {
-    const uint32_t* src = EPI == EPI_MUL ? a.e.tab + (int64_t)a.e.trow[w.slot] * N + p0 : a.e.x.at(w.poly, w.slot) + p0;
+    const uint32_t* src = EPI == EPI_MUL ? sc.tab + p0 : a.e.x.at(w.poly, w.slot) + p0;
     if (NMAJOR) {
 #pragma unroll
       for (int j = 0; j < OUTS; ++j) pre0[j] = __ldg(src + (int64_t)j * a.rows_m);
@@ -259,9 +291,8 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
       }
     }
   }
-  if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) scal = a.e.scal[w.slot];
   if (EPI == EPI_MODDOWN) {
-    add_base = (a.e.base_mask >> (w.poly % a.e.base.E)) & 1u;
+    add_base = (a.e.base_mask >> ((unsigned)w.poly % (unsigned)a.e.base.E)) & 1u;
     if (add_base) {
       const uint4* b = reinterpret_cast<const uint4*>(a.e.base.at(w.poly, w.slot) + p0);
 #pragma unroll
@@ -274,12 +305,12 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
       }
     }
   }
-  const ModC mc = a.mods[limb];
+  const ModC& mc = sc.mc;
   bool ok = mbar_wait(tfull, parity, abort, a.err, 4);
   ok = __all_sync(0xffffffffu, ok);
   if (!ok) return false;
   tc_fence_after();
-  uint32_t* o = a.out + w.poly * a.out_ps + (int64_t)w.slot * a.out_ss + p0;
+  uint32_t* o = a.out + (int64_t)w.poly * a.out_ps + (int64_t)w.slot * a.out_ss + p0;
   const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
 #pragma unroll
   for (int chunk = 0; chunk < OUTS / 8; ++chunk) {
@@ -333,8 +364,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
   extern __shared__ uint8_t smem_raw[];
   Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tiles = a.rows_m / BM, n_tiles = a.nout / 64, kst = a.kw / 32;
-  const int64_t units = (int64_t)a.slots * a.polys * m_tiles * n_tiles;
+  const int kst = a.kw / 32;
+  const int mt_shift = __ffs(a.rows_m / BM) - 1, nt_shift = __ffs(a.nout / 64) - 1;
+  const int units = a.slots * a.polys << (mt_shift + nt_shift);
+  const int polys = (int)a.polys;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -367,8 +400,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
       // ---------------- TMA producer ----------------
       uint32_t stage = 0, phase = 0;
       int issued = 0;
-      for (int64_t u = blockIdx.x; u < units && !S.abort; u += gridDim.x) {
-        const Unit w = decode(u, n_tiles, m_tiles, a.polys);
+      for (int u = blockIdx.x; u < units && !S.abort; u += gridDim.x) {
+        const Unit w = decode(u, nt_shift, mt_shift, polys);
         const int limb = a.limbs[w.slot];
         for (int ks = 0; ks < kst; ++ks) {
           if (!mbar_wait(&S.empty[stage], phase ^ 1, S.abort, a.err, 1)) break;
@@ -396,7 +429,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       uint32_t stage = 0, phase = 0, acc = 0, aphase = 0;
-      for (int64_t u = blockIdx.x; u < units && !S.abort; u += gridDim.x) {
+      for (int u = blockIdx.x; u < units && !S.abort; u += gridDim.x) {
         if (!mbar_wait(&S.tempty[acc], aphase ^ 1, S.abort, a.err, 2)) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
@@ -430,9 +463,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
   } else {
     // ---------------- epilogue (warps 2..17) ----------------
     uint32_t acc = 0, aphase = 0;
-    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
-      const Unit w = decode(u, n_tiles, m_tiles, a.polys);
-      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, true, warp, lane))
+    SlotCache sc;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const Unit w = decode(u, nt_shift, mt_shift, polys);
+      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, true, warp, lane,
+                                            sc))
         break;
       tc_fence_before();
       mbar_arrive(&S.tempty[acc]);
@@ -467,13 +502,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
 constexpr int B2_ROWS = BN / 2;                  // B rows held per CTA
 constexpr int B2_CHUNK = B2_ROWS * BKB;          // 16 KiB per 128-byte K chunk
 constexpr int B2_CHUNKS = 8;                     // kw <= 256
+constexpr int KPS = 2;                           // 128-byte K chunks per A stage (8 MMAs per stage)
+constexpr int STAGES2 = 3;                       // A ring: 96 KiB in flight per CTA
 constexpr uint32_t IDESC2 = (2u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
 
 struct Smem2 {
-  uint8_t a[STAGES][A_STAGE];
+  uint8_t a[STAGES2][KPS * A_STAGE];
   uint8_t b[B2_CHUNKS][B2_CHUNK];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[STAGES2];
+  uint64_t empty[STAGES2];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t bfull, bempty, drain;
@@ -481,6 +518,7 @@ struct Smem2 {
   volatile int abort;
 };
 constexpr size_t SMEM2_BYTES = sizeof(Smem2) + 1024;
+static_assert(SMEM2_BYTES <= 232448, "k_bat_tc2 shared memory exceeds 227 KiB");
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -496,8 +534,11 @@ __device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr(p)), "r"(rank));
   return r;
 }
+// Arrive on a barrier of either CTA of the cluster (the epilogue's release of
+// an accumulator: tcgen05.fence::before_thread_sync orders its TMEM reads, no
+// global memory ordering is needed, so the default CTA-scope release).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
 }
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* tm, uint32_t bar_cl, int c0, int c1,
                                                  int c2, int c3) {
@@ -513,6 +554,11 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* t
       "%4}], [%2];" ::"r"(saddr(dst)),
       "l"((uint64_t)tm), "r"(bar_cl), "r"(c0), "r"(c1)
       : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* tm, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"((uint64_t)tm), "r"(c0),
+               "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
 }
 __device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   const uint32_t z = 0;
@@ -538,36 +584,48 @@ __device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
 
 // Work of a pair: group g = pair / n_tiles over items [t0, t1) of the
 // (slot, j) sequence (j = row-block pair, ipc per slot), n tile pair % n_tiles.
+// The host keeps slots * ipc below 2^31.
 struct PairWork {
-  int64_t t0, t1, ipc, rbs;
-  int nt;
+  int t0, t1, ipc, rbs, nt, mt_shift;
 };
-__device__ __forceinline__ PairWork pair_work(const Args& a, int m_tiles, int n_tiles) {
+__device__ __forceinline__ PairWork pair_work(const Args& a) {
   PairWork pw;
-  const int64_t pair = blockIdx.x >> 1, groups = (gridDim.x >> 1) / n_tiles;
-  const int64_t g = pair / n_tiles;
-  pw.nt = (int)(pair % n_tiles);
-  pw.rbs = a.polys * m_tiles;
+  const int n_tiles = a.nout / 64;
+  const int pair = blockIdx.x >> 1, groups = (gridDim.x >> 1) / n_tiles;
+  const int g = pair / n_tiles;
+  pw.nt = pair - g * n_tiles;
+  pw.mt_shift = __ffs(a.rows_m / BM) - 1;
+  pw.rbs = (int)a.polys << pw.mt_shift;
   pw.ipc = (pw.rbs + 1) / 2;
   const int64_t total = (int64_t)a.slots * pw.ipc;
-  pw.t0 = total * g / groups;
-  pw.t1 = total * (g + 1) / groups;
+  pw.t0 = (int)(total * g / groups);
+  pw.t1 = (int)(total * (g + 1) / groups);
   return pw;
 }
-// Row block of this CTA in item t (the peer of an odd last pair repeats the
-// leader's row block and stores nothing).
-__device__ __forceinline__ Unit pair_unit(int64_t t, const PairWork& pw, uint32_t rank, int m_tiles, bool& valid) {
-  Unit w;
-  w.slot = (int)(t / pw.ipc);
-  const int64_t j = t % pw.ipc;
-  int64_t rb = 2 * j + rank;
-  valid = rb < pw.rbs;
-  if (!valid) rb = 2 * j;
-  w.poly = rb / m_tiles;
-  w.mt = (int)(rb % m_tiles);
-  w.nt = pw.nt;
-  return w;
-}
+// Walks the items of a pair in order without divisions.
+struct PairIter {
+  int slot, j;
+  __device__ __forceinline__ PairIter(const PairWork& pw) : slot(pw.t0 / pw.ipc), j(pw.t0 - slot * pw.ipc) {}
+  __device__ __forceinline__ void next(const PairWork& pw) {
+    if (++j == pw.ipc) {
+      j = 0;
+      ++slot;
+    }
+  }
+  // Row block of this CTA (the peer of an odd last pair repeats the leader's
+  // row block and stores nothing).
+  __device__ __forceinline__ Unit unit(const PairWork& pw, uint32_t rank, bool& valid) const {
+    Unit w;
+    w.slot = slot;
+    int rb = 2 * j + (int)rank;
+    valid = rb < pw.rbs;
+    if (!valid) rb = 2 * j;
+    w.poly = rb >> pw.mt_shift;
+    w.mt = rb & ((1 << pw.mt_shift) - 1);
+    w.nt = pw.nt;
+    return w;
+  }
+};
 
 template <int EPI, bool NMAJOR, bool FAST>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
@@ -576,11 +634,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   Smem2& S = *reinterpret_cast<Smem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
-  const int m_tiles = a.rows_m / BM, n_tiles = a.nout / 64, kst = a.kw / 32;
-  const PairWork pw = pair_work(a, m_tiles, n_tiles);
+  const int kst = a.kw / 32;
+  const PairWork pw = pair_work(a);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < STAGES2; ++s) {
       mbar_init(&S.full[s], 1);
       mbar_init(&S.empty[s], 1);
     }
@@ -614,9 +672,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       uint32_t stage = 0, phase = 0, bphase = 0;
       int prev_slot = -1;
       int issued = 0;
-      for (int64_t t = pw.t0; t < pw.t1 && !S.abort; ++t) {
+      PairIter it(pw);
+      for (int t = pw.t0; t < pw.t1 && !S.abort; ++t, it.next(pw)) {
         bool valid;
-        const Unit w = pair_unit(t, pw, rank, m_tiles, valid);
+        const Unit w = it.unit(pw, rank, valid);
+        if (t + 1 < pw.t1) {
+          // pull the next item's A rows into L2 while this item streams
+          PairIter nx = it;
+          nx.next(pw);
+          bool nv;
+          const Unit wn = nx.unit(pw, rank, nv);
+          for (int kc = 0; kc < kst; ++kc) tma_prefetch_l2_4d(&tmA, kc * 32, wn.mt * BM, wn.slot, wn.poly);
+        }
         if (w.slot != prev_slot) {
           // the MMAs that read the resident B half have completed
           if (!mbar_wait(&S.bempty, bphase ^ 1, S.abort, a.err, 11)) break;
@@ -628,12 +695,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             tma_load_2d_pair(S.b[kc], &tmB, bar, kc * BKB, limb * 4 * a.nout + w.nt * BN + (int)rank * B2_ROWS);
           prev_slot = w.slot;
         }
-        for (int kc = 0; kc < kst; ++kc) {
+        for (int kc = 0; kc < kst; kc += KPS) {
           if (!mbar_wait(&S.empty[stage], phase ^ 1, S.abort, a.err, 12)) break;
-          if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * A_STAGE);
-          tma_load_4d_pair(S.a[stage], &tmA, mapa(&S.full[stage], 0), kc * 32, w.mt * BM, w.slot, (int)w.poly);
+          if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * KPS * A_STAGE);
+          const uint32_t bar = mapa(&S.full[stage], 0);
+          for (int h = 0; h < KPS; ++h)
+            tma_load_4d_pair(S.a[stage] + h * A_STAGE, &tmA, bar, (kc + h) * 32, w.mt * BM, w.slot, w.poly);
           ++issued;
-          if (++stage == STAGES) {
+          if (++stage == STAGES2) {
             stage = 0;
             phase ^= 1;
           }
@@ -641,9 +710,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
       if (S.abort && rank == 0) {
         // let the copies already issued land before the CTA exits
-        for (int i = 0; i < STAGES && i < issued; ++i) {
-          stage = stage == 0 ? STAGES - 1 : stage - 1;
-          if (stage == STAGES - 1) phase ^= 1;
+        for (int i = 0; i < STAGES2 && i < issued; ++i) {
+          stage = stage == 0 ? STAGES2 - 1 : stage - 1;
+          if (stage == STAGES2 - 1) phase ^= 1;
           const uint64_t t0 = globaltimer();
           while (!mbar_test(&S.full[stage], phase) && globaltimer() - t0 < WAIT_NS) __nanosleep(200);
         }
@@ -654,8 +723,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       // ---------------- MMA issuer (leader) ----------------
       uint32_t stage = 0, phase = 0, acc = 0, aphase = 0, bphase = 0;
       int prev_slot = -1;
-      for (int64_t t = pw.t0; t < pw.t1 && !S.abort; ++t) {
-        const int slot = (int)(t / pw.ipc);
+      PairIter it(pw);
+      for (int t = pw.t0; t < pw.t1 && !S.abort; ++t, it.next(pw)) {
+        const int slot = it.slot;
         if (!mbar_wait(&S.tempty[acc], aphase ^ 1, S.abort, a.err, 13)) break;
         if (slot != prev_slot) {
           if (!mbar_wait(&S.bfull, bphase, S.abort, a.err, 14)) break;
@@ -665,18 +735,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         bool ok = true;
-        for (int kc = 0; kc < kst; ++kc) {
+        for (int kc = 0; kc < kst; kc += KPS) {
           if (!mbar_wait(&S.full[stage], phase, S.abort, a.err, 15)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t as = saddr(S.a[stage]), bs = saddr(S.b[kc]);
 #pragma unroll
-          for (int k = 0; k < BKB / 32; ++k)
-            mma_i8_pair(d, sw128_desc(as + 32 * k), sw128_desc(bs + 32 * k), (kc | k) != 0);
+          for (int h = 0; h < KPS; ++h) {
+            const uint32_t as = saddr(S.a[stage] + h * A_STAGE), bs = saddr(S.b[kc + h]);
+#pragma unroll
+            for (int k = 0; k < BKB / 32; ++k)
+              mma_i8_pair(d, sw128_desc(as + 32 * k), sw128_desc(bs + 32 * k), (kc | h | k) != 0);
+          }
           mma_commit_pair_both(&S.empty[stage]);
-          if (++stage == STAGES) {
+          if (++stage == STAGES2) {
             stage = 0;
             phase ^= 1;
           }
@@ -685,7 +758,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         mma_commit_pair_both(&S.tfull[acc]);
         acc ^= 1;
         if (acc == 0) aphase ^= 1;
-        if (t + 1 == pw.t1 || (int)((t + 1) / pw.ipc) != slot) mma_commit_pair_both(&S.bempty);
+        if (t + 1 == pw.t1 || it.j + 1 == pw.ipc) mma_commit_pair_both(&S.bempty);
       }
       // every MMA issued by this thread has completed once `drain` flips
       mma_commit_pair_local(&S.drain);
@@ -695,10 +768,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else {
     // ---------------- epilogue (both CTAs, warps 2..17) ----------------
     uint32_t acc = 0, aphase = 0;
-    for (int64_t t = pw.t0; t < pw.t1; ++t) {
+    SlotCache sc;
+    PairIter it(pw);
+    for (int t = pw.t0; t < pw.t1; ++t, it.next(pw)) {
       bool valid;
-      const Unit w = pair_unit(t, pw, rank, m_tiles, valid);
-      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, valid, warp, lane))
+      const Unit w = it.unit(pw, rank, valid);
+      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, valid, warp, lane,
+                                            sc))
         break;
       tc_fence_before();
       __syncwarp();
@@ -842,6 +918,11 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
   CUtensorMap tmA;
   int rc = make_tmap_a(&tmA, A, kw, rows_m, slots, polys, a_ss, a_ps);
   if (rc) return rc;
+  // unit and item indices are 32-bit inside the kernels
+  if ((int64_t)slots * polys * (rows_m / BM) * (nout / 64) >= ((int64_t)1 << 31)) {
+    set_error("tcgen05 stage: %lld limb-polynomials exceed one launch", (long long)(polys * slots));
+    return CROSS_ERR_UNSUPPORTED;
+  }
   Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->tc_err, e};
   if (!nmajor && e.op != EPI_NONE) {
     // row-major operands are read with 16-byte loads
@@ -856,7 +937,7 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
     }
   }
   const bool f = P->tc_fast != 0;
-  const bool pair = P->tc_pair && kw <= 32 * B2_CHUNKS;
+  const bool pair = P->tc_pair && kw <= 32 * B2_CHUNKS && kw % (32 * KPS) == 0;
 #define CROSS_TC_LAUNCH(OP, NM)                                                                      \
   return pair ? (f ? launch2<OP, NM, true>(tmA, tmB2, a, st) : launch2<OP, NM, false>(tmA, tmB2, a, st)) \
               : (f ? launch<OP, NM, true>(tmA, tmB, a, st) : launch<OP, NM, false>(tmA, tmB, a, st))
@@ -882,7 +963,7 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
 }  // namespace tc
 
 bool tc_supported(int r, int c) {
-  auto ok = [](int x) { return x % 128 == 0 && x >= 128 && x <= 1024; };
+  auto ok = [](int x) { return x >= 128 && x <= 1024 && (x & (x - 1)) == 0; };
   return ok(r) && ok(c);
 }
 

@@ -70,7 +70,7 @@ class BarrettContext(FiniteFieldContextBase):
         return self._handle
 
     def __del__(self):
-        if getattr(self, "_handle", None) is not None and _lib._lib is not None:
+        if getattr(self, "_handle", None) is not None and getattr(_lib, "_lib", None) is not None:
             _lib._lib.cross_moduli_destroy(self._handle)
             self._handle = None
 

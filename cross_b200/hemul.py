@@ -120,7 +120,7 @@ class HEMul:
                                                    eb.ctypes.data, ea.shape[-1]), "cross_hemul_set_keys")
 
     def _free_plan(self):
-        if getattr(self, "_plan", None) is not None and _lib._lib is not None:
+        if getattr(self, "_plan", None) is not None and getattr(_lib, "_lib", None) is not None:
             _lib._lib.cross_hemul_plan_destroy(self._plan)
         self._plan = None
 

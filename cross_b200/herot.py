@@ -103,7 +103,7 @@ class HERot:
                    "cross_herot_set_keys")
 
     def _free_plan(self):
-        if getattr(self, "_plan", None) is not None and _lib._lib is not None:
+        if getattr(self, "_plan", None) is not None and getattr(_lib, "_lib", None) is not None:
             _lib._lib.cross_herot_plan_destroy(self._plan)
         self._plan = None
 

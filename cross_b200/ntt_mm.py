@@ -125,7 +125,7 @@ class NTTCiphertextContextBase:
         return self._plan
 
     def __del__(self):
-        if getattr(self, "_plan", None) is not None and _lib._lib is not None:
+        if getattr(self, "_plan", None) is not None and getattr(_lib, "_lib", None) is not None:
             _lib._lib.cross_ntt_plan_destroy(self._plan)
             self._plan = None
 

@@ -19,6 +19,10 @@
  *   - Layouts: CROSS_LAYOUT_REFERENCE is jaxite_word's (..., r, c, limbs),
  *     limb-innermost.  CROSS_LAYOUT_LIMB_MAJOR is (..., limbs, r, c): each
  *     limb-polynomial contiguous, the internal layout of the kernels.
+ *     CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED (cross_ntt only) is limb-major with
+ *     the coefficient side in transposed order (coefficient r*C + c stored at
+ *     c*R + r), the order the tensor-core transforms work in: an NTT from it
+ *     and an INTT into it skip a transpose pass.
  */
 #ifndef CROSS_B200_H_
 #define CROSS_B200_H_
@@ -43,7 +47,8 @@ typedef enum cross_status {
 
 typedef enum cross_layout {
   CROSS_LAYOUT_REFERENCE = 0,
-  CROSS_LAYOUT_LIMB_MAJOR = 1
+  CROSS_LAYOUT_LIMB_MAJOR = 1,
+  CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED = 2
 } cross_layout;
 
 typedef struct cross_moduli_s* cross_moduli;
@@ -135,7 +140,10 @@ size_t cross_ntt_workspace_size(cross_ntt_plan plan, int64_t batch, int layout);
 /* NTTCiphertextBarrettContext.ntt / .intt (ntt_mm.py:351-407):
  * in/out (batch, r, c, M) for CROSS_LAYOUT_REFERENCE or (batch, M, r, c) for
  * CROSS_LAYOUT_LIMB_MAJOR, uint32.  Output of ntt is in bit-reversed
- * evaluation order, exactly as the reference.  in may equal out. */
+ * evaluation order, exactly as the reference.  With
+ * CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED the coefficients (ntt input, intt
+ * output) are (batch, M, c, r) and the evaluations (batch, M, r, c).
+ * in may equal out. */
 int cross_ntt(cross_ntt_plan plan, int inverse, const uint32_t* in, uint32_t* out, int64_t batch,
               int layout, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -87,6 +87,34 @@ def test_two_sm_kernel_matches_one_sm_kernel(monkeypatch, r, c, L, B):
     assert not ((z2.astype(np.int64) - x) % np.array(q, np.int64)).any()
 
 
+@pytest.mark.parametrize("r,c", [(256, 256), (64, 64), (128, 512)])
+def test_ntt_transposed_coefficient_layout(r, c):
+    """CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED: ntt of the transposed coefficients
+    equals ntt of the natural ones, intt returns transposed coefficients."""
+    import torch
+    from cross_b200 import ntt_mm, _lib
+    n, L, B = r * c, 3, 2
+    q = O.find_moduli_ntt(L, 28, 2 * n)
+    x = np.ascontiguousarray(rng_residues(np.random.default_rng(r + c), (B, r, c, L), q).transpose(0, 3, 1, 2))
+    ctx = ntt_mm.NTTCiphertextBarrettContext(q, {"r": r, "c": c})
+    lib = _lib.lib()
+
+    def run(inv, src, layout):
+        d = torch.from_numpy(np.ascontiguousarray(src)).cuda()
+        o = torch.empty_like(d)
+        ws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), B, layout), dtype=torch.uint8, device="cuda")
+        _lib.check(lib.cross_ntt(ctx.plan(), inv, d.data_ptr(), o.data_ptr(), B, layout, ws.data_ptr(), ws.numel(),
+                                 None), "cross_ntt")
+        return _np(o)
+
+    xt = x.transpose(0, 1, 3, 2)
+    y = run(0, x, _lib.LAYOUT_LIMB_MAJOR)
+    np.testing.assert_array_equal(run(0, xt, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED).reshape(y.shape), y)
+    z = run(1, y, _lib.LAYOUT_LIMB_MAJOR)
+    np.testing.assert_array_equal(run(1, y, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED).reshape(xt.shape),
+                                  z.transpose(0, 1, 3, 2))
+
+
 def test_ntt_round_trip_and_linearity_full_size():
     """Size-independent properties at N = 2^16, 24 limbs: INTT(NTT(x)) == x mod q
     and NTT(x + y) == NTT(x) + NTT(y) mod q."""
