@@ -64,6 +64,7 @@ _SIGS = {
     "cross_ntt_plan_check": (i32, [vp]),
     "cross_bconv_plan_create": (i32, [vp, vp, vp, vp, vp, C.POINTER(vp)]),
     "cross_bconv_plan_destroy": (i32, [vp]),
+    "cross_bconv_plan_check": (i32, [vp]),
     "cross_bconv": (i32, [vp, i32, vp, vp, i64, i64, i32, vp]),
     "cross_rescale_plan_create": (i32, [C.POINTER(RescaleDesc), C.POINTER(vp)]),
     "cross_rescale_plan_destroy": (i32, [vp]),

@@ -68,6 +68,12 @@ class BConv:
                 if p is not None:
                     _lib._lib.cross_bconv_plan_destroy(p)
 
+    def check_device(self):
+        """Raise TimeoutError if a tensor-core kernel of these plans hit a bounded wait."""
+        for p in self._plans:
+            if p is not None:
+                _lib.check(_lib.lib().cross_bconv_plan_check(p), "cross_bconv_plan_check")
+
     def _run(self, in_tower, control_index, bat):
         x = _tensor.to_u32(in_tower)
         sq = len(self.original_moduli[control_index])

@@ -6,10 +6,19 @@
 // and out_j = Barrett_dst_j(S_j).  The inner sum over the four bytes a of one
 // c_i is one dp4a against the packed BAT column.
 // basis_change: S_j = sum_i c_i * QHatModp[i, j] in uint64, then Barrett.
+//
+// Two kernels compute basis_change_bat.  k_bconv_tc (contiguous coefficients,
+// n % 128 == 0) runs the contraction on the tensor cores: for 128 coefficients
+// t, A[t][(i, a)] = byte_a(c_i[t]) (K = 4 sq bytes) against
+// B[(j, b)][(i, a)] = QHatModpBAT[(i, a), j, b] (N = 4 sp), one
+// tcgen05.mma.kind::i8 per 8 source limbs, and the epilogue recombines the four
+// byte planes b of every target limb.  k_bconv (any strides) uses dp4a.
+#include <cstdlib>
 #include <type_traits>
 #include <vector>
 
 #include "internal.hpp"
+#include "tc_ptx.cuh"
 
 namespace cross {
 
@@ -116,6 +125,231 @@ __global__ void __launch_bounds__(BC_THREADS) k_bconv(const uint32_t* __restrict
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core basis conversion.  One CTA of 128 threads per tile of 128
+// coefficients of one polynomial, thread t owning coefficient row t (TMEM lane
+// t):
+//   1. c_i = Barrett_src_i(x_i[t] * QHatInvModq_i) written as row t of the
+//      K-major A tile (no swizzle: 8-row x 16-byte core matrices, K halves 128 B
+//      apart, 8-row groups 256 B apart; one 16-byte store per 4 limbs);
+//   2. thread 0 issues kb MMAs (M = 128, N = nn, K = 32) into TMEM and commits;
+//   3. every thread reads its accumulator row and writes
+//      out_j[t] = Barrett_dst_j(sum_b D[t][4j + b] << 8b) (times the psi twist).
+// The B image (QHatModpBAT in the same core-matrix layout) and the per-limb
+// constants stay in shared memory.  The MMA completion wait is bounded; on
+// expiry the kernel records code 21 in the plan's error word and stops.
+constexpr int BT_THREADS = 128;
+using namespace tc;
+
+struct BconvTcArgs {
+  const uint32_t* in;
+  int64_t in_ps, in_ls;
+  uint32_t* out;
+  int64_t out_ps, out_ls;
+  int polys, n, sq, sp, kb, nn;
+  uint32_t tmem_cols;
+  const ModC* src;
+  const ModC* dst;
+  const uint32_t* qhat_inv;
+  const uint8_t* bimg;
+  const uint32_t* twist;
+  const uint16_t* trow;
+  int* err;
+};
+
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
+  // start >> 4, leading (K) byte offset 128 >> 4, stride (8-row) byte offset
+  // 256 >> 4, descriptor version 1, layout SWIZZLE_NONE
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
+         ((uint64_t)1 << 46);
+}
+
+template <bool FAST, bool TWIST, int KB, int SPMAX>
+__global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* As = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Bs = As + a.kb * 4096;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(Bs + a.kb * (a.nn / 8) * 256);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  volatile int& abort = *reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* dq = tmem_slot + 2;          // [sp] target q, m, s_w, twist row
+  uint32_t* dm = dq + a.sp;
+  uint32_t* dsw = dm + a.sp;
+  uint32_t* dtr = dsw + a.sp;
+  ModC* sc = reinterpret_cast<ModC*>((reinterpret_cast<uintptr_t>(dtr + a.sp) + 7) & ~uintptr_t(7));   // [sq] source moduli
+  uint32_t* shi = reinterpret_cast<uint32_t*>(sc + a.sq);        // [sq] QHatInvModq
+  const int t = threadIdx.x, warp = t >> 5;
+
+  for (int i = t; i < a.kb * (a.nn / 8) * 16; i += BT_THREADS)
+    reinterpret_cast<uint4*>(Bs)[i] = reinterpret_cast<const uint4*>(a.bimg)[i];
+  for (int j = t; j < a.sp; j += BT_THREADS) {
+    dq[j] = (uint32_t)a.dst[j].q;
+    dm[j] = (uint32_t)a.dst[j].m;
+    dsw[j] = a.dst[j].s_w;
+    dtr[j] = TWIST ? a.trow[j] : 0u;
+  }
+  for (int i = t; i < a.sq; i += BT_THREADS) {
+    sc[i] = a.src[i];
+    shi[i] = a.qhat_inv[i];
+  }
+  if (t == 0) {
+    mbar_init(bar, 1);
+    abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                 "r"(a.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t idesc = (2u << 4) | ((uint32_t)(a.nn >> 3) << 17) | ((uint32_t)(BT_THREADS >> 4) << 24);
+  const int tiles_pp = a.n / BT_THREADS;
+  const int total = a.polys * tiles_pp;
+  // inputs of the next tile, loaded while the current one is converted
+  uint32_t xin[8 * KB];
+  auto load_inputs = [&](int w) {
+    const int poly = w / tiles_pp;
+    const uint32_t* x = a.in + (int64_t)poly * a.in_ps + (w - poly * tiles_pp) * BT_THREADS + t;
+#pragma unroll
+    for (int i = 0; i < 8 * KB; ++i) xin[i] = i < a.sq ? __ldg(x + (int64_t)i * a.in_ls) : 0u;
+  };
+  if ((int)blockIdx.x < total) load_inputs(blockIdx.x);
+  uint32_t phase = 0;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int poly = w / tiles_pp;
+    const int t0 = (w - poly * tiles_pp) * BT_THREADS;
+    // 1. source residues, 4 limbs (16 bytes of K) per store
+#pragma unroll
+    for (int g = 0; g < 2 * KB; ++g) {
+      if (g < 2 * a.kb) {
+        uint32_t c[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = 4 * g + e;
+          uint32_t v = 0;
+          if (i < a.sq) {
+            const uint64_t z = (uint64_t)xin[i] * shi[i];
+            v = FAST ? barrett_w32(z, (uint32_t)sc[i].q, (uint32_t)sc[i].m, sc[i].s_w) : barrett(z, sc[i]);
+          }
+          c[e] = v;
+        }
+        *reinterpret_cast<uint4*>(As + (g >> 1) * 4096 + (t >> 3) * 256 + (g & 1) * 128 + (t & 7) * 16) =
+            make_uint4(c[0], c[1], c[2], c[3]);
+      }
+    }
+    if (w + (int)gridDim.x < total) load_inputs(w + gridDim.x);
+    // twist factors of this tile, in flight during the MMA
+    uint32_t tw[SPMAX];
+    if (TWIST) {
+#pragma unroll
+      for (int j = 0; j < SPMAX; ++j) tw[j] = j < a.sp ? __ldg(a.twist + (int64_t)dtr[j] * a.n + t0 + t) : 0u;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    bool ok = true;
+    if (t == 0) {
+      tc_fence_after();
+      for (int k = 0; k < a.kb; ++k) {
+        const uint64_t ad = kmajor_desc(saddr(As + k * 4096));
+        const uint64_t bd = kmajor_desc(saddr(Bs + k * (a.nn / 8) * 256));
+        const uint32_t acc = k > 0, z = 0;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(tmem),
+            "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(z));
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+                   : "memory");
+      // 2. accumulator ready (one waiting thread; the others sleep in the barrier)
+      ok = mbar_wait(bar, phase, abort, a.err, 21);
+    }
+    phase ^= 1;
+    if (__syncthreads_or(!ok)) break;
+    tc_fence_after();
+    // 3. eight target limbs per 32 accumulator columns
+    uint32_t* y = a.out + (int64_t)poly * a.out_ps + t0 + t;
+#pragma unroll
+    for (int ch = 0; ch < SPMAX / 8; ++ch) {
+      if (ch * 32 < a.nn) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + ch * 32, v);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int j = ch * 8 + jj;
+          if (j < a.sp) {
+            const uint32_t q = dq[j], m = dm[j], sw = dsw[j];
+            const uint64_t z = combine4_mad(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+            uint32_t r;
+            if (FAST) {
+              r = reduce_fast(z, q, m, sw);
+              if (TWIST) r = reduce_fast2(r * tw[j], __umulhi(r, tw[j]), q, m, sw);
+            } else {
+              const ModC mc = a.dst[j];
+              r = barrett(z, mc);
+              if (TWIST) r = barrett((uint64_t)r * tw[j], mc);
+            }
+            y[(int64_t)j * a.out_ls] = r;
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+}
+
+// Shared memory of one k_bconv_tc CTA: the A and B tiles plus constants,
+// padded so that no more CTAs fit on an SM (sm_bytes of shared memory, 1 KiB
+// reserved per CTA) than its 512 TMEM columns serve.  0 when impossible.
+size_t bconv_tc_smem(int sq, int sp, int kb, int nn, uint32_t tmem_cols, size_t sm_bytes, int* ctas_per_sm) {
+  const size_t need = 1024 + (size_t)kb * 4096 + (size_t)kb * (nn / 8) * 256 + 16 + (size_t)sp * 16 + 8 +
+                      (size_t)sq * (sizeof(ModC) + 4);
+  const int ctas = (int)(512 / tmem_cols);
+  // (ctas + 1) CTAs of s + 1 KiB each must not fit, ctas of them must
+  const size_t lo = sm_bytes / (ctas + 1), hi = sm_bytes / ctas - 1024;
+  if (lo + 64 > hi) return 0;
+  size_t s = (lo + hi) / 2;
+  if (s < need) s = need;
+  *ctas_per_sm = ctas;
+  return (s > hi) ? 0 : s;
+}
+
+template <bool FAST, bool TWIST, int KB, int SPMAX>
+int launch_bconv_tc(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    CROSS_CHECK_CUDA(cudaGetDevice(&dev));
+    CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  auto kern = k_bconv_tc<FAST, TWIST, KB, SPMAX>;
+  CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t total = (int64_t)a.polys * (a.n / BT_THREADS);
+  const int64_t cap = (int64_t)sms * ctas_per_sm;
+  kern<<<(unsigned)(total < cap ? total : cap), BT_THREADS, smem, st>>>(a);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+template <bool FAST, bool TWIST>
+int launch_bconv_tc_any(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
+  if (a.kb == 1 && a.sp <= 24) return launch_bconv_tc<FAST, TWIST, 1, 24>(a, smem, ctas_per_sm, st);
+  if (a.kb == 1) return launch_bconv_tc<FAST, TWIST, 1, 64>(a, smem, ctas_per_sm, st);
+  return launch_bconv_tc<FAST, TWIST, 4, 64>(a, smem, ctas_per_sm, st);
+}
+
 template <int SQMAX, bool BAT>
 int launch_bconv(const cross_bconv_plan_s* P, bool vec, const uint32_t* in, int64_t in_ps, int64_t in_ls,
                  int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
@@ -148,6 +382,26 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
               int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
               int64_t n, cudaStream_t st, const uint32_t* twist, const uint16_t* trow) {
   if (polys == 0 || n == 0) return CROSS_OK;
+  if (bat && P->tc_bimg && in_ts == 1 && out_ts == 1 && n % BT_THREADS == 0 && polys * (n / BT_THREADS) < (1ll << 31)) {
+    BconvTcArgs a{in, in_ps, in_ls, out, out_ps, out_ls, (int)polys, (int)n, P->sq, P->sp, P->tc_kb, P->tc_nn, 0,
+                  P->src, P->dst, P->qhat_inv, P->tc_bimg, twist, trow, P->err};
+    a.tmem_cols = 64;   // at most 8 CTAs per SM
+    while ((int)a.tmem_cols < a.nn) a.tmem_cols <<= 1;
+    static int sm_bytes = 0;
+    if (!sm_bytes) {
+      int dev = 0;
+      CROSS_CHECK_CUDA(cudaGetDevice(&dev));
+      CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&sm_bytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    }
+    int ctas = 0;
+    const size_t sm = bconv_tc_smem(P->sq, P->sp, P->tc_kb, P->tc_nn, a.tmem_cols, (size_t)sm_bytes, &ctas);
+    if (sm) {
+      const bool f = P->tc_fast != 0;
+      if (twist)
+        return f ? launch_bconv_tc_any<true, true>(a, sm, ctas, st) : launch_bconv_tc_any<false, true>(a, sm, ctas, st);
+      return f ? launch_bconv_tc_any<true, false>(a, sm, ctas, st) : launch_bconv_tc_any<false, false>(a, sm, ctas, st);
+    }
+  }
   const size_t smem = (size_t)P->sp * 4 * P->sq * sizeof(uint32_t);
   if (smem > 200 * 1024 || P->sq > 64) {
     set_error("bconv: size_q=%d size_p=%d exceed the supported tile (size_q <= 64)", P->sq, P->sp);
@@ -199,7 +453,33 @@ int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* 
   for (int i = 0; i < sq; ++i)
     for (int j = 0; j < sp; ++j) qm[(size_t)j * sq + i] = qhat_modp[(size_t)i * sp + j];
   std::vector<uint32_t> qi(qhat_inv_modq, qhat_inv_modq + sq);
+  // tensor-core B operand: row n = 4j + b, K byte 4i + a, in the K-major
+  // no-swizzle core-matrix layout of k_bconv_tc (sq <= 32, sp <= 64)
+  std::vector<uint8_t> bimg;
+  if (sq <= 32 && sp <= 64) {
+    P->tc_kb = (sq + 7) / 8;
+    P->tc_nn = (4 * sp + 15) / 16 * 16;
+    const int kb = P->tc_kb, nn = P->tc_nn;
+    bimg.assign((size_t)kb * (nn / 8) * 256, 0);
+    for (int n = 0; n < 4 * sp; ++n)
+      for (int i = 0; i < sq; ++i) {
+        const uint32_t word = bat[(size_t)n * sq + i];   // bat[j][b][i], n = 4j + b
+        for (int a = 0; a < 4; ++a) {
+          const int kbyte = 4 * i + a, k = kbyte / 32, kk = kbyte % 32;
+          bimg[(size_t)k * (nn / 8) * 256 + (n / 8) * 256 + (kk / 16) * 128 + (n % 8) * 16 + kk % 16] =
+              (uint8_t)(word >> (8 * a));
+        }
+      }
+    bool fast = true;
+    for (const ModC& mc : P->dst_host) fast = fast && reduce_fast_ok(mc);
+    for (const ModC& mc : P->src_host) fast = fast && barrett_w32_ok(mc);
+    P->tc_fast = fast ? 1 : 0;
+  }
+  std::vector<int> zero(1, 0);
   int rc = upload_vec(&P->src, P->src_host);
+  if (!rc) rc = upload(&P->err, zero.data(), 1);
+  if (!rc && !bimg.empty() && !(getenv("CROSS_B200_DISABLE_TC") && getenv("CROSS_B200_DISABLE_TC")[0] == '1'))
+    rc = upload_vec(&P->tc_bimg, bimg);
   if (!rc) rc = upload_vec(&P->dst, P->dst_host);
   if (!rc) rc = upload_vec(&P->qhat_inv, qi);
   if (!rc) rc = upload_vec(&P->bat, bat);
@@ -219,7 +499,22 @@ int cross_bconv_plan_destroy(cross_bconv_plan P) {
   dfree(P->qhat_inv);
   dfree(P->bat);
   dfree(P->qhat_modp);
+  dfree(P->tc_bimg);
+  dfree(P->err);
   delete P;
+  return CROSS_OK;
+}
+
+int cross_bconv_plan_check(cross_bconv_plan P) {
+  CROSS_REQUIRE(P, "cross_bconv_plan_check: null plan");
+  int e = 0;
+  CROSS_CHECK_CUDA(cudaMemcpy(&e, P->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    const int zero = 0;
+    CROSS_CHECK_CUDA(cudaMemcpy(P->err, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    set_error("tensor-core basis conversion: a bounded wait expired (code %d); output invalid", e);
+    return CROSS_ERR_TIMEOUT;
+  }
   return CROSS_OK;
 }
 

@@ -48,6 +48,10 @@ struct cross_ntt_plan_s {
 
 struct cross_bconv_plan_s {
   int sq = 0, sp = 0;
+  int tc_fast = 0;                  // tensor-core kernel may use reduce_fast / barrett_w32
+  int tc_kb = 0, tc_nn = 0;         // K blocks of 8 source limbs, MMA N (4 sp rounded up to 16)
+  uint8_t* tc_bimg = nullptr;       // B operand in its shared-memory image (K-major, no swizzle)
+  int* err = nullptr;               // device error word of the tensor-core kernel
   std::vector<cross::ModC> src_host, dst_host;
   cross::ModC* src = nullptr;       // [sq]
   cross::ModC* dst = nullptr;       // [sp]
@@ -57,6 +61,22 @@ struct cross_bconv_plan_s {
 };
 
 namespace cross {
+
+// reduce_fast (tc_ptx.cuh) returns finite_field.py's Barrett value exactly for
+// modulus mc when the true remainder z - t q stays inside (-(2^32 - q), 2^32)
+// for every input: with t = floor(z m / 2^s) and m within one of 2^s / q,
+// |r| < (z / 2^s + 2) q, checked here for z < 2^53 and z < 2^31 q.
+inline bool reduce_fast_ok(const ModC& mc) {
+  if (mc.w != 32 || mc.s_w >= 32 || mc.m >= (1ull << 32)) return false;
+  const unsigned __int128 q = mc.q;
+  const unsigned s_bits = mc.w + mc.s_w;
+  const unsigned __int128 lim = ((unsigned __int128)1 << 32) - q;
+  for (unsigned __int128 z : {(unsigned __int128)1 << 53, ((unsigned __int128)1 << 31) * q})
+    if (((z >> s_bits) + 3) * q >= lim) return false;
+  return true;
+}
+// barrett_w32 (common.cuh) equals barrett for this modulus.
+inline bool barrett_w32_ok(const ModC& mc) { return mc.w == 32 && mc.m < (1ull << 32); }
 
 // Bump allocator over a caller-provided workspace (or a size query when
 // base == nullptr).

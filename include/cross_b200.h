@@ -182,6 +182,11 @@ int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* 
                             cross_bconv_plan* out);
 int cross_bconv_plan_destroy(cross_bconv_plan plan);
 
+/* Reports (and clears) the error word of the plan's tensor-core kernel:
+ * CROSS_OK, or CROSS_ERR_TIMEOUT when its bounded wait expired (that launch
+ * stopped early and its output is invalid).  Synchronises the device. */
+int cross_bconv_plan_check(cross_bconv_plan plan);
+
 /* BConv.basis_change_bat (bconv.py:215-252) when bat != 0, else
  * BConv.basis_change (bconv.py:173-212).  CROSS_LAYOUT_REFERENCE:
  * in (batch, n, size_q) -> out (batch, n, size_p);  CROSS_LAYOUT_LIMB_MAJOR:

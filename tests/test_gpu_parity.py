@@ -175,6 +175,35 @@ def test_bconv_vs_oracle(n, sq, sp, batch):
     np.testing.assert_array_equal(_np(b.basis_change(x)), o.basis_change(x))
 
 
+@pytest.mark.parametrize("n,sq,sp,batch", [(4096, 8, 23, 3), (1024, 7, 24, 2), (128, 8, 8, 5), (4096, 16, 40, 2),
+                                           (256, 3, 5, 4), (1024, 32, 64, 1), (65536, 8, 23, 2)])
+def test_bconv_limb_major_tensor_core(monkeypatch, n, sq, sp, batch):
+    """Limb-major BConv with contiguous coefficients (n % 128 == 0) runs the
+    tcgen05 kernel: bit-exact against the oracle and the dp4a kernel."""
+    import torch
+    from cross_b200 import bconv, _lib
+    ov = O.find_moduli_ntt(sq + sp, 28, 2 * n)
+    x = rng_residues(np.random.default_rng(n + sq + sp), (batch, n, sq), ov[:sq])
+    o = O.BConvBarrett(ov)
+    o.control_gen([(list(range(sq)), list(range(sq, sq + sp)))])
+    want = o.basis_change_bat(x).transpose(0, 2, 1)
+    xl = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 1))).cuda()
+
+    def run():
+        b = bconv.BConvBarrett(ov)
+        b.control_gen([(list(range(sq)), list(range(sq, sq + sp)))])
+        out = torch.empty((batch, sp, n), dtype=xl.dtype, device="cuda")
+        _lib.check(_lib.lib().cross_bconv(b.plan(0), 1, xl.data_ptr(), out.data_ptr(), batch, n,
+                                          _lib.LAYOUT_LIMB_MAJOR, None), "cross_bconv")
+        got = _np(out)
+        b.check_device()
+        return got
+
+    np.testing.assert_array_equal(run(), want)
+    monkeypatch.setenv("CROSS_B200_DISABLE_TC", "1")
+    np.testing.assert_array_equal(run(), want)
+
+
 # ---------------------------------------------------------------------------
 # Elementwise
 # ---------------------------------------------------------------------------
