@@ -129,9 +129,17 @@ __global__ void __launch_bounds__(256) k_transpose_ref(const uint32_t* __restric
     const uint32_t* ref_in = in + p * n * L + t0 * L;
     const uint32_t* lm_in = in + p * L * n + t0;
     if (TO_LM) {
-      for (int k = threadIdx.x; k < per; k += blockDim.x) {
-        const int t = (int)(((float)k + 0.5f) * inv), l = k - t * L;
-        sm[t * ld + l] = ref_in[k];
+      // 16-byte loads of the contiguous reference-layout run (t0 * L words in,
+      // t0 a multiple of TT, so every run starts 16-byte aligned)
+      for (int k4 = threadIdx.x; k4 < per / 4; k4 += blockDim.x) {
+        const uint4 v = reinterpret_cast<const uint4*>(ref_in)[k4];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = 4 * k4 + e;
+          const int t = (int)(((float)k + 0.5f) * inv), l = k - t * L;
+          sm[t * ld + l] = w[e];
+        }
       }
     } else {
       for (int l = threadIdx.x / TT; l < L; l += blockDim.x / TT) sm[(threadIdx.x % TT) * ld + l] = lm_in[(int64_t)l * n + threadIdx.x % TT];
@@ -142,9 +150,15 @@ __global__ void __launch_bounds__(256) k_transpose_ref(const uint32_t* __restric
       for (int l = threadIdx.x / TT; l < L; l += blockDim.x / TT) o[(int64_t)l * n + threadIdx.x % TT] = sm[(threadIdx.x % TT) * ld + l];
     } else {
       uint32_t* o = out + p * n * L + t0 * L;
-      for (int k = threadIdx.x; k < per; k += blockDim.x) {
-        const int t = (int)(((float)k + 0.5f) * inv), l = k - t * L;
-        o[k] = sm[t * ld + l];
+      for (int k4 = threadIdx.x; k4 < per / 4; k4 += blockDim.x) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = 4 * k4 + e;
+          const int t = (int)(((float)k + 0.5f) * inv), l = k - t * L;
+          w[e] = sm[t * ld + l];
+        }
+        reinterpret_cast<uint4*>(o)[k4] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
     __syncthreads();
@@ -241,7 +255,9 @@ int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows
     return CROSS_ERR_UNSUPPORTED;
   }
   // (P, N, L) <-> (P, L, N) with few limbs: the coalesced tile kernel
-  const bool to_lm = cols <= TT_MAX_L && rows % TT == 0, to_ref = rows <= TT_MAX_L && cols % TT == 0;
+  // (16-byte accesses on the contiguous side need 16-byte aligned buffers)
+  const bool al = (((uintptr_t)in | (uintptr_t)out) & 15) == 0;
+  const bool to_lm = al && cols <= TT_MAX_L && rows % TT == 0, to_ref = al && rows <= TT_MAX_L && cols % TT == 0;
   if (to_lm || to_ref) {
     const int64_t n = to_lm ? rows : cols;
     const int L = (int)(to_lm ? cols : rows);

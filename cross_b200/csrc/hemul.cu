@@ -21,6 +21,18 @@ struct PartPtrs {
   int64_t ps[MAXPARTS];          // E_j poly stride (words)
 };
 
+// Barrett of finite_field.py:224-230; W32 selects the 32-bit form, exact when
+// every modulus of the launch has w = 32 and m < 2^32 (plan_w32).
+template <bool W32>
+__device__ __forceinline__ uint32_t red(uint64_t z, const ModC& mc) {
+  return W32 ? barrett_w32(z, (uint32_t)mc.q, (uint32_t)mc.m, mc.s_w) : barrett(z, mc);
+}
+bool plan_w32(const cross_ntt_plan_s* p) {
+  for (const ModC& mc : p->mods_host)
+    if (!barrett_w32_ok(mc)) return false;
+  return true;
+}
+
 unsigned gx_for(int64_t nv) {
   int64_t g = (nv + T - 1) / T;
   return (unsigned)(g < 1 ? 1 : (g > 64 ? 64 : g));
@@ -28,34 +40,44 @@ unsigned gx_for(int64_t nv) {
 unsigned gy_for(int64_t rows) { return (unsigned)(rows < 65535 ? rows : 65535); }
 
 // ciphertext.py:279-295: centred lift of the last limb into every q_i,
-// times gamma_i psi_i^t, Barrett.  LL: [polys][N]; out: [polys][L1][N].
+// times gamma_i psi_i^t, Barrett.  LL: [polys][N]; out: [polys][L1][N].  A
+// thread reads its four last-limb words once and writes them lifted into all
+// L1 limbs (two limbs per step, table loads ahead of the arithmetic).
+template <bool W32>
 __global__ void k_rescale_lift(const uint32_t* __restrict__ LL, uint32_t* __restrict__ out, int64_t polys,
                                int L1, int64_t n, uint32_t thr, uint32_t q_last,
                                const uint32_t* __restrict__ gpsi, const ModC* __restrict__ mods) {
-  const int64_t nv = n >> 2, rows = polys * L1;
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    const int64_t p = row / L1;
-    const int i = (int)(row % L1);
-    const ModC mc = mods[i];
-    const uint4* src = (const uint4*)(LL + p * n);
-    const uint4* g = (const uint4*)(gpsi + (size_t)i * n);
-    uint4* dst = (uint4*)(out + row * n);
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
-      const uint4 x = src[v], t = g[v];
+  const int64_t nv = n >> 2;
+  for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < polys * nv;
+       w += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = w / nv, v = w - p * nv;
+    const uint4 x = reinterpret_cast<const uint4*>(LL + p * n)[v];
+    uint4* dst = reinterpret_cast<uint4*>(out + p * L1 * n) + v;
+    auto one = [&](int i, const uint4 t) {
+      const ModC mc = mods[i];
       auto lift = [&](uint32_t a) -> uint64_t {
         return a < thr ? (uint64_t)a : (mc.q - (uint64_t)q_last + (uint64_t)a);
       };
       uint4 o;
-      o.x = barrett_any(lift(x.x) * t.x, mc);
-      o.y = barrett_any(lift(x.y) * t.y, mc);
-      o.z = barrett_any(lift(x.z) * t.z, mc);
-      o.w = barrett_any(lift(x.w) * t.w, mc);
-      dst[v] = o;
+      o.x = red<W32>(lift(x.x) * t.x, mc);
+      o.y = red<W32>(lift(x.y) * t.y, mc);
+      o.z = red<W32>(lift(x.z) * t.z, mc);
+      o.w = red<W32>(lift(x.w) * t.w, mc);
+      dst[(int64_t)i * (n >> 2)] = o;
+    };
+    int i = 0;
+    for (; i + 1 < L1; i += 2) {
+      const uint4 t0 = reinterpret_cast<const uint4*>(gpsi + (size_t)i * n)[v];
+      const uint4 t1 = reinterpret_cast<const uint4*>(gpsi + (size_t)(i + 1) * n)[v];
+      one(i, t0);
+      one(i + 1, t1);
     }
+    if (i < L1) one(i, reinterpret_cast<const uint4*>(gpsi + (size_t)i * n)[v]);
   }
 }
 
 // ciphertext.py:309-324 on [b][4][L1][N] -> D [b][3][L1][N].
+template <bool W32>
 __global__ void k_tensor_lm(const uint32_t* __restrict__ R, uint32_t* __restrict__ D, int64_t batch, int L1,
                             int64_t n, const ModC* __restrict__ mods) {
   const int64_t nv = n >> 2, rows = batch * L1, es = (int64_t)L1 * n;
@@ -70,9 +92,9 @@ __global__ void k_tensor_lm(const uint32_t* __restrict__ R, uint32_t* __restrict
       const uint4 b0 = ((const uint4*)(base + 2 * es))[v], b1 = ((const uint4*)(base + 3 * es))[v];
       uint4 d0, d1, d2;
 #define TP(c)                                                                   \
-  d0.c = barrett_any((uint64_t)a0.c * b0.c, mc);                                \
-  d1.c = barrett_any((uint64_t)a0.c * b1.c + (uint64_t)a1.c * b0.c, mc);        \
-  d2.c = barrett_any((uint64_t)a1.c * b1.c, mc);
+  d0.c = red<W32>((uint64_t)a0.c * b0.c, mc);                                  \
+  d1.c = red<W32>((uint64_t)a0.c * b1.c + (uint64_t)a1.c * b0.c, mc);          \
+  d2.c = red<W32>((uint64_t)a1.c * b1.c, mc);
       TP(x) TP(y) TP(z) TP(w)
 #undef TP
       ((uint4*)ob)[v] = d0;
@@ -86,14 +108,59 @@ __global__ void k_tensor_lm(const uint32_t* __restrict__ R, uint32_t* __restrict
 // for every limb l of Q'+P, ext_j(l) is the NTT-form input limb when l is in
 // digit j and the ModUp result otherwise; acc0 = sum_j ext_j * evk_b[j],
 // acc1 = sum_j ext_j * evk_a[j] in uint64, then Barrett.
+// Rows are walked limb-major (all ciphertexts of one limb together) so the
+// limb's evaluation-key rows are read from HBM once per launch and from L2 for
+// the rest of the batch.
+template <bool W32, int NPMAX>
 __global__ void k_ks_inner(LP dig, PartPtrs parts, int nparts, const int16_t* __restrict__ src, int LT,
                            int64_t n, int64_t batch, const uint32_t* __restrict__ evka,
                            const uint32_t* __restrict__ evkb, uint32_t* __restrict__ KS,
                            const ModC* __restrict__ mods) {
   const int64_t nv = n >> 2, rows = batch * LT;
   for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    const int64_t b = row / LT;
-    const int l = (int)(row % LT);
+    const int l = (int)(row / batch);
+    const int64_t b = row - (int64_t)l * batch;
+    const ModC mc = mods[l];
+    uint4* o0 = (uint4*)(KS + (b * 2 * LT + l) * n);
+    uint4* o1 = (uint4*)(KS + (b * 2 * LT + LT + l) * n);
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      uint64_t s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+      uint4 e[NPMAX], kb[NPMAX], ka[NPMAX];
+#pragma unroll
+      for (int j = 0; j < NPMAX; ++j) {
+        if (j < nparts) {
+          const int s = src[j * LT + l];
+          e[j] = s < 0 ? ((const uint4*)(dig.p + b * dig.ps + (int64_t)l * dig.ss))[v]
+                       : ((const uint4*)(parts.e[j] + b * parts.ps[j] + (int64_t)s * n))[v];
+          kb[j] = ((const uint4*)(evkb + ((size_t)j * LT + l) * n))[v];
+          ka[j] = ((const uint4*)(evka + ((size_t)j * LT + l) * n))[v];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NPMAX; ++j) {
+        if (j < nparts) {
+          s0[0] += (uint64_t)e[j].x * kb[j].x; s0[1] += (uint64_t)e[j].y * kb[j].y;
+          s0[2] += (uint64_t)e[j].z * kb[j].z; s0[3] += (uint64_t)e[j].w * kb[j].w;
+          s1[0] += (uint64_t)e[j].x * ka[j].x; s1[1] += (uint64_t)e[j].y * ka[j].y;
+          s1[2] += (uint64_t)e[j].z * ka[j].z; s1[3] += (uint64_t)e[j].w * ka[j].w;
+        }
+      }
+      o0[v] = make_uint4(red<W32>(s0[0], mc), red<W32>(s0[1], mc), red<W32>(s0[2], mc), red<W32>(s0[3], mc));
+      o1[v] = make_uint4(red<W32>(s1[0], mc), red<W32>(s1[1], mc), red<W32>(s1[2], mc), red<W32>(s1[3], mc));
+    }
+  }
+}
+
+// k_ks_inner for more than four digits: one digit at a time.
+template <bool W32>
+__global__ void k_ks_inner_loop(LP dig, PartPtrs parts, int nparts, const int16_t* __restrict__ src, int LT,
+                                int64_t n, int64_t batch, const uint32_t* __restrict__ evka,
+                                const uint32_t* __restrict__ evkb, uint32_t* __restrict__ KS,
+                                const ModC* __restrict__ mods) {
+  const int64_t nv = n >> 2, rows = batch * LT;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int l = (int)(row / batch);
+    const int64_t b = row - (int64_t)l * batch;
     const ModC mc = mods[l];
     uint4* o0 = (uint4*)(KS + (b * 2 * LT + l) * n);
     uint4* o1 = (uint4*)(KS + (b * 2 * LT + LT + l) * n);
@@ -110,10 +177,30 @@ __global__ void k_ks_inner(LP dig, PartPtrs parts, int nparts, const int16_t* __
         s1[0] += (uint64_t)e.x * ka.x; s1[1] += (uint64_t)e.y * ka.y;
         s1[2] += (uint64_t)e.z * ka.z; s1[3] += (uint64_t)e.w * ka.w;
       }
-      o0[v] = make_uint4(barrett_any(s0[0], mc), barrett_any(s0[1], mc), barrett_any(s0[2], mc), barrett_any(s0[3], mc));
-      o1[v] = make_uint4(barrett_any(s1[0], mc), barrett_any(s1[1], mc), barrett_any(s1[2], mc), barrett_any(s1[3], mc));
+      o0[v] = make_uint4(red<W32>(s0[0], mc), red<W32>(s0[1], mc), red<W32>(s0[2], mc), red<W32>(s0[3], mc));
+      o1[v] = make_uint4(red<W32>(s1[0], mc), red<W32>(s1[1], mc), red<W32>(s1[2], mc), red<W32>(s1[3], mc));
     }
   }
+}
+
+// Launches the key-switch inner product over batch x LT rows.
+int ks_inner(bool w32, LP dig, const PartPtrs& pp, int nparts, const int16_t* src, int LT, int64_t n, int64_t B,
+             const uint32_t* evka, const uint32_t* evkb, uint32_t* KS, const ModC* mods, cudaStream_t st) {
+  const dim3 g(gx_for(n >> 2), gy_for(B * LT));
+  if (nparts <= 4) {
+    if (w32)
+      k_ks_inner<true, 4><<<g, T, 0, st>>>(dig, pp, nparts, src, LT, n, B, evka, evkb, KS, mods);
+    else
+      k_ks_inner<false, 4><<<g, T, 0, st>>>(dig, pp, nparts, src, LT, n, B, evka, evkb, KS, mods);
+  } else {
+    if (w32)
+      k_ks_inner_loop<true><<<g, T, 0, st>>>(dig, pp, nparts, src, LT, n, B, evka, evkb, KS, mods);
+    else
+      k_ks_inner_loop<false><<<g, T, 0, st>>>(dig, pp, nparts, src, LT, n, B, evka, evkb, KS, mods);
+  }
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
 }
 
 // out[p][l][j] = in[p][l][map[j]] (limb-major automorphism, jnp.take semantics).
@@ -174,8 +261,14 @@ int rescale_run(const RescaleArgs& a, const uint32_t* X, int64_t xps, uint32_t* 
   if ((rc = ntt_exec(a.ntt, true, LP{X + (int64_t)L1 * N, xps, 0}, COEF_NATURAL, LPo{LL, N, 0}, COEF_TRANSPOSED, polys,
                      1, a.m_last, twist, tmp, st)))
     return rc;
-  k_rescale_lift<<<dim3(gx_for(nv), gy_for(polys * L1)), T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last,
-                                                                      a.gamma_psi_t, a.mods_q1);
+  {
+    int64_t gb = (polys * nv + T - 1) / T;
+    const unsigned g = (unsigned)(gb < 148 * 16 ? gb : 148 * 16);
+    if (plan_w32(a.ntt))
+      k_rescale_lift<true><<<g, T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last, a.gamma_psi_t, a.mods_q1);
+    else
+      k_rescale_lift<false><<<g, T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last, a.gamma_psi_t, a.mods_q1);
+  }
   count_launch();
   Epi comb;
   comb.op = EPI_COMBINE;
@@ -436,7 +529,11 @@ int cross_hemul(cross_hemul_plan P, const uint32_t* in, uint32_t* out, int64_t B
     if ((rc = rescale_run(ra, X, (int64_t)L * N, b.R, b.LL, b.tmp, B * 4, st))) return rc;
   }
   // 2. tensor product (ciphertext.py:309-324)
-  k_tensor_lm<<<dim3(gx_for(nv), gy_for(B * L1)), blk, 0, st>>>(b.R, b.D, B, L1, N, P->mods_dle);
+  const bool w32 = plan_w32(P->ntt_qp);
+  if (w32)
+    k_tensor_lm<true><<<dim3(gx_for(nv), gy_for(B * L1)), blk, 0, st>>>(b.R, b.D, B, L1, N, P->mods_dle);
+  else
+    k_tensor_lm<false><<<dim3(gx_for(nv), gy_for(B * L1)), blk, 0, st>>>(b.R, b.D, B, L1, N, P->mods_dle);
   count_launch();
   // 3. key switch on d2 (ciphertext.py:455-519): INTT x psi^-i (fused, transposed
   // coefficients) -> per digit BConv x psi^i (fused) -> NTT -> inner product
@@ -462,9 +559,9 @@ int cross_hemul(cross_hemul_plan P, const uint32_t* in, uint32_t* out, int64_t B
     pp.e[j] = b.E[j];
     pp.ps[j] = eps;
   }
-  k_ks_inner<<<dim3(gx_for(nv), gy_for(B * LT)), blk, 0, st>>>(LP{D2, Dps, N}, pp, P->parts, P->ks_src, LT, N, B,
-                                                               P->evk_a, P->evk_b, b.KS, P->mods_dle);
-  count_launch();
+  if ((rc = ks_inner(w32, LP{D2, Dps, N}, pp, P->parts, P->ks_src, LT, N, B, P->evk_a, P->evk_b, b.KS, P->mods_dle,
+                     st)))
+    return rc;
   // 4. ModDown (hemul.py:175-215): INTT of the P limbs of both elements x psi^-i
   // -> BConv P -> Q' x psi^i -> NTT whose last stage applies the subtraction, the
   // P^-1 scaling and the add of (d0, d1).  Element e of ciphertext b is e' = 2b + e.
@@ -677,7 +774,6 @@ int cross_herot(cross_herot_plan P, const uint32_t* in, uint32_t* out, int64_t B
     if ((rc = transpose_u32(in, b.X, B * 2, N, L, st))) return rc;
     X = b.X;
   }
-  const int64_t nv = N / 4;
   const dim3 blk(T);
   const int64_t Xps = 2 * (int64_t)L * N;
   const uint32_t* X1 = X + (int64_t)L * N;   // in_tower = element 1 (herot.py:201)
@@ -703,9 +799,9 @@ int cross_herot(cross_herot_plan P, const uint32_t* in, uint32_t* out, int64_t B
     pp.e[j] = b.E[j];
     pp.ps[j] = eps;
   }
-  k_ks_inner<<<dim3(gx_for(nv), gy_for(B * LT)), blk, 0, st>>>(LP{X1, Xps, N}, pp, P->parts, P->ks_src, LT, N, B,
-                                                               P->evk_a, P->evk_b, b.KS, P->ntt->mods);
-  count_launch();
+  if ((rc = ks_inner(plan_w32(P->ntt), LP{X1, Xps, N}, pp, P->parts, P->ks_src, LT, N, B, P->evk_a, P->evk_b, b.KS,
+                     P->ntt->mods, st)))
+    return rc;
   // 2. ModDown of both elements (herot.py:255-289) and c0 += ModDown_0
   // (herot.py:292-296), the tail fused into the last NTT stage.
   const int64_t KSes = (int64_t)LT * N;

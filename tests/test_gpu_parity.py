@@ -421,6 +421,13 @@ def test_layout_conversions(polys, n, L):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(lm.cpu().numpy(), x.transpose(0, 2, 1))
     np.testing.assert_array_equal(back.cpu().numpy(), x)
+    # buffers offset by one word (not 16-byte aligned) take the generic kernel
+    xo = torch.zeros(polys * n * L + 1, dtype=xd.dtype, device="cuda")
+    xo[1:] = xd.reshape(-1)
+    lo = torch.zeros(polys * n * L + 1, dtype=xd.dtype, device="cuda")
+    _lib.check(lib.cross_to_limb_major(xo.data_ptr() + 4, lo.data_ptr() + 4, polys, n, L, None), "cross_to_limb_major")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(lo[1:].cpu().numpy().reshape(polys, L, n), x.transpose(0, 2, 1))
 
 
 def test_errors_are_reference_exceptions():
