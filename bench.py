@@ -175,9 +175,8 @@ def main():
 
     import numpy as np
     import torch
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from cross_b200 import shard
+    world, rank, local = shard.rank_env()
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -219,11 +218,7 @@ def main():
         torch.cuda.synchronize()
         h1 = time.time()
         launches = lib.cross_launch_count() - l0
-    ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
     value = world * batch * args.steps / (ms / 1000.0)
 
     # e2e through the public API with pinned host buffers (H2D + compute + D2H).
@@ -244,11 +239,7 @@ def main():
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
-    ems = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ems], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
+    ems = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
     e2e = world * batch * args.steps / (ems / 1000.0)
 
     # Dominant kernel: the tensor-core BAT contraction.  One forward NTT in the

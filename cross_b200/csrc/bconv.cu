@@ -172,22 +172,15 @@ __global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
   uint64_t* bar = reinterpret_cast<uint64_t*>(Bs + a.kb * (a.nn / 8) * 256);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
   volatile int& abort = *reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint32_t* dq = tmem_slot + 2;          // [sp] target q, m, s_w, twist row
-  uint32_t* dm = dq + a.sp;
-  uint32_t* dsw = dm + a.sp;
-  uint32_t* dtr = dsw + a.sp;
-  ModC* sc = reinterpret_cast<ModC*>((reinterpret_cast<uintptr_t>(dtr + a.sp) + 7) & ~uintptr_t(7));   // [sq] source moduli
+  uint4* dc = reinterpret_cast<uint4*>(tmem_slot + 2);   // [sp] target {q, m, s_w, twist row}
+  ModC* sc = reinterpret_cast<ModC*>(dc + a.sp);          // [sq] source moduli
   uint32_t* shi = reinterpret_cast<uint32_t*>(sc + a.sq);        // [sq] QHatInvModq
   const int t = threadIdx.x, warp = t >> 5;
 
   for (int i = t; i < a.kb * (a.nn / 8) * 16; i += BT_THREADS)
     reinterpret_cast<uint4*>(Bs)[i] = reinterpret_cast<const uint4*>(a.bimg)[i];
-  for (int j = t; j < a.sp; j += BT_THREADS) {
-    dq[j] = (uint32_t)a.dst[j].q;
-    dm[j] = (uint32_t)a.dst[j].m;
-    dsw[j] = a.dst[j].s_w;
-    dtr[j] = TWIST ? a.trow[j] : 0u;
-  }
+  for (int j = t; j < a.sp; j += BT_THREADS)
+    dc[j] = make_uint4((uint32_t)a.dst[j].q, (uint32_t)a.dst[j].m, a.dst[j].s_w, TWIST ? a.trow[j] : 0u);
   for (int i = t; i < a.sq; i += BT_THREADS) {
     sc[i] = a.src[i];
     shi[i] = a.qhat_inv[i];
@@ -248,7 +241,7 @@ __global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
     uint32_t tw[SPMAX];
     if (TWIST) {
 #pragma unroll
-      for (int j = 0; j < SPMAX; ++j) tw[j] = j < a.sp ? __ldg(a.twist + (int64_t)dtr[j] * a.n + t0 + t) : 0u;
+      for (int j = 0; j < SPMAX; ++j) tw[j] = j < a.sp ? __ldg(a.twist + (int64_t)dc[j].w * a.n + t0 + t) : 0u;
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
@@ -285,7 +278,8 @@ __global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
         for (int jj = 0; jj < 8; ++jj) {
           const int j = ch * 8 + jj;
           if (j < a.sp) {
-            const uint32_t q = dq[j], m = dm[j], sw = dsw[j];
+            const uint4 cj = dc[j];
+            const uint32_t q = cj.x, m = cj.y, sw = cj.z;
             const uint64_t z = combine4_mad(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
             uint32_t r;
             if (FAST) {
@@ -313,7 +307,7 @@ __global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
 // padded so that no more CTAs fit on an SM (sm_bytes of shared memory, 1 KiB
 // reserved per CTA) than its 512 TMEM columns serve.  0 when impossible.
 size_t bconv_tc_smem(int sq, int sp, int kb, int nn, uint32_t tmem_cols, size_t sm_bytes, int* ctas_per_sm) {
-  const size_t need = 1024 + (size_t)kb * 4096 + (size_t)kb * (nn / 8) * 256 + 16 + (size_t)sp * 16 + 8 +
+  const size_t need = 1024 + (size_t)kb * 4096 + (size_t)kb * (nn / 8) * 256 + 16 + (size_t)sp * 16 +
                       (size_t)sq * (sizeof(ModC) + 4);
   const int ctas = (int)(512 / tmem_cols);
   // (ctas + 1) CTAs of s + 1 KiB each must not fit, ctas of them must

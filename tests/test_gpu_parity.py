@@ -366,11 +366,13 @@ def test_herot_vs_oracle(n, L, K, dnum, batch, k):
     np.testing.assert_array_equal(_np(h.rotate(ct)), ref.rotate(ct))
 
 
-def test_hemul_full_size_vs_oracle():
-    """The benchmark parameter set (N = 2^16, L = 24, K = 8, dnum = 3) for one
-    ciphertext, bit-exact against the oracle."""
+@pytest.mark.parametrize("L,K,dnum", [(24, 8, 3), (35, 7, 5)])
+def test_hemul_full_size_vs_oracle(L, K, dnum):
+    """N = 2^16 parameter sets for one ciphertext, bit-exact against the oracle:
+    the benchmark point (L = 24, K = 8, dnum = 3) and the multi-GPU box point
+    (L = 35, K = 7, dnum = 5)."""
     from cross_b200 import hemul
-    n, L, K, dnum = 65536, 24, 8, 3
+    n = 65536
     ov = O.find_moduli_ntt(L + K, 28, 2 * n)
     Q, P = ov[:L], ov[L:]
     rng = np.random.default_rng(2024)
@@ -384,6 +386,28 @@ def test_hemul_full_size_vs_oracle():
     ref = O.HEMul(1, 256, 256, dnum, 1, Q, P)
     ref.setup_relinearization(evk_a, evk_b)
     np.testing.assert_array_equal(got, ref.mul(ct))
+
+
+def test_herot_full_size_vs_oracle():
+    """HE-Rotate at N = 2^16, L = 24, K = 8, dnum = 3 for one ciphertext and a
+    seeded rotation index, bit-exact against the oracle."""
+    from cross_b200 import herot, util
+    n, L, K, dnum = 65536, 24, 8, 3
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    Q, P = ov[:L], ov[L:]
+    rng = np.random.default_rng(0)
+    k = int(rng.integers(1, n // 2))
+    ct = rng_residues(rng, (1, 2, 256, 256, L), Q)
+    evk_a = rng_residues(rng, (dnum, n, L + K), ov)
+    evk_b = rng_residues(rng, (dnum, n, L + K), ov)
+    cm = util.precompute_auto_map(n, util.find_automorphism_index_2n_complex(k, 2 * n))
+    h = herot.HERot(256, 256, dnum, Q, P)
+    h.control_gen(batch=1, degree_layout=(256, 256))
+    h.setup_rotate(evk_a, evk_b, cm)
+    ref = O.HERot(256, 256, dnum, Q, P)
+    ref.control_gen(1)
+    ref.setup_rotate(evk_a.reshape(dnum, 256, 256, -1), evk_b.reshape(dnum, 256, 256, -1), cm)
+    np.testing.assert_array_equal(_np(h.rotate(ct)), ref.rotate(ct))
 
 
 def test_limb_major_layout_matches_reference_layout():
