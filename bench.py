@@ -24,6 +24,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 N_DEG, R, C, L, K, DNUM, BATCH = 65536, 256, 256, 24, 8, 3, 64
+# DRAM bytes (read + write) per k_bat_tc2 launch of the roofline NTT at batch 64,
+# from profiles/k_bat_tc2_ntt_n65536.md (batch-16 ncu capture scaled by 4).
+TRAFFIC_PER_LAUNCH = 3.242e9
 METRIC = "HE-Mult/s (N=2^16, L=24, dnum=3)"
 WORKLOAD = "CKKS HE-Mult + relinearisation, N=2^16 (256x256), L=24 x 28-bit, K=8, dnum=3, batch 64 per GPU"
 
@@ -292,7 +295,8 @@ def main():
         "roofline": {"kernel": "k_bat_tc2 tensor-core BAT contraction (NTT column + row stage launches), "
                                "23 limbs x 256 polys, N=2^16",
                      "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
-                     "frac": achieved / int8_peak, "traffic": None,
+                     "frac": achieved / int8_peak, "traffic": TRAFFIC_PER_LAUNCH,
+                     "traffic_unit": "bytes per launch (ncu dram read + write)",
                      "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); no int8 measurement on this pool",
                      "launches": ntt_launches, "ms_per_launch": ntt_ms / max(ntt_launches, 1),
                      "algorithmic_ops_per_launch": ops / max(ntt_launches, 1)},
