@@ -236,9 +236,23 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[(int64_t)(chunk * 8 + j) * a.rows_m] = res[j];
       } else {
-        uint4* dst = reinterpret_cast<uint4*>(o + chunk * 8);
-        dst[0] = make_uint4(res[0], res[1], res[2], res[3]);
-        dst[1] = make_uint4(res[4], res[5], res[6], res[7]);
+        // Lanes 2k and 2k+1 hold rows m and m+1 (1 KiB or more apart), eight
+        // outputs each.  They swap halves so that each store instruction
+        // writes whole 32-byte row segments: the first store row m
+        // (even lane: its outputs 0-3, odd lane: the even lane's 4-7), the
+        // second row m+1.
+        const int odd = lane & 1;
+        const uint4 lo = make_uint4(res[0], res[1], res[2], res[3]);
+        const uint4 hi = make_uint4(res[4], res[5], res[6], res[7]);
+        const uint4 x = odd ? lo : hi;
+        uint4 y;
+        y.x = __shfl_xor_sync(0xffffffffu, x.x, 1);
+        y.y = __shfl_xor_sync(0xffffffffu, x.y, 1);
+        y.z = __shfl_xor_sync(0xffffffffu, x.z, 1);
+        y.w = __shfl_xor_sync(0xffffffffu, x.w, 1);
+        uint32_t* base = o + chunk * 8 + odd * 4;
+        *reinterpret_cast<uint4*>(base - (int64_t)odd * a.nout) = odd ? y : lo;
+        *reinterpret_cast<uint4*>(base + (int64_t)(1 - odd) * a.nout) = odd ? hi : y;
       }
     }
   }
