@@ -9,6 +9,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import _lib, _tensor, util
+from ._pipeline import HostPipeline
 from .bconv import BConvBarrett
 from .finite_field import BarrettContext
 from .ntt_mm import NTTCiphertextBarrettContext
@@ -53,6 +54,8 @@ class HEMul:
         self.extend_moduli = list(extend_moduli)
         self.last_tower_moduli = self.original_moduli[-1]
         self._plan = None
+        self._host = None
+        self._host_ws = None
 
     def control_gen(self, degree_layout=None, perf_test=False):
         """hemul.py:24-132 (perf_test keeps the real constants: same cost)."""
@@ -130,13 +133,21 @@ class HEMul:
     def workspace_size(self, batch: int, layout: int = _lib.LAYOUT_REFERENCE) -> int:
         return int(_lib.lib().cross_hemul_workspace_size(self._plan, batch, layout))
 
-    def mul(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE):
+    def mul(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE, chunk: int = 8,
+            sync: bool = True):
         """hemul.py:153-217: (B, 4, r, c, L) uint32 -> (B, 2, r, c, L-1) uint32.
 
         With layout=LAYOUT_LIMB_MAJOR the input is (B, 4, L, N) and the output
-        (B, 2, L-1, N).  `out` and `workspace` may be passed to reuse buffers."""
+        (B, 2, L-1, N).  `out` and `workspace` may be passed to reuse buffers.
+        A CPU uint32 tensor input (pinned for asynchronous copies) returns a CPU
+        result (or fills a CPU `out`): the batch runs in chunks of `chunk`
+        ciphertexts with host-device copies overlapped with compute; the result
+        is ready on return unless sync=False (then the current stream orders it)."""
         if self._plan is None:
             raise RuntimeError("call control_gen() and setup_relinearization() first")
+        t = _tensor.torch()
+        if isinstance(in_ciphertexts, t.Tensor) and in_ciphertexts.device.type == "cpu":
+            return self._mul_host(in_ciphertexts, out, layout, chunk, sync)
         x = _tensor.to_u32(in_ciphertexts)
         B = x.shape[0]
         L = len(self.original_moduli)
@@ -152,3 +163,30 @@ class HEMul:
         _tensor.call("cross_hemul", self._plan, x.data_ptr(), out.data_ptr(), B, layout, workspace.data_ptr(),
                      workspace.numel(), _lib.cuda_stream())
         return out
+
+    def _mul_host(self, x, out, layout, chunk, sync):
+        t = _tensor.torch()
+        if x.dtype != t.uint32:
+            raise TypeError(f"host input must be uint32, got {x.dtype}")
+        x = x.contiguous()
+        B, L, n = x.shape[0], len(self.original_moduli), self.r * self.c
+        if x.numel() != B * 4 * n * L:
+            raise ValueError(f"expected {B} x 4 x {n} x {L} residues, got shape {tuple(x.shape)}")
+        oshape = (B, 2, *self.degree_layout, L - 1) if layout == _lib.LAYOUT_REFERENCE else (B, 2, L - 1, n)
+        if out is None:
+            out = t.empty(oshape, dtype=t.uint32, pin_memory=x.is_pinned())
+        if out.device.type != "cpu" or tuple(out.shape) != oshape or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous CPU tensor of shape {oshape}")
+        if self._host is None:
+            self._host = HostPipeline()
+        cb = max(1, min(chunk, B))
+        need = self.workspace_size(cb, layout)
+        if self._host_ws is None or self._host_ws.numel() < need:
+            self._host_ws = _tensor.workspace(need)
+        ws = self._host_ws
+
+        def compute(xd, od, nb, stream):
+            _tensor.call("cross_hemul", self._plan, xd.data_ptr(), od.data_ptr(), nb, layout, ws.data_ptr(),
+                         ws.numel(), stream.cuda_stream)
+
+        return self._host.run(x.reshape(B, -1), out.reshape(B, -1), cb, compute, sync).reshape(oshape)

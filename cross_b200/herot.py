@@ -4,6 +4,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import _lib, _tensor, util
+from ._pipeline import HostPipeline
 from .bconv import BConvBarrett
 from .finite_field import BarrettContext
 from .hemul import digits, psi_tables
@@ -113,11 +114,17 @@ class HERot:
     def workspace_size(self, batch: int, layout: int = _lib.LAYOUT_REFERENCE) -> int:
         return int(_lib.lib().cross_herot_workspace_size(self._plan, batch, layout))
 
-    def rotate(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE):
+    def rotate(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE, chunk: int = 8,
+               sync: bool = True):
         """herot.py:183-302: (B, 2, r, c, L) -> (B, 2, N, L) uint32
-        (LAYOUT_LIMB_MAJOR: (B, 2, L, N) -> (B, 2, L, N))."""
+        (LAYOUT_LIMB_MAJOR: (B, 2, L, N) -> (B, 2, L, N)).  A CPU uint32 tensor
+        input runs in chunks with host-device copies overlapped with compute
+        and returns a CPU result (ready on return unless sync=False)."""
         if self._plan is None:
             raise RuntimeError("call control_gen() and setup_rotate() first")
+        t = _tensor.torch()
+        if isinstance(in_ciphertexts, t.Tensor) and in_ciphertexts.device.type == "cpu":
+            return self._rotate_host(in_ciphertexts, out, layout, chunk, sync)
         x = _tensor.to_u32(in_ciphertexts)
         B = x.shape[0]
         n, L = self.r * self.c, self.sizeQl
@@ -131,3 +138,30 @@ class HERot:
         _tensor.call("cross_herot", self._plan, x.data_ptr(), out.data_ptr(), B, layout, workspace.data_ptr(),
                      workspace.numel(), _lib.cuda_stream())
         return out
+
+    def _rotate_host(self, x, out, layout, chunk, sync):
+        t = _tensor.torch()
+        if x.dtype != t.uint32:
+            raise TypeError(f"host input must be uint32, got {x.dtype}")
+        x = x.contiguous()
+        B, n, L = x.shape[0], self.r * self.c, self.sizeQl
+        if x.numel() != B * 2 * n * L:
+            raise ValueError(f"expected {B} x 2 x {n} x {L} residues, got shape {tuple(x.shape)}")
+        oshape = (B, 2, n, L) if layout == _lib.LAYOUT_REFERENCE else (B, 2, L, n)
+        if out is None:
+            out = t.empty(oshape, dtype=t.uint32, pin_memory=x.is_pinned())
+        if out.device.type != "cpu" or tuple(out.shape) != oshape or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous CPU tensor of shape {oshape}")
+        if getattr(self, "_host", None) is None:
+            self._host, self._host_ws = HostPipeline(), None
+        cb = max(1, min(chunk, B))
+        need = self.workspace_size(cb, layout)
+        if self._host_ws is None or self._host_ws.numel() < need:
+            self._host_ws = _tensor.workspace(need)
+        ws = self._host_ws
+
+        def compute(xd, od, nb, stream):
+            _tensor.call("cross_herot", self._plan, xd.data_ptr(), od.data_ptr(), nb, layout, ws.data_ptr(),
+                         ws.numel(), stream.cuda_stream)
+
+        return self._host.run(x.reshape(B, -1), out.reshape(B, -1), cb, compute, sync).reshape(oshape)
