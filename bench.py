@@ -226,7 +226,7 @@ def main():
 
     # e2e through the public API with pinned host buffers: HEMul.mul on CPU
     # tensors copies every input word in and every output word out inside the
-    # timed region (in chunks of 8 ciphertexts, copies overlapped with compute).
+    # timed region (in chunks of 4 ciphertexts, copies overlapped with compute).
     hin = torch.from_numpy(ct).pin_memory()
     hout = torch.empty(out.shape, dtype=torch.uint32).pin_memory()
 

@@ -133,7 +133,7 @@ class HEMul:
     def workspace_size(self, batch: int, layout: int = _lib.LAYOUT_REFERENCE) -> int:
         return int(_lib.lib().cross_hemul_workspace_size(self._plan, batch, layout))
 
-    def mul(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE, chunk: int = 8,
+    def mul(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE, chunk: int = 4,
             sync: bool = True):
         """hemul.py:153-217: (B, 4, r, c, L) uint32 -> (B, 2, r, c, L-1) uint32.
 

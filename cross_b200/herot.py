@@ -114,7 +114,7 @@ class HERot:
     def workspace_size(self, batch: int, layout: int = _lib.LAYOUT_REFERENCE) -> int:
         return int(_lib.lib().cross_herot_workspace_size(self._plan, batch, layout))
 
-    def rotate(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE, chunk: int = 8,
+    def rotate(self, in_ciphertexts, out=None, workspace=None, layout: int = _lib.LAYOUT_REFERENCE, chunk: int = 4,
                sync: bool = True):
         """herot.py:183-302: (B, 2, r, c, L) -> (B, 2, N, L) uint32
         (LAYOUT_LIMB_MAJOR: (B, 2, L, N) -> (B, 2, L, N)).  A CPU uint32 tensor
