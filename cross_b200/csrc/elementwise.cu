@@ -118,8 +118,13 @@ constexpr int TT_MAX_L = 64;
 template <bool TO_LM>
 __global__ void __launch_bounds__(256) k_transpose_ref(const uint32_t* __restrict__ in, uint32_t* __restrict__ out,
                                                       int64_t n, int L, int64_t tiles) {
-  extern __shared__ uint32_t sm[];
-  const int ld = L + 1;
+  extern __shared__ uint4 sm4[];
+  uint32_t* sm = reinterpret_cast<uint32_t*>(sm4);
+  // Row pitch of the tile: odd, so the limb-major side (consecutive t, fixed l)
+  // is free of bank conflicts.  For odd L the pitch is L itself and the tile
+  // is the contiguous reference-layout run, read and written as 16-byte words.
+  const int ld = (L & 1) ? L : L + 1;
+  const bool flat = ld == L;
   const int per = TT * L;
   const float inv = 1.0f / (float)L;
   const int64_t tiles_per_poly = n / TT;
@@ -133,6 +138,10 @@ __global__ void __launch_bounds__(256) k_transpose_ref(const uint32_t* __restric
       // t0 a multiple of TT, so every run starts 16-byte aligned)
       for (int k4 = threadIdx.x; k4 < per / 4; k4 += blockDim.x) {
         const uint4 v = reinterpret_cast<const uint4*>(ref_in)[k4];
+        if (flat) {
+          sm4[k4] = v;
+          continue;
+        }
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -151,6 +160,10 @@ __global__ void __launch_bounds__(256) k_transpose_ref(const uint32_t* __restric
     } else {
       uint32_t* o = out + p * n * L + t0 * L;
       for (int k4 = threadIdx.x; k4 < per / 4; k4 += blockDim.x) {
+        if (flat) {
+          reinterpret_cast<uint4*>(o)[k4] = sm4[k4];
+          continue;
+        }
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {

@@ -111,43 +111,43 @@ __global__ void k_tensor_lm(const uint32_t* __restrict__ R, uint32_t* __restrict
 // Rows are walked limb-major (all ciphertexts of one limb together) so the
 // limb's evaluation-key rows are read from HBM once per launch and from L2 for
 // the rest of the batch.
-template <bool W32, int NPMAX>
-__global__ void k_ks_inner(LP dig, PartPtrs parts, int nparts, const int16_t* __restrict__ src, int LT,
-                           int64_t n, int64_t batch, const uint32_t* __restrict__ evka,
-                           const uint32_t* __restrict__ evkb, uint32_t* __restrict__ KS,
-                           const ModC* __restrict__ mods) {
-  const int64_t nv = n >> 2, rows = batch * LT;
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    const int l = (int)(row / batch);
-    const int64_t b = row - (int64_t)l * batch;
+template <bool W32, int NP>
+__global__ void __launch_bounds__(128) k_ks_inner(LP dig, PartPtrs parts, const int16_t* __restrict__ src, int LT,
+                                                  int64_t n, int batch, const uint32_t* __restrict__ evka,
+                                                  const uint32_t* __restrict__ evkb, uint32_t* __restrict__ KS,
+                                                  const ModC* __restrict__ mods) {
+  // items: (limb l, ciphertext b, chunk of 128 x 4 coefficients), limb-major;
+  // the host keeps their number below 2^31
+  const unsigned nv = (unsigned)(n >> 2), chunks = (nv + 127) / 128;
+  const unsigned items = (unsigned)batch * (unsigned)LT * chunks;
+  for (unsigned it = blockIdx.x; it < items; it += gridDim.x) {
+    const unsigned row = it / chunks, c = it - row * chunks;
+    const int l = (int)(row / (unsigned)batch);
+    const int64_t b = row - (unsigned)l * (unsigned)batch;
+    const unsigned v = c * 128 + threadIdx.x;
+    if (v >= nv) continue;
+    uint4 e[NP], kb[NP], ka[NP];
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const int s = src[j * LT + l];
+      e[j] = s < 0 ? ((const uint4*)(dig.p + b * dig.ps + (int64_t)l * dig.ss))[v]
+                   : ((const uint4*)(parts.e[j] + b * parts.ps[j] + (int64_t)s * n))[v];
+      kb[j] = ((const uint4*)(evkb + ((size_t)j * LT + l) * n))[v];
+      ka[j] = ((const uint4*)(evka + ((size_t)j * LT + l) * n))[v];
+    }
     const ModC mc = mods[l];
+    uint64_t s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      s0[0] += (uint64_t)e[j].x * kb[j].x; s0[1] += (uint64_t)e[j].y * kb[j].y;
+      s0[2] += (uint64_t)e[j].z * kb[j].z; s0[3] += (uint64_t)e[j].w * kb[j].w;
+      s1[0] += (uint64_t)e[j].x * ka[j].x; s1[1] += (uint64_t)e[j].y * ka[j].y;
+      s1[2] += (uint64_t)e[j].z * ka[j].z; s1[3] += (uint64_t)e[j].w * ka[j].w;
+    }
     uint4* o0 = (uint4*)(KS + (b * 2 * LT + l) * n);
     uint4* o1 = (uint4*)(KS + (b * 2 * LT + LT + l) * n);
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
-      uint64_t s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
-      uint4 e[NPMAX], kb[NPMAX], ka[NPMAX];
-#pragma unroll
-      for (int j = 0; j < NPMAX; ++j) {
-        if (j < nparts) {
-          const int s = src[j * LT + l];
-          e[j] = s < 0 ? ((const uint4*)(dig.p + b * dig.ps + (int64_t)l * dig.ss))[v]
-                       : ((const uint4*)(parts.e[j] + b * parts.ps[j] + (int64_t)s * n))[v];
-          kb[j] = ((const uint4*)(evkb + ((size_t)j * LT + l) * n))[v];
-          ka[j] = ((const uint4*)(evka + ((size_t)j * LT + l) * n))[v];
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < NPMAX; ++j) {
-        if (j < nparts) {
-          s0[0] += (uint64_t)e[j].x * kb[j].x; s0[1] += (uint64_t)e[j].y * kb[j].y;
-          s0[2] += (uint64_t)e[j].z * kb[j].z; s0[3] += (uint64_t)e[j].w * kb[j].w;
-          s1[0] += (uint64_t)e[j].x * ka[j].x; s1[1] += (uint64_t)e[j].y * ka[j].y;
-          s1[2] += (uint64_t)e[j].z * ka[j].z; s1[3] += (uint64_t)e[j].w * ka[j].w;
-        }
-      }
-      o0[v] = make_uint4(red<W32>(s0[0], mc), red<W32>(s0[1], mc), red<W32>(s0[2], mc), red<W32>(s0[3], mc));
-      o1[v] = make_uint4(red<W32>(s1[0], mc), red<W32>(s1[1], mc), red<W32>(s1[2], mc), red<W32>(s1[3], mc));
-    }
+    o0[v] = make_uint4(red<W32>(s0[0], mc), red<W32>(s0[1], mc), red<W32>(s0[2], mc), red<W32>(s0[3], mc));
+    o1[v] = make_uint4(red<W32>(s1[0], mc), red<W32>(s1[1], mc), red<W32>(s1[2], mc), red<W32>(s1[3], mc));
   }
 }
 
@@ -183,16 +183,38 @@ __global__ void k_ks_inner_loop(LP dig, PartPtrs parts, int nparts, const int16_
   }
 }
 
-// Launches the key-switch inner product over batch x LT rows.
+// Launches the key-switch inner product over batch x LT rows: the persistent
+// item kernel for 2..4 digits, one block row per limb-ciphertext otherwise.
+template <bool W32, int NP>
+void ks_inner_items(LP dig, const PartPtrs& pp, const int16_t* src, int LT, int64_t n, int64_t B, const uint32_t* evka,
+                    const uint32_t* evkb, uint32_t* KS, const ModC* mods, cudaStream_t st) {
+  static int resident = 0;   // blocks of this instantiation that fit on the GPU at once
+  if (!resident) {
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_ks_inner<W32, NP>, 128, 0);
+    resident = (sms > 0 ? sms : 148) * (per_sm > 0 ? per_sm : 4);
+  }
+  const int64_t items = B * LT * (((n >> 2) + 127) / 128);
+  const int64_t cap = resident;
+  k_ks_inner<W32, NP><<<(unsigned)(items < cap ? items : cap), 128, 0, st>>>(dig, pp, src, LT, n, (int)B, evka, evkb,
+                                                                           KS, mods);
+}
+
 int ks_inner(bool w32, LP dig, const PartPtrs& pp, int nparts, const int16_t* src, int LT, int64_t n, int64_t B,
              const uint32_t* evka, const uint32_t* evkb, uint32_t* KS, const ModC* mods, cudaStream_t st) {
-  const dim3 g(gx_for(n >> 2), gy_for(B * LT));
-  if (nparts <= 4) {
-    if (w32)
-      k_ks_inner<true, 4><<<g, T, 0, st>>>(dig, pp, nparts, src, LT, n, B, evka, evkb, KS, mods);
-    else
-      k_ks_inner<false, 4><<<g, T, 0, st>>>(dig, pp, nparts, src, LT, n, B, evka, evkb, KS, mods);
+  const int64_t items = B * LT * (((n >> 2) + 127) / 128);
+  if (nparts >= 2 && nparts <= 4 && items < ((int64_t)1 << 31)) {
+#define CROSS_KS(NP)                                                                              \
+  (w32 ? ks_inner_items<true, NP>(dig, pp, src, LT, n, B, evka, evkb, KS, mods, st)               \
+       : ks_inner_items<false, NP>(dig, pp, src, LT, n, B, evka, evkb, KS, mods, st))
+    if (nparts == 2) CROSS_KS(2);
+    else if (nparts == 3) CROSS_KS(3);
+    else CROSS_KS(4);
+#undef CROSS_KS
   } else {
+    const dim3 g(gx_for(n >> 2), gy_for(B * LT));
     if (w32)
       k_ks_inner_loop<true><<<g, T, 0, st>>>(dig, pp, nparts, src, LT, n, B, evka, evkb, KS, mods);
     else
