@@ -126,19 +126,20 @@ __global__ void __launch_bounds__(BC_THREADS) k_bconv(const uint32_t* __restrict
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core basis conversion.  One CTA of 128 threads per tile of 128
-// coefficients of one polynomial, thread t owning coefficient row t (TMEM lane
-// t):
+// Tensor-core basis conversion.  One CTA of 256 threads per tile of 128
+// coefficients of one polynomial, two threads per coefficient row t (TMEM lane
+// t), each taking half of the source and half of the target limbs:
 //   1. c_i = Barrett_src_i(x_i[t] * QHatInvModq_i) written as row t of the
 //      K-major A tile (no swizzle: 8-row x 16-byte core matrices, K halves 128 B
 //      apart, 8-row groups 256 B apart; one 16-byte store per 4 limbs);
 //   2. thread 0 issues kb MMAs (M = 128, N = nn, K = 32) into TMEM and commits;
-//   3. every thread reads its accumulator row and writes
+//   3. every thread reads its half of the accumulator row and writes
 //      out_j[t] = Barrett_dst_j(sum_b D[t][4j + b] << 8b) (times the psi twist).
 // The B image (QHatModpBAT in the same core-matrix layout) and the per-limb
 // constants stay in shared memory.  The MMA completion wait is bounded; on
 // expiry the kernel records code 21 in the plan's error word and stops.
-constexpr int BT_THREADS = 128;
+constexpr int BT_ROWS = 128;      // coefficients per tile (TMEM lanes)
+constexpr int BT_THREADS = 256;   // two threads per coefficient row
 using namespace tc;
 
 struct BconvTcArgs {
@@ -165,7 +166,7 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
 }
 
 template <bool FAST, bool TWIST, int KB, int SPMAX>
-__global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
+__global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a) {
   extern __shared__ uint8_t sm_raw[];
   uint8_t* As = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* Bs = As + a.kb * 4096;
@@ -201,47 +202,61 @@ __global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t idesc = (2u << 4) | ((uint32_t)(a.nn >> 3) << 17) | ((uint32_t)(BT_THREADS >> 4) << 24);
-  const int tiles_pp = a.n / BT_THREADS;
+  const uint32_t idesc = (2u << 4) | ((uint32_t)(a.nn >> 3) << 17) | ((uint32_t)(BT_ROWS >> 4) << 24);
+  const int tiles_pp = a.n / BT_ROWS;
   const int total = a.polys * tiles_pp;
+  // Thread (row, h): coefficient row = TMEM lane, half h of the work.  It packs
+  // the source limbs 4g..4g+3 for the K-halves g = 2gi + h, and produces the
+  // target limbs [h * SPMAX/2, (h + 1) * SPMAX/2).
+  const int row = t & (BT_ROWS - 1), h = t / BT_ROWS;
+  constexpr int JH = SPMAX / 2;
   // inputs of the next tile, loaded while the current one is converted
-  uint32_t xin[8 * KB];
+  uint32_t xin[4 * KB];
   auto load_inputs = [&](int w) {
     const int poly = w / tiles_pp;
-    const uint32_t* x = a.in + (int64_t)poly * a.in_ps + (w - poly * tiles_pp) * BT_THREADS + t;
+    const uint32_t* x = a.in + (int64_t)poly * a.in_ps + (w - poly * tiles_pp) * BT_ROWS + row;
 #pragma unroll
-    for (int i = 0; i < 8 * KB; ++i) xin[i] = i < a.sq ? __ldg(x + (int64_t)i * a.in_ls) : 0u;
+    for (int gi = 0; gi < KB; ++gi)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * (2 * gi + h) + e;
+        xin[4 * gi + e] = i < a.sq ? __ldg(x + (int64_t)i * a.in_ls) : 0u;
+      }
   };
   if ((int)blockIdx.x < total) load_inputs(blockIdx.x);
   uint32_t phase = 0;
   for (int w = blockIdx.x; w < total; w += gridDim.x) {
     const int poly = w / tiles_pp;
-    const int t0 = (w - poly * tiles_pp) * BT_THREADS;
+    const int t0 = (w - poly * tiles_pp) * BT_ROWS;
     // 1. source residues, 4 limbs (16 bytes of K) per store
 #pragma unroll
-    for (int g = 0; g < 2 * KB; ++g) {
-      if (g < 2 * a.kb) {
+    for (int gi = 0; gi < KB; ++gi) {
+      if (gi < a.kb) {
+        const int g = 2 * gi + h;
         uint32_t c[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int i = 4 * g + e;
           uint32_t v = 0;
           if (i < a.sq) {
-            const uint64_t z = (uint64_t)xin[i] * shi[i];
+            const uint64_t z = (uint64_t)xin[4 * gi + e] * shi[i];
             v = FAST ? barrett_w32(z, (uint32_t)sc[i].q, (uint32_t)sc[i].m, sc[i].s_w) : barrett(z, sc[i]);
           }
           c[e] = v;
         }
-        *reinterpret_cast<uint4*>(As + (g >> 1) * 4096 + (t >> 3) * 256 + (g & 1) * 128 + (t & 7) * 16) =
+        *reinterpret_cast<uint4*>(As + gi * 4096 + (row >> 3) * 256 + h * 128 + (row & 7) * 16) =
             make_uint4(c[0], c[1], c[2], c[3]);
       }
     }
     if (w + (int)gridDim.x < total) load_inputs(w + gridDim.x);
     // twist factors of this tile, in flight during the MMA
-    uint32_t tw[SPMAX];
+    uint32_t tw[JH];
     if (TWIST) {
 #pragma unroll
-      for (int j = 0; j < SPMAX; ++j) tw[j] = j < a.sp ? __ldg(a.twist + (int64_t)dc[j].w * a.n + t0 + t) : 0u;
+      for (int jj = 0; jj < JH; ++jj) {
+        const int j = h * JH + jj;
+        tw[jj] = j < a.sp ? __ldg(a.twist + (int64_t)dc[j].w * a.n + t0 + row) : 0u;
+      }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
@@ -267,28 +282,30 @@ __global__ void __launch_bounds__(BT_THREADS) k_bconv_tc(const BconvTcArgs a) {
     phase ^= 1;
     if (__syncthreads_or(!ok)) break;
     tc_fence_after();
-    // 3. eight target limbs per 32 accumulator columns
-    uint32_t* y = a.out + (int64_t)poly * a.out_ps + t0 + t;
+    // 3. four target limbs per 16 accumulator columns, this half's limbs only
+    uint32_t* y = a.out + (int64_t)poly * a.out_ps + t0 + row;
 #pragma unroll
-    for (int ch = 0; ch < SPMAX / 8; ++ch) {
-      if (ch * 32 < a.nn) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + ch * 32, v);
+    for (int qc = 0; qc < JH / 4; ++qc) {
+      const int j0 = h * JH + 4 * qc;
+      if (4 * j0 < a.nn) {
+        uint32_t v[16];
+        tmem_ld16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + 4 * j0, v);
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const int j = ch * 8 + jj;
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = j0 + jj;
           if (j < a.sp) {
             const uint4 cj = dc[j];
             const uint32_t q = cj.x, m = cj.y, sw = cj.z;
             const uint64_t z = combine4_mad(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+            const uint32_t twj = tw[4 * qc + jj];
             uint32_t r;
             if (FAST) {
               r = reduce_fast(z, q, m, sw);
-              if (TWIST) r = reduce_fast2(r * tw[j], __umulhi(r, tw[j]), q, m, sw);
+              if (TWIST) r = reduce_fast2(r * twj, __umulhi(r, twj), q, m, sw);
             } else {
               const ModC mc = a.dst[j];
               r = barrett(z, mc);
-              if (TWIST) r = barrett((uint64_t)r * tw[j], mc);
+              if (TWIST) r = barrett((uint64_t)r * twj, mc);
             }
             y[(int64_t)j * a.out_ls] = r;
           }
@@ -329,7 +346,7 @@ int launch_bconv_tc(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cudaStre
   }
   auto kern = k_bconv_tc<FAST, TWIST, KB, SPMAX>;
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const int64_t total = (int64_t)a.polys * (a.n / BT_THREADS);
+  const int64_t total = (int64_t)a.polys * (a.n / BT_ROWS);
   const int64_t cap = (int64_t)sms * ctas_per_sm;
   kern<<<(unsigned)(total < cap ? total : cap), BT_THREADS, smem, st>>>(a);
   count_launch();
@@ -376,7 +393,7 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
               int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
               int64_t n, cudaStream_t st, const uint32_t* twist, const uint16_t* trow) {
   if (polys == 0 || n == 0) return CROSS_OK;
-  if (bat && P->tc_bimg && in_ts == 1 && out_ts == 1 && n % BT_THREADS == 0 && polys * (n / BT_THREADS) < (1ll << 31)) {
+  if (bat && P->tc_bimg && in_ts == 1 && out_ts == 1 && n % BT_ROWS == 0 && polys * (n / BT_ROWS) < (1ll << 31)) {
     BconvTcArgs a{in, in_ps, in_ls, out, out_ps, out_ls, (int)polys, (int)n, P->sq, P->sp, P->tc_kb, P->tc_nn, 0,
                   P->src, P->dst, P->qhat_inv, P->tc_bimg, twist, trow, P->err};
     a.tmem_cols = 64;   // at most 8 CTAs per SM
