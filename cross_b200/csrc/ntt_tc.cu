@@ -135,6 +135,16 @@ struct SlotCache {
   uint32_t scal = 0;               // EPI_COMBINE / EPI_MODDOWN scalar of the slot
 };
 
+// Matrix dimensions of a launch: compile-time 256 for the 256 x 256 stages of
+// N = 2^16 (DIM = 256), so every stride folds into an immediate, else the
+// launch arguments (DIM = 0).
+template <int DIM>
+__device__ __forceinline__ int dim_rows(const Args& a) { return DIM ? DIM : a.rows_m; }
+template <int DIM>
+__device__ __forceinline__ int dim_nout(const Args& a) { return DIM ? DIM : a.nout; }
+template <int DIM>
+__device__ __forceinline__ int dim_kw(const Args& a) { return DIM ? DIM : a.kw; }
+
 // Epilogue of one 128 x 256 accumulator tile, run by the 16 epilogue warps
 // (TMEM lane quadrant warp % 4, column quarter (warp - 2) / 4): tcgen05.ld,
 // byte recombination, Barrett, the fused position-wise op, stores.  Output
@@ -142,23 +152,24 @@ struct SlotCache {
 // operands of the fused op are read at the same positions before the
 // accumulator is ready (16 consecutive words per thread when row major: four
 // 16-byte loads).  Returns false when the wait for the accumulator gave up.
-template <int EPI, bool NMAJOR, bool FAST>
+template <int EPI, bool NMAJOR, bool FAST, int DIM>
 __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, uint64_t* tfull, uint32_t parity,
                                               volatile int& abort, const Unit& w, bool store, int warp, int lane,
                                               SlotCache& sc) {
   constexpr int OUTS = 16;                     // outputs (64 columns) per thread and tile
+  const int rows_m = dim_rows<DIM>(a), nout = dim_nout<DIM>(a);
   const int quad = warp & 3, part = (warp - 2) >> 2;
   constexpr int P0 = EPI == EPI_NONE ? 1 : OUTS;
   constexpr int P1 = EPI == EPI_MODDOWN ? OUTS : 1;
   if (w.slot != sc.slot) {
     sc.slot = w.slot;
     sc.mc = a.mods[a.limbs[w.slot]];
-    if (EPI == EPI_MUL) sc.tab = a.e.tab + (int64_t)a.e.trow[w.slot] * ((int64_t)a.rows_m * a.nout);
+    if (EPI == EPI_MUL) sc.tab = a.e.tab + (int64_t)a.e.trow[w.slot] * ((int64_t)rows_m * nout);
     if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) sc.scal = a.e.scal[w.slot];
   }
   const int m = w.mt * BM + quad * 32 + lane;
   const int n0 = w.nt * 64 + part * OUTS;
-  const int64_t p0 = NMAJOR ? (int64_t)n0 * a.rows_m + m : (int64_t)m * a.nout + n0;
+  const int64_t p0 = NMAJOR ? (int64_t)n0 * rows_m + m : (int64_t)m * nout + n0;
   uint32_t pre0[P0], pre1[P1];
   const uint32_t scal = sc.scal;
   bool add_base = false;
@@ -166,7 +177,7 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
     const uint32_t* src = EPI == EPI_MUL ? sc.tab + p0 : a.e.x.at(w.poly, w.slot) + p0;
     if (NMAJOR) {
 #pragma unroll
-      for (int j = 0; j < OUTS; ++j) pre0[j] = __ldg(src + (int64_t)j * a.rows_m);
+      for (int j = 0; j < OUTS; ++j) pre0[j] = __ldg(src + (int64_t)j * rows_m);
     } else {
 #pragma unroll
       for (int j = 0; j < OUTS / 4; ++j) {
@@ -234,7 +245,7 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
     if (store) {
       if (NMAJOR) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[(int64_t)(chunk * 8 + j) * a.rows_m] = res[j];
+        for (int j = 0; j < 8; ++j) o[(int64_t)(chunk * 8 + j) * rows_m] = res[j];
       } else {
         // Lanes 2k and 2k+1 hold rows m and m+1 (1 KiB or more apart), eight
         // outputs each.  They swap halves so that each store instruction
@@ -251,8 +262,8 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
         y.z = __shfl_xor_sync(0xffffffffu, x.z, 1);
         y.w = __shfl_xor_sync(0xffffffffu, x.w, 1);
         uint32_t* base = o + chunk * 8 + odd * 4;
-        *reinterpret_cast<uint4*>(base - (int64_t)odd * a.nout) = odd ? y : lo;
-        *reinterpret_cast<uint4*>(base + (int64_t)(1 - odd) * a.nout) = odd ? hi : y;
+        *reinterpret_cast<uint4*>(base - (int64_t)odd * nout) = odd ? y : lo;
+        *reinterpret_cast<uint4*>(base + (int64_t)(1 - odd) * nout) = odd ? hi : y;
       }
     }
   }
@@ -367,8 +378,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
     SlotCache sc;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit w = decode(u, nt_shift, mt_shift, polys);
-      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, true, warp, lane,
-                                            sc))
+      if (!epilogue_tile<EPI, NMAJOR, FAST, 0>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, true, warp,
+                                               lane, sc))
         break;
       tc_fence_before();
       mbar_arrive(&S.tempty[acc]);
@@ -489,13 +500,14 @@ __device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
 struct PairWork {
   int t0, t1, ipc, rbs, nt, mt_shift;
 };
+template <int DIM>
 __device__ __forceinline__ PairWork pair_work(const Args& a) {
   PairWork pw;
-  const int n_tiles = a.nout / 64;
+  const int n_tiles = dim_nout<DIM>(a) / 64;
   const int pair = blockIdx.x >> 1, groups = (gridDim.x >> 1) / n_tiles;
   const int g = pair / n_tiles;
   pw.nt = pair - g * n_tiles;
-  pw.mt_shift = __ffs(a.rows_m / BM) - 1;
+  pw.mt_shift = __ffs(dim_rows<DIM>(a) / BM) - 1;
   pw.rbs = (int)a.polys << pw.mt_shift;
   pw.ipc = (pw.rbs + 1) / 2;
   const int64_t total = (int64_t)a.slots * pw.ipc;
@@ -528,15 +540,15 @@ struct PairIter {
   }
 };
 
-template <int EPI, bool NMAJOR, bool FAST>
+template <int EPI, bool NMAJOR, bool FAST, int DIM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     k_bat_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   Smem2& S = *reinterpret_cast<Smem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
-  const int kst = a.kw / 32;
-  const PairWork pw = pair_work(a);
+  const int kst = dim_kw<DIM>(a) / 32;
+  const PairWork pw = pair_work<DIM>(a);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES2; ++s) {
@@ -593,7 +605,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (rank == 0) mbar_expect_tx(&S.bfull, 2 * kst * B2_CHUNK);
           const uint32_t bar = mapa(&S.bfull, 0);
           for (int kc = 0; kc < kst; ++kc)
-            tma_load_2d_pair(S.b[kc], &tmB, bar, kc * BKB, limb * 4 * a.nout + w.nt * BN + (int)rank * B2_ROWS);
+            tma_load_2d_pair(S.b[kc], &tmB, bar, kc * BKB, limb * 4 * dim_nout<DIM>(a) + w.nt * BN + (int)rank * B2_ROWS);
           prev_slot = w.slot;
         }
         for (int kc = 0; kc < kst; kc += KPS) {
@@ -674,8 +686,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     for (int t = pw.t0; t < pw.t1; ++t, it.next(pw)) {
       bool valid;
       const Unit w = it.unit(pw, rank, valid);
-      if (!epilogue_tile<EPI, NMAJOR, FAST>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, valid, warp, lane,
-                                            sc))
+      if (!epilogue_tile<EPI, NMAJOR, FAST, DIM>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, valid, warp,
+                                                 lane, sc))
         break;
       tc_fence_before();
       __syncwarp();
@@ -781,9 +793,9 @@ int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaSt
 
 int g_max_pairs = 0;
 
-template <int EPI, bool NM, bool FAST>
+template <int EPI, bool NM, bool FAST, int DIM>
 int launch2(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
-  auto kern = k_bat_tc2<EPI, NM, FAST>;
+  auto kern = k_bat_tc2<EPI, NM, FAST, DIM>;
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES));
   if (!g_max_pairs) {
     // clusters of two 197 KiB CTAs that fit at once (compile-time cluster dims)
@@ -839,8 +851,10 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
   }
   const bool f = P->tc_fast != 0;
   const bool pair = P->tc_pair && kw <= 32 * B2_CHUNKS && kw % (32 * KPS) == 0;
-#define CROSS_TC_LAUNCH(OP, NM)                                                                      \
-  return pair ? (f ? launch2<OP, NM, true>(tmA, tmB2, a, st) : launch2<OP, NM, false>(tmA, tmB2, a, st)) \
+  const bool d256 = rows_m == 256 && nout == 256 && kw == 256;
+#define CROSS_TC_LAUNCH(OP, NM)                                                                                  \
+  return pair ? (d256 ? (f ? launch2<OP, NM, true, 256>(tmA, tmB2, a, st) : launch2<OP, NM, false, 256>(tmA, tmB2, a, st)) \
+                      : (f ? launch2<OP, NM, true, 0>(tmA, tmB2, a, st) : launch2<OP, NM, false, 0>(tmA, tmB2, a, st)))  \
               : (f ? launch<OP, NM, true>(tmA, tmB, a, st) : launch<OP, NM, false>(tmA, tmB, a, st))
   switch (e.op) {
     case EPI_NONE:
