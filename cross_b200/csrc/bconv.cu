@@ -174,14 +174,17 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
   volatile int& abort = *reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint4* dc = reinterpret_cast<uint4*>(tmem_slot + 2);   // [sp] target {q, m, s_w, twist row}
-  ModC* sc = reinterpret_cast<ModC*>(dc + a.sp);          // [sq] source moduli
+  const uint32_t** tp = reinterpret_cast<const uint32_t**>(dc + a.sp);   // [sp] twist row of each target limb
+  ModC* sc = reinterpret_cast<ModC*>(tp + a.sp);          // [sq] source moduli
   uint32_t* shi = reinterpret_cast<uint32_t*>(sc + a.sq);        // [sq] QHatInvModq
   const int t = threadIdx.x, warp = t >> 5;
 
   for (int i = t; i < a.kb * (a.nn / 8) * 16; i += BT_THREADS)
     reinterpret_cast<uint4*>(Bs)[i] = reinterpret_cast<const uint4*>(a.bimg)[i];
-  for (int j = t; j < a.sp; j += BT_THREADS)
+  for (int j = t; j < a.sp; j += BT_THREADS) {
     dc[j] = make_uint4((uint32_t)a.dst[j].q, (uint32_t)a.dst[j].m, a.dst[j].s_w, TWIST ? a.trow[j] : 0u);
+    tp[j] = TWIST ? a.twist + (int64_t)a.trow[j] * a.n : nullptr;
+  }
   for (int i = t; i < a.sq; i += BT_THREADS) {
     sc[i] = a.src[i];
     shi[i] = a.qhat_inv[i];
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
 #pragma unroll
       for (int jj = 0; jj < JH; ++jj) {
         const int j = h * JH + jj;
-        tw[jj] = j < a.sp ? __ldg(a.twist + (int64_t)dc[j].w * a.n + t0 + row) : 0u;
+        tw[jj] = j < a.sp ? __ldg(tp[j] + t0 + row) : 0u;
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
 // padded so that no more CTAs fit on an SM (sm_bytes of shared memory, 1 KiB
 // reserved per CTA) than its 512 TMEM columns serve.  0 when impossible.
 size_t bconv_tc_smem(int sq, int sp, int kb, int nn, uint32_t tmem_cols, size_t sm_bytes, int* ctas_per_sm) {
-  const size_t need = 1024 + (size_t)kb * 4096 + (size_t)kb * (nn / 8) * 256 + 16 + (size_t)sp * 16 +
+  const size_t need = 1024 + (size_t)kb * 4096 + (size_t)kb * (nn / 8) * 256 + 16 + (size_t)sp * (16 + 8) +
                       (size_t)sq * (sizeof(ModC) + 4);
   const int ctas = (int)(512 / tmem_cols);
   // (ctas + 1) CTAs of s + 1 KiB each must not fit, ctas of them must

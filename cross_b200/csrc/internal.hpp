@@ -137,7 +137,8 @@ struct View {
 // Barrett-reduced transform output at a position:
 //   EPI_MUL      r = Barrett(r * tab[trow[slot]][pos])              (psi twists)
 //   EPI_COMBINE  r = Barrett(x[pos] * scal[slot] + r)               (rescale, ciphertext.py:299-302)
-//   EPI_MODDOWN  s = x[pos] < r ? x[pos] + q - r : x[pos] - r       (ModDown, hemul.py:198-215)
+//   EPI_MODDOWN  s = x[pos] < r ? x[pos] + q - r : x[pos] - r       (ModDown, hemul.py:198-215;
+//                x must be a lazy residue < 2q, as the key-switch sums are)
 //                t = Barrett(s * scal[slot]);
 //                r = base on for e % E ? (base[pos] + t >= q ? base[pos] + t - q : base[pos] + t) : t
 enum EpiOp { EPI_NONE = 0, EPI_MUL = 1, EPI_COMBINE = 2, EPI_MODDOWN = 3 };
