@@ -45,8 +45,13 @@ class HostPipeline:
         cb = max(1, min(chunk, B))
         bufs = self._buffers(t, cb, x_host.shape[1:], out_host.shape[1:])
         ev = [[t.cuda.Event() for _ in range(3)] for _ in range(self.NBUF)]   # copied in, computed, copied out
-        for k, lo in enumerate(range(0, B, cb)):
-            hi = min(B, lo + cb)
+        # full chunks, then the last chunk one ciphertext at a time so that little
+        # compute and copy-out remains after the final copy-in
+        bounds = [(lo, min(B, lo + cb)) for lo in range(0, B, cb)]
+        if len(bounds) > 1:
+            lo, hi = bounds.pop()
+            bounds += [(i, i + 1) for i in range(lo, hi)]
+        for k, (lo, hi) in enumerate(bounds):
             nb = hi - lo
             i = k % self.NBUF
             xd, od = bufs[i]

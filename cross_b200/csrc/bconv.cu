@@ -156,6 +156,7 @@ struct BconvTcArgs {
   const uint32_t* twist;
   const uint16_t* trow;
   int* err;
+  bool src_fast;  // reduce_fast is exact for every source modulus
 };
 
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
@@ -242,8 +243,15 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
           const int i = 4 * g + e;
           uint32_t v = 0;
           if (i < a.sq) {
-            const uint64_t z = (uint64_t)xin[4 * gi + e] * shi[i];
-            v = FAST ? barrett_w32(z, (uint32_t)sc[i].q, (uint32_t)sc[i].m, sc[i].s_w) : barrett(z, sc[i]);
+            const uint32_t xv = xin[4 * gi + e], hv = shi[i];
+            // x < 2^31 and QHatInv < q keep the product below 2^31 q, where the
+            // fast form is exact (always so for transform outputs)
+            if (FAST && a.src_fast && xv < 0x80000000u)
+              v = reduce_fast2(xv * hv, __umulhi(xv, hv), (uint32_t)sc[i].q, (uint32_t)sc[i].m, sc[i].s_w);
+            else if (FAST)
+              v = barrett_w32((uint64_t)xv * hv, (uint32_t)sc[i].q, (uint32_t)sc[i].m, sc[i].s_w);
+            else
+              v = barrett((uint64_t)xv * hv, sc[i]);
           }
           c[e] = v;
         }
@@ -398,7 +406,7 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
   if (polys == 0 || n == 0) return CROSS_OK;
   if (bat && P->tc_bimg && in_ts == 1 && out_ts == 1 && n % BT_ROWS == 0 && polys * (n / BT_ROWS) < (1ll << 31)) {
     BconvTcArgs a{in, in_ps, in_ls, out, out_ps, out_ls, (int)polys, (int)n, P->sq, P->sp, P->tc_kb, P->tc_nn, 0,
-                  P->src, P->dst, P->qhat_inv, P->tc_bimg, twist, trow, P->err};
+                  P->src, P->dst, P->qhat_inv, P->tc_bimg, twist, trow, P->err, P->tc_src_fast != 0};
     a.tmem_cols = 64;   // at most 8 CTAs per SM
     while ((int)a.tmem_cols < a.nn) a.tmem_cols <<= 1;
     static int sm_bytes = 0;
@@ -488,6 +496,9 @@ int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* 
     for (const ModC& mc : P->dst_host) fast = fast && reduce_fast_ok(mc);
     for (const ModC& mc : P->src_host) fast = fast && barrett_w32_ok(mc);
     P->tc_fast = fast ? 1 : 0;
+    bool src_fast = true;
+    for (const ModC& mc : P->src_host) src_fast = src_fast && reduce_fast_ok(mc);
+    P->tc_src_fast = src_fast ? 1 : 0;
   }
   std::vector<int> zero(1, 0);
   int rc = upload_vec(&P->src, P->src_host);

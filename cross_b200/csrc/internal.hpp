@@ -49,6 +49,7 @@ struct cross_ntt_plan_s {
 struct cross_bconv_plan_s {
   int sq = 0, sp = 0;
   int tc_fast = 0;                  // tensor-core kernel may use reduce_fast / barrett_w32
+  int tc_src_fast = 0;              // reduce_fast is exact for every source modulus
   int tc_kb = 0, tc_nn = 0;         // K blocks of 8 source limbs, MMA N (4 sp rounded up to 16)
   uint8_t* tc_bimg = nullptr;       // B operand in its shared-memory image (K-major, no swizzle)
   int* err = nullptr;               // device error word of the tensor-core kernel
@@ -137,8 +138,7 @@ struct View {
 // Barrett-reduced transform output at a position:
 //   EPI_MUL      r = Barrett(r * tab[trow[slot]][pos])              (psi twists)
 //   EPI_COMBINE  r = Barrett(x[pos] * scal[slot] + r)               (rescale, ciphertext.py:299-302)
-//   EPI_MODDOWN  s = x[pos] < r ? x[pos] + q - r : x[pos] - r       (ModDown, hemul.py:198-215;
-//                x must be a lazy residue < 2q, as the key-switch sums are)
+//   EPI_MODDOWN  s = x[pos] < r ? x[pos] + q - r : x[pos] - r       (ModDown, hemul.py:198-215)
 //                t = Barrett(s * scal[slot]);
 //                r = base on for e % E ? (base[pos] + t >= q ? base[pos] + t - q : base[pos] + t) : t
 enum EpiOp { EPI_NONE = 0, EPI_MUL = 1, EPI_COMBINE = 2, EPI_MODDOWN = 3 };

@@ -229,12 +229,17 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
         const uint64_t zc = (uint64_t)pre0[jj] * scal + r;
         r = FAST ? barrett_w32(zc, q32, m32, sw) : barrett(zc, mc);
       } else if (EPI == EPI_MODDOWN) {
-        // x and r are lazy residues (< 2q), so sub < 2q and zm < 2q^2, inside
-        // the range reduce_fast is proven exact for
+        // sub < 2^31 with P^-1 < q keeps the product below 2^31 q, where the
+        // fast form is exact; larger operands take the 64-bit form
         const uint32_t x = pre0[jj];
         const uint32_t sub = x < r ? x + q32 - r : x - r;
-        const uint32_t t = FAST ? reduce_fast2(sub * scal, __umulhi(sub, scal), q32, m32, sw)
-                                : barrett((uint64_t)sub * scal, mc);
+        uint32_t t;
+        if (FAST && sub < 0x80000000u)
+          t = reduce_fast2(sub * scal, __umulhi(sub, scal), q32, m32, sw);
+        else if (FAST)
+          t = barrett_w32((uint64_t)sub * scal, q32, m32, sw);
+        else
+          t = barrett((uint64_t)sub * scal, mc);
         if (add_base) {
           const uint32_t s2 = pre1[jj] + t;
           r = s2 >= q32 ? s2 - q32 : s2;

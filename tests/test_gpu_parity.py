@@ -447,6 +447,40 @@ def test_host_buffer_pipeline_matches_device_call(pinned):
     np.testing.assert_array_equal(got_r.numpy(), want_r)
 
 
+def test_unreduced_inputs_stay_bit_exact():
+    """Full-range uint32 inputs and keys (not reduced mod q) drive the epilogue
+    and BConv operands outside the lazy-residue range; the guarded fast Barrett
+    forms must still return the reference's values (tensor-core path, N = 2^14)."""
+    import torch
+    from cross_b200 import hemul, bconv, _lib
+    n, L, K, dnum, B = 16384, 6, 2, 3, 2
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    Q, P = ov[:L], ov[L:]
+    rng = np.random.default_rng(99)
+    ct = rng.integers(0, 2 ** 32, size=(B, 4, 128, 128, L), dtype=np.uint64).astype(U32)
+    ek = [rng.integers(0, 2 ** 32, size=(dnum, n, L + K), dtype=np.uint64).astype(U32) for _ in range(2)]
+    he = hemul.HEMul(B, 128, 128, dnum, 1, Q, P)
+    he.control_gen(degree_layout=(128, 128))
+    he.setup_relinearization(*ek)
+    got = _np(he.mul(ct))
+    ref = O.HEMul(B, 128, 128, dnum, 1, Q, P)
+    ref.setup_relinearization(*ek)
+    np.testing.assert_array_equal(got, ref.mul(ct))
+    # BConv 8 -> 23 (tensor-core kernel, limb-major) on full-range inputs
+    mv = O.find_moduli_ntt(31, 28, 2 * 4096)
+    x = rng.integers(0, 2 ** 32, size=(2, 4096, 8), dtype=np.uint64).astype(U32)
+    ob = O.BConvBarrett(mv)
+    ob.control_gen([(list(range(8)), list(range(8, 31)))])
+    b = bconv.BConvBarrett(mv)
+    b.control_gen([(list(range(8)), list(range(8, 31)))])
+    xl = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 1))).cuda()
+    yl = torch.empty((2, 23, 4096), dtype=xl.dtype, device="cuda")
+    _lib.check(_lib.lib().cross_bconv(b.plan(0), 1, xl.data_ptr(), yl.data_ptr(), 2, 4096, _lib.LAYOUT_LIMB_MAJOR,
+                                      None), "cross_bconv")
+    np.testing.assert_array_equal(_np(yl), ob.basis_change_bat(x).transpose(0, 2, 1))
+    b.check_device()
+
+
 def test_limb_major_layout_matches_reference_layout():
     import torch
     from cross_b200 import hemul, LAYOUT_LIMB_MAJOR
