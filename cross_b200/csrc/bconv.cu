@@ -349,12 +349,7 @@ size_t bconv_tc_smem(int sq, int sp, int kb, int nn, uint32_t tmem_cols, size_t 
 
 template <bool FAST, bool TWIST, int KB, int SPMAX>
 int launch_bconv_tc(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    CROSS_CHECK_CUDA(cudaGetDevice(&dev));
-    CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  }
+  const int sms = device_sm_count();
   auto kern = k_bconv_tc<FAST, TWIST, KB, SPMAX>;
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t total = (int64_t)a.polys * (a.n / BT_ROWS);
@@ -409,12 +404,7 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
                   P->src, P->dst, P->qhat_inv, P->tc_bimg, twist, trow, P->err, P->tc_src_fast != 0};
     a.tmem_cols = 64;   // at most 8 CTAs per SM
     while ((int)a.tmem_cols < a.nn) a.tmem_cols <<= 1;
-    static int sm_bytes = 0;
-    if (!sm_bytes) {
-      int dev = 0;
-      CROSS_CHECK_CUDA(cudaGetDevice(&dev));
-      CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&sm_bytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
-    }
+    const int sm_bytes = device_smem_per_sm();
     int ctas = 0;
     const size_t sm = bconv_tc_smem(P->sq, P->sp, P->tc_kb, P->tc_nn, a.tmem_cols, (size_t)sm_bytes, &ctas);
     if (sm) {

@@ -275,13 +275,7 @@ int transpose_u32(const uint32_t* in, uint32_t* out, int64_t batch, int64_t rows
     const int64_t n = to_lm ? rows : cols;
     const int L = (int)(to_lm ? cols : rows);
     const int64_t tiles = batch * (n / TT);
-    static int blocks = 0;
-    if (!blocks) {
-      int dev = 0, sms = 0;
-      CROSS_CHECK_CUDA(cudaGetDevice(&dev));
-      CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-      blocks = sms * 8;
-    }
+    const int blocks = device_sm_count() * 8;
     const unsigned grid = (unsigned)(tiles < blocks ? tiles : blocks);
     const size_t smem = (size_t)TT * (L + 1) * sizeof(uint32_t);
     if (to_lm)

@@ -20,6 +20,20 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+static int device_attr(cudaDeviceAttr attr, int fallback) {
+  int d = 0, v = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || cudaDeviceGetAttribute(&v, attr, d) != cudaSuccess || v <= 0) {
+    (void)cudaGetLastError();
+    return fallback;
+  }
+  return v;
+}
+static PerDevice g_sms, g_smem;
+int device_sm_count() { return g_sms.get([] { return device_attr(cudaDevAttrMultiProcessorCount, 148); }); }
+int device_smem_per_sm() {
+  return g_smem.get([] { return device_attr(cudaDevAttrMaxSharedMemoryPerMultiprocessor, 233472); });
+}
+
 int fail_cuda(cudaError_t e, const char* where) {
   set_error("CUDA error %d (%s) at %s", (int)e, cudaGetErrorString(e), where);
   return CROSS_ERR_CUDA;

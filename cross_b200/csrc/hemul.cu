@@ -188,14 +188,15 @@ __global__ void k_ks_inner_loop(LP dig, PartPtrs parts, int nparts, const int16_
 template <bool W32, int NP>
 void ks_inner_items(LP dig, const PartPtrs& pp, const int16_t* src, int LT, int64_t n, int64_t B, const uint32_t* evka,
                     const uint32_t* evkb, uint32_t* KS, const ModC* mods, cudaStream_t st) {
-  static int resident = 0;   // blocks of this instantiation that fit on the GPU at once
-  if (!resident) {
-    int dev = 0, sms = 0, per_sm = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_ks_inner<W32, NP>, 128, 0);
-    resident = (sms > 0 ? sms : 148) * (per_sm > 0 ? per_sm : 4);
-  }
+  static PerDevice cache;   // blocks of this instantiation that fit on the GPU at once
+  const int resident = cache.get([] {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_ks_inner<W32, NP>, 128, 0) != cudaSuccess) {
+      (void)cudaGetLastError();
+      per_sm = 4;
+    }
+    return device_sm_count() * (per_sm > 0 ? per_sm : 4);
+  });
   const int64_t items = B * LT * (((n >> 2) + 127) / 128);
   const int64_t cap = resident;
   k_ks_inner<W32, NP><<<(unsigned)(items < cap ? items : cap), 128, 0, st>>>(dig, pp, src, LT, n, (int)B, evka, evkb,

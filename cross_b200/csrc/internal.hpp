@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdint>
 #include <vector>
 
@@ -62,6 +63,27 @@ struct cross_bconv_plan_s {
 };
 
 namespace cross {
+
+// A positive int cached per CUDA device (0 = not computed yet); safe to read and
+// fill from several host threads (a racing first use computes the same value).
+struct PerDevice {
+  static constexpr int kDevices = 64;
+  std::atomic<int> v[kDevices];
+  template <class F>
+  int get(F&& compute) {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kDevices) return compute();
+    int x = v[d].load(std::memory_order_relaxed);
+    if (x <= 0) {
+      x = compute();
+      v[d].store(x, std::memory_order_relaxed);
+    }
+    return x;
+  }
+};
+// Multiprocessors and shared memory per multiprocessor of the current device.
+int device_sm_count();
+int device_smem_per_sm();
 
 // reduce_fast (tc_ptx.cuh) returns finite_field.py's Barrett value exactly for
 // modulus mc when the true remainder z - t q stays inside (-(2^32 - q), 2^32)

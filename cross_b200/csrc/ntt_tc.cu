@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <vector>
 
@@ -726,11 +727,11 @@ __global__ void k_transpose_lp(LP in, uint32_t* __restrict__ out, int64_t lps, i
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-int g_num_sms = 0;
+// The driver's tensor-map encoder (one entry point for all devices).
+std::atomic<PFN_cuTensorMapEncodeTiled_v12000> g_encode{nullptr};
 
 int init_driver() {
-  if (!g_encode) {
+  if (!g_encode.load(std::memory_order_acquire)) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     CROSS_CHECK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
@@ -738,12 +739,7 @@ int init_driver() {
       set_error("cuTensorMapEncodeTiled is not available from the driver");
       return CROSS_ERR_UNSUPPORTED;
     }
-    g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
-  }
-  if (!g_num_sms) {
-    int dev = 0;
-    CROSS_CHECK_CUDA(cudaGetDevice(&dev));
-    CROSS_CHECK_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
+    g_encode.store((PFN_cuTensorMapEncodeTiled_v12000)fn, std::memory_order_release);
   }
   return CROSS_OK;
 }
@@ -751,7 +747,7 @@ int init_driver() {
 int encode(CUtensorMap* tm, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
            const cuuint64_t* strides, const cuuint32_t* box) {
   cuuint32_t es[4] = {1, 1, 1, 1};
-  CUresult r = g_encode(tm, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = g_encode.load(std::memory_order_acquire)(tm, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -791,36 +787,37 @@ int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaSt
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<EPI, NM, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)SMEM_BYTES));
   const int64_t units = (int64_t)a.slots * a.polys * (a.rows_m / BM) * (a.nout / 64);
-  const unsigned grid = (unsigned)(units < g_num_sms ? units : g_num_sms);
+  const int sms = device_sm_count();
+  const unsigned grid = (unsigned)(units < sms ? units : sms);
   k_bat_tc<EPI, NM, FAST><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }
 
-int g_max_pairs = 0;
-
 template <int EPI, bool NM, bool FAST, int DIM>
 int launch2(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
   auto kern = k_bat_tc2<EPI, NM, FAST, DIM>;
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES));
-  if (!g_max_pairs) {
-    // clusters of two 197 KiB CTAs that fit at once (compile-time cluster dims)
+  // clusters of two 225 KiB CTAs that fit at once (compile-time cluster dims);
+  // every instantiation has the same resources
+  static PerDevice pairs_cache;
+  const int max_pairs = pairs_cache.get([&] {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(g_num_sms & ~1));
+    cfg.gridDim = dim3((unsigned)(device_sm_count() & ~1));
     cfg.blockDim = dim3(THREADS);
     cfg.dynamicSmemBytes = SMEM2_BYTES;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &cfg) != cudaSuccess || n < 1) {
       (void)cudaGetLastError();
-      n = g_num_sms / 2;
+      n = device_sm_count() / 2;
     }
-    g_max_pairs = n;
-  }
+    return n;
+  });
   const int m_tiles = a.rows_m / BM, n_tiles = a.nout / 64;
   const int64_t rbs = a.polys * m_tiles, total = (int64_t)a.slots * ((rbs + 1) / 2);
   if (total == 0) return CROSS_OK;
-  int64_t groups = g_max_pairs / n_tiles;
+  int64_t groups = max_pairs / n_tiles;
   if (groups < 1) groups = 1;
   if (groups > total) groups = total;
   kern<<<(unsigned)(2 * groups * n_tiles), THREADS, SMEM2_BYTES, st>>>(tmA, tmB, a);
