@@ -26,7 +26,7 @@ sys.path.insert(0, ROOT)
 N_DEG, R, C, L, K, DNUM, BATCH = 65536, 256, 256, 24, 8, 3, 64
 # DRAM bytes (read + write) per k_bat_tc2 launch of the roofline NTT at batch 64,
 # from profiles/k_bat_tc2_ntt_n65536.md (batch-16 ncu capture scaled by 4).
-TRAFFIC_PER_LAUNCH = 3.242e9
+TRAFFIC_PER_LAUNCH = 3.148e9
 METRIC = "HE-Mult/s (N=2^16, L=24, dnum=3)"
 WORKLOAD = "CKKS HE-Mult + relinearisation, N=2^16 (256x256), L=24 x 28-bit, K=8, dnum=3, batch 64 per GPU"
 
@@ -201,7 +201,9 @@ def main():
     stream = torch.cuda.current_stream()
 
     def step():
+        torch.cuda.nvtx.range_push("hemul")
         he.mul(x, out=out, workspace=ws)
+        torch.cuda.nvtx.range_pop()
 
     for _ in range(args.warmup):
         step()
@@ -231,7 +233,9 @@ def main():
     hout = torch.empty(out.shape, dtype=torch.uint32).pin_memory()
 
     def e2e_step():
+        torch.cuda.nvtx.range_push("e2e")
         he.mul(hin, out=hout)
+        torch.cuda.nvtx.range_pop()
 
     e2e_step()
     torch.cuda.synchronize()
@@ -257,8 +261,12 @@ def main():
                       dtype=torch.uint8, device=dev)
 
     def ntt_once():
+        # NVTX range "roofline": profilers select these launches with
+        # --nvtx --nvtx-include "roofline/"
+        torch.cuda.nvtx.range_push("roofline")
         _lib.check(lib.cross_ntt(ctx.plan(), 0, xin.data_ptr(), xo.data_ptr(), lps, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED,
                                  nws.data_ptr(), nws.numel(), stream.cuda_stream), "cross_ntt")
+        torch.cuda.nvtx.range_pop()
 
     for _ in range(2):
         ntt_once()
