@@ -88,13 +88,14 @@ int device_smem_per_sm();
 // reduce_fast (tc_ptx.cuh) returns finite_field.py's Barrett value exactly for
 // modulus mc when the true remainder z - t q stays inside (-(2^32 - q), 2^32)
 // for every input: with t = floor(z m / 2^s) and m within one of 2^s / q,
-// |r| < (z / 2^s + 2) q, checked here for z < 2^53 and z < 2^31 q.
+// |r| < (z / 2^s + 2) q, checked here for z < 2^53 and z < 2^31 q + 2^32 (a
+// product of a word below 2^31 and a residue, plus a word).
 inline bool reduce_fast_ok(const ModC& mc) {
   if (mc.w != 32 || mc.s_w >= 32 || mc.m >= (1ull << 32)) return false;
   const unsigned __int128 q = mc.q;
   const unsigned s_bits = mc.w + mc.s_w;
   const unsigned __int128 lim = ((unsigned __int128)1 << 32) - q;
-  for (unsigned __int128 z : {(unsigned __int128)1 << 53, ((unsigned __int128)1 << 31) * q})
+  for (unsigned __int128 z : {(unsigned __int128)1 << 53, ((unsigned __int128)1 << 31) * q + ((unsigned __int128)1 << 32)})
     if (((z >> s_bits) + 3) * q >= lim) return false;
   return true;
 }

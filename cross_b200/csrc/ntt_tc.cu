@@ -227,8 +227,16 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
         else
           r = barrett((uint64_t)r * pre0[jj], mc);
       } else if (EPI == EPI_COMBINE) {
-        const uint64_t zc = (uint64_t)pre0[jj] * scal + r;
-        r = FAST ? barrett_w32(zc, q32, m32, sw) : barrett(zc, mc);
+        // x < 2^31 with beta < q and r < 2^32 keeps x beta + r below
+        // 2^31 q + 2^32, where the fast form is exact; larger x take the 64-bit form
+        const uint32_t x = pre0[jj];
+        if (FAST && x < 0x80000000u) {
+          const uint64_t zc = (uint64_t)x * scal + r;
+          r = reduce_fast2((uint32_t)zc, (uint32_t)(zc >> 32), q32, m32, sw);
+        } else {
+          const uint64_t zc = (uint64_t)x * scal + r;
+          r = FAST ? barrett_w32(zc, q32, m32, sw) : barrett(zc, mc);
+        }
       } else if (EPI == EPI_MODDOWN) {
         // sub < 2^31 with P^-1 < q keeps the product below 2^31 q, where the
         // fast form is exact; larger operands take the 64-bit form

@@ -115,7 +115,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 // min(r, r - q) is that comparison (r - q wraps above r exactly when r < q).
 // Callers enable this path only when reduce_fast_ok (internal.hpp) holds for
 // every modulus, which covers inputs z < 2^53 (contraction sums) and
-// z < 2^31 * q (products of a reduced value and a table entry).
+// z < 2^31 * q + 2^32 (a word below 2^31 times a residue, plus a word).
 __device__ __forceinline__ uint32_t reduce_fast2(uint32_t zlo, uint32_t zhi, uint32_t q, uint32_t m, uint32_t s_w) {
   const uint64_t u = (uint64_t)zhi * m + __umulhi(zlo, m);
   const uint32_t t = __funnelshift_r((uint32_t)u, (uint32_t)(u >> 32), s_w);
