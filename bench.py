@@ -278,6 +278,9 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize()
     ntt_ms = e0.elapsed_time(e1) / reps
+    # every tensor-core kernel of the timed work completed (no bounded wait expired)
+    he.check_device()
+    ctx.check_device()
     l0 = lib.cross_launch_count()
     ntt_once()
     torch.cuda.synchronize()

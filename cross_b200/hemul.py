@@ -130,6 +130,14 @@ class HEMul:
     def __del__(self):
         self._free_plan()
 
+    def check_device(self):
+        """Raise TimeoutError if a tensor-core kernel of this operator's plans hit
+        a bounded wait (its output is then invalid).  Synchronises the device."""
+        for name in ('ntt_qp', 'ntt_p', 'ks_bconv', 'bconv'):
+            obj = getattr(self, name, None)
+            if obj is not None and hasattr(obj, "check_device"):
+                obj.check_device()
+
     def workspace_size(self, batch: int, layout: int = _lib.LAYOUT_REFERENCE) -> int:
         return int(_lib.lib().cross_hemul_workspace_size(self._plan, batch, layout))
 

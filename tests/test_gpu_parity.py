@@ -383,6 +383,7 @@ def test_hemul_full_size_vs_oracle(L, K, dnum):
     he.control_gen(degree_layout=(256, 256))
     he.setup_relinearization(evk_a, evk_b)
     got = _np(he.mul(ct))
+    he.check_device()
     ref = O.HEMul(1, 256, 256, dnum, 1, Q, P)
     ref.setup_relinearization(evk_a, evk_b)
     np.testing.assert_array_equal(got, ref.mul(ct))
@@ -404,10 +405,12 @@ def test_herot_full_size_vs_oracle():
     h = herot.HERot(256, 256, dnum, Q, P)
     h.control_gen(batch=1, degree_layout=(256, 256))
     h.setup_rotate(evk_a, evk_b, cm)
+    got = _np(h.rotate(ct))
+    h.check_device()
     ref = O.HERot(256, 256, dnum, Q, P)
     ref.control_gen(1)
     ref.setup_rotate(evk_a.reshape(dnum, 256, 256, -1), evk_b.reshape(dnum, 256, 256, -1), cm)
-    np.testing.assert_array_equal(_np(h.rotate(ct)), ref.rotate(ct))
+    np.testing.assert_array_equal(got, ref.rotate(ct))
 
 
 @pytest.mark.parametrize("pinned", [True, False])
