@@ -535,7 +535,8 @@ int cross_bconv_plan_check(cross_bconv_plan P) {
 
 int cross_bconv(cross_bconv_plan P, int bat, const uint32_t* in, uint32_t* out, int64_t batch, int64_t n,
                 int layout, void* stream) {
-  CROSS_REQUIRE(P && in && out && in != out && batch >= 0 && n >= 0, "cross_bconv: bad argument");
+  CROSS_REQUIRE(P && batch >= 0 && n >= 0 && (batch == 0 || n == 0 || (in && out && in != out)),
+                "cross_bconv: bad argument");
   const int sq = P->sq, sp = P->sp;
   if (layout == CROSS_LAYOUT_REFERENCE)
     return bconv_run(P, bat != 0, in, n * sq, 1, sq, out, n * sp, 1, sp, batch, n, (cudaStream_t)stream);

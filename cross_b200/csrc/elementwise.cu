@@ -347,7 +347,7 @@ extern "C" {
 
 int cross_mod_reduce(cross_moduli mods, const void* in, int in_is_u64, uint32_t* out, int64_t rows,
                      void* stream) {
-  CROSS_REQUIRE(mods && in && out && rows >= 0, "cross_mod_reduce: bad argument");
+  CROSS_REQUIRE(mods && rows >= 0 && (rows == 0 || (in && out)), "cross_mod_reduce: bad argument");
   const int64_t total = rows * mods->n;
   if (total == 0) return CROSS_OK;
   if (in_is_u64) {
@@ -362,7 +362,7 @@ int cross_mod_reduce(cross_moduli mods, const void* in, int in_is_u64, uint32_t*
 
 int cross_modmul(cross_moduli mods, const void* a, int a_is_u64, const void* b, int b_is_u64,
                  int64_t b_rows, uint32_t* out, int64_t rows, void* stream) {
-  CROSS_REQUIRE(mods && a && b && out && rows >= 0 && b_rows >= 1, "cross_modmul: bad argument");
+  CROSS_REQUIRE(mods && rows >= 0 && b_rows >= 1 && (rows == 0 || (a && b && out)), "cross_modmul: bad argument");
   const int64_t total = rows * mods->n;
   if (total == 0) return CROSS_OK;
   k_modmul_ref<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, a_is_u64, b, b_is_u64, b_rows, out,
@@ -373,7 +373,8 @@ int cross_modmul(cross_moduli mods, const void* a, int a_is_u64, const void* b, 
 
 int cross_tensor_product(cross_moduli mods, const uint32_t* ct, uint32_t* out01, uint32_t* out2,
                          int64_t batch, int64_t n, void* stream) {
-  CROSS_REQUIRE(mods && ct && out01 && out2 && batch >= 0 && n >= 0, "cross_tensor_product: bad argument");
+  CROSS_REQUIRE(mods && batch >= 0 && n >= 0 && (batch == 0 || n == 0 || (ct && out01 && out2)),
+                "cross_tensor_product: bad argument");
   const int64_t per = n * mods->n;
   if (batch * per == 0) return CROSS_OK;
   k_tensor_ref<<<ew_blocks(batch * per, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(ct, out01, out2, batch, per,
@@ -384,7 +385,8 @@ int cross_tensor_product(cross_moduli mods, const uint32_t* ct, uint32_t* out01,
 
 int cross_add_mod(cross_moduli mods, const uint32_t* a, const uint32_t* b, uint32_t* out, int64_t elements,
                   int64_t n, void* stream) {
-  CROSS_REQUIRE(mods && a && b && out && elements >= 0 && n >= 0, "cross_add_mod: bad argument");
+  CROSS_REQUIRE(mods && elements >= 0 && n >= 0 && (elements == 0 || n == 0 || (a && b && out)),
+                "cross_add_mod: bad argument");
   const int64_t total = elements * mods->n * n;
   if (total == 0) return CROSS_OK;
   k_add_mod<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, b, out, total, n, mods->n, mods->dev); count_launch();
@@ -394,7 +396,7 @@ int cross_add_mod(cross_moduli mods, const uint32_t* a, const uint32_t* b, uint3
 
 int cross_automorphism(const uint32_t* in, const int32_t* coef_map, uint32_t* out, int64_t polys, int64_t n,
                        int num_limbs, void* stream) {
-  CROSS_REQUIRE(in && coef_map && out && polys >= 0 && n > 0 && num_limbs > 0 && in != out,
+  CROSS_REQUIRE(polys >= 0 && n > 0 && num_limbs > 0 && (polys == 0 || (in && coef_map && out && in != out)),
                 "cross_automorphism: bad argument (in and out must differ)");
   const int64_t total = polys * n * num_limbs;
   if (total == 0) return CROSS_OK;
@@ -405,14 +407,14 @@ int cross_automorphism(const uint32_t* in, const int32_t* coef_map, uint32_t* ou
 
 int cross_to_limb_major(const uint32_t* in, uint32_t* out, int64_t polys, int64_t n, int num_limbs,
                         void* stream) {
-  CROSS_REQUIRE(in && out && in != out && polys >= 0 && n > 0 && num_limbs > 0,
+  CROSS_REQUIRE(polys >= 0 && n > 0 && num_limbs > 0 && (polys == 0 || (in && out && in != out)),
                 "cross_to_limb_major: bad argument (in and out must differ)");
   return transpose_u32(in, out, polys, n, num_limbs, (cudaStream_t)stream);
 }
 
 int cross_to_reference(const uint32_t* in, uint32_t* out, int64_t polys, int64_t n, int num_limbs,
                        void* stream) {
-  CROSS_REQUIRE(in && out && in != out && polys >= 0 && n > 0 && num_limbs > 0,
+  CROSS_REQUIRE(polys >= 0 && n > 0 && num_limbs > 0 && (polys == 0 || (in && out && in != out)),
                 "cross_to_reference: bad argument (in and out must differ)");
   return transpose_u32(in, out, polys, num_limbs, n, (cudaStream_t)stream);
 }

@@ -520,7 +520,7 @@ size_t cross_hemul_workspace_size(cross_hemul_plan P, int64_t batch, int layout)
 
 int cross_hemul(cross_hemul_plan P, const uint32_t* in, uint32_t* out, int64_t B, int layout, void* ws,
                 size_t ws_bytes, void* stream) {
-  CROSS_REQUIRE(P && in && out && B >= 0, "cross_hemul: bad argument");
+  CROSS_REQUIRE(P && B >= 0 && (B == 0 || (in && out)), "cross_hemul: bad argument");
   CROSS_REQUIRE(P->evk_a && P->evk_b, "cross_hemul: keys not set (call cross_hemul_set_keys)");
   CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR, "cross_hemul: bad layout");
   CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || (((uintptr_t)in | (uintptr_t)out) & 15) == 0,
@@ -774,7 +774,7 @@ size_t cross_herot_workspace_size(cross_herot_plan P, int64_t batch, int layout)
 
 int cross_herot(cross_herot_plan P, const uint32_t* in, uint32_t* out, int64_t B, int layout, void* ws,
                 size_t ws_bytes, void* stream) {
-  CROSS_REQUIRE(P && in && out && B >= 0, "cross_herot: bad argument");
+  CROSS_REQUIRE(P && B >= 0 && (B == 0 || (in && out)), "cross_herot: bad argument");
   CROSS_REQUIRE(P->evk_a && P->evk_b && P->coef_map, "cross_herot: keys not set (call cross_herot_set_keys)");
   CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR, "cross_herot: bad layout");
   CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || (((uintptr_t)in | (uintptr_t)out) & 15) == 0,
@@ -935,7 +935,7 @@ size_t cross_rescale_workspace_size(cross_rescale_plan P, int64_t polys, int lay
 
 int cross_rescale(cross_rescale_plan P, const uint32_t* in, uint32_t* out, int64_t polys, int layout, void* ws,
                   size_t ws_bytes, void* stream) {
-  CROSS_REQUIRE(P && in && out && polys >= 0, "cross_rescale: bad argument");
+  CROSS_REQUIRE(P && polys >= 0 && (polys == 0 || (in && out)), "cross_rescale: bad argument");
   CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR, "cross_rescale: bad layout");
   if (polys == 0) return CROSS_OK;
   const size_t need = cross_rescale_workspace_size(P, polys, layout);

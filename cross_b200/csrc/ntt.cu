@@ -327,7 +327,7 @@ size_t cross_ntt_workspace_size(cross_ntt_plan P, int64_t batch, int layout) {
 
 int cross_ntt(cross_ntt_plan P, int inverse, const uint32_t* in, uint32_t* out, int64_t batch, int layout,
               void* workspace, size_t workspace_bytes, void* stream) {
-  CROSS_REQUIRE(P && in && out && batch >= 0, "cross_ntt: null argument or negative batch");
+  CROSS_REQUIRE(P && batch >= 0 && (batch == 0 || (in && out)), "cross_ntt: null argument or negative batch");
   CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR ||
                     layout == CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED,
                 "cross_ntt: unknown layout %d", layout);

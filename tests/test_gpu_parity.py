@@ -538,3 +538,49 @@ def test_errors_are_reference_exceptions():
     he.control_gen()
     with pytest.raises(RuntimeError):
         he.mul(np.zeros((1, 4, 4, 4, 2), U32))
+
+
+def test_empty_batches_are_no_ops():
+    """Batch 0 through every operator returns empty results without launching."""
+    import torch
+    from cross_b200 import hemul, herot, ntt_mm, bconv, _lib, util
+    n, L, K, dnum = 4096, 4, 2, 2
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    Q, P = ov[:L], ov[L:]
+    ctx = ntt_mm.NTTCiphertextBarrettContext(Q, {"r": 64, "c": 64})
+    assert tuple(ctx.ntt(np.zeros((0, 64, 64, L), U32)).shape) == (0, 64, 64, L)
+    b = bconv.BConvBarrett(ov)
+    b.control_gen([(list(range(L)), list(range(L, L + K)))])
+    assert tuple(b.basis_change_bat(np.zeros((0, n, L), U32)).shape) == (0, n, K)
+    rng = np.random.default_rng(5)
+    ek = [rng_residues(rng, (dnum, n, L + K), ov) for _ in range(2)]
+    he = hemul.HEMul(1, 64, 64, dnum, 1, Q, P)
+    he.control_gen(degree_layout=(64, 64))
+    he.setup_relinearization(*ek)
+    assert tuple(he.mul(np.zeros((0, 4, 64, 64, L), U32)).shape) == (0, 2, 64, 64, L - 1)
+    r, c = util.default_rc(n)
+    h = herot.HERot(r, c, dnum, Q, P)
+    h.control_gen(batch=1, degree_layout=(r, c))
+    h.setup_rotate(*ek, util.precompute_auto_map(n, util.find_automorphism_index_2n_complex(3, 2 * n)))
+    assert tuple(h.rotate(np.zeros((0, 2, r, c, L), U32)).shape) == (0, 2, n, L)
+
+
+def test_hemul_non_square_tensor_core_vs_oracle():
+    """HE-Mult on the tensor-core path with r != c (N = 2^15, 128 x 256; the
+    default (r, c) of the ModDown and key-switch transforms differs from the
+    input layout's), bit-exact against the oracle."""
+    from cross_b200 import hemul
+    n, L, K, dnum, B = 32768, 5, 2, 3, 2
+    ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+    Q, P = ov[:L], ov[L:]
+    rng = np.random.default_rng(31)
+    ct = rng_residues(rng, (B, 4, 128, 256, L), Q)
+    ek = [rng_residues(rng, (dnum, n, L + K), ov) for _ in range(2)]
+    he = hemul.HEMul(B, 128, 256, dnum, 1, Q, P)
+    he.control_gen(degree_layout=(128, 256))
+    he.setup_relinearization(*ek)
+    got = _np(he.mul(ct))
+    he.check_device()
+    ref = O.HEMul(B, 128, 256, dnum, 1, Q, P)
+    ref.setup_relinearization(*ek)
+    np.testing.assert_array_equal(got, ref.mul(ct))
