@@ -2,7 +2,7 @@
 
 TEST INFRASTRUCTURE ONLY.  Nothing in the ``cross_b200`` product imports,
 links or executes this package.  It may be used by ``tests/``, by
-``__graft_entry__.smoke()`` (as the checker of one small GPU invocation) and
+``__graft_entry__.smoke()`` (to verify one small GPU invocation) and
 by ``bench.py`` (the ``cpu_baseline`` leg and ``--impl reference``).
 
 ``cross_oracle`` is a numpy restatement of the reference's integer

@@ -369,7 +369,7 @@ def test_herot_vs_oracle(n, L, K, dnum, batch, k):
 @pytest.mark.parametrize("L,K,dnum", [(24, 8, 3), (35, 7, 5)])
 def test_hemul_full_size_vs_oracle(L, K, dnum):
     """N = 2^16 parameter sets for one ciphertext, bit-exact against the oracle:
-    the benchmark point (L = 24, K = 8, dnum = 3) and the multi-GPU box point
+    the benchmark point (L = 24, K = 8, dnum = 3) and the eight-GPU configuration
     (L = 35, K = 7, dnum = 5)."""
     from cross_b200 import hemul
     n = 65536
