@@ -166,7 +166,9 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
          ((uint64_t)1 << 46);
 }
 
-template <bool FAST, bool TWIST, int KB, int SPMAX>
+// NN: compile-time polynomial length with unit-stride limb rows (in_ls = out_ls
+// = n = NN), so tile arithmetic and store offsets are immediates; 0 = run time.
+template <bool FAST, bool TWIST, int KB, int SPMAX, int NN>
 __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a) {
   extern __shared__ uint8_t sm_raw[];
   uint8_t* As = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
@@ -179,12 +181,14 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
   ModC* sc = reinterpret_cast<ModC*>(tp + a.sp);          // [sq] source moduli
   uint32_t* shi = reinterpret_cast<uint32_t*>(sc + a.sq);        // [sq] QHatInvModq
   const int t = threadIdx.x, warp = t >> 5;
+  const int n = NN ? NN : a.n;
+  const int64_t in_ls = NN ? NN : a.in_ls, out_ls = NN ? NN : a.out_ls;
 
   for (int i = t; i < a.kb * (a.nn / 8) * 16; i += BT_THREADS)
     reinterpret_cast<uint4*>(Bs)[i] = reinterpret_cast<const uint4*>(a.bimg)[i];
   for (int j = t; j < a.sp; j += BT_THREADS) {
     dc[j] = make_uint4((uint32_t)a.dst[j].q, (uint32_t)a.dst[j].m, a.dst[j].s_w, TWIST ? a.trow[j] : 0u);
-    tp[j] = TWIST ? a.twist + (int64_t)a.trow[j] * a.n : nullptr;
+    tp[j] = TWIST ? a.twist + (int64_t)a.trow[j] * n : nullptr;
   }
   for (int i = t; i < a.sq; i += BT_THREADS) {
     sc[i] = a.src[i];
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t idesc = (2u << 4) | ((uint32_t)(a.nn >> 3) << 17) | ((uint32_t)(BT_ROWS >> 4) << 24);
-  const int tiles_pp = a.n / BT_ROWS;
+  const int tiles_pp = n / BT_ROWS;
   const int total = a.polys * tiles_pp;
   // Thread (row, h): coefficient row = TMEM lane, half h of the work.  It packs
   // the source limbs 4g..4g+3 for the K-halves g = 2gi + h, and produces the
@@ -224,7 +228,7 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int i = 4 * (2 * gi + h) + e;
-        xin[4 * gi + e] = i < a.sq ? __ldg(x + (int64_t)i * a.in_ls) : 0u;
+        xin[4 * gi + e] = i < a.sq ? __ldg(x + (int64_t)i * in_ls) : 0u;
       }
   };
   if ((int)blockIdx.x < total) load_inputs(blockIdx.x);
@@ -318,7 +322,7 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tc(const BconvTcArgs a)
               r = barrett(z, mc);
               if (TWIST) r = barrett((uint64_t)r * twj, mc);
             }
-            y[(int64_t)j * a.out_ls] = r;
+            y[(int64_t)j * out_ls] = r;
           }
         }
       }
@@ -347,10 +351,10 @@ size_t bconv_tc_smem(int sq, int sp, int kb, int nn, uint32_t tmem_cols, size_t 
   return (s > hi) ? 0 : s;
 }
 
-template <bool FAST, bool TWIST, int KB, int SPMAX>
+template <bool FAST, bool TWIST, int KB, int SPMAX, int NN>
 int launch_bconv_tc(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
   const int sms = device_sm_count();
-  auto kern = k_bconv_tc<FAST, TWIST, KB, SPMAX>;
+  auto kern = k_bconv_tc<FAST, TWIST, KB, SPMAX, NN>;
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t total = (int64_t)a.polys * (a.n / BT_ROWS);
   const int64_t cap = (int64_t)sms * ctas_per_sm;
@@ -362,9 +366,12 @@ int launch_bconv_tc(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cudaStre
 
 template <bool FAST, bool TWIST>
 int launch_bconv_tc_any(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
-  if (a.kb == 1 && a.sp <= 24) return launch_bconv_tc<FAST, TWIST, 1, 24>(a, smem, ctas_per_sm, st);
-  if (a.kb == 1) return launch_bconv_tc<FAST, TWIST, 1, 64>(a, smem, ctas_per_sm, st);
-  return launch_bconv_tc<FAST, TWIST, 4, 64>(a, smem, ctas_per_sm, st);
+  const bool n64k = a.n == 65536 && a.in_ls == 65536 && a.out_ls == 65536;
+  if (a.kb == 1 && a.sp <= 24)
+    return n64k ? launch_bconv_tc<FAST, TWIST, 1, 24, 65536>(a, smem, ctas_per_sm, st)
+                : launch_bconv_tc<FAST, TWIST, 1, 24, 0>(a, smem, ctas_per_sm, st);
+  if (a.kb == 1) return launch_bconv_tc<FAST, TWIST, 1, 64, 0>(a, smem, ctas_per_sm, st);
+  return launch_bconv_tc<FAST, TWIST, 4, 64, 0>(a, smem, ctas_per_sm, st);
 }
 
 template <int SQMAX, bool BAT>
