@@ -11,6 +11,7 @@ needs the reference checkout when the fixtures are regenerated:
 
 Sources:
   ntt_mm_test.py:13-24      NTT / INTT, N=16 (4x4), 3 x 134219681
+  ntt_sm_test.py:11-22      single-modulus NTT / INTT, N=16 (4x4), 134219681
   bconv_test.py:13-23       basis change 2 -> 5 moduli, N=16
   rescale_test.py:19-46     rescale 5 -> 4 moduli, N=16, OpenFHE text format
   herot_test.py:75-222      HE-Rotate, N=16, dnum=3, with stage references
@@ -80,6 +81,12 @@ def main(ref_dir):
     name, q, _psi, _batch, r, c, coef_in, eval_in = ntt[0]
     _dump("ntt_mm.json", dict(source="ntt_mm_test.py:13-24", moduli=q, r=r, c=c,
                               test_batch=2, coef_in=coef_in, eval_in=eval_in))
+
+    # ntt_sm_test.py:11-22 -- (name, modulus, psi, batch, r, c, coef_in, eval_in)
+    ntt = _top_assign(_module(os.path.join(ref_dir, "ntt_sm_test.py")), "NTT")
+    name, q, _psi, batch, r, c, coef_in, eval_in = ntt[0]
+    _dump("ntt_sm.json", dict(source="ntt_sm_test.py:11-22", modulus=q, r=r, c=c, batch=batch,
+                              coef_in=coef_in, eval_in=eval_in))
 
     # bconv_test.py:13-23
     tp = _top_assign(_module(os.path.join(ref_dir, "bconv_test.py")), "TEST_PARAMS")[0]

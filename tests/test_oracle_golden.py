@@ -135,3 +135,104 @@ def test_ntt_matches_schoolbook_negacyclic(n):
     omega = psi * psi % q
     nat = [sum(int(tw[i]) * pow(omega, i * k, q) for i in range(n)) % q for k in range(n)]
     np.testing.assert_array_equal(out, np.array(O.bit_reverse_array(nat)))
+
+
+# ---------------------------------------------------------------------------
+# Montgomery / Shoup / BAT-lazy variants (oracle/variants.py)
+# ---------------------------------------------------------------------------
+
+def _ntt_golden_batch():
+    g = load_golden("ntt_mm")
+    r, c, b = g["r"], g["c"], g["test_batch"]
+    coef = np.concatenate([np.array(g["coef_in"], np.uint64).T.reshape(1, r * c, -1)] * b, 0)
+    ev = np.concatenate([np.array(g["eval_in"], U32).T.reshape(1, r * c, -1)] * b, 0)
+    return g["moduli"], r, c, b, coef, ev
+
+
+def test_ntt_montgomery_golden():
+    """ntt_mm_test.py:56-90 (test_NTT_Montgomery): Montgomery-form input, NTT,
+    back to the original format."""
+    from oracle import variants as V
+    q, r, c, b, coef, ev = _ntt_golden_batch()
+    ctx = V.NTTVariant(q, r, c, "montgomery")
+    y = ctx.ntt(ctx.mont.to_computation_format(coef).reshape(b, r, c, -1))
+    np.testing.assert_array_equal(ctx.mont.to_original_format(y.reshape(b, r * c, -1)), ev)
+    np.testing.assert_array_equal(ctx.mont.to_original_format(ctx.intt(y).reshape(b, r * c, -1)), coef)
+
+
+def test_ntt_shoup_golden():
+    """ntt_mm_test.py:92-114 (test_NTT_Shoup)."""
+    from oracle import variants as V
+    q, r, c, b, coef, ev = _ntt_golden_batch()
+    ctx = V.NTTVariant(q, r, c, "shoup")
+    y = ctx.ntt(coef.astype(U32).reshape(b, r, c, -1))
+    np.testing.assert_array_equal(ctx.sh.to_original_format(y).reshape(b, r * c, -1), ev)
+    np.testing.assert_array_equal(ctx.sh.to_original_format(ctx.intt(y)).reshape(b, r * c, -1), coef)
+
+
+def test_ntt_bat_lazy_golden():
+    """ntt_mm_test.py:116-133 (test_NTT_BATLazy): exact equality."""
+    from oracle import variants as V
+    q, r, c, b, coef, ev = _ntt_golden_batch()
+    ctx = V.NTTVariant(q, r, c, "bat_lazy")
+    y = ctx.ntt(coef.astype(U32).reshape(b, r, c, -1))
+    np.testing.assert_array_equal(y.reshape(b, r * c, -1), ev)
+    np.testing.assert_array_equal(ctx.intt(y).reshape(b, r * c, -1), coef)
+
+
+@pytest.mark.parametrize("reduction", ["barrett", "montgomery", "bat_lazy", "shoup"])
+def test_ntt_single_modulus_golden(reduction):
+    """ntt_sm_test.py:28-107: the single-modulus contexts are the multi-modulus
+    transform with one modulus."""
+    from oracle import variants as V
+    g = load_golden("ntt_sm")
+    q, r, c = g["modulus"], g["r"], g["c"]
+    coef = np.array(g["coef_in"], np.uint64).reshape(1, r, c, 1)
+    ev = np.array(g["eval_in"], np.uint64)
+    ctx = O.NTTBarrett([q], r, c) if reduction == "barrett" else V.NTTVariant([q], r, c, reduction)
+    if reduction == "montgomery":
+        y = ctx.ntt(ctx.mont.to_computation_format(coef))
+        np.testing.assert_array_equal(ctx.mont.to_original_format(y).reshape(-1), ev)
+        np.testing.assert_array_equal(ctx.mont.to_original_format(ctx.intt(y)).reshape(-1), coef.reshape(-1))
+        return
+    y = ctx.ntt(coef.astype(U32))
+    np.testing.assert_array_equal(y.reshape(-1).astype(np.uint64) % q, ev)
+    np.testing.assert_array_equal(ctx.intt(y).reshape(-1).astype(np.uint64) % q, coef.reshape(-1))
+
+
+def test_bconv_bat_lazy_golden():
+    """bconv_test.py:53-76 (test_bat_lazy_context): uint64 output congruent to
+    the reference result."""
+    from oracle import variants as V
+    g = load_golden("bconv")
+    x = np.array(g["in_tower"], np.uint64).T
+    ref = np.array(g["reference_result"], np.uint64).T
+    bc = V.BConvVariant(g["original_moduli"] + g["target_moduli"], "bat_lazy")
+    bc.control_gen([(list(range(2)), list(range(2, 7)))])
+    out = bc.basis_change(x)
+    assert out.dtype == np.uint64
+    diff = (out.astype(np.int64) - ref.astype(np.int64)) % np.array(g["target_moduli"])
+    assert not diff.any()
+
+
+def test_reduction_contexts_known_answers():
+    """finite_field_test.py:40-80: Montgomery, Shoup and BAT-lazy single-modulus
+    products reduce to a*b mod q; plus the reference's 16-bit-split Montgomery
+    equals (z_hi + q - hi32(t q)) mod 2^32 on random 64-bit inputs."""
+    from oracle import variants as V
+    q = O.find_moduli_ntt(1, 31, 16)[0]
+    rng = np.random.default_rng(0)
+    a = rng.integers(0, q - 1, 4096, dtype=np.uint64)
+    b = rng.integers(0, q - 1, 4096, dtype=np.uint64)
+    ab_q = (a * b) % np.uint64(q)
+    mo = V.Montgomery(q)
+    res = mo.reduce(mo.to_computation_format(a).astype(np.uint64) * mo.to_computation_format(b).astype(np.uint64))
+    np.testing.assert_array_equal(mo.to_original_format(res), ab_q)
+    sh = V.Shoup(q)
+    np.testing.assert_array_equal(sh.to_original_format(sh.reduce(a * b, sh.precompute_constant_operand(a) * b)), ab_q)
+    lz = V.BATLazy(q)
+    np.testing.assert_array_equal(lz.to_original_format(lz.reduce(a * b)), ab_q)
+    z = rng.integers(0, 2 ** 63, 4096, dtype=np.uint64) * np.uint64(2) + rng.integers(0, 2, 4096, dtype=np.uint64)
+    qi = pow(q, -1, 1 << 32)
+    want = [((int(v) >> 32) + q - (((int(v) & 0xFFFFFFFF) * qi & 0xFFFFFFFF) * q >> 32)) & 0xFFFFFFFF for v in z]
+    np.testing.assert_array_equal(mo.reduce(z), np.array(want, np.uint64))
