@@ -2,9 +2,10 @@
 
 Drop-in for the jaxite_word operator API:
 
-    finite_field  BarrettContext (+ Montgomery/Shoup/BATLazy host formats)
-    ntt_mm        NTTCiphertextBarrettContext(moduli, {"r", "c", ...}).ntt / .intt
-    bconv         BConvBarrett(overall).control_gen(...).basis_change_bat / .basis_change
+    finite_field  BarrettContext, MontgomeryContext, ShoupContext, BATLazyContext
+    ntt_mm        NTTCiphertext{Barrett,Montgomery,Shoup,BATLazy}Context(moduli, {"r", "c", ...}).ntt / .intt
+    ntt_sm        NTT{Barrett,Montgomery,BATLazy,Shoup}Context(q, {"r", "c", ...}): one modulus
+    bconv         BConv{Barrett,Montgomery,Shoup,BATLazy}(overall).control_gen(...).basis_change_bat / .basis_change
     ciphertext    Ciphertext(shapes, parameters) with rescale / key_switch / ...
     hemul         HEMul(batch, r, c, dnum, 1, Q, P).control_gen / setup_relinearization / mul
     herot         HERot(r, c, dnum, Q, P).control_gen / setup_rotate / rotate

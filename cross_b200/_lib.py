@@ -16,6 +16,12 @@ LAYOUT_REFERENCE = 0
 LAYOUT_LIMB_MAJOR = 1
 LAYOUT_LIMB_MAJOR_TRANSPOSED = 2   # cross_ntt only: coefficients (M, c, r), evaluations (M, r, c)
 
+# cross_reduction (include/cross_b200.h): the finite_field.py context of a plan
+REDUCTION_BARRETT = 0
+REDUCTION_MONTGOMERY = 1
+REDUCTION_SHOUP = 2
+REDUCTION_BAT_LAZY = 3
+
 _STATUS = {-1: ValueError, -2: RuntimeError, -3: NotImplementedError, -4: MemoryError, -5: TimeoutError}
 
 vp = C.c_void_p
@@ -50,6 +56,7 @@ _SIGS = {
     "cross_moduli_create": (i32, [i32, vp, vp, vp, vp, C.POINTER(vp)]),
     "cross_moduli_destroy": (i32, [vp]),
     "cross_mod_reduce": (i32, [vp, vp, i32, vp, i64, vp]),
+    "cross_mod_reduce_ex": (i32, [vp, i32, vp, vp, vp, i64, vp]),
     "cross_modmul": (i32, [vp, vp, i32, vp, i32, i64, vp, i64, vp]),
     "cross_tensor_product": (i32, [vp, vp, vp, vp, i64, i64, vp]),
     "cross_add_mod": (i32, [vp, vp, vp, vp, i64, i64, vp]),
@@ -57,12 +64,18 @@ _SIGS = {
     "cross_to_limb_major": (i32, [vp, vp, i64, i64, i32, vp]),
     "cross_to_reference": (i32, [vp, vp, i64, i64, i32, vp]),
     "cross_ntt_plan_create": (i32, [vp, i32, i32, vp, vp, vp, vp, vp, vp, C.POINTER(vp)]),
+    "cross_ntt_plan_create_ex": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, C.POINTER(vp)]),
+    "cross_ntt_plan_create_shoup": (i32, [vp, i32, i32, C.POINTER(vp), C.POINTER(vp)]),
+    "cross_ntt_plan_reduction": (i32, [vp]),
     "cross_ntt_plan_destroy": (i32, [vp]),
     "cross_ntt_workspace_size": (sz, [vp, i64, i32]),
     "cross_ntt": (i32, [vp, i32, vp, vp, i64, i32, vp, sz, vp]),
     "cross_ntt_noalloc": (i32, [vp, i32, vp, vp, i64, vp]),
     "cross_ntt_plan_check": (i32, [vp]),
     "cross_bconv_plan_create": (i32, [vp, vp, vp, vp, vp, C.POINTER(vp)]),
+    "cross_bconv_plan_create_ex": (i32, [vp, vp, i32, vp, vp, vp, vp, vp, C.POINTER(vp)]),
+    "cross_bconv_output_bytes": (i32, [vp]),
+    "cross_bconv_ex": (i32, [vp, i32, vp, vp, i64, i64, i32, vp]),
     "cross_bconv_plan_destroy": (i32, [vp]),
     "cross_bconv_plan_check": (i32, [vp]),
     "cross_bconv": (i32, [vp, i32, vp, vp, i64, i64, i32, vp]),

@@ -39,6 +39,23 @@ def _u64_to_u32(x):
     return lo.contiguous().view(t.uint32)
 
 
+def to_u64(x):
+    """A contiguous uint64 CUDA tensor holding x (values zero-extended)."""
+    t = torch()
+    if isinstance(x, t.Tensor):
+        if x.dtype == t.uint64:
+            return x.to(device()).contiguous()
+        if x.dtype == t.uint32:
+            x = x.to(device()).contiguous()
+            lo = x.view(t.int32).to(t.int64) & 0xFFFFFFFF
+            return lo.view(t.uint64)
+        if x.dtype in (t.int64, t.int32):
+            return x.to(device()).to(t.int64).contiguous().view(t.uint64)
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    a = np.ascontiguousarray(np.asarray(x).astype(np.uint64))
+    return t.from_numpy(a).to(device())
+
+
 def to_any(x):
     """(tensor, is_u64) for an operand that may be uint32 or uint64."""
     t = torch()
@@ -62,9 +79,9 @@ def workspace(nbytes: int):
 
 
 def to_numpy(x):
-    t = torch()
-    if isinstance(x, t.Tensor):
-        return x.cpu().numpy()
+    """Host numpy view of a tensor (device tensors are copied) or array."""
+    if hasattr(x, "detach") and hasattr(x, "cpu"):
+        return x.detach().cpu().numpy()
     return np.asarray(x)
 
 

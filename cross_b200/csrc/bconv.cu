@@ -406,6 +406,10 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
               int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
               int64_t n, cudaStream_t st, const uint32_t* twist, const uint16_t* trow) {
   if (polys == 0 || n == 0) return CROSS_OK;
+  if (P->red != CROSS_REDUCTION_BARRETT) {
+    set_error("bconv: the HE chains take Barrett plans only (plan reduction %d)", P->red);
+    return CROSS_ERR_INVALID_ARG;
+  }
   if (bat && P->tc_bimg && in_ts == 1 && out_ts == 1 && n % BT_ROWS == 0 && polys * (n / BT_ROWS) < (1ll << 31)) {
     BconvTcArgs a{in, in_ps, in_ls, out, out_ps, out_ls, (int)polys, (int)n, P->sq, P->sp, P->tc_kb, P->tc_nn, 0,
                   P->src, P->dst, P->qhat_inv, P->tc_bimg, twist, trow, P->err, P->tc_src_fast != 0};
@@ -451,12 +455,19 @@ using namespace cross;
 
 extern "C" {
 
-int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* qhat_inv_modq,
-                            const uint32_t* qhat_modp, const uint8_t* qhat_modp_bat, cross_bconv_plan* out) {
+int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction, const uint32_t* qhat_inv_modq,
+                               const uint32_t* qhat_inv_modq_shoup, const uint32_t* qhat_modp,
+                               const uint32_t* qhat_modp_shoup, const uint8_t* qhat_modp_bat,
+                               cross_bconv_plan* out) {
   CROSS_REQUIRE(src && dst && qhat_inv_modq && qhat_modp && qhat_modp_bat && out,
                 "cross_bconv_plan_create: null argument");
+  CROSS_REQUIRE(reduction >= CROSS_REDUCTION_BARRETT && reduction <= CROSS_REDUCTION_BAT_LAZY,
+                "cross_bconv_plan_create_ex: unknown reduction %d", reduction);
+  CROSS_REQUIRE(reduction != CROSS_REDUCTION_SHOUP || (qhat_inv_modq_shoup && qhat_modp_shoup),
+                "cross_bconv_plan_create_ex: Shoup plans need the companion tables");
   *out = nullptr;
   auto* P = new cross_bconv_plan_s();
+  P->red = reduction;
   P->sq = src->n;
   P->sp = dst->n;
   P->src_host = src->host;
@@ -475,7 +486,7 @@ int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* 
   // tensor-core B operand: row n = 4j + b, K byte 4i + a, in the K-major
   // no-swizzle core-matrix layout of k_bconv_tc (sq <= 32, sp <= 64)
   std::vector<uint8_t> bimg;
-  if (sq <= 32 && sp <= 64) {
+  if (reduction == CROSS_REDUCTION_BARRETT && sq <= 32 && sp <= 64) {
     P->tc_kb = (sq + 7) / 8;
     P->tc_nn = (4 * sp + 15) / 16 * 16;
     const int kb = P->tc_kb, nn = P->tc_nn;
@@ -506,12 +517,34 @@ int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* 
   if (!rc) rc = upload_vec(&P->qhat_inv, qi);
   if (!rc) rc = upload_vec(&P->bat, bat);
   if (!rc) rc = upload_vec(&P->qhat_modp, qm);
+  if (!rc && reduction != CROSS_REDUCTION_BARRETT) {
+    rc = upload_vec(&P->src_v, make_varc(P->src_host));
+    if (!rc) rc = upload_vec(&P->dst_v, make_varc(P->dst_host));
+    if (!rc && reduction == CROSS_REDUCTION_SHOUP) {
+      std::vector<uint32_t> qs(qhat_inv_modq_shoup, qhat_inv_modq_shoup + sq), qms((size_t)sp * sq);
+      for (int i = 0; i < sq; ++i)
+        for (int j = 0; j < sp; ++j) qms[(size_t)j * sq + i] = qhat_modp_shoup[(size_t)i * sp + j];
+      rc = upload_vec(&P->qhat_inv_s, qs);
+      if (!rc) rc = upload_vec(&P->qhat_modp_s, qms);
+    }
+  }
   if (rc) {
     cross_bconv_plan_destroy(P);
     return rc;
   }
   *out = P;
   return CROSS_OK;
+}
+
+int cross_bconv_plan_create(cross_moduli src, cross_moduli dst, const uint32_t* qhat_inv_modq,
+                            const uint32_t* qhat_modp, const uint8_t* qhat_modp_bat, cross_bconv_plan* out) {
+  return cross_bconv_plan_create_ex(src, dst, CROSS_REDUCTION_BARRETT, qhat_inv_modq, nullptr, qhat_modp, nullptr,
+                                    qhat_modp_bat, out);
+}
+
+int cross_bconv_output_bytes(cross_bconv_plan P) {
+  CROSS_REQUIRE(P, "cross_bconv_output_bytes: null plan");
+  return P->red == CROSS_REDUCTION_BAT_LAZY ? 8 : 4;
 }
 
 int cross_bconv_plan_destroy(cross_bconv_plan P) {
@@ -523,6 +556,10 @@ int cross_bconv_plan_destroy(cross_bconv_plan P) {
   dfree(P->qhat_modp);
   dfree(P->tc_bimg);
   dfree(P->err);
+  dfree(P->src_v);
+  dfree(P->dst_v);
+  dfree(P->qhat_inv_s);
+  dfree(P->qhat_modp_s);
   delete P;
   return CROSS_OK;
 }
@@ -540,10 +577,25 @@ int cross_bconv_plan_check(cross_bconv_plan P) {
   return CROSS_OK;
 }
 
+int cross_bconv_ex(cross_bconv_plan P, int bat, const uint32_t* in, void* out, int64_t batch, int64_t n,
+                   int layout, void* stream) {
+  CROSS_REQUIRE(P && batch >= 0 && n >= 0 && (batch == 0 || n == 0 || (in && out && (const void*)in != out)),
+                "cross_bconv_ex: bad argument");
+  if (P->red == CROSS_REDUCTION_BARRETT) return cross_bconv(P, bat, in, (uint32_t*)out, batch, n, layout, stream);
+  const int sq = P->sq, sp = P->sp;
+  if (layout == CROSS_LAYOUT_REFERENCE)
+    return bconv_var_run(P, bat != 0, in, n * sq, 1, sq, out, n * sp, 1, sp, batch, n, (cudaStream_t)stream);
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_LIMB_MAJOR, "cross_bconv_ex: unknown layout %d", layout);
+  return bconv_var_run(P, bat != 0, in, n * sq, n, 1, out, n * sp, n, 1, batch, n, (cudaStream_t)stream);
+}
+
 int cross_bconv(cross_bconv_plan P, int bat, const uint32_t* in, uint32_t* out, int64_t batch, int64_t n,
                 int layout, void* stream) {
   CROSS_REQUIRE(P && batch >= 0 && n >= 0 && (batch == 0 || n == 0 || (in && out && in != out)),
                 "cross_bconv: bad argument");
+  CROSS_REQUIRE(P->red != CROSS_REDUCTION_BAT_LAZY,
+                "cross_bconv: BAT-lazy plans produce uint64 outputs; use cross_bconv_ex");
+  if (P->red != CROSS_REDUCTION_BARRETT) return cross_bconv_ex(P, bat, in, out, batch, n, layout, stream);
   const int sq = P->sq, sp = P->sp;
   if (layout == CROSS_LAYOUT_REFERENCE)
     return bconv_run(P, bat != 0, in, n * sq, 1, sq, out, n * sp, 1, sp, batch, n, (cudaStream_t)stream);

@@ -49,6 +49,44 @@ __device__ __forceinline__ uint32_t barrett_any(uint64_t z, const ModC& c) {
   return barrett(z, c);
 }
 
+// Per-modulus constants of the Montgomery and BAT-lazy reductions, derived
+// from q on the host (make_varc):
+//   qinv = q^-1 mod 2^32          MontgomeryContext.moduli_inv_32 (finite_field.py:72)
+//   winv = 2^-32 mod q            MontgomeryContext.w_inv         (finite_field.py:67)
+//   r[i] = 2^(32 + 8 i) mod q     BATLazyContext.R rows as words  (finite_field.py:363-370)
+struct VarC {
+  uint32_t q;
+  uint32_t qinv;
+  uint32_t winv;
+  uint32_t pad;
+  uint32_t r[4];
+};
+
+// MontgomeryContext.modular_reduction (finite_field.py:94-154):
+// t = z_lo q^-1 mod 2^32, result (z_hi + q - hi32(t q)) mod 2^32.  The
+// reference assembles hi32(t q) from four 16 x 16-bit partial products; the
+// 32 x 32 high word is the same integer.  Lazy: the result lies in [1, 2q)
+// when z_hi < q.
+__device__ __forceinline__ uint32_t montgomery(uint64_t z, uint32_t q, uint32_t qinv) {
+  const uint32_t t = (uint32_t)z * qinv;
+  return (uint32_t)(z >> 32) + q - __umulhi(t, q);
+}
+
+// BATLazyContext.modular_reduction (finite_field.py:384-425): with z split
+// into its low word A and the bytes B_i of its high word,
+// sum_j (sum_i B_i R[i][j] + A_j) << 8j = A + sum_i B_i (2^(32+8i) mod q),
+// exactly (every byte lane stays below 2^32).  uint64 result, congruent to z.
+__device__ __forceinline__ uint64_t bat_lazy(uint64_t z, const uint32_t* r) {
+  const uint32_t hi = (uint32_t)(z >> 32);
+  return (z & 0xFFFFFFFFull) + (uint64_t)(hi & 0xFFu) * r[0] + (uint64_t)((hi >> 8) & 0xFFu) * r[1] +
+         (uint64_t)((hi >> 16) & 0xFFu) * r[2] + (uint64_t)(hi >> 24) * r[3];
+}
+
+// ShoupContext.modular_reduction (finite_field.py:305-330) cast to uint32:
+// (z - (z_s >> 32) q) mod 2^32 depends only on the low word of z and of
+// t = z_s >> 32.
+__device__ __forceinline__ uint32_t shoup(uint32_t z_lo, uint32_t t, uint32_t q) { return z_lo - t * q; }
+
 // Byte recombination of the BAT contraction (ntt_mm.py:33-37):
 // sum_p acc_p << 8p in uint64.
 __device__ __forceinline__ uint64_t combine4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {

@@ -25,6 +25,23 @@ __global__ void k_mod_reduce(const void* __restrict__ in, uint32_t* __restrict__
   }
 }
 
+// The other finite_field.py reductions, elementwise with moduli on the last
+// axis: Montgomery and Shoup to uint32, BAT-lazy to uint64.
+template <int RED>
+__global__ void k_mod_reduce_var(const uint64_t* __restrict__ z, const uint64_t* __restrict__ zs,
+                                 void* __restrict__ out, int64_t total, int M, const VarC* __restrict__ v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const VarC& c = v[i % M];
+    if (RED == CROSS_REDUCTION_MONTGOMERY)
+      static_cast<uint32_t*>(out)[i] = montgomery(z[i], c.q, c.qinv);
+    else if (RED == CROSS_REDUCTION_SHOUP)
+      static_cast<uint32_t*>(out)[i] = shoup((uint32_t)z[i], (uint32_t)(zs[i] >> 32), c.q);
+    else
+      static_cast<uint64_t*>(out)[i] = bat_lazy(z[i], c.r);
+  }
+}
+
 __global__ void k_modmul_ref(const void* __restrict__ a, int a64, const void* __restrict__ b, int b64,
                              int64_t b_rows, uint32_t* __restrict__ out, int64_t total, int M,
                              const ModC* __restrict__ mods) {
@@ -354,6 +371,37 @@ int cross_mod_reduce(cross_moduli mods, const void* in, int in_is_u64, uint32_t*
     k_mod_reduce<true><<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, out, total, mods->n, mods->dev);
   } else {
     k_mod_reduce<false><<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, out, total, mods->n, mods->dev);
+  }
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_mod_reduce_ex(cross_moduli mods, int reduction, const uint64_t* z, const uint64_t* z_s, void* out,
+                        int64_t rows, void* stream) {
+  CROSS_REQUIRE(mods && rows >= 0 && (rows == 0 || (z && out)), "cross_mod_reduce_ex: bad argument");
+  CROSS_REQUIRE(reduction != CROSS_REDUCTION_SHOUP || rows == 0 || z_s,
+                "cross_mod_reduce_ex: Shoup's reduction needs z_s");
+  if (reduction == CROSS_REDUCTION_BARRETT) return cross_mod_reduce(mods, z, 1, (uint32_t*)out, rows, stream);
+  const int64_t total = rows * mods->n;
+  if (total == 0) return CROSS_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (reduction) {
+    case CROSS_REDUCTION_MONTGOMERY:
+      k_mod_reduce_var<CROSS_REDUCTION_MONTGOMERY><<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(z, z_s, out, total,
+                                                                                               mods->n, mods->dev_v);
+      break;
+    case CROSS_REDUCTION_SHOUP:
+      k_mod_reduce_var<CROSS_REDUCTION_SHOUP><<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(z, z_s, out, total, mods->n,
+                                                                                          mods->dev_v);
+      break;
+    case CROSS_REDUCTION_BAT_LAZY:
+      k_mod_reduce_var<CROSS_REDUCTION_BAT_LAZY><<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(z, z_s, out, total,
+                                                                                             mods->n, mods->dev_v);
+      break;
+    default:
+      set_error("cross_mod_reduce_ex: unknown reduction %d", reduction);
+      return CROSS_ERR_INVALID_ARG;
   }
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());

@@ -53,6 +53,40 @@ template int upload<uint8_t>(uint8_t**, const uint8_t*, size_t);
 template int upload<int16_t>(int16_t**, const int16_t*, size_t);
 template int upload<int32_t>(int32_t**, const int32_t*, size_t);
 template int upload<ModC>(ModC**, const ModC*, size_t);
+template int upload<VarC>(VarC**, const VarC*, size_t);
+
+// Inverse of a modulo an odd m (extended Euclid on signed 64-bit values; the
+// callers keep a and m below 2^32).
+static uint64_t inv_mod(uint64_t a, uint64_t m) {
+  int64_t t = 0, nt = 1, r = (int64_t)m, nr = (int64_t)(a % m);
+  while (nr) {
+    const int64_t qt = r / nr;
+    const int64_t t2 = t - qt * nt, r2 = r - qt * nr;
+    t = nt; nt = t2; r = nr; nr = r2;
+  }
+  return (uint64_t)(t < 0 ? t + (int64_t)m : t);
+}
+
+std::vector<VarC> make_varc(const std::vector<ModC>& mods) {
+  std::vector<VarC> v(mods.size());
+  for (size_t i = 0; i < mods.size(); ++i) {
+    const uint64_t q = mods[i].q;
+    VarC& c = v[i];
+    c.q = (uint32_t)q;
+    // q^-1 mod 2^32 by Newton's iteration (each step doubles the correct low bits)
+    uint32_t x = (uint32_t)q;
+    for (int k = 0; k < 5; ++k) x *= 2u - (uint32_t)q * x;
+    c.qinv = x;
+    c.winv = (uint32_t)inv_mod((1ull << 32) % q, q);
+    c.pad = 0;
+    uint64_t p = (1ull << 32) % q;
+    for (int j = 0; j < 4; ++j) {
+      c.r[j] = (uint32_t)p;
+      p = (p << 8) % q;
+    }
+  }
+  return v;
+}
 
 void dfree(void* p) {
   if (p) cudaFree(p);
@@ -86,7 +120,10 @@ int cross_moduli_create(int num_moduli, const uint32_t* moduli, const uint64_t* 
     s->host.push_back(cross::ModC{moduli[i], barrett_m[i], barrett_w[i], barrett_s_w[i]});
   }
   int rc = cross::upload_vec(&s->dev, s->host);
+  if (!rc) rc = cross::upload_vec(&s->dev_v, cross::make_varc(s->host));
   if (rc) {
+    cross::dfree(s->dev);
+    cross::dfree(s->dev_v);
     delete s;
     return rc;
   }
@@ -97,6 +134,7 @@ int cross_moduli_create(int num_moduli, const uint32_t* moduli, const uint64_t* 
 int cross_moduli_destroy(cross_moduli m) {
   if (!m) return CROSS_OK;
   cross::dfree(m->dev);
+  cross::dfree(m->dev_v);
   delete m;
   return CROSS_OK;
 }

@@ -386,6 +386,9 @@ int cross_hemul_plan_create(const cross_hemul_desc* d, cross_hemul_plan* out) {
   CROSS_REQUIRE(d->ntt_qp && d->ntt_p && d->ks_bconv && d->down_bconv && d->inv_psi_last && d->gamma_psi &&
                     d->betas && d->inv_psi_q && d->psi_qp && d->inv_psi_p && d->p_inv_mod_q,
                 "cross_hemul_plan_create: null table or plan");
+  CROSS_REQUIRE(d->ntt_qp->red == CROSS_REDUCTION_BARRETT && d->ntt_p->red == CROSS_REDUCTION_BARRETT &&
+                    d->down_bconv->red == CROSS_REDUCTION_BARRETT,
+                "cross_hemul_plan_create: HE-Mult runs on Barrett plans (hemul.py:58,69,98)");
   const int L = d->L, L1 = L - 1, K = d->K;
   const int64_t N = (int64_t)d->r * d->c;
   CROSS_REQUIRE(N % 4 == 0, "cross_hemul_plan_create: N=%lld must be a multiple of 4", (long long)N);
@@ -678,6 +681,8 @@ int cross_herot_plan_create(const cross_herot_desc* d, cross_herot_plan* out) {
   CROSS_REQUIRE(d->L >= 1 && d->K >= 1 && d->dnum >= 1 && d->ntt_qp && d->ks_bconv && d->down_bconv &&
                     d->inv_psi_q && d->psi_qp && d->inv_psi_p && d->p_inv_mod_q,
                 "cross_herot_plan_create: bad descriptor");
+  CROSS_REQUIRE(d->ntt_qp->red == CROSS_REDUCTION_BARRETT && d->down_bconv->red == CROSS_REDUCTION_BARRETT,
+                "cross_herot_plan_create: HE-Rotate runs on Barrett plans (herot.py:64, 161-175)");
   const int L = d->L, K = d->K, LT = L + K;
   const int64_t N = (int64_t)d->r * d->c;
   CROSS_REQUIRE(N % 4 == 0 && d->ntt_qp->M == LT && (int64_t)d->ntt_qp->r * d->ntt_qp->c == N,
@@ -899,6 +904,8 @@ int cross_rescale_plan_destroy(cross_rescale_plan P) {
 int cross_rescale_plan_create(const cross_rescale_desc* d, cross_rescale_plan* out) {
   CROSS_REQUIRE(d && out && d->ntt_q && d->inv_psi_last && d->gamma_psi && d->betas && d->L >= 2,
                 "cross_rescale_plan_create: bad descriptor");
+  CROSS_REQUIRE(d->ntt_q->red == CROSS_REDUCTION_BARRETT,
+                "cross_rescale_plan_create: rescale runs on a Barrett plan (ciphertext.py:251)");
   *out = nullptr;
   const int64_t N = (int64_t)d->r * d->c;
   CROSS_REQUIRE(N % 4 == 0 && (int64_t)d->ntt_q->r * d->ntt_q->c == N && d->ntt_q->M >= d->L,

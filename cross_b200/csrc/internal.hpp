@@ -13,6 +13,7 @@ struct cross_moduli_s {
   int n = 0;
   std::vector<cross::ModC> host;
   cross::ModC* dev = nullptr;
+  cross::VarC* dev_v = nullptr;     // Montgomery / Shoup / BAT-lazy constants of the same moduli
 };
 
 // NTT plan: the reference's BAT tables re-laid out for the kernels.
@@ -22,8 +23,16 @@ struct cross_moduli_s {
 // "brcmq,cqlpm").
 struct cross_ntt_plan_s {
   int r = 0, c = 0, M = 0;
+  int red = CROSS_REDUCTION_BARRETT;   // cross_reduction of the transform's reductions
   std::vector<cross::ModC> mods_host;
   cross::ModC* mods = nullptr;      // [M]
+  cross::VarC* varc = nullptr;      // [M] Montgomery / BAT-lazy constants (variant plans)
+  // Shoup plans (CUDA-core path): plain uint32 tables and their companions
+  // floor(T 2^32 / q), per limb, row-major:
+  //   sh[0] ntt T1 [M][r][r]   sh[1] ntt T2 [M][r][c]   sh[2] ntt T3 [M][c][c]
+  //   sh[3] intt T1 [M][c][c]  sh[4] intt T2 [M][r][c]  sh[5] intt T3 [M][r][r]
+  uint32_t* sh[6] = {};
+  uint32_t* sh_s[6] = {};
   // dp4a operands: 4 bytes over q packed into one u32, planes p separate.
   uint32_t* col_fwd = nullptr;      // [M][4 p][r z][r k]   from ntt_bat_tf_step1
   uint32_t* col_inv = nullptr;      // [M][4 p][r l][r k]   from intt_bat_tf_step3
@@ -49,6 +58,11 @@ struct cross_ntt_plan_s {
 
 struct cross_bconv_plan_s {
   int sq = 0, sp = 0;
+  int red = CROSS_REDUCTION_BARRETT;   // cross_reduction of the source / target contexts
+  cross::VarC* src_v = nullptr;        // [sq] variant constants of the source moduli
+  cross::VarC* dst_v = nullptr;        // [sp] variant constants of the target moduli
+  uint32_t* qhat_inv_s = nullptr;      // [sq]      Shoup companion of qhat_inv
+  uint32_t* qhat_modp_s = nullptr;     // [sp][sq]  Shoup companion of qhat_modp
   int tc_fast = 0;                  // tensor-core kernel may use reduce_fast / barrett_w32
   int tc_src_fast = 0;              // reduce_fast is exact for every source modulus
   int tc_kb = 0, tc_nn = 0;         // K blocks of 8 source limbs, MMA N (4 sp rounded up to 16)
@@ -101,6 +115,14 @@ inline bool reduce_fast_ok(const ModC& mc) {
 }
 // barrett_w32 (common.cuh) equals barrett for this modulus.
 inline bool barrett_w32_ok(const ModC& mc) { return mc.w == 32 && mc.m < (1ull << 32); }
+
+// Reduction applied by a contraction epilogue (template argument of the
+// kernels): the reference Barrett (generic or the exact 32-bit forms), or the
+// Montgomery / BAT-lazy variants of the NTT.
+enum RedMode { RED_BARRETT = 0, RED_BARRETT_FAST = 1, RED_MONTGOMERY = 2, RED_BAT_LAZY = 3 };
+
+// VarC of odd moduli q < 2^31 (cross_moduli guarantees both).
+std::vector<VarC> make_varc(const std::vector<ModC>& mods);
 
 // Bump allocator over a caller-provided workspace (or a size query when
 // base == nullptr).
@@ -188,6 +210,16 @@ int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, 
 void tc_plan_free(cross_ntt_plan_s* P);
 int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo out, int out_layout,
                 int64_t polys, int slots, const uint16_t* limbs, const Epi& epi, uint32_t* tmp, cudaStream_t st);
+
+// Natural-order NTT / INTT of a Shoup plan on the CUDA cores (ntt_shoup.cu).
+int ntt_run_shoup(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+                  const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
+
+// Basis conversion of a Montgomery / Shoup / BAT-lazy plan (bconv_var.cu);
+// out is uint64 for BAT-lazy plans, else uint32 (strides in elements).
+int bconv_var_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t in_ps, int64_t in_ls,
+                  int64_t in_ts, void* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
+                  int64_t n, cudaStream_t st);
 
 // NTT over polys x slots limb-polynomials (internal layout); limbs[slot] is the
 // plan limb of each slot (device array).  tmp holds ntt_tmp_words() words.

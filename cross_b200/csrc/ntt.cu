@@ -24,13 +24,29 @@ constexpr int TM = 16;   // output rows per block
 constexpr int TN = 64;   // output cols per block
 constexpr int TK = 32;   // contraction chunk
 
+// Reductions of one output: step 1 (+ step 2 when TWIDDLE) or step 3 of
+// ntt_mm.py:372-377 with the plan's reduction (RedMode): Barrett, Montgomery
+// (every reduction, ntt_mm.py:432-440), or BAT-lazy (step 1 lazy in uint64,
+// the step-2 product in uint64 with wrap-around, Barrett after; ntt_mm.py:602-630).
+template <bool TWIDDLE, int RED>
+__device__ __forceinline__ uint32_t stage_reduce(uint64_t z, const ModC& mc, const VarC& vc, uint32_t tw) {
+  if (RED == RED_MONTGOMERY) {
+    const uint32_t v = montgomery(z, vc.q, vc.qinv);
+    return TWIDDLE ? montgomery((uint64_t)v * tw, vc.q, vc.qinv) : v;
+  }
+  if (RED == RED_BAT_LAZY && TWIDDLE) return barrett_any(bat_lazy(z, vc.r) * tw, mc);
+  const uint32_t v = barrett_any(z, mc);
+  return TWIDDLE ? barrett_any((uint64_t)v * tw, mc) : v;
+}
+
 // Column transform: out[z, c] = epi( sum_k W[z, k] (.) X[k, c] ), k over R.
-template <bool TWIDDLE>
+template <bool TWIDDLE, int RED>
 __global__ void __launch_bounds__(256) k_col_dp4a(LP in, LPo out, int64_t lps, int slots,
                                                   const uint16_t* __restrict__ limbs, int R, int C,
                                                   const uint32_t* __restrict__ W,
                                                   const uint32_t* __restrict__ T2,
-                                                  const ModC* __restrict__ mods) {
+                                                  const ModC* __restrict__ mods,
+                                                  const VarC* __restrict__ varc) {
   __shared__ uint32_t Xs[TK][TN + 4];
   __shared__ uint32_t Ws[4][TM][TK + 1];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -76,13 +92,15 @@ __global__ void __launch_bounds__(256) k_col_dp4a(LP in, LPo out, int64_t lps, i
     const int z = z0 + ty;
     if (z < R) {
       const ModC mc = mods[limb];
+      VarC vc{};
+      if (RED >= RED_MONTGOMERY) vc = varc[limb];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int cc = c0 + tx * 4 + j;
         if (cc < C) {
-          uint32_t v = barrett_any(combine4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]), mc);
-          if (TWIDDLE) v = barrett_any((uint64_t)v * T2[((size_t)limb * R + z) * C + cc], mc);
-          y[(size_t)z * C + cc] = v;
+          const uint32_t tw = TWIDDLE ? T2[((size_t)limb * R + z) * C + cc] : 0u;
+          y[(size_t)z * C + cc] =
+              stage_reduce<TWIDDLE, RED>(combine4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]), mc, vc, tw);
         }
       }
     }
@@ -90,12 +108,13 @@ __global__ void __launch_bounds__(256) k_col_dp4a(LP in, LPo out, int64_t lps, i
 }
 
 // Row transform: out[r, n] = epi( sum_k X[r, k] (.) U[k, n] ), k over C.
-template <bool TWIDDLE>
+template <bool TWIDDLE, int RED>
 __global__ void __launch_bounds__(256) k_row_dp4a(LP in, LPo out, int64_t lps, int slots,
                                                   const uint16_t* __restrict__ limbs, int R, int C,
                                                   const uint32_t* __restrict__ U,
                                                   const uint32_t* __restrict__ T2,
-                                                  const ModC* __restrict__ mods) {
+                                                  const ModC* __restrict__ mods,
+                                                  const VarC* __restrict__ varc) {
   __shared__ uint32_t Xs[TM][TK + 1];
   __shared__ uint32_t Us[4][TK][TN + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -140,13 +159,15 @@ __global__ void __launch_bounds__(256) k_row_dp4a(LP in, LPo out, int64_t lps, i
     const int r = r0 + ty;
     if (r < R) {
       const ModC mc = mods[limb];
+      VarC vc{};
+      if (RED >= RED_MONTGOMERY) vc = varc[limb];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int nn = n0 + tx * 4 + j;
         if (nn < C) {
-          uint32_t v = barrett_any(combine4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]), mc);
-          if (TWIDDLE) v = barrett_any((uint64_t)v * T2[((size_t)limb * R + r) * C + nn], mc);
-          y[(size_t)r * C + nn] = v;
+          const uint32_t tw = TWIDDLE ? T2[((size_t)limb * R + r) * C + nn] : 0u;
+          y[(size_t)r * C + nn] =
+              stage_reduce<TWIDDLE, RED>(combine4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]), mc, vc, tw);
         }
       }
     }
@@ -197,6 +218,7 @@ int ntt_exec(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo 
   if (P->tc) return ntt_exec_tc(P, inverse, in, in_layout, out, out_layout, polys, slots, limbs, epi, tmp, st);
   // CUDA-core path: natural-order transforms composed with the layout
   // conversions and the position-wise op.
+  auto run = P->red == CROSS_REDUCTION_SHOUP ? ntt_run_shoup : ntt_run_dp4a;
   const int R = P->r, C = P->c;
   const int64_t N = (int64_t)R * C;
   uint32_t* t2 = tmp + lps * N;
@@ -207,14 +229,35 @@ int ntt_exec(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo 
       if ((rc = transpose_lp(in, LPo{t2, slots * N, N}, polys, slots, C, R, st))) return rc;
       src = LP{t2, slots * N, N};
     }
-    if ((rc = ntt_run_dp4a(P, false, src, out, polys, slots, limbs, tmp, st))) return rc;
+    if ((rc = run(P, false, src, out, polys, slots, limbs, tmp, st))) return rc;
   } else if (out_layout == COEF_NATURAL) {
-    if ((rc = ntt_run_dp4a(P, true, in, out, polys, slots, limbs, tmp, st))) return rc;
+    if ((rc = run(P, true, in, out, polys, slots, limbs, tmp, st))) return rc;
   } else {
-    if ((rc = ntt_run_dp4a(P, true, in, LPo{t2, slots * N, N}, polys, slots, limbs, tmp, st))) return rc;
+    if ((rc = run(P, true, in, LPo{t2, slots * N, N}, polys, slots, limbs, tmp, st))) return rc;
     if ((rc = transpose_lp(LP{t2, slots * N, N}, out, polys, slots, R, C, st))) return rc;
   }
   return apply_epi(epi, out, polys, slots, N, limbs, P->mods, st);
+}
+
+template <int RED>
+static int run_dp4a(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, LPo mid, LP mid_in, int64_t lps, int slots,
+                    const uint16_t* limbs, cudaStream_t st) {
+  const int R = P->r, C = P->c;
+  dim3 blk(256);
+  dim3 g((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
+  if (!inverse) {
+    k_col_dp4a<true, RED><<<g, blk, 0, st>>>(in, mid, lps, slots, limbs, R, C, P->col_fwd, P->tw_fwd, P->mods, P->varc);
+    count_launch();
+    k_row_dp4a<false, RED><<<g, blk, 0, st>>>(mid_in, out, lps, slots, limbs, R, C, P->row_fwd, nullptr, P->mods, P->varc);
+    count_launch();
+  } else {
+    k_row_dp4a<true, RED><<<g, blk, 0, st>>>(in, mid, lps, slots, limbs, R, C, P->row_inv, P->tw_inv, P->mods, P->varc);
+    count_launch();
+    k_col_dp4a<false, RED><<<g, blk, 0, st>>>(mid_in, out, lps, slots, limbs, R, C, P->col_inv, nullptr, P->mods, P->varc);
+    count_launch();
+  }
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
 }
 
 static int ntt_run_dp4a(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
@@ -225,20 +268,34 @@ static int ntt_run_dp4a(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out,
   if (lps == 0) return CROSS_OK;
   LPo mid{tmp, (int64_t)slots * N, N};
   LP mid_in{tmp, (int64_t)slots * N, N};
-  dim3 blk(256);
-  if (!inverse) {
-    dim3 g1((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
-    k_col_dp4a<true><<<g1, blk, 0, st>>>(in, mid, lps, slots, limbs, R, C, P->col_fwd, P->tw_fwd, P->mods); count_launch();
-    dim3 g2((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
-    k_row_dp4a<false><<<g2, blk, 0, st>>>(mid_in, out, lps, slots, limbs, R, C, P->row_fwd, nullptr, P->mods); count_launch();
-  } else {
-    dim3 g1((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
-    k_row_dp4a<true><<<g1, blk, 0, st>>>(in, mid, lps, slots, limbs, R, C, P->row_inv, P->tw_inv, P->mods); count_launch();
-    dim3 g2((C + TN - 1) / TN, (R + TM - 1) / TM, grid_z(lps));
-    k_col_dp4a<false><<<g2, blk, 0, st>>>(mid_in, out, lps, slots, limbs, R, C, P->col_inv, nullptr, P->mods); count_launch();
+  switch (P->red) {
+    case CROSS_REDUCTION_MONTGOMERY:
+      return run_dp4a<RED_MONTGOMERY>(P, inverse, in, out, mid, mid_in, lps, slots, limbs, st);
+    case CROSS_REDUCTION_BAT_LAZY:
+      return run_dp4a<RED_BAT_LAZY>(P, inverse, in, out, mid, mid_in, lps, slots, limbs, st);
+    default:
+      return run_dp4a<RED_BARRETT>(P, inverse, in, out, mid, mid_in, lps, slots, limbs, st);
   }
-  CROSS_CHECK_CUDA(cudaGetLastError());
-  return CROSS_OK;
+}
+
+// Plan fields shared by every reduction: sizes, moduli, identity limb map and,
+// for Montgomery / BAT-lazy, the per-limb VarC.  On failure *out is freed.
+static int plan_base(cross_moduli moduli, int r, int c, int red, cross_ntt_plan_s** out) {
+  const int M = moduli->n;
+  auto* P = new cross_ntt_plan_s();
+  *out = P;
+  P->r = r;
+  P->c = c;
+  P->M = M;
+  P->red = red;
+  P->mods_host = moduli->host;
+  std::vector<uint16_t> ident(M);
+  for (int i = 0; i < M; ++i) ident[i] = (uint16_t)i;
+  int rc = upload_vec(&P->mods, P->mods_host);
+  if (!rc) rc = upload_vec(&P->identity, ident);
+  if (!rc && (red == CROSS_REDUCTION_MONTGOMERY || red == CROSS_REDUCTION_BAT_LAZY))
+    rc = upload_vec(&P->varc, make_varc(P->mods_host));
+  return rc;
 }
 
 }  // namespace cross
@@ -247,28 +304,24 @@ using namespace cross;
 
 extern "C" {
 
-int cross_ntt_plan_create(cross_moduli moduli, int r, int c, const uint8_t* ntt_bat_tf_step1,
-                          const uint32_t* ntt_tf_step2, const uint8_t* ntt_bat_tf_step3,
-                          const uint8_t* intt_bat_tf_step1, const uint32_t* intt_tf_step2,
-                          const uint8_t* intt_bat_tf_step3, cross_ntt_plan* out) {
+int cross_ntt_plan_create_ex(cross_moduli moduli, int r, int c, int reduction, const uint8_t* ntt_bat_tf_step1,
+                             const uint32_t* ntt_tf_step2, const uint8_t* ntt_bat_tf_step3,
+                             const uint8_t* intt_bat_tf_step1, const uint32_t* intt_tf_step2,
+                             const uint8_t* intt_bat_tf_step3, cross_ntt_plan* out) {
   CROSS_REQUIRE(out && moduli && ntt_bat_tf_step1 && ntt_tf_step2 && ntt_bat_tf_step3 &&
                     intt_bat_tf_step1 && intt_tf_step2 && intt_bat_tf_step3,
                 "cross_ntt_plan_create: null argument");
   CROSS_REQUIRE(r >= 1 && c >= 1 && r <= 4096 && c <= 4096,
                 "cross_ntt_plan_create: r=%d c=%d out of range", r, c);
+  CROSS_REQUIRE(reduction == CROSS_REDUCTION_BARRETT || reduction == CROSS_REDUCTION_MONTGOMERY ||
+                    reduction == CROSS_REDUCTION_BAT_LAZY,
+                "cross_ntt_plan_create_ex: reduction %d needs another table set (Shoup: "
+                "cross_ntt_plan_create_shoup)", reduction);
   *out = nullptr;
+  cross_ntt_plan_s* P = nullptr;
+  int rc = plan_base(moduli, r, c, reduction, &P);
   const int M = moduli->n;
-  auto* P = new cross_ntt_plan_s();
-  P->r = r;
-  P->c = c;
-  P->M = M;
-  P->mods_host = moduli->host;
   std::vector<uint32_t> buf;
-  std::vector<uint16_t> ident(M);
-  for (int i = 0; i < M; ++i) ident[i] = (uint16_t)i;
-  int rc = CROSS_OK;
-  if (!rc) rc = upload_vec(&P->mods, P->mods_host);
-  if (!rc) rc = upload_vec(&P->identity, ident);
   if (!rc) { pack_bat(ntt_bat_tf_step1, r, r, M, buf); rc = upload_vec(&P->col_fwd, buf); }
   if (!rc) { pack_bat(intt_bat_tf_step3, r, r, M, buf); rc = upload_vec(&P->col_inv, buf); }
   if (!rc) { pack_bat(ntt_bat_tf_step3, c, c, M, buf); rc = upload_vec(&P->row_fwd, buf); }
@@ -286,6 +339,47 @@ int cross_ntt_plan_create(cross_moduli moduli, int r, int c, const uint8_t* ntt_
   }
   *out = P;
   return CROSS_OK;
+}
+
+int cross_ntt_plan_create(cross_moduli moduli, int r, int c, const uint8_t* ntt_bat_tf_step1,
+                          const uint32_t* ntt_tf_step2, const uint8_t* ntt_bat_tf_step3,
+                          const uint8_t* intt_bat_tf_step1, const uint32_t* intt_tf_step2,
+                          const uint8_t* intt_bat_tf_step3, cross_ntt_plan* out) {
+  return cross_ntt_plan_create_ex(moduli, r, c, CROSS_REDUCTION_BARRETT, ntt_bat_tf_step1, ntt_tf_step2,
+                                  ntt_bat_tf_step3, intt_bat_tf_step1, intt_tf_step2, intt_bat_tf_step3, out);
+}
+
+int cross_ntt_plan_create_shoup(cross_moduli moduli, int r, int c, const uint32_t* const* tables,
+                                cross_ntt_plan* out) {
+  CROSS_REQUIRE(out && moduli && tables, "cross_ntt_plan_create_shoup: null argument");
+  for (int i = 0; i < 12; ++i) CROSS_REQUIRE(tables[i], "cross_ntt_plan_create_shoup: table %d is null", i);
+  CROSS_REQUIRE(r >= 1 && c >= 1 && r <= 4096 && c <= 4096,
+                "cross_ntt_plan_create_shoup: r=%d c=%d out of range", r, c);
+  *out = nullptr;
+  cross_ntt_plan_s* P = nullptr;
+  int rc = plan_base(moduli, r, c, CROSS_REDUCTION_SHOUP, &P);
+  // (X, Y, M) host tables -> [M][X][Y]
+  const int dims[6][2] = {{r, r}, {r, c}, {c, c}, {c, c}, {r, c}, {r, r}};
+  std::vector<uint32_t> buf;
+  for (int i = 0; i < 6 && !rc; ++i) {
+    unpack_tw(tables[i], dims[i][0], dims[i][1], P->M, buf);
+    rc = upload_vec(&P->sh[i], buf);
+    if (!rc) {
+      unpack_tw(tables[6 + i], dims[i][0], dims[i][1], P->M, buf);
+      rc = upload_vec(&P->sh_s[i], buf);
+    }
+  }
+  if (rc) {
+    cross_ntt_plan_destroy(P);
+    return rc;
+  }
+  *out = P;
+  return CROSS_OK;
+}
+
+int cross_ntt_plan_reduction(cross_ntt_plan P) {
+  CROSS_REQUIRE(P, "cross_ntt_plan_reduction: null plan");
+  return P->red;
 }
 
 int cross_ntt_plan_check(cross_ntt_plan P) {
@@ -311,6 +405,11 @@ int cross_ntt_plan_destroy(cross_ntt_plan P) {
   dfree(P->row_inv);
   dfree(P->tw_fwd);
   dfree(P->tw_inv);
+  dfree(P->varc);
+  for (int i = 0; i < 6; ++i) {
+    dfree(P->sh[i]);
+    dfree(P->sh_s[i]);
+  }
   tc_plan_free(P);
   delete P;
   return CROSS_OK;

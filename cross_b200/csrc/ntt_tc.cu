@@ -67,6 +67,7 @@ struct Args {
   int64_t polys;
   int rows_m, kw, nout;
   const ModC* mods;
+  const VarC* varc;                // Montgomery / BAT-lazy constants per plan limb (variant plans)
   int* err;
   Epi e;                           // fused position-wise op (EpiOp)
 };
@@ -132,6 +133,7 @@ __device__ __forceinline__ Unit decode(int u, int nt_shift, int mt_shift, int po
 struct SlotCache {
   int slot = -1;
   ModC mc;
+  VarC vc;                         // RED_MONTGOMERY / RED_BAT_LAZY constants of the slot
   const uint32_t* tab = nullptr;   // EPI_MUL table row of the slot
   uint32_t scal = 0;               // EPI_COMBINE / EPI_MODDOWN scalar of the slot
 };
@@ -153,10 +155,16 @@ __device__ __forceinline__ int dim_kw(const Args& a) { return DIM ? DIM : a.kw; 
 // operands of the fused op are read at the same positions before the
 // accumulator is ready (16 consecutive words per thread when row major: four
 // 16-byte loads).  Returns false when the wait for the accumulator gave up.
-template <int EPI, bool NMAJOR, bool FAST, int DIM>
+// RED (RedMode) selects the reductions: Barrett (RED_BARRETT_FAST: the exact
+// 32-bit forms), or for the plain transforms of the variant plans Montgomery
+// (every reduction) or BAT-lazy (the first reduction lazy, Barrett after).
+template <int EPI, bool NMAJOR, int RED, int DIM>
 __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, uint64_t* tfull, uint32_t parity,
                                               volatile int& abort, const Unit& w, bool store, int warp, int lane,
                                               SlotCache& sc) {
+  static_assert(RED < RED_MONTGOMERY || EPI == EPI_NONE || EPI == EPI_MUL,
+                "variant reductions only run the plain transform epilogues");
+  constexpr bool FAST = RED == RED_BARRETT_FAST;
   constexpr int OUTS = 16;                     // outputs (64 columns) per thread and tile
   const int rows_m = dim_rows<DIM>(a), nout = dim_nout<DIM>(a);
   const int quad = warp & 3, part = (warp - 2) >> 2;
@@ -165,6 +173,7 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
   if (w.slot != sc.slot) {
     sc.slot = w.slot;
     sc.mc = a.mods[a.limbs[w.slot]];
+    if (RED >= RED_MONTGOMERY) sc.vc = a.varc[a.limbs[w.slot]];
     if (EPI == EPI_MUL) sc.tab = a.e.tab + (int64_t)a.e.trow[w.slot] * ((int64_t)rows_m * nout);
     if (EPI == EPI_COMBINE || EPI == EPI_MODDOWN) sc.scal = a.e.scal[w.slot];
   }
@@ -220,9 +229,19 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
     for (int j = 0; j < 8; ++j) {
       const int jj = chunk * 8 + j;
       const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      uint32_t r = FAST ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
+      uint32_t r;
+      if (RED == RED_MONTGOMERY)
+        r = montgomery(z, q32, sc.vc.qinv);
+      else if (RED == RED_BAT_LAZY && EPI == EPI_MUL)
+        r = 0;   // the lazy value feeds the twiddle product below
+      else
+        r = FAST ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
       if (EPI == EPI_MUL) {
-        if (FAST)
+        if (RED == RED_MONTGOMERY)
+          r = montgomery((uint64_t)r * pre0[jj], q32, sc.vc.qinv);
+        else if (RED == RED_BAT_LAZY)
+          r = barrett(bat_lazy(z, sc.vc.r) * pre0[jj], mc);
+        else if (FAST)
           r = reduce_fast2(r * pre0[jj], __umulhi(r, pre0[jj]), q32, m32, sw);
         else
           r = barrett((uint64_t)r * pre0[jj], mc);
@@ -286,7 +305,7 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
   return true;
 }
 
-template <int EPI, bool NMAJOR, bool FAST>
+template <int EPI, bool NMAJOR, int RED>
 __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ CUtensorMap tmA,
                                                        const __grid_constant__ CUtensorMap tmB, const Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -394,7 +413,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_bat_tc(const __grid_constant__ C
     SlotCache sc;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit w = decode(u, nt_shift, mt_shift, polys);
-      if (!epilogue_tile<EPI, NMAJOR, FAST, 0>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, true, warp,
+      if (!epilogue_tile<EPI, NMAJOR, RED, 0>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, true, warp,
                                                lane, sc))
         break;
       tc_fence_before();
@@ -556,7 +575,7 @@ struct PairIter {
   }
 };
 
-template <int EPI, bool NMAJOR, bool FAST, int DIM>
+template <int EPI, bool NMAJOR, int RED, int DIM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     k_bat_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -702,7 +721,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     for (int t = pw.t0; t < pw.t1; ++t, it.next(pw)) {
       bool valid;
       const Unit w = it.unit(pw, rank, valid);
-      if (!epilogue_tile<EPI, NMAJOR, FAST, DIM>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, valid, warp,
+      if (!epilogue_tile<EPI, NMAJOR, RED, DIM>(a, tmem + acc * BN, &S.tfull[acc], aphase, S.abort, w, valid, warp,
                                                  lane, sc))
         break;
       tc_fence_before();
@@ -790,22 +809,22 @@ int make_tmap_b(CUtensorMap* tm, const uint8_t* base, int kw, int nout, int M, i
   return encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box);
 }
 
-template <int EPI, bool NM, bool FAST>
+template <int EPI, bool NM, int RED>
 int launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
-  CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<EPI, NM, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  CROSS_CHECK_CUDA(cudaFuncSetAttribute(k_bat_tc<EPI, NM, RED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)SMEM_BYTES));
   const int64_t units = (int64_t)a.slots * a.polys * (a.rows_m / BM) * (a.nout / 64);
   const int sms = device_sm_count();
   const unsigned grid = (unsigned)(units < sms ? units : sms);
-  k_bat_tc<EPI, NM, FAST><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
+  k_bat_tc<EPI, NM, RED><<<grid, THREADS, SMEM_BYTES, st>>>(tmA, tmB, a);
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }
 
-template <int EPI, bool NM, bool FAST, int DIM>
+template <int EPI, bool NM, int RED, int DIM>
 int launch2(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, cudaStream_t st) {
-  auto kern = k_bat_tc2<EPI, NM, FAST, DIM>;
+  auto kern = k_bat_tc2<EPI, NM, RED, DIM>;
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES));
   // clusters of two 225 KiB CTAs that fit at once (compile-time cluster dims);
   // every instantiation has the same resources
@@ -848,7 +867,7 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
     set_error("tcgen05 stage: %lld limb-polynomials exceed one launch", (long long)(polys * slots));
     return CROSS_ERR_UNSUPPORTED;
   }
-  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->tc_err, e};
+  Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->varc, P->tc_err, e};
   if (!nmajor && e.op != EPI_NONE) {
     // row-major operands are read with 16-byte loads
     const View& x = e.op == EPI_MUL ? View{e.tab, 0, 0, 0, 1} : e.x;
@@ -864,10 +883,29 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
   const bool f = P->tc_fast != 0;
   const bool pair = P->tc_pair && kw <= 32 * B2_CHUNKS && kw % (32 * KPS) == 0;
   const bool d256 = rows_m == 256 && nout == 256 && kw == 256;
+  if (P->red == CROSS_REDUCTION_MONTGOMERY || P->red == CROSS_REDUCTION_BAT_LAZY) {
+    // variant plans: the plain transform stages (ntt_exec_tc's three epilogue
+    // shapes) with run-time dimensions
+#define CROSS_TC_VAR(OP, NM)                                                                       \
+  return P->red == CROSS_REDUCTION_MONTGOMERY                                                     \
+             ? (pair ? launch2<OP, NM, RED_MONTGOMERY, 0>(tmA, tmB2, a, st)                       \
+                     : launch<OP, NM, RED_MONTGOMERY>(tmA, tmB, a, st))                           \
+             : (pair ? launch2<OP, NM, RED_BAT_LAZY, 0>(tmA, tmB2, a, st)                         \
+                     : launch<OP, NM, RED_BAT_LAZY>(tmA, tmB, a, st))
+    if (e.op == EPI_MUL && nmajor) CROSS_TC_VAR(EPI_MUL, true);
+    if (e.op == EPI_NONE && nmajor) CROSS_TC_VAR(EPI_NONE, true);
+    if (e.op == EPI_NONE && !nmajor) CROSS_TC_VAR(EPI_NONE, false);
+#undef CROSS_TC_VAR
+    set_error("tcgen05 stage: epilogue %d (output major %d) not available with reduction %d", e.op, (int)nmajor,
+              P->red);
+    return CROSS_ERR_UNSUPPORTED;
+  }
 #define CROSS_TC_LAUNCH(OP, NM)                                                                                  \
-  return pair ? (d256 ? (f ? launch2<OP, NM, true, 256>(tmA, tmB2, a, st) : launch2<OP, NM, false, 256>(tmA, tmB2, a, st)) \
-                      : (f ? launch2<OP, NM, true, 0>(tmA, tmB2, a, st) : launch2<OP, NM, false, 0>(tmA, tmB2, a, st)))  \
-              : (f ? launch<OP, NM, true>(tmA, tmB, a, st) : launch<OP, NM, false>(tmA, tmB, a, st))
+  return pair ? (d256 ? (f ? launch2<OP, NM, RED_BARRETT_FAST, 256>(tmA, tmB2, a, st)                             \
+                           : launch2<OP, NM, RED_BARRETT, 256>(tmA, tmB2, a, st))                                 \
+                      : (f ? launch2<OP, NM, RED_BARRETT_FAST, 0>(tmA, tmB2, a, st)                               \
+                           : launch2<OP, NM, RED_BARRETT, 0>(tmA, tmB2, a, st)))                                  \
+              : (f ? launch<OP, NM, RED_BARRETT_FAST>(tmA, tmB, a, st) : launch<OP, NM, RED_BARRETT>(tmA, tmB, a, st))
   switch (e.op) {
     case EPI_NONE:
       if (nmajor) CROSS_TC_LAUNCH(EPI_NONE, true);

@@ -1,8 +1,12 @@
 """Multi-modulus BAT 3-step NTT (jaxite_word ntt_mm.py) on the GPU.
 
 The constructors precompute exactly the reference's tables (same names,
-shapes and values, ntt_mm.py:136-255); ``ntt`` / ``intt`` run the CUDA
-kernels of libcross_b200.so through the C ABI.
+shapes and values, ntt_mm.py:136-255, in the context's computation format);
+``ntt`` / ``intt`` run the CUDA kernels of libcross_b200.so through the C ABI.
+The reduction follows the reference: the finite-field context's type for the
+base / Barrett / Montgomery classes (ntt_mm.py:351-407 call
+``self.ff_ctx.modular_reduction``), BAT-lazy then Barrett for
+NTTCiphertextBATLazyContext, Shoup's for NTTCiphertextShoupContext.
 """
 from __future__ import annotations
 
@@ -33,6 +37,9 @@ def basis_aligned_transformation(matrix: np.ndarray, moduli) -> np.ndarray:
 class NTTCiphertextContextBase:
     """ntt_mm.py:125-419."""
 
+    def _default_ff_ctx(self):
+        return ff_context.BarrettContext(self.moduli)
+
     def __init__(self, moduli, parameters: dict, perf_test: bool = False):
         self.ff_ctx = parameters.get("finite_field_context", None)
         self.num_bytes = 4
@@ -50,15 +57,35 @@ class NTTCiphertextContextBase:
         # (ntt_mm.py:150-171); the real tables cost the same here, so they are
         # always used and results stay checkable.
         self.perf_test = perf_test
+        if self.ff_ctx is None:
+            self.ff_ctx = self._default_ff_ctx()
         self.memory_aligned_transformation()
         self.ntt_tf_step1, self.ntt_tf_step2, self.ntt_tf_step3 = self.ntt_coefficients_precompute()
         self.intt_tf_step1, self.intt_tf_step2, self.intt_tf_step3 = self.intt_coefficients_precompute()
-        self.ntt_bat_tf_step1 = basis_aligned_transformation(self.ntt_tf_step1, self.moduli)
-        self.ntt_bat_tf_step3 = basis_aligned_transformation(self.ntt_tf_step3, self.moduli)
-        self.intt_bat_tf_step1 = basis_aligned_transformation(self.intt_tf_step1, self.moduli)
-        self.intt_bat_tf_step3 = basis_aligned_transformation(self.intt_tf_step3, self.moduli)
+        self._format_tables()
         self._plan = None
         self._plan_barrett = None
+
+    def _format_tables(self):
+        """ntt_mm.py:172-181: BAT of the tables in the computation format."""
+        fmt = self.to_computation_format
+        self.ntt_bat_tf_step1 = basis_aligned_transformation(fmt(self.ntt_tf_step1), self.moduli)
+        self.ntt_tf_step2 = fmt(self.ntt_tf_step2).astype(U64)
+        self.ntt_bat_tf_step3 = basis_aligned_transformation(fmt(self.ntt_tf_step3), self.moduli)
+        self.intt_bat_tf_step1 = basis_aligned_transformation(fmt(self.intt_tf_step1), self.moduli)
+        self.intt_tf_step2 = fmt(self.intt_tf_step2).astype(U64)
+        self.intt_bat_tf_step3 = basis_aligned_transformation(fmt(self.intt_tf_step3), self.moduli)
+
+    def _reduction(self) -> int:
+        """The reduction ntt / intt apply: that of the finite-field context."""
+        if isinstance(self.ff_ctx, ff_context.MontgomeryContext):
+            return _lib.REDUCTION_MONTGOMERY
+        if isinstance(self.ff_ctx, ff_context.BarrettContext):
+            return _lib.REDUCTION_BARRETT
+        if isinstance(self.ff_ctx, ff_context.ShoupContext):
+            # ntt_mm.py:372 calls modular_reduction(z); Shoup's takes (z, z_s)
+            raise TypeError("ShoupContext.modular_reduction() needs z_s: use NTTCiphertextShoupContext")
+        raise NotImplementedError(f"{type(self).__name__}: no device transform for {type(self.ff_ctx).__name__}")
 
     # -- offline --------------------------------------------------------------
     def memory_aligned_transformation(self):
@@ -96,10 +123,12 @@ class NTTCiphertextContextBase:
         return st(t1), st(t2), st(t3)
 
     def to_computation_format(self, a):
-        return self.ff_ctx.to_computation_format(np.asarray(a).astype(U64)).astype(U32)
+        """ntt_mm.py:242-243 (host)."""
+        return np.asarray(self.ff_ctx.to_computation_format(_tensor.to_numpy(a).astype(U64))).astype(U32)
 
     def to_original_format(self, a):
-        return self.ff_ctx.to_original_format(np.asarray(a).astype(U64)).astype(U32)
+        """ntt_mm.py:245-246 (host)."""
+        return np.asarray(self.ff_ctx.to_original_format(_tensor.to_numpy(a).astype(U64))).astype(U32)
 
     def get_jax_parameters(self):
         return {"rows": self.r, "cols": self.c, "finite_field_parameters": self.ff_ctx.get_jax_parameters()}
@@ -118,8 +147,9 @@ class NTTCiphertextContextBase:
             arrs = [c(self.ntt_bat_tf_step1), c(self.ntt_tf_step2.astype(U32)), c(self.ntt_bat_tf_step3),
                     c(self.intt_bat_tf_step1), c(self.intt_tf_step2.astype(U32)), c(self.intt_bat_tf_step3)]
             out = _lib.vp()
-            _lib.check(_lib.lib().cross_ntt_plan_create(self._moduli_ctx().handle(), self.r, self.c,
-                                                        *[a.ctypes.data for a in arrs], _lib.C.byref(out)),
+            _lib.check(_lib.lib().cross_ntt_plan_create_ex(self._moduli_ctx().handle(), self.r, self.c,
+                                                           self._reduction(), *[a.ctypes.data for a in arrs],
+                                                           _lib.C.byref(out)),
                        "cross_ntt_plan_create")
             self._plan = out
         return self._plan
@@ -165,6 +195,10 @@ class NTTCiphertextContextBase:
         return self._single(limb_index).intt(_tensor.to_u32(v).unsqueeze(-1))[..., 0]
 
     def _single(self, i):
+        # ntt_limb uses BarrettContext.modular_reduction_single_modulus (ntt_mm.py:316-320),
+        # which only the Barrett context has
+        if self._reduction() != _lib.REDUCTION_BARRETT:
+            raise AttributeError(f"{type(self.ff_ctx).__name__} has no modular_reduction_single_modulus")
         return NTTCiphertextBarrettContext([self.moduli[i]], {"r": self.r, "c": self.c})
 
     def drop_last_modulus(self):
@@ -189,24 +223,92 @@ class NTTCiphertextBarrettContext(NTTCiphertextContextBase):
         assert self.moduli == list(self.ff_ctx.moduli), "moduli must be the same as the moduli of the finite_field_context"
 
 
-class _UnsupportedDeviceNTT(NTTCiphertextContextBase):
-    """Montgomery / Shoup / BAT-lazy NTT contexts: the constructors and tables
-    are the reference's; the device transforms are not implemented (they are
-    off the HE-Mult / HE-Rotate path, which always uses Barrett)."""
+class NTTCiphertextMontgomeryContext(NTTCiphertextContextBase):
+    """ntt_mm.py:432-440: Montgomery-form tables, Montgomery reductions."""
 
-    def ntt(self, v):
-        raise NotImplementedError(f"{type(self).__name__}.ntt has no device kernel; use NTTCiphertextBarrettContext")
+    def _default_ff_ctx(self):
+        return ff_context.MontgomeryContext(self.moduli)
 
-    intt = ntt
-
-
-class NTTCiphertextMontgomeryContext(_UnsupportedDeviceNTT):
-    """ntt_mm.py:432-440."""
+    def __init__(self, moduli, parameters: dict, perf_test: bool = False):
+        super().__init__(moduli, parameters, perf_test=perf_test)
+        assert self.moduli == list(self.ff_ctx.moduli), "moduli must be the same as the moduli of the finite_field_context"
 
 
-class NTTCiphertextShoupContext(_UnsupportedDeviceNTT):
-    """ntt_mm.py:443-587."""
+class NTTCiphertextBATLazyContext(NTTCiphertextContextBase):
+    """ntt_mm.py:590-658: step 1 reduced by BATLazyContext (a uint64 value),
+    the step-2 product taken in uint64 and Barrett-reduced, step 3 Barrett."""
+
+    def __init__(self, moduli, parameters: dict, perf_test: bool = False):
+        super().__init__(moduli, parameters, perf_test=perf_test)
+        assert self.moduli == list(self.ff_ctx.moduli), "moduli must be the same as the moduli of the finite_field_context"
+        self.ff_ctx_bat_lazy = ff_context.BATLazyContext(self.moduli)
+
+    def _reduction(self) -> int:
+        if not isinstance(self.ff_ctx, ff_context.BarrettContext):
+            raise NotImplementedError("NTTCiphertextBATLazyContext runs steps 2 and 3 with a BarrettContext")
+        return _lib.REDUCTION_BAT_LAZY
 
 
-class NTTCiphertextBATLazyContext(_UnsupportedDeviceNTT):
-    """ntt_mm.py:590-658."""
+class NTTCiphertextShoupContext(NTTCiphertextContextBase):
+    """ntt_mm.py:443-587: uint32 tables with their Shoup companions; every
+    matrix product is the exact uint64 (wrapping) sum, reduced by Shoup's
+    method and cast to uint32.  Runs on the CUDA cores."""
+
+    _TABLES = ("ntt_tf_step1", "ntt_tf_step2", "ntt_tf_step3", "intt_tf_step1", "intt_tf_step2", "intt_tf_step3")
+
+    def _default_ff_ctx(self):
+        return ff_context.ShoupContext(self.moduli)
+
+    def __init__(self, moduli, parameters: dict, perf_test: bool = False):
+        super().__init__(moduli, parameters, perf_test=perf_test)
+        assert self.moduli == list(self.ff_ctx.moduli), "moduli must be the same as the moduli of the finite_field_context"
+
+    def _format_tables(self):
+        """ntt_mm.py:457-469: computation format (a mod q) and the companions
+        floor(T 2^32 / q), computed from uint64 (ntt_mm.py:475-476)."""
+        ff = self.ff_ctx
+        for name in self._TABLES:
+            t = np.asarray(getattr(self, name))
+            setattr(self, name, self.to_computation_format(t).astype(U64 if name.endswith("step2") else U32))
+            setattr(self, name + "_shoup", np.asarray(ff.precompute_constant_operand(t.astype(U64))).astype(U64))
+        self.ntt_bat_tf_step1 = self.ntt_tf_step1
+        self.ntt_bat_tf_step3 = self.ntt_tf_step3
+        self.intt_bat_tf_step1 = self.intt_tf_step1
+        self.intt_bat_tf_step3 = self.intt_tf_step3
+
+    def to_computation_format(self, a):
+        """ntt_mm.py:471-472."""
+        return self.ff_ctx.to_computation_format(_tensor.to_numpy(a).astype(U64))
+
+    def to_shoup_computation_format(self, a):
+        """ntt_mm.py:474-475."""
+        return self.ff_ctx.precompute_constant_operand(np.asarray(a).astype(U64))
+
+    def to_original_format(self, a):
+        """ntt_mm.py:477-478."""
+        return self.ff_ctx.to_original_format(_tensor.to_numpy(a).astype(U64))
+
+    def _reduction(self) -> int:
+        return _lib.REDUCTION_SHOUP
+
+    def plan(self):
+        if self._plan is None:
+            names = list(self._TABLES) + [n + "_shoup" for n in self._TABLES]
+            arrs = [np.ascontiguousarray(np.asarray(getattr(self, n)).astype(U32)) for n in names]
+            ptrs = (_lib.vp * 12)(*[a.ctypes.data for a in arrs])
+            out = _lib.vp()
+            _lib.check(_lib.lib().cross_ntt_plan_create_shoup(self._moduli_ctx().handle(), self.r, self.c, ptrs,
+                                                              _lib.C.byref(out)), "cross_ntt_plan_create_shoup")
+            self._plan = out
+        return self._plan
+
+    def drop_last_modulus(self):
+        """ntt_mm.py:412-419; the Shoup tables the transform reads are sliced too."""
+        for name in list(self._TABLES) + [n + "_shoup" for n in self._TABLES]:
+            setattr(self, name, np.ascontiguousarray(getattr(self, name)[..., :-1]))
+        for name in ("ntt_bat_tf_step1", "ntt_bat_tf_step3", "intt_bat_tf_step1", "intt_bat_tf_step3"):
+            setattr(self, name, np.ascontiguousarray(getattr(self, name)[..., :-1]))
+        self.ff_ctx.drop_last_modulus()
+        if self._plan is not None:
+            _lib.lib().cross_ntt_plan_destroy(self._plan)
+            self._plan = None

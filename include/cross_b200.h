@@ -51,6 +51,15 @@ typedef enum cross_layout {
   CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED = 2
 } cross_layout;
 
+/* Modular reduction of a transform or basis conversion: the finite_field.py
+ * context the reference builds it on. */
+typedef enum cross_reduction {
+  CROSS_REDUCTION_BARRETT = 0,      /* BarrettContext    (finite_field.py:170-272) */
+  CROSS_REDUCTION_MONTGOMERY = 1,   /* MontgomeryContext (finite_field.py:58-164)  */
+  CROSS_REDUCTION_SHOUP = 2,        /* ShoupContext      (finite_field.py:278-338) */
+  CROSS_REDUCTION_BAT_LAZY = 3      /* BATLazyContext    (finite_field.py:344-428) */
+} cross_reduction;
+
 typedef struct cross_moduli_s* cross_moduli;
 typedef struct cross_ntt_plan_s* cross_ntt_plan;
 typedef struct cross_bconv_plan_s* cross_bconv_plan;
@@ -87,6 +96,14 @@ int cross_moduli_destroy(cross_moduli moduli);
  * `in` is uint64 when in_is_u64, else uint32. */
 int cross_mod_reduce(cross_moduli moduli, const void* in, int in_is_u64, uint32_t* out,
                      int64_t rows, void* stream);
+
+/* MontgomeryContext / ShoupContext / BATLazyContext.modular_reduction
+ * (finite_field.py:94-154, 305-330, 384-425), moduli on the last axis:
+ * z (rows, M) uint64 and, for Shoup, its companion product z_s (rows, M);
+ * out (rows, M) uint32, or uint64 for CROSS_REDUCTION_BAT_LAZY.
+ * CROSS_REDUCTION_BARRETT is cross_mod_reduce of uint64 input. */
+int cross_mod_reduce_ex(cross_moduli moduli, int reduction, const uint64_t* z, const uint64_t* z_s, void* out,
+                        int64_t rows, void* stream);
 
 /* Ciphertext.modmul (ciphertext.py:189-193) with the broadcast the reference
  * uses for its constant tables: out[i,m] = Barrett_m(a[i,m] * b[i % b_rows, m])
@@ -133,6 +150,41 @@ int cross_ntt_plan_create(cross_moduli moduli, int r, int c,
                           const uint32_t* intt_tf_step2, const uint8_t* intt_bat_tf_step3,
                           cross_ntt_plan* out);
 int cross_ntt_plan_destroy(cross_ntt_plan plan);
+
+/* The same transform with another reduction (same table arguments):
+ *   CROSS_REDUCTION_BARRETT     cross_ntt_plan_create.
+ *   CROSS_REDUCTION_MONTGOMERY  NTTCiphertextMontgomeryContext (ntt_mm.py:432-440)
+ *       and ntt_sm.NTTMontgomeryContext (ntt_sm.py:339-346): the tables are
+ *       the reference's Montgomery-form ones (ntt_mm.py:172-181), every
+ *       reduction is MontgomeryContext.modular_reduction.
+ *   CROSS_REDUCTION_BAT_LAZY    NTTCiphertextBATLazyContext (ntt_mm.py:590-658)
+ *       and ntt_sm.NTTBATLazyContext (ntt_sm.py:348-412): Barrett tables; the
+ *       first reduction of each transform is BATLazyContext.modular_reduction
+ *       (a uint64 value), multiplied by the step-2 table in uint64 with
+ *       wrap-around and Barrett-reduced; the last reduction is Barrett.
+ * `moduli` carries the Barrett constants in every case (the Montgomery and
+ * BAT-lazy constants are derived from the moduli). */
+int cross_ntt_plan_create_ex(cross_moduli moduli, int r, int c, int reduction,
+                             const uint8_t* ntt_bat_tf_step1, const uint32_t* ntt_tf_step2,
+                             const uint8_t* ntt_bat_tf_step3, const uint8_t* intt_bat_tf_step1,
+                             const uint32_t* intt_tf_step2, const uint8_t* intt_bat_tf_step3,
+                             cross_ntt_plan* out);
+
+/* NTTCiphertextShoupContext (ntt_mm.py:443-587) and ntt_sm.NTTShoupContext
+ * (ntt_sm.py:415-494): uint32 twiddle tables and their Shoup companions
+ * floor(T 2^32 / q), host arrays in the reference shapes, limbs last:
+ *   tables[0] ntt_tf_step1 (r, r, M)   tables[1] ntt_tf_step2 (r, c, M)
+ *   tables[2] ntt_tf_step3 (c, c, M)   tables[3] intt_tf_step1 (c, c, M)
+ *   tables[4] intt_tf_step2 (r, c, M)  tables[5] intt_tf_step3 (r, r, M)
+ *   tables[6..11] the *_shoup companions in the same order.
+ * Each matrix product is the reference's byte convolution recombined in
+ * uint64 (ntt_mm.py:40-65), i.e. the exact sum modulo 2^64, followed by
+ * ShoupContext.modular_reduction cast to uint32. */
+int cross_ntt_plan_create_shoup(cross_moduli moduli, int r, int c, const uint32_t* const* tables,
+                                cross_ntt_plan* out);
+
+/* The plan's cross_reduction. */
+int cross_ntt_plan_reduction(cross_ntt_plan plan);
 
 /* Scratch needed by cross_ntt for `batch` polynomials of all plan limbs. */
 size_t cross_ntt_workspace_size(cross_ntt_plan plan, int64_t batch, int layout);
@@ -193,6 +245,33 @@ int cross_bconv_plan_check(cross_bconv_plan plan);
  * in (batch, size_q, n) -> out (batch, size_p, n). */
 int cross_bconv(cross_bconv_plan plan, int bat, const uint32_t* in, uint32_t* out, int64_t batch,
                 int64_t n, int layout, void* stream);
+
+/* BConvMontgomery / BConvShoup / BConvBATLazy (bconv.py:261-390), or
+ * BConvBarrett for CROSS_REDUCTION_BARRETT (= cross_bconv_plan_create).  The
+ * arguments are the control's tables in the context's computation format
+ * (bconv.py:67-97): Montgomery form for MONTGOMERY, plain residues otherwise.
+ * qhat_inv_modq_shoup (size_q) and qhat_modp_shoup (size_q, size_p) are the
+ * Shoup companions of BConvShoup.control_gen (bconv.py:300-314); required for
+ * SHOUP, ignored (may be NULL) otherwise. */
+int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction, const uint32_t* qhat_inv_modq,
+                               const uint32_t* qhat_inv_modq_shoup, const uint32_t* qhat_modp,
+                               const uint32_t* qhat_modp_shoup, const uint8_t* qhat_modp_bat,
+                               cross_bconv_plan* out);
+
+/* Bytes per output element of cross_bconv_ex for this plan: 8 for
+ * CROSS_REDUCTION_BAT_LAZY (BATLazyContext.modular_reduction returns uint64,
+ * finite_field.py:421-425), else 4. */
+int cross_bconv_output_bytes(cross_bconv_plan plan);
+
+/* cross_bconv for a plan of any reduction; `out` holds elements of
+ * cross_bconv_output_bytes(plan) bytes.  Reference behaviours kept:
+ *   - MONTGOMERY basis_change (bat = 0) re-encodes source limb i with target
+ *     modulus i (bconv.py:278-280 broadcasts size_q against size_p), so it
+ *     needs size_q == size_p or size_p == 1, else CROSS_ERR_INVALID_ARG;
+ *   - SHOUP with bat != 0 is CROSS_ERR_UNSUPPORTED (the base-class BAT path
+ *     calls the two-operand Shoup reduction with one operand, bconv.py:244). */
+int cross_bconv_ex(cross_bconv_plan plan, int bat, const uint32_t* in, void* out, int64_t batch, int64_t n,
+                   int layout, void* stream);
 
 /* ------------------------------------------------------------------ */
 /* Rescale by the last prime (ciphertext.py:223-303)                   */

@@ -111,3 +111,66 @@ def test_digit_partition_matches():
         a, p, g = digits(L, d)
         oa, op, og = O.digit_partition(L, d)
         assert (a, p, g) == (oa, op, og)
+
+
+# ---------------------------------------------------------------------------
+# Montgomery / Shoup / BAT-lazy variants: host-side tables equal the oracle's
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("reduction", ["montgomery", "shoup", "bat_lazy"])
+def test_variant_ntt_tables_match_oracle(reduction):
+    """ntt_mm.py:172-181 (computation format + BAT) and 457-469 (Shoup)."""
+    from cross_b200 import ntt_mm
+    from oracle import variants as V
+    q = O.find_moduli_ntt(3, 28, 2 * 256)
+    cls = {"montgomery": ntt_mm.NTTCiphertextMontgomeryContext, "shoup": ntt_mm.NTTCiphertextShoupContext,
+           "bat_lazy": ntt_mm.NTTCiphertextBATLazyContext}[reduction]
+    ctx = cls(q, {"r": 16, "c": 16})
+    ref = V.NTTVariant(q, 16, 16, reduction)
+    if reduction == "shoup":
+        names = [n + s for n in cls._TABLES for s in ("", "_shoup")]
+    else:
+        names = ["ntt_bat_tf_step1", "ntt_tf_step2", "ntt_bat_tf_step3", "intt_bat_tf_step1", "intt_tf_step2",
+                 "intt_bat_tf_step3"]
+    for n in names:
+        np.testing.assert_array_equal(np.asarray(getattr(ctx, n)).astype(np.uint64),
+                                      np.asarray(getattr(ref, n)).astype(np.uint64), err_msg=n)
+
+
+@pytest.mark.parametrize("reduction", ["montgomery", "shoup", "bat_lazy"])
+def test_variant_bconv_constants_match_oracle(reduction):
+    """bconv.py:67-97 in the contexts' computation formats; BConvShoup's
+    companions (bconv.py:300-314) are 0: the reference shifts uint32 arrays by
+    32 under JAX."""
+    from cross_b200 import bconv
+    from oracle import variants as V
+    ov = O.find_moduli_ntt(9, 28, 64)
+    ctl = [([0, 1, 2], [3, 4, 5, 6, 7, 8])]
+    dev = {"montgomery": bconv.BConvMontgomery, "shoup": bconv.BConvShoup,
+           "bat_lazy": bconv.BConvBATLazy}[reduction](ov)
+    dev.control_gen(ctl)
+    ref = V.BConvVariant(ov, reduction)
+    ref.control_gen(ctl)
+    c = ref.controls[0]
+    np.testing.assert_array_equal(np.asarray(dev.QHatInvModq[0]).astype(np.uint64), c["qhat_inv"])
+    np.testing.assert_array_equal(np.asarray(dev.QHatModp[0]).astype(np.uint64), c["qhat_modp"])
+    np.testing.assert_array_equal(dev.QHatModpBAT[0], c["bat"])
+    if reduction == "shoup":
+        assert not np.asarray(dev.QHatInvModq_shoup[0]).any() and not np.asarray(dev.QHatModp_shoup[0]).any()
+        np.testing.assert_array_equal(dev.QHatModp_shoup[0], c["qhat_modp_shoup"])
+
+
+def test_single_modulus_contexts_expose_reference_tables():
+    """ntt_sm.py:143-152,214-221: the single-modulus tables are the
+    multi-modulus ones of one modulus."""
+    from cross_b200 import finite_field as ff, ntt_sm
+    q = O.find_moduli_ntt(1, 28, 2 * 256)[0]
+    ctx = ntt_sm.NTTBarrettContext(q, {"r": 16, "c": 16, "finite_field_context": ff.BarrettContext(q)})
+    ref = O.NTTBarrett([q], 16, 16)
+    np.testing.assert_array_equal(ctx.ntt_tf_bat_mat_comp_step1, ref.ntt_bat_tf_step1[..., 0])
+    np.testing.assert_array_equal(ctx.intt_tf_mat_comp_step2.astype(np.uint64), ref.intt_tf_step2[..., 0])
+    sh = ntt_sm.NTTShoupContext(q, {"r": 16, "c": 16, "finite_field_context": ff.ShoupContext(q)})
+    t = sh.ntt_tf_mat_step1
+    np.testing.assert_array_equal(sh.to_shoup_computation_format(t), sh.ntt_tf_mat_step1_shoup)
+    with pytest.raises(TypeError):
+        ntt_sm.NTTContextBase(q, {"r": 16, "c": 16, "finite_field_context": ff.ShoupContext(q)})
