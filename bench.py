@@ -7,7 +7,10 @@ rank processes its own batch of 64 (the reference shards the batch axis only).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Prints one JSON line on rank 0.
+Prints one JSON line on rank 0.  --workload ntt / bconv measure the transform
+and the basis conversion alone for one reduction (--reduction barrett,
+montgomery, shoup or bat_lazy): N = 2^16 NTT + INTT over 24 limbs x 16
+polynomials, and the 24 -> 25 limb BConv over 32 polynomials of N = 2^16.
 """
 from __future__ import annotations
 
@@ -164,6 +167,158 @@ def run_reference(args):
           flush=True)
 
 
+class _Timer:
+    """CUDA-event timing of `steps` calls on the current stream, max over ranks."""
+
+    def __init__(self, torch, dist, dev):
+        self.torch, self.dist, self.dev = torch, dist, dev
+
+    def __call__(self, fn, steps):
+        from cross_b200 import shard
+        t = self.torch
+        t.cuda.synchronize()
+        if self.dist:
+            self.dist.barrier()
+        e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+        st = t.cuda.current_stream()
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        t.cuda.synchronize()
+        return shard.max_over_ranks(e0.elapsed_time(e1), device=self.dev)
+
+
+def run_component(args, torch, dist, world, rank, local):
+    """--workload ntt | bconv for one reduction: device throughput, end-to-end
+    throughput through the operator API with host buffers, the kernel's
+    roofline and the oracle on the host cores."""
+    import numpy as np
+    from cross_b200 import _lib, bconv, finite_field as ff, ntt_mm
+    from oracle import cross_oracle as O
+    from oracle import variants as V
+    dev = torch.device("cuda", local)
+    timer = _Timer(torch, dist, dev)
+    lib = _lib.lib()
+    red = args.reduction
+    pk, src = peaks()
+    rng = np.random.default_rng(200 + rank)
+    if args.workload == "ntt":
+        Lw, B = 24, 16
+        q = O.find_moduli_ntt(Lw, 28, 2 * N_DEG)
+        cls = {"barrett": ntt_mm.NTTCiphertextBarrettContext, "montgomery": ntt_mm.NTTCiphertextMontgomeryContext,
+               "shoup": ntt_mm.NTTCiphertextShoupContext, "bat_lazy": ntt_mm.NTTCiphertextBATLazyContext}[red]
+        ctx = cls(q, {"r": R, "c": C})
+        xh = (rng.integers(0, 2 ** 62, size=(B, Lw, R, C), dtype=np.uint64) %
+              np.array(q, np.uint64)[:, None, None]).astype(np.uint32)
+        x = torch.from_numpy(xh).to(dev)
+        y = torch.empty_like(x)
+        ws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), B, _lib.LAYOUT_LIMB_MAJOR), dtype=torch.uint8,
+                         device=dev)
+        cs = torch.cuda.current_stream().cuda_stream
+
+        def step():
+            for inv, a, b in ((0, x, y), (1, y, y)):
+                _lib.check(lib.cross_ntt(ctx.plan(), inv, a.data_ptr(), b.data_ptr(), B, _lib.LAYOUT_LIMB_MAJOR,
+                                         ws.data_ptr(), ws.numel(), cs), "cross_ntt")
+        units = 2 * B * Lw                                   # limb-transforms per step
+        metric, unit = f"NTT+INTT limb-transforms/s (N=2^16, {red})", "limb-transform/s"
+        workload = f"BAT NTT then INTT, {red} reduction, N=2^16 (256x256), 24 limbs x 16 polys per GPU"
+        hin = torch.from_numpy(np.ascontiguousarray(xh.transpose(0, 2, 3, 1))).pin_memory()   # (B, R, C, L)
+
+        def e2e_step():
+            out = ctx.intt(ctx.ntt(hin))
+            return out.cpu()
+        sample_x = np.ascontiguousarray(xh[:1].transpose(0, 2, 3, 1))
+
+        def cpu_once():
+            ref = O.NTTBarrett(q, R, C) if red == "barrett" else V.NTTVariant(q, R, C, red)
+            t0 = time.perf_counter()
+            ref.intt(ref.ntt(sample_x))
+            return time.perf_counter() - t0
+        cpu_units = 2 * Lw
+        if red == "shoup":
+            # CUDA cores: per limb-transform 2 N (R + C) multiply-adds (the sum and
+            # its Shoup companion over both stages)
+            ops = units * 2.0 * N_DEG * (R + C)
+            nominal = 148 * 128 * 1.965e9 / 1e12
+            roof = {"bound": "cuda-core int32 issue", "unit": "TMAC/s", "peak": nominal,
+                    "peak_source": "nominal 148 SMs x 128 int32 lanes x 1965 MHz (no measured figure on this pool)"}
+        else:
+            ops = units * 32.0 * N_DEG * (R + C)
+            roof = {"bound": "tensor", "unit": "TOPS (int8)", "peak": 2.0 * pk["bf16_tflops"],
+                    "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src})"}
+        roof["kernel"] = "all launches of one NTT + INTT (2 contraction stages each)"
+    else:
+        sq, sp, B = 24, 25, 32
+        ov = O.find_moduli_ntt(sq + sp, 28, 2 * N_DEG)
+        cls = {"barrett": bconv.BConvBarrett, "montgomery": bconv.BConvMontgomery, "shoup": bconv.BConvShoup,
+               "bat_lazy": bconv.BConvBATLazy}[red]
+        bc = cls(ov)
+        bc.control_gen([(list(range(sq)), list(range(sq, sq + sp)))])
+        bat = red != "shoup"
+        xh = (rng.integers(0, 2 ** 62, size=(B, sq, N_DEG), dtype=np.uint64) %
+              np.array(ov[:sq], np.uint64)[:, None]).astype(np.uint32)
+        x = torch.from_numpy(xh).to(dev)
+        ob = lib.cross_bconv_output_bytes(bc.plan(0))
+        y = torch.empty((B, sp, N_DEG), dtype=torch.uint64 if ob == 8 else torch.uint32, device=dev)
+        cs = torch.cuda.current_stream().cuda_stream
+
+        def step():
+            _lib.check(lib.cross_bconv_ex(bc.plan(0), int(bat), x.data_ptr(), y.data_ptr(), B, N_DEG,
+                                          _lib.LAYOUT_LIMB_MAJOR, cs), "cross_bconv_ex")
+        units = B
+        metric, unit = f"BConv polys/s (N=2^16, 24->25 limbs, {red})", "poly/s"
+        workload = f"basis conversion {'basis_change_bat' if bat else 'basis_change'}, {red}, 24 -> 25 limbs, N=2^16, 32 polys per GPU"
+        hin = torch.from_numpy(np.ascontiguousarray(xh.transpose(0, 2, 1))).pin_memory()      # (B, N, sq)
+
+        def e2e_step():
+            out = bc.basis_change_bat(hin) if bat else bc.basis_change(hin)
+            return out.cpu()
+        sample_x = np.ascontiguousarray(xh[:1].transpose(0, 2, 1))
+
+        def cpu_once():
+            ref = O.BConvBarrett(ov) if red == "barrett" else V.BConvVariant(ov, red)
+            ref.control_gen([(list(range(sq)), list(range(sq, sq + sp)))])
+            t0 = time.perf_counter()
+            ref.basis_change_bat(sample_x) if bat else ref.basis_change(sample_x)
+            return time.perf_counter() - t0
+        cpu_units = 1
+        ops = units * (sq * 4 + sp * ob) * N_DEG
+        roof = {"bound": "hbm", "unit": "GB/s", "peak": pk["hbm_gbs"],
+                "peak_source": f"hbm_gbs of MEASURED_PEAKS.json ({src})",
+                "kernel": "k_bconv_tc (Barrett) / k_bconv_var (variants), one launch per step"}
+    for _ in range(args.warmup):
+        step()
+    ms = timer(step, args.steps)
+    l0 = lib.cross_launch_count()
+    step()
+    torch.cuda.synchronize()
+    launches = (lib.cross_launch_count() - l0) * args.steps
+    value = world * units * args.steps / (ms / 1000.0)
+    e2e_step()
+    ems = timer(e2e_step, args.steps)
+    e2e = world * units * args.steps / (ems / 1000.0)
+    per = ms / args.steps / 1000.0
+    achieved = ops / per / (1e12 if roof["unit"] != "GB/s" else 1e9)
+    roof.update({"achieved": achieved, "frac": achieved / roof["peak"], "traffic": None,
+                 "ms_per_step": ms / args.steps})
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u32 residues, u64 intermediates",
+            "data": "synthetic seeded uniform residues", "config": {"workload": workload, "reduction": red,
+                                                                    "l2": "inputs larger than L2"},
+            "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": int(hin.numel() * 4),
+                    "d2h_bytes_per_step": int(y.numel() * y.element_size())},
+            "gpu_launches": int(launches), "roofline": roof}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt = cpu_once()
+        line["cpu_baseline"] = {"value": cpu_units / dt, "unit": unit, "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"{cpu_units} units of the workload (oracle, numpy BLAS threads)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -172,6 +327,8 @@ def main():
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling runs use a small case)")
+    ap.add_argument("--workload", choices=["hemul", "ntt", "bconv"], default="hemul")
+    ap.add_argument("--reduction", choices=["barrett", "montgomery", "shoup", "bat_lazy"], default="barrett")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -186,6 +343,12 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    if args.workload != "hemul":
+        run_component(args, torch, dist, world, rank, local)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     from cross_b200 import _lib, hemul, ntt_mm
     batch = args.batch
