@@ -10,6 +10,8 @@ NTTCiphertextBATLazyContext, Shoup's for NTTCiphertextShoupContext.
 """
 from __future__ import annotations
 
+import functools
+
 import numpy as np
 
 from . import _lib, _tensor, util
@@ -32,6 +34,31 @@ def basis_aligned_transformation(matrix: np.ndarray, moduli) -> np.ndarray:
     red = np.stack([((mu << U64(8 * i)) % qs).astype(U32) for i in range(4)], 0)
     u8 = np.ascontiguousarray(red).view(np.uint8).reshape(*red.shape, 4)
     return np.ascontiguousarray(u8.transpose(1, 0, 2, 4, 3))
+
+
+@functools.lru_cache(maxsize=512)
+def _limb_tables(q: int, r: int, c: int):
+    """The six raw twiddle tables of one modulus (ntt_mm.py:186-240), shared
+    by every context that uses (q, r, c): HE-Mult, HE-Rotate and ciphertext
+    objects over overlapping moduli compute each limb once per process.
+    Read-only arrays."""
+    n = r * c
+    om = pow(util.root_of_unity(2 * n, q), 2, q)
+    perm_r, perm_c = get_bit_reverse_perm(r), get_bit_reverse_perm(c)
+    t1 = util.twiddle_matrix(r, r, q, pow(om, c, q))[perm_r, :]
+    t2 = util.twiddle_matrix(r, c, q, om)[perm_r, :]
+    t3 = util.twiddle_matrix(c, c, q, pow(om, r, q))[:, perm_c]
+    inv_col = pow(pow(om, c, q), -1, q)
+    inv_row = pow(pow(om, r, q), -1, q)
+    a = util.twiddle_matrix(c, c, q, inv_row)[perm_c, :]
+    b = util.twiddle_matrix(r, c, q, pow(om, -1, q))[perm_r, :]
+    d = util.twiddle_matrix(r, r, q, inv_col)[:, perm_r]
+    b = (b * U64(pow(c, -1, q))) % U64(q)
+    d = (d * U64(pow(r, -1, q))) % U64(q)
+    out = tuple(np.ascontiguousarray(t.astype(U32)) for t in (t1, t2, t3, a, b, d))
+    for t in out:
+        t.flags.writeable = False
+    return out
 
 
 class NTTCiphertextContextBase:
@@ -93,34 +120,17 @@ class NTTCiphertextContextBase:
         self.perm_r = get_bit_reverse_perm(self.r)
         self.perm_c = get_bit_reverse_perm(self.c)
 
+    def _tables(self, first: int):
+        per = [_limb_tables(int(q), self.r, self.c) for q in self.moduli]
+        return tuple(np.stack([t[first + k] for t in per], -1) for k in range(3))
+
     def ntt_coefficients_precompute(self):
-        """ntt_mm.py:186-209."""
-        t1, t2, t3 = [], [], []
-        for i, q in enumerate(self.moduli):
-            om = self.omega_list[i]
-            t1.append(util.twiddle_matrix(self.r, self.r, q, pow(om, self.c, q))[self.perm_r, :])
-            t2.append(util.twiddle_matrix(self.r, self.c, q, om)[self.perm_r, :])
-            t3.append(util.twiddle_matrix(self.c, self.c, q, pow(om, self.r, q))[:, self.perm_c])
-        st = lambda v: np.stack(v, -1).astype(U32)  # noqa: E731
-        return st(t1), st(t2), st(t3)
+        """ntt_mm.py:186-209 (per-modulus tables cached by _limb_tables)."""
+        return self._tables(0)
 
     def intt_coefficients_precompute(self):
-        """ntt_mm.py:211-240."""
-        t1, t2, t3 = [], [], []
-        for i, q in enumerate(self.moduli):
-            om = self.omega_list[i]
-            inv_col = pow(pow(om, self.c, q), -1, q)
-            inv_row = pow(pow(om, self.r, q), -1, q)
-            a = util.twiddle_matrix(self.c, self.c, q, inv_row)[self.perm_c, :]
-            b = util.twiddle_matrix(self.r, self.c, q, pow(om, -1, q))[self.perm_r, :]
-            d = util.twiddle_matrix(self.r, self.r, q, inv_col)[:, self.perm_r]
-            b = (b * U64(pow(self.c, -1, q))) % U64(q)
-            d = (d * U64(pow(self.r, -1, q))) % U64(q)
-            t1.append(a)
-            t2.append(b)
-            t3.append(d)
-        st = lambda v: np.stack(v, -1).astype(U32)  # noqa: E731
-        return st(t1), st(t2), st(t3)
+        """ntt_mm.py:211-240 (per-modulus tables cached by _limb_tables)."""
+        return self._tables(3)
 
     def to_computation_format(self, a):
         """ntt_mm.py:242-243 (host)."""
