@@ -79,6 +79,17 @@ _SIGS = {
     "cross_bconv_plan_destroy": (i32, [vp]),
     "cross_bconv_plan_check": (i32, [vp]),
     "cross_bconv": (i32, [vp, i32, vp, vp, i64, i64, i32, vp]),
+    "cross_fft_special": (i32, [vp, i64, i32, i32, vp, vp, i32, C.c_double, vp]),
+    "cross_ckks_max_abs_scaled": (i32, [vp, i64, C.c_double, vp, vp]),
+    "cross_ckks_quantize": (i32, [vp, vp, i32, C.c_double, i32, vp, vp, vp]),
+    "cross_mul_reduce_lm": (i32, [vp, vp, vp, vp, i64, vp]),
+    "cross_ckks_decrypt_sum": (i32, [vp, vp, i32, vp, vp, i64, vp]),
+    "cross_ckks_encrypt": (i32, [vp, vp, vp, vp, vp, vp, vp, C.c_uint64, vp, vp, i64, vp]),
+    "cross_pke_b": (i32, [vp, vp, vp, vp, C.c_uint64, vp, i64, vp]),
+    "cross_crt_combine": (i32, [vp, vp, i64, vp, vp, vp, i32, vp, vp]),
+    "cross_ckks_decode_scale": (i32, [vp, i32, vp, vp, C.c_double, i32, i32, vp, vp, vp]),
+    "cross_ckks_decode_stddev": (i32, [vp, i32, vp, vp]),
+    "cross_ckks_decode_combine": (i32, [vp, vp, i32, C.c_double, vp]),
     "cross_rescale_plan_create": (i32, [C.POINTER(RescaleDesc), C.POINTER(vp)]),
     "cross_rescale_plan_destroy": (i32, [vp]),
     "cross_rescale_workspace_size": (sz, [vp, i64, i32]),

@@ -19,7 +19,7 @@ OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "libcross_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "cross_b200.h")
 SOURCES = ["errors.cu", "ntt.cu", "ntt_tc.cu", "ntt_shoup.cu", "ntt_noalloc.cu", "elementwise.cu", "bconv.cu",
-           "bconv_var.cu", "hemul.cu"]
+           "bconv_var.cu", "hemul.cu", "ckks.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 

@@ -274,6 +274,77 @@ int cross_bconv_ex(cross_bconv_plan plan, int bat, const uint32_t* in, void* out
                    int layout, void* stream);
 
 /* ------------------------------------------------------------------ */
+/* CKKS client side (ckks_ctx.py, key_gen.py)                          */
+/* ------------------------------------------------------------------ */
+/* Double-precision steps evaluate every complex product as
+ * (a.re b.re - a.im b.im, a.re b.im + a.im b.re) and every sum in CPython's
+ * order without fused multiply-adds, so with the caller's twiddles (the
+ * reference's cmath.exp values) the results are bit-identical. */
+
+/* FFTSpecialInv / FFTSpecial (ckks_ctx.py:48-110) in place on `batch`
+ * vectors of nh complex doubles (interleaved re, im); m a power of two, at
+ * least 4 nh (decode runs nh = slots with m = 2 degree); roots: the m
+ * complex values exp(2 pi i k / m) (_roots), rot: the nh powers of 5 mod m
+ * (_rot_group); inv_scale: 1.0 / nh, applied by the inverse transform. */
+int cross_fft_special(double* vals, int64_t batch, int nh, int m, const double* roots, const uint32_t* rot,
+                      int inverse, double inv_scale, void* stream);
+
+/* max |scale * v| over n doubles, written to *out (device); encode takes
+ * ceil(log2) of it (ckks_ctx.py:357-365). */
+int cross_ckks_max_abs_scaled(const double* v, int64_t n, double scale, double* out, void* stream);
+
+/* ckks_ctx.py:356-387: the 2 nh coefficients of slot_to_coeffs(y) (y: nh
+ * complex doubles) scaled, divided by 2^log_approx, rounded with
+ * nearest_int, fitted into every tower (fit_to_native_vector), times
+ * 2^log_approx and times factor[t] (device array, NULL = 1) mod q_t:
+ * out (M, 2 nh) uint32 coefficients. */
+int cross_ckks_quantize(cross_moduli moduli, const double* y, int nh, double scale, int log_approx,
+                        const uint32_t* factor, uint32_t* out, void* stream);
+
+/* out[t][i] = x[t][i] * tab[t][i] mod q_t, fully reduced (tab NULL: x mod q_t);
+ * x, tab, out (M, n) limb-major. */
+int cross_mul_reduce_lm(cross_moduli moduli, const uint32_t* x, const uint32_t* tab, uint32_t* out, int64_t n,
+                        void* stream);
+
+/* ckks_decrypt's accumulation (ckks_ctx.py:264-294): c0 + sum_{i>=1} c_i s^i
+ * per tower, reduced after every step; c (elements, n, M), s (M, n) in
+ * evaluation form; out (M, n). */
+int cross_ckks_decrypt_sum(cross_moduli moduli, const uint32_t* c, int elements, const uint32_t* s, uint32_t* out,
+                           int64_t n, void* stream);
+
+/* ckks_encrypt's combination (ckks_ctx.py:198-228): c0 = ((v pk0 + ns e0) mod q
+ * + m) mod q, c1 = (v pk1 + ns e1) mod q; v, e0, e1, pk0, pk1 (M, n);
+ * m, c0, c1 (n, M). */
+int cross_ckks_encrypt(cross_moduli moduli, const uint32_t* m, const uint32_t* v, const uint32_t* e0,
+                       const uint32_t* e1, const uint32_t* pk0, const uint32_t* pk1, uint64_t noise_scale,
+                       uint32_t* c0, uint32_t* c1, int64_t n, void* stream);
+
+/* gen_pke_pair's b (key_gen.py:328-337): ((e ns) mod q - (a s) mod q) mod q, all (M, n). */
+int cross_pke_b(cross_moduli moduli, const uint32_t* e, const uint32_t* a, const uint32_t* s, uint64_t noise_scale,
+                uint32_t* b, int64_t n, void* stream);
+
+/* _crt_combine_rns_plaintext (ckks_ctx.py:517-545): rns (n, M) -> out (n,
+ * words) little-endian uint32 words of X mod Q.  inv (M): (Q/q_i)^-1 mod q_i;
+ * mi (M, words): Q/q_i; q_words (words): Q.  words <= 66, M <= 64. */
+int cross_crt_combine(cross_moduli moduli, const uint32_t* rns, int64_t n, const uint32_t* inv, const uint32_t* mi,
+                      const uint32_t* q_words, int words, uint32_t* out, void* stream);
+
+/* ckks_decode's first step (ckks_ctx.py:421-441): for slot i < slots, the
+ * big-integer coefficients i and i + nh centred at Q/2 (half_words = Q >> 1),
+ * converted to double (round to nearest even), times sf_pre, truncated:
+ * out (slots) complex doubles.  *overflow (device int) is set when a value
+ * does not fit a double (CPython raises OverflowError). */
+int cross_ckks_decode_scale(const uint32_t* x, int words, const uint32_t* q_words, const uint32_t* half_words,
+                            double sf_pre, int slots, int nh, double* out, int* overflow, void* stream);
+
+/* The approximation-error estimate of ckks_decode (ckks_ctx.py:458-481), one
+ * sequential pass: *out (device) = the standard deviation. */
+int cross_ckks_decode_stddev(const double* cur, int slots, double* out, void* stream);
+
+/* ckks_ctx.py:496-505: out[i] = in[i] scale + conj(in)[i] scale (component-wise). */
+int cross_ckks_decode_combine(const double* in, double* out, int slots, double scale, void* stream);
+
+/* ------------------------------------------------------------------ */
 /* Rescale by the last prime (ciphertext.py:223-303)                   */
 /* ------------------------------------------------------------------ */
 

@@ -236,3 +236,69 @@ def test_reduction_contexts_known_answers():
     qi = pow(q, -1, 1 << 32)
     want = [((int(v) >> 32) + q - (((int(v) & 0xFFFFFFFF) * qi & 0xFFFFFFFF) * q >> 32)) & 0xFFFFFFFF for v in z]
     np.testing.assert_array_equal(mo.reduce(z), np.array(want, np.uint64))
+
+
+# ---------------------------------------------------------------------------
+# CKKS client side (oracle/ckks.py)
+# ---------------------------------------------------------------------------
+
+CKKS_TEST = dict(degree=16, slots=8, q_towers=[1073742881, 1073742721, 1073741441, 1073741857, 524353],
+                 p_towers=[1073740609, 1073739937, 1073739649], scale=563019763943521, p=30)
+CKKS_IN1 = [complex(v, 0) for v in (0.25, 0.5, 0.75, 1, 2, 3, 4, 5)]
+
+
+def _ckks_keys(rng):
+    from oracle import ckks as K
+    c = CKKS_TEST
+    deg, mods = c["degree"], c["q_towers"] + c["p_towers"]
+    s = [int(v) for v in rng.integers(0, 2, deg)]
+    e = [int(v) for v in np.rint(rng.normal(0, 3.19, deg))]
+    a = [[int(v) for v in rng.integers(0, q, deg)] for q in mods]
+    return K.gen_pke_pair(c["q_towers"], c["p_towers"], deg, s, a, e)
+
+
+def test_ckks_encode_decode_round_trip():
+    """ckks_ctx_test.py:75-83 (decimal=3) on the oracle."""
+    from oracle import ckks as K
+    c = CKKS_TEST
+    enc = K.ckks_encode(CKKS_IN1, 2 * c["degree"], c["q_towers"], c["scale"])
+    dec = K.decode_rns(enc, c["q_towers"], c["scale"], c["slots"], c["p"], is_ntt=True)
+    np.testing.assert_array_almost_equal([d.real for d in dec], [v.real for v in CKKS_IN1], decimal=3)
+
+
+def test_ckks_encrypt_decrypt_round_trip():
+    """ckks_ctx_test.py:85-97 (decimal=3) on the oracle, with seeded keys and noise."""
+    from oracle import ckks as K
+    c = CKKS_TEST
+    deg, qt = c["degree"], c["q_towers"]
+    rng = np.random.default_rng(3)
+    kp = _ckks_keys(rng)
+    ev = lambda co, q: O.bit_reverse_array(K.ntt_negacyclic([x % q for x in co], q, O.root_of_unity(2 * deg, q)))  # noqa: E731
+    vco = [int(v) for v in rng.integers(0, 2, deg)]
+    e0 = [int(v) for v in np.rint(rng.normal(0, 3.19, deg))]
+    e1 = [int(v) for v in np.rint(rng.normal(0, 3.19, deg))]
+    enc = K.ckks_encode(CKKS_IN1, 2 * deg, qt, c["scale"])
+    ctx = K.ckks_encrypt(enc, kp["public_key"], qt, [ev(vco, q) for q in qt],
+                         ([ev(e0, q) for q in qt], [ev(e1, q) for q in qt]))
+    dec = K.decode_rns(O.ckks_decrypt(ctx, kp["secret_key"], qt), qt, c["scale"], c["slots"], c["p"])
+    np.testing.assert_array_almost_equal([d.real for d in dec], [v.real for v in CKKS_IN1], decimal=3)
+
+
+def test_ckks_decode_of_the_hemul_golden():
+    """hemul_test.py:100-140: the decrypted HE-Mult result decodes (CRT +
+    special FFT of oracle/ckks.py) to the reference's slot values."""
+    from oracle import ckks as K
+    g = load_golden("hemul")
+    qt = g["q_towers"][:4]
+    vals = K.decode_rns(g["decrypted_result_ref"], qt, (g["scalingFactor"] / g["q_towers"][-1]) ** 2,
+                        g["num_slots"], g["p"])
+    np.testing.assert_array_almost_equal([v.real for v in vals], g["real_values_multiply_result"], decimal=3)
+
+
+def test_negacyclic_transform_round_trip():
+    """util.py:763-827: intt_negacyclic inverts ntt_negacyclic."""
+    from oracle import ckks as K
+    q = O.find_moduli_ntt(1, 28, 64)[0]
+    psi = O.root_of_unity(64, q)
+    a = [int(v) for v in np.random.default_rng(0).integers(0, q, 32)]
+    assert O.intt_negacyclic(K.ntt_negacyclic(a, q, psi), q, psi) == a
