@@ -259,6 +259,8 @@ def ckks_encrypt(plaintext, public_key, q_towers, noise_scale_degree: int = 1, s
     pk0 = _rows(public_key[0])[:nt].contiguous()
     pk1 = _rows(public_key[1])[:nt].contiguous()
     v, e0, e1 = (_rows(a)[:nt].contiguous() for a in (v, e0, e1))
+    if pt.shape != (degree, nt) or any(tuple(a.shape) != (nt, degree) for a in (pk0, pk1, v, e0, e1)):
+        raise ValueError(f"ckks_encrypt: plaintext must be (degree, {nt}) and keys / noise ({nt}, degree)")
     c0, c1 = _tensor.empty_u32((degree, nt)), _tensor.empty_u32((degree, nt))
     _tensor.call("cross_ckks_encrypt", neg.ff.handle(), pt.data_ptr(), v.data_ptr(), e0.data_ptr(), e1.data_ptr(),
                  pk0.data_ptr(), pk1.data_ptr(), int(noise_scale_degree), c0.data_ptr(), c1.data_ptr(), degree,
@@ -278,8 +280,12 @@ def ckks_decrypt(ciphertext, private_key, q_towers):
         c = _tensor.to_u32(ciphertext).contiguous()
     else:
         c = t.stack([_rows(el) for el in ciphertext]).contiguous()
+    if c.dim() != 3:
+        raise ValueError("ckks_decrypt: ciphertext must be (elements, degree, moduli)")
     elements, degree, nt = c.shape
     s = _rows(private_key)[:nt].contiguous()
+    if tuple(s.shape) != (nt, degree) or nt > len(q_towers):
+        raise ValueError(f"ckks_decrypt: the secret key must cover the {nt} towers of degree {degree}")
     neg = _negacyclic(list(q_towers)[:nt], degree)
     acc = _tensor.empty_u32((nt, degree))
     _tensor.call("cross_ckks_decrypt_sum", neg.ff.handle(), c.data_ptr(), elements, s.data_ptr(), acc.data_ptr(),
@@ -312,6 +318,8 @@ def _crt_tables(moduli):
 def _crt_words(rns, moduli):
     """(degree, words) CUDA tensor of the CRT values of rns (degree, moduli)."""
     x = _rows(rns)
+    if x.dim() != 2 or x.shape[1] != len(moduli):
+        raise ValueError(f"CRT: residues must be (degree, {len(moduli)})")
     M, W, inv, mi, qw = _crt_tables(list(moduli))
     out = _tensor.empty_u32((x.shape[0], W))
     _tensor.call("cross_crt_combine", _negacyclic_ff(moduli).handle(), x.data_ptr(), x.shape[0], inv.data_ptr(),
@@ -367,6 +375,8 @@ def ckks_decode(plaintext, scalingFactor: float, slots: int, q: int, p: int, CKK
     """ckks_ctx.py:407-514: plaintext = the CRT-combined coefficients (Python
     integers); returns the slots' complex values (real parts)."""
     degree = len(plaintext)
+    if not 0 < slots <= degree // 2:
+        raise ValueError(f"ckks_decode: slots={slots} must be in (0, degree/2]")
     W = _int_words(q)
     t = _tensor.torch()
     x = t.from_numpy(_to_words(plaintext, W).copy()).to(_tensor.device())

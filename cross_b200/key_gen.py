@@ -52,6 +52,8 @@ def gen_pke_pair(q_towers, p_towers, degree: int, noise_std: float = sigma, nois
     a = _rows(a_ref) if a_ref is not None else a
     e = neg.forward(gen_gaussian_polynomial(degree, moduli, noise_std).coeffs)
     e = _rows(e_ref) if e_ref is not None else e
+    if any(tuple(x.shape) != (len(moduli), degree) for x in (s, a, e)):
+        raise ValueError(f"gen_pke_pair: s, a, e must be ({len(moduli)}, {degree})")
     b = _tensor.empty_u32((len(moduli), degree))
     _tensor.call("cross_pke_b", neg.ff.handle(), e.data_ptr(), a.data_ptr(), s.data_ptr(), int(noise_scale),
                  b.data_ptr(), degree, _lib.cuda_stream())
