@@ -319,6 +319,94 @@ def run_component(args, torch, dist, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_ckks(args, torch, dist, world, rank, local):
+    """--workload ckks: one CKKS round trip per step at N = 2^16 with 24 towers
+    (ckks_ctx.py: encode -> encrypt with fresh noise -> decrypt -> decode of
+    N/2 real slots), through the operator API (host slot values in, host
+    complex values out)."""
+    import math
+    import numpy as np
+    from cross_b200 import _lib, ckks_ctx, key_gen, util
+    dev = torch.device("cuda", local)
+    timer = _Timer(torch, dist, dev)
+    lib = _lib.lib()
+    deg, towers = N_DEG, 24
+    mods = util.find_moduli_ntt(32, 28, 2 * deg)
+    qt, pt = mods[:towers], mods[towers:]
+    kp = key_gen.gen_pke_pair(qt, pt, deg)
+    ctx = ckks_ctx.CKKSContext({"degree": deg, "num_slots": deg // 2, "scalingFactor": 2.0 ** 40,
+                                "output_scale": 2.0 ** 40, "q_towers": qt, "p_towers": pt, "p": 40,
+                                "public_key": kp["public_key"], "secret_key": kp["secret_key"]})
+    rng = np.random.default_rng(300 + rank)
+    x = [complex(v, 0.0) for v in rng.uniform(-1.0, 1.0, deg // 2)]
+    xd = torch.from_numpy(np.array(x, np.complex128)).to(dev)
+    res = {}
+
+    def step_dev():
+        res["out"] = ctx.decode(ctx.decrypt(ctx.encrypt(ctx.encode(xd))))
+
+    def step_host():
+        res["out"] = ctx.decode(ctx.decrypt(ctx.encrypt(ctx.encode(x))))
+    for _ in range(args.warmup):
+        step_dev()
+    err = float(np.max(np.abs(res["out"].real - np.array([v.real for v in x]))))
+    if err > 1e-3:
+        raise RuntimeError(f"CKKS round trip error {err}")
+    ms = timer(step_dev, args.steps)
+    l0 = lib.cross_launch_count()
+    step_dev()
+    torch.cuda.synchronize()
+    launches = (lib.cross_launch_count() - l0) * args.steps
+    step_host()
+    ems = timer(step_host, args.steps)
+    value = world * args.steps / (ms / 1000.0)
+    e2e = world * args.steps / (ems / 1000.0)
+    # forward / inverse negacyclic transforms per step: encode 1, encrypt 3 (v, e0, e1), decrypt 1
+    transforms = 5 * towers
+    ops = transforms * 32.0 * deg * (R + C)
+    pk, src = peaks()
+    achieved = ops / (ms / args.steps / 1000.0) / 1e12
+    line = {"metric": "CKKS encode+encrypt+decrypt+decode round trips/s (N=2^16, 24 towers)", "value": value,
+            "unit": "round-trip/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u32 residues, f64 slot values", "data": "synthetic seeded uniform slot values",
+            "config": {"workload": "CKKSContext encode -> encrypt (sampled noise) -> decrypt -> decode, N=2^16, "
+                                   "24 x 28-bit towers, scale 2^40, N/2 real slots", "round_trip_max_error": err},
+            "e2e": {"value": e2e, "unit": "round-trip/s", "h2d_bytes_per_step": int(deg // 2 * 16),
+                    "d2h_bytes_per_step": int(deg // 2 * 16)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "latency (launch- and host-bound chain of small kernels)",
+                         "kernel": "the 5 x 24 negacyclic transforms of a step on the tensor cores",
+                         "achieved": achieved, "peak": 2.0 * pk["bf16_tflops"], "unit": "TOPS (int8)",
+                         "frac": achieved / (2.0 * pk["bf16_tflops"]), "traffic": None,
+                         "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src})"}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import ckks as K
+        from oracle import cross_oracle as O
+        d2 = 8192
+        m2 = O.find_moduli_ntt(32, 28, 2 * d2)
+        q2, p2 = m2[:towers], m2[towers:]
+        r2 = np.random.default_rng(1)
+        xs = [complex(v, 0.0) for v in r2.uniform(-1.0, 1.0, d2 // 2)]
+        s2 = [int(v) for v in r2.integers(0, 2, d2)]
+        e2 = [int(v) for v in np.rint(r2.normal(0, 3.19, d2))]
+        a2 = [[int(v) for v in r2.integers(0, q, d2)] for q in m2]
+        kp2 = K.gen_pke_pair(q2, p2, d2, s2, a2, e2)
+        ev = lambda co, q: O.bit_reverse_array(K.ntt_negacyclic([c % q for c in co], q, O.root_of_unity(2 * d2, q)))  # noqa: E731
+        t0 = time.perf_counter()
+        enc = K.ckks_encode(xs, 2 * d2, q2, 2.0 ** 40)
+        v2 = [ev(s2, q) for q in q2]
+        ct2 = K.ckks_encrypt(enc, kp2["public_key"], q2, v2, (v2, v2))
+        K.decode_rns(O.ckks_decrypt(ct2, kp2["secret_key"], q2), q2, 2.0 ** 40, d2 // 2, 40)
+        dt = time.perf_counter() - t0
+        scale_n = (deg * math.log2(deg)) / (d2 * math.log2(d2))
+        line["cpu_baseline"] = {"value": 1.0 / (dt * scale_n), "unit": "round-trip/s", "cores": 1, "kind": "port",
+                                "sample": f"one round trip at N=2^13 with 24 towers on the oracle (pure Python, "
+                                          f"{dt:.1f} s), scaled to N=2^16 by N log N (x{scale_n:.2f})"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -327,7 +415,7 @@ def main():
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling runs use a small case)")
-    ap.add_argument("--workload", choices=["hemul", "ntt", "bconv"], default="hemul")
+    ap.add_argument("--workload", choices=["hemul", "ntt", "bconv", "ckks"], default="hemul")
     ap.add_argument("--reduction", choices=["barrett", "montgomery", "shoup", "bat_lazy"], default="barrett")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -344,7 +432,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     if args.workload != "hemul":
-        run_component(args, torch, dist, world, rank, local)
+        (run_ckks if args.workload == "ckks" else run_component)(args, torch, dist, world, rank, local)
         if dist:
             dist.barrier()
             dist.destroy_process_group()
