@@ -96,21 +96,36 @@ class Ciphertext:
         self.bit_reverse_indices = util.bit_reverse_indices(self.degree)
         self.shape_in_ntt_all_limbs = (-1, self.r, self.c, self.num_moduli)
         if parameters is not None and parameters.get("BAT_lazy", False):
-            self.ntt_ctx = ntt.NTTCiphertextBATLazyContext(self.moduli, ntt_params)
+            self._ntt_cls = ntt.NTTCiphertextBATLazyContext
         elif isinstance(ffc, ff_context.BarrettContext):
-            self.ntt_ctx = ntt.NTTCiphertextBarrettContext(self.moduli, ntt_params)
+            self._ntt_cls = ntt.NTTCiphertextBarrettContext
         elif isinstance(ffc, ff_context.MontgomeryContext):
-            self.ntt_ctx = ntt.NTTCiphertextMontgomeryContext(self.moduli, ntt_params)
+            self._ntt_cls = ntt.NTTCiphertextMontgomeryContext
         elif isinstance(ffc, ff_context.ShoupContext):
-            self.ntt_ctx = ntt.NTTCiphertextShoupContext(self.moduli, ntt_params)
+            self._ntt_cls = ntt.NTTCiphertextShoupContext
         else:
             raise ValueError(f"Unsupported finite field context type: {type(ffc)}")
+        # the NTT context (ciphertext.py:98-107) is built at its first use:
+        # objects that only carry data (the CKKS context's results) skip the
+        # table precompute
+        self._ntt_args = (list(self.moduli), ntt_params)
+        self._ntt_ctx = None
         self.moduli_array = np.array(self.moduli, dtype=self.modulus_dtype)
         self.ciphertext = _tensor.torch().zeros((self.batch, self.num_elements, self.degree, self.num_moduli),
                                                 dtype=_tensor.torch().uint32 if self.precision <= 32 else _tensor.torch().uint64,
                                                 device=_tensor.device())
         self.bconv = None
         self.bconv_indices_list = []
+
+    @property
+    def ntt_ctx(self):
+        if self._ntt_ctx is None:
+            self._ntt_ctx = self._ntt_cls(*self._ntt_args)
+        return self._ntt_ctx
+
+    @ntt_ctx.setter
+    def ntt_ctx(self, value):
+        self._ntt_ctx = value
 
     def _create_bconv(self, moduli):
         if self.bconv is None:

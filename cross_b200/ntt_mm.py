@@ -61,6 +61,19 @@ def _limb_tables(q: int, r: int, c: int):
     return out
 
 
+@functools.lru_cache(maxsize=512)
+def _limb_bat(q: int, r: int, c: int):
+    """basis_aligned_transformation of the four contraction tables of one
+    modulus in the Barrett (identity) computation format (ntt_mm.py:172-181),
+    shared like _limb_tables.  Read-only arrays."""
+    t1, _, t3, it1, _, it3 = _limb_tables(q, r, c)
+    out = tuple(np.ascontiguousarray(basis_aligned_transformation(t[..., None], [q])[..., 0])
+                for t in (t1, t3, it1, it3))
+    for t in out:
+        t.flags.writeable = False
+    return out
+
+
 class NTTCiphertextContextBase:
     """ntt_mm.py:125-419."""
 
@@ -95,6 +108,15 @@ class NTTCiphertextContextBase:
 
     def _format_tables(self):
         """ntt_mm.py:172-181: BAT of the tables in the computation format."""
+        if type(self.ff_ctx) is ff_context.BarrettContext:
+            # identity format: the per-modulus BAT tables are shared
+            per = [_limb_bat(int(q), self.r, self.c) for q in self.moduli]
+            st = lambda k: np.stack([p[k] for p in per], -1)  # noqa: E731
+            self.ntt_bat_tf_step1, self.ntt_bat_tf_step3 = st(0), st(1)
+            self.intt_bat_tf_step1, self.intt_bat_tf_step3 = st(2), st(3)
+            self.ntt_tf_step2 = self.ntt_tf_step2.astype(U64)
+            self.intt_tf_step2 = self.intt_tf_step2.astype(U64)
+            return
         fmt = self.to_computation_format
         self.ntt_bat_tf_step1 = basis_aligned_transformation(fmt(self.ntt_tf_step1), self.moduli)
         self.ntt_tf_step2 = fmt(self.ntt_tf_step2).astype(U64)
