@@ -168,7 +168,20 @@ __global__ void __launch_bounds__(256) k_transpose_ref(const uint32_t* __restric
         }
       }
     } else {
-      for (int l = threadIdx.x / TT; l < L; l += blockDim.x / TT) sm[(threadIdx.x % TT) * ld + l] = lm_in[(int64_t)l * n + threadIdx.x % TT];
+      // the limb rows of this tile (coalesced 512-byte runs), all loads issued
+      // before the shared-memory stores
+      constexpr int LG = 8;   // loads in flight per thread
+      const int t = threadIdx.x % TT;
+      for (int lb = threadIdx.x / TT; lb < L; lb += 2 * LG) {
+        uint32_t wb[LG];
+        const uint32_t* src = lm_in + (int64_t)lb * n + t;
+#pragma unroll
+        for (int k = 0; k < LG; ++k)
+          if (lb + 2 * k < L) wb[k] = src[(int64_t)(2 * k) * n];
+#pragma unroll
+        for (int k = 0; k < LG; ++k)
+          if (lb + 2 * k < L) sm[t * ld + lb + 2 * k] = wb[k];
+      }
     }
     __syncthreads();
     if (TO_LM) {

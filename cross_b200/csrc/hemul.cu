@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "internal.hpp"
+#include "tc_ptx.cuh"
 
 namespace cross {
 
@@ -43,7 +44,11 @@ unsigned gy_for(int64_t rows) { return (unsigned)(rows < 65535 ? rows : 65535); 
 // times gamma_i psi_i^t, Barrett.  LL: [polys][N]; out: [polys][L1][N].  A
 // thread reads its four last-limb words once and writes them lifted into all
 // L1 limbs (two limbs per step, table loads ahead of the arithmetic).
-template <bool W32>
+// FAST (every modulus passes reduce_fast_ok): the lifted word is below
+// q_i + 2 q_last < 2^31 (LL is a Barrett output, below 2 q_last) and the table
+// entry below q_i, so the product is below 2^31 q_i, where the 32-bit
+// remainder form equals Barrett exactly.
+template <bool W32, bool FAST>
 __global__ void k_rescale_lift(const uint32_t* __restrict__ LL, uint32_t* __restrict__ out, int64_t polys,
                                int L1, int64_t n, uint32_t thr, uint32_t q_last,
                                const uint32_t* __restrict__ gpsi, const ModC* __restrict__ mods) {
@@ -59,10 +64,22 @@ __global__ void k_rescale_lift(const uint32_t* __restrict__ LL, uint32_t* __rest
         return a < thr ? (uint64_t)a : (mc.q - (uint64_t)q_last + (uint64_t)a);
       };
       uint4 o;
-      o.x = red<W32>(lift(x.x) * t.x, mc);
-      o.y = red<W32>(lift(x.y) * t.y, mc);
-      o.z = red<W32>(lift(x.z) * t.z, mc);
-      o.w = red<W32>(lift(x.w) * t.w, mc);
+      if (FAST) {
+        const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
+        auto f = [&](uint32_t a, uint32_t tv) {
+          const uint32_t l = (uint32_t)lift(a);
+          return tc::reduce_fast2(l * tv, __umulhi(l, tv), q32, m32, sw);
+        };
+        o.x = f(x.x, t.x);
+        o.y = f(x.y, t.y);
+        o.z = f(x.z, t.z);
+        o.w = f(x.w, t.w);
+      } else {
+        o.x = red<W32>(lift(x.x) * t.x, mc);
+        o.y = red<W32>(lift(x.y) * t.y, mc);
+        o.z = red<W32>(lift(x.z) * t.z, mc);
+        o.w = red<W32>(lift(x.w) * t.w, mc);
+      }
       dst[(int64_t)i * (n >> 2)] = o;
     };
     int i = 0;
@@ -287,10 +304,12 @@ int rescale_run(const RescaleArgs& a, const uint32_t* X, int64_t xps, uint32_t* 
   {
     int64_t gb = (polys * nv + T - 1) / T;
     const unsigned g = (unsigned)(gb < 148 * 16 ? gb : 148 * 16);
-    if (plan_w32(a.ntt))
-      k_rescale_lift<true><<<g, T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last, a.gamma_psi_t, a.mods_q1);
+    if (a.ntt->tc_fast)
+      k_rescale_lift<true, true><<<g, T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last, a.gamma_psi_t, a.mods_q1);
+    else if (plan_w32(a.ntt))
+      k_rescale_lift<true, false><<<g, T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last, a.gamma_psi_t, a.mods_q1);
     else
-      k_rescale_lift<false><<<g, T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last, a.gamma_psi_t, a.mods_q1);
+      k_rescale_lift<false, false><<<g, T, 0, st>>>(LL, R, polys, L1, N, a.thr, a.q_last, a.gamma_psi_t, a.mods_q1);
   }
   count_launch();
   Epi comb;
