@@ -83,6 +83,7 @@ _SIGS = {
     "cross_ckks_max_abs_scaled": (i32, [vp, i64, C.c_double, vp, vp]),
     "cross_ckks_quantize": (i32, [vp, vp, i32, C.c_double, i32, vp, vp, vp]),
     "cross_mul_reduce_lm": (i32, [vp, vp, vp, vp, i64, vp]),
+    "cross_rns_from_signed": (i32, [vp, vp, i64, vp, vp]),
     "cross_ckks_decrypt_sum": (i32, [vp, vp, i32, vp, vp, i64, vp]),
     "cross_ckks_encrypt": (i32, [vp, vp, vp, vp, vp, vp, vp, C.c_uint64, vp, vp, i64, vp]),
     "cross_pke_b": (i32, [vp, vp, vp, vp, C.c_uint64, vp, i64, vp]),

@@ -227,9 +227,14 @@ def _sample_coeffs(degree: int, kind: str, sigma_: float = sigma):
 
 
 def _rns_of(coeffs, moduli):
-    """gen_rns_polynomial: integer coefficients reduced into every modulus (M, N)."""
-    c = np.asarray(coeffs, np.int64)
-    return np.stack([np.mod(c, np.int64(q)) for q in moduli]).astype(U32)
+    """gen_rns_polynomial: integer coefficients reduced into every modulus,
+    (M, N) on the device."""
+    t = _tensor.torch()
+    c = t.from_numpy(np.ascontiguousarray(np.asarray(coeffs, np.int64))).to(_tensor.device())
+    out = _tensor.empty_u32((len(moduli), c.numel()))
+    _tensor.call("cross_rns_from_signed", _negacyclic_ff(moduli).handle(), c.data_ptr(), c.numel(), out.data_ptr(),
+                 _lib.cuda_stream())
+    return out
 
 
 def ckks_encrypt(plaintext, public_key, q_towers, noise_scale_degree: int = 1, sigma=sigma, v=None, e=None,
@@ -335,7 +340,7 @@ def _crt_combine_rns_plaintext(rns_plaintext, moduli) -> List[int]:
 
 
 def _decode_words(x, W: int, q: int, scalingFactor: float, slots: int, p: int, degree: int,
-                  CKKS_M_FACTOR: int = 1, ADD_NOISE: bool = False):
+                  CKKS_M_FACTOR: int = 1, ADD_NOISE: bool = False, as_array: bool = False):
     t = _tensor.torch()
     dev = _tensor.device()
     nh = degree // 2
@@ -351,7 +356,7 @@ def _decode_words(x, W: int, q: int, scalingFactor: float, slots: int, p: int, d
     _tensor.call("cross_ckks_decode_stddev", cur.data_ptr(), slots, sd_t.data_ptr(), _lib.cuda_stream())
     if int(flag.item()):
         raise OverflowError("int too large to convert to float")
-    sd = float(sd_t.item())
+    sd = float(sd_t.cpu()[0])
     logstd = math.log2(sd) if sd > 0 else float("-inf")
     if sd < 0.125 * math.sqrt(degree):
         sd = 0.125 * math.sqrt(degree)
@@ -367,6 +372,8 @@ def _decode_words(x, W: int, q: int, scalingFactor: float, slots: int, p: int, d
         out += t.from_numpy(pow_p * rng.normal(0.0, std, size=(slots, 2))).to(dev)
     y = t.view_as_complex(out).reshape(1, slots)
     _fft_dev(y, degree * 2, False)
+    if as_array:
+        return y[0].real.cpu().numpy().astype(np.complex128)
     return [complex(float(v), 0.0) for v in y[0].real.cpu().numpy()]
 
 
@@ -440,9 +447,9 @@ class CKKSContext:
         if is_ntt:
             rns = _negacyclic(towers, self.degree).inverse(rns.t().contiguous()).t().contiguous()
         words, big_q, W = _crt_words(rns, towers)
-        res = _decode_words(words, W, big_q, self.output_scale, self.num_slots, self.p, self.degree,
-                            self.CKKS_M_FACTOR)
-        return np.array(res)
+        # the reference returns jnp.array of the complex list: the same values as an array
+        return _decode_words(words, W, big_q, self.output_scale, self.num_slots, self.p, self.degree,
+                             self.CKKS_M_FACTOR, as_array=True)
 
     def multiply(self, ciphertext1, ciphertext2):
         raise NotImplementedError("Mul function not implemented")

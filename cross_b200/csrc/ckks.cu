@@ -116,6 +116,18 @@ __global__ void k_ckks_quantize(const double* __restrict__ yv, int nh, double sc
   }
 }
 
+// gen_rns_polynomial: signed integer coefficients reduced into every tower
+// (Python's %: non-negative results).  out: (M, n).
+__global__ void k_rns_from_signed(const long long* __restrict__ x, int64_t n, int M, const ModC* __restrict__ mods,
+                                  uint32_t* __restrict__ out) {
+  const int64_t total = (int64_t)M * n;
+  for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
+    const long long q = (long long)mods[k / n].q;
+    const long long r = x[k % n] % q;
+    out[k] = (uint32_t)(r < 0 ? r + q : r);
+  }
+}
+
 // x[t][i] = (x[t][i] * tab[t][i]) mod q_t, fully reduced (tab == nullptr: x mod q_t).
 __global__ void k_mul_reduce_lm(const uint32_t* __restrict__ x, const uint32_t* __restrict__ tab,
                                 uint32_t* __restrict__ out, int64_t n, int M, const ModC* __restrict__ mods) {
@@ -422,6 +434,16 @@ int cross_mul_reduce_lm(cross_moduli moduli, const uint32_t* x, const uint32_t* 
   if (n == 0) return CROSS_OK;
   k_mul_reduce_lm<<<ck_blocks(n * moduli->n), CK_THREADS, 0, (cudaStream_t)stream>>>(x, tab, out, n, moduli->n,
                                                                                      moduli->dev);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_rns_from_signed(cross_moduli moduli, const int64_t* x, int64_t n, uint32_t* out, void* stream) {
+  CROSS_REQUIRE(moduli && n >= 0 && (n == 0 || (x && out)), "cross_rns_from_signed: bad argument");
+  if (n == 0) return CROSS_OK;
+  k_rns_from_signed<<<ck_blocks(n * moduli->n), CK_THREADS, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const long long*>(x), n, moduli->n, moduli->dev, out);
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;

@@ -301,6 +301,10 @@ int cross_ckks_max_abs_scaled(const double* v, int64_t n, double scale, double* 
 int cross_ckks_quantize(cross_moduli moduli, const double* y, int nh, double scale, int log_approx,
                         const uint32_t* factor, uint32_t* out, void* stream);
 
+/* gen_rns_polynomial (rns.py): signed coefficients x (n) reduced into every
+ * tower, non-negative: out (M, n). */
+int cross_rns_from_signed(cross_moduli moduli, const int64_t* x, int64_t n, uint32_t* out, void* stream);
+
 /* out[t][i] = x[t][i] * tab[t][i] mod q_t, fully reduced (tab NULL: x mod q_t);
  * x, tab, out (M, n) limb-major. */
 int cross_mul_reduce_lm(cross_moduli moduli, const uint32_t* x, const uint32_t* tab, uint32_t* out, int64_t n,
