@@ -87,6 +87,8 @@ _SIGS = {
     "cross_ckks_decrypt_sum": (i32, [vp, vp, i32, vp, vp, i64, vp]),
     "cross_ckks_encrypt": (i32, [vp, vp, vp, vp, vp, vp, vp, C.c_uint64, vp, vp, i64, vp]),
     "cross_pke_b": (i32, [vp, vp, vp, vp, C.c_uint64, vp, i64, vp]),
+    "cross_mod_switch_lift": (i32, [vp, i64, C.c_uint32, vp, vp, vp]),
+    "cross_ks_key_b": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, C.c_uint64, vp, i64, vp]),
     "cross_crt_combine": (i32, [vp, vp, i64, vp, vp, vp, i32, vp, vp]),
     "cross_ckks_decode_scale": (i32, [vp, i32, vp, vp, C.c_double, i32, i32, vp, vp, vp]),
     "cross_ckks_decode_stddev": (i32, [vp, i32, vp, vp]),

@@ -190,6 +190,41 @@ __global__ void k_pke_b(const uint32_t* __restrict__ e, const uint32_t* __restri
   }
 }
 
+// modulus_switch (key_gen.py:77-105) of one tower's coefficients v (residues
+// mod q_from) into every target modulus p_t: v below (q_from + 1) / 2 stays,
+// larger v becomes v - q_from; out (M, n) holds that signed value mod p_t,
+// the residue the following negacyclic transform reduces it to.
+__global__ void k_mod_switch_lift(const uint32_t* __restrict__ v, int64_t n, uint32_t q_from, int M,
+                                  const ModC* __restrict__ mods, uint32_t* __restrict__ out) {
+  const int64_t total = (int64_t)M * n;
+  const uint32_t thr = (uint32_t)(((uint64_t)q_from + 1) / 2);
+  for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
+    const long long p = (long long)mods[k / n].q;
+    const uint32_t x = v[k % n];
+    long long c = x < thr ? (long long)x : (long long)x - (long long)q_from;
+    c %= p;
+    out[k] = (uint32_t)(c < 0 ? c + p : c);
+  }
+}
+
+// key_switch_gen's b (key_gen.py:228-246) for one part: rows i of Q + P,
+// b = (-a s mod q + [P s_old mod q for start <= i < end] + ns e mod q) mod q.
+// a, e, s, b: (Q + P, n); s_old: (Q, n); p_mod_q: (Q).
+__global__ void k_ks_key_b(const uint32_t* __restrict__ a, const uint32_t* __restrict__ e,
+                           const uint32_t* __restrict__ s, const uint32_t* __restrict__ s_old,
+                           const uint32_t* __restrict__ p_mod_q, int start, int end, uint64_t ns,
+                           uint32_t* __restrict__ b, int64_t n, int M, const ModC* __restrict__ mods) {
+  const int64_t total = (int64_t)M * n;
+  for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
+    const int i = (int)(k / n);
+    const uint64_t q = mods[i].q;
+    const uint64_t as = (uint64_t)a[k] * s[k] % q;
+    uint64_t r = (as ? q - as : 0) + (uint64_t)e[k] * (ns % q) % q;
+    if (i >= start && i < end) r += (uint64_t)p_mod_q[i] * s_old[k] % q;
+    b[k] = (uint32_t)(r % q);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Big integers: little-endian uint32 words.
 // ---------------------------------------------------------------------------
@@ -444,6 +479,31 @@ int cross_rns_from_signed(cross_moduli moduli, const int64_t* x, int64_t n, uint
   if (n == 0) return CROSS_OK;
   k_rns_from_signed<<<ck_blocks(n * moduli->n), CK_THREADS, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const long long*>(x), n, moduli->n, moduli->dev, out);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_mod_switch_lift(const uint32_t* v, int64_t n, uint32_t q_from, cross_moduli to, uint32_t* out,
+                          void* stream) {
+  CROSS_REQUIRE(to && n >= 0 && q_from > 1 && (n == 0 || (v && out)), "cross_mod_switch_lift: bad argument");
+  if (n == 0) return CROSS_OK;
+  k_mod_switch_lift<<<ck_blocks(n * to->n), CK_THREADS, 0, (cudaStream_t)stream>>>(v, n, q_from, to->n, to->dev, out);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_ks_key_b(cross_moduli moduli, const uint32_t* a, const uint32_t* e, const uint32_t* s, const uint32_t* s_old,
+                   const uint32_t* p_mod_q, int start, int end, uint64_t noise_scale, uint32_t* b, int64_t n,
+                   void* stream) {
+  CROSS_REQUIRE(moduli && n >= 0 && start >= 0 && end >= start && end <= moduli->n &&
+                    (n == 0 || (a && e && s && b && (start == end || (s_old && p_mod_q)))),
+                "cross_ks_key_b: bad argument");
+  if (n == 0) return CROSS_OK;
+  k_ks_key_b<<<ck_blocks(n * moduli->n), CK_THREADS, 0, (cudaStream_t)stream>>>(a, e, s, s_old, p_mod_q, start, end,
+                                                                                noise_scale, b, n, moduli->n,
+                                                                                moduli->dev);
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;

@@ -76,9 +76,18 @@ class HERot:
         rd, cd = util.default_rc(n)
         self.ntt_qp = NTTCiphertextBarrettContext(ov, {"r": rd, "c": cd, "finite_field_context": BarrettContext(ov)})
         self._free_plan()
+        if getattr(self, "_pending_keys", None) is not None:
+            # the reference stores the keys in setup_rotate and uses them at rotate
+            # time, so setup_rotate may come first (ckks_ctx_test.py:104-106)
+            keys, self._pending_keys = self._pending_keys, None
+            self.setup_rotate(*keys)
 
     def setup_rotate(self, evalkey_a_vector, evalkey_b_vector, coefMap):
-        """herot.py:178-181: evk (dnum, N, L + K) (or (dnum, r, c, L + K))."""
+        """herot.py:178-181: evk (dnum, N, L + K) (or (dnum, r, c, L + K)).
+        Before control_gen the keys are kept and installed by control_gen."""
+        if not hasattr(self, "sizeQlP"):
+            self._pending_keys = (evalkey_a_vector, evalkey_b_vector, coefMap)
+            return
         n = self.r * self.c
         ea = np.ascontiguousarray(_tensor.to_numpy(evalkey_a_vector).astype(U32)).reshape(-1, n, self.sizeQlP)
         eb = np.ascontiguousarray(_tensor.to_numpy(evalkey_b_vector).astype(U32)).reshape(-1, n, self.sizeQlP)

@@ -327,6 +327,19 @@ int cross_ckks_encrypt(cross_moduli moduli, const uint32_t* m, const uint32_t* v
 int cross_pke_b(cross_moduli moduli, const uint32_t* e, const uint32_t* a, const uint32_t* s, uint64_t noise_scale,
                 uint32_t* b, int64_t n, void* stream);
 
+/* modulus_switch (key_gen.py:77-105) of one tower's coefficients v (mod
+ * q_from) into every modulus of `to`: the centred value (v, or v - q_from for
+ * v >= (q_from + 1) / 2) reduced mod p_t: out (M_to, n). */
+int cross_mod_switch_lift(const uint32_t* v, int64_t n, uint32_t q_from, cross_moduli to, uint32_t* out,
+                          void* stream);
+
+/* key_switch_gen's b of one part (key_gen.py:228-246): rows i of Q + P,
+ * b = (-a s mod q + [P s_old mod q when start <= i < end] + noise_scale e mod q) mod q;
+ * a, e, s, b (Q + P, n) evaluations; s_old (Q, n); p_mod_q (Q): P mod q_i. */
+int cross_ks_key_b(cross_moduli moduli, const uint32_t* a, const uint32_t* e, const uint32_t* s, const uint32_t* s_old,
+                   const uint32_t* p_mod_q, int start, int end, uint64_t noise_scale, uint32_t* b, int64_t n,
+                   void* stream);
+
 /* _crt_combine_rns_plaintext (ckks_ctx.py:517-545): rns (n, M) -> out (n,
  * words) little-endian uint32 words of X mod Q.  inv (M): (Q/q_i)^-1 mod q_i;
  * mi (M, words): Q/q_i; q_words (words): Q.  words <= 66, M <= 64. */

@@ -14,6 +14,8 @@ operation order, so every integer and every double matches the reference:
   ckks_ctx.py:517-545  _crt_combine_rns_plaintext
   util.py:707-798      ntt_bit_reverse, ntt_negacyclic_bit_reverse
   key_gen.py:299-347   gen_pke_pair (with given s, a, e coefficients)
+  key_gen.py:77-297    modulus_switch, gen_evaluation_key, key_switch_gen,
+                       precompute_rotation_key_map, gen_rotation_key (given a, e)
 The decrypt side (ckks_ctx.py:238-328) is ``cross_oracle.ckks_decrypt``.
 """
 
@@ -313,3 +315,77 @@ def gen_pke_pair(q_towers, p_towers, degree, s_coeffs, a_coeffs, e_coeffs, noise
     b = [[((e[i][j] * noise_scale) % q - (a[i][j] * s[i][j]) % q) % q for j in range(degree)]
          for i, q in enumerate(moduli)]
     return {"public_key": [b, a], "secret_key": s[:len(q_towers)]}
+
+
+# ---------------------------------------------------------------------------
+# key_gen.py:77-297: key-switching keys with given a, e
+# ---------------------------------------------------------------------------
+
+def modulus_switch(values, cur: int, target: int) -> List[int]:
+    """key_gen.py:77-105 (list form): centred lift from Z_cur to Z_target."""
+    thr = (cur + 1) // 2
+    return [v if v < thr else target + v - cur for v in (int(x) for x in values)]
+
+
+def key_switch_gen(s_old, s_new, q_list, p_list, a, e, noise_scale: int = 1, dnum: int = 3):
+    """key_gen.py:147-254 with the a and e samples given (parts x (Q+P) x N,
+    evaluation form).  s_old (Q x N) and s_new (Q x N) in evaluation form."""
+    degree = len(s_new[0])
+    q_list, p_list = list(q_list), list(p_list)
+    s_out = [intt_negacyclic(bit_reverse_array(list(limb)), q, root_of_unity(2 * degree, q))
+             for limb, q in zip(s_new, q_list)]
+    s_qp = [list(r) for r in s_out] + [modulus_switch(s_out[0], q_list[0], p) for p in p_list]
+    s_eva = [bit_reverse_array(ntt_negacyclic(limb, q, root_of_unity(2 * degree, q)))
+             for limb, q in zip(s_qp, q_list + p_list)]
+    P = 1
+    for p in p_list:
+        P *= p
+    pmq = [P % q for q in q_list]
+    size_q, size_qp = len(q_list), len(q_list) + len(p_list)
+    per = (size_q + dnum - 1) // dnum
+    parts = math.ceil(size_q / per)
+    moduli = q_list + p_list
+    b_parts = []
+    for part in range(parts):
+        start, end = per * part, min(size_q, per * part + per)
+        rows = []
+        for i in range(size_qp):
+            q = moduli[i]
+            ar, er, sr = a[part][i], e[part][i], s_eva[i]
+            if start <= i < end:
+                rows.append([((-ar[j] * sr[j]) % q + (pmq[i] * s_old[i][j]) % q + (noise_scale * er[j]) % q) % q
+                             for j in range(degree)])
+            else:
+                rows.append([((-ar[j] * sr[j]) % q + (noise_scale * er[j]) % q) % q for j in range(degree)])
+        b_parts.append(rows)
+    return {"a": a, "b": b_parts, "modulus": {"Q": q_list, "P": p_list}, "P": p_list,
+            "shape": (parts, size_qp, degree)}
+
+
+def gen_evaluation_key(private_key, q_list, p_list, a, e, noise_scale: int = 1, dnum: int = 3):
+    """key_gen.py:108-144: s_old = s^2 (evaluation form)."""
+    s_old = [[(x * x) % q for x in row] for row, q in zip(private_key, q_list)]
+    return key_switch_gen(s_old, private_key, q_list, p_list, a, e, noise_scale, dnum)
+
+
+def precompute_rotation_key_map(n: int, k: int) -> List[int]:
+    """key_gen.py:273-285."""
+    logm = (2 * n).bit_length() - 1
+    logn = n.bit_length() - 1
+    out = [0] * n
+    for j in range(n):
+        mul = ((j << 1) + 1) * k
+        idx = (mul - ((mul >> logm) << logm)) >> 1
+        jrev = int(format(j, f"0{logn}b")[::-1], 2) if logn else 0
+        out[jrev] = int(format(idx, f"0{logn}b")[::-1], 2) if logn else 0
+    return out
+
+
+def gen_rotation_key(sk, q_list, p_list, rot_index: int, a, e, noise_scale: int = 1, dnum: int = 3):
+    """key_gen.py:288-296: key from s to s permuted by the rotation's map."""
+    from .cross_oracle import find_automorphism_index_2n_complex
+    n = len(sk[0])
+    k = find_automorphism_index_2n_complex(rot_index, 2 * n)
+    order = precompute_rotation_key_map(n, pow(k, -1, 2 * n))
+    sk_rot = [[row[order[j]] for j in range(n)] for row in sk]
+    return key_switch_gen(sk, sk_rot, q_list, p_list, a, e, noise_scale, dnum)

@@ -189,3 +189,101 @@ def test_ckks_round_trip_full_size():
     ctx = ckks_ctx.CKKSContext(params)
     dec = ctx.decode(ctx.decrypt(ctx.encrypt(ctx.encode(x))))
     np.testing.assert_array_almost_equal(dec.real, [v.real for v in x], decimal=3)
+
+
+# ---------------------------------------------------------------------------
+# key-switching keys and the reference's end-to-end tests
+# ---------------------------------------------------------------------------
+
+def _seeded_parts(mods, deg, parts, rng):
+    a = [[_ev([int(v) for v in rng.integers(0, 2, deg)], q, deg) for q in mods] for _ in range(parts)]
+    e = [[_ev([int(v) for v in np.rint(rng.normal(0, 3.19, deg))], q, deg) for q in mods] for _ in range(parts)]
+    return a, e
+
+
+def test_evaluation_and_rotation_keys_bit_exact():
+    """key_gen.py:108-297 with a and e given: b equals the oracle's for the
+    relinearisation key and a rotation key."""
+    from cross_b200 import key_gen
+    c = CKKS_TEST
+    deg, qt, pt = c["degree"], c["q_towers"], c["p_towers"]
+    mods = qt + pt
+    rng = np.random.default_rng(21)
+    sk = [_ev([int(v) for v in rng.integers(0, 2, deg)], q, deg) for q in qt]
+    a, e = _seeded_parts(mods, deg, 3, rng)
+    got = key_gen.gen_evaluation_key(sk, qt, pt, a=a, e=e, dnum=3)
+    want = K.gen_evaluation_key(sk, qt, pt, a, e, dnum=3)
+    np.testing.assert_array_equal(_np(got["b"]).astype(np.int64), np.array(want["b"], np.int64))
+    for rot in (1, 3, -1):
+        got = key_gen.gen_rotation_key(sk, qt, pt, rot, dnum=3, a=a, e=e)
+        want = K.gen_rotation_key(sk, qt, pt, rot, a, e, dnum=3)
+        np.testing.assert_array_equal(_np(got["b"]).astype(np.int64), np.array(want["b"], np.int64))
+
+
+def _e2e_params(kp, scale_out=None):
+    c = CKKS_TEST
+    return {"degree": c["degree"], "num_slots": c["slots"], "scalingFactor": c["scale"],
+            "output_scale": c["scale"] if scale_out is None else scale_out, "q_towers": c["q_towers"],
+            "p_towers": c["p_towers"], "p": c["p"], "CKKS_M_FACTOR": 1, "max_bits_in_word": 61,
+            "noise_scale_degree": 1, "public_key": kp["public_key"], "secret_key": kp["secret_key"]}
+
+
+def test_ckks_encrypt_multiply_decrypt():
+    """ckks_ctx_test.py:152-190 on the GPU: device keys (public and
+    relinearisation), encode, encrypt, HE-Mult, decrypt, decode."""
+    from cross_b200 import ckks_ctx, hemul, key_gen
+    c = CKKS_TEST
+    qt, pt = c["q_towers"], c["p_towers"]
+    kp = key_gen.gen_pke_pair(qt, pt, c["degree"])
+    ek = key_gen.gen_evaluation_key(kp["secret_key"], q=qt, P=pt, noise_std=3.19, noise_scale=1, dnum=3)
+    eva, evb = (_np(ek[k]).transpose(0, 2, 1).astype(U32) for k in ("a", "b"))
+    ctx = ckks_ctx.CKKSContext(_e2e_params(kp, (c["scale"] / qt[-1]) ** 2))
+    he = hemul.HEMul(1, 4, 4, 3, 1, qt, pt)
+    he.control_gen(degree_layout=(4, 4))
+    he.setup_relinearization(eva, evb)
+    in2 = [complex(v, 0) for v in (5, 4, 3, 2, 1, 0.75, 0.5, 0.25)]
+    e1, e2 = ctx.encrypt(ctx.encode(CKKS_IN1)), ctx.encrypt(ctx.encode(in2))
+    ins = np.concatenate([_np(e1.ciphertext), _np(e2.ciphertext)], 1).reshape(1, 4, 4, 4, len(qt)).astype(U32)
+    res = _np(he.mul(ins))
+    e1.drop_last_modulus()
+    e1.set_batch_ciphertext(res.reshape(1, 2, c["degree"], len(qt) - 1))
+    dec = ctx.decode(ctx.decrypt(e1))
+    np.testing.assert_array_almost_equal(dec.real, [1.25, 2, 2.25, 2, 2, 2.25, 2, 1.25], decimal=3)
+
+
+def test_ckks_encrypt_rotate_decrypt():
+    """ckks_ctx_test.py:99-121 on the GPU with a device rotation key."""
+    from cross_b200 import ckks_ctx, herot, key_gen, util
+    c = CKKS_TEST
+    qt, pt, deg = c["q_towers"], c["p_towers"], c["degree"]
+    kp = key_gen.gen_pke_pair(qt, pt, deg)
+    coef_map = util.precompute_auto_map(deg, key_gen.find_automorphism_index_2n_complex(1, deg))
+    ek = key_gen.gen_rotation_key(kp["secret_key"], qt, pt, rot_index=1, dnum=3, noise_std=3.19, noise_scale=1)
+    hr = herot.HERot(4, 4, 3, qt, pt)
+    hr.setup_rotate(_np(ek["a"]).astype(np.uint64).transpose(0, 2, 1).reshape(3, 4, 4, -1),
+                    _np(ek["b"]).astype(np.uint64).transpose(0, 2, 1).reshape(3, 4, 4, -1), coef_map)
+    hr.control_gen(batch=1, degree_layout=(4, 4))
+    ctx = ckks_ctx.CKKSContext(_e2e_params(kp))
+    enc = ctx.encrypt(ctx.encode(CKKS_IN1))
+    res = _np(hr.rotate(_np(enc.ciphertext).reshape(1, 2, 4, 4, len(qt))))
+    enc.set_batch_ciphertext(res.reshape(1, 2, deg, len(qt)))
+    dec = ctx.decode(ctx.decrypt(enc))
+    np.testing.assert_array_almost_equal(dec.real, [0.5, 0.75, 1, 2, 3, 4, 5, 0.25], decimal=3)
+
+
+def test_ckks_encrypt_rescale_decrypt():
+    """ckks_ctx_test.py:123-150 on the GPU: Ciphertext.rescale between encrypt and decrypt."""
+    from cross_b200 import ciphertext, ckks_ctx, key_gen
+    c = CKKS_TEST
+    qt, pt, deg = c["q_towers"], c["p_towers"], c["degree"]
+    kp = key_gen.gen_pke_pair(qt, pt, deg)
+    ctx = ckks_ctx.CKKSContext(_e2e_params(kp, c["scale"] / qt[-1]))
+    ct = ciphertext.Ciphertext({"batch": 1, "num_elements": 2, "degree": deg, "num_moduli": 5, "precision": 32,
+                                "degree_layout": (4, 4)}, {"moduli": qt, "r": 4, "c": 4})
+    ct.modulus_switch_control_gen(degree_layout=(4, 4))
+    enc = ctx.encrypt(ctx.encode(CKKS_IN1))
+    ct.set_batch_ciphertext(_np(enc.ciphertext).reshape(1, 2, 4, 4, 5))
+    ct.rescale()
+    ct.ciphertext = ct.ciphertext.reshape(1, 2, deg, 4)
+    dec = ctx.decode(ctx.decrypt(ct))
+    np.testing.assert_array_almost_equal(dec.real, [v.real for v in CKKS_IN1], decimal=3)
