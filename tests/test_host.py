@@ -174,3 +174,33 @@ def test_single_modulus_contexts_expose_reference_tables():
     np.testing.assert_array_equal(sh.to_shoup_computation_format(t), sh.ntt_tf_mat_step1_shoup)
     with pytest.raises(TypeError):
         ntt_sm.NTTContextBase(q, {"r": 16, "c": 16, "finite_field_context": ff.ShoupContext(q)})
+
+
+def test_ckks_host_helpers_match_oracle():
+    """ckks_ctx.py:113-153 and key_gen.py:77-105: the host helpers of the CKKS
+    client equal the oracle's on edge values."""
+    from cross_b200 import ckks_ctx, key_gen
+    from oracle import ckks as K
+    for x in (0.0, 0.5, -0.5, 1.5, -1.5, 2.4999999, -2.5000001, 1e17 + 0.5, -7.0):
+        assert ckks_ctx.nearest_int(x) == K.nearest_int(x)
+    q = 1073741441
+    vals = [0, 1, 5, 2 ** 40, K.MAX_INT_64 - 3, (K.MAX_INT_64 >> 1) + 1, K.MAX_INT_64 >> 1]
+    assert ckks_ctx.fit_to_native_vector(vals, K.MAX_INT_64, q, 14) == K.fit_to_native_vector(vals, K.MAX_INT_64, q, 14)
+    y = [complex(1.5, -2.0), complex(0.0, 3.25)]
+    assert ckks_ctx.slot_to_coeffs(y) == [1.5, 0.0, -2.0, 3.25]
+    coeffs = [0, 1, 524352 // 2, 524353 // 2 + 1, 524352]
+    assert key_gen.modulus_switch(coeffs, 524353, 1073740609) == K.modulus_switch(coeffs, 524353, 1073740609)
+    # threshold (cur + 1) // 2 = 7: 6 stays, 7 and 12 become 101 + v - 13
+    assert [key_gen.modulus_switch(v, 13, 101) for v in (6, 7, 12)] == [6, 95, 100]
+
+
+def test_shoup_precompute_follows_the_reference_dtypes():
+    """finite_field.py:295-297 under JAX: a uint32 operand shifted by 32 is 0
+    (so BConvShoup's companions are 0); wider operands give floor(a 2^32 / q)."""
+    from cross_b200 import finite_field as ff
+    q = [1073741441, 1073740609]
+    sh = ff.ShoupContext(q)
+    a = np.array([5, 1073741440], np.uint32)
+    assert not sh.precompute_constant_operand(a).any()
+    np.testing.assert_array_equal(sh.precompute_constant_operand(a.astype(np.uint64)),
+                                  (a.astype(np.uint64) << np.uint64(32)) // np.array(q, np.uint64))
