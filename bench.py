@@ -7,10 +7,14 @@ rank processes its own batch of 64 (the reference shards the batch axis only).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Prints one JSON line on rank 0.  --workload ntt / bconv measure the transform
-and the basis conversion alone for one reduction (--reduction barrett,
-montgomery, shoup or bat_lazy): N = 2^16 NTT + INTT over 24 limbs x 16
-polynomials, and the 24 -> 25 limb BConv over 32 polynomials of N = 2^16.
+Prints one JSON line on rank 0.  Other workloads of the same line format:
+  --workload herot              HE-Rotate at the same point (B, 2, r, c, L) -> (B, 2, N, L)
+  --limbs L --special K --dnum D  another HE-Mult / HE-Rotate point (35, 7, 5: the 8-GPU box point)
+  --workload ntt / bconv        the transform or the basis conversion alone for one reduction
+                                (--reduction barrett | montgomery | shoup | bat_lazy): NTT + INTT
+                                over --ntt-limbs limbs x --ntt-polys polys of N = --ntt-degree
+                                (default 2^16, 24, 16); BConv 24 -> 25 limbs, 32 polys of N = 2^16
+  --workload ckks               a CKKS encode -> encrypt -> decrypt -> decode round trip
 """
 from __future__ import annotations
 
@@ -32,6 +36,29 @@ N_DEG, R, C, L, K, DNUM, BATCH = 65536, 256, 256, 24, 8, 3, 64
 TRAFFIC_PER_LAUNCH = 3.148e9
 METRIC = "HE-Mult/s (N=2^16, L=24, dnum=3)"
 WORKLOAD = "CKKS HE-Mult + relinearisation, N=2^16 (256x256), L=24 x 28-bit, K=8, dnum=3, batch 64 per GPU"
+
+
+def set_point(workload: str, limbs: int, special: int, dnum: int, batch: int) -> None:
+    """Select the HE operator point (module constants used by the helpers)."""
+    global L, K, DNUM, METRIC, WORKLOAD
+    L, K, DNUM = limbs, special, dnum
+    if workload == "herot":
+        METRIC = f"HE-Rotate/s (N=2^16, L={L}, dnum={DNUM})"
+        WORKLOAD = (f"CKKS HE-Rotate (hybrid key switch), N=2^16 (256x256), L={L} x 28-bit, K={K}, dnum={DNUM}, "
+                    f"batch {batch} per GPU")
+    else:
+        METRIC = f"HE-Mult/s (N=2^16, L={L}, dnum={DNUM})"
+        WORKLOAD = (f"CKKS HE-Mult + relinearisation, N=2^16 (256x256), L={L} x 28-bit, K={K}, dnum={DNUM}, "
+                    f"batch {batch} per GPU")
+
+
+def rotation_map(seed: int = 0):
+    """A seeded rotation index k in [1, N/2) and its coefficient map
+    (util.py:652-693)."""
+    import numpy as np
+    from cross_b200 import util
+    k = int(np.random.default_rng(seed).integers(1, N_DEG // 2))
+    return k, util.precompute_auto_map(N_DEG, util.find_automorphism_index_2n_complex(k, 2 * N_DEG))
 
 
 def moduli():
@@ -117,23 +144,33 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-def cpu_baseline(steps: int = 1):
-    """The oracle (numpy restatement of jaxite_word) on the host cores: one
-    ciphertext per step."""
-    import numpy as np
+def _oracle_op(workload: str):
+    """The oracle's operator for one ciphertext of the workload and its input."""
     from oracle import cross_oracle as O
     Q, P = moduli()
     ct, ea, eb = inputs(0, 1)
+    if workload == "herot":
+        op = O.HERot(R, C, DNUM, Q, P)
+        op.control_gen(1)
+        op.setup_rotate(ea.reshape(DNUM, R, C, -1), eb.reshape(DNUM, R, C, -1), rotation_map()[1])
+        return op.rotate, ct[:, :2], "HE-Rot/s", "HERot.rotate"
     he = O.HEMul(1, R, C, DNUM, 1, Q, P)
     he.setup_relinearization(ea, eb)
+    return he.mul, ct, "HE-Mult/s", "HEMul.mul"
+
+
+def cpu_baseline(steps: int = 1, workload: str = "hemul"):
+    """The oracle (numpy restatement of jaxite_word) on the host cores: one
+    ciphertext per step."""
+    fn, ct, unit, name = _oracle_op(workload)
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
-        he.mul(ct)
+        fn(ct)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    return {"value": 1.0 / t, "unit": "HE-Mult/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{steps} x 1 ciphertext of the workload (oracle/cross_oracle.py HEMul.mul, numpy BLAS threads)",
+    return {"value": 1.0 / t, "unit": unit, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} x 1 ciphertext of the workload (oracle/cross_oracle.py {name}, numpy BLAS threads)",
             "seconds_per_ct": t}
 
 
@@ -143,27 +180,23 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import cross_oracle as O
-    Q, P = moduli()
-    ct, ea, eb = inputs(0, 1)
-    he = O.HEMul(1, R, C, DNUM, 1, Q, P)
-    he.setup_relinearization(ea, eb)
+    fn, ct, unit, name = _oracle_op(args.workload)
     for _ in range(args.warmup):
-        he.mul(ct)
+        fn(ct)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        he.mul(ct)
+        fn(ct)
     dt = (time.perf_counter() - t0) / max(args.steps, 1)
     v = 1.0 / dt
-    sample = "1 ciphertext of the workload per step (oracle/cross_oracle.py HEMul.mul, numpy BLAS threads)"
-    print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "HE-Mult/s", "n_gpus": args.gpus,
+    sample = f"1 ciphertext of the workload per step (oracle/cross_oracle.py {name}, numpy BLAS threads)"
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": unit, "n_gpus": args.gpus,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt,
                       "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                       "dtype": "u32 residues, u64 intermediates, u8 BAT contractions", "data": "synthetic seeded",
                       "config": {"workload": WORKLOAD, "sample": "1 ciphertext per step"},
-                      "cpu_baseline": {"value": v, "unit": "HE-Mult/s", "cores": os.cpu_count(), "kind": "port",
+                      "cpu_baseline": {"value": v, "unit": unit, "cores": os.cpu_count(), "kind": "port",
                                        "sample": sample},
-                      "e2e": {"value": v, "unit": "HE-Mult/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                      "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
           flush=True)
 
 
@@ -415,9 +448,16 @@ def main():
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling runs use a small case)")
-    ap.add_argument("--workload", choices=["hemul", "ntt", "bconv", "ckks"], default="hemul")
+    ap.add_argument("--workload", choices=["hemul", "herot", "ntt", "bconv", "ckks"], default="hemul")
     ap.add_argument("--reduction", choices=["barrett", "montgomery", "shoup", "bat_lazy"], default="barrett")
+    ap.add_argument("--limbs", type=int, default=L, help="L of the HE-Mult / HE-Rotate point")
+    ap.add_argument("--special", type=int, default=K, help="K of the HE-Mult / HE-Rotate point")
+    ap.add_argument("--dnum", type=int, default=DNUM, help="key-switch digits of the HE-Mult / HE-Rotate point")
+    ap.add_argument("--ntt-degree", type=int, default=N_DEG)
+    ap.add_argument("--ntt-limbs", type=int, default=24)
+    ap.add_argument("--ntt-polys", type=int, default=16)
     args = ap.parse_args()
+    set_point(args.workload, args.limbs, args.special, args.dnum, args.batch)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -431,29 +471,37 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
-    if args.workload != "hemul":
+    if args.workload not in ("hemul", "herot"):
         (run_ckks if args.workload == "ckks" else run_component)(args, torch, dist, world, rank, local)
         if dist:
             dist.barrier()
             dist.destroy_process_group()
         return
 
-    from cross_b200 import _lib, hemul, ntt_mm
+    from cross_b200 import _lib, hemul, herot, ntt_mm
     batch = args.batch
     Q, P = moduli()
     ct, ea, eb = inputs(100 + rank, batch)
-    he = hemul.HEMul(batch, R, C, DNUM, 1, Q, P)
-    he.control_gen(degree_layout=(R, C))
-    he.setup_relinearization(ea, eb)
     dev = torch.device("cuda", local)
+    if args.workload == "herot":
+        he = herot.HERot(R, C, DNUM, Q, P)
+        he.control_gen(batch=batch, degree_layout=(R, C))
+        he.setup_rotate(ea, eb, rotation_map()[1])
+        ct = ct[:, :2].copy()
+        op, out_shape, unit, tag = he.rotate, (batch, 2, N_DEG, L), "HE-Rot/s", "herot"
+    else:
+        he = hemul.HEMul(batch, R, C, DNUM, 1, Q, P)
+        he.control_gen(degree_layout=(R, C))
+        he.setup_relinearization(ea, eb)
+        op, out_shape, unit, tag = he.mul, (batch, 2, R, C, L - 1), "HE-Mult/s", "hemul"
     x = torch.from_numpy(ct).to(dev)
-    out = torch.empty((batch, 2, R, C, L - 1), dtype=torch.uint32, device=dev)
+    out = torch.empty(out_shape, dtype=torch.uint32, device=dev)
     ws = torch.empty(he.workspace_size(batch), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
 
     def step():
-        torch.cuda.nvtx.range_push("hemul")
-        he.mul(x, out=out, workspace=ws)
+        torch.cuda.nvtx.range_push(tag)
+        op(x, out=out, workspace=ws)
         torch.cuda.nvtx.range_pop()
 
     for _ in range(args.warmup):
@@ -485,7 +533,7 @@ def main():
 
     def e2e_step():
         torch.cuda.nvtx.range_push("e2e")
-        he.mul(hin, out=hout)
+        op(hin, out=hout)
         torch.cuda.nvtx.range_pop()
 
     e2e_step()
@@ -503,9 +551,10 @@ def main():
     # Dominant kernel: the tensor-core BAT contraction.  One forward NTT in the
     # kernels' native coefficient order is exactly two contraction launches (the
     # column stage with its twiddle epilogue, the row stage); timed alone over
-    # the 4 x 64 x 23 limb-polynomials of the rescale NTT.
+    # the polys x (L - 1) limb-polynomials of the input (for HE-Mult, those of
+    # its rescale NTT).
     ctx = ntt_mm.NTTCiphertextBarrettContext(Q[:L - 1], {"r": R, "c": C})
-    lps = batch * 4
+    lps = x.numel() // (L * N_DEG)
     xin = x.reshape(-1)[: lps * (L - 1) * N_DEG].reshape(lps, L - 1, R, C)   # residues < q
     xo = torch.empty_like(xin)
     nws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), lps, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED),
@@ -543,21 +592,23 @@ def main():
     achieved = ops / (ntt_ms / 1000.0) / 1e12
 
     line = {
-        "metric": METRIC, "value": value, "unit": "HE-Mult/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u32 residues, u64 intermediates, u8 BAT contractions",
         "data": "synthetic seeded uniform residues (no dataset in the reference)",
         "config": {"workload": WORKLOAD, "global_batch": world * batch, "batch_per_gpu": batch, "N": N_DEG, "r": R, "c": C, "L": L, "K": K,
                    "dnum": DNUM, "parallelism": f"batch-sharded x{world}",
-                   "l2": "inputs 1.6 GB per GPU, larger than L2 (no flush needed)"},
-        "e2e": {"value": e2e, "unit": "HE-Mult/s", "h2d_bytes_per_step": int(hin.numel() * 4),
+                   "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB per GPU, larger than L2 (no flush needed)"},
+        "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": int(hin.numel() * 4),
                 "d2h_bytes_per_step": int(hout.numel() * 4)},
         "gpu_launches": int(launches),
         "clocks": clk.summary(h0, h1),
         "roofline": {"kernel": "k_bat_tc2 tensor-core BAT contraction (NTT column + row stage launches), "
-                               "23 limbs x 256 polys, N=2^16",
+                               f"{L - 1} limbs x {lps} polys, N=2^16",
                      "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
-                     "frac": achieved / int8_peak, "traffic": TRAFFIC_PER_LAUNCH,
+                     "frac": achieved / int8_peak,
+                     # the captured launch processed 256 x 23 limb-polynomials; traffic scales with them
+                     "traffic": TRAFFIC_PER_LAUNCH * transforms / (256 * 23),
                      "traffic_unit": "bytes per launch (ncu dram read + write)",
                      "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); no int8 measurement on this pool",
                      "launches": ntt_launches, "ms_per_launch": ntt_ms / max(ntt_launches, 1),
@@ -565,7 +616,7 @@ def main():
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            line["cpu_baseline"] = {k: v for k, v in cpu_baseline(1).items() if k != "seconds_per_ct"}
+            line["cpu_baseline"] = {k: v for k, v in cpu_baseline(1, args.workload).items() if k != "seconds_per_ct"}
         except Exception as exc:  # noqa: BLE001
             line["cpu_baseline"] = {"error": str(exc)}
     if rank == 0:
