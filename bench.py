@@ -227,7 +227,7 @@ def run_component(args, torch, dist, world, rank, local):
     throughput through the operator API with host buffers, the kernel's
     roofline and the oracle on the host cores."""
     import numpy as np
-    from cross_b200 import _lib, bconv, finite_field as ff, ntt_mm
+    from cross_b200 import _lib, bconv, ntt_mm, util
     from oracle import cross_oracle as O
     from oracle import variants as V
     dev = torch.device("cuda", local)
@@ -237,12 +237,13 @@ def run_component(args, torch, dist, world, rank, local):
     pk, src = peaks()
     rng = np.random.default_rng(200 + rank)
     if args.workload == "ntt":
-        Lw, B = 24, 16
-        q = O.find_moduli_ntt(Lw, 28, 2 * N_DEG)
+        Lw, B, nd = args.ntt_limbs, args.ntt_polys, args.ntt_degree
+        rr, cc = util.default_rc(nd)
+        q = O.find_moduli_ntt(Lw, 28, 2 * nd)
         cls = {"barrett": ntt_mm.NTTCiphertextBarrettContext, "montgomery": ntt_mm.NTTCiphertextMontgomeryContext,
                "shoup": ntt_mm.NTTCiphertextShoupContext, "bat_lazy": ntt_mm.NTTCiphertextBATLazyContext}[red]
-        ctx = cls(q, {"r": R, "c": C})
-        xh = (rng.integers(0, 2 ** 62, size=(B, Lw, R, C), dtype=np.uint64) %
+        ctx = cls(q, {"r": rr, "c": cc})
+        xh = (rng.integers(0, 2 ** 62, size=(B, Lw, rr, cc), dtype=np.uint64) %
               np.array(q, np.uint64)[:, None, None]).astype(np.uint32)
         x = torch.from_numpy(xh).to(dev)
         y = torch.empty_like(x)
@@ -255,8 +256,8 @@ def run_component(args, torch, dist, world, rank, local):
                 _lib.check(lib.cross_ntt(ctx.plan(), inv, a.data_ptr(), b.data_ptr(), B, _lib.LAYOUT_LIMB_MAJOR,
                                          ws.data_ptr(), ws.numel(), cs), "cross_ntt")
         units = 2 * B * Lw                                   # limb-transforms per step
-        metric, unit = f"NTT+INTT limb-transforms/s (N=2^16, {red})", "limb-transform/s"
-        workload = f"BAT NTT then INTT, {red} reduction, N=2^16 (256x256), 24 limbs x 16 polys per GPU"
+        metric, unit = f"NTT+INTT limb-transforms/s (N={nd}, {red})", "limb-transform/s"
+        workload = f"BAT NTT then INTT, {red} reduction, N={nd} ({rr}x{cc}), {Lw} limbs x {B} polys per GPU"
         hin = torch.from_numpy(np.ascontiguousarray(xh.transpose(0, 2, 3, 1))).pin_memory()   # (B, R, C, L)
 
         def e2e_step():
@@ -265,7 +266,7 @@ def run_component(args, torch, dist, world, rank, local):
         sample_x = np.ascontiguousarray(xh[:1].transpose(0, 2, 3, 1))
 
         def cpu_once():
-            ref = O.NTTBarrett(q, R, C) if red == "barrett" else V.NTTVariant(q, R, C, red)
+            ref = O.NTTBarrett(q, rr, cc) if red == "barrett" else V.NTTVariant(q, rr, cc, red)
             t0 = time.perf_counter()
             ref.intt(ref.ntt(sample_x))
             return time.perf_counter() - t0
@@ -273,12 +274,12 @@ def run_component(args, torch, dist, world, rank, local):
         if red == "shoup":
             # CUDA cores: per limb-transform 2 N (R + C) multiply-adds (the sum and
             # its Shoup companion over both stages)
-            ops = units * 2.0 * N_DEG * (R + C)
+            ops = units * 2.0 * nd * (rr + cc)
             nominal = 148 * 128 * 1.965e9 / 1e12
             roof = {"bound": "cuda-core int32 issue", "unit": "TMAC/s", "peak": nominal,
                     "peak_source": "nominal 148 SMs x 128 int32 lanes x 1965 MHz (no measured figure on this pool)"}
         else:
-            ops = units * 32.0 * N_DEG * (R + C)
+            ops = units * 32.0 * nd * (rr + cc)
             roof = {"bound": "tensor", "unit": "TOPS (int8)", "peak": 2.0 * pk["bf16_tflops"],
                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src})"}
         roof["kernel"] = "all launches of one NTT + INTT (2 contraction stages each)"
