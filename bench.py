@@ -9,7 +9,7 @@ rank processes its own batch of 64 (the reference shards the batch axis only).
 
 Prints one JSON line on rank 0.  Other workloads of the same line format:
   --workload herot              HE-Rotate at the same point (B, 2, r, c, L) -> (B, 2, N, L)
-  --limbs L --special K --dnum D  another HE-Mult / HE-Rotate point (35, 7, 5: the 8-GPU box point)
+  --limbs L --special K --dnum D  another HE-Mult / HE-Rotate point (35, 7, 5: the 8-GPU point)
   --workload ntt / bconv        the transform or the basis conversion alone for one reduction
                                 (--reduction barrett | montgomery | shoup | bat_lazy): NTT + INTT
                                 over --ntt-limbs limbs x --ntt-polys polys of N = --ntt-degree

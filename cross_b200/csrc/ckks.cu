@@ -345,42 +345,63 @@ __global__ void k_decode_scale(const uint32_t* __restrict__ x, int W, const uint
   }
 }
 
-// ckks_ctx.py:458-481 (_stddev) in CPython's order: one thread, sequential
-// sums.  cur: the slots values; out: the standard deviation estimate.
-__global__ void k_decode_stddev(const double2* __restrict__ cur, int s, double* __restrict__ out) {
-  if (threadIdx.x || blockIdx.x) return;
-  auto conj = [&](int idx) -> double2 {
-    if (idx == 0) return make_double2(cur[0].x, -cur[0].y);
-    const double2 z = cur[s - idx];
-    return make_double2(-z.y, -z.x);
-  };
+// Sum of one double per thread over a block of SD_THREADS threads (warp
+// shuffles, then the warp totals); every thread receives the total.
+constexpr int SD_THREADS = 1024;
+__device__ double block_sum(double v, double* red) {
+  for (int o = 16; o; o >>= 1) v = __dadd_rn(v, __shfl_down_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double w = red[threadIdx.x];
+    for (int o = 16; o; o >>= 1) w = __dadd_rn(w, __shfl_down_sync(0xffffffffu, w, o));
+    if (threadIdx.x == 0) red[0] = w;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// ckks_ctx.py:458-481 (_stddev): the mean and variance of cur - conj(cur)
+// over slots 0 .. s/2, as one block with parallel sums.  CPython's sum()
+// compensates its own float additions, so no summation order reproduces the
+// reference's last bits; the estimate only decides whether decode raises.
+// cur: the slot values; out: the standard deviation estimate.
+__global__ void __launch_bounds__(SD_THREADS) k_decode_stddev(const double2* __restrict__ cur, int s,
+                                                              double* __restrict__ out) {
+  __shared__ double red[SD_THREADS / 32];
   if (s == 1) {
-    *out = cur[0].y;
+    if (threadIdx.x == 0) *out = cur[0].y;
     return;
   }
+  auto cv = [&](int i) -> double2 {
+    const double2 c = i == 0 ? make_double2(cur[0].x, -cur[0].y) : make_double2(-cur[s - i].y, -cur[s - i].x);
+    return csub(cur[i], c);
+  };
   const double dslots = 2.0 * s;
-  auto cv = [&](int i) { return csub(cur[i], conj(i)); };
-  double sum = 0.0;
-  for (int i = 1; i < s / 2; ++i) {
+  double part = 0.0;
+  for (int i = 1 + threadIdx.x; i < s / 2; i += SD_THREADS) {
     const double2 c = cv(i);
-    sum = __dadd_rn(sum, __dadd_rn(c.x, c.y));
+    part = __dadd_rn(part, __dadd_rn(c.x, c.y));
   }
-  double mean = __dmul_rn(2.0, sum);
+  double mean = __dmul_rn(2.0, block_sum(part, red));
   mean = __dadd_rn(mean, cv(0).y);
   mean = __dadd_rn(mean, __dmul_rn(2.0, cv(s / 2).x));
   mean = __ddiv_rn(mean, __dsub_rn(dslots, 1.0));
-  double vs = 0.0;
-  for (int i = 1; i < s / 2; ++i) {
+  part = 0.0;
+  for (int i = 1 + threadIdx.x; i < s / 2; i += SD_THREADS) {
     const double2 c = cv(i);
     const double a = __dsub_rn(c.x, mean), b = __dsub_rn(c.y, mean);
-    vs = __dadd_rn(vs, __dadd_rn(__dmul_rn(a, a), __dmul_rn(b, b)));
+    part = __dadd_rn(part, __dadd_rn(__dmul_rn(a, a), __dmul_rn(b, b)));
   }
-  double var = __dmul_rn(2.0, vs);
-  const double a0 = __dsub_rn(cv(0).y, mean), a1 = __dsub_rn(cv(s / 2).x, mean);
-  var = __dadd_rn(var, __dmul_rn(a0, a0));
-  var = __dadd_rn(var, __dmul_rn(2.0, __dmul_rn(a1, a1)));
-  var = __ddiv_rn(var, __dsub_rn(dslots, 2.0));
-  *out = __dmul_rn(0.5, __dsqrt_rn(var));
+  double var = __dmul_rn(2.0, block_sum(part, red));
+  if (threadIdx.x == 0) {
+    const double a0 = __dsub_rn(cv(0).y, mean), a1 = __dsub_rn(cv(s / 2).x, mean);
+    var = __dadd_rn(var, __dmul_rn(a0, a0));
+    var = __dadd_rn(var, __dmul_rn(2.0, __dmul_rn(a1, a1)));
+    var = __ddiv_rn(var, __dsub_rn(dslots, 2.0));
+    *out = __dmul_rn(0.5, __dsqrt_rn(var));
+  }
 }
 
 // ckks_ctx.py:496-505: cur[i] = (re_i s + conj_i.re s, im_i s + conj_i.im s).
@@ -572,7 +593,7 @@ int cross_ckks_decode_scale(const uint32_t* x, int words, const uint32_t* q_word
 
 int cross_ckks_decode_stddev(const double* cur, int slots, double* out, void* stream) {
   CROSS_REQUIRE(slots >= 1 && cur && out, "cross_ckks_decode_stddev: bad argument");
-  k_decode_stddev<<<1, 32, 0, (cudaStream_t)stream>>>(reinterpret_cast<const double2*>(cur), slots, out);
+  k_decode_stddev<<<1, SD_THREADS, 0, (cudaStream_t)stream>>>(reinterpret_cast<const double2*>(cur), slots, out);
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;

@@ -354,8 +354,8 @@ int cross_crt_combine(cross_moduli moduli, const uint32_t* rns, int64_t n, const
 int cross_ckks_decode_scale(const uint32_t* x, int words, const uint32_t* q_words, const uint32_t* half_words,
                             double sf_pre, int slots, int nh, double* out, int* overflow, void* stream);
 
-/* The approximation-error estimate of ckks_decode (ckks_ctx.py:458-481), one
- * sequential pass: *out (device) = the standard deviation. */
+/* The approximation-error estimate of ckks_decode (ckks_ctx.py:458-481):
+ * *out (device) = the standard deviation (one block, parallel sums). */
 int cross_ckks_decode_stddev(const double* cur, int slots, double* out, void* stream);
 
 /* ckks_ctx.py:496-505: out[i] = in[i] scale + conj(in)[i] scale (component-wise). */

@@ -227,8 +227,8 @@ def crt_combine(rns, moduli) -> List[int]:
     return out
 
 
-def decode_stddev_check(cur: list, degree: int, p: int) -> None:
-    """ckks_ctx.py:448-486: the approximation-error check of ckks_decode."""
+def decode_stddev(cur: list) -> float:
+    """ckks_ctx.py:448-481: the approximation-error estimate of ckks_decode."""
     n = len(cur)
     conj = [None] * n
     for idx in range(1, n):
@@ -250,6 +250,12 @@ def decode_stddev_check(cur: list, degree: int, p: int) -> None:
         var += 2 * (cv[s // 2].real - mean) ** 2
         var /= (dslots - 2.0)
         sd = 0.5 * math.sqrt(var)
+    return sd
+
+
+def decode_stddev_check(cur: list, degree: int, p: int) -> None:
+    """ckks_ctx.py:482-486: the approximation-error check of ckks_decode."""
+    sd = decode_stddev(cur)
     logstd = math.log2(sd) if sd > 0 else float("-inf")
     if logstd > p - 5.0:
         raise Exception("The decryption failed because the approximation error is too high. Check the parameters. ")

@@ -107,6 +107,22 @@ def test_decrypt_crt_decode_vs_oracle(deg, towers):
     assert ints == K.crt_combine(want, qt)
 
 
+@pytest.mark.parametrize("slots", [1, 2, 4, 6, 4096, 32768])
+def test_decode_stddev_vs_oracle(slots):
+    """ckks_ctx.py:448-481: the device's approximation-error estimate (parallel
+    sums) against the oracle's sequential one at a relative tolerance of 1e-12;
+    the reference's sum() compensates, so no summation order is bit for bit."""
+    import torch
+    from cross_b200 import _lib, _tensor
+    rng = np.random.default_rng(slots)
+    cur = rng.normal(0.0, 3.0, size=(slots, 2)) + 0.25
+    want = K.decode_stddev([complex(a, b) for a, b in cur])
+    dev = torch.from_numpy(cur).cuda()
+    out = torch.empty(1, dtype=torch.float64, device="cuda")
+    _tensor.call("cross_ckks_decode_stddev", dev.data_ptr(), slots, out.data_ptr(), _lib.cuda_stream())
+    assert float(out.cpu()[0]) == pytest.approx(want, rel=1e-12)
+
+
 def test_decode_bit_exact_random():
     """ckks_ctx.py:407-514 on an encoded (noise-free) plaintext of N = 2^12:
     the device slot values equal the oracle's exactly."""
