@@ -178,16 +178,21 @@ __global__ void __launch_bounds__(256) k_row_dp4a(LP in, LPo out, int64_t lps, i
 // dst[m][p][row][col] u32 (4 q-bytes per word).  `transpose_xy` selects
 // whether the first BAT axis (X) is the output row (col transforms: [z][k]) or
 // the contraction row (row transforms: [k][n]).
+// Every limb's output is written in order and each word once; the M limbs of
+// one source position are read together (contiguous in the source).
 void pack_bat(const uint8_t* bat, int X, int Y, int M, std::vector<uint32_t>& dst) {
-  dst.assign((size_t)M * 4 * X * Y, 0u);
-  for (int x = 0; x < X; ++x)
-    for (int q = 0; q < 4; ++q)
-      for (int y = 0; y < Y; ++y)
-        for (int p = 0; p < 4; ++p)
-          for (int m = 0; m < M; ++m) {
-            const uint8_t b = bat[((((size_t)x * 4 + q) * Y + y) * 4 + p) * M + m];
-            dst[(((size_t)m * 4 + p) * X + x) * Y + y] |= (uint32_t)b << (8 * q);
-          }
+  dst.resize((size_t)M * 4 * X * Y);
+  const size_t lw = (size_t)4 * X * Y;     // words per limb
+  const size_t qs = (size_t)Y * 4 * M;     // source stride of q
+  for (int p = 0; p < 4; ++p)
+    for (int x = 0; x < X; ++x)
+      for (int y = 0; y < Y; ++y) {
+        const uint8_t* s = bat + (((size_t)x * 4 * Y + y) * 4 + p) * M;
+        uint32_t* d = dst.data() + ((size_t)p * X + x) * Y + y;
+        for (int m = 0; m < M; ++m)
+          d[m * lw] = (uint32_t)s[m] | (uint32_t)s[qs + m] << 8 | (uint32_t)s[2 * qs + m] << 16 |
+                      (uint32_t)s[3 * qs + m] << 24;
+      }
 }
 
 void unpack_tw(const uint32_t* tw, int R, int C, int M, std::vector<uint32_t>& dst) {

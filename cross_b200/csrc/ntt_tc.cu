@@ -28,6 +28,7 @@
 
 #include <atomic>
 #include <cstdlib>
+#include <cstring>
 #include <vector>
 
 #include "internal.hpp"
@@ -936,18 +937,25 @@ bool tc_supported(int r, int c) {
 //   bat (X, 4 q, Y, 4 p, M); `x_is_out` when the first axis indexes the output n
 //   (ntt step 1 / intt step 3: n = z or l, w = r), else the second spatial axis does
 //   (ntt step 3 / intt step 1: w = c, n = n or l).
+//   dst[m][n][p][w][q] bytes: the four q-bytes of one (m, n, p, w) are one
+//   little-endian word, written in order per limb.
 void pack_tc(const uint8_t* bat, int X, int Y, int M, bool x_is_out, std::vector<uint8_t>& dst) {
   const int nout = x_is_out ? X : Y, kw = x_is_out ? Y : X;
-  dst.assign((size_t)M * 4 * nout * 4 * kw, 0);
-  for (int x = 0; x < X; ++x)
-    for (int q = 0; q < 4; ++q)
-      for (int y = 0; y < Y; ++y)
-        for (int p = 0; p < 4; ++p) {
-          const int n = x_is_out ? x : y, w = x_is_out ? y : x;
-          const size_t src = (((size_t)x * 4 + q) * Y + y) * 4 + p;
-          for (int m = 0; m < M; ++m)
-            dst[((size_t)m * 4 * nout + (size_t)n * 4 + p) * 4 * kw + (size_t)w * 4 + q] = bat[src * M + m];
+  dst.resize((size_t)M * 4 * nout * 4 * kw);
+  const size_t lw = (size_t)4 * nout * kw;     // words per limb
+  const size_t qs = (size_t)Y * 4 * M;         // source stride of q
+  for (int n = 0; n < nout; ++n)
+    for (int p = 0; p < 4; ++p)
+      for (int w = 0; w < kw; ++w) {
+        const int x = x_is_out ? n : w, y = x_is_out ? w : n;
+        const uint8_t* s = bat + (((size_t)x * 4 * Y + y) * 4 + p) * M;
+        uint8_t* d = dst.data() + (((size_t)n * 4 + p) * kw + w) * 4;
+        for (int m = 0; m < M; ++m) {
+          const uint32_t word = (uint32_t)s[m] | (uint32_t)s[qs + m] << 8 | (uint32_t)s[2 * qs + m] << 16 |
+                                (uint32_t)s[3 * qs + m] << 24;
+          std::memcpy(d + m * lw * 4, &word, 4);
         }
+      }
 }
 
 int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, const uint8_t* intt1,
@@ -967,9 +975,11 @@ int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, 
   if ((rc = upload_vec(&P->tc_row_inv, buf))) return rc;
   // intt twiddle as [limb][l][r] (output index major) for the row-stage epilogue
   std::vector<uint32_t> tw((size_t)M * R * C);
-  for (int r = 0; r < R; ++r)
-    for (int l = 0; l < C; ++l)
-      for (int m = 0; m < M; ++m) tw[((size_t)m * C + l) * R + r] = intt_tw[((size_t)r * C + l) * M + m];
+  for (int l = 0; l < C; ++l)
+    for (int r = 0; r < R; ++r) {
+      const uint32_t* s = intt_tw + ((size_t)r * C + l) * M;
+      for (int m = 0; m < M; ++m) tw[((size_t)m * C + l) * R + r] = s[m];
+    }
   if ((rc = upload_vec(&P->tc_tw_inv, tw))) return rc;
   std::vector<int> zero(1, 0);
   if ((rc = upload(&P->tc_err, zero.data(), 1))) return rc;
