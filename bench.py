@@ -15,6 +15,9 @@ Prints one JSON line on rank 0.  Other workloads of the same line format:
                                 over --ntt-limbs limbs x --ntt-polys polys of N = --ntt-degree
                                 (default 2^16, 24, 16); BConv 24 -> 25 limbs, 32 polys of N = 2^16
   --workload ckks               a CKKS encode -> encrypt -> decrypt -> decode round trip
+  --workload bts                the bootstrapping kernel mix: every (kernel, size) of a CKKS
+                                bootstrapping's schedule timed, latencies weighted by invocation
+                                counts (us per polynomial, lower is better)
 """
 from __future__ import annotations
 
@@ -179,6 +182,22 @@ def run_reference(args):
     cores (all BLAS threads), W warm-up and K timed steps of one ciphertext."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "bts":
+        t0 = time.perf_counter()
+        for _ in range(args.warmup + args.steps):
+            total, per, sample = bts_oracle_estimate()
+        dt = (time.perf_counter() - t0) / max(args.warmup + args.steps, 1)
+        print(json.dumps({"impl": "reference", "metric": "CKKS bootstrapping kernel-mix latency (us per polynomial, N=2^16)",
+                          "value": total, "unit": "us", "n_gpus": args.gpus, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": 1000.0 * dt, "higher_is_better": False,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "u32 residues, u64 intermediates",
+                          "data": "synthetic seeded", "config": {"workload": "tabIX bootstrapping schedule"},
+                          "by_kernel_us": per,
+                          "cpu_baseline": {"value": total, "unit": "us", "cores": os.cpu_count(), "kind": "port",
+                                           "sample": sample},
+                          "e2e": {"value": total, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
         return
     fn, ct, unit, name = _oracle_op(args.workload)
     for _ in range(args.warmup):
@@ -353,6 +372,167 @@ def run_component(args, torch, dist, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# Algorithmic work per polynomial of each kernel of the bootstrapping mix:
+# HBM bytes for the element-wise kernels and the permutation, int8 tensor
+# operations for the transform and the basis conversion (the same per-limb
+# counts as the NTT and BConv configurations).
+def _bts_work(kernel, dims):
+    n = N_DEG
+    if kernel in ("add", "mult"):
+        return "hbm", 3 * 4 * n * dims[0]
+    if kernel == "automorph":
+        return "hbm", 2 * 4 * n * dims[0]
+    if kernel == "ntt_common":
+        return "tensor", 32.0 * n * (R + C) * dims[0]
+    return "tensor", 2.0 * n * (4 * dims[0]) * (4 * dims[1])
+
+
+def bts_oracle_estimate():
+    """The oracle's latency for the bootstrapping mix on the host cores, from a
+    bounded sample: one row of each kernel type timed (add 30, mult 30,
+    automorph 30 limbs, ntt_common 10 limbs, basis_convert 10 -> 30), every
+    row of the schedule scaled from its type's sample by limbs (a x b for the
+    basis conversion).  Returns (total us, per-type us, sample text)."""
+    import numpy as np
+    from cross_b200 import bts_mix, util
+    from oracle import cross_oracle as O
+    from oracle import variants as V
+    q = bts_mix.default_moduli()
+    rng = np.random.default_rng(7)
+
+    def res(shape, mods, axis):
+        qa = np.array(mods, np.uint64).reshape([-1 if a == axis else 1 for a in range(len(shape))])
+        return (rng.integers(0, 2 ** 62, size=shape, dtype=np.uint64) % qa).astype(np.uint32)
+    cmap = np.asarray(util.precompute_auto_map(N_DEG, util.find_automorphism_index_2n_complex(1, N_DEG)), np.int64)
+    ntt = V.NTTVariant(q[:10], R, C, "montgomery")
+    bc = O.BConvBarrett(q[:40])
+    bc.control_gen([(list(range(10)), list(range(10, 40)))])
+    a30, b30 = res((1, 30, N_DEG), q[:30], 1), res((1, 30, N_DEG), q[:30], 1)
+    m30, n30 = res((N_DEG, 30), q[:30], 1), res((N_DEG, 30), q[:30], 1)
+    x10, xb = res((1, R, C, 10), q[:10], 3), res((1, N_DEG, 10), q[:10], 2)
+    bar = O.Barrett(q[:30])
+    samples = {
+        "add": (30, lambda: O.jax_add(a30, b30, q[:30])),
+        "mult": (30, lambda: bar.reduce(m30.astype(np.uint64) * n30)),
+        "automorph": (30, lambda: m30[None][:, cmap, :]),
+        "ntt_common": (10, lambda: ntt.ntt(x10)),
+        "basis_convert": (300, lambda: bc.basis_change_bat(xb)),
+    }
+    per_unit = {}
+    for k, (units, fn) in samples.items():
+        fn()
+        t0 = time.perf_counter()
+        fn()
+        per_unit[k] = (time.perf_counter() - t0) * 1e6 / units
+    totals, total = {}, 0.0
+    for kernel, dims, count in bts_mix.invocations():
+        units = dims[0] * dims[1] if kernel == "basis_convert" else dims[0]
+        lat = per_unit[kernel] * units
+        part = lat if (kernel == "ntt_common" and dims[0] == 1) else lat * count
+        totals[kernel] = totals.get(kernel, 0.0) + part
+        total += part
+    return total, totals, ("one row of each kernel type on the oracle (add/mult/automorph 30 limbs, "
+                           "Montgomery NTT 10 limbs, BConv 10->30), every schedule row scaled from it by limbs")
+
+
+def run_bts(args, torch, dist, world, rank, local):
+    """--workload bts: the CKKS bootstrapping kernel mix (tabIX.py).  Every
+    (kernel, size) of the schedule is timed on device-resident operands with
+    CUDA events (W warm-up and max(K, copies) timed calls cycling through
+    enough operand copies to defeat L2, run back to back on the device); the
+    value is the schedule's accumulated latency per polynomial, max over ranks
+    divided by the ranks (each GPU runs its own polynomials, as the
+    reference's one per device).  host_issued_total_us is the same sum with
+    the calls timed as Python issues them one by one."""
+    from cross_b200 import _lib, bts_mix, shard
+    dev = torch.device("cuda", local)
+    lib = _lib.lib()
+    rows = bts_mix.invocations()
+    mix = bts_mix.KernelMix(batch=args.bts_batch, seed=rank, layout=args.bts_layout)
+    lines, host_lines = [], []
+    launches = 0
+    logf = open(args.bts_log, "w") if (args.bts_log and rank == 0) else None
+    order = bts_mix.schedule_order(rows)
+    with ClockSampler(local) as clk:
+        h0 = time.time()
+        for i, (kernel, dims) in enumerate(order):
+            cs = mix.case(kernel, dims)
+            l0 = lib.cross_launch_count()
+            us = mix.time_case(cs, reps=args.steps, warmup=args.warmup, queued=True)
+            timed = max(args.steps, cs.sets)          # time_case's timed calls
+            launches += (lib.cross_launch_count() - l0) * timed // (timed + args.warmup)
+            host_us = mix.time_case(cs, reps=args.steps, warmup=0, queued=False)
+            lines.append(bts_mix.latency_line(kernel, dims, us))
+            host_lines.append(bts_mix.latency_line(kernel, dims, host_us))
+            if logf:
+                logf.write(lines[-1] + "\n")
+                logf.flush()
+            if rank == 0 and (i + 1) % 40 == 0:
+                print(f"bts: {i + 1}/{len(order)} rows, {time.time() - h0:.1f} s", file=sys.stderr, flush=True)
+            del cs
+        h1 = time.time()
+    if logf:
+        logf.close()
+    for ctx in (mix._ntt, mix._ntt_sm):
+        if ctx is not None:
+            ctx.check_device()
+    log = "\n".join(lines) + "\n"
+    summ = bts_mix.summary(log)
+    host_total = bts_mix.accumulate_latency_from_log("\n".join(host_lines) + "\n")
+    total = shard.max_over_ranks(summ["total_us"], device=dev)
+    value = total / world
+    lat = bts_mix.parse_latency_log(log)
+    pk, src = peaks()
+    by_kernel = {}
+    for kernel in bts_mix.KERNELS:
+        work = t_us = 0.0
+        bound = None
+        for k, dims, count in rows:
+            if k != kernel:
+                continue
+            bound, w = _bts_work(k, dims)
+            c = 1 if (k == "ntt_common" and dims[0] == 1) else count
+            work += w * c
+            t_us += lat[(k, ",".join(map(str, dims)))] * c
+        if bound == "hbm":
+            a = work / (t_us * 1e-6) / 1e9
+            by_kernel[kernel] = {"bound": "hbm", "achieved": a, "unit": "GB/s", "peak": pk["hbm_gbs"],
+                                 "frac": a / pk["hbm_gbs"], "share_pct": summ["ratios_pct"].get(kernel)}
+        else:
+            a = work / (t_us * 1e-6) / 1e12
+            by_kernel[kernel] = {"bound": "tensor", "achieved": a, "unit": "TOPS (int8)",
+                                 "peak": 2.0 * pk["bf16_tflops"], "frac": a / (2.0 * pk["bf16_tflops"]),
+                                 "share_pct": summ["ratios_pct"].get(kernel)}
+    top = max(summ["ratios_pct"], key=summ["ratios_pct"].get)
+    roof = dict(by_kernel[top])
+    roof.update({"kernel": f"{top} rows of the schedule (count-weighted)", "traffic": None,
+                 "peak_source": f"MEASURED_PEAKS.json ({src}); int8 = 2 x bf16_tflops"})
+    line = {"metric": "CKKS bootstrapping kernel-mix latency (us per polynomial, N=2^16)", "value": value,
+            "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": value / 1000.0, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u32 residues, u64 intermediates, u8 BAT contractions",
+            "data": "synthetic seeded uniform residues",
+            "config": {"workload": f"tabIX bootstrapping schedule: {len(rows)} (kernel, size) rows, N=2^16 "
+                                   f"(256x256), {args.bts_batch} polynomial(s) per call per GPU",
+                       "layout": {"native": "limb-major (the library's on-device layout)",
+                                  "reference": "limbs last (the reference's)"}[args.bts_layout],
+                       "l2": "each row cycles through operand copies totalling > 1.25 x L2"},
+            "by_kernel_us": summ["by_kernel_us"], "ratios_pct": summ["ratios_pct"],
+            "timing": "device time of each row's calls run back to back (issued while a spin kernel holds the "
+                      "stream), as tabIX.py reads kernel durations from the device trace",
+            "host_issued_total_us": host_total,
+            "e2e": None,
+            "e2e_note": "the mix is defined on device-resident operands (tabIX.py times jitted kernels on device arrays)",
+            "gpu_launches": int(launches), "clocks": clk.summary(h0, h1), "roofline": roof,
+            "by_kernel_roofline": by_kernel}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        t, per, sample = bts_oracle_estimate()
+        line["cpu_baseline"] = {"value": t, "unit": "us", "cores": os.cpu_count(), "kind": "port",
+                                "sample": sample, "by_kernel_us": per}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_ckks(args, torch, dist, world, rank, local):
     """--workload ckks: one CKKS round trip per step at N = 2^16 with 24 towers
     (ckks_ctx.py: encode -> encrypt with fresh noise -> decrypt -> decode of
@@ -449,7 +629,10 @@ def main():
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling runs use a small case)")
-    ap.add_argument("--workload", choices=["hemul", "herot", "ntt", "bconv", "ckks"], default="hemul")
+    ap.add_argument("--workload", choices=["hemul", "herot", "ntt", "bconv", "ckks", "bts"], default="hemul")
+    ap.add_argument("--bts-batch", type=int, default=1, help="polynomials per call of the bootstrapping mix")
+    ap.add_argument("--bts-log", default=None, help="write the mix's latency lines (tabIX.py format) here")
+    ap.add_argument("--bts-layout", choices=["native", "reference"], default="native")
     ap.add_argument("--reduction", choices=["barrett", "montgomery", "shoup", "bat_lazy"], default="barrett")
     ap.add_argument("--limbs", type=int, default=L, help="L of the HE-Mult / HE-Rotate point")
     ap.add_argument("--special", type=int, default=K, help="K of the HE-Mult / HE-Rotate point")
@@ -473,7 +656,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     if args.workload not in ("hemul", "herot"):
-        (run_ckks if args.workload == "ckks" else run_component)(args, torch, dist, world, rank, local)
+        {"ckks": run_ckks, "bts": run_bts}.get(args.workload, run_component)(args, torch, dist, world, rank, local)
         if dist:
             dist.barrier()
             dist.destroy_process_group()
