@@ -37,6 +37,16 @@ def basis_aligned_transformation(matrix: np.ndarray, moduli) -> np.ndarray:
 
 
 @functools.lru_cache(maxsize=512)
+def gen_twiddle_matrix(rows: int, cols: int, q: int, omega: int) -> np.ndarray:
+    """ntt_mm.py:75-97: T[r, c] = omega^(r c) mod q (int64)."""
+    return util.twiddle_matrix(rows, cols, q, omega).astype(np.int64)
+
+
+def gen_twiddle_matrix_inv(rows: int, cols: int, q: int, omega: int) -> np.ndarray:
+    """ntt_mm.py:100-119: T[r, c] = omega^-(r c) mod q (int64)."""
+    return util.twiddle_matrix(rows, cols, q, pow(omega, -1, q)).astype(np.int64)
+
+
 def _limb_tables(q: int, r: int, c: int):
     """The six raw twiddle tables of one modulus (ntt_mm.py:186-240), shared
     by every context that uses (q, r, c): HE-Mult, HE-Rotate and ciphertext
@@ -161,6 +171,12 @@ class NTTCiphertextContextBase:
     def to_original_format(self, a):
         """ntt_mm.py:245-246 (host)."""
         return np.asarray(self.ff_ctx.to_original_format(_tensor.to_numpy(a).astype(U64))).astype(U32)
+
+    def basis_aligned_transformation(self, matrix):
+        """ntt_mm.py:248-255: (rows, 4, cols, 4, M) uint8, the bytes of
+        (matrix << 8 i) mod q_m for a (rows, cols, M) table."""
+        m = np.asarray(matrix)
+        return basis_aligned_transformation(m, self.moduli[: m.shape[-1]])
 
     def get_jax_parameters(self):
         return {"rows": self.r, "cols": self.c, "finite_field_parameters": self.ff_ctx.get_jax_parameters()}

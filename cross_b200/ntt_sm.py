@@ -37,6 +37,7 @@ class NTTContextBase:
         assert self.c != 0, "c must be non-zero"
         assert self.ff_ctx is not None, "finite_field_context must be provided"
         self.transform_length = self.r * self.c
+        self._q = int(moduli)
         self._mm = self._make_mm()
         self.psi = self._mm.psi_list[0]
         self.omega = self._mm.omega_list[0]
@@ -63,19 +64,55 @@ class NTTContextBase:
         return cls([self.moduli], {"r": self.r, "c": self.c, "finite_field_context": self._mm_ff_ctx()})
 
     def _expose_tables(self):
-        """ntt_sm.py:143-152,214-221 names: the MAT tables and their BAT forms
-        in the computation format, for the one modulus."""
-        m = self._mm
-        self.ntt_tf_step1, self.ntt_tf_step2, self.ntt_tf_step3 = (
-            t[..., 0] for t in m.ntt_coefficients_precompute())
-        self.intt_tf_step1, self.intt_tf_step2, self.intt_tf_step3 = (
-            t[..., 0] for t in m.intt_coefficients_precompute())
-        self.ntt_tf_bat_mat_comp_step1 = m.ntt_bat_tf_step1[..., 0]
-        self.ntt_tf_mat_comp_step2 = np.asarray(m.ntt_tf_step2)[..., 0]
-        self.ntt_tf_bat_mat_comp_step3 = m.ntt_bat_tf_step3[..., 0]
-        self.intt_tf_bat_mat_comp_step1 = m.intt_bat_tf_step1[..., 0]
-        self.intt_tf_mat_comp_step2 = np.asarray(m.intt_tf_step2)[..., 0]
-        self.intt_tf_bat_mat_comp_step3 = m.intt_bat_tf_step3[..., 0]
+        """ntt_sm.py:143-152 with the reference's names for the one modulus:
+        the twiddle matrices (``*_tf_step*``, int64), their memory-aligned
+        forms (``*_tf_mat_step*``) and those in the computation format, BAT
+        for steps 1 and 3 (``*_tf_bat_mat_comp_step*``)."""
+        self._raw_tables()
+        self.memory_aligned_transformation()
+        fmt = self.to_computation_format
+        self.ntt_tf_bat_mat_comp_step1 = self.basis_aligned_transformation(fmt(self.ntt_tf_mat_step1))
+        self.ntt_tf_mat_comp_step2 = np.asarray(fmt(self.ntt_tf_mat_step2)).astype(U64)
+        self.ntt_tf_bat_mat_comp_step3 = self.basis_aligned_transformation(fmt(self.ntt_tf_mat_step3))
+        self.intt_tf_bat_mat_comp_step1 = self.basis_aligned_transformation(fmt(self.intt_tf_mat_step1))
+        self.intt_tf_mat_comp_step2 = np.asarray(fmt(self.intt_tf_mat_step2)).astype(U64)
+        self.intt_tf_bat_mat_comp_step3 = self.basis_aligned_transformation(fmt(self.intt_tf_mat_step3))
+
+    def _raw_tables(self):
+        """The twiddle matrices of ntt_sm.py:156-177 (not memory-aligned),
+        from the multi-modulus context's memory-aligned ones: the
+        bit-reversal permutation is its own inverse."""
+        q = self._q
+        pr, pc = np.array(ntt_mm.get_bit_reverse_perm(self.r)), np.array(ntt_mm.get_bit_reverse_perm(self.c))
+        t1, t2, t3, a, b, d = (t.astype(np.int64) for t in ntt_mm._limb_tables(q, self.r, self.c))
+        self.ntt_tf_step1, self.ntt_tf_step2, self.ntt_tf_step3 = t1[pr, :], t2[pr, :], t3[:, pc]
+        self.intt_tf_step1, self.intt_tf_step2, self.intt_tf_step3 = a[pc, :], b[pr, :], d[:, pr]
+
+    # -- offline (the reference's public table functions) ---------------------
+    def ntt_coefficients_precompute(self):
+        """ntt_sm.py:156-162: (step 1, step 2, step 3) twiddle matrices."""
+        return self.ntt_tf_step1.copy(), self.ntt_tf_step2.copy(), self.ntt_tf_step3.copy()
+
+    def intt_coefficients_precompute(self):
+        """ntt_sm.py:164-177: the inverse matrices, 1/C and 1/R folded into
+        steps 2 and 3."""
+        return self.intt_tf_step1.copy(), self.intt_tf_step2.copy(), self.intt_tf_step3.copy()
+
+    def memory_aligned_transformation(self):
+        """ntt_sm.py:195-221: bit-reversal row / column permutations of the
+        twiddle matrices into the ``*_tf_mat_step*`` attributes."""
+        pr, pc = np.array(ntt_mm.get_bit_reverse_perm(self.r)), np.array(ntt_mm.get_bit_reverse_perm(self.c))
+        self.ntt_tf_mat_step1 = self.ntt_tf_step1[pr, :]
+        self.ntt_tf_mat_step2 = self.ntt_tf_step2[pr, :]
+        self.ntt_tf_mat_step3 = self.ntt_tf_step3[:, pc]
+        self.intt_tf_mat_step1 = self.intt_tf_step1[pc, :]
+        self.intt_tf_mat_step2 = self.intt_tf_step2[pr, :]
+        self.intt_tf_mat_step3 = self.intt_tf_step3[:, pr]
+
+    def basis_aligned_transformation(self, matrix):
+        """ntt_sm.py:185-193: (rows, 4, cols, 4) uint8, the bytes of
+        (matrix << 8 i) mod q for i < 4."""
+        return ntt_mm.basis_aligned_transformation(np.asarray(matrix)[..., None], [self._q])[..., 0]
 
     def to_computation_format(self, a):
         """ntt_sm.py:179-180."""
@@ -143,14 +180,22 @@ class NTTShoupContext(NTTContextBase):
 
     def __init__(self, moduli: int, parameters: dict):
         super().__init__(moduli, parameters)
-        assert [self.moduli] == list(self.ff_ctx.moduli), "moduli must be the same as the moduli of the finite_field_context"
+        if type(self.moduli) is int:
+            self.moduli = [self.moduli]                 # ntt_sm.py:422-423
+        assert self.moduli == list(self.ff_ctx.moduli), "moduli must be the same as the moduli of the finite_field_context"
 
     def _expose_tables(self):
+        """ntt_sm.py:420-437: the base tables, then the memory-aligned ones in
+        the computation format with their Shoup companions."""
+        super()._expose_tables()
         m = self._mm
         for name in ("ntt_tf", "intt_tf"):
             for k in (1, 2, 3):
                 setattr(self, f"{name}_mat_step{k}", np.asarray(getattr(m, f"{name}_step{k}"))[..., 0])
-                setattr(self, f"{name}_mat_step{k}_shoup", np.asarray(getattr(m, f"{name}_step{k}_shoup"))[..., 0])
+                # companions as the reference stores them: uint32 for steps 1
+                # and 3 (below 2^32 since T < q), uint64 for step 2
+                setattr(self, f"{name}_mat_step{k}_shoup",
+                        np.asarray(getattr(m, f"{name}_step{k}_shoup"))[..., 0].astype(U64 if k == 2 else U32))
 
     def to_shoup_computation_format(self, a):
         """ntt_sm.py:440-447."""

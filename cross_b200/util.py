@@ -6,6 +6,7 @@ take seconds here instead of minutes).
 """
 from __future__ import annotations
 
+import copy
 import math
 from typing import List, Sequence
 
@@ -14,8 +15,74 @@ import numpy as np
 U32, U64 = np.uint32, np.uint64
 
 
+def num_bits(x: int) -> int:
+    """util.py:61-63: x.bit_length() - 1."""
+    return x.bit_length() - 1
+
+
 def is_power_of_two(x: int) -> bool:
     return x > 0 and (x & (x - 1)) == 0
+
+
+def to_tuple(a):
+    """util.py:71-76: nested tuples of an array or nested sequence."""
+    try:
+        return tuple(to_tuple(i) for i in a)
+    except TypeError:
+        return a
+
+
+def slice_first_k_along_axis0(arrays, k):
+    """util.py:79-89: (obj[:k] for every obj)."""
+    return tuple(arr[:k] for arr in arrays)
+
+
+def slice_k_to_end_along_axis0(arrays, k):
+    """util.py:92-102: (obj[k:] for every obj)."""
+    return tuple(arr[k:] for arr in arrays)
+
+
+def slice_kth_along_axis0(arrays, k):
+    """util.py:105-115: (obj[k] for every obj)."""
+    return tuple(arr[k] for arr in arrays)
+
+
+def slice_0_to_k0_to_k1_along_axis0(arrays, k0, k1):
+    """util.py:118-134: every object without its entries k0 .. k1-1.  Arrays
+    (numpy or torch) are concatenated, as the reference does for jax arrays;
+    sequences in a tuple or list are joined with ``+``."""
+    first = arrays[0]
+    if isinstance(first, np.ndarray):
+        return tuple(np.concatenate([x[:k0], x[k1:]]) for x in arrays)
+    if hasattr(first, "data_ptr"):
+        import torch
+        return tuple(torch.cat([x[:k0], x[k1:]]) for x in arrays)
+    if isinstance(arrays, tuple):
+        return tuple([arr[:k0] + arr[k1:] for arr in arrays])
+    if isinstance(arrays, list):
+        return [arr[:k0] + arr[k1:] for arr in arrays]
+    raise ValueError(f"Unsupported type: {type(arrays)}")
+
+
+def slice_k0_to_k1_axis0(arrays, k0, k1):
+    """util.py:137-146: (obj[k0:k1] for every obj)."""
+    return tuple(arr[k0:k1] for arr in arrays)
+
+
+def extended_gcd(a, b):
+    """util.py:151-157: (g, x, y) with a x + b y = g = gcd(a, b)."""
+    if b == 0:
+        return (a, 1, 0)
+    g, x, y = extended_gcd(b, a % b)
+    return (g, y, x - (a // b) * y)
+
+
+def modinv_manual(x, q):
+    """util.py:160-166: the inverse of x mod q by the extended Euclid."""
+    g, inv, _ = extended_gcd(x, q)
+    if g != 1:
+        raise Exception(f'Modular inverse does not exist for {x} modulo {q}')
+    return inv % q
 
 
 def modinv(x: int, q: int) -> int:
@@ -135,8 +202,10 @@ def find_moduli_ntt(total_number: int, precision: int, ntt_length: int) -> List[
     return out
 
 
-def compute_QHatInvModq_QHatModp(original_moduli: Sequence[int], target_moduli: Sequence[int]):
-    """util.py:311-353."""
+def compute_QHatInvModq_QHatModp(original_moduli: Sequence[int], target_moduli: Sequence[int],
+                                 perf_test: bool = False):
+    """util.py:311-353 (perf_test builds the real constants too: same cost,
+    checkable results)."""
     Q = 1
     for q in original_moduli:
         Q *= q
@@ -145,8 +214,8 @@ def compute_QHatInvModq_QHatModp(original_moduli: Sequence[int], target_moduli: 
     return inv, [[h % p for p in target_moduli] for h in qhat]
 
 
-def gamma_beta_calculation(moduli_list: Sequence[int]):
-    """util.py:461-492."""
+def gamma_beta_calculation(moduli_list: Sequence[int], perf_test: bool = False):
+    """util.py:461-492 (perf_test builds the real constants too)."""
     Q = 1
     for m in moduli_list[:-1]:
         Q *= m
@@ -164,6 +233,22 @@ def bit_reverse(x: int, bits: int) -> int:
         if (x >> i) & 1:
             r |= 1 << (bits - 1 - i)
     return r
+
+
+def bit_reverse_array(in_tower):
+    """util.py:623-630: a copy of the sequence in bit-reversed index order
+    (lists stay lists, arrays stay arrays)."""
+    x = copy.deepcopy(in_tower)
+    n = len(x)
+    rev = bit_reverse_indices(n) if n > 1 else np.zeros(n, np.int64)
+    if isinstance(x, np.ndarray):
+        return x[rev]
+    if hasattr(x, "data_ptr"):
+        import torch
+        return x[torch.as_tensor(rev, device=x.device)]
+    if isinstance(x, tuple):
+        return tuple(x[int(j)] for j in rev)
+    return [x[int(j)] for j in rev]
 
 
 def bit_reverse_indices(n: int) -> np.ndarray:
@@ -229,11 +314,84 @@ def barrett_constants(moduli: Sequence[int]):
     return s, w, sw, m
 
 
-def random_parameters(shape, modulus_list, seed: int = 0, dtype=np.uint32):
-    """Seeded stand-in of util.py:533-539: uniform in [0, min(moduli) - 1)."""
+def random_parameters(shape, modulus_list, dtype=np.int32, seed: int = 0):
+    """Seeded stand-in of util.py:533-539: uniform in [0, min(moduli) - 1).
+    numpy draws the values (the reference's come from jax.random, whose bits
+    are not reproduced)."""
     rng = np.random.default_rng(seed)
     hi = min(modulus_list) - 1
     return rng.integers(0, hi, size=shape, dtype=np.uint64).astype(dtype)
+
+
+def random_batched_ciphertext(shape, modulus_list, dtype=np.int32, seed: int = 0):
+    """Seeded stand-in of util.py:497-512: shape (B, r, c, M), limb m uniform
+    in [0, modulus_list[m])."""
+    assert len(modulus_list) == shape[-1]
+    rng = np.random.default_rng(seed)
+    q = np.array(modulus_list, np.uint64)
+    return (rng.integers(0, 2 ** 62, size=tuple(shape), dtype=np.uint64) % q).astype(dtype)
+
+
+def random_ciphertext(shape, modulus_list, dtype=np.int32, seed: int = 0):
+    """Seeded stand-in of util.py:515-530: shape (B, N, M), limb m uniform in
+    [0, modulus_list[m])."""
+    assert len(modulus_list) == shape[-1]
+    rng = np.random.default_rng(seed)
+    q = np.array(modulus_list, np.uint64)
+    return (rng.integers(0, 2 ** 62, size=tuple(shape), dtype=np.uint64) % q).astype(dtype)
+
+
+def any_primitive_root_of_unity(n: int, q: int) -> int:
+    """util.py:252-288: g^((q-1)/n) for the generator g of find_generator,
+    checked to have order exactly n."""
+    if (q - 1) % n != 0:
+        raise ValueError("n must divide q-1 for a primitive n-th root of unity to exist.")
+    omega = pow(find_generator(q), (q - 1) // n, q)
+    if pow(omega, n, q) != 1:
+        raise ValueError("Something went wrong: omega^n != 1")
+    for d in range(1, n):
+        if n % d == 0 and pow(omega, d, q) == 1:
+            raise ValueError("Found an exponent d < n with omega^d == 1, so omega is not primitive.")
+    return omega
+
+
+def compute_barrett_mu(modulus: int):
+    """util.py:291-308: (mu, k) with b = 2^(floor(ln m) + 1), k the digits of m
+    in base b, mu = floor(b^(2k) / m)."""
+    b = 2 ** (math.floor(math.log(modulus)) + 1)
+    k_val = math.floor(math.log(modulus, b)) + 1
+    return (b ** (2 * k_val)) // modulus, k_val
+
+
+def approx_mod_down_control_generation(current_moduli, target_moduli, perf_test: bool = False):
+    """util.py:356-367: (P^-1 mod q for the target moduli, the index where the
+    target moduli start and where the current ones start in current +
+    target, QHatInvModq, QHatModp of current -> target)."""
+    P = 1
+    for m in current_moduli:
+        P *= m
+    p_inv = [modinv(P, q) for q in target_moduli]
+    overall = list(current_moduli) + list(target_moduli)
+    inv, qm = compute_QHatInvModq_QHatModp(current_moduli, target_moduli)
+    return p_inv, len(overall) - len(target_moduli), len(overall) - len(current_moduli), inv, qm
+
+
+def compute_powers_of_psi(ring_dim: int, moduli: Sequence[int], perf_test: bool = False) -> np.ndarray:
+    """util.py:370-382: psi_q^i for i < ring_dim, psi_q = root_of_unity(2
+    ring_dim, q), one row per modulus, uint64."""
+    return np.stack([powers(root_of_unity(2 * ring_dim, q), ring_dim, q) for q in moduli]).astype(U64)
+
+
+def chunk_decomposition(x: int, chunkwidth: int = 8) -> np.ndarray:
+    """util.py:833-861: the chunkwidth-bit digits of x, least significant
+    first (uint16 / uint32 for widths 16 / 32, else uint8)."""
+    dtype = {16: np.uint16, 32: np.uint32}.get(chunkwidth, np.uint8)
+    mask = (1 << chunkwidth) - 1
+    out = []
+    while x > 0:
+        out.append(x & mask)
+        x >>= chunkwidth
+    return np.array(out, dtype=dtype)
 
 
 def parse_ciphertext_string(input_str: str):

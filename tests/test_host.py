@@ -204,3 +204,51 @@ def test_shoup_precompute_follows_the_reference_dtypes():
     assert not sh.precompute_constant_operand(a).any()
     np.testing.assert_array_equal(sh.precompute_constant_operand(a.astype(np.uint64)),
                                   (a.astype(np.uint64) << np.uint64(32)) // np.array(q, np.uint64))
+
+
+def _twiddle(rows, cols, q, omega):
+    """ntt_mm.py:75-97 restated: omega^(r c) mod q, one pow per entry."""
+    return np.array([[pow(omega, r * c, q) for c in range(cols)] for r in range(rows)], np.int64)
+
+
+def test_twiddle_matrix_functions_and_single_modulus_tables():
+    """ntt_mm.py:75-119 and ntt_sm.py:143-221: the twiddle matrices, their
+    memory-aligned forms and the BAT forms under the reference's names."""
+    from cross_b200 import finite_field as ff, ntt_mm, ntt_sm, util
+    q = O.find_moduli_ntt(1, 28, 2 * 256)[0]
+    r = c = 16
+    psi = util.root_of_unity(2 * r * c, q)
+    om = psi * psi % q
+    np.testing.assert_array_equal(ntt_mm.gen_twiddle_matrix(8, 4, q, om), _twiddle(8, 4, q, om))
+    inv = ntt_mm.gen_twiddle_matrix_inv(4, 8, q, om)
+    assert inv.dtype == np.int64
+    np.testing.assert_array_equal(inv, _twiddle(4, 8, q, pow(om, -1, q)))
+    for ffc, cls in ((ff.BarrettContext(q), ntt_sm.NTTBarrettContext),
+                     (ff.MontgomeryContext(q), ntt_sm.NTTMontgomeryContext)):
+        ctx = cls(q, {"r": r, "c": c, "finite_field_context": ffc})
+        oc, orow = pow(om, c, q), pow(om, r, q)
+        want = (_twiddle(r, r, q, oc), _twiddle(r, c, q, om), _twiddle(c, c, q, orow))
+        for got, w in zip(ctx.ntt_coefficients_precompute(), want):
+            assert got.dtype == np.int64
+            np.testing.assert_array_equal(got, w)
+        i1, i2, i3 = ctx.intt_coefficients_precompute()
+        np.testing.assert_array_equal(i1, _twiddle(c, c, q, pow(orow, -1, q)))
+        np.testing.assert_array_equal(i2, _twiddle(r, c, q, pow(om, -1, q)) * pow(c, -1, q) % q)
+        np.testing.assert_array_equal(i3, _twiddle(r, r, q, pow(oc, -1, q)) * pow(r, -1, q) % q)
+        perm = util.bit_reverse_indices(r)
+        np.testing.assert_array_equal(ctx.ntt_tf_mat_step1, ctx.ntt_tf_step1[perm, :])
+        np.testing.assert_array_equal(ctx.ntt_tf_mat_step3, ctx.ntt_tf_step3[:, perm])
+        np.testing.assert_array_equal(ctx.intt_tf_mat_step3, ctx.intt_tf_step3[:, perm])
+        # the BAT tables the device plan uses are those of the memory-aligned
+        # tables in the computation format
+        mm = ctx._mm
+        np.testing.assert_array_equal(ctx.ntt_tf_bat_mat_comp_step1, mm.ntt_bat_tf_step1[..., 0])
+        np.testing.assert_array_equal(ctx.intt_tf_bat_mat_comp_step3, mm.intt_bat_tf_step3[..., 0])
+        np.testing.assert_array_equal(ctx.ntt_tf_mat_comp_step2, np.asarray(mm.ntt_tf_step2)[..., 0])
+        bat = ctx.basis_aligned_transformation(ctx.ntt_tf_mat_step1)
+        assert bat.shape == (r, 4, r, 4) and bat.dtype == np.uint8
+        np.testing.assert_array_equal(mm.basis_aligned_transformation(ctx.ntt_tf_mat_step1[..., None])[..., 0], bat)
+    sh = ntt_sm.NTTShoupContext(q, {"r": r, "c": c, "finite_field_context": ff.ShoupContext(q)})
+    assert sh.moduli == [q]
+    assert sh.ntt_tf_mat_step1_shoup.dtype == np.uint32 and sh.ntt_tf_mat_step2_shoup.dtype == np.uint64
+    np.testing.assert_array_equal(sh.ntt_tf_step1, _twiddle(r, r, q, pow(om, c, q)))
