@@ -14,6 +14,8 @@ import numpy as np
 
 from . import _tensor, ntt_mm
 from . import finite_field as ff_context
+# ntt_sm.py:75-119 repeat ntt_mm.py's twiddle-matrix functions
+from .ntt_mm import gen_twiddle_matrix, gen_twiddle_matrix_inv  # noqa: F401
 
 U32, U64 = np.uint32, np.uint64
 
