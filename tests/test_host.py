@@ -252,3 +252,20 @@ def test_twiddle_matrix_functions_and_single_modulus_tables():
     assert sh.moduli == [q]
     assert sh.ntt_tf_mat_step1_shoup.dtype == np.uint32 and sh.ntt_tf_mat_step2_shoup.dtype == np.uint64
     np.testing.assert_array_equal(sh.ntt_tf_step1, _twiddle(r, r, q, pow(om, c, q)))
+
+
+def test_coefmap_factorisation_and_its_errors():
+    """herot.py:15-53: row / column factors of a decomposable map, and the
+    reference's ValueError for every malformed one."""
+    from cross_b200 import herot
+    row, col = herot.mat_1d_shuffle_to_2d(np.arange(16)[::-1].copy(), 4, 4)
+    assert row.dtype == np.int32 and row.tolist() == [3, 2, 1, 0] and col.tolist() == [3, 2, 1, 0]
+    row, col = herot.mat_1d_shuffle_to_2d(np.arange(16), 8, 2)
+    assert row.tolist() == list(range(8)) and col.tolist() == [0, 1]
+    swapped = np.arange(16)
+    swapped[[0, 1]] = swapped[[1, 0]]
+    for args, msg in (((np.arange(15), 4, 4), "1D of length"), ((np.arange(16).reshape(4, 4), 4, 4), "1D of length"),
+                      ((np.arange(0), 0, 0), "positive"), ((np.arange(12), 4, 3), "powers of two"),
+                      ((swapped, 4, 4), "NOT decomposable")):
+        with pytest.raises(ValueError, match=msg):
+            herot.mat_1d_shuffle_to_2d(*args)
