@@ -7,6 +7,7 @@ take seconds here instead of minutes).
 from __future__ import annotations
 
 import copy
+import functools
 import math
 from typing import List, Sequence
 
@@ -251,13 +252,16 @@ def bit_reverse_array(in_tower):
     return [x[int(j)] for j in rev]
 
 
+@functools.lru_cache(maxsize=64)
 def bit_reverse_indices(n: int) -> np.ndarray:
-    """util.py:633-645."""
+    """util.py:633-645.  Computed once per n and returned read-only (like the
+    reference's jax array): every ciphertext object of degree n holds it."""
     bits = int(math.log2(n))
     idx = np.arange(n, dtype=np.int64)
     rev = np.zeros(n, np.int64)
     for i in range(bits):
         rev |= ((idx >> i) & 1) << (bits - 1 - i)
+    rev.flags.writeable = False
     return rev
 
 
