@@ -1,0 +1,57 @@
+"""Cases recorded by make_golden_shim.py: the reference's own operators run on
+seeded inputs at sizes its tests do not cover, stored as digests of their
+outputs.  Shared by the generator and tests/test_oracle_shim.py, which
+rebuilds the same inputs and holds the oracle to the digests."""
+import hashlib
+
+import numpy as np
+
+U32 = np.uint32
+
+# (name, kind, parameters); N = r * c
+CASES = [
+    ("ntt_barrett_64x64_m8", "ntt", dict(reduction="barrett", r=64, c=64, limbs=8, batch=2)),
+    ("ntt_barrett_32x128_m4", "ntt", dict(reduction="barrett", r=32, c=128, limbs=4, batch=2)),
+    ("ntt_montgomery_64x64_m4", "ntt", dict(reduction="montgomery", r=64, c=64, limbs=4, batch=2)),
+    ("ntt_bat_lazy_64x64_m4", "ntt", dict(reduction="bat_lazy", r=64, c=64, limbs=4, batch=2)),
+    ("ntt_barrett_256x256_m1", "ntt", dict(reduction="barrett", r=256, c=256, limbs=1, batch=1)),
+    ("bconv_bat_n4096_8to23", "bconv", dict(bat=True, n=4096, sq=8, sp=23, batch=2)),
+    ("bconv_plain_n4096_8to23", "bconv", dict(bat=False, n=4096, sq=8, sp=23, batch=2)),
+    ("rescale_64x64_l6", "rescale", dict(r=64, c=64, limbs=6, batch=2)),
+    ("hemul_64x64_l6_k2_dnum3", "hemul", dict(r=64, c=64, limbs=6, special=2, dnum=3, batch=1)),
+    ("herot_64x64_l6_k2_dnum3", "herot", dict(r=64, c=64, limbs=6, special=2, dnum=3, batch=1, rotation=3)),
+    # the benchmark point: N = 2^16, L = 24, K = 8, dnum = 3, one ciphertext
+    ("bconv_bat_n65536_24to25", "bconv", dict(bat=True, n=65536, sq=24, sp=25, batch=1)),
+    ("hemul_256x256_l24_k8_dnum3", "hemul", dict(r=256, c=256, limbs=24, special=8, dnum=3, batch=1)),
+    ("herot_256x256_l24_k8_dnum3", "herot", dict(r=256, c=256, limbs=24, special=8, dnum=3, batch=1, rotation=5)),
+]
+
+
+def digest(a) -> str:
+    a = np.ascontiguousarray(np.asarray(a))
+    return hashlib.sha256(str(a.dtype).encode() + str(a.shape).encode() + a.tobytes()).hexdigest()
+
+
+def residues(seed: int, shape, moduli) -> np.ndarray:
+    """Uniform residues, limb m (the last axis) below moduli[m]."""
+    rng = np.random.default_rng(seed)
+    q = np.array(moduli, np.uint64)
+    return (rng.integers(0, 2 ** 62, size=tuple(shape), dtype=np.uint64) % q).astype(U32)
+
+
+def inputs(name: str, kind: str, p: dict, moduli):
+    """The seeded operands of one case, in the reference's layouts."""
+    seed = sum(map(ord, name))
+    if kind == "ntt":
+        return {"x": residues(seed, (p["batch"], p["r"], p["c"], p["limbs"]), moduli)}
+    if kind == "bconv":
+        return {"x": residues(seed, (p["batch"], p["n"], p["sq"]), moduli[:p["sq"]])}
+    if kind == "rescale":
+        return {"x": residues(seed, (p["batch"], 2, p["r"], p["c"], p["limbs"]), moduli)}
+    L, K, d, r, c = p["limbs"], p["special"], p["dnum"], p["r"], p["c"]
+    elems = 4 if kind == "hemul" else 2
+    out = {"x": residues(seed, (p["batch"], elems, r, c, L), moduli[:L])}
+    kshape = (d, r * c, L + K) if kind == "hemul" else (d, r, c, L + K)
+    out["evk_a"] = residues(seed + 1, kshape, moduli)
+    out["evk_b"] = residues(seed + 2, kshape, moduli)
+    return out

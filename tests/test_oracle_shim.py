@@ -1,0 +1,60 @@
+"""The oracle against the reference's own operators at sizes beyond the
+reference's N = 16 golden vectors: tests/golden/shim_digests.json holds the
+sha256 of jaxite_word's outputs (run by tests/golden/make_golden_shim.py on a
+numpy stand-in for jax, itself checked on those N = 16 goldens) on seeded
+inputs at N = 2^12 and 2^16; the oracle must produce the same bytes."""
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from oracle import cross_oracle as O
+from oracle import variants as V
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import shim_cases as S  # noqa: E402
+
+with open(os.path.join(HERE, "golden", "shim_digests.json")) as f:
+    DIGESTS = json.load(f)["cases"]
+
+
+def _oracle(name, kind, p, moduli):
+    ins = S.inputs(name, kind, p, moduli)
+    x = ins["x"]
+    if kind == "ntt":
+        if p["reduction"] == "barrett":
+            return O.NTTBarrett(moduli, p["r"], p["c"]).ntt(x)
+        return V.NTTVariant(moduli, p["r"], p["c"], p["reduction"]).ntt(x)
+    if kind == "bconv":
+        bc = O.BConvBarrett(moduli)
+        bc.control_gen([(list(range(p["sq"])), list(range(p["sq"], p["sq"] + p["sp"])))])
+        return bc.basis_change_bat(x) if p["bat"] else bc.basis_change(x)
+    if kind == "rescale":
+        return O.RescalePlan(moduli, p["r"], p["c"]).rescale(x)
+    L, r, c, d = p["limbs"], p["r"], p["c"], p["dnum"]
+    if kind == "hemul":
+        he = O.HEMul(p["batch"], r, c, d, 1, moduli[:L], moduli[L:])
+        he.setup_relinearization(ins["evk_a"], ins["evk_b"])
+        return he.mul(x)
+    n = r * c
+    h = O.HERot(r, c, d, moduli[:L], moduli[L:])
+    h.control_gen(p["batch"])
+    h.setup_rotate(ins["evk_a"], ins["evk_b"],
+                   O.precompute_auto_map(n, O.find_automorphism_index_2n_complex(p["rotation"], 2 * n)))
+    return h.rotate(x)
+
+
+def test_every_case_is_recorded():
+    assert sorted(DIGESTS) == sorted(name for name, _, _ in S.CASES)
+
+
+@pytest.mark.parametrize("name,kind,p", S.CASES, ids=[c[0] for c in S.CASES])
+def test_oracle_matches_the_reference_run(name, kind, p):
+    rec = DIGESTS[name]
+    assert rec["kind"] == kind and rec["params"] == p
+    out = np.asarray(_oracle(name, kind, p, rec["moduli"]))
+    assert list(out.shape) == rec["shape"]
+    assert S.digest(out.astype(rec["dtype"])) == rec["sha256"], f"{name}: oracle differs from the reference"
