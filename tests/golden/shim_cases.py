@@ -24,6 +24,10 @@ CASES = [
     ("bconv_bat_n65536_24to25", "bconv", dict(bat=True, n=65536, sq=24, sp=25, batch=1)),
     ("hemul_256x256_l24_k8_dnum3", "hemul", dict(r=256, c=256, limbs=24, special=8, dnum=3, batch=1)),
     ("herot_256x256_l24_k8_dnum3", "herot", dict(r=256, c=256, limbs=24, special=8, dnum=3, batch=1, rotation=5)),
+    # the CKKS client (ckks_ctx.py) at N = 2^12 with six 28-bit towers
+    ("ckks_encode_n4096_l6", "ckks_encode", dict(degree=4096, towers=6, scale=2.0 ** 40)),
+    ("ckks_encrypt_n4096_l6", "ckks_encrypt", dict(degree=4096, towers=6, scale=2.0 ** 40)),
+    ("ckks_decode_n4096_l6", "ckks_decode", dict(degree=4096, towers=6, scale=2.0 ** 40, p=40)),
 ]
 
 
@@ -37,6 +41,25 @@ def residues(seed: int, shape, moduli) -> np.ndarray:
     rng = np.random.default_rng(seed)
     q = np.array(moduli, np.uint64)
     return (rng.integers(0, 2 ** 62, size=tuple(shape), dtype=np.uint64) % q).astype(U32)
+
+
+def ckks_slots(name: str, p: dict):
+    """N/2 complex slot values, real and imaginary parts uniform in [-1, 1)."""
+    rng = np.random.default_rng(sum(map(ord, name)))
+    v = rng.uniform(-1.0, 1.0, size=(p["degree"] // 2, 2))
+    return [complex(a, b) for a, b in v]
+
+
+def ckks_encrypt_operands(name: str, p: dict, moduli):
+    """Public key (2, towers, N), v (towers, N) and e = (e0, e1) as Python
+    integer lists of residues."""
+    n, t = p["degree"], len(moduli)
+    pk = residues(sum(map(ord, name)) + 1, (2, n, t), moduli).transpose(0, 2, 1)
+    v = residues(sum(map(ord, name)) + 2, (n, t), moduli).T
+    e = residues(sum(map(ord, name)) + 3, (2, n, t), moduli).transpose(0, 2, 1)
+    as_lists = lambda a: [[[int(x) for x in row] for row in el] for el in a] if a.ndim == 3 else \
+        [[int(x) for x in row] for row in a]  # noqa: E731
+    return as_lists(pk), as_lists(v), as_lists(e)
 
 
 def inputs(name: str, kind: str, p: dict, moduli):

@@ -2,7 +2,8 @@
 reference's N = 16 golden vectors: tests/golden/shim_digests.json holds the
 sha256 of jaxite_word's outputs (run by tests/golden/make_golden_shim.py on a
 numpy stand-in for jax, itself checked on those N = 16 goldens) on seeded
-inputs at N = 2^12 and 2^16; the oracle must produce the same bytes."""
+inputs at N = 2^12 and 2^16, the CKKS client's encode / encrypt / decode
+included; the oracle must produce the same bytes (doubles too)."""
 import json
 import os
 import sys
@@ -10,6 +11,7 @@ import sys
 import numpy as np
 import pytest
 
+from oracle import ckks as K
 from oracle import cross_oracle as O
 from oracle import variants as V
 
@@ -21,7 +23,28 @@ with open(os.path.join(HERE, "golden", "shim_digests.json")) as f:
     DIGESTS = json.load(f)["cases"]
 
 
+def _oracle_ckks(name, kind, p, q):
+    n = p["degree"]
+    enc = K.ckks_encode(S.ckks_slots(name, p), 2 * n, q, p["scale"])
+    if kind == "ckks_encode":
+        return np.array(enc, np.uint64)
+    if kind == "ckks_encrypt":
+        pk, v, e = S.ckks_encrypt_operands(name, p, q)
+        return np.array(K.ckks_encrypt(enc, pk, q, v, e), np.uint64)
+    coefs = [[0] * len(q) for _ in range(n)]
+    for j, qj in enumerate(q):
+        col = O.intt_negacyclic(O.bit_reverse_array([enc[d][j] for d in range(n)]), qj, O.root_of_unity(2 * n, qj))
+        for d in range(n):
+            coefs[d][j] = col[d]
+    big_q = 1
+    for qj in q:
+        big_q *= qj
+    return np.array(K.ckks_decode(K.crt_combine(coefs, q), p["scale"], n // 2, big_q, p["p"]), np.complex128)
+
+
 def _oracle(name, kind, p, moduli):
+    if kind.startswith("ckks"):
+        return _oracle_ckks(name, kind, p, moduli)
     ins = S.inputs(name, kind, p, moduli)
     x = ins["x"]
     if kind == "ntt":
