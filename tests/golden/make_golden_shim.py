@@ -117,6 +117,12 @@ def run_case(name, kind, p, util, ntt, ff, bconv, Ciphertext, HEMul, HERot):
         return q, np.asarray(ct.get_batch_ciphertext())
     if kind.startswith("ckks"):
         return run_ckks(name, kind, p, util)
+    if kind == "evk":
+        import key_gen
+        ov = util.find_moduli_ntt(p["limbs"] + p["special"], 28, 2 * p["degree"])
+        sk, a, e = S.evk_operands(name, p, ov)
+        key = key_gen.gen_evaluation_key(sk, ov[:p["limbs"]], ov[p["limbs"]:], a=a, e=e, dnum=p["dnum"])
+        return ov, np.array(key["b"], np.uint64)
     r, c, L, K, d, B = p["r"], p["c"], p["limbs"], p["special"], p["dnum"], p["batch"]
     n = r * c
     ov = util.find_moduli_ntt(L + K, 28, 2 * n)

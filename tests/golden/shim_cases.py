@@ -28,6 +28,11 @@ CASES = [
     ("ckks_encode_n4096_l6", "ckks_encode", dict(degree=4096, towers=6, scale=2.0 ** 40)),
     ("ckks_encrypt_n4096_l6", "ckks_encrypt", dict(degree=4096, towers=6, scale=2.0 ** 40)),
     ("ckks_decode_n4096_l6", "ckks_decode", dict(degree=4096, towers=6, scale=2.0 ** 40, p=40)),
+    # the relinearisation key with given a and e (key_gen.py:108-254)
+    ("evk_n4096_l6_k2_dnum3", "evk", dict(degree=4096, limbs=6, special=2, dnum=3)),
+    # the variants at N = 2^16 (the BAT-lazy step-2 product wraps in uint64 there)
+    ("ntt_montgomery_256x256_m1", "ntt", dict(reduction="montgomery", r=256, c=256, limbs=1, batch=1)),
+    ("ntt_bat_lazy_256x256_m1", "ntt", dict(reduction="bat_lazy", r=256, c=256, limbs=1, batch=1)),
 ]
 
 
@@ -60,6 +65,19 @@ def ckks_encrypt_operands(name: str, p: dict, moduli):
     as_lists = lambda a: [[[int(x) for x in row] for row in el] for el in a] if a.ndim == 3 else \
         [[int(x) for x in row] for row in a]  # noqa: E731
     return as_lists(pk), as_lists(v), as_lists(e)
+
+
+def evk_operands(name: str, p: dict, moduli):
+    """private key (Q x N), a and e (parts x (Q + P) x N) as integer lists of
+    residues, evaluation form."""
+    n, L, d = p["degree"], p["limbs"], p["dnum"]
+    per = (L + d - 1) // d
+    parts = -(-L // per)
+    seed = sum(map(ord, name))
+    sk = residues(seed, (n, L), moduli[:L]).T
+    a = residues(seed + 1, (parts, n, len(moduli)), moduli).transpose(0, 2, 1)
+    e = residues(seed + 2, (parts, n, len(moduli)), moduli).transpose(0, 2, 1)
+    return sk.tolist(), a.tolist(), e.tolist()
 
 
 def inputs(name: str, kind: str, p: dict, moduli):

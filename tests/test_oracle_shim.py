@@ -45,6 +45,10 @@ def _oracle_ckks(name, kind, p, q):
 def _oracle(name, kind, p, moduli):
     if kind.startswith("ckks"):
         return _oracle_ckks(name, kind, p, moduli)
+    if kind == "evk":
+        sk, a, e = S.evk_operands(name, p, moduli)
+        key = K.gen_evaluation_key(sk, moduli[:p["limbs"]], moduli[p["limbs"]:], a, e, dnum=p["dnum"])
+        return np.array(key["b"], np.uint64)
     ins = S.inputs(name, kind, p, moduli)
     x = ins["x"]
     if kind == "ntt":
