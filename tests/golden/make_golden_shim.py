@@ -102,7 +102,9 @@ def run_case(name, kind, p, util, ntt, ff, bconv, Ciphertext, HEMul, HERot):
     if kind == "bconv":
         ov = util.find_moduli_ntt(p["sq"] + p["sp"], 28, 2 * p["n"])
         x = S.inputs(name, kind, p, ov)["x"]
-        bc = bconv.BConvBarrett(ov)
+        cls = {"barrett": bconv.BConvBarrett, "montgomery": bconv.BConvMontgomery, "bat_lazy": bconv.BConvBATLazy,
+               "shoup": bconv.BConvShoup}[p.get("reduction", "barrett")]
+        bc = cls(ov)
         bc.control_gen([(list(range(p["sq"])), list(range(p["sq"], p["sq"] + p["sp"])))])
         return ov, np.asarray(bc.basis_change_bat(x) if p["bat"] else bc.basis_change(x))
     if kind == "rescale":

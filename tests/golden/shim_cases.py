@@ -33,6 +33,14 @@ CASES = [
     # the variants at N = 2^16 (the BAT-lazy step-2 product wraps in uint64 there)
     ("ntt_montgomery_256x256_m1", "ntt", dict(reduction="montgomery", r=256, c=256, limbs=1, batch=1)),
     ("ntt_bat_lazy_256x256_m1", "ntt", dict(reduction="bat_lazy", r=256, c=256, limbs=1, batch=1)),
+    # the BConv reduction variants (bconv.py:261-390); BConvMontgomery's plain
+    # path needs size_q == size_p (bconv.py:280 broadcasts the one basis
+    # against the other)
+    ("bconv_montgomery_bat_n4096_8to23", "bconv", dict(bat=True, n=4096, sq=8, sp=23, batch=2, reduction="montgomery")),
+    ("bconv_montgomery_plain_n4096_8to8", "bconv", dict(bat=False, n=4096, sq=8, sp=8, batch=2, reduction="montgomery")),
+    ("bconv_bat_lazy_bat_n4096_8to23", "bconv", dict(bat=True, n=4096, sq=8, sp=23, batch=2, reduction="bat_lazy")),
+    ("bconv_bat_lazy_plain_n4096_8to23", "bconv", dict(bat=False, n=4096, sq=8, sp=23, batch=2, reduction="bat_lazy")),
+    ("bconv_shoup_plain_n4096_8to23", "bconv", dict(bat=False, n=4096, sq=8, sp=23, batch=2, reduction="shoup")),
 ]
 
 

@@ -64,7 +64,8 @@ def _device(name, kind, p, moduli):
         ctx = ctx_cls(moduli, {"r": p["r"], "c": p["c"], "finite_field_context": ff_cls(moduli)})
         return _np(ctx.ntt(x))
     if kind == "bconv":
-        b = bconv.BConvBarrett(moduli)
+        b = {"barrett": bconv.BConvBarrett, "montgomery": bconv.BConvMontgomery, "bat_lazy": bconv.BConvBATLazy,
+             "shoup": bconv.BConvShoup}[p.get("reduction", "barrett")](moduli)
         b.control_gen([(list(range(p["sq"])), list(range(p["sq"], p["sq"] + p["sp"])))])
         return _np(b.basis_change_bat(x) if p["bat"] else b.basis_change(x))
     r, c = p["r"], p["c"]

@@ -56,7 +56,8 @@ def _oracle(name, kind, p, moduli):
             return O.NTTBarrett(moduli, p["r"], p["c"]).ntt(x)
         return V.NTTVariant(moduli, p["r"], p["c"], p["reduction"]).ntt(x)
     if kind == "bconv":
-        bc = O.BConvBarrett(moduli)
+        red = p.get("reduction", "barrett")
+        bc = O.BConvBarrett(moduli) if red == "barrett" else V.BConvVariant(moduli, red)
         bc.control_gen([(list(range(p["sq"])), list(range(p["sq"], p["sq"] + p["sp"])))])
         return bc.basis_change_bat(x) if p["bat"] else bc.basis_change(x)
     if kind == "rescale":
