@@ -52,19 +52,15 @@ class _AtIndex:
 
 
 class ndarray(_np.ndarray):
-    """jax array stand-in.  Mixing uint64 with signed 64-bit arrays raises:
-    numpy would promote to float64 where jax does not, so such an operation
-    would not reproduce the reference."""
+    """jax array stand-in.  Binary operations promote as numpy does; for the
+    integer operands the reference mixes this is jax's lattice too (int64
+    with uint64 gives float64 in both)."""
 
     @property
     def at(self):
         return _At(self)
 
     def __array_ufunc__(self, ufunc, method, *inputs, **kwargs):
-        arrs = [x for x in inputs if isinstance(x, _np.ndarray) and x.ndim > 0]
-        kinds = {(x.dtype.kind, x.dtype.itemsize) for x in arrs}
-        if ("u", 8) in kinds and ("i", 8) in kinds:
-            raise TypeError(f"{ufunc.__name__}: uint64 with int64 operands (numpy would promote to float64)")
         args = [_np.asarray(x) if isinstance(x, ndarray) else x for x in inputs]
         if "out" in kwargs:
             kwargs["out"] = tuple(_np.asarray(o) if isinstance(o, ndarray) else o for o in kwargs["out"])

@@ -42,6 +42,12 @@ def check_stand_in(util, ntt, ff, bconv, Ciphertext, HEMul, HERot):
     out = np.asarray(ctx.ntt(coef))
     assert np.array_equal(out, ev), "NTT golden"
     assert np.array_equal(np.asarray(ctx.intt(out)), coef), "INTT golden"
+    # ntt_mm_test.py:86-121: the Shoup transform (byte convolutions)
+    sh = ntt.NTTCiphertextShoupContext(moduli=q, parameters={"r": r, "c": c,
+                                                              "finite_field_context": ff.ShoupContext(moduli=q)})
+    sh_ev = sh.ntt(coef)
+    assert np.array_equal(np.asarray(sh.to_original_format(sh_ev)), ev), "Shoup NTT golden"
+    assert np.array_equal(np.asarray(sh.to_original_format(sh.intt(sh_ev))), coef), "Shoup INTT golden"
 
     g = load("bconv")
     bc = bconv.BConvBarrett(g["original_moduli"] + g["target_moduli"])
@@ -93,12 +99,25 @@ def run_case(name, kind, p, util, ntt, ff, bconv, Ciphertext, HEMul, HERot):
         # transform reduces steps 2 and 3 with a BarrettContext)
         ctx_cls, ff_cls = {"barrett": (ntt.NTTCiphertextBarrettContext, ff.BarrettContext),
                            "montgomery": (ntt.NTTCiphertextMontgomeryContext, ff.MontgomeryContext),
-                           "bat_lazy": (ntt.NTTCiphertextBATLazyContext, ff.BarrettContext)}[p["reduction"]]
+                           "bat_lazy": (ntt.NTTCiphertextBATLazyContext, ff.BarrettContext),
+                           "shoup": (ntt.NTTCiphertextShoupContext, ff.ShoupContext)}[p["reduction"]]
         ctx = ctx_cls(moduli=q, parameters={"r": p["r"], "c": p["c"], "finite_field_context": ff_cls(moduli=q)})
         out = np.asarray(ctx.ntt(x))
         if p["reduction"] == "barrett":
             assert np.array_equal(np.asarray(ctx.intt(out)), x), f"{name}: INTT(NTT(x)) != x"
         return q, out
+    if kind == "ntt_sm":
+        import ntt_sm
+        q = util.find_moduli_ntt(1, 28, 2 * p["r"] * p["c"])
+        x = S.inputs(name, kind, p, q)["x"]
+        # the finite-field contexts of ntt_sm_test.py (the BAT-lazy one is
+        # the lazy context; the transform adds its own Barrett context)
+        ctx_cls, ff_cls = {"barrett": (ntt_sm.NTTBarrettContext, ff.BarrettContext),
+                           "montgomery": (ntt_sm.NTTMontgomeryContext, ff.MontgomeryContext),
+                           "bat_lazy": (ntt_sm.NTTBATLazyContext, ff.BATLazyContext),
+                           "shoup": (ntt_sm.NTTShoupContext, ff.ShoupContext)}[p["reduction"]]
+        ctx = ctx_cls(q[0], {"r": p["r"], "c": p["c"], "finite_field_context": ff_cls(moduli=q[0])})
+        return q, np.asarray(ctx.ntt(x))
     if kind == "bconv":
         ov = util.find_moduli_ntt(p["sq"] + p["sp"], 28, 2 * p["n"])
         x = S.inputs(name, kind, p, ov)["x"]

@@ -41,6 +41,13 @@ CASES = [
     ("bconv_bat_lazy_bat_n4096_8to23", "bconv", dict(bat=True, n=4096, sq=8, sp=23, batch=2, reduction="bat_lazy")),
     ("bconv_bat_lazy_plain_n4096_8to23", "bconv", dict(bat=False, n=4096, sq=8, sp=23, batch=2, reduction="bat_lazy")),
     ("bconv_shoup_plain_n4096_8to23", "bconv", dict(bat=False, n=4096, sq=8, sp=23, batch=2, reduction="shoup")),
+    # the Shoup transform (byte convolutions, ntt_mm.py:443-587)
+    ("ntt_shoup_64x64_m4", "ntt", dict(reduction="shoup", r=64, c=64, limbs=4, batch=2)),
+    # the single-modulus contexts (ntt_sm.py:330-494); Shoup takes one matrix
+    ("ntt_sm_barrett_64x64", "ntt_sm", dict(reduction="barrett", r=64, c=64, batch=2)),
+    ("ntt_sm_montgomery_64x64", "ntt_sm", dict(reduction="montgomery", r=64, c=64, batch=2)),
+    ("ntt_sm_bat_lazy_64x64", "ntt_sm", dict(reduction="bat_lazy", r=64, c=64, batch=2)),
+    ("ntt_sm_shoup_64x64", "ntt_sm", dict(reduction="shoup", r=64, c=64, batch=0)),
 ]
 
 
@@ -93,6 +100,9 @@ def inputs(name: str, kind: str, p: dict, moduli):
     seed = sum(map(ord, name))
     if kind == "ntt":
         return {"x": residues(seed, (p["batch"], p["r"], p["c"], p["limbs"]), moduli)}
+    if kind == "ntt_sm":
+        shape = (p["batch"], p["r"], p["c"]) if p["batch"] else (p["r"], p["c"])
+        return {"x": residues(seed, shape + (1,), moduli)[..., 0]}
     if kind == "bconv":
         return {"x": residues(seed, (p["batch"], p["n"], p["sq"]), moduli[:p["sq"]])}
     if kind == "rescale":

@@ -60,8 +60,17 @@ def _device(name, kind, p, moduli):
     if kind == "ntt":
         ctx_cls, ff_cls = {"barrett": (ntt_mm.NTTCiphertextBarrettContext, finite_field.BarrettContext),
                            "montgomery": (ntt_mm.NTTCiphertextMontgomeryContext, finite_field.MontgomeryContext),
-                           "bat_lazy": (ntt_mm.NTTCiphertextBATLazyContext, finite_field.BarrettContext)}[p["reduction"]]
+                           "bat_lazy": (ntt_mm.NTTCiphertextBATLazyContext, finite_field.BarrettContext),
+                           "shoup": (ntt_mm.NTTCiphertextShoupContext, finite_field.ShoupContext)}[p["reduction"]]
         ctx = ctx_cls(moduli, {"r": p["r"], "c": p["c"], "finite_field_context": ff_cls(moduli)})
+        return _np(ctx.ntt(x))
+    if kind == "ntt_sm":
+        from cross_b200 import ntt_sm
+        ctx_cls, ff_cls = {"barrett": (ntt_sm.NTTBarrettContext, finite_field.BarrettContext),
+                           "montgomery": (ntt_sm.NTTMontgomeryContext, finite_field.MontgomeryContext),
+                           "bat_lazy": (ntt_sm.NTTBATLazyContext, finite_field.BATLazyContext),
+                           "shoup": (ntt_sm.NTTShoupContext, finite_field.ShoupContext)}[p["reduction"]]
+        ctx = ctx_cls(moduli[0], {"r": p["r"], "c": p["c"], "finite_field_context": ff_cls(moduli[0])})
         return _np(ctx.ntt(x))
     if kind == "bconv":
         b = {"barrett": bconv.BConvBarrett, "montgomery": bconv.BConvMontgomery, "bat_lazy": bconv.BConvBATLazy,

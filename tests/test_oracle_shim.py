@@ -55,6 +55,12 @@ def _oracle(name, kind, p, moduli):
         if p["reduction"] == "barrett":
             return O.NTTBarrett(moduli, p["r"], p["c"]).ntt(x)
         return V.NTTVariant(moduli, p["r"], p["c"], p["reduction"]).ntt(x)
+    if kind == "ntt_sm":
+        # one modulus: the multi-modulus transform with M = 1 (Shoup on one matrix)
+        red, r, c = p["reduction"], p["r"], p["c"]
+        ctx = O.NTTBarrett(moduli, r, c) if red == "barrett" else V.NTTVariant(moduli, r, c, red)
+        y = ctx.ntt(x[..., None] if p["batch"] else x[None, ..., None])[..., 0]
+        return y if p["batch"] else y[0]
     if kind == "bconv":
         red = p.get("reduction", "barrett")
         bc = O.BConvBarrett(moduli) if red == "barrett" else V.BConvVariant(moduli, red)
