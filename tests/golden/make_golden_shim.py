@@ -106,6 +106,16 @@ def run_case(name, kind, p, util, ntt, ff, bconv, Ciphertext, HEMul, HERot):
         if p["reduction"] == "barrett":
             assert np.array_equal(np.asarray(ctx.intt(out)), x), f"{name}: INTT(NTT(x)) != x"
         return q, out
+    if kind == "ff":
+        import jax.numpy as jnp
+        q = util.find_moduli_ntt(p["limbs"], 28, 2 * 4096)
+        ins = {k: jnp.asarray(v) for k, v in S.inputs(name, kind, p, q).items()}
+        cls = {"barrett": ff.BarrettContext, "montgomery": ff.MontgomeryContext, "shoup": ff.ShoupContext,
+               "bat_lazy": ff.BATLazyContext}[p["reduction"]]
+        ctx = cls(moduli=q)
+        out = ctx.modular_reduction(ins["z"], ins["z_s"]) if p["reduction"] == "shoup" else \
+            ctx.modular_reduction(ins["z"])
+        return q, np.asarray(out)
     if kind == "ntt_sm":
         import ntt_sm
         q = util.find_moduli_ntt(1, 28, 2 * p["r"] * p["c"])

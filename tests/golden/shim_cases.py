@@ -48,6 +48,12 @@ CASES = [
     ("ntt_sm_montgomery_64x64", "ntt_sm", dict(reduction="montgomery", r=64, c=64, batch=2)),
     ("ntt_sm_bat_lazy_64x64", "ntt_sm", dict(reduction="bat_lazy", r=64, c=64, batch=2)),
     ("ntt_sm_shoup_64x64", "ntt_sm", dict(reduction="shoup", r=64, c=64, batch=0)),
+    # the four finite_field.py reductions on products of residues
+    # (moduli on the last axis; Shoup with its companion product)
+    ("ff_barrett_4096x6", "ff", dict(reduction="barrett", rows=4096, limbs=6)),
+    ("ff_montgomery_4096x6", "ff", dict(reduction="montgomery", rows=4096, limbs=6)),
+    ("ff_shoup_4096x6", "ff", dict(reduction="shoup", rows=4096, limbs=6)),
+    ("ff_bat_lazy_4096x6", "ff", dict(reduction="bat_lazy", rows=4096, limbs=6)),
 ]
 
 
@@ -100,6 +106,16 @@ def inputs(name: str, kind: str, p: dict, moduli):
     seed = sum(map(ord, name))
     if kind == "ntt":
         return {"x": residues(seed, (p["batch"], p["r"], p["c"], p["limbs"]), moduli)}
+    if kind == "ff":
+        shape = (p["rows"], p["limbs"])
+        a = residues(seed, shape, moduli).astype(np.uint64)
+        t = residues(seed + 1, shape, moduli).astype(np.uint64)
+        out = {"z": a * t}
+        if p["reduction"] == "shoup":
+            # z_s = a * floor(t 2^32 / q) (finite_field.py:295-302)
+            ts = np.array([[(int(v) << 32) // q for v, q in zip(row, moduli)] for row in t.tolist()], np.uint64)
+            out["z_s"] = a * ts
+        return out
     if kind == "ntt_sm":
         shape = (p["batch"], p["r"], p["c"]) if p["batch"] else (p["r"], p["c"])
         return {"x": residues(seed, shape + (1,), moduli)[..., 0]}

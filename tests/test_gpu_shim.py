@@ -56,7 +56,7 @@ def _device(name, kind, p, moduli):
         return _np(key_gen.gen_evaluation_key(sk, moduli[:p["limbs"]], moduli[p["limbs"]:], a=a, e=e,
                                               dnum=p["dnum"])["b"])
     ins = S.inputs(name, kind, p, moduli)
-    x = ins["x"]
+    x = ins.get("x")
     if kind == "ntt":
         ctx_cls, ff_cls = {"barrett": (ntt_mm.NTTCiphertextBarrettContext, finite_field.BarrettContext),
                            "montgomery": (ntt_mm.NTTCiphertextMontgomeryContext, finite_field.MontgomeryContext),
@@ -64,6 +64,11 @@ def _device(name, kind, p, moduli):
                            "shoup": (ntt_mm.NTTCiphertextShoupContext, finite_field.ShoupContext)}[p["reduction"]]
         ctx = ctx_cls(moduli, {"r": p["r"], "c": p["c"], "finite_field_context": ff_cls(moduli)})
         return _np(ctx.ntt(x))
+    if kind == "ff":
+        red = p["reduction"]
+        ctx = {"barrett": finite_field.BarrettContext, "montgomery": finite_field.MontgomeryContext,
+               "shoup": finite_field.ShoupContext, "bat_lazy": finite_field.BATLazyContext}[red](moduli)
+        return _np(ctx.modular_reduction(ins["z"], ins["z_s"]) if red == "shoup" else ctx.modular_reduction(ins["z"]))
     if kind == "ntt_sm":
         from cross_b200 import ntt_sm
         ctx_cls, ff_cls = {"barrett": (ntt_sm.NTTBarrettContext, finite_field.BarrettContext),

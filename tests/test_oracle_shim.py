@@ -50,11 +50,18 @@ def _oracle(name, kind, p, moduli):
         key = K.gen_evaluation_key(sk, moduli[:p["limbs"]], moduli[p["limbs"]:], a, e, dnum=p["dnum"])
         return np.array(key["b"], np.uint64)
     ins = S.inputs(name, kind, p, moduli)
-    x = ins["x"]
+    x = ins.get("x")
     if kind == "ntt":
         if p["reduction"] == "barrett":
             return O.NTTBarrett(moduli, p["r"], p["c"]).ntt(x)
         return V.NTTVariant(moduli, p["r"], p["c"], p["reduction"]).ntt(x)
+    if kind == "ff":
+        red = p["reduction"]
+        if red == "barrett":
+            return O.Barrett(moduli).reduce(ins["z"])
+        if red == "shoup":
+            return V.Shoup(moduli).reduce(ins["z"], ins["z_s"])
+        return {"montgomery": V.Montgomery, "bat_lazy": V.BATLazy}[red](moduli).reduce(ins["z"])
     if kind == "ntt_sm":
         # one modulus: the multi-modulus transform with M = 1 (Shoup on one matrix)
         red, r, c = p["reduction"], p["r"], p["c"]
