@@ -10,7 +10,11 @@ algorithms; every function cites the file:line of
 EfficientPPML/CROSS/jaxite_word it follows.  It is pinned against the
 reference's own golden vectors (OpenFHE-produced, embedded in the reference
 test files) that ``tests/golden/make_golden.py`` extracts into
-``tests/golden/*.json``.
+``tests/golden/*.json``, and, at sizes those vectors do not reach (up to
+HE-Mult and HE-Rotate at N = 2^16, L = 24), against digests of the
+reference's own outputs on seeded inputs (``tests/golden/shim_digests.json``,
+recorded by ``tests/golden/make_golden_shim.py`` with the reference's code
+run on a numpy stand-in for jax).
 """
 
 from . import cross_oracle  # noqa: F401
