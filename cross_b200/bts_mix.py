@@ -175,7 +175,7 @@ class Case:
 
 class KernelMix:
     """The kernels of the schedule on the current CUDA device, through the
-    library's C ABI on device-resident operands in the reference's layouts.
+    library's C ABI on device-resident operands.
 
     moduli: the basis (at least 53 primes for the full schedule);
     batch: polynomials per call (latencies are reported per polynomial);
