@@ -398,6 +398,22 @@ def chunk_decomposition(x: int, chunkwidth: int = 8) -> np.ndarray:
     return np.array(out, dtype=dtype)
 
 
+def format_ciphertext_string(data, modulus) -> str:
+    """The inverse of parse_ciphertext_string (util.py:545-608): OpenFHE's
+    text form of a ciphertext, one ``Element k:`` group per element and one
+    ``i: EVAL: [...] modulus: q_i`` line per tower.  data: (elements,
+    towers, N) integers; modulus: one value per tower.  No counterpart in the
+    reference, which only reads the format."""
+    lines = []
+    for k, element in enumerate(data):
+        if len(element) != len(modulus):
+            raise ValueError(f"element {k} has {len(element)} towers for {len(modulus)} moduli")
+        for i, (tower, q) in enumerate(zip(element, modulus)):
+            body = f"{i}: EVAL: [{' '.join(str(int(v)) for v in tower)}] modulus: {int(q)}"
+            lines.append(f"Element {k}: {body}" if i == 0 else body)
+    return "\n".join(lines) + "\n"
+
+
 def parse_ciphertext_string(input_str: str):
     """util.py:545-608: OpenFHE text format -> (data, moduli)."""
     import re

@@ -122,3 +122,22 @@ def test_chunk_decomposition():
     d4 = util.chunk_decomposition(0xAB, 4)
     assert d4.dtype == np.uint8 and d4.tolist() == [0xB, 0xA]
     assert util.chunk_decomposition(0).size == 0
+
+
+def test_openfhe_text_round_trip():
+    """format_ciphertext_string writes what parse_ciphertext_string (util.py:
+    545-608) reads back, in the layout of the reference's test fixtures."""
+    import json
+    import os
+    rng = np.random.default_rng(5)
+    data = [[rng.integers(0, q, 16).tolist() for q in Q] for _ in range(2)]
+    text = util.format_ciphertext_string(data, Q)
+    assert text.startswith("Element 0: 0: EVAL: [") and "\nElement 1: 0: EVAL: [" in text
+    assert util.parse_ciphertext_string(text) == (data, list(Q))
+    # a fixture written by OpenFHE (rescale_test.py:19-45) survives parse -> format -> parse
+    with open(os.path.join(os.path.dirname(__file__), "golden", "rescale.json")) as f:
+        g = json.load(f)
+    d, m = util.parse_ciphertext_string(g["in_ciphertexts_str"])
+    assert util.parse_ciphertext_string(util.format_ciphertext_string(d, m)) == (d, m)
+    with pytest.raises(ValueError):
+        util.format_ciphertext_string([[[1, 2]]], Q)
