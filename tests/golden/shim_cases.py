@@ -56,6 +56,8 @@ CASES = [
     ("ff_bat_lazy_4096x6", "ff", dict(reduction="bat_lazy", rows=4096, limbs=6)),
     # the eight-GPU configuration: L = 35, K = 7, five key-switch digits
     ("hemul_256x256_l35_k7_dnum5", "hemul", dict(r=256, c=256, limbs=35, special=7, dnum=5, batch=1)),
+    ("rescale_256x256_l24", "rescale", dict(r=256, c=256, limbs=24, batch=1)),
+    ("herot_256x256_l35_k7_dnum5", "herot", dict(r=256, c=256, limbs=35, special=7, dnum=5, batch=1, rotation=7)),
 ]
 
 
