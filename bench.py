@@ -1,19 +1,30 @@
-"""Benchmark: CKKS HE-Mult with relinearisation at N = 2^16.
+"""Benchmark: CKKS HE-Mult (with its input rescale) and relinearisation at N = 2^16.
 
-Workload (one step): HEMul.mul over a batch of 64 ciphertexts with N = 2^16
-(256 x 256), L = 24 limbs of 28-bit NTT primes, K = 8 special limbs, dnum = 3;
-seeded uniform residues; evaluation keys seeded uniform.  Weak scaling: every
-rank processes its own batch of 64 (the reference shards the batch axis only).
+Workload (one step): HEMul.mul (hemul.py:153-217: rescale of the inputs,
+tensor product, hybrid key switch, ModDown) over the box-scale batch of 512
+ciphertexts with N = 2^16 (256 x 256), L = 35 limbs of 28-bit NTT primes,
+K = 7 special limbs, dnum = 5; seeded uniform residues; evaluation keys
+seeded uniform.  The 512 ciphertexts are split across the ranks (512 / N per
+GPU, strong scaling); ciphertexts are independent, so ranks exchange nothing
+on the data path (the reference shards the batch axis only, util.py:40-58).
+Each rank runs its share in calls of 64 ciphertexts.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Prints one JSON line on rank 0.  Other workloads of the same line format:
-  --workload herot              HE-Rotate at the same point (B, 2, r, c, L) -> (B, 2, N, L)
-  --limbs L --special K --dnum D  another HE-Mult / HE-Rotate point (35, 7, 5: the 8-GPU point)
+Prints one JSON line on rank 0.  On one GPU the line also carries the other
+configurations of the scope (key "configs"): the N = 2^12 NTT + INTT, the
+24 -> 25 limb BConv, HE-Mult and HE-Rotate at L = 24, K = 8, dnum = 3 with 64
+ciphertexts, each with its own roofline.  Other workloads of the same line
+format:
+  --workload herot              HE-Rotate (B, 2, r, c, L) -> (B, 2, N, L)
+  --limbs L --special K --dnum D --global-batch B
+                                another HE-Mult / HE-Rotate point (24, 8, 3, 64: one GPU's
+                                L = 24 benchmark point)
   --workload ntt / bconv        the transform or the basis conversion alone for one reduction
                                 (--reduction barrett | montgomery | shoup | bat_lazy): NTT + INTT
                                 over --ntt-limbs limbs x --ntt-polys polys of N = --ntt-degree
                                 (default 2^16, 24, 16); BConv 24 -> 25 limbs, 32 polys of N = 2^16
+  --workload i8peak             the int8 tensor-core probe alone (burst and sustained)
   --workload ckks               a CKKS encode -> encrypt -> decrypt -> decode round trip
   --workload bts                the bootstrapping kernel mix: every (kernel, size) of a CKKS
                                 bootstrapping's schedule timed, latencies weighted by invocation
@@ -22,6 +33,7 @@ Prints one JSON line on rank 0.  Other workloads of the same line format:
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -29,30 +41,76 @@ import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_DEG, R, C, L, K, DNUM, BATCH = 65536, 256, 256, 24, 8, 3, 64
-# DRAM bytes (read + write) per k_bat_tc2 launch of the roofline NTT at batch 64,
-# from profiles/k_bat_tc2_ntt_n65536.md (batch-16 ncu capture scaled by 4).
-TRAFFIC_PER_LAUNCH = 3.148e9
-METRIC = "HE-Mult/s (N=2^16, L=24, dnum=3)"
-WORKLOAD = "CKKS HE-Mult + relinearisation, N=2^16 (256x256), L=24 x 28-bit, K=8, dnum=3, batch 64 per GPU"
+N_DEG, R, C = 65536, 256, 256
+# DRAM bytes (read + write) of one k_bat_tc2 launch of the roofline NTT per
+# limb-polynomial it processes: the ncu capture of profiles/k_bat_tc2_ntt_n65536.md
+# (3.148 GB per launch over 256 polys x 23 limbs; traffic grows with the
+# limb-polynomials processed).
+TRAFFIC_PER_LP = 3.148e9 / (256 * 23)
 
 
-def set_point(workload: str, limbs: int, special: int, dnum: int, batch: int) -> None:
-    """Select the HE operator point (module constants used by the helpers)."""
-    global L, K, DNUM, METRIC, WORKLOAD
-    L, K, DNUM = limbs, special, dnum
-    if workload == "herot":
-        METRIC = f"HE-Rotate/s (N=2^16, L={L}, dnum={DNUM})"
-        WORKLOAD = (f"CKKS HE-Rotate (hybrid key switch), N=2^16 (256x256), L={L} x 28-bit, K={K}, dnum={DNUM}, "
-                    f"batch {batch} per GPU")
-    else:
-        METRIC = f"HE-Mult/s (N=2^16, L={L}, dnum={DNUM})"
-        WORKLOAD = (f"CKKS HE-Mult + relinearisation, N=2^16 (256x256), L={L} x 28-bit, K={K}, dnum={DNUM}, "
-                    f"batch {batch} per GPU")
+@dataclass
+class Point:
+    """An HE operator configuration: operator, limbs, special limbs, digits,
+    ciphertexts per step over all ranks, ciphertexts per call."""
+    workload: str = "hemul"
+    L: int = 35
+    K: int = 7
+    dnum: int = 5
+    global_batch: int = 512
+    call_batch: int = 64
+
+    @property
+    def metric(self):
+        op = "HE-Rotate/s" if self.workload == "herot" else "HE-Mult/s"
+        return f"{op} (N=2^16, L={self.L}, K={self.K}, dnum={self.dnum})"
+
+    @property
+    def unit(self):
+        return "HE-Rot/s" if self.workload == "herot" else "HE-Mult/s"
+
+    def describe(self, per_gpu):
+        op = ("CKKS HE-Rotate (hybrid key switch)" if self.workload == "herot" else
+              "CKKS HE-Mult with input rescale + relinearisation")
+        return (f"{op}, N=2^16 (256x256), L={self.L} x 28-bit, K={self.K}, dnum={self.dnum}, "
+                f"{self.global_batch} ciphertexts per step ({per_gpu} per GPU, calls of {self.call_batch})")
+
+    def transforms_per_ct(self):
+        """Limb-transforms of one ciphertext (rescale, key switch, ModDown)."""
+        L, K, d = self.L, self.K, self.dnum
+        if self.workload == "herot":
+            alpha = -(-L // d)
+            parts = [min(alpha, L - j * alpha) for j in range(d)]
+            return L + sum(L + K - a for a in parts) + 2 * K + 2 * L
+        L1 = L - 1
+        alpha = -(-L1 // d)
+        parts = [min(alpha, L1 - j * alpha) for j in range(-(-L1 // alpha))]
+        return 4 + 4 * L1 + L1 + sum(L1 + K - a for a in parts) + 2 * K + 2 * L1
+
+    def int8_ops_per_ct(self):
+        """Algorithmic int8 operations of one ciphertext: 32 N (R + C) per
+        limb-transform plus 2 N (4 sq)(4 sp) per basis conversion."""
+        L, K, d, n = self.L, self.K, self.dnum, N_DEG
+        ops = self.transforms_per_ct() * 32.0 * n * (R + C)
+        if self.workload == "herot":
+            alpha = -(-L // d)
+            parts = [min(alpha, L - j * alpha) for j in range(d)]
+            bc = sum(a * (L + K - a) for a in parts) + 2 * K * L
+        else:
+            L1 = L - 1
+            alpha = -(-L1 // d)
+            parts = [min(alpha, L1 - j * alpha) for j in range(-(-L1 // alpha))]
+            bc = sum(a * (L1 + K - a) for a in parts) + 2 * K * L1
+        return ops + 2.0 * n * 16 * bc
+
+
+BOX = Point()
+L24 = Point(L=24, K=8, dnum=3, global_batch=64)
 
 
 def rotation_map(seed: int = 0):
@@ -64,23 +122,42 @@ def rotation_map(seed: int = 0):
     return k, util.precompute_auto_map(N_DEG, util.find_automorphism_index_2n_complex(k, 2 * N_DEG))
 
 
-def moduli():
+def moduli(pt):
     from cross_b200 import util
-    ov = util.find_moduli_ntt(L + K, 28, 2 * N_DEG)
-    return ov[:L], ov[L:]
+    ov = util.find_moduli_ntt(pt.L + pt.K, 28, 2 * N_DEG)
+    return ov[:pt.L], ov[pt.L:]
 
 
-def inputs(seed_ct: int, batch: int):
+def keys(pt):
+    """Seeded uniform evaluation keys (dnum, N, L + K)."""
     import numpy as np
-    Q, P = moduli()
-    rng = np.random.default_rng(seed_ct)
-    q = np.array(Q, np.uint64)
-    ct = (rng.integers(0, 2 ** 62, size=(batch, 4, R, C, L), dtype=np.uint64) % q).astype(np.uint32)
+    Q, P = moduli(pt)
     krng = np.random.default_rng(1)
     ov = np.array(Q + P, np.uint64)
-    ea = (krng.integers(0, 2 ** 62, size=(DNUM, N_DEG, L + K), dtype=np.uint64) % ov).astype(np.uint32)
-    eb = (krng.integers(0, 2 ** 62, size=(DNUM, N_DEG, L + K), dtype=np.uint64) % ov).astype(np.uint32)
-    return ct, ea, eb
+    ea = (krng.integers(0, 2 ** 62, size=(pt.dnum, N_DEG, pt.L + pt.K), dtype=np.uint64) % ov).astype(np.uint32)
+    eb = (krng.integers(0, 2 ** 62, size=(pt.dnum, N_DEG, pt.L + pt.K), dtype=np.uint64) % ov).astype(np.uint32)
+    return ea, eb
+
+
+def device_residues(torch, shape, mods, seed, dev, axis=-1):
+    """Seeded uniform residues below mods[i] along `axis`, drawn on the device."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    view = [1] * len(shape)
+    view[axis] = len(mods)
+    q = torch.tensor(mods, dtype=torch.int64, device=dev).reshape(view)
+    out = torch.empty(shape, dtype=torch.int32, device=dev)
+    flat = out.view(shape[0], -1)
+    for i in range(shape[0]):           # one leading slice at a time bounds the int64 temporary
+        x = torch.randint(0, 2 ** 62, (1, *shape[1:]), generator=g, device=dev, dtype=torch.int64)
+        flat[i] = (x % q).to(torch.int32).reshape(-1)
+    return out.view(torch.uint32)
+
+
+def host_residues(shape, mods, seed):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    return (rng.integers(0, 2 ** 62, size=shape, dtype=np.uint64) % np.array(mods, np.uint64)).astype(np.uint32)
 
 
 class ClockSampler:
@@ -137,6 +214,7 @@ class ClockSampler:
                 "power_w_max": max(pw) if pw else None, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -147,38 +225,108 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-def _oracle_op(workload: str):
+_I8 = {}
+
+
+def i8_probe(torch, dev, sustained_s=3.0, kchunks=8192):
+    """The int8 tensor-core peak of this GPU, measured: cross_tc_i8_probe
+    launches on every SM, operands resident in shared memory, timed with CUDA
+    events on the launching stream.  burst = best of five launches after
+    warm-up (the denominator for a kernel timed alone); sustained = launches
+    back to back for `sustained_s` seconds (for kernels timed inside a long
+    step).  pair = the two-SM cta_group::2 form of the NTT contraction."""
+    key = (str(dev), sustained_s)
+    if key in _I8:
+        return _I8[key]
+    from cross_b200 import _lib
+    lib = _lib.lib()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ctas = ctypes.c_int(0)
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def go(pair):
+        _lib.check(lib.cross_tc_i8_probe(pair, kchunks, ctypes.c_void_p(err.data_ptr()), ctypes.byref(ctas),
+                                         ctypes.c_void_p(st.cuda_stream)), "cross_tc_i8_probe")
+
+    res = {}
+    for pair in (1, 0):
+        for _ in range(3):
+            go(pair)
+        torch.cuda.synchronize(dev)
+        best = float("inf")
+        for _ in range(5):
+            e0.record(st)
+            go(pair)
+            e1.record(st)
+            torch.cuda.synchronize(dev)
+            best = min(best, e0.elapsed_time(e1))
+        ops = ctas.value * kchunks * 2.0 * 128 * 256 * 128
+        res[pair] = (ops / (best * 1e-3) / 1e12, best, ops)
+    reps = max(3, int(sustained_s * 1e3 / res[1][1]))
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        torch.cuda.synchronize(dev)
+        h0 = time.time()
+        e0.record(st)
+        for _ in range(reps):
+            go(1)
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+        h1 = time.time()
+    sustained = reps * res[1][2] / (e0.elapsed_time(e1) * 1e-3) / 1e12
+    if int(err.item()) != 0:
+        raise TimeoutError(f"cross_tc_i8_probe: a bounded wait expired (code {int(err.item())})")
+    out = {"burst_tops": res[1][0], "sustained_tops": sustained, "burst_tops_1sm": res[0][0],
+           "ms_per_launch": res[1][1], "kchunks": kchunks, "sustained_launches": reps,
+           "sustained_seconds": e0.elapsed_time(e1) / 1e3, "clocks_sustained": clk.summary(h0, h1),
+           "how": "cross_tc_i8_probe: tcgen05.mma kind::i8 M=256 N=256 K=32 (cta_group::2) on shared-memory "
+                  "operands on every SM, CUDA events; burst = best of 5 launches, sustained = back to back"}
+    _I8[key] = out
+    return out
+
+
+def int8_peak(torch, dev, sustained=False):
+    """(TOPS, source) of the int8 roofline denominator: the probe measured in
+    this process (burst for a kernel timed alone, sustained for a long step)."""
+    p = i8_probe(torch, dev)
+    v = p["sustained_tops"] if sustained else p["burst_tops"]
+    return v, (f"int8 tensor-core peak measured in this run ({'sustained' if sustained else 'burst'}): "
+               f"{p['how']}")
+
+
+def _oracle_op(pt):
     """The oracle's operator for one ciphertext of the workload and its input."""
     from oracle import cross_oracle as O
-    Q, P = moduli()
-    ct, ea, eb = inputs(0, 1)
-    if workload == "herot":
-        op = O.HERot(R, C, DNUM, Q, P)
+    Q, P = moduli(pt)
+    ea, eb = keys(pt)
+    ct = host_residues((1, 4 if pt.workload == "hemul" else 2, R, C, pt.L), Q, seed=0)
+    if pt.workload == "herot":
+        op = O.HERot(R, C, pt.dnum, Q, P)
         op.control_gen(1)
-        op.setup_rotate(ea.reshape(DNUM, R, C, -1), eb.reshape(DNUM, R, C, -1), rotation_map()[1])
-        return op.rotate, ct[:, :2], "HE-Rot/s", "HERot.rotate"
-    he = O.HEMul(1, R, C, DNUM, 1, Q, P)
+        op.setup_rotate(ea.reshape(pt.dnum, R, C, -1), eb.reshape(pt.dnum, R, C, -1), rotation_map()[1])
+        return op.rotate, ct, "HERot.rotate"
+    he = O.HEMul(1, R, C, pt.dnum, 1, Q, P)
     he.setup_relinearization(ea, eb)
-    return he.mul, ct, "HE-Mult/s", "HEMul.mul"
+    return he.mul, ct, "HEMul.mul"
 
 
-def cpu_baseline(steps: int = 1, workload: str = "hemul"):
+def cpu_baseline(pt, steps=2):
     """The oracle (numpy restatement of jaxite_word) on the host cores: one
-    ciphertext per step."""
-    fn, ct, unit, name = _oracle_op(workload)
+    ciphertext per step, the median of `steps`."""
+    fn, ct, name = _oracle_op(pt)
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
         fn(ct)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    return {"value": 1.0 / t, "unit": unit, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{steps} x 1 ciphertext of the workload (oracle/cross_oracle.py {name}, numpy BLAS threads)",
-            "seconds_per_ct": t}
+    return {"value": 1.0 / t, "unit": pt.unit, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} x 1 ciphertext of the workload (oracle/cross_oracle.py {name}, numpy BLAS threads; "
+                      f"median {t:.2f} s per ciphertext)"}
 
 
-def run_reference(args):
-    """--impl reference: the oracle port of jaxite_word's HEMul.mul on the host
+def run_reference(args, pt):
+    """--impl reference: the oracle port of jaxite_word's operator on the host
     cores (all BLAS threads), W warm-up and K timed steps of one ciphertext."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -199,7 +347,7 @@ def run_reference(args):
                           "e2e": {"value": total, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
               flush=True)
         return
-    fn, ct, unit, name = _oracle_op(args.workload)
+    fn, ct, name = _oracle_op(pt)
     for _ in range(args.warmup):
         fn(ct)
     t0 = time.perf_counter()
@@ -208,14 +356,15 @@ def run_reference(args):
     dt = (time.perf_counter() - t0) / max(args.steps, 1)
     v = 1.0 / dt
     sample = f"1 ciphertext of the workload per step (oracle/cross_oracle.py {name}, numpy BLAS threads)"
-    print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": unit, "n_gpus": args.gpus,
+    print(json.dumps({"impl": "reference", "metric": pt.metric, "value": v, "unit": pt.unit, "n_gpus": args.gpus,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt,
-                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                       "dtype": "u32 residues, u64 intermediates, u8 BAT contractions", "data": "synthetic seeded",
-                      "config": {"workload": WORKLOAD, "sample": "1 ciphertext per step"},
-                      "cpu_baseline": {"value": v, "unit": unit, "cores": os.cpu_count(), "kind": "port",
+                      "config": {"workload": pt.describe(pt.global_batch // max(args.gpus, 1)),
+                                 "sample": "1 ciphertext per step"},
+                      "cpu_baseline": {"value": v, "unit": pt.unit, "cores": os.cpu_count(), "kind": "port",
                                        "sample": sample},
-                      "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                      "e2e": {"value": v, "unit": pt.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
           flush=True)
 
 
@@ -241,10 +390,11 @@ class _Timer:
         return shard.max_over_ranks(e0.elapsed_time(e1), device=self.dev)
 
 
-def run_component(args, torch, dist, world, rank, local):
+def measure_component(workload, torch, dist, world, rank, local, steps, warmup, reduction="barrett",
+                      ntt_limbs=24, ntt_polys=16, ntt_degree=N_DEG, cpu=True, e2e=True):
     """--workload ntt | bconv for one reduction: device throughput, end-to-end
     throughput through the operator API with host buffers, the kernel's
-    roofline and the oracle on the host cores."""
+    roofline and the oracle on the host cores.  Returns the JSON line."""
     import numpy as np
     from cross_b200 import _lib, bconv, ntt_mm, util
     from oracle import cross_oracle as O
@@ -252,11 +402,11 @@ def run_component(args, torch, dist, world, rank, local):
     dev = torch.device("cuda", local)
     timer = _Timer(torch, dist, dev)
     lib = _lib.lib()
-    red = args.reduction
+    red = reduction
     pk, src = peaks()
     rng = np.random.default_rng(200 + rank)
-    if args.workload == "ntt":
-        Lw, B, nd = args.ntt_limbs, args.ntt_polys, args.ntt_degree
+    if workload == "ntt":
+        Lw, B, nd = ntt_limbs, ntt_polys, ntt_degree
         rr, cc = util.default_rc(nd)
         q = O.find_moduli_ntt(Lw, 28, 2 * nd)
         cls = {"barrett": ntt_mm.NTTCiphertextBarrettContext, "montgomery": ntt_mm.NTTCiphertextMontgomeryContext,
@@ -276,7 +426,7 @@ def run_component(args, torch, dist, world, rank, local):
                                          ws.data_ptr(), ws.numel(), cs), "cross_ntt")
         units = 2 * B * Lw                                   # limb-transforms per step
         metric, unit = f"NTT+INTT limb-transforms/s (N={nd}, {red})", "limb-transform/s"
-        workload = f"BAT NTT then INTT, {red} reduction, N={nd} ({rr}x{cc}), {Lw} limbs x {B} polys per GPU"
+        wl = f"BAT NTT then INTT, {red} reduction, N={nd} ({rr}x{cc}), {Lw} limbs x {B} polys per GPU"
         hin = torch.from_numpy(np.ascontiguousarray(xh.transpose(0, 2, 3, 1))).pin_memory()   # (B, R, C, L)
 
         def e2e_step():
@@ -299,9 +449,12 @@ def run_component(args, torch, dist, world, rank, local):
                     "peak_source": "nominal 148 SMs x 128 int32 lanes x 1965 MHz (no measured figure on this pool)"}
         else:
             ops = units * 32.0 * nd * (rr + cc)
-            roof = {"bound": "tensor", "unit": "TOPS (int8)", "peak": 2.0 * pk["bf16_tflops"],
-                    "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src})"}
-        roof["kernel"] = "all launches of one NTT + INTT (2 contraction stages each)"
+            # HBM bound as well: 8 N bytes per limb-transform (read + write)
+            hbm_s = units * 8.0 * nd / (pk["hbm_gbs"] * 1e9)
+            pv, ps = int8_peak(torch, dev)
+            roof = {"bound": "tensor", "unit": "TOPS (int8)", "peak": pv, "peak_source": ps,
+                    "hbm_bound_ms_per_step": 1e3 * hbm_s, "hbm_peak_source": f"hbm_gbs of MEASURED_PEAKS.json ({src})"}
+        roof["kernel"] = "all launches of one NTT + INTT"
     else:
         sq, sp, B = 24, 25, 32
         ov = O.find_moduli_ntt(sq + sp, 28, 2 * N_DEG)
@@ -322,7 +475,8 @@ def run_component(args, torch, dist, world, rank, local):
                                           _lib.LAYOUT_LIMB_MAJOR, cs), "cross_bconv_ex")
         units = B
         metric, unit = f"BConv polys/s (N=2^16, 24->25 limbs, {red})", "poly/s"
-        workload = f"basis conversion {'basis_change_bat' if bat else 'basis_change'}, {red}, 24 -> 25 limbs, N=2^16, 32 polys per GPU"
+        wl = (f"basis conversion {'basis_change_bat' if bat else 'basis_change'}, {red}, 24 -> 25 limbs, "
+              f"N=2^16, 32 polys per GPU")
         hin = torch.from_numpy(np.ascontiguousarray(xh.transpose(0, 2, 1))).pin_memory()      # (B, N, sq)
 
         def e2e_step():
@@ -341,36 +495,54 @@ def run_component(args, torch, dist, world, rank, local):
         roof = {"bound": "hbm", "unit": "GB/s", "peak": pk["hbm_gbs"],
                 "peak_source": f"hbm_gbs of MEASURED_PEAKS.json ({src})",
                 "kernel": "k_bconv_tc (Barrett) / k_bconv_var (variants), one launch per step"}
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
-    ms = timer(step, args.steps)
+    ms = timer(step, steps)
     l0 = lib.cross_launch_count()
     step()
     torch.cuda.synchronize()
-    launches = (lib.cross_launch_count() - l0) * args.steps
-    value = world * units * args.steps / (ms / 1000.0)
-    e2e_step()
-    ems = timer(e2e_step, args.steps)
-    e2e = world * units * args.steps / (ems / 1000.0)
-    per = ms / args.steps / 1000.0
+    launches = (lib.cross_launch_count() - l0) * steps
+    value = world * units * steps / (ms / 1000.0)
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u32 residues, u64 intermediates",
+            "data": "synthetic seeded uniform residues", "config": {"workload": wl, "reduction": red,
+                                                                    "l2": "inputs larger than L2"},
+            "gpu_launches": int(launches)}
+    if e2e:
+        e2e_step()
+        ems = timer(e2e_step, steps)
+        line["e2e"] = {"value": world * units * steps / (ems / 1000.0), "unit": unit,
+                       "h2d_bytes_per_step": int(hin.numel() * 4),
+                       "d2h_bytes_per_step": int(y.numel() * y.element_size())}
+    per = ms / steps / 1000.0
     achieved = ops / per / (1e12 if roof["unit"] != "GB/s" else 1e9)
     roof.update({"achieved": achieved, "frac": achieved / roof["peak"], "traffic": None,
-                 "ms_per_step": ms / args.steps})
-    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "u32 residues, u64 intermediates",
-            "data": "synthetic seeded uniform residues", "config": {"workload": workload, "reduction": red,
-                                                                    "l2": "inputs larger than L2"},
-            "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": int(hin.numel() * 4),
-                    "d2h_bytes_per_step": int(y.numel() * y.element_size())},
-            "gpu_launches": int(launches), "roofline": roof}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                 "ms_per_step": ms / steps})
+    if "hbm_bound_ms_per_step" in roof:
+        roof["frac_of_hbm_bound"] = roof["hbm_bound_ms_per_step"] / (ms / steps)
+    line["roofline"] = roof
+    if cpu and rank == 0 and world == 1:
         dt = cpu_once()
         line["cpu_baseline"] = {"value": cpu_units / dt, "unit": unit, "cores": os.cpu_count(), "kind": "port",
                                 "sample": f"{cpu_units} units of the workload (oracle, numpy BLAS threads)"}
+    return line
+
+
+def run_component(args, torch, dist, world, rank, local):
+    line = measure_component(args.workload, torch, dist, world, rank, local, args.steps, args.warmup,
+                             args.reduction, args.ntt_limbs, args.ntt_polys, args.ntt_degree,
+                             cpu=not args.no_cpu_baseline)
     if rank == 0:
         print(json.dumps(line), flush=True)
 
+
+def run_i8peak(args, torch, dist, world, rank, local):
+    dev = torch.device("cuda", local)
+    p = i8_probe(torch, dev, sustained_s=4.0)
+    if rank == 0:
+        print(json.dumps({"metric": "int8 tensor-core peak (TOPS)", "value": p["burst_tops"], "unit": "TOPS",
+                          "n_gpus": world, "higher_is_better": True, "probe": p}), flush=True)
 
 # Algorithmic work per polynomial of each kernel of the bootstrapping mix:
 # HBM bytes for the element-wise kernels and the permutation, int8 tensor
@@ -500,13 +672,13 @@ def run_bts(args, torch, dist, world, rank, local):
                                  "frac": a / pk["hbm_gbs"], "share_pct": summ["ratios_pct"].get(kernel)}
         else:
             a = work / (t_us * 1e-6) / 1e12
+            i8, _ = int8_peak(torch, dev)
             by_kernel[kernel] = {"bound": "tensor", "achieved": a, "unit": "TOPS (int8)",
-                                 "peak": 2.0 * pk["bf16_tflops"], "frac": a / (2.0 * pk["bf16_tflops"]),
-                                 "share_pct": summ["ratios_pct"].get(kernel)}
+                                 "peak": i8, "frac": a / i8, "share_pct": summ["ratios_pct"].get(kernel)}
     top = max(summ["ratios_pct"], key=summ["ratios_pct"].get)
     roof = dict(by_kernel[top])
     roof.update({"kernel": f"{top} rows of the schedule (count-weighted)", "traffic": None,
-                 "peak_source": f"MEASURED_PEAKS.json ({src}); int8 = 2 x bf16_tflops"})
+                 "peak_source": f"hbm_gbs of MEASURED_PEAKS.json ({src}); {int8_peak(torch, dev)[1]}"})
     line = {"metric": "CKKS bootstrapping kernel-mix latency (us per polynomial, N=2^16)", "value": value,
             "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": value / 1000.0, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
@@ -578,7 +750,7 @@ def run_ckks(args, torch, dist, world, rank, local):
     # forward / inverse negacyclic transforms per step: encode 1, encrypt 3 (v, e0, e1), decrypt 1
     transforms = 5 * towers
     ops = transforms * 32.0 * deg * (R + C)
-    pk, src = peaks()
+    i8, i8_src = int8_peak(torch, dev)
     achieved = ops / (ms / args.steps / 1000.0) / 1e12
     line = {"metric": "CKKS encode+encrypt+decrypt+decode round trips/s (N=2^16, 24 towers)", "value": value,
             "unit": "round-trip/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -591,9 +763,8 @@ def run_ckks(args, torch, dist, world, rank, local):
             "gpu_launches": int(launches),
             "roofline": {"bound": "latency (launch- and host-bound chain of small kernels)",
                          "kernel": "the 5 x 24 negacyclic transforms of a step on the tensor cores",
-                         "achieved": achieved, "peak": 2.0 * pk["bf16_tflops"], "unit": "TOPS (int8)",
-                         "frac": achieved / (2.0 * pk["bf16_tflops"]), "traffic": None,
-                         "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src})"}}
+                         "achieved": achieved, "peak": i8, "unit": "TOPS (int8)",
+                         "frac": achieved / i8, "traffic": None, "peak_source": i8_src}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import ckks as K
         from oracle import cross_oracle as O
@@ -621,6 +792,206 @@ def run_ckks(args, torch, dist, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+
+def measure_he(pt, torch, dist, world, rank, local, steps, warmup, e2e=True, cpu=True, roofline=True):
+    """One HE operator point: each rank runs its share of pt.global_batch
+    ciphertexts (inputs resident in HBM) in calls of pt.call_batch; CUDA events
+    around the timed steps, max over ranks.  Returns the JSON line."""
+    from cross_b200 import _lib, hemul, herot, ntt_mm, shard
+    dev = torch.device("cuda", local)
+    lib = _lib.lib()
+    lo, hi = shard.shard_bounds(pt.global_batch, world, rank)
+    nb = hi - lo
+    cb = max(1, min(pt.call_batch, nb))
+    Q, P = moduli(pt)
+    ea, eb = keys(pt)
+    if pt.workload == "herot":
+        he = herot.HERot(R, C, pt.dnum, Q, P)
+        he.control_gen(batch=cb, degree_layout=(R, C))
+        he.setup_rotate(ea, eb, rotation_map()[1])
+        E, op, out_shape, tag = 2, he.rotate, (nb, 2, N_DEG, pt.L), "herot"
+    else:
+        he = hemul.HEMul(cb, R, C, pt.dnum, 1, Q, P)
+        he.control_gen(degree_layout=(R, C))
+        he.setup_relinearization(ea, eb)
+        E, op, out_shape, tag = 4, he.mul, (nb, 2, R, C, pt.L - 1), "hemul"
+    del ea, eb
+    x = device_residues(torch, (nb, E, R, C, pt.L), Q, 100 + lo, dev)
+    out = torch.empty(out_shape, dtype=torch.uint32, device=dev)
+    ws = torch.empty(he.workspace_size(cb), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        torch.cuda.nvtx.range_push(tag)
+        for a in range(0, nb, cb):
+            b = min(nb, a + cb)
+            op(x[a:b], out=out[a:b], workspace=ws)
+        torch.cuda.nvtx.range_pop()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        l0 = lib.cross_launch_count()
+        h0 = time.time()
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        h1 = time.time()
+        launches = lib.cross_launch_count() - l0
+    ms = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
+    he.check_device()
+    value = pt.global_batch * steps / (ms / 1000.0)
+    sus, sus_src = int8_peak(torch, dev, sustained=True)
+    ops_ct = pt.int8_ops_per_ct()
+    per_gpu = value / world
+    line = {
+        "metric": pt.metric, "value": value, "unit": pt.unit, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u32 residues, u64 intermediates, u8 BAT contractions",
+        "data": "synthetic seeded uniform residues (no dataset in the reference)",
+        "config": {"workload": pt.describe(nb), "global_batch": pt.global_batch, "batch_per_gpu": nb,
+                   "call_batch": cb, "N": N_DEG, "r": R, "c": C, "L": pt.L, "K": pt.K, "dnum": pt.dnum,
+                   "parallelism": f"batch-sharded x{world} (ciphertexts independent, no data-path collective)",
+                   "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB per GPU, larger than L2 (no flush needed)"},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(h0, h1),
+        "operator_roofline": {"bound": "tensor", "unit": "TOPS (int8)", "int8_ops_per_ct": ops_ct,
+                              "limb_transforms_per_ct": pt.transforms_per_ct(),
+                              "achieved": per_gpu * ops_ct / 1e12, "peak": sus,
+                              "frac": per_gpu * ops_ct / 1e12 / sus, "peak_source": sus_src,
+                              "roofline_ct_per_s_per_gpu": sus * 1e12 / ops_ct},
+    }
+    if e2e:
+        # through the public API with pinned host buffers: the operator on CPU
+        # tensors copies every input word in and every output word out inside
+        # the timed region (chunks of 4 ciphertexts, copies overlapped with compute)
+        hin = torch.empty(x.shape, dtype=torch.uint32, pin_memory=True)
+        hin.copy_(x)
+        hout = torch.empty(out.shape, dtype=torch.uint32, pin_memory=True)
+        del x, out, ws
+        torch.cuda.empty_cache()
+
+        def e2e_step():
+            torch.cuda.nvtx.range_push("e2e")
+            op(hin, out=hout)
+            torch.cuda.nvtx.range_pop()
+
+        e2e_step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0.record(stream)
+        for _ in range(steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
+        line["e2e"] = {"value": pt.global_batch * steps / (ems / 1000.0), "unit": pt.unit,
+                       "h2d_bytes_per_step": int(hin.numel() * 4), "d2h_bytes_per_step": int(hout.numel() * 4)}
+        del hin, hout
+    else:
+        del x, out, ws
+    torch.cuda.empty_cache()
+    if roofline:
+        line["roofline"] = ntt_roofline(torch, dev, lib, Q[:pt.L - 1])
+    if cpu and rank == 0 and world == 1:
+        try:
+            line["cpu_baseline"] = cpu_baseline(pt)
+        except Exception as exc:  # noqa: BLE001
+            line["cpu_baseline"] = {"error": str(exc)}
+    del he
+    torch.cuda.empty_cache()
+    return line
+
+
+def ntt_roofline(torch, dev, lib, mods, polys=256):
+    """The dominant kernel, the two-SM tensor-core BAT contraction k_bat_tc2:
+    one forward NTT of `polys` x len(mods) limb-polynomials in the kernels'
+    native coefficient order is exactly two launches (the column stage with its
+    twiddle epilogue, the row stage), timed alone with CUDA events on the
+    launching stream; inputs are residues below each limb's modulus."""
+    from cross_b200 import _lib, ntt_mm
+    stream = torch.cuda.current_stream()
+    M = len(mods)
+    ctx = ntt_mm.NTTCiphertextBarrettContext(list(mods), {"r": R, "c": C})
+    xin = device_residues(torch, (polys, M, R, C), list(mods), 17, dev, axis=1)
+    xo = torch.empty_like(xin)
+    nws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), polys, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED),
+                      dtype=torch.uint8, device=dev)
+
+    def ntt_once():
+        # NVTX range "roofline": profilers select these launches with
+        # --nvtx --nvtx-include "roofline/"
+        torch.cuda.nvtx.range_push("roofline")
+        _lib.check(lib.cross_ntt(ctx.plan(), 0, xin.data_ptr(), xo.data_ptr(), polys,
+                                 _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED, nws.data_ptr(), nws.numel(),
+                                 stream.cuda_stream), "cross_ntt")
+        torch.cuda.nvtx.range_pop()
+
+    for _ in range(2):
+        ntt_once()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record(stream)
+    for _ in range(reps):
+        ntt_once()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ntt_ms = e0.elapsed_time(e1) / reps
+    ctx.check_device()
+    l0 = lib.cross_launch_count()
+    ntt_once()
+    torch.cuda.synchronize()
+    launches = lib.cross_launch_count() - l0              # 2: column + row contraction
+    lps = polys * M
+    ops = lps * 32.0 * N_DEG * (R + C)                    # int8 MAC x2 per limb-transform
+    peak, src = int8_peak(torch, dev)
+    achieved = ops / (ntt_ms / 1000.0) / 1e12
+    del xin, xo, nws, ctx
+    return {"kernel": f"k_bat_tc2 tensor-core BAT contraction (NTT column + row stage launches), {M} limbs x "
+                      f"{polys} polys, N=2^16",
+            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS (int8)", "frac": achieved / peak,
+            "traffic": TRAFFIC_PER_LP * lps, "traffic_unit": "bytes per launch (ncu dram read + write, scaled by "
+                                                             "limb-polynomials from the profiled launch)",
+            "peak_source": src, "launches": launches, "ms_per_launch": ntt_ms / max(launches, 1),
+            "algorithmic_ops_per_launch": ops / max(launches, 1)}
+
+
+def _summary(line):
+    keep = ("metric", "value", "unit", "ms_per_step", "gpu_launches")
+    s = {k: line[k] for k in keep if k in line}
+    s["workload"] = line["config"]["workload"]
+    for k in ("roofline", "operator_roofline"):
+        if k in line:
+            s[k] = {kk: line[k][kk] for kk in ("bound", "achieved", "peak", "unit", "frac", "frac_of_hbm_bound",
+                                               "hbm_bound_ms_per_step") if kk in line[k]}
+    return s
+
+
+def other_configs(torch, local, steps=10, warmup=3):
+    """The scope's other configurations on this GPU (device-resident inputs)."""
+    out = {}
+    c = measure_component("ntt", torch, None, 1, 0, local, steps, warmup, ntt_limbs=8, ntt_polys=16,
+                          ntt_degree=4096, cpu=False, e2e=False)
+    out["1_ntt_intt_n4096_64x64_8limbs_16polys"] = _summary(c)
+    c = measure_component("bconv", torch, None, 1, 0, local, steps, warmup, cpu=False, e2e=False)
+    out["2_bconv_modup_n65536_24to25_32polys"] = _summary(c)
+    c = measure_he(L24, torch, None, 1, 0, local, steps, warmup, e2e=False, cpu=False, roofline=False)
+    out["3_hemul_n65536_l24_k8_dnum3_64ct"] = _summary(c)
+    c = measure_he(Point("herot", 24, 8, 3, 64, 64), torch, None, 1, 0, local, steps, warmup, e2e=False, cpu=False,
+                   roofline=False)
+    out["4_herot_n65536_l24_k8_dnum3_64ct"] = _summary(c)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -628,24 +999,26 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling runs use a small case)")
-    ap.add_argument("--workload", choices=["hemul", "herot", "ntt", "bconv", "ckks", "bts"], default="hemul")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other configurations on one GPU")
+    ap.add_argument("--workload", choices=["hemul", "herot", "ntt", "bconv", "ckks", "bts", "i8peak"], default="hemul")
+    ap.add_argument("--limbs", type=int, default=BOX.L, help="L of the HE-Mult / HE-Rotate point")
+    ap.add_argument("--special", type=int, default=BOX.K, help="K of the HE-Mult / HE-Rotate point")
+    ap.add_argument("--dnum", type=int, default=BOX.dnum, help="key-switch digits of the HE-Mult / HE-Rotate point")
+    ap.add_argument("--global-batch", type=int, default=BOX.global_batch, help="ciphertexts per step over all GPUs")
+    ap.add_argument("--call-batch", type=int, default=BOX.call_batch, help="ciphertexts per operator call")
     ap.add_argument("--bts-batch", type=int, default=1, help="polynomials per call of the bootstrapping mix")
     ap.add_argument("--bts-log", default=None, help="write the mix's latency lines (tabIX.py format) here")
     ap.add_argument("--bts-layout", choices=["native", "reference"], default="native")
     ap.add_argument("--reduction", choices=["barrett", "montgomery", "shoup", "bat_lazy"], default="barrett")
-    ap.add_argument("--limbs", type=int, default=L, help="L of the HE-Mult / HE-Rotate point")
-    ap.add_argument("--special", type=int, default=K, help="K of the HE-Mult / HE-Rotate point")
-    ap.add_argument("--dnum", type=int, default=DNUM, help="key-switch digits of the HE-Mult / HE-Rotate point")
     ap.add_argument("--ntt-degree", type=int, default=N_DEG)
     ap.add_argument("--ntt-limbs", type=int, default=24)
     ap.add_argument("--ntt-polys", type=int, default=16)
     args = ap.parse_args()
-    set_point(args.workload, args.limbs, args.special, args.dnum, args.batch)
+    pt = Point("herot" if args.workload == "herot" else "hemul", args.limbs, args.special, args.dnum,
+               args.global_batch, args.call_batch)
     if args.impl == "reference":
-        return run_reference(args)
+        return run_reference(args, pt)
 
-    import numpy as np
     import torch
     from cross_b200 import shard
     world, rank, local = shard.rank_env()
@@ -654,161 +1027,20 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
     if args.workload not in ("hemul", "herot"):
-        {"ckks": run_ckks, "bts": run_bts}.get(args.workload, run_component)(args, torch, dist, world, rank, local)
-        if dist:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-
-    from cross_b200 import _lib, hemul, herot, ntt_mm
-    batch = args.batch
-    Q, P = moduli()
-    ct, ea, eb = inputs(100 + rank, batch)
-    dev = torch.device("cuda", local)
-    if args.workload == "herot":
-        he = herot.HERot(R, C, DNUM, Q, P)
-        he.control_gen(batch=batch, degree_layout=(R, C))
-        he.setup_rotate(ea, eb, rotation_map()[1])
-        ct = ct[:, :2].copy()
-        op, out_shape, unit, tag = he.rotate, (batch, 2, N_DEG, L), "HE-Rot/s", "herot"
+        {"ckks": run_ckks, "bts": run_bts, "i8peak": run_i8peak}.get(args.workload, run_component)(
+            args, torch, dist, world, rank, local)
     else:
-        he = hemul.HEMul(batch, R, C, DNUM, 1, Q, P)
-        he.control_gen(degree_layout=(R, C))
-        he.setup_relinearization(ea, eb)
-        op, out_shape, unit, tag = he.mul, (batch, 2, R, C, L - 1), "HE-Mult/s", "hemul"
-    x = torch.from_numpy(ct).to(dev)
-    out = torch.empty(out_shape, dtype=torch.uint32, device=dev)
-    ws = torch.empty(he.workspace_size(batch), dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream()
-
-    def step():
-        torch.cuda.nvtx.range_push(tag)
-        op(x, out=out, workspace=ws)
-        torch.cuda.nvtx.range_pop()
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    lib = _lib.lib()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
-        l0 = lib.cross_launch_count()
-        h0 = time.time()
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        h1 = time.time()
-        launches = lib.cross_launch_count() - l0
-    ms = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
-    value = world * batch * args.steps / (ms / 1000.0)
-
-    # e2e through the public API with pinned host buffers: HEMul.mul on CPU
-    # tensors copies every input word in and every output word out inside the
-    # timed region (in chunks of 4 ciphertexts, copies overlapped with compute).
-    hin = torch.from_numpy(ct).pin_memory()
-    hout = torch.empty(out.shape, dtype=torch.uint32).pin_memory()
-
-    def e2e_step():
-        torch.cuda.nvtx.range_push("e2e")
-        op(hin, out=hout)
-        torch.cuda.nvtx.range_pop()
-
-    e2e_step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ems = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
-    e2e = world * batch * args.steps / (ems / 1000.0)
-
-    # Dominant kernel: the tensor-core BAT contraction.  One forward NTT in the
-    # kernels' native coefficient order is exactly two contraction launches (the
-    # column stage with its twiddle epilogue, the row stage); timed alone over
-    # the polys x (L - 1) limb-polynomials of the input (for HE-Mult, those of
-    # its rescale NTT).
-    ctx = ntt_mm.NTTCiphertextBarrettContext(Q[:L - 1], {"r": R, "c": C})
-    lps = x.numel() // (L * N_DEG)
-    xin = x.reshape(-1)[: lps * (L - 1) * N_DEG].reshape(lps, L - 1, R, C)   # residues < q
-    xo = torch.empty_like(xin)
-    nws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), lps, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED),
-                      dtype=torch.uint8, device=dev)
-
-    def ntt_once():
-        # NVTX range "roofline": profilers select these launches with
-        # --nvtx --nvtx-include "roofline/"
-        torch.cuda.nvtx.range_push("roofline")
-        _lib.check(lib.cross_ntt(ctx.plan(), 0, xin.data_ptr(), xo.data_ptr(), lps, _lib.LAYOUT_LIMB_MAJOR_TRANSPOSED,
-                                 nws.data_ptr(), nws.numel(), stream.cuda_stream), "cross_ntt")
-        torch.cuda.nvtx.range_pop()
-
-    for _ in range(2):
-        ntt_once()
-    torch.cuda.synchronize()
-    reps = 3
-    e0.record(stream)
-    for _ in range(reps):
-        ntt_once()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ntt_ms = e0.elapsed_time(e1) / reps
-    # every tensor-core kernel of the timed work completed (no bounded wait expired)
-    he.check_device()
-    ctx.check_device()
-    l0 = lib.cross_launch_count()
-    ntt_once()
-    torch.cuda.synchronize()
-    ntt_launches = lib.cross_launch_count() - l0              # 2: column + row contraction
-    transforms = lps * (L - 1)
-    ops = transforms * 32.0 * N_DEG * (R + C)              # int8 MAC x2 per limb-transform
-    pk, src = peaks()
-    int8_peak = 2.0 * pk["bf16_tflops"]                     # TOPS: dense int8 = 2 x dense bf16 on B200
-    achieved = ops / (ntt_ms / 1000.0) / 1e12
-
-    line = {
-        "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u32 residues, u64 intermediates, u8 BAT contractions",
-        "data": "synthetic seeded uniform residues (no dataset in the reference)",
-        "config": {"workload": WORKLOAD, "global_batch": world * batch, "batch_per_gpu": batch, "N": N_DEG, "r": R, "c": C, "L": L, "K": K,
-                   "dnum": DNUM, "parallelism": f"batch-sharded x{world}",
-                   "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB per GPU, larger than L2 (no flush needed)"},
-        "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": int(hin.numel() * 4),
-                "d2h_bytes_per_step": int(hout.numel() * 4)},
-        "gpu_launches": int(launches),
-        "clocks": clk.summary(h0, h1),
-        "roofline": {"kernel": "k_bat_tc2 tensor-core BAT contraction (NTT column + row stage launches), "
-                               f"{L - 1} limbs x {lps} polys, N=2^16",
-                     "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
-                     "frac": achieved / int8_peak,
-                     # the captured launch processed 256 x 23 limb-polynomials; traffic scales with them
-                     "traffic": TRAFFIC_PER_LAUNCH * transforms / (256 * 23),
-                     "traffic_unit": "bytes per launch (ncu dram read + write)",
-                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); no int8 measurement on this pool",
-                     "launches": ntt_launches, "ms_per_launch": ntt_ms / max(ntt_launches, 1),
-                     "algorithmic_ops_per_launch": ops / max(ntt_launches, 1)},
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            line["cpu_baseline"] = {k: v for k, v in cpu_baseline(1, args.workload).items() if k != "seconds_per_ct"}
-        except Exception as exc:  # noqa: BLE001
-            line["cpu_baseline"] = {"error": str(exc)}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+        line = measure_he(pt, torch, dist, world, rank, local, args.steps, args.warmup,
+                          cpu=not args.no_cpu_baseline)
+        if world == 1 and not args.no_configs and pt == BOX:
+            line["configs"] = other_configs(torch, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-    del np
 
 
 if __name__ == "__main__":

@@ -10,7 +10,11 @@
 // file-scope array below instead of a caller workspace.
 //
 // The array is CROSS_NTT_NOALLOC_SCRATCH_BYTES (16 MiB) per GPU and is held
-// by every GPU that loads this library until the process exits.  All calls
+// by every GPU that loads this library until the process exits.  The
+// intermediate takes two words per input word (ntt_tmp_words), so one call
+// converts at most CROSS_NTT_NOALLOC_MAX_WORDS = 2 Mi input words.  Its device
+// address is looked up once per device and cached for the process, so
+// cudaDeviceReset after the first call is not supported.  All calls
 // share it and it keeps the previous call's contents (the NTT overwrites
 // every word it reads, so nothing needs clearing); calls that overlap on the
 // GPU -- on different streams, or from different host threads -- race on it,

@@ -1058,3 +1058,140 @@ int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, L
 }
 
 }  // namespace cross
+
+// ---------------------------------------------------------------------------
+// Throughput probe of tcgen05.mma kind::i8: the peak that the contraction
+// kernels' roofline fractions are quoted against.  Every CTA keeps one A tile
+// (128 rows x 128 B) and one B tile (N rows x 128 B), SWIZZLE_128B, filled
+// with hashed bytes so the data is not all zero, in shared memory; one thread
+// issues kchunks x 4 back-to-back MMAs of K = 32 into a 256-column TMEM
+// accumulator -- M = 128, N = 256 per CTA (pair = 0) or M = 256, N = 256 per
+// cluster of two CTAs with cta_group::2 (pair = 1, the form of k_bat_tc2) --
+// and commits once.  No global memory is read; the only wait is the bounded
+// wait for that commit (code 31 in *err on expiry).
+namespace cross {
+namespace tc {
+
+constexpr int PROBE_THREADS = 128;
+// more than half an SM's shared memory, so that no SM holds two probe CTAs
+// (only the first 48 KiB + barrier are used)
+constexpr size_t PROBE_SMEM = 160 * 1024;
+
+template <bool PAIR>
+__global__ void __launch_bounds__(PROBE_THREADS, 1) k_i8_probe(int64_t kchunks, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // A: 128 rows x 128 B; B: N rows x 128 B (256 rows for one CTA, 128 per CTA
+  // of a pair), so the barrier follows 48 KiB of operands
+  uint8_t* As = base;
+  uint8_t* Bs = base + A_STAGE;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + A_STAGE + B_STAGE);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  volatile int& abort = *reinterpret_cast<volatile int*>(tslot + 1);
+  const int warp = threadIdx.x >> 5;
+  const uint32_t rank = PAIR ? cluster_rank() : 0;
+  for (int i = threadIdx.x; i < (A_STAGE + B_STAGE) / 4; i += PROBE_THREADS) {
+    uint32_t h = (uint32_t)i * 2654435761u ^ (blockIdx.x * 0x9E3779B9u);
+    h ^= h >> 15;
+    h *= 2246822519u;
+    h ^= h >> 13;
+    reinterpret_cast<uint32_t*>(base)[i] = h;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(256)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(256)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+  }
+  // the generic-proxy fill must be visible to the tensor cores' async proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  if (PAIR) cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (threadIdx.x == 0 && rank == 0) {
+    const uint32_t as = saddr(As), bs = saddr(Bs);
+    for (int64_t i = 0; i < kchunks; ++i) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (PAIR)
+          mma_i8_pair(tmem, sw128_desc(as + 32 * k), sw128_desc(bs + 32 * k), (i | k) != 0);
+        else
+          mma_i8(tmem, sw128_desc(as + 32 * k), sw128_desc(bs + 32 * k), (i | k) != 0);
+      }
+    }
+    if (PAIR)
+      mma_commit_pair_both(bar);
+    else
+      mma_commit(bar);
+  }
+  if (threadIdx.x == 0) mbar_wait(bar, 0, abort, err, 31);
+  tc_fence_before();
+  __syncthreads();
+  if (PAIR) cluster_sync();
+  tc_fence_after();
+  if (warp == 1) {
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+  }
+}
+
+template <bool PAIR>
+int launch_probe(int64_t kchunks, int* err, int* ctas, cudaStream_t st) {
+  auto kern = k_i8_probe<PAIR>;
+  CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PROBE_SMEM));
+  const int sms = device_sm_count();
+  int grid = sms;
+  if (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(sms & ~1));
+    cfg.blockDim = dim3(PROBE_THREADS);
+    cfg.dynamicSmemBytes = PROBE_SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &cfg) != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = sms / 2;
+    }
+    // one CTA per SM (the shared-memory request keeps a second one out)
+    grid = 2 * (n < sms / 2 ? n : sms / 2);
+    cfg.gridDim = dim3((unsigned)grid);
+    CROSS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, kchunks, err));
+  } else {
+    kern<<<grid, PROBE_THREADS, PROBE_SMEM, st>>>(kchunks, err);
+  }
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  *ctas = grid;
+  return CROSS_OK;
+}
+
+}  // namespace tc
+}  // namespace cross
+
+extern "C" int cross_tc_i8_probe(int pair, int64_t kchunks, int* err, int* ctas, void* stream) {
+  CROSS_REQUIRE(err && ctas && kchunks >= 1 && kchunks <= (1 << 20),
+                "cross_tc_i8_probe: need err, ctas and 1 <= kchunks <= 2^20");
+  return pair ? cross::tc::launch_probe<true>(kchunks, err, ctas, (cudaStream_t)stream)
+              : cross::tc::launch_probe<false>(kchunks, err, ctas, (cudaStream_t)stream);
+}

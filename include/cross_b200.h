@@ -72,6 +72,17 @@ const char* cross_last_error(void);
  * threads); a diagnostic for benchmarks. */
 uint64_t cross_launch_count(void);
 
+/* Throughput probe of the int8 tensor cores (no counterpart in the
+ * reference; the measured peak that the contraction kernels' roofline
+ * fractions are quoted against).  One launch on all SMs: each CTA issues
+ * kchunks x 4 tcgen05.mma kind::i8 of K = 32 bytes on operands resident in
+ * shared memory, M = 128 x N = 256 per CTA (pair = 0) or M = 256 x N = 256 per
+ * cluster of two CTAs with cta_group::2 (pair != 0, the form of the NTT
+ * contraction), i.e. 2 * 128 * 256 * 128 int8 operations per CTA per chunk.
+ * *ctas (host) receives the CTAs launched; err is a device int that the
+ * bounded completion wait sets to 31 when it expires.  1 <= kchunks <= 2^20. */
+int cross_tc_i8_probe(int pair, int64_t kchunks, int* err, int* ctas, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Modulus sets                                                        */
 /* ------------------------------------------------------------------ */
@@ -212,13 +223,17 @@ int cross_ntt_plan_check(cross_ntt_plan plan);
  * only in/out (limb-major layout, (batch, M, r, c) uint32, in may equal out)
  * and keeps the NTT intermediate in a file-scope static device array of
  * CROSS_NTT_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits.
- * batch * M * r * c must not exceed CROSS_NTT_NOALLOC_SCRATCH_BYTES / 4
- * words, else CROSS_ERR_WORKSPACE.  It calls no allocator.  The first call on
- * each device looks up the array's device address (cudaGetSymbolAddress) and
- * caches it; make that first call before any stream capture.  All calls share
- * the array: calls that overlap on the GPU (other streams or threads) race,
- * so issue them on one stream. */
+ * The intermediate is two words per input word, so batch * M * r * c must not
+ * exceed CROSS_NTT_NOALLOC_MAX_WORDS (CROSS_NTT_NOALLOC_SCRATCH_BYTES / 8 =
+ * 2 Mi words, e.g. batch 4 of 8 limbs at N = 2^16), else CROSS_ERR_WORKSPACE
+ * before any launch.  It calls no allocator.  The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress) and caches it for
+ * the process; make that first call before any stream capture, and do not
+ * call cudaDeviceReset afterwards (the cached address would be stale).  All
+ * calls share the array: calls that overlap on the GPU (other streams or
+ * threads) race, so issue them on one stream. */
 #define CROSS_NTT_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define CROSS_NTT_NOALLOC_MAX_WORDS (CROSS_NTT_NOALLOC_SCRATCH_BYTES / 8u)
 int cross_ntt_noalloc(cross_ntt_plan plan, int inverse, const uint32_t* in, uint32_t* out, int64_t batch,
                       void* stream);
 

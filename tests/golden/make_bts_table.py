@@ -1,9 +1,11 @@
 """Writes bts_invocations.csv: the invocation counts of the CKKS bootstrapping
 kernel mix, read as text from the reference's tabIX.py (the
 BTS_KERNEL_INVOCATION_CSV literal, tabIX.py:399-580).  The reference module
-imports jax, so it is parsed, not imported.
+imports jax, so it is parsed, not imported.  The table is product data
+(cross_b200/data/bts_invocations.csv, read by cross_b200.bts_mix); this
+script only regenerates it.
 
-    python cross_b200/data/make_bts_table.py /root/reference/jaxite_word
+    python tests/golden/make_bts_table.py <path of the reference's jaxite_word directory>
 """
 import csv
 import io
@@ -27,7 +29,8 @@ def extract(tabix_source: str) -> list:
 def main(ref_dir: str) -> None:
     with open(os.path.join(ref_dir, "tabIX.py")) as f:
         rows = extract(f.read())
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "bts_invocations.csv")
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    path = os.path.join(root, "cross_b200", "data", "bts_invocations.csv")
     with open(path, "w", newline="") as f:
         w = csv.writer(f, lineterminator="\n")
         w.writerow(["kernel", "dims", "count"])
@@ -37,4 +40,6 @@ def main(ref_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/jaxite_word")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_bts_table.py <jaxite_word directory of the reference>")
+    main(sys.argv[1])

@@ -7,7 +7,7 @@ reference is imported or executed) and writes one JSON file per test into this
 directory.  The committed JSON files are what the tests use; this script only
 needs the reference checkout when the fixtures are regenerated:
 
-    python tests/golden/make_golden.py /root/reference/jaxite_word
+    python tests/golden/make_golden.py <path of the reference's jaxite_word directory>
 
 Sources:
   ntt_mm_test.py:13-24      NTT / INTT, N=16 (4x4), 3 x 134219681
@@ -127,4 +127,6 @@ def main(ref_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/jaxite_word")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <jaxite_word directory of the reference>")
+    main(sys.argv[1])

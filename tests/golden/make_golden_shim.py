@@ -8,7 +8,7 @@ The stand-in is first held to the reference's own golden vectors at N = 16
 herot_test.py, as extracted into tests/golden/*.json): if the reference run
 through it does not reproduce them, nothing is written.
 
-    python tests/golden/make_golden_shim.py /root/reference/jaxite_word [--regenerate]
+    python tests/golden/make_golden_shim.py <path of the reference's jaxite_word directory> [--regenerate]
 """
 import json
 import os
@@ -235,4 +235,6 @@ def main(ref_dir, regenerate=False):
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if a != "--regenerate"]
-    main(args[0] if args else "/root/reference/jaxite_word", regenerate="--regenerate" in sys.argv)
+    if len(args) != 1:
+        sys.exit("usage: python tests/golden/make_golden_shim.py <jaxite_word directory of the reference> [--regenerate]")
+    main(args[0], regenerate="--regenerate" in sys.argv)
