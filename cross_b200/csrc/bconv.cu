@@ -374,6 +374,245 @@ int launch_bconv_tc_any(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cuda
   return launch_bconv_tc<FAST, TWIST, 4, 64, 0>(a, smem, ctas_per_sm, st);
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core basis conversion with every per-limb constant in the kernel's
+// parameter space (k_bconv_tcc).  Same tile structure as k_bconv_tc -- a CTA
+// of 256 threads per tile of 128 coefficients, thread (row, h) packs the source
+// limb groups 2k + h and produces the target limbs [h JH, (h + 1) JH) -- but the
+// half h is a template argument of the per-thread work, so every limb index is
+// a compile-time constant: the moduli, Barrett constants, QHatInvModq and twist
+// rows are read from the constant bank as instruction operands, the limb-row
+// strides of the N = 2^16 instantiation are immediates, and the byte planes
+// are recombined in two 32-bit multiply-adds and one widening one (every BAT
+// sum of at most 32 source limbs is below 2^23).  Used when every source and
+// target modulus passes reduce_fast_ok (all moduli of the HE parameter sets).
+struct BconvConsts {
+  uint32_t sq_q[32], sq_m[32], sq_sw[32], sq_hi[32];   // source q_i, Barrett m, s_w, QHatInvModq_i
+  uint32_t dq[64], dm[64], dsw[64];                    // target q_j, Barrett m, s_w
+  const uint32_t* tp[64];                              // twist row of target j (TWIST)
+};
+
+struct BconvTccArgs {
+  const uint32_t* in;
+  int64_t in_ps, in_ls;
+  uint32_t* out;
+  int64_t out_ps, out_ls;
+  int polys, n, sq, sp, kb, nn;
+  uint32_t tmem_cols;
+  const uint8_t* bimg;
+  int* err;
+  BconvConsts k;
+};
+
+// sum_p a_p << 8p (bconv.py:31-37) for a_p < 2^23: a0 + a1 2^8 and a2 + a3 2^8
+// fit 32 bits, and the sum is their first plus 2^16 times the second.
+__device__ __forceinline__ uint64_t combine4_small(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {
+  const uint32_t s = a0 + (a1 << 8), u = a2 + (a3 << 8);
+  return (uint64_t)s + ((uint64_t)u << 16);
+}
+
+template <int H, int KB, int NN>
+__device__ __forceinline__ void bcc_load(const BconvTccArgs& a, int w, int tiles_pp, int row, uint32_t (&xin)[4 * KB]) {
+  const int64_t in_ls = NN ? NN : a.in_ls;
+  const int poly = w / tiles_pp;
+  const uint32_t* x = a.in + (int64_t)poly * a.in_ps + (w - poly * tiles_pp) * BT_ROWS + row;
+#pragma unroll
+  for (int k = 0; k < KB; ++k)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * (2 * k + H) + e;
+      xin[4 * k + e] = i < a.sq ? __ldg(x + (int64_t)i * in_ls) : 0u;
+    }
+}
+
+// c_i = Barrett_i(x_i QHatInvModq_i) of this thread's source groups as row
+// `row` of the K-major A tile (the exact 32-bit form for x < 2^31, where
+// x QHatInv < 2^31 q; the 64-bit form above).
+template <int H, int KB>
+__device__ __forceinline__ void bcc_pack(const BconvTccArgs& a, uint8_t* As, int row, const uint32_t (&xin)[4 * KB]) {
+#pragma unroll
+  for (int k = 0; k < KB; ++k) {
+    if (k < a.kb) {
+      uint32_t c[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * (2 * k + H) + e;
+        uint32_t v = 0;
+        if (i < a.sq) {
+          const uint32_t xv = xin[4 * k + e], hv = a.k.sq_hi[i], q = a.k.sq_q[i], m = a.k.sq_m[i],
+                         sw = a.k.sq_sw[i];
+          v = xv < 0x80000000u ? reduce_fast2(xv * hv, __umulhi(xv, hv), q, m, sw)
+                               : barrett_w32((uint64_t)xv * hv, q, m, sw);
+        }
+        c[e] = v;
+      }
+      *reinterpret_cast<uint4*>(As + k * 4096 + (row >> 3) * 256 + H * 128 + (row & 7) * 16) =
+          make_uint4(c[0], c[1], c[2], c[3]);
+    }
+  }
+}
+
+template <int H, int JH, bool TWIST>
+__device__ __forceinline__ void bcc_twist(const BconvTccArgs& a, int t, uint32_t (&tw)[JH]) {
+  if (TWIST) {
+#pragma unroll
+    for (int jj = 0; jj < JH; ++jj) {
+      const int j = H * JH + jj;
+      tw[jj] = j < a.sp ? __ldg(a.k.tp[j] + t) : 0u;
+    }
+  }
+}
+
+// out_j[t] = Barrett_j(sum_b D[t][4j + b] << 8b) (x psi twist) for this
+// thread's targets; lane quadrant (warp & 3) of the accumulator.
+template <int H, int JH, bool TWIST, int NN>
+__device__ __forceinline__ void bcc_store(const BconvTccArgs& a, uint32_t tmem, int warp, uint32_t* y,
+                                          const uint32_t (&tw)[JH]) {
+  const int64_t out_ls = NN ? NN : a.out_ls;
+#pragma unroll
+  for (int qc = 0; qc < JH / 4; ++qc) {
+    constexpr int J0 = H * JH;
+    const int j0 = J0 + 4 * qc;
+    if (4 * j0 < a.nn) {
+      uint32_t v[16];
+      tmem_ld16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + 4 * j0, v);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = j0 + jj;
+        if (j < a.sp) {
+          const uint32_t q = a.k.dq[j], m = a.k.dm[j], sw = a.k.dsw[j];
+          const uint64_t z = combine4_small(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+          uint32_t r = reduce_fast(z, q, m, sw);
+          if (TWIST) {
+            const uint32_t twj = tw[4 * qc + jj];
+            r = reduce_fast2(r * twj, __umulhi(r, twj), q, m, sw);
+          }
+          y[(int64_t)j * out_ls] = r;
+        }
+      }
+    }
+  }
+}
+
+template <bool TWIST, int KB, int SPMAX, int NN>
+__global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tcc(const __grid_constant__ BconvTccArgs a) {
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* As = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Bs = As + a.kb * 4096;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(Bs + a.kb * (a.nn / 8) * 256);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  volatile int& abort = *reinterpret_cast<volatile int*>(tmem_slot + 1);
+  constexpr int JH = SPMAX / 2;
+  const int t = threadIdx.x, warp = t >> 5;
+  const int row = t & (BT_ROWS - 1), h = t / BT_ROWS;   // h is uniform per warp
+  const int n = NN ? NN : a.n;
+  for (int i = t; i < a.kb * (a.nn / 8) * 16; i += BT_THREADS)
+    reinterpret_cast<uint4*>(Bs)[i] = reinterpret_cast<const uint4*>(a.bimg)[i];
+  if (t == 0) {
+    mbar_init(bar, 1);
+    abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                 "r"(a.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t idesc = (2u << 4) | ((uint32_t)(a.nn >> 3) << 17) | ((uint32_t)(BT_ROWS >> 4) << 24);
+  const int tiles_pp = n / BT_ROWS;
+  const int total = a.polys * tiles_pp;
+  uint32_t xin[4 * KB];
+  uint32_t tw[JH];
+  if ((int)blockIdx.x < total) {
+    if (h == 0) bcc_load<0, KB, NN>(a, blockIdx.x, tiles_pp, row, xin);
+    else bcc_load<1, KB, NN>(a, blockIdx.x, tiles_pp, row, xin);
+  }
+  uint32_t phase = 0;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int poly = w / tiles_pp;
+    const int t0 = (w - poly * tiles_pp) * BT_ROWS;
+    // 1. source residues into the A tile, then the next tile's inputs and
+    //    this tile's twists, in flight during the MMA
+    const bool more = w + (int)gridDim.x < total;
+    if (h == 0) {
+      bcc_pack<0, KB>(a, As, row, xin);
+      if (more) bcc_load<0, KB, NN>(a, w + gridDim.x, tiles_pp, row, xin);
+      bcc_twist<0, JH, TWIST>(a, t0 + row, tw);
+    } else {
+      bcc_pack<1, KB>(a, As, row, xin);
+      if (more) bcc_load<1, KB, NN>(a, w + gridDim.x, tiles_pp, row, xin);
+      bcc_twist<1, JH, TWIST>(a, t0 + row, tw);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    bool ok = true;
+    if (t == 0) {
+      tc_fence_after();
+      for (int k = 0; k < a.kb; ++k) {
+        const uint64_t ad = kmajor_desc(saddr(As + k * 4096));
+        const uint64_t bd = kmajor_desc(saddr(Bs + k * (a.nn / 8) * 256));
+        const uint32_t acc = k > 0, z = 0;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(tmem),
+            "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(z));
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+                   : "memory");
+      // 2. accumulator ready (one waiting thread; the others sleep in the barrier)
+      ok = mbar_wait(bar, phase, abort, a.err, 22);
+    }
+    phase ^= 1;
+    if (__syncthreads_or(!ok)) break;
+    tc_fence_after();
+    // 3. this half's target limbs
+    uint32_t* y = a.out + (int64_t)poly * a.out_ps + t0 + row;
+    if (h == 0) bcc_store<0, JH, TWIST, NN>(a, tmem, warp, y, tw);
+    else bcc_store<1, JH, TWIST, NN>(a, tmem, warp, y, tw);
+    tc_fence_before();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+}
+
+template <bool TWIST, int KB, int SPMAX, int NN>
+int launch_bconv_tcc(const BconvTccArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
+  const int sms = device_sm_count();
+  auto kern = k_bconv_tcc<TWIST, KB, SPMAX, NN>;
+  CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t total = (int64_t)a.polys * (a.n / BT_ROWS);
+  const int64_t cap = (int64_t)sms * ctas_per_sm;
+  kern<<<(unsigned)(total < cap ? total : cap), BT_THREADS, smem, st>>>(a);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+template <bool TWIST>
+int launch_bconv_tcc_any(const BconvTccArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
+  const bool n64k = a.n == 65536 && a.in_ls == 65536 && a.out_ls == 65536;
+#define CROSS_BCC(KB, SPM)                                                                        \
+  return n64k ? launch_bconv_tcc<TWIST, KB, SPM, 65536>(a, smem, ctas_per_sm, st)                 \
+              : launch_bconv_tcc<TWIST, KB, SPM, 0>(a, smem, ctas_per_sm, st)
+  if (a.kb == 1 && a.sp <= 24) CROSS_BCC(1, 24);
+  if (a.kb == 1 && a.sp <= 40) CROSS_BCC(1, 40);
+  if (a.kb == 1) CROSS_BCC(1, 64);
+  if (a.kb <= 2 && a.sp <= 40) CROSS_BCC(2, 40);
+  if (a.kb <= 3 && a.sp <= 40) CROSS_BCC(3, 40);
+  CROSS_BCC(4, 64);
+#undef CROSS_BCC
+}
+
 template <int SQMAX, bool BAT>
 int launch_bconv(const cross_bconv_plan_s* P, bool vec, const uint32_t* in, int64_t in_ps, int64_t in_ls,
                  int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
@@ -404,7 +643,7 @@ int launch_bconv(const cross_bconv_plan_s* P, bool vec, const uint32_t* in, int6
 
 int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t in_ps, int64_t in_ls,
               int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
-              int64_t n, cudaStream_t st, const uint32_t* twist, const uint16_t* trow) {
+              int64_t n, cudaStream_t st, const uint32_t* twist, const uint16_t* trow, const int* trow_host) {
   if (polys == 0 || n == 0) return CROSS_OK;
   if (P->red != CROSS_REDUCTION_BARRETT) {
     set_error("bconv: the HE chains take Barrett plans only (plan reduction %d)", P->red);
@@ -418,6 +657,26 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
     const int sm_bytes = device_smem_per_sm();
     int ctas = 0;
     const size_t sm = bconv_tc_smem(P->sq, P->sp, P->tc_kb, P->tc_nn, a.tmem_cols, (size_t)sm_bytes, &ctas);
+    static const bool generic_only = getenv("CROSS_B200_BCONV_GENERIC") && getenv("CROSS_B200_BCONV_GENERIC")[0] == '1';
+    if (sm && P->tc_fast && P->tc_src_fast && (!twist || trow_host) && !generic_only) {
+      BconvTccArgs c{in, in_ps, in_ls, out, out_ps, out_ls, (int)polys, (int)n, P->sq, P->sp, P->tc_kb, P->tc_nn,
+                     a.tmem_cols, P->tc_bimg, P->err, {}};
+      for (int i = 0; i < P->sq; ++i) {
+        const ModC& mc = P->src_host[i];
+        c.k.sq_q[i] = (uint32_t)mc.q;
+        c.k.sq_m[i] = (uint32_t)mc.m;
+        c.k.sq_sw[i] = mc.s_w;
+        c.k.sq_hi[i] = P->qhat_inv_host[i];
+      }
+      for (int j = 0; j < P->sp; ++j) {
+        const ModC& mc = P->dst_host[j];
+        c.k.dq[j] = (uint32_t)mc.q;
+        c.k.dm[j] = (uint32_t)mc.m;
+        c.k.dsw[j] = mc.s_w;
+        c.k.tp[j] = twist ? twist + (int64_t)trow_host[j] * n : nullptr;
+      }
+      return twist ? launch_bconv_tcc_any<true>(c, sm, ctas, st) : launch_bconv_tcc_any<false>(c, sm, ctas, st);
+    }
     if (sm) {
       const bool f = P->tc_fast != 0;
       if (twist)
@@ -483,6 +742,7 @@ int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction
   for (int i = 0; i < sq; ++i)
     for (int j = 0; j < sp; ++j) qm[(size_t)j * sq + i] = qhat_modp[(size_t)i * sp + j];
   std::vector<uint32_t> qi(qhat_inv_modq, qhat_inv_modq + sq);
+  P->qhat_inv_host = qi;
   // tensor-core B operand: row n = 4j + b, K byte 4i + a, in the K-major
   // no-swizzle core-matrix layout of k_bconv_tc (sq <= 32, sp <= 64)
   std::vector<uint8_t> bimg;

@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(128) k_ks_inner(LP dig, PartPtrs parts, const 
   }
 }
 
-// k_ks_inner for more than four digits: one digit at a time.
+// k_ks_inner for more than eight digits: one digit at a time.
 template <bool W32>
 __global__ void k_ks_inner_loop(LP dig, PartPtrs parts, int nparts, const int16_t* __restrict__ src, int LT,
                                 int64_t n, int64_t batch, const uint32_t* __restrict__ evka,
@@ -201,7 +201,7 @@ __global__ void k_ks_inner_loop(LP dig, PartPtrs parts, int nparts, const int16_
 }
 
 // Launches the key-switch inner product over batch x LT rows: the persistent
-// item kernel for 2..4 digits, one block row per limb-ciphertext otherwise.
+// item kernel for 2..8 digits, one block row per limb-ciphertext otherwise.
 template <bool W32, int NP>
 void ks_inner_items(LP dig, const PartPtrs& pp, const int16_t* src, int LT, int64_t n, int64_t B, const uint32_t* evka,
                     const uint32_t* evkb, uint32_t* KS, const ModC* mods, cudaStream_t st) {
@@ -223,13 +223,19 @@ void ks_inner_items(LP dig, const PartPtrs& pp, const int16_t* src, int LT, int6
 int ks_inner(bool w32, LP dig, const PartPtrs& pp, int nparts, const int16_t* src, int LT, int64_t n, int64_t B,
              const uint32_t* evka, const uint32_t* evkb, uint32_t* KS, const ModC* mods, cudaStream_t st) {
   const int64_t items = B * LT * (((n >> 2) + 127) / 128);
-  if (nparts >= 2 && nparts <= 4 && items < ((int64_t)1 << 31)) {
+  if (nparts >= 2 && nparts <= 8 && items < ((int64_t)1 << 31)) {
 #define CROSS_KS(NP)                                                                              \
   (w32 ? ks_inner_items<true, NP>(dig, pp, src, LT, n, B, evka, evkb, KS, mods, st)               \
        : ks_inner_items<false, NP>(dig, pp, src, LT, n, B, evka, evkb, KS, mods, st))
-    if (nparts == 2) CROSS_KS(2);
-    else if (nparts == 3) CROSS_KS(3);
-    else CROSS_KS(4);
+    switch (nparts) {
+      case 2: CROSS_KS(2); break;
+      case 3: CROSS_KS(3); break;
+      case 4: CROSS_KS(4); break;
+      case 5: CROSS_KS(5); break;
+      case 6: CROSS_KS(6); break;
+      case 7: CROSS_KS(7); break;
+      default: CROSS_KS(8); break;
+    }
 #undef CROSS_KS
   } else {
     const dim3 g(gx_for(n >> 2), gy_for(B * LT));
@@ -342,6 +348,7 @@ struct cross_hemul_plan_s {
   cross_bconv_plan_s* down = nullptr;
   std::vector<int> dstart, dlen;
   std::vector<std::vector<int>> comp;   // complement, indices in Q'+P
+  std::vector<int> seq_host;            // 0, 1, ... (the ModDown twist rows)
   uint32_t thr = 0, q_last = 0;
   // device tables; _t = transposed coefficient order, _d = ModDown order
   uint32_t *inv_psi_last_t = nullptr, *gamma_psi_t = nullptr, *inv_psi_q_t = nullptr, *psi_qp_t = nullptr,
@@ -466,6 +473,7 @@ int cross_hemul_plan_create(const cross_hemul_desc* d, cross_hemul_plan* out) {
   P->thr = (P->q_last + 1) / 2;                                 // ciphertext.py:260
   std::vector<uint16_t> seq(std::max<int>(LT, 4) + 1), last{(uint16_t)(L - 1)}, zero{0}, pp, q1;
   for (size_t i = 0; i < seq.size(); ++i) seq[i] = (uint16_t)i;
+  P->seq_host.assign(seq.begin(), seq.end());
   for (int k = 0; k < K; ++k) pp.push_back((uint16_t)(P->p_off + k));
   for (int i = 0; i < L1; ++i) q1.push_back((uint16_t)i);
   const int R = d->r, C = d->c;
@@ -596,7 +604,7 @@ int cross_hemul(cross_hemul_plan P, const uint32_t* in, uint32_t* out, int64_t B
     const int ns = LT - P->dlen[j];
     const int64_t eps = (int64_t)ns * N;
     if ((rc = bconv_run(P->ks_bconv[j], true, b.Cc + (int64_t)P->dstart[j] * N, (int64_t)L1 * N, N, 1, b.E[j], eps,
-                        N, 1, B, N, st, P->psi_qp_t, P->comp_dle[j])))
+                        N, 1, B, N, st, P->psi_qp_t, P->comp_dle[j], P->comp[j].data())))
       return rc;
     if ((rc = ntt_exec(P->ntt_qp, false, LP{b.E[j], eps, N}, COEF_TRANSPOSED, LPo{b.E[j], eps, N}, COEF_NATURAL, B, ns,
                        P->comp_plan[j], Epi{}, b.tmp, st)))
@@ -616,7 +624,7 @@ int cross_hemul(cross_hemul_plan P, const uint32_t* in, uint32_t* out, int64_t B
                      P->down_layout, B * 2, K, P->m_p_plan, tw, b.tmp, st)))
     return rc;
   if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L1 * N, N, 1, B * 2, N, st, P->psi_q_d,
-                      P->seq)))
+                      P->seq, P->seq_host.data())))
     return rc;
   Epi md;
   md.op = EPI_MODDOWN;
@@ -650,6 +658,8 @@ struct cross_herot_plan_s {
   uint32_t *inv_psi_q_t = nullptr, *psi_qp_t = nullptr, *inv_psi_p_t = nullptr, *pinv = nullptr;
   uint16_t *seq = nullptr, *m_p = nullptr;
   std::vector<uint16_t*> comp;
+  std::vector<std::vector<int>> comp_host;   // the same complements on the host
+  std::vector<int> seq_host;
   int16_t* ks_src = nullptr;
   uint32_t *evk_a = nullptr, *evk_b = nullptr;
   int32_t* coef_map = nullptr;
@@ -736,6 +746,7 @@ int cross_herot_plan_create(const cross_herot_desc* d, cross_herot_plan* out) {
       if (!same_q(bc->dst_host[i], mq[comp[i]])) return fail("ks_bconv target moduli", j);
     for (size_t i = 0; i < comp.size(); ++i) src[(size_t)j * LT + comp[i]] = (int16_t)i;
     P->ks_bconv.push_back(d->ks_bconv[j]);
+    P->comp_host.push_back(comp);
     std::vector<uint16_t> cu(comp.begin(), comp.end());
     uint16_t* dp = nullptr;
     if (upload_vec(&dp, cu)) return fail("upload");
@@ -746,6 +757,7 @@ int cross_herot_plan_create(const cross_herot_desc* d, cross_herot_plan* out) {
   if (P->down->sq != K || P->down->sp != L) return fail("down_bconv shape mismatch");
   std::vector<uint16_t> seq(LT + 1), mp;
   for (size_t i = 0; i < seq.size(); ++i) seq[i] = (uint16_t)i;
+  P->seq_host.assign(seq.begin(), seq.end());
   for (int k = 0; k < K; ++k) mp.push_back((uint16_t)(L + k));
   int rc = CROSS_OK;
   const int R = d->ntt_qp->r, C = d->ntt_qp->c;
@@ -838,7 +850,7 @@ int cross_herot(cross_herot_plan P, const uint32_t* in, uint32_t* out, int64_t B
     const int ns = LT - P->dlen[j];
     const int64_t eps = (int64_t)ns * N;
     if ((rc = bconv_run(P->ks_bconv[j], true, b.Cq + (int64_t)P->dstart[j] * N, (int64_t)L * N, N, 1, b.E[j], eps, N,
-                        1, B, N, st, P->psi_qp_t, P->comp[j])))
+                        1, B, N, st, P->psi_qp_t, P->comp[j], P->comp_host[j].data())))
       return rc;
     if ((rc = ntt_exec(P->ntt, false, LP{b.E[j], eps, N}, COEF_TRANSPOSED, LPo{b.E[j], eps, N}, COEF_NATURAL, B, ns,
                        P->comp[j], Epi{}, b.tmp, st)))
@@ -857,7 +869,7 @@ int cross_herot(cross_herot_plan P, const uint32_t* in, uint32_t* out, int64_t B
                      COEF_TRANSPOSED, B * 2, K, P->m_p, tw, b.tmp, st)))
     return rc;
   if ((rc = bconv_run(P->down, true, b.KP, (int64_t)K * N, N, 1, b.F, (int64_t)L * N, N, 1, B * 2, N, st, P->psi_qp_t,
-                      P->seq)))
+                      P->seq, P->seq_host.data())))
     return rc;
   Epi md;
   md.op = EPI_MODDOWN;

@@ -52,6 +52,7 @@ struct cross_ntt_plan_s {
   int* tc_err = nullptr;            // device error word of the tensor-core kernels
   int tc_fast = 0;                  // 32-bit remainder Barrett is exact for every limb
   int tc_pair = 0;                  // two-SM kernel (k_bat_tc2) for K extents kw <= 256
+  bool tc64 = false;                // 64 x 64 Barrett plan: plain transforms by k_ntt64 (one launch)
   CUtensorMap tm_col_fwd, tm_col_inv, tm_row_fwd, tm_row_inv;       // boxes of 256 B rows
   CUtensorMap tm2_col_fwd, tm2_col_inv, tm2_row_fwd, tm2_row_inv;   // boxes of 128 B rows
 };
@@ -72,6 +73,7 @@ struct cross_bconv_plan_s {
   cross::ModC* src = nullptr;       // [sq]
   cross::ModC* dst = nullptr;       // [sp]
   uint32_t* qhat_inv = nullptr;     // [sq]
+  std::vector<uint32_t> qhat_inv_host;   // [sq] (the constant-bank kernel's parameters)
   uint32_t* bat = nullptr;          // [sp][4 b][sq]: sum_a bat[(i*4+a), j, b] << 8a
   uint32_t* qhat_modp = nullptr;    // [sp][sq]
 };
@@ -208,6 +210,10 @@ bool tc_supported(int r, int c);
 int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, const uint8_t* intt1,
                  const uint8_t* intt3, const uint32_t* intt_tw);
 void tc_plan_free(cross_ntt_plan_s* P);
+// Plain NTT / INTT of a 64 x 64 plan (tc64), natural coefficient order, one
+// launch; in / out limb-polynomial bases and strides 16-byte aligned.
+int ntt64_run(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+              const uint16_t* limbs, cudaStream_t st);
 int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo out, int out_layout,
                 int64_t polys, int slots, const uint16_t* limbs, const Epi& epi, uint32_t* tmp, cudaStream_t st);
 
@@ -229,10 +235,13 @@ int ntt_run(const cross_ntt_plan_s* plan, bool inverse, LP in, LPo out, int64_t 
 // bconv over polys with arbitrary limb / coefficient strides.  With tab set,
 // output limb j is further multiplied by tab[trow[j]][t] (position t) and
 // Barrett-reduced with the target modulus (the psi twist of ciphertext.py:496).
+// trow_host: the same rows on the host (lets the tensor-core kernel take the
+// twist rows as parameters; without it a twisted conversion takes the
+// generic kernel).
 int bconv_run(const cross_bconv_plan_s* plan, bool bat, const uint32_t* in, int64_t in_ps,
               int64_t in_ls, int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls,
               int64_t out_ts, int64_t polys, int64_t n, cudaStream_t st, const uint32_t* tab = nullptr,
-              const uint16_t* trow = nullptr);
+              const uint16_t* trow = nullptr, const int* trow_host = nullptr);
 
 // y[poly, slot, t] = Barrett_{mods[midx[slot]]}(x * tab[trow[slot] * n + t])
 int modmul_table_lm(LP x, LPo y, int64_t polys, int slots, int64_t n, const uint32_t* tab,
