@@ -52,6 +52,7 @@ N_DEG, R, C = 65536, 256, 256
 # (3.148 GB per launch over 256 polys x 23 limbs; traffic grows with the
 # limb-polynomials processed).
 TRAFFIC_PER_LP = 3.148e9 / (256 * 23)
+L2_BYTES = 126 * 2 ** 20                # B200 L2
 
 
 @dataclass
@@ -415,13 +416,21 @@ def measure_component(workload, torch, dist, world, rank, local, steps, warmup, 
         xh = (rng.integers(0, 2 ** 62, size=(B, Lw, rr, cc), dtype=np.uint64) %
               np.array(q, np.uint64)[:, None, None]).astype(np.uint32)
         x = torch.from_numpy(xh).to(dev)
-        y = torch.empty_like(x)
+        # a configuration smaller than L2 cycles through enough copies of its
+        # input (> 1.25 x L2 in all) that every timed step reads cold data
+        nsets = max(1, -(-int(1.25 * L2_BYTES) // (2 * x.numel() * 4))) if x.numel() * 4 < L2_BYTES else 1
+        xs = [x] + [x.clone() for _ in range(nsets - 1)]
+        ys = [torch.empty_like(x) for _ in range(nsets)]
+        y = ys[0]
         ws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), B, _lib.LAYOUT_LIMB_MAJOR), dtype=torch.uint8,
                          device=dev)
-        cs = torch.cuda.current_stream().cuda_stream
+        ctr = [0]
 
         def step():
-            for inv, a, b in ((0, x, y), (1, y, y)):
+            cs = torch.cuda.current_stream().cuda_stream
+            k = ctr[0] % nsets
+            ctr[0] += 1
+            for inv, a, b in ((0, xs[k], ys[k]), (1, ys[k], ys[k])):
                 _lib.check(lib.cross_ntt(ctx.plan(), inv, a.data_ptr(), b.data_ptr(), B, _lib.LAYOUT_LIMB_MAJOR,
                                          ws.data_ptr(), ws.numel(), cs), "cross_ntt")
         units = 2 * B * Lw                                   # limb-transforms per step
@@ -468,9 +477,9 @@ def measure_component(workload, torch, dist, world, rank, local, steps, warmup, 
         x = torch.from_numpy(xh).to(dev)
         ob = lib.cross_bconv_output_bytes(bc.plan(0))
         y = torch.empty((B, sp, N_DEG), dtype=torch.uint64 if ob == 8 else torch.uint32, device=dev)
-        cs = torch.cuda.current_stream().cuda_stream
 
         def step():
+            cs = torch.cuda.current_stream().cuda_stream
             _lib.check(lib.cross_bconv_ex(bc.plan(0), int(bat), x.data_ptr(), y.data_ptr(), B, N_DEG,
                                           _lib.LAYOUT_LIMB_MAJOR, cs), "cross_bconv_ex")
         units = B
@@ -497,17 +506,33 @@ def measure_component(workload, torch, dist, world, rank, local, steps, warmup, 
                 "kernel": "k_bconv_tc (Barrett) / k_bconv_var (variants), one launch per step"}
     for _ in range(warmup):
         step()
-    ms = timer(step, steps)
+    torch.cuda.synchronize()
     l0 = lib.cross_launch_count()
     step()
     torch.cuda.synchronize()
     launches = (lib.cross_launch_count() - l0) * steps
+    # the K timed steps captured once in a CUDA graph and replayed: device time
+    # without the host's per-call issue cost (one step of the N = 2^12
+    # transform is a few microseconds)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+        for _ in range(steps):
+            step()
+    graph.replay()
+    flush = torch.empty(int(2 * L2_BYTES) // 4, dtype=torch.int32, device=dev)
+    flush.fill_(1)                       # evict L2 before the timed replay
+    ms = timer(graph.replay, 1)
+    del flush
     value = world * units * steps / (ms / 1000.0)
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
             "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u32 residues, u64 intermediates",
-            "data": "synthetic seeded uniform residues", "config": {"workload": wl, "reduction": red,
-                                                                    "l2": "inputs larger than L2"},
+            "data": "synthetic seeded uniform residues",
+            "config": {"workload": wl, "reduction": red,
+                       "l2": "inputs larger than L2" if x.numel() * 4 > L2_BYTES else
+                             "each timed step on its own copy of the input (copies > 1.25 x L2 in all; L2 "
+                             "flushed before the timed replay)",
+                       "timing": "K steps captured in one CUDA graph, replayed once between CUDA events"},
             "gpu_launches": int(launches)}
     if e2e:
         e2e_step()
@@ -793,7 +818,7 @@ def run_ckks(args, torch, dist, world, rank, local):
 
 
 
-def measure_he(pt, torch, dist, world, rank, local, steps, warmup, e2e=True, cpu=True, roofline=True):
+def measure_he(pt, torch, dist, world, rank, local, steps, warmup, e2e=True, cpu=True, roofline=True, probe=True):
     """One HE operator point: each rank runs its share of pt.global_batch
     ciphertexts (inputs resident in HBM) in calls of pt.call_batch; CUDA events
     around the timed steps, max over ranks.  Returns the JSON line."""
@@ -848,7 +873,10 @@ def measure_he(pt, torch, dist, world, rank, local, steps, warmup, e2e=True, cpu
     ms = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
     he.check_device()
     value = pt.global_batch * steps / (ms / 1000.0)
-    sus, sus_src = int8_peak(torch, dev, sustained=True)
+    if probe:
+        sus, sus_src = int8_peak(torch, dev, sustained=True)
+    else:
+        sus, sus_src = 4500.0, "nominal B200 dense int8 (probe skipped)"
     ops_ct = pt.int8_ops_per_ct()
     per_gpu = value / world
     line = {
@@ -907,6 +935,72 @@ def measure_he(pt, torch, dist, world, rank, local, steps, warmup, e2e=True, cpu
         except Exception as exc:  # noqa: BLE001
             line["cpu_baseline"] = {"error": str(exc)}
     del he
+    torch.cuda.empty_cache()
+    return line
+
+
+def measure_he_limb(pt, torch, dist, world, rank, local, steps, warmup):
+    """HE-Mult with the limbs of every ciphertext split across the ranks
+    (cross_b200.limb_shard): each rank holds its Q' limbs (and the last limb
+    of Q) of all pt.global_batch ciphertexts and runs the three phases per
+    call of pt.call_batch ciphertexts, with the ModUp and ModDown limb
+    all-gathers over NCCL in between.  Returns the JSON line."""
+    from cross_b200 import _lib, hemul, limb_shard, shard
+    dev = torch.device("cuda", local)
+    lib = _lib.lib()
+    B, cb = pt.global_batch, max(1, min(pt.call_batch, pt.global_batch))
+    Q, P = moduli(pt)
+    ea, eb = keys(pt)
+    he = hemul.HEMul(cb, R, C, pt.dnum, 1, Q, P)
+    he.control_gen(degree_layout=(R, C))
+    he.setup_relinearization(ea, eb)
+    del ea, eb
+    sh = limb_shard.LimbShard(he, rank, world)
+    own_mods = Q[sh.q0:sh.q1] + [Q[-1]]
+    x = device_residues(torch, (B, 4, sh.nq + 1, N_DEG), own_mods, 100 + rank, dev, axis=2)
+    outs = [None] * (-(-B // cb))
+
+    def step():
+        torch.cuda.nvtx.range_push("hemul_limb")
+        for i, a in enumerate(range(0, B, cb)):
+            outs[i] = sh.mul(x[a:a + cb])
+        torch.cuda.nvtx.range_pop()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        l0 = lib.cross_launch_count()
+        h0 = time.time()
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        h1 = time.time()
+        launches = lib.cross_launch_count() - l0
+    ms = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
+    he.check_device()
+    value = B * steps / (ms / 1000.0)
+    cc_bytes = (world * sh.cq) * B * N_DEG * 4
+    kp_bytes = (world * sh.cp) * 2 * B * N_DEG * 4
+    line = {"metric": pt.metric + " limb-sharded", "value": value, "unit": pt.unit, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u32 residues, u64 intermediates, u8 BAT contractions",
+            "data": "synthetic seeded uniform residues",
+            "config": {"workload": pt.describe(B) + ", limbs split across the GPUs", "global_batch": B,
+                       "call_batch": cb, "L": pt.L, "K": pt.K, "dnum": pt.dnum,
+                       "parallelism": f"limb-sharded x{world}: Q' limbs [{sh.q0}, {sh.q1}), P limbs [{sh.p0}, "
+                                      f"{sh.p1}) on rank {rank}; ModUp and ModDown all-gathers over NCCL",
+                       "allgather_bytes_per_step": cc_bytes + kp_bytes},
+            "gpu_launches": int(launches), "clocks": clk.summary(h0, h1),
+            "e2e": None, "e2e_note": "inputs are resident per rank by limb (no host-buffer API for a limb split)"}
+    del x, outs, sh, he
     torch.cuda.empty_cache()
     return line
 
@@ -1000,12 +1094,17 @@ def main():
     ap.add_argument("--impl", default="cross_b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the other configurations on one GPU")
+    ap.add_argument("--lean", action="store_true",
+                    help="time the HE step only: no end-to-end pass, roofline NTT, tensor-core probe, CPU baseline "
+                         "or other configurations (small profiler captures)")
     ap.add_argument("--workload", choices=["hemul", "herot", "ntt", "bconv", "ckks", "bts", "i8peak"], default="hemul")
     ap.add_argument("--limbs", type=int, default=BOX.L, help="L of the HE-Mult / HE-Rotate point")
     ap.add_argument("--special", type=int, default=BOX.K, help="K of the HE-Mult / HE-Rotate point")
     ap.add_argument("--dnum", type=int, default=BOX.dnum, help="key-switch digits of the HE-Mult / HE-Rotate point")
     ap.add_argument("--global-batch", type=int, default=BOX.global_batch, help="ciphertexts per step over all GPUs")
     ap.add_argument("--call-batch", type=int, default=BOX.call_batch, help="ciphertexts per operator call")
+    ap.add_argument("--shard", choices=["batch", "limb"], default="batch",
+                    help="split the ciphertexts (batch) or the limbs of every ciphertext (limb) across GPUs")
     ap.add_argument("--bts-batch", type=int, default=1, help="polynomials per call of the bootstrapping mix")
     ap.add_argument("--bts-log", default=None, help="write the mix's latency lines (tabIX.py format) here")
     ap.add_argument("--bts-layout", choices=["native", "reference"], default="native")
@@ -1031,10 +1130,17 @@ def main():
     if args.workload not in ("hemul", "herot"):
         {"ckks": run_ckks, "bts": run_bts, "i8peak": run_i8peak}.get(args.workload, run_component)(
             args, torch, dist, world, rank, local)
+    elif args.shard == "limb":
+        if pt.workload != "hemul":
+            raise SystemExit("--shard limb is implemented for HE-Mult")
+        line = measure_he_limb(pt, torch, dist, world, rank, local, args.steps, args.warmup)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
     else:
-        line = measure_he(pt, torch, dist, world, rank, local, args.steps, args.warmup,
-                          cpu=not args.no_cpu_baseline)
-        if world == 1 and not args.no_configs and pt == BOX:
+        lean = args.lean
+        line = measure_he(pt, torch, dist, world, rank, local, args.steps, args.warmup, e2e=not lean,
+                          cpu=not (args.no_cpu_baseline or lean), roofline=not lean, probe=not lean)
+        if world == 1 and not (args.no_configs or lean) and pt == BOX:
             line["configs"] = other_configs(torch, local)
         if rank == 0:
             print(json.dumps(line), flush=True)

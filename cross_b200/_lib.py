@@ -43,6 +43,11 @@ class RescaleDesc(C.Structure):
                 ("inv_psi_last", vp), ("gamma_psi", vp), ("betas", vp)]
 
 
+class HemulShardDesc(C.Structure):
+    _fields_ = [("plan", vp), ("q_begin", i32), ("q_end", i32), ("p_begin", i32), ("p_end", i32),
+                ("ks_bconv", C.POINTER(vp)), ("down_bconv", vp)]
+
+
 class HerotDesc(C.Structure):
     _fields_ = [("r", i32), ("c", i32), ("L", i32), ("K", i32), ("dnum", i32),
                 ("ntt_qp", vp), ("ks_bconv", C.POINTER(vp)), ("down_bconv", vp),
@@ -103,6 +108,12 @@ _SIGS = {
     "cross_hemul_plan_destroy": (i32, [vp]),
     "cross_hemul_workspace_size": (sz, [vp, i64, i32]),
     "cross_hemul": (i32, [vp, vp, vp, i64, i32, vp, sz, vp]),
+    "cross_hemul_shard_create": (i32, [C.POINTER(HemulShardDesc), C.POINTER(vp)]),
+    "cross_hemul_shard_destroy": (i32, [vp]),
+    "cross_hemul_shard_workspace_size": (sz, [vp, i64]),
+    "cross_hemul_shard_modup_input": (i32, [vp, vp, i64, vp, vp, sz, vp]),
+    "cross_hemul_shard_keyswitch": (i32, [vp, vp, i64, vp, vp, sz, vp]),
+    "cross_hemul_shard_moddown": (i32, [vp, vp, i64, vp, vp, sz, vp]),
     "cross_herot_plan_create": (i32, [C.POINTER(HerotDesc), C.POINTER(vp)]),
     "cross_herot_set_keys": (i32, [vp, vp, vp, vp]),
     "cross_herot_plan_destroy": (i32, [vp]),

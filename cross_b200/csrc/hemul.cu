@@ -1001,3 +1001,307 @@ int cross_rescale(cross_rescale_plan P, const uint32_t* in, uint32_t* out, int64
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// HE-Mult sharded by RNS limb (one rank per GPU).  Rank g owns the Q' limbs
+// [q0, q1) and the P limbs [p0, p1) of every ciphertext and computes exactly
+// the per-limb operations of cross_hemul for them, so its output limbs are
+// bit-identical to the one-GPU result.  The key switch needs two exchanges,
+// done by the caller between the phases (an all-gather over the ranks):
+//   1. ModUp: every digit's limbs of INTT(d2) psi^-i in coefficient form
+//      (cc, limb-outer: Q' limb l at index l);
+//   2. ModDown: the P limbs of INTT(KS) psi^-i of both elements (kp, limb-outer:
+//      P limb k at index k).
+// Everything else -- rescale, tensor product, the ModUp basis conversions into
+// the rank's own limbs, the NTTs, the inner product and the ModDown tail -- is
+// limb-local.
+// ---------------------------------------------------------------------------
+
+struct cross_hemul_shard_s {
+  const cross_hemul_plan_s* P = nullptr;
+  int q0 = 0, q1 = 0, p0 = 0, p1 = 0, nq = 0, np = 0, lt = 0;
+  std::vector<cross_bconv_plan_s*> ks;          // per digit (nullptr when the rank has no target)
+  std::vector<int> ns;                          // targets per digit
+  std::vector<std::vector<int>> tgt_dle;        // targets per digit, indices in Q' + P
+  cross_bconv_plan_s* down = nullptr;
+  ModC* mods_own = nullptr;                     // [lt] own Q' then own P
+  uint16_t *m_q = nullptr, *m_p = nullptr, *rows_p = nullptr;
+  std::vector<uint16_t*> tgt_plan, tgt_rows;
+  std::vector<int> q_rows_host;                 // q0 .. q1 - 1
+  int16_t* src = nullptr;                       // [parts][lt]
+  uint32_t *evk_a = nullptr, *evk_b = nullptr;  // [parts][lt][N]
+};
+
+namespace {
+
+struct ShardBufs {
+  uint32_t *LL, *R, *D, *KS, *F, *tmp;
+  std::vector<uint32_t*> E;
+};
+
+void shard_layout(const cross_hemul_shard_s* S, int64_t B, Arena& a, ShardBufs& b) {
+  const int64_t N = S->P->N;
+  b.LL = a.take<uint32_t>((size_t)B * 4 * N);
+  b.R = a.take<uint32_t>((size_t)B * 4 * S->nq * N);
+  b.D = a.take<uint32_t>((size_t)B * 3 * S->nq * N);
+  b.E.clear();
+  int64_t tw = B * 4 * std::max(S->nq, 1);
+  for (size_t j = 0; j < S->ns.size(); ++j) {
+    b.E.push_back(a.take<uint32_t>((size_t)B * S->ns[j] * N));
+    tw = std::max<int64_t>(tw, B * S->ns[j]);
+  }
+  b.KS = a.take<uint32_t>((size_t)B * 2 * S->lt * N);
+  b.F = a.take<uint32_t>((size_t)B * 2 * S->nq * N);
+  tw = std::max<int64_t>(tw, B * 2 * std::max(S->nq, S->np));
+  b.tmp = a.take<uint32_t>((size_t)std::max(ntt_tmp_words(S->P->ntt_qp, tw), ntt_tmp_words(S->P->ntt_p, tw)));
+}
+
+int shard_ws_check(const cross_hemul_shard_s* S, int64_t B, void* ws, size_t bytes, ShardBufs& b, const char* who) {
+  Arena q(nullptr, 0);
+  shard_layout(S, B, q, b);
+  if (!ws || bytes < q.off) {
+    set_error("%s: workspace of %zu bytes required, %zu given", who, q.off, bytes);
+    return CROSS_ERR_WORKSPACE;
+  }
+  Arena a(ws, bytes);
+  shard_layout(S, B, a, b);
+  return CROSS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cross_hemul_shard_destroy(cross_hemul_shard S) {
+  if (!S) return CROSS_OK;
+  for (void* p : {(void*)S->mods_own, (void*)S->m_q, (void*)S->m_p, (void*)S->rows_p, (void*)S->src,
+                  (void*)S->evk_a, (void*)S->evk_b})
+    dfree(p);
+  for (auto* p : S->tgt_plan) dfree(p);
+  for (auto* p : S->tgt_rows) dfree(p);
+  delete S;
+  return CROSS_OK;
+}
+
+int cross_hemul_shard_create(const cross_hemul_shard_desc* d, cross_hemul_shard* out) {
+  CROSS_REQUIRE(d && out && d->plan, "cross_hemul_shard_create: null argument");
+  *out = nullptr;
+  const cross_hemul_plan_s* P = d->plan;
+  CROSS_REQUIRE(P->evk_a && P->evk_b, "cross_hemul_shard_create: the plan's keys are not set");
+  CROSS_REQUIRE(0 <= d->q_begin && d->q_begin <= d->q_end && d->q_end <= P->L1 && 0 <= d->p_begin &&
+                    d->p_begin <= d->p_end && d->p_end <= P->K,
+                "cross_hemul_shard_create: limb ranges [%d, %d) of Q' (%d) and [%d, %d) of P (%d) out of range",
+                d->q_begin, d->q_end, P->L1, d->p_begin, d->p_end, P->K);
+  auto* S = new cross_hemul_shard_s();
+  S->P = P;
+  S->q0 = d->q_begin; S->q1 = d->q_end; S->p0 = d->p_begin; S->p1 = d->p_end;
+  S->nq = S->q1 - S->q0; S->np = S->p1 - S->p0; S->lt = S->nq + S->np;
+  const int L1 = P->L1, LT = L1 + P->K;
+  auto fail = [&](const char* msg, int j) {
+    set_error("cross_hemul_shard_create: %s (%d)", msg, j);
+    cross_hemul_shard_destroy(S);
+    return CROSS_ERR_INVALID_ARG;
+  };
+  // own limbs in Q' + P order: Q' [q0, q1) then P [p0, p1) (dle indices)
+  std::vector<int> own;
+  for (int l = S->q0; l < S->q1; ++l) own.push_back(l);
+  for (int k = S->p0; k < S->p1; ++k) own.push_back(L1 + k);
+  const auto& mq = P->ntt_qp->mods_host;
+  auto dle_mod = [&](int l) { return l < L1 ? mq[l] : mq[P->L + (l - L1)]; };
+  std::vector<int16_t> src((size_t)P->parts * std::max(S->lt, 1), -1);
+  for (int j = 0; j < P->parts; ++j) {
+    std::vector<int> tg;
+    for (int l : own)
+      if (l < P->dstart[j] || l >= P->dstart[j] + P->dlen[j]) tg.push_back(l);
+    S->tgt_dle.push_back(tg);
+    S->ns.push_back((int)tg.size());
+    for (size_t i = 0; i < tg.size(); ++i)
+      for (int s = 0; s < S->lt; ++s)
+        if (own[s] == tg[i]) src[(size_t)j * S->lt + s] = (int16_t)i;
+    cross_bconv_plan_s* bc = d->ks_bconv ? d->ks_bconv[j] : nullptr;
+    if (!tg.empty()) {
+      if (!bc || bc->red != CROSS_REDUCTION_BARRETT || bc->sq != P->dlen[j] || bc->sp != (int)tg.size())
+        return fail("ks_bconv shape mismatch", j);
+      for (int i = 0; i < bc->sq; ++i)
+        if (!same_q(bc->src_host[i], dle_mod(P->dstart[j] + i))) return fail("ks_bconv source moduli", j);
+      for (size_t i = 0; i < tg.size(); ++i)
+        if (!same_q(bc->dst_host[i], dle_mod(tg[i]))) return fail("ks_bconv target moduli", j);
+    }
+    S->ks.push_back(tg.empty() ? nullptr : bc);
+  }
+  if (S->nq > 0) {
+    S->down = d->down_bconv;
+    if (!S->down || S->down->red != CROSS_REDUCTION_BARRETT || S->down->sq != P->K || S->down->sp != S->nq)
+      return fail("down_bconv shape mismatch", S->nq);
+    for (int k = 0; k < P->K; ++k)
+      if (!same_q(S->down->src_host[k], mq[P->L + k])) return fail("down_bconv source moduli", k);
+    for (int i = 0; i < S->nq; ++i)
+      if (!same_q(S->down->dst_host[i], mq[S->q0 + i])) return fail("down_bconv target moduli", i);
+  }
+  std::vector<ModC> mo;
+  for (int l : own) mo.push_back(dle_mod(l));
+  std::vector<uint16_t> mqv, mpv, rpv;
+  for (int l = S->q0; l < S->q1; ++l) { mqv.push_back((uint16_t)l); S->q_rows_host.push_back(l); }
+  for (int k = S->p0; k < S->p1; ++k) { mpv.push_back((uint16_t)(P->p_off + k)); rpv.push_back((uint16_t)k); }
+  int rc = CROSS_OK;
+  if (!mo.empty()) rc = upload_vec(&S->mods_own, mo);
+  if (!rc && !mqv.empty()) rc = upload_vec(&S->m_q, mqv);
+  if (!rc && !mpv.empty()) rc = upload_vec(&S->m_p, mpv);
+  if (!rc && !rpv.empty()) rc = upload_vec(&S->rows_p, rpv);
+  if (!rc) rc = upload_vec(&S->src, src);
+  for (int j = 0; j < P->parts && !rc; ++j) {
+    std::vector<uint16_t> tp, tr;
+    for (int l : S->tgt_dle[j]) { tr.push_back((uint16_t)l); tp.push_back((uint16_t)(l < L1 ? l : l + 1)); }
+    uint16_t *a = nullptr, *b = nullptr;
+    if (!tp.empty()) {
+      rc = upload_vec(&a, tp);
+      if (!rc) rc = upload_vec(&b, tr);
+    }
+    S->tgt_plan.push_back(a);
+    S->tgt_rows.push_back(b);
+  }
+  // the owned rows of the evaluation keys, [parts][lt][N]
+  const int64_t N = P->N;
+  if (!rc && S->lt > 0) {
+    const size_t words = (size_t)P->parts * S->lt * N;
+    CROSS_CHECK_CUDA(cudaMalloc(&S->evk_a, words * 4));
+    CROSS_CHECK_CUDA(cudaMalloc(&S->evk_b, words * 4));
+    for (int j = 0; j < P->parts && !rc; ++j)
+      for (int s = 0; s < S->lt; ++s) {
+        const size_t from = ((size_t)j * LT + own[s]) * N, to = ((size_t)j * S->lt + s) * N;
+        CROSS_CHECK_CUDA(cudaMemcpy(S->evk_a + to, P->evk_a + from, N * 4, cudaMemcpyDeviceToDevice));
+        CROSS_CHECK_CUDA(cudaMemcpy(S->evk_b + to, P->evk_b + from, N * 4, cudaMemcpyDeviceToDevice));
+      }
+  }
+  if (rc) {
+    cross_hemul_shard_destroy(S);
+    return rc;
+  }
+  *out = S;
+  return CROSS_OK;
+}
+
+size_t cross_hemul_shard_workspace_size(cross_hemul_shard S, int64_t batch) {
+  if (!S || batch < 0) return 0;
+  Arena a(nullptr, 0);
+  ShardBufs b;
+  shard_layout(S, batch, a, b);
+  return a.off;
+}
+
+int cross_hemul_shard_modup_input(cross_hemul_shard S, const uint32_t* in, int64_t B, uint32_t* cc_out, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  CROSS_REQUIRE(S && B >= 0 && (B == 0 || (in && (cc_out || S->nq == 0))), "cross_hemul_shard_modup_input: bad argument");
+  CROSS_REQUIRE((((uintptr_t)in | (uintptr_t)cc_out) & 15) == 0,
+                "cross_hemul_shard_modup_input: buffers must be 16-byte aligned");
+  if (B == 0 || S->nq == 0) return CROSS_OK;
+  ShardBufs b;
+  int rc = shard_ws_check(S, B, ws, ws_bytes, b, "cross_hemul_shard_modup_input");
+  if (rc) return rc;
+  const cross_hemul_plan_s* P = S->P;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t N = P->N;
+  const int nq = S->nq;
+  // 1. rescale of the owned limbs (ciphertext.py:267-303); in holds them at
+  //    slots 0 .. nq - 1 and the last limb of Q at slot nq
+  RescaleArgs ra{P->ntt_qp, P->m_last, P->m_zero, S->m_q, P->mods_dle + S->q0, P->inv_psi_last_t,
+                 P->gamma_psi_t + (int64_t)S->q0 * N, P->betas + S->q0, P->thr, P->q_last, nq + 1, N};
+  if ((rc = rescale_run(ra, in, (int64_t)(nq + 1) * N, b.R, b.LL, b.tmp, B * 4, st))) return rc;
+  // 2. tensor product (ciphertext.py:309-324)
+  const bool w32 = plan_w32(P->ntt_qp);
+  const int64_t nv = N / 4;
+  if (w32)
+    k_tensor_lm<true><<<dim3(gx_for(nv), gy_for(B * nq)), T, 0, st>>>(b.R, b.D, B, nq, N, P->mods_dle + S->q0);
+  else
+    k_tensor_lm<false><<<dim3(gx_for(nv), gy_for(B * nq)), T, 0, st>>>(b.R, b.D, B, nq, N, P->mods_dle + S->q0);
+  count_launch();
+  // 3. INTT(d2) x psi^-i into this rank's limbs of cc (limb-outer: [limb][ct][N])
+  Epi tw;
+  tw.op = EPI_MUL;
+  tw.tab = P->inv_psi_q_t;
+  tw.trow = S->m_q;
+  if ((rc = ntt_exec(P->ntt_qp, true, LP{b.D + 2 * (int64_t)nq * N, 3 * (int64_t)nq * N, N}, COEF_NATURAL,
+                     LPo{cc_out, N, B * N}, COEF_TRANSPOSED, B, nq, S->m_q, tw, b.tmp, st)))
+    return rc;
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_hemul_shard_keyswitch(cross_hemul_shard S, const uint32_t* cc_all, int64_t B, uint32_t* kp_out, void* ws,
+                                size_t ws_bytes, void* stream) {
+  CROSS_REQUIRE(S && B >= 0 && (B == 0 || (cc_all && (kp_out || S->np == 0))), "cross_hemul_shard_keyswitch: bad argument");
+  CROSS_REQUIRE((((uintptr_t)cc_all | (uintptr_t)kp_out) & 15) == 0,
+                "cross_hemul_shard_keyswitch: buffers must be 16-byte aligned");
+  if (B == 0 || S->lt == 0) return CROSS_OK;
+  ShardBufs b;
+  int rc = shard_ws_check(S, B, ws, ws_bytes, b, "cross_hemul_shard_keyswitch");
+  if (rc) return rc;
+  const cross_hemul_plan_s* P = S->P;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t N = P->N;
+  const int nq = S->nq;
+  // ModUp of every digit into the owned limbs outside it, x psi^i, NTT
+  PartPtrs pp{};
+  for (int j = 0; j < P->parts; ++j) {
+    const int ns = S->ns[j];
+    pp.e[j] = b.E[j];
+    pp.ps[j] = (int64_t)ns * N;
+    if (!ns) continue;
+    if ((rc = bconv_run(S->ks[j], true, cc_all + (int64_t)P->dstart[j] * B * N, N, B * N, 1, b.E[j], (int64_t)ns * N,
+                        N, 1, B, N, st, P->psi_qp_t, S->tgt_rows[j], S->tgt_dle[j].data())))
+      return rc;
+    if ((rc = ntt_exec(P->ntt_qp, false, LP{b.E[j], (int64_t)ns * N, N}, COEF_TRANSPOSED, LPo{b.E[j], (int64_t)ns * N, N},
+                       COEF_NATURAL, B, ns, S->tgt_plan[j], Epi{}, b.tmp, st)))
+      return rc;
+  }
+  // inner product with the evaluation key over the owned limbs
+  if ((rc = ks_inner(plan_w32(P->ntt_qp), LP{b.D + 2 * (int64_t)nq * N, 3 * (int64_t)nq * N, N}, pp, P->parts, S->src,
+                     S->lt, N, B, S->evk_a, S->evk_b, b.KS, S->mods_own, st)))
+    return rc;
+  // INTT of the owned P limbs of both elements x psi^-i into kp (limb-outer:
+  // [limb][ct element][N])
+  if (S->np > 0) {
+    Epi tw;
+    tw.op = EPI_MUL;
+    tw.tab = P->inv_psi_p_d;
+    tw.trow = S->rows_p;
+    if ((rc = ntt_exec(P->ntt_p, true, LP{b.KS + (int64_t)nq * N, (int64_t)S->lt * N, N}, COEF_NATURAL,
+                       LPo{kp_out, N, 2 * B * N}, P->down_layout, B * 2, S->np, S->m_p, tw, b.tmp, st)))
+      return rc;
+  }
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_hemul_shard_moddown(cross_hemul_shard S, const uint32_t* kp_all, int64_t B, uint32_t* out, void* ws,
+                              size_t ws_bytes, void* stream) {
+  CROSS_REQUIRE(S && B >= 0 && (B == 0 || S->nq == 0 || (kp_all && out)), "cross_hemul_shard_moddown: bad argument");
+  CROSS_REQUIRE((((uintptr_t)kp_all | (uintptr_t)out) & 15) == 0,
+                "cross_hemul_shard_moddown: buffers must be 16-byte aligned");
+  if (B == 0 || S->nq == 0) return CROSS_OK;
+  ShardBufs b;
+  int rc = shard_ws_check(S, B, ws, ws_bytes, b, "cross_hemul_shard_moddown");
+  if (rc) return rc;
+  const cross_hemul_plan_s* P = S->P;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t N = P->N;
+  const int nq = S->nq;
+  // BConv P -> owned Q' limbs x psi^i, then the NTT with the ModDown tail
+  // (hemul.py:175-215) and the add of (d0, d1)
+  if ((rc = bconv_run(S->down, true, kp_all, N, 2 * B * N, 1, b.F, (int64_t)nq * N, N, 1, B * 2, N, st, P->psi_q_d,
+                      S->m_q, S->q_rows_host.data())))
+    return rc;
+  Epi md;
+  md.op = EPI_MODDOWN;
+  md.x = View{b.KS, (int64_t)S->lt * N, 0, N, 1};
+  md.scal = P->pinv + S->q0;
+  md.base = View{b.D, 3 * (int64_t)nq * N, (int64_t)nq * N, N, 2};
+  md.base_mask = 3u;
+  if ((rc = ntt_exec(P->ntt_qp, false, LP{b.F, (int64_t)nq * N, N}, P->down_layout, LPo{out, (int64_t)nq * N, N},
+                     COEF_NATURAL, B * 2, nq, S->m_q, md, b.tmp, st)))
+    return rc;
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+}  // extern "C"

@@ -221,6 +221,10 @@ int ntt_exec(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, LPo 
   const int64_t lps = polys * slots;
   if (lps == 0) return CROSS_OK;
   if (P->tc) return ntt_exec_tc(P, inverse, in, in_layout, out, out_layout, polys, slots, limbs, epi, tmp, st);
+  if (P->tc64 && in_layout == COEF_NATURAL && out_layout == COEF_NATURAL && epi.op == EPI_NONE &&
+      (((uintptr_t)in.p | (uintptr_t)out.p) & 15) == 0 && in.ps % 4 == 0 && in.ss % 4 == 0 && out.ps % 4 == 0 &&
+      out.ss % 4 == 0)
+    return ntt64_run(P, inverse, in, out, polys, slots, limbs, st);
   // CUDA-core path: natural-order transforms composed with the layout
   // conversions and the position-wise op.
   auto run = P->red == CROSS_REDUCTION_SHOUP ? ntt_run_shoup : ntt_run_dp4a;

@@ -221,15 +221,26 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
   tc_fence_after();
   uint32_t* o = a.out + (int64_t)w.poly * a.out_ps + (int64_t)w.slot * a.out_ss + p0;
   const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
+  // accumulator columns in quarters of 16 (four outputs): the next quarter's
+  // tcgen05.ld is in flight while the current quarter is reduced
+  const uint32_t tbase = tmem_acc + ((uint32_t)(quad * 32) << 16) + part * 64;
+  uint32_t va[16], vb[16];
+  tmem_ld16_issue(tbase, va);
+  tmem_wait16(va);
 #pragma unroll
   for (int chunk = 0; chunk < OUTS / 8; ++chunk) {
-    uint32_t v[32];
-    tmem_ld32(tmem_acc + ((uint32_t)(quad * 32) << 16) + part * 64 + chunk * 32, v);
     uint32_t res[8];
+    tmem_ld16_issue(tbase + chunk * 32 + 16, vb);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
+      if (j == 4) {
+        tmem_wait16(vb);
+        if (chunk + 1 < OUTS / 8) tmem_ld16_issue(tbase + (chunk + 1) * 32, va);
+      }
+      const uint32_t* v = j < 4 ? va : vb;
+      const int jv = j & 3;
       const int jj = chunk * 8 + j;
-      const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      const uint64_t z = combine4_mad(v[4 * jv], v[4 * jv + 1], v[4 * jv + 2], v[4 * jv + 3]);
       uint32_t r;
       if (RED == RED_MONTGOMERY)
         r = montgomery(z, q32, sc.vc.qinv);
@@ -302,6 +313,7 @@ __device__ __forceinline__ bool epilogue_tile(const Args& a, uint32_t tmem_acc, 
         *reinterpret_cast<uint4*>(base + (int64_t)(1 - odd) * nout) = odd ? hi : y;
       }
     }
+    if (chunk + 1 < OUTS / 8) tmem_wait16(va);
   }
   return true;
 }
@@ -926,6 +938,242 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
   return CROSS_ERR_UNSUPPORTED;
 }
 
+
+// ---------------------------------------------------------------------------
+// N = 2^12 (64 x 64): both contraction stages of a transform in one launch.
+// A CTA takes a pair of limb-polynomials of one plan limb (M = 128 rows, 64
+// per polynomial) and keeps everything in shared memory: the two stages' B
+// matrices (256 rows x 256 B each, TMA, SWIZZLE_128B), the stage-1 A tile
+// (written by the threads in the same swizzled K-major layout: transposed for
+// the forward transform, which contracts over r, as is for the inverse, which
+// contracts over c) and the stage-2 A tile, which the stage-1 epilogue writes
+// directly (byte recombination, Barrett, twiddle multiply, Barrett).  Per
+// stage 8 tcgen05.mma kind::i8 of M = 128, N = 256, K = 32 into one 256-column
+// TMEM accumulator; the stage-2 epilogue (recombination, Barrett) stores the
+// natural-order result.  Bounded waits as in k_bat_tc (codes 41 to 44).
+constexpr int T64_THREADS = 256;
+struct Smem64 {
+  uint8_t b1[2][256 * 128];    // stage-1 B: two 128-byte K chunks of 256 rows
+  uint8_t b2[2][256 * 128];    // stage-2 B
+  uint8_t a1[2][128 * 128];    // stage-1 A: two K chunks of 128 rows
+  uint8_t a2[2][128 * 128];    // stage-2 A
+  uint64_t bbar, mbar, drain;
+  uint32_t tmem_base;
+  volatile int abort;
+};
+constexpr size_t SMEM64_BYTES = sizeof(Smem64) + 1024;
+static_assert(SMEM64_BYTES <= 232448, "k_ntt64 shared memory exceeds 227 KiB");
+
+struct Args64 {
+  LP in;
+  LPo out;
+  int64_t polys;
+  int slots;
+  const uint16_t* limbs;
+  const ModC* mods;
+  const uint32_t* tw;   // forward: tf_step2 [limb][z][c]; inverse: intt_tf_step2 transposed [limb][l][r]
+  int* err;
+};
+
+// byte offset of (row, 16-byte chunk k16 of the 256-byte K extent) in a
+// 128-row, two-chunk SWIZZLE_128B K-major tile
+__device__ __forceinline__ uint32_t sw_off(int row, int k16) {
+  return (uint32_t)((k16 >> 3) * (128 * 128) + (row >> 3) * 1024 + (row & 7) * 128 + (((k16 & 7) ^ (row & 7)) << 4));
+}
+
+// Issue the 8 MMAs of one stage (A: 128 rows x 256 B, B: 256 rows x 256 B) and commit.
+__device__ __forceinline__ void ntt64_mma(uint32_t tmem, const uint8_t* a, const uint8_t* b, uint64_t* bar) {
+#pragma unroll
+  for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      mma_i8(tmem, sw128_desc(saddr(a + kc * 128 * 128) + 32 * k), sw128_desc(saddr(b + kc * 256 * 128) + 32 * k),
+             (kc | k) != 0);
+  mma_commit(bar);
+}
+
+template <bool INV, bool FAST>
+__global__ void __launch_bounds__(T64_THREADS, 1)
+    k_ntt64(const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2, const Args64 a) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem64& S = *reinterpret_cast<Smem64*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int64_t pairs = (a.polys + 1) / 2;
+  const int64_t total = (int64_t)a.slots * pairs;
+  const int64_t i0 = total * blockIdx.x / gridDim.x, i1 = total * (blockIdx.x + 1) / gridDim.x;
+  if (t == 0) {
+    mbar_init(&S.bbar, 1);
+    mbar_init(&S.mbar, 1);
+    mbar_init(&S.drain, 1);
+    S.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB1) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB2) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&S.tmem_base)),
+                 "r"(256)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+  uint32_t bphase = 0, mphase = 0;
+  int cur_slot = -1;
+  // epilogue role: TMEM lane quadrant q = warp % 4 (rows 32 q .. 32 q + 31),
+  // output half h = warp / 4 (accumulator columns 128 h .. 128 h + 127)
+  const int q = warp & 3, h = warp >> 2;
+  const int m = 32 * q + lane, mp = m >> 6, mm = m & 63;
+  for (int64_t it = i0; it < i1; ++it) {
+    const int slot = (int)(it / pairs);
+    const int64_t p0 = 2 * (it - (int64_t)slot * pairs);
+    const bool two = p0 + 1 < a.polys;
+    const int limb = a.limbs[slot];
+    if (slot != cur_slot && t == 0) {
+      // the MMAs that read the previous slot's B tiles have completed (waited below)
+      mbar_expect_tx(&S.bbar, 4 * 256 * 128);
+      for (int kc = 0; kc < 2; ++kc) {
+        tma_load_2d(S.b1[kc], &tmB1, &S.bbar, kc * 128, limb * 256);
+        tma_load_2d(S.b2[kc], &tmB2, &S.bbar, kc * 128, limb * 256);
+      }
+    }
+    // stage-1 A tile from global memory
+#pragma unroll
+    for (int pp = 0; pp < 2; ++pp) {
+      if (pp == 1 && !two) break;
+      const uint32_t* x = a.in.p + (p0 + pp) * a.in.ps + (int64_t)slot * a.in.ss;
+      if (!INV) {
+        // forward: A rows c, K words r (the transpose of X[r][c])
+        const int c = t & 63, rg = t >> 6;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r0 = 16 * i + 4 * rg;
+          uint4 v;
+          v.x = __ldg(x + (r0 + 0) * 64 + c);
+          v.y = __ldg(x + (r0 + 1) * 64 + c);
+          v.z = __ldg(x + (r0 + 2) * 64 + c);
+          v.w = __ldg(x + (r0 + 3) * 64 + c);
+          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(pp * 64 + c, r0 >> 2)) = v;
+        }
+      } else {
+        // inverse: A rows r, K words c (X as stored)
+        const int c4 = t & 15;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = (t >> 4) + 16 * i;
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + r * 64) + c4);
+          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(pp * 64 + r, c4)) = v;
+        }
+      }
+    }
+    // stage-1 twiddles of this thread's outputs, in flight during the MMA
+    const ModC mc = a.mods[limb];
+    const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
+    uint32_t tw[32];
+    {
+      const uint32_t* tb = a.tw + (int64_t)limb * 4096 + mm;
+#pragma unroll
+      for (int o = 0; o < 32; ++o) tw[o] = __ldg(tb + (32 * h + o) * 64);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (t == 0) {
+      bool ok = true;
+      if (slot != cur_slot) {
+        ok = mbar_wait(&S.bbar, bphase, S.abort, a.err, 41);
+        bphase ^= 1;
+      }
+      if (ok) {
+        tc_fence_after();
+        ntt64_mma(tmem, &S.a1[0][0], &S.b1[0][0], &S.mbar);
+        if (!mbar_wait(&S.mbar, mphase, S.abort, a.err, 42)) S.abort = 1;
+      } else {
+        S.abort = 1;
+      }
+    }
+    cur_slot = slot;
+    mphase ^= 1;
+    __syncthreads();
+    if (S.abort) break;
+    tc_fence_after();
+    // stage-1 epilogue: Y = Barrett(Barrett(sum) x twiddle) into the stage-2 A tile
+    // (row: output index o of this polynomial, K word: this thread's row mm)
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128 * h + 32 * ch, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int o = 32 * h + 8 * ch + j;
+        const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        const uint32_t wv = tw[8 * ch + j];
+        uint32_t r;
+        if (FAST) {
+          r = reduce_fast(z, q32, m32, sw);
+          r = reduce_fast2(r * wv, __umulhi(r, wv), q32, m32, sw);
+        } else {
+          r = barrett(z, mc);
+          r = barrett((uint64_t)r * wv, mc);
+        }
+        *reinterpret_cast<uint32_t*>(&S.a2[0][0] + sw_off(mp * 64 + o, mm >> 2) + 4 * (mm & 3)) = r;
+      }
+    }
+    tc_fence_before();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (t == 0) {
+      tc_fence_after();
+      ntt64_mma(tmem, &S.a2[0][0], &S.b2[0][0], &S.mbar);
+      if (!mbar_wait(&S.mbar, mphase, S.abort, a.err, 43)) S.abort = 1;
+    }
+    mphase ^= 1;
+    __syncthreads();
+    if (S.abort) break;
+    tc_fence_after();
+    // stage-2 epilogue: Barrett, natural-order stores of this polynomial
+    const bool store = mp == 0 || two;
+    uint32_t* y = a.out.p + (p0 + mp) * a.out.ps + (int64_t)slot * a.out.ss;
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128 * h + 32 * ch, v);
+      uint32_t res[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        res[j] = FAST ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
+      }
+      if (store) {
+        const int o0 = 32 * h + 8 * ch;
+        if (!INV) {
+          // forward: Z[z][n], this thread's row z = mm, outputs n = o0 .. o0 + 7
+          uint4* d = reinterpret_cast<uint4*>(y + mm * 64 + o0);
+          d[0] = make_uint4(res[0], res[1], res[2], res[3]);
+          d[1] = make_uint4(res[4], res[5], res[6], res[7]);
+        } else {
+          // inverse: Z[l][c], this thread's column c = mm, rows l = o0 .. o0 + 7
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[(o0 + j) * 64 + mm] = res[j];
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (t == 0 && S.abort) {
+    // let anything still in flight land before TMEM is freed and the CTA exits
+    mma_commit(&S.drain);
+    const uint64_t t0 = globaltimer();
+    while (!mbar_test(&S.drain, 0) && globaltimer() - t0 < WAIT_NS) __nanosleep(100);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+}
+
 }  // namespace tc
 
 bool tc_supported(int r, int c) {
@@ -960,7 +1208,10 @@ void pack_tc(const uint8_t* bat, int X, int Y, int M, bool x_is_out, std::vector
 
 int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, const uint8_t* intt1,
                  const uint8_t* intt3, const uint32_t* intt_tw) {
-  if (!tc_supported(P->r, P->c)) return CROSS_OK;
+  // 64 x 64 Barrett plans (N = 2^12) get the single-launch kernel k_ntt64 for
+  // their plain transforms (the B matrices and maps below serve both kernels)
+  const bool n64 = P->r == 64 && P->c == 64 && P->red == CROSS_REDUCTION_BARRETT;
+  if (!tc_supported(P->r, P->c) && !n64) return CROSS_OK;
   int rc = tc::init_driver();
   if (rc) return rc;
   const int R = P->r, C = P->c, M = P->M;
@@ -998,7 +1249,8 @@ int tc_plan_init(cross_ntt_plan_s* P, const uint8_t* ntt1, const uint8_t* ntt3, 
   bool fast = true;
   for (const ModC& mc : P->mods_host) fast = fast && reduce_fast_ok(mc);
   P->tc_fast = fast ? 1 : 0;
-  P->tc = true;
+  P->tc = !n64;
+  P->tc64 = n64;
   return CROSS_OK;
 }
 
@@ -1055,6 +1307,28 @@ int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, L
   // or Z^T[c'][l'] = out[m][n] (transposed)
   return tc::stage(P, P->tm_col_inv, P->tm2_col_inv, out_layout == COEF_NATURAL, epi, t1, slots * N, N, C, R, R, out, polys, slots,
                    limbs, st);
+}
+
+// NTT / INTT of polys x slots limb-polynomials of a 64 x 64 plan, natural
+// coefficient order on both sides, in one launch.
+int ntt64_run(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
+              const uint16_t* limbs, cudaStream_t st) {
+  const int64_t total = (int64_t)slots * ((polys + 1) / 2);
+  if (total == 0) return CROSS_OK;
+  tc::Args64 a{in, out, polys, slots, limbs, P->mods, inverse ? P->tc_tw_inv : P->tw_fwd, P->tc_err};
+  const int sms = device_sm_count();
+  const unsigned grid = (unsigned)(total < sms ? total : sms);
+  const CUtensorMap& b1 = inverse ? P->tm_row_inv : P->tm_col_fwd;
+  const CUtensorMap& b2 = inverse ? P->tm_col_inv : P->tm_row_fwd;
+  auto go = [&](auto kern) -> int {
+    CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::SMEM64_BYTES));
+    kern<<<grid, tc::T64_THREADS, tc::SMEM64_BYTES, st>>>(b1, b2, a);
+    count_launch();
+    CROSS_CHECK_CUDA(cudaGetLastError());
+    return CROSS_OK;
+  };
+  if (P->tc_fast) return inverse ? go(tc::k_ntt64<true, true>) : go(tc::k_ntt64<false, true>);
+  return inverse ? go(tc::k_ntt64<true, false>) : go(tc::k_ntt64<false, false>);
 }
 
 }  // namespace cross

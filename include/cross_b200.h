@@ -442,6 +442,51 @@ int cross_hemul(cross_hemul_plan plan, const uint32_t* in, uint32_t* out, int64_
                 void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------ */
+/* HE-Mult sharded by RNS limb across GPUs                             */
+/* ------------------------------------------------------------------ */
+/* The reference shards only the ciphertext batch (util.py:40-58); for large
+ * parameter sets each GPU can instead own a contiguous range of the limbs of
+ * every ciphertext.  A shard computes exactly cross_hemul's per-limb
+ * operations (hemul.py:153-217) for its limbs, so its output limbs are
+ * bit-identical to the one-GPU result.  The key switch's two basis
+ * conversions need every digit's limbs (ModUp, ciphertext.py:486-498) and
+ * every P limb (ModDown, hemul.py:179-186) in coefficient form, which the
+ * caller exchanges between the phases (an all-gather over the ranks, e.g.
+ * NCCL over NVLink):
+ *   1. cross_hemul_shard_modup_input: in (B, 4, nq + 1, N) limb-major, the
+ *      owned Q' limbs then the last limb of Q -> cc_out (nq, B, N):
+ *      INTT(d2) psi^-i of the owned limbs, coefficient order transposed;
+ *   2. all-gather into cc_all, Q' limb l at cc_all + l * B * N;
+ *   3. cross_hemul_shard_keyswitch: cc_all -> kp_out (np, 2 B, N): the owned
+ *      P limbs of INTT(KS) psi^-i for both elements (e' = 2 b + e);
+ *   4. all-gather into kp_all, P limb k at kp_all + k * 2 * B * N;
+ *   5. cross_hemul_shard_moddown: kp_all -> out (B, 2, nq, N), limb-major.
+ * Q' is Q without its last modulus; nq = q_end - q_begin, np = p_end -
+ * p_begin.  The phases share the workspace (cross_hemul_shard_workspace_size)
+ * and must run in order on one stream per shard. */
+typedef struct cross_hemul_shard_s* cross_hemul_shard;
+typedef struct cross_hemul_shard_desc {
+  cross_hemul_plan plan;        /* the HE-Mult plan with its keys set          */
+  int q_begin, q_end;           /* owned limbs of Q'                            */
+  int p_begin, p_end;           /* owned limbs of P                             */
+  /* per key-switch digit j: BConv control digit j -> the owned limbs outside
+   * digit j (owned Q' limbs, then owned P limbs, in Q' + P order); NULL where a
+   * shard has no such limb */
+  cross_bconv_plan* ks_bconv;
+  cross_bconv_plan down_bconv;  /* P -> the owned Q' limbs; NULL when nq = 0   */
+} cross_hemul_shard_desc;
+
+int cross_hemul_shard_create(const cross_hemul_shard_desc* desc, cross_hemul_shard* out);
+int cross_hemul_shard_destroy(cross_hemul_shard shard);
+size_t cross_hemul_shard_workspace_size(cross_hemul_shard shard, int64_t batch);
+int cross_hemul_shard_modup_input(cross_hemul_shard shard, const uint32_t* in, int64_t batch, uint32_t* cc_out,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+int cross_hemul_shard_keyswitch(cross_hemul_shard shard, const uint32_t* cc_all, int64_t batch, uint32_t* kp_out,
+                                void* workspace, size_t workspace_bytes, void* stream);
+int cross_hemul_shard_moddown(cross_hemul_shard shard, const uint32_t* kp_all, int64_t batch, uint32_t* out,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ */
 /* HE-Rotate (herot.py)                                                */
 /* ------------------------------------------------------------------ */
 

@@ -65,6 +65,41 @@ def test_tensor_core_path_matches_cuda_core_path(monkeypatch):
     np.testing.assert_array_equal(z_tc, _np(cc.intt(y_tc)))
 
 
+@pytest.mark.parametrize("B,L", [(16, 8), (3, 5), (300, 1), (40, 8)])
+def test_ntt64_single_launch_vs_oracle(monkeypatch, B, L):
+    """N = 2^12 (64 x 64): the single-launch tensor-core transform (two
+    polynomials of one limb per CTA) against the oracle and against the
+    CUDA-core path, for the benchmark shape (16 x 8), an odd batch (the last
+    pair has one polynomial), CTAs that walk several pairs of one limb (300 x 1)
+    and CTAs whose pairs cross a limb boundary (40 x 8); limb-major through the
+    C ABI, in place, and in the reference layout through the context."""
+    import torch
+    from cross_b200 import _lib, ntt_mm
+    n = 4096
+    q = O.find_moduli_ntt(L, 28, 2 * n)
+    x = rng_residues(np.random.default_rng(B * 10 + L), (B, 64, 64, L), q)
+    ref = O.NTTBarrett(q, 64, 64)
+    yr = ref.ntt(x)
+    ctx = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 64, "c": 64})
+    np.testing.assert_array_equal(_np(ctx.ntt(x)), yr)
+    np.testing.assert_array_equal(_np(ctx.intt(yr)), ref.intt(yr))
+    lib = _lib.lib()
+    xl = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 3, 1, 2))).cuda()     # (B, L, 64, 64)
+    ws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), B, _lib.LAYOUT_LIMB_MAJOR), dtype=torch.uint8,
+                     device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.cross_ntt(ctx.plan(), 0, xl.data_ptr(), xl.data_ptr(), B, _lib.LAYOUT_LIMB_MAJOR, ws.data_ptr(),
+                             ws.numel(), st), "cross_ntt")
+    np.testing.assert_array_equal(_np(xl), yr.transpose(0, 3, 1, 2))
+    _lib.check(lib.cross_ntt(ctx.plan(), 1, xl.data_ptr(), xl.data_ptr(), B, _lib.LAYOUT_LIMB_MAJOR, ws.data_ptr(),
+                             ws.numel(), st), "cross_ntt")
+    np.testing.assert_array_equal(_np(xl), ref.intt(yr).transpose(0, 3, 1, 2))
+    ctx.check_device()
+    monkeypatch.setenv("CROSS_B200_DISABLE_TC", "1")
+    cc = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 64, "c": 64})
+    np.testing.assert_array_equal(_np(cc.ntt(x)), yr)
+
+
 @pytest.mark.parametrize("r,c,L,B", [(256, 256, 5, 5), (128, 128, 3, 5), (128, 256, 4, 3), (512, 128, 2, 3)])
 def test_two_sm_kernel_matches_one_sm_kernel(monkeypatch, r, c, L, B):
     """The cta_group::2 contraction (B half resident per CTA, K extent <= 256

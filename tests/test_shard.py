@@ -1,5 +1,6 @@
 """Multi-rank host logic of the batch sharding (cross_b200/shard.py) on CPU:
-world size 2 over gloo on 127.0.0.1, one spawned process per rank."""
+world size 2 over gloo on 127.0.0.1, one spawned process per rank, including a
+batch-sharded HE-Mult (the oracle's) that must equal the one-rank bytes."""
 import os
 import socket
 
@@ -43,6 +44,20 @@ def _worker(rank, world, port, q):
         batch = torch.arange(5 * 3, dtype=torch.int64).reshape(5, 3)
         out = shard.apply_sharded(lambda x: x * 7 + 1, batch, world, rank)
         assert torch.equal(out, batch * 7 + 1)
+        # a batch-sharded HE operator (the oracle's HEMul.mul, hemul.py:153-217)
+        # assembled on every rank equals the one-rank result byte for byte
+        import numpy as np
+        from oracle import cross_oracle as O
+        from tests.conftest import rng_residues
+        n, r, c, L, K, dnum, B = 1024, 32, 32, 4, 2, 2, 3
+        ov = O.find_moduli_ntt(L + K, 28, 2 * n)
+        rng = np.random.default_rng(9)
+        ct = rng_residues(rng, (B, 4, r, c, L), ov[:L])
+        he = O.HEMul(B, r, c, dnum, 1, ov[:L], ov[L:])
+        he.setup_relinearization(rng_residues(rng, (dnum, n, L + K), ov), rng_residues(rng, (dnum, n, L + K), ov))
+        mul = lambda x: torch.from_numpy(he.mul(x.numpy().view(np.uint32)).view(np.int32))  # noqa: E731
+        got = shard.apply_sharded(mul, torch.from_numpy(ct.view(np.int32)), world, rank)
+        assert np.array_equal(got.numpy().view(np.uint32), he.mul(ct))
         q.put((rank, "ok"))
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, repr(e)))
