@@ -66,6 +66,9 @@ _SIGS = {
     "cross_modmul": (i32, [vp, vp, i32, vp, i32, i64, vp, i64, vp]),
     "cross_tensor_product": (i32, [vp, vp, vp, vp, i64, i64, vp]),
     "cross_add_mod": (i32, [vp, vp, vp, vp, i64, i64, vp]),
+    "cross_ks_inner_product": (i32, [vp, C.POINTER(vp), i32, vp, vp, vp, i64, i64, i32, vp]),
+    "cross_moddown_sub_mul": (i32, [vp, vp, vp, vp, vp, vp, i64, vp]),
+    "cross_rescale_lift": (i32, [vp, vp, C.c_uint32, vp, vp, i64, i64, i32, vp]),
     "cross_automorphism": (i32, [vp, vp, vp, i64, i64, i32, vp]),
     "cross_to_limb_major": (i32, [vp, vp, i64, i64, i32, vp]),
     "cross_to_reference": (i32, [vp, vp, i64, i64, i32, vp]),

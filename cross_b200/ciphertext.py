@@ -331,16 +331,19 @@ class Ciphertext:
         self.ks_params["ct_ks_parts"] = [Ciphertext({**common, "num_moduli": len(ns)}, {**pc, "moduli": [dle[i] for i in ns]})
                                          for ns in non]
         self.ks_params["ct_drop_last_extend"] = Ciphertext({**common, "num_moduli": len(dle)}, {**pc, "moduli": dle})
-        ea = np.asarray(_tensor.to_numpy(evalkey_a)).astype(U64)
-        eb = np.asarray(_tensor.to_numpy(evalkey_b)).astype(U64)
+        ea = np.asarray(_tensor.to_numpy(evalkey_a)).astype(U32)
+        eb = np.asarray(_tensor.to_numpy(evalkey_b)).astype(U32)
         K = len(extend_moduli)
         Lc = len(cur)
-        cat = lambda e: np.concatenate([e[..., :Lc], e[..., e.shape[-1] - K:]], -1).reshape(-1, *self.degree_layout, len(dle))  # noqa: E731
+        cat = lambda e: np.ascontiguousarray(np.concatenate([e[..., :Lc], e[..., e.shape[-1] - K:]], -1).reshape(  # noqa: E731
+            -1, *self.degree_layout, len(dle)))
         self.ks_params["evk_a_precomp"] = _tensor.torch().from_numpy(cat(ea)).to(_tensor.device())
         self.ks_params["evk_b_precomp"] = _tensor.torch().from_numpy(cat(eb)).to(_tensor.device())
+        self.ks_params["ff_drop_last_extend"] = ff_context.BarrettContext(moduli=dle)
 
     def key_switch(self):
-        """ciphertext.py:455-519."""
+        """ciphertext.py:455-519; the inner product with the evaluation key
+        (:506-518) is cross_ks_inner_product."""
         if not hasattr(self, "ks_params"):
             raise RuntimeError("Key switch parameters not initialized. Call key_switch_control_gen first.")
         t = _t()
@@ -350,7 +353,7 @@ class Ciphertext:
         self.modmul(p["power_of_inv_psi_arr_drop_last"])
         coef = self.ciphertext
         take = lambda x, idx: x.view(t.int32)[..., list(idx)].contiguous().view(t.uint32)  # noqa: E731
-        res0 = res1 = None
+        exts = []
         for part in range(p["numPartQl"]):
             sel, ns = p["select_tower_index_overall"][part], p["non_select_tower_index_overall"][part]
             tw = np.ascontiguousarray(p["drop_last_power_of_psi"][..., ns])
@@ -360,15 +363,17 @@ class Ciphertext:
             cp.modmul(tw)
             cp.to_ntt_form()
             ext = t.cat([take(input_ntt, sel).view(t.int32), cp.ciphertext.view(t.int32)], -1)
-            ext = ext[..., list(p["restore_indices"][part])].contiguous().view(t.uint32)
-            e64 = _u64(ext).view(t.int64)
-            kb = p["evk_b_precomp"][part][None, None].view(t.int64)
-            ka = p["evk_a_precomp"][part][None, None].view(t.int64)
-            r0, r1 = e64 * kb, e64 * ka
-            res0 = r0 if res0 is None else res0 + r0
-            res1 = r1 if res1 is None else res1 + r1
-        result = t.cat([res0, res1], 1).view(t.uint64)
+            exts.append(ext[..., list(p["restore_indices"][part])].contiguous().view(t.uint32))
+        # res0 = sum_j ext_j evk_b[j], res1 = sum_j ext_j evk_a[j] in uint64, then
+        # mod_reduce of the concatenation (ciphertext.py:508-518)
+        B = exts[0].shape[0]
+        LT = exts[0].shape[-1]
+        n = exts[0].numel() // (B * LT)
+        result = _tensor.empty_u32((B, 2, *exts[0].shape[2:]))
+        ptrs = (_lib.vp * len(exts))(*[e.data_ptr() for e in exts])
+        _tensor.call("cross_ks_inner_product", p["ff_drop_last_extend"].handle(), ptrs, len(exts),
+                     p["evk_a_precomp"].data_ptr(), p["evk_b_precomp"].data_ptr(), result.data_ptr(), B, n,
+                     _lib.LAYOUT_REFERENCE, _lib.cuda_stream())
         cd = p["ct_drop_last_extend"]
         cd.set_batch_ciphertext(result)
-        cd.mod_reduce()
         self.set_batch_ciphertext(cd.get_batch_ciphertext())

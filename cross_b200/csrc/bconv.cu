@@ -659,23 +659,38 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
     const size_t sm = bconv_tc_smem(P->sq, P->sp, P->tc_kb, P->tc_nn, a.tmem_cols, (size_t)sm_bytes, &ctas);
     static const bool generic_only = getenv("CROSS_B200_BCONV_GENERIC") && getenv("CROSS_B200_BCONV_GENERIC")[0] == '1';
     if (sm && P->tc_fast && P->tc_src_fast && (!twist || trow_host) && !generic_only) {
-      BconvTccArgs c{in, in_ps, in_ls, out, out_ps, out_ls, (int)polys, (int)n, P->sq, P->sp, P->tc_kb, P->tc_nn,
-                     a.tmem_cols, P->tc_bimg, P->err, {}};
-      for (int i = 0; i < P->sq; ++i) {
-        const ModC& mc = P->src_host[i];
-        c.k.sq_q[i] = (uint32_t)mc.q;
-        c.k.sq_m[i] = (uint32_t)mc.m;
-        c.k.sq_sw[i] = mc.s_w;
-        c.k.sq_hi[i] = P->qhat_inv_host[i];
+      // targets [j0, j1) from image bimg of MMA width nn
+      auto run = [&](int j0, int j1, const uint8_t* bimg, int nn) -> int {
+        BconvTccArgs c{in, in_ps, in_ls, out + (int64_t)j0 * out_ls, out_ps, out_ls, (int)polys, (int)n, P->sq,
+                       j1 - j0, P->tc_kb, nn, 64, bimg, P->err, {}};
+        while ((int)c.tmem_cols < nn) c.tmem_cols <<= 1;
+        int cpsm = 0;
+        const size_t smc = bconv_tc_smem(P->sq, j1 - j0, P->tc_kb, nn, c.tmem_cols, (size_t)sm_bytes, &cpsm);
+        if (!smc) {
+          set_error("bconv: no shared-memory split for size_p=%d", j1 - j0);
+          return CROSS_ERR_UNSUPPORTED;
+        }
+        for (int i = 0; i < P->sq; ++i) {
+          const ModC& mc = P->src_host[i];
+          c.k.sq_q[i] = (uint32_t)mc.q;
+          c.k.sq_m[i] = (uint32_t)mc.m;
+          c.k.sq_sw[i] = mc.s_w;
+          c.k.sq_hi[i] = P->qhat_inv_host[i];
+        }
+        for (int j = j0; j < j1; ++j) {
+          const ModC& mc = P->dst_host[j];
+          c.k.dq[j - j0] = (uint32_t)mc.q;
+          c.k.dm[j - j0] = (uint32_t)mc.m;
+          c.k.dsw[j - j0] = mc.s_w;
+          c.k.tp[j - j0] = twist ? twist + (int64_t)trow_host[j] * n : nullptr;
+        }
+        return twist ? launch_bconv_tcc_any<true>(c, smc, cpsm, st) : launch_bconv_tcc_any<false>(c, smc, cpsm, st);
+      };
+      if (P->tc_split && P->tc_bimg_half[0] && P->tc_bimg_half[1]) {
+        const int rc = run(0, P->tc_split, P->tc_bimg_half[0], P->tc_nn_half[0]);
+        return rc ? rc : run(P->tc_split, P->sp, P->tc_bimg_half[1], P->tc_nn_half[1]);
       }
-      for (int j = 0; j < P->sp; ++j) {
-        const ModC& mc = P->dst_host[j];
-        c.k.dq[j] = (uint32_t)mc.q;
-        c.k.dm[j] = (uint32_t)mc.m;
-        c.k.dsw[j] = mc.s_w;
-        c.k.tp[j] = twist ? twist + (int64_t)trow_host[j] * n : nullptr;
-      }
-      return twist ? launch_bconv_tcc_any<true>(c, sm, ctas, st) : launch_bconv_tcc_any<false>(c, sm, ctas, st);
+      return run(0, P->sp, P->tc_bimg, P->tc_nn);
     }
     if (sm) {
       const bool f = P->tc_fast != 0;
@@ -745,21 +760,32 @@ int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction
   P->qhat_inv_host = qi;
   // tensor-core B operand: row n = 4j + b, K byte 4i + a, in the K-major
   // no-swizzle core-matrix layout of k_bconv_tc (sq <= 32, sp <= 64)
-  std::vector<uint8_t> bimg;
+  std::vector<uint8_t> bimg, bimg_half[2];
   if (reduction == CROSS_REDUCTION_BARRETT && sq <= 32 && sp <= 64) {
     P->tc_kb = (sq + 7) / 8;
     P->tc_nn = (4 * sp + 15) / 16 * 16;
-    const int kb = P->tc_kb, nn = P->tc_nn;
-    bimg.assign((size_t)kb * (nn / 8) * 256, 0);
-    for (int n = 0; n < 4 * sp; ++n)
-      for (int i = 0; i < sq; ++i) {
-        const uint32_t word = bat[(size_t)n * sq + i];   // bat[j][b][i], n = 4j + b
-        for (int a = 0; a < 4; ++a) {
-          const int kbyte = 4 * i + a, k = kbyte / 32, kk = kbyte % 32;
-          bimg[(size_t)k * (nn / 8) * 256 + (n / 8) * 256 + (kk / 16) * 128 + (n % 8) * 16 + kk % 16] =
-              (uint8_t)(word >> (8 * a));
+    const int kb = P->tc_kb;
+    // image of the targets [j0, j1): row n = 4 (j - j0) + b, K byte 4i + a
+    auto image = [&](int j0, int j1, std::vector<uint8_t>& img) {
+      const int nn = (4 * (j1 - j0) + 15) / 16 * 16;
+      img.assign((size_t)kb * (nn / 8) * 256, 0);
+      for (int n = 0; n < 4 * (j1 - j0); ++n)
+        for (int i = 0; i < sq; ++i) {
+          const uint32_t word = bat[((size_t)4 * j0 + n) * sq + i];   // bat[j][b][i], row 4j + b
+          for (int a = 0; a < 4; ++a) {
+            const int kbyte = 4 * i + a, k = kbyte / 32, kk = kbyte % 32;
+            img[(size_t)k * (nn / 8) * 256 + (n / 8) * 256 + (kk / 16) * 128 + (n % 8) * 16 + kk % 16] =
+                (uint8_t)(word >> (8 * a));
+          }
         }
-      }
+      return nn;
+    };
+    image(0, sp, bimg);
+    if (4 * sp > 128) {
+      P->tc_split = (sp + 1) / 2;
+      P->tc_nn_half[0] = image(0, P->tc_split, bimg_half[0]);
+      P->tc_nn_half[1] = image(P->tc_split, sp, bimg_half[1]);
+    }
     bool fast = true;
     for (const ModC& mc : P->dst_host) fast = fast && reduce_fast_ok(mc);
     for (const ModC& mc : P->src_host) fast = fast && barrett_w32_ok(mc);
@@ -771,8 +797,10 @@ int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction
   std::vector<int> zero(1, 0);
   int rc = upload_vec(&P->src, P->src_host);
   if (!rc) rc = upload(&P->err, zero.data(), 1);
-  if (!rc && !bimg.empty() && !(getenv("CROSS_B200_DISABLE_TC") && getenv("CROSS_B200_DISABLE_TC")[0] == '1'))
+  if (!rc && !bimg.empty() && !(getenv("CROSS_B200_DISABLE_TC") && getenv("CROSS_B200_DISABLE_TC")[0] == '1')) {
     rc = upload_vec(&P->tc_bimg, bimg);
+    for (int h = 0; h < 2 && !rc && P->tc_split; ++h) rc = upload_vec(&P->tc_bimg_half[h], bimg_half[h]);
+  }
   if (!rc) rc = upload_vec(&P->dst, P->dst_host);
   if (!rc) rc = upload_vec(&P->qhat_inv, qi);
   if (!rc) rc = upload_vec(&P->bat, bat);
@@ -815,6 +843,8 @@ int cross_bconv_plan_destroy(cross_bconv_plan P) {
   dfree(P->bat);
   dfree(P->qhat_modp);
   dfree(P->tc_bimg);
+  dfree(P->tc_bimg_half[0]);
+  dfree(P->tc_bimg_half[1]);
   dfree(P->err);
   dfree(P->src_v);
   dfree(P->dst_v);

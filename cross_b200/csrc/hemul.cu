@@ -1305,3 +1305,149 @@ int cross_hemul_shard_moddown(cross_hemul_shard S, const uint32_t* kp_all, int64
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Standalone steps of the HE chains (each fused inside cross_hemul /
+// cross_herot), for callers that bind the reference's Ciphertext operators
+// one at a time.  Element-wise, one word per thread, grid-stride.
+// ---------------------------------------------------------------------------
+
+namespace cross {
+namespace {
+
+struct ExtPtrs {
+  const uint32_t* p[MAXPARTS];
+};
+
+// element e of a (rows x M) limb-innermost array or an (outer x M x n)
+// limb-major one: its limb index
+template <bool LM>
+__device__ __forceinline__ int limb_of(int64_t e, int M, int64_t n) {
+  return LM ? (int)((e / n) % M) : (int)(e % M);
+}
+
+template <bool LM>
+__global__ void k_ks_inner_any(ExtPtrs ext, int dnum, const uint32_t* __restrict__ evka, const uint32_t* __restrict__ evkb,
+                               uint32_t* __restrict__ out, int64_t batch, int64_t n, int M,
+                               const ModC* __restrict__ mods) {
+  const int64_t per = n * M, total = batch * per;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = e / per, w = e - b * per;   // w: position inside one ciphertext element
+    uint64_t s0 = 0, s1 = 0;
+    for (int j = 0; j < dnum; ++j) {
+      const uint64_t x = ext.p[j][e];
+      s0 += x * evkb[(int64_t)j * per + w];
+      s1 += x * evka[(int64_t)j * per + w];
+    }
+    const ModC mc = mods[limb_of<LM>(w, M, n)];
+    out[b * 2 * per + w] = barrett_any(s0, mc);
+    out[b * 2 * per + per + w] = barrett_any(s1, mc);
+  }
+}
+
+__global__ void k_moddown_sub_mul(const uint32_t* __restrict__ x, const uint32_t* __restrict__ y,
+                                  const uint32_t* __restrict__ pinv, const uint32_t* __restrict__ base,
+                                  uint32_t* __restrict__ out, int64_t rows, int M, const ModC* __restrict__ mods) {
+  const int64_t total = rows * M;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int l = (int)(e % M);
+    const ModC mc = mods[l];
+    const uint32_t q = (uint32_t)mc.q, a = x[e], b = y[e];
+    const uint32_t s = a < b ? a + q - b : a - b;                 // uint32 wrap, hemul.py:199-203
+    uint32_t t = barrett_any((uint64_t)s * pinv[l], mc);          // modmul(PInvModq), hemul.py:205-206
+    if (base) {
+      const uint32_t v = base[e] + t;                             // hemul.py:214-215
+      t = v >= q ? v - q : v;
+    }
+    out[e] = t;
+  }
+}
+
+template <bool LM>
+__global__ void k_rescale_lift_any(const uint32_t* __restrict__ last, uint32_t q_last, uint32_t thr,
+                                   const uint32_t* __restrict__ gpsi, uint32_t* __restrict__ out, int64_t polys,
+                                   int64_t n, int M, const ModC* __restrict__ mods) {
+  const int64_t per = n * M, total = polys * per;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = e / per, w = e - p * per;
+    const int l = limb_of<LM>(w, M, n);
+    const int64_t t = LM ? w % n : w / M;
+    const ModC mc = mods[l];
+    const uint32_t a = last[p * n + t];
+    const uint64_t lifted = a < thr ? (uint64_t)a : mc.q - (uint64_t)q_last + (uint64_t)a;   // ciphertext.py:285-290
+    out[e] = barrett_any(lifted * gpsi[w], mc);                                           // :291-295
+  }
+}
+
+unsigned ew_grid(int64_t total) {
+  const int64_t g = (total + T - 1) / T;
+  const int64_t cap = (int64_t)device_sm_count() * 16;
+  return (unsigned)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+}  // namespace
+}  // namespace cross
+
+extern "C" {
+
+int cross_ks_inner_product(cross_moduli moduli, const uint32_t* const* ext, int dnum, const uint32_t* evk_a,
+                           const uint32_t* evk_b, uint32_t* out, int64_t batch, int64_t n, int layout, void* stream) {
+  CROSS_REQUIRE(moduli && ext && evk_a && evk_b && out && batch >= 0 && n >= 1,
+                "cross_ks_inner_product: bad argument");
+  CROSS_REQUIRE(dnum >= 1 && dnum <= MAXPARTS, "cross_ks_inner_product: dnum=%d out of range 1..%d", dnum, MAXPARTS);
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR,
+                "cross_ks_inner_product: unknown layout %d", layout);
+  if (batch == 0) return CROSS_OK;
+  ExtPtrs e{};
+  for (int j = 0; j < dnum; ++j) {
+    CROSS_REQUIRE(ext[j], "cross_ks_inner_product: ext[%d] is null", j);
+    e.p[j] = ext[j];
+  }
+  const int M = moduli->n;
+  const int64_t total = batch * n * M;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (layout == CROSS_LAYOUT_LIMB_MAJOR)
+    k_ks_inner_any<true><<<ew_grid(total), T, 0, st>>>(e, dnum, evk_a, evk_b, out, batch, n, M, moduli->dev);
+  else
+    k_ks_inner_any<false><<<ew_grid(total), T, 0, st>>>(e, dnum, evk_a, evk_b, out, batch, n, M, moduli->dev);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_moddown_sub_mul(cross_moduli moduli, const uint32_t* x, const uint32_t* y, const uint32_t* p_inv_mod_q,
+                          const uint32_t* base, uint32_t* out, int64_t rows, void* stream) {
+  CROSS_REQUIRE(moduli && x && y && p_inv_mod_q && out && rows >= 0, "cross_moddown_sub_mul: bad argument");
+  if (rows == 0) return CROSS_OK;
+  const int64_t total = rows * moduli->n;
+  k_moddown_sub_mul<<<ew_grid(total), T, 0, (cudaStream_t)stream>>>(x, y, p_inv_mod_q, base, out, rows, moduli->n,
+                                                                   moduli->dev);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+int cross_rescale_lift(cross_moduli moduli, const uint32_t* last, uint32_t q_last, const uint32_t* gamma_psi,
+                       uint32_t* out, int64_t polys, int64_t n, int layout, void* stream) {
+  CROSS_REQUIRE(moduli && last && gamma_psi && out && polys >= 0 && n >= 1 && q_last >= 3,
+                "cross_rescale_lift: bad argument");
+  CROSS_REQUIRE(layout == CROSS_LAYOUT_REFERENCE || layout == CROSS_LAYOUT_LIMB_MAJOR,
+                "cross_rescale_lift: unknown layout %d", layout);
+  for (const ModC& mc : moduli->host)
+    CROSS_REQUIRE(mc.q + 1 > q_last, "cross_rescale_lift: target modulus %llu below q_last - 1",
+                  (unsigned long long)mc.q);
+  if (polys == 0) return CROSS_OK;
+  const int M = moduli->n;
+  const int64_t total = polys * n * M;
+  const uint32_t thr = (q_last + 1) / 2;                          // ciphertext.py:260
+  cudaStream_t st = (cudaStream_t)stream;
+  if (layout == CROSS_LAYOUT_LIMB_MAJOR)
+    k_rescale_lift_any<true><<<ew_grid(total), T, 0, st>>>(last, q_last, thr, gamma_psi, out, polys, n, M, moduli->dev);
+  else
+    k_rescale_lift_any<false><<<ew_grid(total), T, 0, st>>>(last, q_last, thr, gamma_psi, out, polys, n, M, moduli->dev);
+  count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  return CROSS_OK;
+}
+
+}  // extern "C"

@@ -68,6 +68,11 @@ struct cross_bconv_plan_s {
   int tc_src_fast = 0;              // reduce_fast is exact for every source modulus
   int tc_kb = 0, tc_nn = 0;         // K blocks of 8 source limbs, MMA N (4 sp rounded up to 16)
   uint8_t* tc_bimg = nullptr;       // B operand in its shared-memory image (K-major, no swizzle)
+  // 4 sp > 128 (an accumulator wider than 128 TMEM columns): the targets
+  // [0, tc_split) and [tc_split, sp) as two half images, converted by two
+  // launches of half the width (twice the CTAs per SM)
+  int tc_split = 0, tc_nn_half[2] = {0, 0};
+  uint8_t* tc_bimg_half[2] = {nullptr, nullptr};
   int* err = nullptr;               // device error word of the tensor-core kernel
   std::vector<cross::ModC> src_host, dst_host;
   cross::ModC* src = nullptr;       // [sq]

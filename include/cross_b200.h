@@ -127,6 +127,34 @@ int cross_modmul(cross_moduli moduli, const void* a, int a_is_u64, const void* b
 int cross_tensor_product(cross_moduli moduli, const uint32_t* ct, uint32_t* out01, uint32_t* out2,
                          int64_t batch, int64_t n, void* stream);
 
+/* The key-switch inner product of Ciphertext.key_switch (ciphertext.py:506-518,
+ * herot.py:236-246): ext[j] (j < dnum <= 16; a host array of device pointers) is
+ * digit j's extended ciphertext in restored limb order, (batch, n, M) for
+ * CROSS_LAYOUT_REFERENCE or (batch, M, n) for CROSS_LAYOUT_LIMB_MAJOR; evk_a,
+ * evk_b are the key's limbs in the same order, (dnum, n, M) or (dnum, M, n);
+ * out (batch, 2, n, M) or (batch, 2, M, n):
+ *   out[:, 0] = Barrett(sum_j ext[j] evk_b[j]),  out[:, 1] = Barrett(sum_j ext[j] evk_a[j]),
+ * the sums in uint64 with wrap-around.  moduli: the M limbs (Q' then P). */
+int cross_ks_inner_product(cross_moduli moduli, const uint32_t* const* ext, int dnum, const uint32_t* evk_a,
+                           const uint32_t* evk_b, uint32_t* out, int64_t batch, int64_t n, int layout, void* stream);
+
+/* The ModDown tail of hemul.py:199-207 and 214-215 (herot.py:277-296):
+ * x, y, out (rows, M), limbs last; s = x < y ? x + q - y : x - y in uint32,
+ * t = Barrett(s * p_inv_mod_q[m]) (p_inv_mod_q: device array of M, P^-1 mod q_m);
+ * out = base + t, minus q where that is >= q, when base (rows, M) is not NULL,
+ * else t. */
+int cross_moddown_sub_mul(cross_moduli moduli, const uint32_t* x, const uint32_t* y, const uint32_t* p_inv_mod_q,
+                          const uint32_t* base, uint32_t* out, int64_t rows, void* stream);
+
+/* The centred lift of rescale (ciphertext.py:279-295): last (polys, n) is the
+ * coefficient-form last limb (Barrett outputs of modulus q_last); gamma_psi
+ * holds gamma_i psi_i^t, (n, M) for CROSS_LAYOUT_REFERENCE or (M, n) for
+ * CROSS_LAYOUT_LIMB_MAJOR; out (polys, n, M) or (polys, M, n):
+ *   out = Barrett_i((last < (q_last + 1) / 2 ? last : q_i - q_last + last) * gamma_psi)
+ * with the lift in uint64.  moduli: the M = L - 1 remaining moduli. */
+int cross_rescale_lift(cross_moduli moduli, const uint32_t* last, uint32_t q_last, const uint32_t* gamma_psi,
+                       uint32_t* out, int64_t polys, int64_t n, int layout, void* stream);
+
 /* add.jax_add (add.py:7-27): a, b, out (elements, M, n); result a+b (uint32
  * wrap) minus q where it is strictly greater than q. */
 int cross_add_mod(cross_moduli moduli, const uint32_t* a, const uint32_t* b, uint32_t* out,

@@ -321,6 +321,94 @@ def test_key_switch_vs_oracle():
     np.testing.assert_array_equal(_np(ct.get_batch_ciphertext()), ref)
 
 
+def _lm(a):
+    """(..., n, M) -> (..., M, n)."""
+    return np.ascontiguousarray(np.swapaxes(a, -1, -2))
+
+
+@pytest.mark.parametrize("layout,full", [(0, False), (1, False), (0, True)])
+def test_ks_inner_product_entry_point(layout, full):
+    """cross_ks_inner_product (ciphertext.py:506-518): Barrett of the uint64
+    sums of digit-wise products; full-range words make the sums wrap as the
+    reference's uint64 arithmetic does."""
+    import torch
+    from cross_b200 import _lib, finite_field
+    n, M, dnum, B = 1024, 7, 5, 2
+    q = O.find_moduli_ntt(M, 28, 2 * n)
+    rng = np.random.default_rng(31 + layout + 2 * full)
+    draw = (lambda shape: rng.integers(0, 2 ** 32, size=shape, dtype=np.uint64).astype(U32)) if full else \
+        (lambda shape: rng_residues(rng, shape, q))
+    ext = [draw((B, n, M)) for _ in range(dnum)]
+    ea, eb = draw((dnum, n, M)), draw((dnum, n, M))
+    bar = O.Barrett(q)
+    s0 = sum(e.astype(np.uint64) * eb[j].astype(np.uint64) for j, e in enumerate(ext))
+    s1 = sum(e.astype(np.uint64) * ea[j].astype(np.uint64) for j, e in enumerate(ext))
+    want = np.stack([bar.reduce(s0), bar.reduce(s1)], 1)                          # (B, 2, n, M)
+    if layout == _lib.LAYOUT_LIMB_MAJOR:
+        ext, ea, eb, want = [_lm(e) for e in ext], _lm(ea), _lm(eb), _lm(want)
+    dev = [torch.from_numpy(e).cuda() for e in ext]
+    a, b = torch.from_numpy(ea).cuda(), torch.from_numpy(eb).cuda()
+    out = torch.empty(want.shape, dtype=torch.uint32, device="cuda")
+    ptrs = (_lib.vp * dnum)(*[d.data_ptr() for d in dev])
+    ff = finite_field.BarrettContext(q)
+    _lib.check(_lib.lib().cross_ks_inner_product(ff.handle(), ptrs, dnum, a.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                                 B, n, layout, None), "cross_ks_inner_product")
+    np.testing.assert_array_equal(_np(out), want)
+
+
+@pytest.mark.parametrize("with_base", [False, True])
+def test_moddown_sub_mul_entry_point(with_base):
+    """cross_moddown_sub_mul (hemul.py:199-207, 214-215): the uint32 subtract,
+    the P^-1 modmul and the final add with its >= q correction."""
+    import torch
+    from cross_b200 import _lib, finite_field
+    rows, M = 4096, 6
+    q = O.find_moduli_ntt(M, 28, 2 * 1024)
+    rng = np.random.default_rng(41 + with_base)
+    x = (rng.integers(0, 2 ** 31, size=(rows, M), dtype=np.uint64)).astype(U32)
+    y = rng_residues(rng, (rows, M), q)
+    pinv = rng_residues(rng, (1, M), q)[0]
+    base = rng_residues(rng, (rows, M), q)
+    qa = np.array(q, U32)
+    sub = np.where(x < y, x + qa - y, x - y)
+    t = O.Barrett(q).reduce(sub.astype(np.uint64) * pinv.astype(np.uint64)).astype(U32)
+    want = np.where(base + t >= qa, base + t - qa, base + t) if with_base else t
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    out = torch.empty((rows, M), dtype=torch.uint32, device="cuda")
+    xd, yd, pd, bd = d(x), d(y), d(pinv), d(base)
+    ff = finite_field.BarrettContext(q)          # owns the modulus set for the whole call
+    _lib.check(_lib.lib().cross_moddown_sub_mul(ff.handle(), xd.data_ptr(), yd.data_ptr(), pd.data_ptr(),
+                                                bd.data_ptr() if with_base else None, out.data_ptr(), rows, None),
+               "cross_moddown_sub_mul")
+    np.testing.assert_array_equal(_np(out), want)
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_rescale_lift_entry_point(layout):
+    """cross_rescale_lift (ciphertext.py:279-295): the centred lift of the last
+    limb (lazy Barrett values below 2 q_last) into every remaining modulus times
+    gamma_i psi_i^t."""
+    import torch
+    from cross_b200 import _lib, finite_field
+    n, L, polys = 2048, 6, 3
+    mods = O.find_moduli_ntt(L, 28, 2 * n)
+    qs, ql = mods[:-1], mods[-1]
+    rng = np.random.default_rng(51 + layout)
+    last = (rng.integers(0, 2 * ql, size=(polys, n), dtype=np.uint64)).astype(U32)
+    gpsi = rng_residues(rng, (n, L - 1), qs)
+    lifted = np.where(last[..., None] < (ql + 1) // 2, last[..., None].astype(np.uint64),
+                      np.array(qs, np.uint64) - np.uint64(ql) + last[..., None].astype(np.uint64))
+    want = O.Barrett(qs).reduce(lifted * gpsi.astype(np.uint64))                     # (polys, n, L - 1)
+    if layout == _lib.LAYOUT_LIMB_MAJOR:
+        gpsi, want = _lm(gpsi), _lm(want)
+    out = torch.empty(want.shape, dtype=torch.uint32, device="cuda")
+    ld, gd = torch.from_numpy(last).cuda(), torch.from_numpy(np.ascontiguousarray(gpsi)).cuda()
+    ff = finite_field.BarrettContext(qs)         # owns the modulus set for the whole call
+    _lib.check(_lib.lib().cross_rescale_lift(ff.handle(), ld.data_ptr(), ql, gd.data_ptr(), out.data_ptr(), polys,
+                                             n, layout, None), "cross_rescale_lift")
+    np.testing.assert_array_equal(_np(out), want)
+
+
 # ---------------------------------------------------------------------------
 # HE-Mult / HE-Rotate
 # ---------------------------------------------------------------------------
