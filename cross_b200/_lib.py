@@ -59,6 +59,7 @@ _SIGS = {
     "cross_last_error": (C.c_char_p, []),
     "cross_launch_count": (C.c_uint64, []),
     "cross_tc_i8_probe": (i32, [i32, i64, vp, vp, vp]),
+    "cross_wait_selftest": (i32, [C.c_uint64, vp]),
     "cross_moduli_create": (i32, [i32, vp, vp, vp, vp, C.POINTER(vp)]),
     "cross_moduli_destroy": (i32, [vp]),
     "cross_mod_reduce": (i32, [vp, vp, i32, vp, i64, vp]),

@@ -386,16 +386,21 @@ int launch_bconv_tc_any(const BconvTcArgs& a, size_t smem, int ctas_per_sm, cuda
 // are recombined in two 32-bit multiply-adds and one widening one (every BAT
 // sum of at most 32 source limbs is below 2^23).  Used when every source and
 // target modulus passes reduce_fast_ok (all moduli of the HE parameter sets).
+// Per-limb constants.  Barrett plans: m and s_w in the second and third
+// arrays.  Montgomery: q^-1 mod 2^32 in the second.  BAT-lazy: the words
+// 2^(32 + 8i) mod q, i = 0..3, in the second, third and the two extra arrays.
 struct BconvConsts {
   uint32_t sq_q[32], sq_m[32], sq_sw[32], sq_hi[32];   // source q_i, Barrett m, s_w, QHatInvModq_i
+  uint32_t sq_r2[32], sq_r3[32];                       // source BAT-lazy words 2, 3
   uint32_t dq[64], dm[64], dsw[64];                    // target q_j, Barrett m, s_w
+  uint32_t dr2[64], dr3[64];                           // target BAT-lazy words 2, 3
   const uint32_t* tp[64];                              // twist row of target j (TWIST)
 };
 
 struct BconvTccArgs {
   const uint32_t* in;
   int64_t in_ps, in_ls;
-  uint32_t* out;
+  void* out;                        // uint64 elements for BAT-lazy plans, else uint32
   int64_t out_ps, out_ls;
   int polys, n, sq, sp, kb, nn;
   uint32_t tmem_cols;
@@ -428,7 +433,7 @@ __device__ __forceinline__ void bcc_load(const BconvTccArgs& a, int w, int tiles
 // c_i = Barrett_i(x_i QHatInvModq_i) of this thread's source groups as row
 // `row` of the K-major A tile (the exact 32-bit form for x < 2^31, where
 // x QHatInv < 2^31 q; the 64-bit form above).
-template <int H, int KB>
+template <int H, int KB, int RED>
 __device__ __forceinline__ void bcc_pack(const BconvTccArgs& a, uint8_t* As, int row, const uint32_t (&xin)[4 * KB]) {
 #pragma unroll
   for (int k = 0; k < KB; ++k) {
@@ -441,8 +446,15 @@ __device__ __forceinline__ void bcc_pack(const BconvTccArgs& a, uint8_t* As, int
         if (i < a.sq) {
           const uint32_t xv = xin[4 * k + e], hv = a.k.sq_hi[i], q = a.k.sq_q[i], m = a.k.sq_m[i],
                          sw = a.k.sq_sw[i];
-          v = xv < 0x80000000u ? reduce_fast2(xv * hv, __umulhi(xv, hv), q, m, sw)
-                               : barrett_w32((uint64_t)xv * hv, q, m, sw);
+          if (RED == RED_MONTGOMERY) {
+            v = montgomery((uint64_t)xv * hv, q, m);                       // bconv.py:273
+          } else if (RED == RED_BAT_LAZY) {
+            const uint32_t r[4] = {m, sw, a.k.sq_r2[i], a.k.sq_r3[i]};
+            v = (uint32_t)bat_lazy((uint64_t)xv * hv, r) % q;             // bconv.py:382-386
+          } else {
+            v = xv < 0x80000000u ? reduce_fast2(xv * hv, __umulhi(xv, hv), q, m, sw)
+                                 : barrett_w32((uint64_t)xv * hv, q, m, sw);
+          }
         }
         c[e] = v;
       }
@@ -465,8 +477,8 @@ __device__ __forceinline__ void bcc_twist(const BconvTccArgs& a, int t, uint32_t
 
 // out_j[t] = Barrett_j(sum_b D[t][4j + b] << 8b) (x psi twist) for this
 // thread's targets; lane quadrant (warp & 3) of the accumulator.
-template <int H, int JH, bool TWIST, int NN>
-__device__ __forceinline__ void bcc_store(const BconvTccArgs& a, uint32_t tmem, int warp, uint32_t* y,
+template <int H, int JH, bool TWIST, int NN, int RED>
+__device__ __forceinline__ void bcc_store(const BconvTccArgs& a, uint32_t tmem, int warp, int64_t yoff,
                                           const uint32_t (&tw)[JH]) {
   const int64_t out_ls = NN ? NN : a.out_ls;
 #pragma unroll
@@ -482,19 +494,29 @@ __device__ __forceinline__ void bcc_store(const BconvTccArgs& a, uint32_t tmem, 
         if (j < a.sp) {
           const uint32_t q = a.k.dq[j], m = a.k.dm[j], sw = a.k.dsw[j];
           const uint64_t z = combine4_small(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
-          uint32_t r = reduce_fast(z, q, m, sw);
-          if (TWIST) {
-            const uint32_t twj = tw[4 * qc + jj];
-            r = reduce_fast2(r * twj, __umulhi(r, twj), q, m, sw);
+          if (RED == RED_BAT_LAZY) {
+            const uint32_t r4[4] = {m, sw, a.k.dr2[j], a.k.dr3[j]};
+            static_cast<uint64_t*>(a.out)[yoff + (int64_t)j * out_ls] = bat_lazy(z, r4);   // bconv.py:368
+          } else {
+            uint32_t r;
+            if (RED == RED_MONTGOMERY) {
+              r = montgomery(z, q, m);                                       // bconv.py:288
+            } else {
+              r = reduce_fast(z, q, m, sw);
+              if (TWIST) {
+                const uint32_t twj = tw[4 * qc + jj];
+                r = reduce_fast2(r * twj, __umulhi(r, twj), q, m, sw);
+              }
+            }
+            static_cast<uint32_t*>(a.out)[yoff + (int64_t)j * out_ls] = r;
           }
-          y[(int64_t)j * out_ls] = r;
         }
       }
     }
   }
 }
 
-template <bool TWIST, int KB, int SPMAX, int NN>
+template <bool TWIST, int KB, int SPMAX, int NN, int RED>
 __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tcc(const __grid_constant__ BconvTccArgs a) {
   extern __shared__ uint8_t sm_raw[];
   uint8_t* As = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
@@ -541,11 +563,11 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tcc(const __grid_consta
     //    this tile's twists, in flight during the MMA
     const bool more = w + (int)gridDim.x < total;
     if (h == 0) {
-      bcc_pack<0, KB>(a, As, row, xin);
+      bcc_pack<0, KB, RED>(a, As, row, xin);
       if (more) bcc_load<0, KB, NN>(a, w + gridDim.x, tiles_pp, row, xin);
       bcc_twist<0, JH, TWIST>(a, t0 + row, tw);
     } else {
-      bcc_pack<1, KB>(a, As, row, xin);
+      bcc_pack<1, KB, RED>(a, As, row, xin);
       if (more) bcc_load<1, KB, NN>(a, w + gridDim.x, tiles_pp, row, xin);
       bcc_twist<1, JH, TWIST>(a, t0 + row, tw);
     }
@@ -574,9 +596,9 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tcc(const __grid_consta
     if (__syncthreads_or(!ok)) break;
     tc_fence_after();
     // 3. this half's target limbs
-    uint32_t* y = a.out + (int64_t)poly * a.out_ps + t0 + row;
-    if (h == 0) bcc_store<0, JH, TWIST, NN>(a, tmem, warp, y, tw);
-    else bcc_store<1, JH, TWIST, NN>(a, tmem, warp, y, tw);
+    const int64_t yoff = (int64_t)poly * a.out_ps + t0 + row;
+    if (h == 0) bcc_store<0, JH, TWIST, NN, RED>(a, tmem, warp, yoff, tw);
+    else bcc_store<1, JH, TWIST, NN, RED>(a, tmem, warp, yoff, tw);
     tc_fence_before();
   }
   tc_fence_before();
@@ -585,10 +607,10 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tcc(const __grid_consta
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
 }
 
-template <bool TWIST, int KB, int SPMAX, int NN>
+template <bool TWIST, int KB, int SPMAX, int NN, int RED>
 int launch_bconv_tcc(const BconvTccArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
   const int sms = device_sm_count();
-  auto kern = k_bconv_tcc<TWIST, KB, SPMAX, NN>;
+  auto kern = k_bconv_tcc<TWIST, KB, SPMAX, NN, RED>;
   CROSS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t total = (int64_t)a.polys * (a.n / BT_ROWS);
   const int64_t cap = (int64_t)sms * ctas_per_sm;
@@ -598,12 +620,12 @@ int launch_bconv_tcc(const BconvTccArgs& a, size_t smem, int ctas_per_sm, cudaSt
   return CROSS_OK;
 }
 
-template <bool TWIST>
+template <bool TWIST, int RED = RED_BARRETT_FAST>
 int launch_bconv_tcc_any(const BconvTccArgs& a, size_t smem, int ctas_per_sm, cudaStream_t st) {
   const bool n64k = a.n == 65536 && a.in_ls == 65536 && a.out_ls == 65536;
 #define CROSS_BCC(KB, SPM)                                                                        \
-  return n64k ? launch_bconv_tcc<TWIST, KB, SPM, 65536>(a, smem, ctas_per_sm, st)                 \
-              : launch_bconv_tcc<TWIST, KB, SPM, 0>(a, smem, ctas_per_sm, st)
+  return n64k ? launch_bconv_tcc<TWIST, KB, SPM, 65536, RED>(a, smem, ctas_per_sm, st)            \
+              : launch_bconv_tcc<TWIST, KB, SPM, 0, RED>(a, smem, ctas_per_sm, st)
   if (a.kb == 1 && a.sp <= 24) CROSS_BCC(1, 24);
   if (a.kb == 1 && a.sp <= 40) CROSS_BCC(1, 40);
   if (a.kb == 1) CROSS_BCC(1, 64);
@@ -640,6 +662,46 @@ int launch_bconv(const cross_bconv_plan_s* P, bool vec, const uint32_t* in, int6
 }
 
 }  // namespace
+
+// basis_change_bat of a Montgomery or BAT-lazy plan on the tensor cores
+// (contiguous coefficients, n % 128 == 0): the same BAT contraction as
+// Barrett with the context's input scaling and output reduction (bconv.py:
+// 234-246 with MontgomeryContext / BATLazyContext.modular_reduction).  Returns
+// CROSS_ERR_UNSUPPORTED (nothing launched) when the shape does not qualify.
+int bconv_var_tc(const cross_bconv_plan_s* P, const uint32_t* in, int64_t in_ps, int64_t in_ls, int64_t in_ts,
+                 void* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys, int64_t n,
+                 cudaStream_t st) {
+  if (!P->tc_bimg || in_ts != 1 || out_ts != 1 || n % BT_ROWS != 0 || polys * (n / BT_ROWS) >= (1ll << 31) ||
+      (P->red != CROSS_REDUCTION_MONTGOMERY && P->red != CROSS_REDUCTION_BAT_LAZY) ||
+      (int)P->src_v_host.size() != P->sq || (int)P->dst_v_host.size() != P->sp)
+    return CROSS_ERR_UNSUPPORTED;
+  BconvTccArgs c{in, in_ps, in_ls, out, out_ps, out_ls, (int)polys, (int)n, P->sq, P->sp, P->tc_kb, P->tc_nn,
+                 64, P->tc_bimg, P->err, {}};
+  while ((int)c.tmem_cols < c.nn) c.tmem_cols <<= 1;
+  int cpsm = 0;
+  const size_t smc = bconv_tc_smem(P->sq, P->sp, P->tc_kb, P->tc_nn, c.tmem_cols, (size_t)device_smem_per_sm(), &cpsm);
+  if (!smc) return CROSS_ERR_UNSUPPORTED;
+  const bool mont = P->red == CROSS_REDUCTION_MONTGOMERY;
+  for (int i = 0; i < P->sq; ++i) {
+    const VarC& v = P->src_v_host[i];
+    c.k.sq_q[i] = v.q;
+    c.k.sq_hi[i] = P->qhat_inv_host[i];
+    c.k.sq_m[i] = mont ? v.qinv : v.r[0];
+    c.k.sq_sw[i] = v.r[1];
+    c.k.sq_r2[i] = v.r[2];
+    c.k.sq_r3[i] = v.r[3];
+  }
+  for (int j = 0; j < P->sp; ++j) {
+    const VarC& v = P->dst_v_host[j];
+    c.k.dq[j] = v.q;
+    c.k.dm[j] = mont ? v.qinv : v.r[0];
+    c.k.dsw[j] = v.r[1];
+    c.k.dr2[j] = v.r[2];
+    c.k.dr3[j] = v.r[3];
+  }
+  return mont ? launch_bconv_tcc_any<false, RED_MONTGOMERY>(c, smc, cpsm, st)
+              : launch_bconv_tcc_any<false, RED_BAT_LAZY>(c, smc, cpsm, st);
+}
 
 int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t in_ps, int64_t in_ls,
               int64_t in_ts, uint32_t* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys,
@@ -686,10 +748,6 @@ int bconv_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t
         }
         return twist ? launch_bconv_tcc_any<true>(c, smc, cpsm, st) : launch_bconv_tcc_any<false>(c, smc, cpsm, st);
       };
-      if (P->tc_split && P->tc_bimg_half[0] && P->tc_bimg_half[1]) {
-        const int rc = run(0, P->tc_split, P->tc_bimg_half[0], P->tc_nn_half[0]);
-        return rc ? rc : run(P->tc_split, P->sp, P->tc_bimg_half[1], P->tc_nn_half[1]);
-      }
       return run(0, P->sp, P->tc_bimg, P->tc_nn);
     }
     if (sm) {
@@ -760,8 +818,10 @@ int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction
   P->qhat_inv_host = qi;
   // tensor-core B operand: row n = 4j + b, K byte 4i + a, in the K-major
   // no-swizzle core-matrix layout of k_bconv_tc (sq <= 32, sp <= 64)
-  std::vector<uint8_t> bimg, bimg_half[2];
-  if (reduction == CROSS_REDUCTION_BARRETT && sq <= 32 && sp <= 64) {
+  std::vector<uint8_t> bimg;
+  // the tensor-core image serves every reduction whose basis_change_bat is a
+  // BAT contraction (Barrett, Montgomery, BAT-lazy; not Shoup, bconv.py:244)
+  if (reduction != CROSS_REDUCTION_SHOUP && sq <= 32 && sp <= 64) {
     P->tc_kb = (sq + 7) / 8;
     P->tc_nn = (4 * sp + 15) / 16 * 16;
     const int kb = P->tc_kb;
@@ -781,11 +841,6 @@ int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction
       return nn;
     };
     image(0, sp, bimg);
-    if (4 * sp > 128) {
-      P->tc_split = (sp + 1) / 2;
-      P->tc_nn_half[0] = image(0, P->tc_split, bimg_half[0]);
-      P->tc_nn_half[1] = image(P->tc_split, sp, bimg_half[1]);
-    }
     bool fast = true;
     for (const ModC& mc : P->dst_host) fast = fast && reduce_fast_ok(mc);
     for (const ModC& mc : P->src_host) fast = fast && barrett_w32_ok(mc);
@@ -799,15 +854,16 @@ int cross_bconv_plan_create_ex(cross_moduli src, cross_moduli dst, int reduction
   if (!rc) rc = upload(&P->err, zero.data(), 1);
   if (!rc && !bimg.empty() && !(getenv("CROSS_B200_DISABLE_TC") && getenv("CROSS_B200_DISABLE_TC")[0] == '1')) {
     rc = upload_vec(&P->tc_bimg, bimg);
-    for (int h = 0; h < 2 && !rc && P->tc_split; ++h) rc = upload_vec(&P->tc_bimg_half[h], bimg_half[h]);
   }
   if (!rc) rc = upload_vec(&P->dst, P->dst_host);
   if (!rc) rc = upload_vec(&P->qhat_inv, qi);
   if (!rc) rc = upload_vec(&P->bat, bat);
   if (!rc) rc = upload_vec(&P->qhat_modp, qm);
   if (!rc && reduction != CROSS_REDUCTION_BARRETT) {
-    rc = upload_vec(&P->src_v, make_varc(P->src_host));
-    if (!rc) rc = upload_vec(&P->dst_v, make_varc(P->dst_host));
+    P->src_v_host = make_varc(P->src_host);
+    P->dst_v_host = make_varc(P->dst_host);
+    rc = upload_vec(&P->src_v, P->src_v_host);
+    if (!rc) rc = upload_vec(&P->dst_v, P->dst_v_host);
     if (!rc && reduction == CROSS_REDUCTION_SHOUP) {
       std::vector<uint32_t> qs(qhat_inv_modq_shoup, qhat_inv_modq_shoup + sq), qms((size_t)sp * sq);
       for (int i = 0; i < sq; ++i)
@@ -843,8 +899,6 @@ int cross_bconv_plan_destroy(cross_bconv_plan P) {
   dfree(P->bat);
   dfree(P->qhat_modp);
   dfree(P->tc_bimg);
-  dfree(P->tc_bimg_half[0]);
-  dfree(P->tc_bimg_half[1]);
   dfree(P->err);
   dfree(P->src_v);
   dfree(P->dst_v);

@@ -145,6 +145,11 @@ int bconv_var_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int
 #define CROSS_BV(RED)                                                                                          \
   return bat ? launch_var_sq<RED, true>(P, in, in_ps, in_ls, in_ts, out, out_ps, out_ls, out_ts, polys, n, st) \
              : launch_var_sq<RED, false>(P, in, in_ps, in_ls, in_ts, out, out_ps, out_ls, out_ts, polys, n, st)
+  if (bat && (P->red == CROSS_REDUCTION_MONTGOMERY || P->red == CROSS_REDUCTION_BAT_LAZY)) {
+    // the tensor-core contraction when the shape allows, else the CUDA cores
+    const int rc = bconv_var_tc(P, in, in_ps, in_ls, in_ts, out, out_ps, out_ls, out_ts, polys, n, st);
+    if (rc != CROSS_ERR_UNSUPPORTED) return rc;
+  }
   switch (P->red) {
     case CROSS_REDUCTION_MONTGOMERY:
       if (!bat && P->sq != P->sp && P->sp != 1) {

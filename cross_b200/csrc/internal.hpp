@@ -62,17 +62,13 @@ struct cross_bconv_plan_s {
   int red = CROSS_REDUCTION_BARRETT;   // cross_reduction of the source / target contexts
   cross::VarC* src_v = nullptr;        // [sq] variant constants of the source moduli
   cross::VarC* dst_v = nullptr;        // [sp] variant constants of the target moduli
+  std::vector<cross::VarC> src_v_host, dst_v_host;
   uint32_t* qhat_inv_s = nullptr;      // [sq]      Shoup companion of qhat_inv
   uint32_t* qhat_modp_s = nullptr;     // [sp][sq]  Shoup companion of qhat_modp
   int tc_fast = 0;                  // tensor-core kernel may use reduce_fast / barrett_w32
   int tc_src_fast = 0;              // reduce_fast is exact for every source modulus
   int tc_kb = 0, tc_nn = 0;         // K blocks of 8 source limbs, MMA N (4 sp rounded up to 16)
   uint8_t* tc_bimg = nullptr;       // B operand in its shared-memory image (K-major, no swizzle)
-  // 4 sp > 128 (an accumulator wider than 128 TMEM columns): the targets
-  // [0, tc_split) and [tc_split, sp) as two half images, converted by two
-  // launches of half the width (twice the CTAs per SM)
-  int tc_split = 0, tc_nn_half[2] = {0, 0};
-  uint8_t* tc_bimg_half[2] = {nullptr, nullptr};
   int* err = nullptr;               // device error word of the tensor-core kernel
   std::vector<cross::ModC> src_host, dst_host;
   cross::ModC* src = nullptr;       // [sq]
@@ -226,6 +222,12 @@ int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, L
 int ntt_run_shoup(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
                   const uint16_t* limbs, uint32_t* tmp, cudaStream_t st);
 
+// basis_change_bat of a Montgomery / BAT-lazy plan on the tensor cores
+// (bconv.cu); CROSS_ERR_UNSUPPORTED, nothing launched, for shapes it does not
+// take (strided coefficients, n % 128 != 0).
+int bconv_var_tc(const cross_bconv_plan_s* P, const uint32_t* in, int64_t in_ps, int64_t in_ls, int64_t in_ts,
+                 void* out, int64_t out_ps, int64_t out_ls, int64_t out_ts, int64_t polys, int64_t n,
+                 cudaStream_t st);
 // Basis conversion of a Montgomery / Shoup / BAT-lazy plan (bconv_var.cu);
 // out is uint64 for BAT-lazy plans, else uint32 (strides in elements).
 int bconv_var_run(const cross_bconv_plan_s* P, bool bat, const uint32_t* in, int64_t in_ps, int64_t in_ls,

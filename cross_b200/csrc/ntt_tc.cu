@@ -1463,6 +1463,49 @@ int launch_probe(int64_t kchunks, int* err, int* ctas, cudaStream_t st) {
 }  // namespace tc
 }  // namespace cross
 
+// Self-test of the bounded waits every tensor-core kernel uses: one warp waits
+// on an mbarrier that nothing arrives on, through the same bounded wait, and
+// must give up after bound_ns, record code 51 in the error word and return.
+namespace cross {
+namespace tc {
+__device__ int g_wait_selftest_err;
+
+__global__ void k_wait_selftest(uint64_t bound_ns) {
+  __shared__ uint64_t bar;
+  __shared__ volatile int abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // phase 0 never completes: no thread arrives on bar
+  const bool ok = mbar_wait_for(&bar, 0, abort, &g_wait_selftest_err, 51, bound_ns);
+  if (__any_sync(0xffffffffu, ok) && threadIdx.x == 0) atomicExch(&g_wait_selftest_err, 52);
+}
+}  // namespace tc
+}  // namespace cross
+
+extern "C" int cross_wait_selftest(uint64_t bound_ns, void* stream) {
+  CROSS_REQUIRE(bound_ns >= 1000 && bound_ns <= 1000000000ull,
+                "cross_wait_selftest: bound_ns=%llu outside 1 us .. 1 s", (unsigned long long)bound_ns);
+  int e = 0;
+  CROSS_CHECK_CUDA(cudaMemcpyToSymbolAsync(cross::tc::g_wait_selftest_err, &e, sizeof(int), 0,
+                                           cudaMemcpyHostToDevice, (cudaStream_t)stream));
+  cross::tc::k_wait_selftest<<<1, 32, 0, (cudaStream_t)stream>>>(bound_ns);
+  cross::count_launch();
+  CROSS_CHECK_CUDA(cudaGetLastError());
+  CROSS_CHECK_CUDA(cudaMemcpyFromSymbolAsync(&e, cross::tc::g_wait_selftest_err, sizeof(int), 0,
+                                             cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  CROSS_CHECK_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  if (e == 51) {
+    cross::set_error("bounded wait expired after %llu ns as intended (code %d)", (unsigned long long)bound_ns, e);
+    return CROSS_ERR_TIMEOUT;
+  }
+  cross::set_error("cross_wait_selftest: the wait on a barrier nothing arrives on ended with code %d", e);
+  return CROSS_ERR_CUDA;
+}
+
 extern "C" int cross_tc_i8_probe(int pair, int64_t kchunks, int* err, int* ctas, void* stream) {
   CROSS_REQUIRE(err && ctas && kchunks >= 1 && kchunks <= (1 << 20),
                 "cross_tc_i8_probe: need err, ctas and 1 <= kchunks <= 2^20");

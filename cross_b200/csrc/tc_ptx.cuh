@@ -64,17 +64,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, abort, err, code);
 }
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int& abort, int* err, int code) {
+// The bounded loop with an explicit bound (bound_ns of global timer).
+static __device__ __noinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int& abort, int* err,
+                                                  int code, uint64_t bound_ns) {
   const uint64_t t0 = globaltimer();
   for (;;) {
     if (mbar_try(bar, parity)) return true;
     if (abort) return false;
-    if (globaltimer() - t0 > WAIT_NS) {
+    if (globaltimer() - t0 > bound_ns) {
       atomicCAS(err, 0, code);
       abort = 1;
       return false;
     }
   }
+}
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int& abort, int* err, int code) {
+  return mbar_wait_for(bar, parity, abort, err, code, WAIT_NS);
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

@@ -83,6 +83,15 @@ uint64_t cross_launch_count(void);
  * bounded completion wait sets to 31 when it expires.  1 <= kchunks <= 2^20. */
 int cross_tc_i8_probe(int pair, int64_t kchunks, int* err, int* ctas, void* stream);
 
+/* Self-test of the bounded device waits (no counterpart in the reference):
+ * one warp waits, through the same bounded mbarrier wait the tensor-core
+ * kernels use, on a barrier that nothing arrives on.  The wait must give up
+ * after bound_ns of global timer (1 us .. 1 s), record its code and let the
+ * kernel return; the call synchronizes the stream and returns
+ * CROSS_ERR_TIMEOUT when that happened as intended (the context stays
+ * usable), CROSS_ERR_CUDA otherwise. */
+int cross_wait_selftest(uint64_t bound_ns, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Modulus sets                                                        */
 /* ------------------------------------------------------------------ */
