@@ -48,10 +48,10 @@ sys.path.insert(0, ROOT)
 
 N_DEG, R, C = 65536, 256, 256
 # DRAM bytes (read + write) of one k_bat_tc2 launch of the roofline NTT per
-# limb-polynomial it processes: the ncu capture of profiles/k_bat_tc2_ntt_n65536.md
-# (3.148 GB per launch over 256 polys x 23 limbs; traffic grows with the
-# limb-polynomials processed).
-TRAFFIC_PER_LP = 3.148e9 / (256 * 23)
+# limb-polynomial it processes, from an ncu capture of the same launches at
+# 64 polys x 34 limbs (1222.7 MB and 1195.4 MB for the two stages; traffic
+# grows with the limb-polynomials processed).
+TRAFFIC_PER_LP = (1222.7e6 + 1195.4e6) / 2 / (64 * 34)
 L2_BYTES = 126 * 2 ** 20                # B200 L2
 
 

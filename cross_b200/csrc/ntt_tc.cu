@@ -951,7 +951,7 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
 // stage 8 tcgen05.mma kind::i8 of M = 128, N = 256, K = 32 into one 256-column
 // TMEM accumulator; the stage-2 epilogue (recombination, Barrett) stores the
 // natural-order result.  Bounded waits as in k_bat_tc (codes 41 to 44).
-constexpr int T64_THREADS = 256;
+constexpr int T64_THREADS = 512;   // 16 warps: four per TMEM lane quadrant, 16 outputs each per stage
 struct Smem64 {
   uint8_t b1[2][256 * 128];    // stage-1 B: two 128-byte K chunks of 256 rows
   uint8_t b2[2][256 * 128];    // stage-2 B
@@ -1023,7 +1023,8 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
   uint32_t bphase = 0, mphase = 0;
   int cur_slot = -1;
   // epilogue role: TMEM lane quadrant q = warp % 4 (rows 32 q .. 32 q + 31),
-  // output half h = warp / 4 (accumulator columns 128 h .. 128 h + 127)
+  // output quarter h = warp / 4 (outputs 16 h .. 16 h + 15, accumulator
+  // columns 64 h .. 64 h + 63)
   const int q = warp & 3, h = warp >> 2;
   const int m = 32 * q + lane, mp = m >> 6, mm = m & 63;
   for (int64_t it = i0; it < i1; ++it) {
@@ -1048,8 +1049,8 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
         // forward: A rows c, K words r (the transpose of X[r][c])
         const int c = t & 63, rg = t >> 6;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r0 = 16 * i + 4 * rg;
+        for (int i = 0; i < 2; ++i) {
+          const int r0 = 32 * i + 4 * rg;
           uint4 v;
           v.x = __ldg(x + (r0 + 0) * 64 + c);
           v.y = __ldg(x + (r0 + 1) * 64 + c);
@@ -1061,8 +1062,8 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
         // inverse: A rows r, K words c (X as stored)
         const int c4 = t & 15;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = (t >> 4) + 16 * i;
+        for (int i = 0; i < 2; ++i) {
+          const int r = (t >> 4) + 32 * i;
           const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + r * 64) + c4);
           *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(pp * 64 + r, c4)) = v;
         }
@@ -1071,11 +1072,11 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
     // stage-1 twiddles of this thread's outputs, in flight during the MMA
     const ModC mc = a.mods[limb];
     const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
-    uint32_t tw[32];
+    uint32_t tw[16];
     {
       const uint32_t* tb = a.tw + (int64_t)limb * 4096 + mm;
 #pragma unroll
-      for (int o = 0; o < 32; ++o) tw[o] = __ldg(tb + (32 * h + o) * 64);
+      for (int o = 0; o < 16; ++o) tw[o] = __ldg(tb + (16 * h + o) * 64);
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
@@ -1101,12 +1102,12 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
     // stage-1 epilogue: Y = Barrett(Barrett(sum) x twiddle) into the stage-2 A tile
     // (row: output index o of this polynomial, K word: this thread's row mm)
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
+    for (int ch = 0; ch < 2; ++ch) {
       uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128 * h + 32 * ch, v);
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * h + 32 * ch, v);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int o = 32 * h + 8 * ch + j;
+        const int o = 16 * h + 8 * ch + j;
         const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         const uint32_t wv = tw[8 * ch + j];
         uint32_t r;
@@ -1136,9 +1137,9 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
     const bool store = mp == 0 || two;
     uint32_t* y = a.out.p + (p0 + mp) * a.out.ps + (int64_t)slot * a.out.ss;
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
+    for (int ch = 0; ch < 2; ++ch) {
       uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128 * h + 32 * ch, v);
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * h + 32 * ch, v);
       uint32_t res[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -1146,7 +1147,7 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
         res[j] = FAST ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
       }
       if (store) {
-        const int o0 = 32 * h + 8 * ch;
+        const int o0 = 16 * h + 8 * ch;
         if (!INV) {
           // forward: Z[z][n], this thread's row z = mm, outputs n = o0 .. o0 + 7
           uint4* d = reinterpret_cast<uint4*>(y + mm * 64 + o0);
