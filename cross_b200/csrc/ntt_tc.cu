@@ -881,6 +881,11 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
     return CROSS_ERR_UNSUPPORTED;
   }
   Args a{out.p, out.ps, out.ss, limbs, slots, polys, rows_m, kw, nout, P->mods, P->varc, P->tc_err, e};
+  // row-major outputs are written with 16-byte stores
+  if (!nmajor && (((uintptr_t)out.p & 15) || (slots > 1 && out.ss % 4) || (polys > 1 && out.ps % 4))) {
+    set_error("tcgen05 stage: the output base and strides must be 16-byte aligned");
+    return CROSS_ERR_INVALID_ARG;
+  }
   if (!nmajor && e.op != EPI_NONE) {
     // row-major operands are read with 16-byte loads
     const View& x = e.op == EPI_MUL ? View{e.tab, 0, 0, 0, 1} : e.x;

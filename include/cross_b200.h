@@ -243,7 +243,9 @@ size_t cross_ntt_workspace_size(cross_ntt_plan plan, int64_t batch, int layout);
  * evaluation order, exactly as the reference.  With
  * CROSS_LAYOUT_LIMB_MAJOR_TRANSPOSED the coefficients (ntt input, intt
  * output) are (batch, M, c, r) and the evaluations (batch, M, r, c).
- * in may equal out. */
+ * in may equal out.  In the limb-major layouts the tensor-core plans read and
+ * write in/out in 16-byte pieces: both must be 16-byte aligned, else
+ * CROSS_ERR_INVALID_ARG (CROSS_LAYOUT_REFERENCE has no such rule). */
 int cross_ntt(cross_ntt_plan plan, int inverse, const uint32_t* in, uint32_t* out, int64_t batch,
               int layout, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -707,3 +707,30 @@ def test_hemul_non_square_tensor_core_vs_oracle():
     ref = O.HEMul(B, 128, 256, dnum, 1, Q, P)
     ref.setup_relinearization(*ek)
     np.testing.assert_array_equal(got, ref.mul(ct))
+
+
+def test_ntt_refuses_unaligned_row_major_output():
+    """The row-major stages write 16-byte pieces (bulk tensor stores); an
+    output pointer off a 16-byte boundary through the C ABI is refused with
+    CROSS_ERR_INVALID_ARG before the row stage launches, and the context keeps
+    computing bit-exact results."""
+    import torch
+    from cross_b200 import _lib, ntt_mm
+    q = O.find_moduli_ntt(2, 28, 2 * 65536)
+    ctx = ntt_mm.NTTCiphertextBarrettContext(q, {"r": 256, "c": 256})
+    lib = _lib.lib()
+    B, M, n = 1, 2, 65536
+    x = rng_residues(np.random.default_rng(5), (B, 256, 256, M), q)
+    xl = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 3, 1, 2))).cuda()
+    buf = torch.zeros(B * M * n + 4, dtype=torch.uint32, device="cuda")
+    ws = torch.empty(lib.cross_ntt_workspace_size(ctx.plan(), B, _lib.LAYOUT_LIMB_MAJOR), dtype=torch.uint8,
+                     device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = lib.cross_ntt(ctx.plan(), 0, xl.data_ptr(), buf.data_ptr() + 4, B, _lib.LAYOUT_LIMB_MAJOR, ws.data_ptr(),
+                       ws.numel(), st)
+    assert rc == -1, lib.cross_last_error()                        # CROSS_ERR_INVALID_ARG
+    assert b"16-byte aligned" in lib.cross_last_error()
+    torch.cuda.synchronize()
+    assert int(buf.count_nonzero()) == 0                           # nothing was written
+    np.testing.assert_array_equal(_np(ctx.ntt(x)), O.NTTBarrett(q, 256, 256).ntt(x))
+    ctx.check_device()
