@@ -818,6 +818,51 @@ def run_ckks(args, torch, dist, world, rank, local):
 
 
 
+def copies_alone(torch, dev, hin, hout, units, unit, world):
+    """The operator rate that the end-to-end path's host<->device copies alone
+    would allow: one call's pinned inputs copied in and outputs copied out,
+    H2D alone, D2H alone and both at once on two streams, every rank at the
+    same time (CUDA events around each, best of 3 after a warm-up, max over
+    ranks).  On one GPU the e2e pipeline approaches it when the compute hides
+    under the copies; with several ranks sharing the host's memory and PCIe
+    links, whole-call copies contend more than the pipeline's chunks do, so
+    the e2e value can exceed it."""
+    from cross_b200 import shard
+    din = torch.empty(hin.shape, dtype=hin.dtype, device=dev)
+    dout = torch.empty(hout.shape, dtype=hout.dtype, device=dev)
+    cur = torch.cuda.current_stream(dev)
+    s1, s2 = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+
+    def best(h2d, d2h):
+        times = []
+        for _ in range(4):
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            s1.wait_stream(cur)
+            s2.wait_stream(cur)
+            if h2d:
+                with torch.cuda.stream(s1):
+                    din.copy_(hin, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s2):
+                    hout.copy_(dout, non_blocking=True)
+            cur.wait_stream(s1)
+            cur.wait_stream(s2)
+            e1.record(cur)
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1))
+        return shard.max_over_ranks(min(times[1:]), device=dev)
+
+    h2d_ms, d2h_ms, both_ms = best(True, False), best(False, True), best(True, True)
+    bi, bo = hin.numel() * hin.element_size(), hout.numel() * hout.element_size()
+    del din, dout
+    torch.cuda.empty_cache()
+    return {"value": world * units / (both_ms / 1000.0), "unit": unit, "call_units": units,
+            "h2d_gbs": bi / h2d_ms / 1e6, "d2h_gbs": bo / d2h_ms / 1e6, "both_ms_per_call": both_ms,
+            "note": "pinned host memory, one call's bytes per rank, all ranks at once"}
+
+
 def measure_he(pt, torch, dist, world, rank, local, steps, warmup, e2e=True, cpu=True, roofline=True, probe=True):
     """One HE operator point: each rank runs its share of pt.global_batch
     ciphertexts (inputs resident in HBM) in calls of pt.call_batch; CUDA events
@@ -923,6 +968,7 @@ def measure_he(pt, torch, dist, world, rank, local, steps, warmup, e2e=True, cpu
         ems = shard.max_over_ranks(e0.elapsed_time(e1), device=dev)
         line["e2e"] = {"value": pt.global_batch * steps / (ems / 1000.0), "unit": pt.unit,
                        "h2d_bytes_per_step": int(hin.numel() * 4), "d2h_bytes_per_step": int(hout.numel() * 4)}
+        line["e2e"]["copies_alone"] = copies_alone(torch, dev, hin[:cb], hout[:cb], cb, pt.unit, world)
         del hin, hout
     else:
         del x, out, ws
