@@ -1007,9 +1007,9 @@ def measure_he_limb(pt, torch, dist, world, rank, local, steps, warmup):
     outs = [None] * (-(-B // cb))
 
     def step():
+        # the calls pipelined: each call's all-gathers overlap the others' kernels
         torch.cuda.nvtx.range_push("hemul_limb")
-        for i, a in enumerate(range(0, B, cb)):
-            outs[i] = sh.mul(x[a:a + cb])
+        outs[:] = sh.mul_many([x[a:a + cb] for a in range(0, B, cb)])
         torch.cuda.nvtx.range_pop()
 
     for _ in range(warmup):
@@ -1042,7 +1042,8 @@ def measure_he_limb(pt, torch, dist, world, rank, local, steps, warmup):
             "config": {"workload": pt.describe(B) + ", limbs split across the GPUs", "global_batch": B,
                        "call_batch": cb, "L": pt.L, "K": pt.K, "dnum": pt.dnum,
                        "parallelism": f"limb-sharded x{world}: Q' limbs [{sh.q0}, {sh.q1}), P limbs [{sh.p0}, "
-                                      f"{sh.p1}) on rank {rank}; ModUp and ModDown all-gathers over NCCL",
+                                      f"{sh.p1}) on rank {rank}; ModUp and ModDown all-gathers over NCCL, overlapping the "
+                                      f"neighbouring calls' kernels (calls pipelined {limb_shard.PIPELINE_DEPTH} deep)",
                        "allgather_bytes_per_step": cc_bytes + kp_bytes},
             "gpu_launches": int(launches), "clocks": clk.summary(h0, h1),
             "e2e": None, "e2e_note": "inputs are resident per rank by limb (no host-buffer API for a limb split)"}

@@ -22,8 +22,9 @@ Exchange buffers are limb-outer ([limb][ciphertext][N]) so that each rank's
 slice is contiguous and an all-gather of equal chunks places limb l at index
 l; ranges are chunks of ceil(limbs / world) (the last ranks may own fewer
 limbs, or none).  `limb_sharded_mul` runs the phases of any backend with
-that interface; `LimbShard` is the CUDA backend (the C ABI's
-cross_hemul_shard_* phases).
+that interface for one call; `limb_sharded_mul_many` runs a sequence of calls
+three deep, so that each all-gather overlaps the neighbouring calls' compute;
+`LimbShard` is the CUDA backend (the C ABI's cross_hemul_shard_* phases).
 """
 from __future__ import annotations
 
@@ -43,22 +44,34 @@ def limb_ranges(n: int, world: int) -> Tuple[List[Tuple[int, int]], int]:
     return [(min(n, r * ch), min(n, (r + 1) * ch)) for r in range(world)], ch
 
 
-def all_gather_chunks(buf, chunk: int, rank: int, world: int, group=None) -> None:
-    """Fill buf (world * chunk rows on axis 0) with every rank's rows
-    [rank * chunk, (rank + 1) * chunk): NCCL in place for CUDA tensors, gloo
-    through a list for CPU tensors.  The rows travel as int32 words."""
+def gather_start(buf, chunk: int, rank: int, world: int, group=None):
+    """Start filling buf (world * chunk rows on axis 0) with every rank's rows
+    [rank * chunk, (rank + 1) * chunk) and return the function that completes
+    it.  CUDA tensors: an in-place NCCL all-gather on the process group's
+    stream, which starts once the current stream's earlier work is done;
+    completing it makes the current stream wait for it (the host does not
+    block).  CPU tensors: a gloo all-gather through a list, waited for and
+    copied in on completion.  The rows travel as int32 words."""
     if world == 1 or chunk == 0:
-        return
+        return lambda: None
     import torch
     import torch.distributed as dist
     flat = buf.view(torch.int32) if buf.dtype == torch.uint32 else buf
     mine = flat[rank * chunk:(rank + 1) * chunk]
     if flat.is_cuda:
-        dist.all_gather_into_tensor(flat, mine, group=group)
-    else:
-        parts = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(parts, mine.contiguous(), group=group)
+        return dist.all_gather_into_tensor(flat, mine, group=group, async_op=True).wait
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    work = dist.all_gather(parts, mine.contiguous(), group=group, async_op=True)
+
+    def finish():
+        work.wait()
         flat.copy_(torch.cat(parts, 0))
+    return finish
+
+
+def all_gather_chunks(buf, chunk: int, rank: int, world: int, group=None) -> None:
+    """gather_start, completed at once."""
+    gather_start(buf, chunk, rank, world, group)()
 
 
 def limb_sharded_mul(backend, x_own, rank: int, world: int, group=None):
@@ -77,6 +90,47 @@ def limb_sharded_mul(backend, x_own, rank: int, world: int, group=None):
     out = backend.empty((B, 2, backend.nq, N))
     backend.moddown(kp_all, out)
     return out
+
+
+# calls in flight in limb_sharded_mul_many: phase 1 of call k, phase 2 of
+# call k - 1 and phase 3 of call k - 2
+PIPELINE_DEPTH = 3
+
+
+def limb_sharded_mul_many(backend, xs, rank: int, world: int, group=None):
+    """limb_sharded_mul over a sequence of calls, software-pipelined so that
+    every all-gather overlaps other calls' compute: in step i the rank runs
+    phase 1 of call i (whose ModUp gather then starts), phase 2 of call i - 1
+    (after its ModUp gather; its ModDown gather then starts) and phase 3 of
+    call i - 2 (after its ModDown gather).  Every rank issues the same
+    collectives in the same order.  The backend keeps one workspace per call
+    in flight: its phase methods take `slot` (call index mod PIPELINE_DEPTH).
+    Returns the outputs of the calls in order."""
+    n = len(xs)
+    outs = [None] * n
+    cc, kp, fin1, fin2 = {}, {}, {}, {}
+    for i in range(n + 2):
+        k = i
+        if k < n:
+            B, N = xs[k].shape[0], xs[k].shape[-1]
+            cc[k] = backend.empty((world * backend.cq, B, N))
+            backend.modup_input(xs[k], cc[k][rank * backend.cq:(rank + 1) * backend.cq], slot=k % PIPELINE_DEPTH)
+            fin1[k] = gather_start(cc[k], backend.cq, rank, world, group)
+        k = i - 1
+        if 0 <= k < n:
+            fin1.pop(k)()
+            B, N = xs[k].shape[0], xs[k].shape[-1]
+            kp[k] = backend.empty((world * backend.cp, 2 * B, N))
+            backend.keyswitch(cc[k], kp[k][rank * backend.cp:(rank + 1) * backend.cp], slot=k % PIPELINE_DEPTH)
+            fin2[k] = gather_start(kp[k], backend.cp, rank, world, group)
+        k = i - 2
+        if 0 <= k < n:
+            fin2.pop(k)()
+            B, N = xs[k].shape[0], xs[k].shape[-1]
+            outs[k] = backend.empty((B, 2, backend.nq, N))
+            backend.moddown(kp.pop(k), outs[k], slot=k % PIPELINE_DEPTH)
+            del cc[k]
+    return outs
 
 
 class LimbShard:
@@ -118,7 +172,7 @@ class LimbShard:
         _lib.check(_lib.lib().cross_hemul_shard_create(_lib.C.byref(desc), _lib.C.byref(out)),
                    "cross_hemul_shard_create")
         self._shard = out
-        self._ws = None
+        self._ws = [None] * PIPELINE_DEPTH
 
     def __del__(self):
         if getattr(self, "_shard", None) is not None and getattr(_lib, "_lib", None) is not None:
@@ -128,11 +182,11 @@ class LimbShard:
     def empty(self, shape):
         return _tensor.empty_u32(tuple(shape))
 
-    def _workspace(self, batch):
+    def _workspace(self, batch, slot=0):
         need = int(_lib.lib().cross_hemul_shard_workspace_size(self._shard, batch))
-        if self._ws is None or self._ws.numel() < need:
-            self._ws = _tensor.workspace(need)
-        return self._ws
+        if self._ws[slot] is None or self._ws[slot].numel() < need:
+            self._ws[slot] = _tensor.workspace(need)
+        return self._ws[slot]
 
     def own_input(self, x_lm):
         """The rank's input (B, 4, nq + 1, N) from a full limb-major batch
@@ -141,24 +195,29 @@ class LimbShard:
         xi = x_lm.view(t.int32)
         return t.cat([xi[:, :, self.q0:self.q1], xi[:, :, -1:]], 2).contiguous().view(t.uint32)
 
-    def modup_input(self, x_own, cc_rows):
+    def modup_input(self, x_own, cc_rows, slot=0):
         B = x_own.shape[0]
-        ws = self._workspace(B)
+        ws = self._workspace(B, slot)
         _tensor.call("cross_hemul_shard_modup_input", self._shard, x_own.data_ptr(), B, cc_rows.data_ptr(),
                      ws.data_ptr(), ws.numel(), _lib.cuda_stream())
 
-    def keyswitch(self, cc_all, kp_rows):
+    def keyswitch(self, cc_all, kp_rows, slot=0):
         B = cc_all.shape[1]
-        ws = self._workspace(B)
+        ws = self._workspace(B, slot)
         _tensor.call("cross_hemul_shard_keyswitch", self._shard, cc_all.data_ptr(), B, kp_rows.data_ptr(),
                      ws.data_ptr(), ws.numel(), _lib.cuda_stream())
 
-    def moddown(self, kp_all, out):
+    def moddown(self, kp_all, out, slot=0):
         B = out.shape[0]
-        ws = self._workspace(B)
+        ws = self._workspace(B, slot)
         _tensor.call("cross_hemul_shard_moddown", self._shard, kp_all.data_ptr(), B, out.data_ptr(),
                      ws.data_ptr(), ws.numel(), _lib.cuda_stream())
 
     def mul(self, x_own, group=None):
         """limb_sharded_mul on this shard (collectives in `group`)."""
         return limb_sharded_mul(self, x_own, self.rank, self.world, group)
+
+    def mul_many(self, xs, group=None):
+        """limb_sharded_mul_many on this shard: the calls' exchanges overlap
+        the neighbouring calls' compute."""
+        return limb_sharded_mul_many(self, xs, self.rank, self.world, group)

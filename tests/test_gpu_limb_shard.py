@@ -78,13 +78,19 @@ def _nccl_worker(rank, world, port, q):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
     try:
         from cross_b200 import _lib, limb_shard
-        he, x_lm = _setup(65536, 35, 7, 5, 2, seed=77)
+        he, x_lm = _setup(65536, 35, 7, 5, 3, seed=77)
         want = he.mul(x_lm, layout=_lib.LAYOUT_LIMB_MAJOR)
         s = limb_shard.LimbShard(he, rank, world)
-        out = s.mul(s.own_input(x_lm))
+        mine = want[:, :, s.q0:s.q1].contiguous().view(torch.int32)
+        x_own = s.own_input(x_lm)
+        out = s.mul(x_own)
+        # the pipelined form, one ciphertext per call (three calls in flight:
+        # every workspace slot, gathers overlapping the other calls' kernels)
+        many = s.mul_many([x_own[i:i + 1] for i in range(x_own.shape[0])])
         torch.cuda.synchronize()
-        ok = torch.equal(out.view(torch.int32), want[:, :, s.q0:s.q1].contiguous().view(torch.int32))
-        q.put((rank, "ok" if ok else f"limbs [{s.q0}, {s.q1}) differ"))
+        bad = [] if torch.equal(out.view(torch.int32), mine) else ["one call"]
+        bad += [f"pipelined call {i}" for i, g in enumerate(many) if not torch.equal(g.view(torch.int32), mine[i:i + 1])]
+        q.put((rank, "ok" if not bad else f"limbs [{s.q0}, {s.q1}) differ: {bad}"))
         del s, he
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, repr(e)))

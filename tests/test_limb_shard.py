@@ -50,6 +50,7 @@ class OracleShard:
         self.qown = he.Qd[self.q0:self.q1]
         self.ff_q = O.Barrett(self.qown) if self.nq else None
         self.ntt_q = O.NTTBarrett(self.qown, self.r, self.c) if self.nq else None
+        self.st = {}                       # per-slot state between the phases (the workspace)
 
     def empty(self, shape):
         return torch.zeros(tuple(shape), dtype=torch.int32)
@@ -59,8 +60,9 @@ class OracleShard:
         B, _, M, _ = x_lm.shape
         return np.ascontiguousarray(x_lm.transpose(0, 1, 3, 2)).reshape(B, E, self.r, self.c, M)
 
-    def modup_input(self, x_own, cc_rows):
+    def modup_input(self, x_own, cc_rows, slot=0):
         O, he, own = self.O, self.he, slice(self.q0, self.q1)
+        st = self.st.setdefault(slot, {})
         if not self.nq:
             return
         x = self._ref(x_own.numpy().view(U32), 4)
@@ -72,15 +74,16 @@ class OracleShard:
         red = self.ff_q.reduce(coef.astype(U64) * rp.gammas_power_of_psi_no_last[..., own].astype(U64))
         nt = O._ntt_flat(self.ntt_q, red, inverse=False)
         xr = self.ff_q.reduce(x[..., :self.nq].astype(U64) * rp.betas[own] + nt.astype(U64))
-        self.post, self.d2 = O.ciphertext_mult(xr, self.ff_q)
-        cf = O._ntt_flat(self.ntt_q, self.d2, inverse=True)
+        st["post"], st["d2"] = O.ciphertext_mult(xr, self.ff_q)
+        cf = O._ntt_flat(self.ntt_q, st["d2"], inverse=True)
         cf = O._modmul(self.ff_q, cf, he.ks.inv_psi[..., own])                  # (B, 1, r, c, nq)
         B = cf.shape[0]
         cc_rows[:self.nq] = torch.from_numpy(np.ascontiguousarray(
             cf.reshape(B, -1, self.nq).transpose(2, 0, 1)).view(np.int32))
 
-    def keyswitch(self, cc_all, kp_rows):
+    def keyswitch(self, cc_all, kp_rows, slot=0):
         O, he, ks = self.O, self.he, self.he.ks
+        st = self.st.setdefault(slot, {})
         cc = cc_all.numpy().view(U32)[:self.L1]                                 # (L', B, N)
         B = cc.shape[1]
         coef = np.ascontiguousarray(cc.transpose(1, 2, 0)).reshape(B, 1, self.r, self.c, self.L1)
@@ -97,23 +100,24 @@ class OracleShard:
                 ev = bc.basis_change_bat(coef[..., list(sel)], 0)
                 ev = O._modmul(O.Barrett([self.dle[l] for l in tg]), ev, ks.dl_power_of_psi[..., tg])
                 ev = O._ntt_flat(O.NTTBarrett([self.dle[l] for l in tg], self.r, self.c), ev, inverse=False)
-            cols = [self.d2[..., l - self.q0] if l in sel else ev[..., tg.index(l)] for l in self.own]
+            cols = [st["d2"][..., l - self.q0] if l in sel else ev[..., tg.index(l)] for l in self.own]
             ext = np.stack(cols, -1).astype(U64)
             a = ext * ks.evk_b[j][..., self.own][None, None]
             b = ext * ks.evk_a[j][..., self.own][None, None]
             t0 = a if t0 is None else t0 + a
             t1 = b if t1 is None else t1 + b
-        self.ks_out = O.Barrett([self.dle[l] for l in self.own]).reduce(np.concatenate([t0, t1], axis=1))
+        st["ks_out"] = O.Barrett([self.dle[l] for l in self.own]).reduce(np.concatenate([t0, t1], axis=1))
         if self.np:
             pm = he.P[self.p0:self.p1]
             ntt_p = O.NTTBarrett(pm, he.ntt_ext.r, he.ntt_ext.c)
-            kp = O._ntt_flat(ntt_p, self.ks_out[..., self.nq:], inverse=True)
+            kp = O._ntt_flat(ntt_p, st["ks_out"][..., self.nq:], inverse=True)
             kp = O._modmul(O.Barrett(pm), kp, he.power_of_inv_psi_approx_down[..., self.p0:self.p1])
             kp_rows[:self.np] = torch.from_numpy(np.ascontiguousarray(
                 kp.reshape(2 * B, -1, self.np).transpose(2, 0, 1)).view(np.int32))
 
-    def moddown(self, kp_all, out):
+    def moddown(self, kp_all, out, slot=0):
         O, he, own = self.O, self.he, slice(self.q0, self.q1)
+        st = self.st.setdefault(slot, {})
         if not self.nq:
             return
         kp = kp_all.numpy().view(U32)[:self.K]                                  # (K, 2B, N)
@@ -127,10 +131,10 @@ class OracleShard:
         for e in range(2):
             t = O._modmul(self.ff_q, nb[:, e:e + 1], he.power_of_psi[..., own])
             t = O._ntt_flat(self.ntt_q, t, inverse=False)
-            a = self.ks_out[:, e:e + 1, ..., :self.nq]
+            a = st["ks_out"][:, e:e + 1, ..., :self.nq]
             sub = np.where(a < t, a + q - t, a - t)
             outs.append(O._modmul(self.ff_q, sub, he.PInvModq[own]))
-        res = self.post + np.concatenate(outs, axis=1)
+        res = st["post"] + np.concatenate(outs, axis=1)
         res = np.where(res >= q, res - q, res)
         out.copy_(torch.from_numpy(np.ascontiguousarray(
             res.reshape(B, 2, -1, self.nq).transpose(0, 1, 3, 2)).view(np.int32)))
@@ -150,7 +154,7 @@ def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank))
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     try:
-        n, r, c, L, K, dnum, B = 1024, 32, 32, 5, 2, 2, 2
+        n, r, c, L, K, dnum, B = 1024, 32, 32, 5, 2, 2, 3
         ov = O.find_moduli_ntt(L + K, 28, 2 * n)
         Q, P = ov[:L], ov[L:]
         rng = np.random.default_rng(5)
@@ -167,6 +171,12 @@ def _worker(rank, world, port, q):
         got = got.numpy().view(U32)                                             # (B, 2, nq, N)
         ref = np.ascontiguousarray(want.reshape(B, 2, n, L - 1).transpose(0, 1, 3, 2))[:, :, sh.q0:sh.q1]
         assert np.array_equal(got, ref), f"rank {rank}: limbs [{sh.q0}, {sh.q1}) differ from one rank"
+        # the pipelined form, one ciphertext per call: three calls in flight
+        # use every workspace slot, and the gathers complete out of call order
+        calls = [torch.from_numpy(np.ascontiguousarray(x_own[i:i + 1]).view(np.int32)) for i in range(B)]
+        many = limb_shard.limb_sharded_mul_many(sh, calls, rank, world)
+        for i, g in enumerate(many):
+            assert np.array_equal(g.numpy().view(U32), ref[i:i + 1]), f"rank {rank}: pipelined call {i} differs"
         q.put((rank, "ok"))
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, repr(e)))
