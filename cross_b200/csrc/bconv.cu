@@ -430,38 +430,41 @@ __device__ __forceinline__ void bcc_load(const BconvTccArgs& a, int w, int tiles
     }
 }
 
-// c_i = Barrett_i(x_i QHatInvModq_i) of this thread's source groups as row
-// `row` of the K-major A tile (the exact 32-bit form for x < 2^31, where
-// x QHatInv < 2^31 q; the 64-bit form above).
+// c_i = Barrett_i(x_i QHatInvModq_i) of this thread's source groups (the
+// exact 32-bit form for x < 2^31, where x QHatInv < 2^31 q; the 64-bit form
+// above), and their store as row `row` of the K-major A tile.
 template <int H, int KB, int RED>
-__device__ __forceinline__ void bcc_pack(const BconvTccArgs& a, uint8_t* As, int row, const uint32_t (&xin)[4 * KB]) {
+__device__ __forceinline__ void bcc_reduce(const BconvTccArgs& a, const uint32_t (&xin)[4 * KB], uint32_t (&c)[4 * KB]) {
 #pragma unroll
   for (int k = 0; k < KB; ++k) {
-    if (k < a.kb) {
-      uint32_t c[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = 4 * (2 * k + H) + e;
-        uint32_t v = 0;
-        if (i < a.sq) {
-          const uint32_t xv = xin[4 * k + e], hv = a.k.sq_hi[i], q = a.k.sq_q[i], m = a.k.sq_m[i],
-                         sw = a.k.sq_sw[i];
-          if (RED == RED_MONTGOMERY) {
-            v = montgomery((uint64_t)xv * hv, q, m);                       // bconv.py:273
-          } else if (RED == RED_BAT_LAZY) {
-            const uint32_t r[4] = {m, sw, a.k.sq_r2[i], a.k.sq_r3[i]};
-            v = (uint32_t)bat_lazy((uint64_t)xv * hv, r) % q;             // bconv.py:382-386
-          } else {
-            v = xv < 0x80000000u ? reduce_fast2(xv * hv, __umulhi(xv, hv), q, m, sw)
-                                 : barrett_w32((uint64_t)xv * hv, q, m, sw);
-          }
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * (2 * k + H) + e;
+      uint32_t v = 0;
+      if (k < a.kb && i < a.sq) {
+        const uint32_t xv = xin[4 * k + e], hv = a.k.sq_hi[i], q = a.k.sq_q[i], m = a.k.sq_m[i],
+                       sw = a.k.sq_sw[i];
+        if (RED == RED_MONTGOMERY) {
+          v = montgomery((uint64_t)xv * hv, q, m);                       // bconv.py:273
+        } else if (RED == RED_BAT_LAZY) {
+          const uint32_t r[4] = {m, sw, a.k.sq_r2[i], a.k.sq_r3[i]};
+          v = (uint32_t)bat_lazy((uint64_t)xv * hv, r) % q;             // bconv.py:382-386
+        } else {
+          v = xv < 0x80000000u ? reduce_fast2(xv * hv, __umulhi(xv, hv), q, m, sw)
+                               : barrett_w32((uint64_t)xv * hv, q, m, sw);
         }
-        c[e] = v;
       }
-      *reinterpret_cast<uint4*>(As + k * 4096 + (row >> 3) * 256 + H * 128 + (row & 7) * 16) =
-          make_uint4(c[0], c[1], c[2], c[3]);
+      c[4 * k + e] = v;
     }
   }
+}
+template <int H, int KB>
+__device__ __forceinline__ void bcc_write(const BconvTccArgs& a, uint8_t* As, int row, const uint32_t (&c)[4 * KB]) {
+#pragma unroll
+  for (int k = 0; k < KB; ++k)
+    if (k < a.kb)
+      *reinterpret_cast<uint4*>(As + k * 4096 + (row >> 3) * 256 + H * 128 + (row & 7) * 16) =
+          make_uint4(c[4 * k], c[4 * k + 1], c[4 * k + 2], c[4 * k + 3]);
 }
 
 template <int H, int JH, bool TWIST>
@@ -549,26 +552,42 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tcc(const __grid_consta
   const uint32_t idesc = (2u << 4) | ((uint32_t)(a.nn >> 3) << 17) | ((uint32_t)(BT_ROWS >> 4) << 24);
   const int tiles_pp = n / BT_ROWS;
   const int total = a.polys * tiles_pp;
-  uint32_t xin[4 * KB];
+  // SHADOW (one source group): the next tile's reductions run while the MMA
+  // of this tile is in flight, and its inputs are loaded a tile further ahead
+  constexpr bool SHADOW = KB == 1;
+  uint32_t xin[4 * KB], cv[4 * KB];
   uint32_t tw[JH];
+  const int g = (int)gridDim.x;
   if ((int)blockIdx.x < total) {
     if (h == 0) bcc_load<0, KB, NN>(a, blockIdx.x, tiles_pp, row, xin);
     else bcc_load<1, KB, NN>(a, blockIdx.x, tiles_pp, row, xin);
+    if (SHADOW) {
+      if (h == 0) bcc_reduce<0, KB, RED>(a, xin, cv);
+      else bcc_reduce<1, KB, RED>(a, xin, cv);
+      if ((int)blockIdx.x + g < total) {
+        if (h == 0) bcc_load<0, KB, NN>(a, blockIdx.x + g, tiles_pp, row, xin);
+        else bcc_load<1, KB, NN>(a, blockIdx.x + g, tiles_pp, row, xin);
+      }
+    }
   }
   uint32_t phase = 0;
-  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+  for (int w = blockIdx.x; w < total; w += g) {
     const int poly = w / tiles_pp;
     const int t0 = (w - poly * tiles_pp) * BT_ROWS;
     // 1. source residues into the A tile, then the next tile's inputs and
     //    this tile's twists, in flight during the MMA
-    const bool more = w + (int)gridDim.x < total;
+    const bool more = w + g < total;
+    if (!SHADOW) {
+      if (h == 0) bcc_reduce<0, KB, RED>(a, xin, cv);
+      else bcc_reduce<1, KB, RED>(a, xin, cv);
+    }
     if (h == 0) {
-      bcc_pack<0, KB, RED>(a, As, row, xin);
-      if (more) bcc_load<0, KB, NN>(a, w + gridDim.x, tiles_pp, row, xin);
+      bcc_write<0, KB>(a, As, row, cv);
+      if (more && !SHADOW) bcc_load<0, KB, NN>(a, w + g, tiles_pp, row, xin);
       bcc_twist<0, JH, TWIST>(a, t0 + row, tw);
     } else {
-      bcc_pack<1, KB, RED>(a, As, row, xin);
-      if (more) bcc_load<1, KB, NN>(a, w + gridDim.x, tiles_pp, row, xin);
+      bcc_write<1, KB>(a, As, row, cv);
+      if (more && !SHADOW) bcc_load<1, KB, NN>(a, w + g, tiles_pp, row, xin);
       bcc_twist<1, JH, TWIST>(a, t0 + row, tw);
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -589,9 +608,19 @@ __global__ void __launch_bounds__(BT_THREADS, 4) k_bconv_tcc(const __grid_consta
       }
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
                    : "memory");
-      // 2. accumulator ready (one waiting thread; the others sleep in the barrier)
-      ok = mbar_wait(bar, phase, abort, a.err, 22);
     }
+    if (SHADOW && more) {
+      // the next tile's reductions (registers only: the MMA reads the A tile)
+      // and the inputs of the tile after it
+      if (h == 0) bcc_reduce<0, KB, RED>(a, xin, cv);
+      else bcc_reduce<1, KB, RED>(a, xin, cv);
+      if (w + 2 * g < total) {
+        if (h == 0) bcc_load<0, KB, NN>(a, w + 2 * g, tiles_pp, row, xin);
+        else bcc_load<1, KB, NN>(a, w + 2 * g, tiles_pp, row, xin);
+      }
+    }
+    // 2. accumulator ready (one waiting thread; the others sleep in the barrier)
+    if (t == 0) ok = mbar_wait(bar, phase, abort, a.err, 22);
     phase ^= 1;
     if (__syncthreads_or(!ok)) break;
     tc_fence_after();

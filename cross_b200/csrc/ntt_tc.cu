@@ -946,17 +946,20 @@ int stage(const cross_ntt_plan_s* P, const CUtensorMap& tmB, const CUtensorMap& 
 
 // ---------------------------------------------------------------------------
 // N = 2^12 (64 x 64): both contraction stages of a transform in one launch.
-// A CTA takes a pair of limb-polynomials of one plan limb (M = 128 rows, 64
-// per polynomial) and keeps everything in shared memory: the two stages' B
-// matrices (256 rows x 256 B each, TMA, SWIZZLE_128B), the stage-1 A tile
-// (written by the threads in the same swizzled K-major layout: transposed for
-// the forward transform, which contracts over r, as is for the inverse, which
-// contracts over c) and the stage-2 A tile, which the stage-1 epilogue writes
-// directly (byte recombination, Barrett, twiddle multiply, Barrett).  Per
+// A CTA takes one limb-polynomial at a time and keeps everything in shared
+// memory: the two stages' B matrices (256 rows x 256 B each, TMA,
+// SWIZZLE_128B), the stage-1 A tile (written by the threads in the same
+// swizzled K-major layout: transposed for the forward transform, which
+// contracts over r, as is for the inverse, which contracts over c) and the
+// stage-2 A tile, which the stage-1 epilogue writes directly (byte
+// recombination, Barrett, twiddle multiply, Barrett).  The polynomial's 64
+// rows fill both halves of each 128-row A tile, so the accumulator's lanes
+// 64..127 repeat lanes 0..63 and the warps of the upper lane quadrants reduce
+// the other half of the outputs: eight outputs per thread and stage.  Per
 // stage 8 tcgen05.mma kind::i8 of M = 128, N = 256, K = 32 into one 256-column
 // TMEM accumulator; the stage-2 epilogue (recombination, Barrett) stores the
 // natural-order result.  Bounded waits as in k_bat_tc (codes 41 to 44).
-constexpr int T64_THREADS = 512;   // 16 warps: four per TMEM lane quadrant, 16 outputs each per stage
+constexpr int T64_THREADS = 512;   // 16 warps: four per TMEM lane quadrant, 8 outputs each per stage
 struct Smem64 {
   uint8_t b1[2][256 * 128];    // stage-1 B: two 128-byte K chunks of 256 rows
   uint8_t b2[2][256 * 128];    // stage-2 B
@@ -1003,8 +1006,7 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   Smem64& S = *reinterpret_cast<Smem64*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int64_t pairs = (a.polys + 1) / 2;
-  const int64_t total = (int64_t)a.slots * pairs;
+  const int64_t total = (int64_t)a.slots * a.polys;   // one limb-polynomial per item
   const int64_t i0 = total * blockIdx.x / gridDim.x, i1 = total * (blockIdx.x + 1) / gridDim.x;
   if (t == 0) {
     mbar_init(&S.bbar, 1);
@@ -1027,15 +1029,17 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
   const uint32_t tmem = S.tmem_base;
   uint32_t bphase = 0, mphase = 0;
   int cur_slot = -1;
-  // epilogue role: TMEM lane quadrant q = warp % 4 (rows 32 q .. 32 q + 31),
-  // output quarter h = warp / 4 (outputs 16 h .. 16 h + 15, accumulator
-  // columns 64 h .. 64 h + 63)
+  // epilogue role: the A tiles hold the polynomial's 64 rows twice (rows
+  // 0..63 and 64..127), so TMEM lanes 64..127 repeat lanes 0..63.  Lane
+  // quadrant q = warp % 4 gives row mm (quadrants 0-1 and 2-3 cover the 64 rows
+  // each) and the output half (quadrants 0-1: outputs 0..31, 2-3: 32..63); the
+  // output eighth h = warp / 4 within the half gives the thread's eight
+  // outputs ob .. ob + 7, accumulator columns 4 ob .. 4 ob + 31
   const int q = warp & 3, h = warp >> 2;
-  const int m = 32 * q + lane, mp = m >> 6, mm = m & 63;
+  const int mm = (32 * q + lane) & 63, ob = 32 * (q >> 1) + 8 * h;
   for (int64_t it = i0; it < i1; ++it) {
-    const int slot = (int)(it / pairs);
-    const int64_t p0 = 2 * (it - (int64_t)slot * pairs);
-    const bool two = p0 + 1 < a.polys;
+    const int slot = (int)(it / a.polys);
+    const int64_t p = it - (int64_t)slot * a.polys;
     const int limb = a.limbs[slot];
     if (slot != cur_slot && t == 0) {
       // the MMAs that read the previous slot's B tiles have completed (waited below)
@@ -1045,11 +1049,9 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
         tma_load_2d(S.b2[kc], &tmB2, &S.bbar, kc * 128, limb * 256);
       }
     }
-    // stage-1 A tile from global memory
-#pragma unroll
-    for (int pp = 0; pp < 2; ++pp) {
-      if (pp == 1 && !two) break;
-      const uint32_t* x = a.in.p + (p0 + pp) * a.in.ps + (int64_t)slot * a.in.ss;
+    // stage-1 A tile from global memory, each row stored twice
+    {
+      const uint32_t* x = a.in.p + p * a.in.ps + (int64_t)slot * a.in.ss;
       if (!INV) {
         // forward: A rows c, K words r (the transpose of X[r][c])
         const int c = t & 63, rg = t >> 6;
@@ -1061,7 +1063,8 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
           v.y = __ldg(x + (r0 + 1) * 64 + c);
           v.z = __ldg(x + (r0 + 2) * 64 + c);
           v.w = __ldg(x + (r0 + 3) * 64 + c);
-          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(pp * 64 + c, r0 >> 2)) = v;
+          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(c, r0 >> 2)) = v;
+          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(64 + c, r0 >> 2)) = v;
         }
       } else {
         // inverse: A rows r, K words c (X as stored)
@@ -1070,18 +1073,19 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
         for (int i = 0; i < 2; ++i) {
           const int r = (t >> 4) + 32 * i;
           const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + r * 64) + c4);
-          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(pp * 64 + r, c4)) = v;
+          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(r, c4)) = v;
+          *reinterpret_cast<uint4*>(&S.a1[0][0] + sw_off(64 + r, c4)) = v;
         }
       }
     }
     // stage-1 twiddles of this thread's outputs, in flight during the MMA
     const ModC mc = a.mods[limb];
     const uint32_t q32 = (uint32_t)mc.q, m32 = (uint32_t)mc.m, sw = mc.s_w;
-    uint32_t tw[16];
+    uint32_t tw[8];
     {
       const uint32_t* tb = a.tw + (int64_t)limb * 4096 + mm;
 #pragma unroll
-      for (int o = 0; o < 16; ++o) tw[o] = __ldg(tb + (16 * h + o) * 64);
+      for (int o = 0; o < 8; ++o) tw[o] = __ldg(tb + (ob + o) * 64);
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
@@ -1104,17 +1108,16 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
     __syncthreads();
     if (S.abort) break;
     tc_fence_after();
-    // stage-1 epilogue: Y = Barrett(Barrett(sum) x twiddle) into the stage-2 A tile
-    // (row: output index o of this polynomial, K word: this thread's row mm)
-#pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
+    // stage-1 epilogue: Y = Barrett(Barrett(sum) x twiddle) into the stage-2 A
+    // tile (row: output index o, stored twice; K word: this thread's row mm)
+    {
       uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * h + 32 * ch, v);
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 4 * ob, v);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int o = 16 * h + 8 * ch + j;
+        const int o = ob + j;
         const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        const uint32_t wv = tw[8 * ch + j];
+        const uint32_t wv = tw[j];
         uint32_t r;
         if (FAST) {
           r = reduce_fast(z, q32, m32, sw);
@@ -1123,7 +1126,8 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
           r = barrett(z, mc);
           r = barrett((uint64_t)r * wv, mc);
         }
-        *reinterpret_cast<uint32_t*>(&S.a2[0][0] + sw_off(mp * 64 + o, mm >> 2) + 4 * (mm & 3)) = r;
+        *reinterpret_cast<uint32_t*>(&S.a2[0][0] + sw_off(o, mm >> 2) + 4 * (mm & 3)) = r;
+        *reinterpret_cast<uint32_t*>(&S.a2[0][0] + sw_off(64 + o, mm >> 2) + 4 * (mm & 3)) = r;
       }
     }
     tc_fence_before();
@@ -1139,30 +1143,25 @@ __global__ void __launch_bounds__(T64_THREADS, 1)
     if (S.abort) break;
     tc_fence_after();
     // stage-2 epilogue: Barrett, natural-order stores of this polynomial
-    const bool store = mp == 0 || two;
-    uint32_t* y = a.out.p + (p0 + mp) * a.out.ps + (int64_t)slot * a.out.ss;
-#pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
+    {
+      uint32_t* y = a.out.p + p * a.out.ps + (int64_t)slot * a.out.ss;
       uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 64 * h + 32 * ch, v);
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 4 * ob, v);
       uint32_t res[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint64_t z = combine4_mad(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         res[j] = FAST ? reduce_fast(z, q32, m32, sw) : barrett(z, mc);
       }
-      if (store) {
-        const int o0 = 16 * h + 8 * ch;
-        if (!INV) {
-          // forward: Z[z][n], this thread's row z = mm, outputs n = o0 .. o0 + 7
-          uint4* d = reinterpret_cast<uint4*>(y + mm * 64 + o0);
-          d[0] = make_uint4(res[0], res[1], res[2], res[3]);
-          d[1] = make_uint4(res[4], res[5], res[6], res[7]);
-        } else {
-          // inverse: Z[l][c], this thread's column c = mm, rows l = o0 .. o0 + 7
+      if (!INV) {
+        // forward: Z[z][n], this thread's row z = mm, outputs n = ob .. ob + 7
+        uint4* d = reinterpret_cast<uint4*>(y + mm * 64 + ob);
+        d[0] = make_uint4(res[0], res[1], res[2], res[3]);
+        d[1] = make_uint4(res[4], res[5], res[6], res[7]);
+      } else {
+        // inverse: Z[l][c], this thread's column c = mm, rows l = ob .. ob + 7
 #pragma unroll
-          for (int j = 0; j < 8; ++j) y[(o0 + j) * 64 + mm] = res[j];
-        }
+        for (int j = 0; j < 8; ++j) y[(ob + j) * 64 + mm] = res[j];
       }
     }
     tc_fence_before();
@@ -1319,7 +1318,7 @@ int ntt_exec_tc(const cross_ntt_plan_s* P, bool inverse, LP in, int in_layout, L
 // coefficient order on both sides, in one launch.
 int ntt64_run(const cross_ntt_plan_s* P, bool inverse, LP in, LPo out, int64_t polys, int slots,
               const uint16_t* limbs, cudaStream_t st) {
-  const int64_t total = (int64_t)slots * ((polys + 1) / 2);
+  const int64_t total = (int64_t)slots * polys;
   if (total == 0) return CROSS_OK;
   tc::Args64 a{in, out, polys, slots, limbs, P->mods, inverse ? P->tc_tw_inv : P->tw_fwd, P->tc_err};
   const int sms = device_sm_count();

@@ -67,12 +67,13 @@ def test_tensor_core_path_matches_cuda_core_path(monkeypatch):
 
 @pytest.mark.parametrize("B,L", [(16, 8), (3, 5), (300, 1), (40, 8)])
 def test_ntt64_single_launch_vs_oracle(monkeypatch, B, L):
-    """N = 2^12 (64 x 64): the single-launch tensor-core transform (two
-    polynomials of one limb per CTA) against the oracle and against the
-    CUDA-core path, for the benchmark shape (16 x 8), an odd batch (the last
-    pair has one polynomial), CTAs that walk several pairs of one limb (300 x 1)
-    and CTAs whose pairs cross a limb boundary (40 x 8); limb-major through the
-    C ABI, in place, and in the reference layout through the context."""
+    """N = 2^12 (64 x 64): the single-launch tensor-core transform (one
+    limb-polynomial at a time per CTA, its rows in both halves of the 128-row
+    tiles) against the oracle and against the CUDA-core path, for the
+    benchmark shape (16 x 8), an odd batch (3 x 5), CTAs that walk several
+    polynomials of one limb (300 x 1: more items than CTAs) and CTAs whose
+    items cross a limb boundary (40 x 8); limb-major through the C ABI, in
+    place, and in the reference layout through the context."""
     import torch
     from cross_b200 import _lib, ntt_mm
     n = 4096
