@@ -2,6 +2,7 @@
 // tables, the HE tensor product, modular add, the Galois permutation and the
 // layout conversions.  All are HBM-bound; indices are 64-bit.
 #include "internal.hpp"
+#include "tc_ptx.cuh"
 
 namespace cross {
 
@@ -101,6 +102,117 @@ __global__ void k_gather_rows(const uint32_t* __restrict__ in, const int32_t* __
     out[i] = (src < 0 || src >= n) ? 0xFFFFFFFFu : in[(p * n + src) * M + m];
   }
 }
+
+// 32-bit index forms of the four kernels above, for launches of fewer than
+// 2^31 elements (every call of the HE parameter sets): the limb of element i
+// is one 32-bit remainder, and the other index splits are a 32-bit remainder
+// or, for a power-of-two ring dimension (log2n >= 0), a shift and a mask,
+// instead of 64-bit divisions per element.
+template <bool U64IN>
+__global__ void k_mod_reduce32(const void* __restrict__ in, uint32_t* __restrict__ out, uint32_t total,
+                               uint32_t M, const ModC* __restrict__ mods) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint64_t z = U64IN ? ((const uint64_t*)in)[i] : (uint64_t)((const uint32_t*)in)[i];
+    out[i] = barrett_any(z, mods[i % M]);
+  }
+}
+
+// modmul with the broadcast table: b's element for i is (i / M % b_rows) M +
+// i % M = i % (b_rows M); bm = b_rows M, or 0 when b covers every row.
+template <bool A64, bool B64>
+__global__ void k_modmul32(const void* __restrict__ a, const void* __restrict__ b, uint32_t bm,
+                           uint32_t* __restrict__ out, uint32_t total, uint32_t M, const ModC* __restrict__ mods) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t bi = bm ? i % bm : i;
+    const uint64_t x = A64 ? ((const uint64_t*)a)[i] : (uint64_t)((const uint32_t*)a)[i];
+    const uint64_t y = B64 ? ((const uint64_t*)b)[bi] : (uint64_t)((const uint32_t*)b)[bi];
+    out[i] = barrett_any(x * y, mods[i % M]);
+  }
+}
+
+__global__ void k_add_mod32(const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                            uint32_t* __restrict__ out, uint32_t total, uint32_t n, int log2n, uint32_t M,
+                            const ModC* __restrict__ mods) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t row = log2n >= 0 ? i >> log2n : i / n;
+    const uint32_t q = (uint32_t)mods[row % M].q;
+    const uint32_t s = a[i] + b[i];
+    out[i] = s > q ? s - q : s;
+  }
+}
+
+__global__ void k_gather_rows32(const uint32_t* __restrict__ in, const int32_t* __restrict__ map,
+                                uint32_t* __restrict__ out, uint32_t total, uint32_t n, int log2n, uint32_t M) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t row = i / M, m = i - row * M;
+    const uint32_t p = log2n >= 0 ? row >> log2n : row / n;
+    const uint32_t j = row - p * n;
+    int64_t src = map[j];
+    // jnp.take's default mode, as in k_gather_rows
+    if (src < 0) src += n;
+    out[i] = (src < 0 || src >= (int64_t)n) ? 0xFFFFFFFFu : in[((int64_t)p * n + src) * M + m];
+  }
+}
+
+// Barrett of x * y for modulus c = {q, m, s_w, forms} (cross_moduli_s::dev_f):
+// the exact 32-bit remainder form when the modulus allows it and the product
+// is a word below 2^31 times a residue (tc::reduce_fast2's exactness bound),
+// barrett_w32 for other inputs of a w = 32 modulus, the generic form else.
+// Every branch returns finite_field.py's value.
+__device__ __forceinline__ uint32_t mulmod_packed(uint32_t x, uint32_t y, const uint4& c, const ModC& mc) {
+  if ((c.w & 2u) && x < 0x80000000u && y < c.x) return tc::reduce_fast2(x * y, __umulhi(x, y), c.x, c.y, c.z);
+  if (c.w & 1u) return barrett_w32((uint64_t)x * y, c.x, c.y, c.z);
+  return barrett((uint64_t)x * y, mc);
+}
+
+// 16-byte forms of the uint32 modmul and add: four consecutive elements per
+// thread, one remainder per four (their limbs follow in turn for modmul; they
+// share one limb for add, whose ring dimension is a multiple of 4).  The
+// launcher picks them for 16-byte aligned buffers whose sizes are multiples
+// of 4 (the table period bm too).  modmul reads each limb's constants as one
+// packed 16-byte record.
+template <bool BCAST>
+__global__ void k_modmul32v(const uint32_t* __restrict__ a, const uint32_t* __restrict__ b, uint32_t bm,
+                            uint32_t* __restrict__ out, uint32_t total4, uint32_t M, const ModC* __restrict__ mods,
+                            const uint4* __restrict__ fc) {
+  for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < total4; v += gridDim.x * blockDim.x) {
+    const uint32_t i = 4 * v;
+    const uint4 x = reinterpret_cast<const uint4*>(a)[v];
+    const uint4 y = *reinterpret_cast<const uint4*>(b + (BCAST ? i % bm : i));
+    uint32_t m = i % M;
+    uint4 r;
+    r.x = mulmod_packed(x.x, y.x, __ldg(fc + m), mods[m]);
+    m = m + 1 == M ? 0 : m + 1;
+    r.y = mulmod_packed(x.y, y.y, __ldg(fc + m), mods[m]);
+    m = m + 1 == M ? 0 : m + 1;
+    r.z = mulmod_packed(x.z, y.z, __ldg(fc + m), mods[m]);
+    m = m + 1 == M ? 0 : m + 1;
+    r.w = mulmod_packed(x.w, y.w, __ldg(fc + m), mods[m]);
+    reinterpret_cast<uint4*>(out)[v] = r;
+  }
+}
+
+__global__ void k_add_mod32v(const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                             uint32_t* __restrict__ out, uint32_t total4, uint32_t n, int log2n, uint32_t M,
+                             const ModC* __restrict__ mods) {
+  for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < total4; v += gridDim.x * blockDim.x) {
+    const uint32_t i = 4 * v;
+    const uint32_t row = log2n >= 0 ? i >> log2n : i / n;
+    const uint32_t q = (uint32_t)mods[row % M].q;
+    const uint4 x = reinterpret_cast<const uint4*>(a)[v], y = reinterpret_cast<const uint4*>(b)[v];
+    uint4 s = make_uint4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+    s.x = s.x > q ? s.x - q : s.x;
+    s.y = s.y > q ? s.y - q : s.y;
+    s.z = s.z > q ? s.z - q : s.z;
+    s.w = s.w > q ? s.w - q : s.w;
+    reinterpret_cast<uint4*>(out)[v] = s;
+  }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+int log2_or_neg(int64_t n) { return n > 0 && (n & (n - 1)) == 0 ? __builtin_ctzll((unsigned long long)n) : -1; }
+constexpr int64_t EW32_LIMIT = (int64_t)1 << 31;
 
 // Batched transpose (batch, rows, cols) -> (batch, cols, rows) through a
 // 32x33 shared tile (coalesced on both sides).
@@ -380,10 +492,16 @@ int cross_mod_reduce(cross_moduli mods, const void* in, int in_is_u64, uint32_t*
   CROSS_REQUIRE(mods && rows >= 0 && (rows == 0 || (in && out)), "cross_mod_reduce: bad argument");
   const int64_t total = rows * mods->n;
   if (total == 0) return CROSS_OK;
-  if (in_is_u64) {
-    k_mod_reduce<true><<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, out, total, mods->n, mods->dev);
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (total < EW32_LIMIT) {
+    if (in_is_u64)
+      k_mod_reduce32<true><<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(in, out, (uint32_t)total, mods->n, mods->dev);
+    else
+      k_mod_reduce32<false><<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(in, out, (uint32_t)total, mods->n, mods->dev);
+  } else if (in_is_u64) {
+    k_mod_reduce<true><<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(in, out, total, mods->n, mods->dev);
   } else {
-    k_mod_reduce<false><<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, out, total, mods->n, mods->dev);
+    k_mod_reduce<false><<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(in, out, total, mods->n, mods->dev);
   }
   count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
@@ -426,8 +544,33 @@ int cross_modmul(cross_moduli mods, const void* a, int a_is_u64, const void* b, 
   CROSS_REQUIRE(mods && rows >= 0 && b_rows >= 1 && (rows == 0 || (a && b && out)), "cross_modmul: bad argument");
   const int64_t total = rows * mods->n;
   if (total == 0) return CROSS_OK;
-  k_modmul_ref<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, a_is_u64, b, b_is_u64, b_rows, out,
-                                                                            total, mods->n, mods->dev); count_launch();
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (total < EW32_LIMIT) {
+    const int64_t bm = b_rows >= rows ? 0 : b_rows * mods->n;
+    const unsigned g = ew_blocks(total, 4);
+    const uint32_t t32 = (uint32_t)total, M = (uint32_t)mods->n;
+    if (!a_is_u64 && !b_is_u64 && total % 4 == 0 && bm % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out)) {
+      const auto* a32 = static_cast<const uint32_t*>(a);
+      const auto* b32 = static_cast<const uint32_t*>(b);
+      const unsigned gv = ew_blocks(total / 4, 1);
+      if (bm)
+        k_modmul32v<true><<<gv, EW_THREADS, 0, st>>>(a32, b32, (uint32_t)bm, out, t32 / 4, M, mods->dev, mods->dev_f);
+      else
+        k_modmul32v<false><<<gv, EW_THREADS, 0, st>>>(a32, b32, 0u, out, t32 / 4, M, mods->dev, mods->dev_f);
+    } else if (a_is_u64 && b_is_u64) {
+      k_modmul32<true, true><<<g, EW_THREADS, 0, st>>>(a, b, (uint32_t)bm, out, t32, M, mods->dev);
+    } else if (a_is_u64) {
+      k_modmul32<true, false><<<g, EW_THREADS, 0, st>>>(a, b, (uint32_t)bm, out, t32, M, mods->dev);
+    } else if (b_is_u64) {
+      k_modmul32<false, true><<<g, EW_THREADS, 0, st>>>(a, b, (uint32_t)bm, out, t32, M, mods->dev);
+    } else {
+      k_modmul32<false, false><<<g, EW_THREADS, 0, st>>>(a, b, (uint32_t)bm, out, t32, M, mods->dev);
+    }
+  } else {
+    k_modmul_ref<<<ew_blocks(total, 4), EW_THREADS, 0, st>>>(a, a_is_u64, b, b_is_u64, b_rows, out, total, mods->n,
+                                                          mods->dev);
+  }
+  count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }
@@ -450,7 +593,15 @@ int cross_add_mod(cross_moduli mods, const uint32_t* a, const uint32_t* b, uint3
                 "cross_add_mod: bad argument");
   const int64_t total = elements * mods->n * n;
   if (total == 0) return CROSS_OK;
-  k_add_mod<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, b, out, total, n, mods->n, mods->dev); count_launch();
+  if (total < EW32_LIMIT && n % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out))
+    k_add_mod32v<<<ew_blocks(total / 4, 1), EW_THREADS, 0, (cudaStream_t)stream>>>(
+        a, b, out, (uint32_t)(total / 4), (uint32_t)n, log2_or_neg(n), mods->n, mods->dev);
+  else if (total < EW32_LIMIT)
+    k_add_mod32<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, b, out, (uint32_t)total, (uint32_t)n,
+                                                                             log2_or_neg(n), mods->n, mods->dev);
+  else
+    k_add_mod<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(a, b, out, total, n, mods->n, mods->dev);
+  count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }
@@ -461,7 +612,12 @@ int cross_automorphism(const uint32_t* in, const int32_t* coef_map, uint32_t* ou
                 "cross_automorphism: bad argument (in and out must differ)");
   const int64_t total = polys * n * num_limbs;
   if (total == 0) return CROSS_OK;
-  k_gather_rows<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, coef_map, out, polys, n, num_limbs); count_launch();
+  if (total < EW32_LIMIT)
+    k_gather_rows32<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(
+        in, coef_map, out, (uint32_t)total, (uint32_t)n, log2_or_neg(n), (uint32_t)num_limbs);
+  else
+    k_gather_rows<<<ew_blocks(total, 4), EW_THREADS, 0, (cudaStream_t)stream>>>(in, coef_map, out, polys, n, num_limbs);
+  count_launch();
   CROSS_CHECK_CUDA(cudaGetLastError());
   return CROSS_OK;
 }

@@ -119,11 +119,17 @@ int cross_moduli_create(int num_moduli, const uint32_t* moduli, const uint64_t* 
     }
     s->host.push_back(cross::ModC{moduli[i], barrett_m[i], barrett_w[i], barrett_s_w[i]});
   }
+  std::vector<uint4> packed;
+  for (const cross::ModC& mc : s->host)
+    packed.push_back(make_uint4((uint32_t)mc.q, (uint32_t)mc.m, mc.s_w,
+                                (cross::barrett_w32_ok(mc) ? 1u : 0u) | (cross::reduce_fast_ok(mc) ? 2u : 0u)));
   int rc = cross::upload_vec(&s->dev, s->host);
   if (!rc) rc = cross::upload_vec(&s->dev_v, cross::make_varc(s->host));
+  if (!rc) rc = cross::upload_vec(&s->dev_f, packed);
   if (rc) {
     cross::dfree(s->dev);
     cross::dfree(s->dev_v);
+    cross::dfree(s->dev_f);
     delete s;
     return rc;
   }
@@ -135,6 +141,7 @@ int cross_moduli_destroy(cross_moduli m) {
   if (!m) return CROSS_OK;
   cross::dfree(m->dev);
   cross::dfree(m->dev_v);
+  cross::dfree(m->dev_f);
   delete m;
   return CROSS_OK;
 }

@@ -14,6 +14,8 @@ struct cross_moduli_s {
   std::vector<cross::ModC> host;
   cross::ModC* dev = nullptr;
   cross::VarC* dev_v = nullptr;     // Montgomery / Shoup / BAT-lazy constants of the same moduli
+  uint4* dev_f = nullptr;           // per modulus {q, m, s_w, forms}: the element-wise kernels' packed
+                                    // Barrett constants (forms bit 0: barrett_w32 exact, bit 1: reduce_fast exact)
 };
 
 // NTT plan: the reference's BAT tables re-laid out for the kernels.

@@ -735,3 +735,108 @@ def test_ntt_refuses_unaligned_row_major_output():
     assert int(buf.count_nonzero()) == 0                           # nothing was written
     np.testing.assert_array_equal(_np(ctx.ntt(x)), O.NTTBarrett(q, 256, 256).ntt(x))
     ctx.check_device()
+
+
+@pytest.mark.parametrize("a64,b64", [(False, False), (True, False), (False, True), (True, True)])
+def test_elementwise_index_forms(a64, b64):
+    """The element-wise kernels' index arithmetic (32-bit forms below 2^31
+    elements) on shapes that exercise every split: cross_modmul with a table
+    broadcast over rows (b_rows not dividing rows) and every operand width
+    (ciphertext.py:189-193; products wrap in uint64), cross_add_mod at a
+    ring dimension that is not a power of two (add.py:7-27), cross_automorphism
+    with negative and out-of-range map entries (jnp.take's default mode,
+    herot.py:300), and cross_mod_reduce of uint32 and uint64 input."""
+    import torch
+    from cross_b200 import _lib, finite_field
+    lib = _lib.lib()
+    q = O.find_moduli_ntt(5, 28, 2 * 64)
+    M = len(q)
+    ff = finite_field.BarrettContext(q)
+    bar = O.Barrett(q)
+    rng = np.random.default_rng(11 + 2 * a64 + b64)
+    rows, b_rows = 105, 7
+    a = rng.integers(0, 2 ** 63, size=(rows, M), dtype=np.uint64) if a64 else rng_residues(rng, (rows, M), q)
+    b = rng.integers(0, 2 ** 63, size=(b_rows, M), dtype=np.uint64) if b64 else rng_residues(rng, (b_rows, M), q)
+    want = bar.reduce(a.astype(np.uint64) * b.astype(np.uint64)[np.arange(rows) % b_rows])
+    da, db = torch.from_numpy(a.view(np.int64) if a64 else a.view(np.int32)).cuda(), \
+        torch.from_numpy(b.view(np.int64) if b64 else b.view(np.int32)).cuda()
+    out = torch.empty((rows, M), dtype=torch.int32, device="cuda")
+    _lib.check(lib.cross_modmul(ff.handle(), da.data_ptr(), int(a64), db.data_ptr(), int(b64), b_rows,
+                                out.data_ptr(), rows, None), "cross_modmul")
+    np.testing.assert_array_equal(out.cpu().numpy().view(U32), want)
+    # add at n = 24 on (E, M, n): the sum minus q where it is strictly above q
+    E, n = 3, 24
+    x = rng_residues(rng, (E, n, M), q).transpose(0, 2, 1).copy()
+    y = rng_residues(rng, (E, n, M), q).transpose(0, 2, 1).copy()
+    x[1, 2, :5] = np.uint32(q[2]) - y[1, 2, :5]
+    dx, dy = torch.from_numpy(x.view(np.int32)).cuda(), torch.from_numpy(y.view(np.int32)).cuda()
+    dz = torch.empty_like(dx)
+    _lib.check(lib.cross_add_mod(ff.handle(), dx.data_ptr(), dy.data_ptr(), dz.data_ptr(), E, n, None),
+               "cross_add_mod")
+    np.testing.assert_array_equal(dz.cpu().numpy().view(U32), O.jax_add(x, y, q))
+    # automorphism at n = 24 with a map holding negative and out-of-range entries
+    polys = 3
+    src = rng.integers(0, 2 ** 32, size=(polys, n, M), dtype=np.uint64).astype(U32)
+    cmap = rng.integers(-30, 30, size=n).astype(np.int32)
+    idx = np.where(cmap < 0, cmap + n, cmap)
+    ok = (idx >= 0) & (idx < n)
+    ref = np.where(ok[None, :, None], src[:, np.clip(idx, 0, n - 1)], np.uint32(0xFFFFFFFF))
+    ds = torch.from_numpy(src.view(np.int32)).cuda()
+    dm = torch.from_numpy(cmap).cuda()
+    do = torch.empty_like(ds)
+    _lib.check(lib.cross_automorphism(ds.data_ptr(), dm.data_ptr(), do.data_ptr(), polys, n, M, None),
+               "cross_automorphism")
+    np.testing.assert_array_equal(do.cpu().numpy().view(U32), ref)
+    # Barrett of uint32 and uint64 input
+    z = rng.integers(0, 2 ** 63, size=(rows, M), dtype=np.uint64)
+    dz64 = torch.from_numpy(z.view(np.int64)).cuda()
+    dr = torch.empty((rows, M), dtype=torch.int32, device="cuda")
+    _lib.check(lib.cross_mod_reduce(ff.handle(), dz64.data_ptr(), 1, dr.data_ptr(), rows, None), "cross_mod_reduce")
+    np.testing.assert_array_equal(dr.cpu().numpy().view(U32), bar.reduce(z))
+    z32 = (z & np.uint64(0xFFFFFFFF)).astype(U32)
+    dz32 = torch.from_numpy(z32.view(np.int32)).cuda()
+    _lib.check(lib.cross_mod_reduce(ff.handle(), dz32.data_ptr(), 0, dr.data_ptr(), rows, None), "cross_mod_reduce")
+    np.testing.assert_array_equal(dr.cpu().numpy().view(U32), bar.reduce(z32.astype(np.uint64)))
+
+
+@pytest.mark.parametrize("b_rows,offset,full", [(8, 0, False), (112, 0, False), (112, 0, True), (8, 1, False),
+                                                (7, 0, False)])
+def test_elementwise_vector_forms(b_rows, offset, full):
+    """The 16-byte forms of cross_modmul (uint32 operands, sizes and the table
+    period multiples of 4; residue operands take the exact 32-bit remainder
+    form, full-range words the 64-bit one) and cross_add_mod (ring dimension a
+    multiple of 4), and their fallbacks: buffers one word off a 16-byte
+    boundary, a table period of 35 words, a ring dimension of 26."""
+    import torch
+    from cross_b200 import _lib, finite_field
+    lib = _lib.lib()
+    q = O.find_moduli_ntt(5, 28, 2 * 64)
+    M = len(q)
+    ff = finite_field.BarrettContext(q)
+    rng = np.random.default_rng(100 + b_rows + offset + 7 * full)
+    rows = 112
+    draw = (lambda shape: rng.integers(0, 2 ** 32, size=shape, dtype=np.uint64).astype(U32)) if full else \
+        (lambda shape: rng_residues(rng, shape, q))
+    a, b = draw((rows, M)), draw((b_rows, M))
+    want = O.Barrett(q).reduce(a.astype(np.uint64) * b.astype(np.uint64)[np.arange(rows) % b_rows])
+
+    def dev(x):   # device copy starting `offset` words into a buffer
+        t = torch.zeros(x.size + 4, dtype=torch.int32, device="cuda")
+        t[offset:offset + x.size] = torch.from_numpy(x.reshape(-1).view(np.int32)).cuda()
+        return t
+
+    da, db, do = dev(a), dev(b), dev(np.zeros((rows, M), U32))
+    _lib.check(lib.cross_modmul(ff.handle(), da.data_ptr() + 4 * offset, 0, db.data_ptr() + 4 * offset, 0, b_rows,
+                                do.data_ptr() + 4 * offset, rows, None), "cross_modmul")
+    got = do.cpu().numpy().view(U32)
+    np.testing.assert_array_equal(got[offset:offset + rows * M].reshape(rows, M), want)
+    assert not got[:offset].any() and not got[offset + rows * M:].any()     # nothing written outside
+    for E, n in ((3, 24), (2, 26)):
+        x = rng_residues(rng, (E, n, M), q).transpose(0, 2, 1).copy()
+        y = rng_residues(rng, (E, n, M), q).transpose(0, 2, 1).copy()
+        x[0, 1, :3] = np.uint32(q[1]) - y[0, 1, :3]
+        dx, dy, dz = dev(x), dev(y), dev(np.zeros_like(x))
+        _lib.check(lib.cross_add_mod(ff.handle(), dx.data_ptr() + 4 * offset, dy.data_ptr() + 4 * offset,
+                                     dz.data_ptr() + 4 * offset, E, n, None), "cross_add_mod")
+        z = dz.cpu().numpy().view(U32)
+        np.testing.assert_array_equal(z[offset:offset + x.size].reshape(x.shape), O.jax_add(x, y, q))
