@@ -51,3 +51,39 @@ def test_reference_arm_bts_line():
 def test_reference_arm_other_ranks_exit_quietly(rank):
     """Under torchrun only rank 0 runs the reference arm and prints."""
     assert _run(["--impl", "reference", "--steps", "1", "--warmup", "0"], env={"RANK": rank}, timeout=120) == []
+
+
+def _digits(total, dnum):
+    """Sizes of the key-switch digits (ciphertext.py:329-419: ceil(total / dnum)
+    limbs per digit, the last one shorter)."""
+    alpha = -(-total // dnum)
+    return [min(alpha, total - j * alpha) for j in range(-(-total // alpha))]
+
+
+@pytest.mark.parametrize("workload,L,K,dnum,transforms", [("hemul", 24, 8, 3, 251), ("hemul", 35, 7, 5, 427),
+                                                          ("herot", 24, 8, 3, 160)])
+def test_operator_work_counts(workload, L, K, dnum, transforms):
+    """The algorithmic work the roofline fractions divide by, restated from the
+    operation sequence of hemul.py:153-217 / herot.py:183-302: limb-transforms
+    per ciphertext (rescale: INTT of the last limb of 4 elements and NTT of the
+    lift into L' limbs; key switch: INTT of d2, the NTT of every digit's
+    converted limbs; ModDown: INTT of the K limbs and NTT of the L' limbs of 2
+    elements) and the basis conversions' byte-plane contractions."""
+    sys.path.insert(0, ROOT)
+    import bench
+    pt = bench.Point(workload, L, K, dnum, 64, 64)
+    N = 65536
+    if workload == "hemul":
+        L1 = L - 1
+        parts = _digits(L1, dnum)
+        want_t = 4 + 4 * L1 + L1 + sum(L1 + K - a for a in parts) + 2 * K + 2 * L1
+        convs = [(a, L1 + K - a) for a in parts] + [(K, L1), (K, L1)]
+    else:
+        parts = _digits(L, dnum)
+        want_t = L + sum(L + K - a for a in parts) + 2 * K + 2 * L
+        convs = [(a, L + K - a) for a in parts] + [(K, L), (K, L)]
+    assert want_t == transforms == pt.transforms_per_ct()
+    per_transform = 2 * 2 * (4 * 256) * (4 * 256) * 256      # two BAT stages of 2 (4K)(4K) per output row, K = 256
+    assert per_transform == 32 * N * (256 + 256)
+    want_ops = transforms * per_transform + sum(2 * N * (4 * sq) * (4 * sp) for sq, sp in convs)
+    assert pt.int8_ops_per_ct() == pytest.approx(want_ops, rel=1e-12)
