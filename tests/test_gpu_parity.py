@@ -711,10 +711,10 @@ def test_hemul_non_square_tensor_core_vs_oracle():
 
 
 def test_ntt_refuses_unaligned_row_major_output():
-    """The row-major stages write 16-byte pieces (bulk tensor stores); an
-    output pointer off a 16-byte boundary through the C ABI is refused with
-    CROSS_ERR_INVALID_ARG before the row stage launches, and the context keeps
-    computing bit-exact results."""
+    """The row-major contraction stages write their outputs with 16-byte
+    stores; an output pointer off a 16-byte boundary through the C ABI is
+    refused with CROSS_ERR_INVALID_ARG before the row stage launches, and the
+    context keeps computing bit-exact results."""
     import torch
     from cross_b200 import _lib, ntt_mm
     q = O.find_moduli_ntt(2, 28, 2 * 65536)
