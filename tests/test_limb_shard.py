@@ -200,3 +200,48 @@ def test_limb_sharded_hemul_gloo_matches_one_rank(world):
             p.kill()
     assert results == {r: "ok" for r in range(world)}, results
     assert all(p.exitcode == 0 for p in procs)
+
+
+class _RecordingShard:
+    """Backend that records the phases limb_sharded_mul_many runs."""
+    cq, cp, nq = 2, 1, 2
+
+    def __init__(self):
+        self.log = []
+
+    def empty(self, shape):
+        return torch.zeros(tuple(shape), dtype=torch.int32)
+
+    def modup_input(self, x, cc_rows, slot=0):
+        self.log.append(("modup", int(x[0, 0, 0, 0]), slot))
+
+    def keyswitch(self, cc_all, kp_rows, slot=0):
+        self.log.append(("keyswitch", slot))
+
+    def moddown(self, kp_all, out, slot=0):
+        self.log.append(("moddown", slot))
+        out.fill_(len(self.log))
+
+
+def test_pipelined_schedule_order_and_slots():
+    """limb_sharded_mul_many's schedule on one rank: step i runs phase 1 of
+    call i, phase 2 of call i - 1 and phase 3 of call i - 2, each call keeping
+    the workspace slot call % PIPELINE_DEPTH for all three phases, and the
+    outputs come back in call order (the order every rank follows, so the
+    collectives between the phases match across ranks)."""
+    sh = _RecordingShard()
+    xs = [torch.full((1, 4, 3, 8), k, dtype=torch.int32) for k in range(5)]
+    outs = limb_shard.limb_sharded_mul_many(sh, xs, 0, 1)
+    D = limb_shard.PIPELINE_DEPTH
+    want = []
+    for i in range(len(xs) + 2):
+        if i < len(xs):
+            want.append(("modup", i, i % D))
+        if 0 <= i - 1 < len(xs):
+            want.append(("keyswitch", (i - 1) % D))
+        if 0 <= i - 2 < len(xs):
+            want.append(("moddown", (i - 2) % D))
+    assert sh.log == want
+    moddown_pos = [j + 1 for j, e in enumerate(want) if e[0] == "moddown"]
+    assert [int(o[0, 0, 0, 0]) for o in outs] == moddown_pos
+    assert [tuple(o.shape) for o in outs] == [(1, 2, 2, 8)] * len(xs)
