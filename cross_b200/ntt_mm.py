@@ -36,7 +36,6 @@ def basis_aligned_transformation(matrix: np.ndarray, moduli) -> np.ndarray:
     return np.ascontiguousarray(u8.transpose(1, 0, 2, 4, 3))
 
 
-@functools.lru_cache(maxsize=512)
 def gen_twiddle_matrix(rows: int, cols: int, q: int, omega: int) -> np.ndarray:
     """ntt_mm.py:75-97: T[r, c] = omega^(r c) mod q (int64)."""
     return util.twiddle_matrix(rows, cols, q, omega).astype(np.int64)
@@ -47,6 +46,7 @@ def gen_twiddle_matrix_inv(rows: int, cols: int, q: int, omega: int) -> np.ndarr
     return util.twiddle_matrix(rows, cols, q, pow(omega, -1, q)).astype(np.int64)
 
 
+@functools.lru_cache(maxsize=512)
 def _limb_tables(q: int, r: int, c: int):
     """The six raw twiddle tables of one modulus (ntt_mm.py:186-240), shared
     by every context that uses (q, r, c): HE-Mult, HE-Rotate and ciphertext
