@@ -269,3 +269,20 @@ def test_coefmap_factorisation_and_its_errors():
                       ((swapped, 4, 4), "NOT decomposable")):
         with pytest.raises(ValueError, match=msg):
             herot.mat_1d_shuffle_to_2d(*args)
+
+
+def test_twiddle_table_cache():
+    """The per-modulus twiddle tables are computed once per process and shared
+    read-only by every context over the same (q, r, c); the reference-named
+    gen_twiddle_matrix returns a fresh array each call, so a caller that
+    writes into it cannot change what the next caller gets."""
+    from cross_b200 import ntt_mm
+    q = O.find_moduli_ntt(1, 28, 2 * 256)[0]
+    a, b = ntt_mm._limb_tables(q, 16, 16), ntt_mm._limb_tables(q, 16, 16)
+    assert a is b and all(not t.flags.writeable for t in a)
+    assert ntt_mm._limb_bat(q, 16, 16) is ntt_mm._limb_bat(q, 16, 16)
+    om = 3                                   # any residue: the helper takes its powers
+    m1 = ntt_mm.gen_twiddle_matrix(8, 4, q, om)
+    keep = m1.copy()
+    m1[:] = 0
+    np.testing.assert_array_equal(ntt_mm.gen_twiddle_matrix(8, 4, q, om), keep)
